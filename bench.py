@@ -1,0 +1,368 @@
+"""Benchmark of the B200 MoE routed-expert path (one JSON line on rank 0).
+
+Workload (default): the DeepSeek-V4-Flash-shaped decode layer of the benchmark configurations
+(config 1): H=4096, 256 routed IQ2_XXS experts + 1 Q8_0 shared expert, top-8 learned routing
+(sqrt-softplus + bias, renormalised), I=2048, a decode batch of 64 tokens. A step is one layer
+forward over the batch: router projection, top-k, dispatch, gate/up + SwiGLU, down, combine.
+All inputs are seeded synthetic data with the configuration's distributions (no checkpoint).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--tokens T]
+
+--impl reference times the reference's own CPU implementation (the vastloom library compiled
+from its sources into oracle/_ref, driven by the restated layer loop) on the host cores.
+Multi-GPU (torchrun): every rank runs an independent replica of the layer on its own batch
+(replicas only - no collective on the data path), value = all ranks' tokens / max rank time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s decode & prefill at 1/2/4/8 B200; % HBM / tensor roofline"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def load_peaks():
+    if PEAKS_FILE.exists():
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def phase_bytes(spec, W, layer, T, offsets):
+    """Algorithmic bytes per phase of one forward (weights of the experts actually selected,
+    activations read and written once)."""
+    E, H, I, k = spec.experts, spec.hidden, spec.intermediate, spec.top_k
+    active = [e for e in range(E) if offsets[e + 1] > offsets[e]]
+    sz = lambda m: m.payload_bytes
+    gu = sum(sz(layer.matrices["w1"][e]) + sz(layer.matrices["w3"][e]) for e in active)
+    dn = sum(sz(layer.matrices["w2"][e]) for e in active)
+    P = T * k
+    if layer.shared_matrices:
+        s1, s3, s2 = layer.shared_matrices
+        gu += sz(s1) + sz(s3)
+        dn += sz(s2)
+        P += T
+    return {
+        "route": E * H * 4 + T * H * 4 + T * E * 8,
+        "gate_up": gu + T * H * 4 + P * I * 4,
+        "down": dn + P * I * 4 + P * H * 4,
+        "combine": P * H * 4 + T * H * 4,
+        "weights": gu + dn + E * H * 4,
+        "active_experts": len(active),
+    }
+
+
+def traffic_from_profiles(kernel: str):
+    f = ROOT / "profiles" / "ncu_traffic.json"
+    if not f.exists():
+        return None
+    d = json.loads(f.read_text())
+    return d.get(kernel)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    import vastloom_b200 as vb
+    from vastloom_b200 import synth
+
+    torch.cuda.set_device(local_rank)
+    dev = vb.Device(local_rank)
+    spec = synth.config(1)
+    T = args.tokens
+    W = synth.layer_weights(spec, seed=1)
+    layer = synth.upload_layer(dev, W, max_tokens=max(T, 64))
+    x_host, _, _ = synth.activations(spec, T, seed=2 + rank)
+    stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local_rank))
+    with torch.cuda.stream(stream):
+        x_dev = torch.from_numpy(x_host).cuda()
+        out_dev = torch.empty((T, spec.hidden), dtype=torch.float32, device="cuda")
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        layer.forward_device(x_dev.data_ptr(), T, out_dev.data_ptr(), stream=dev.stream)
+
+    def flush_l2():
+        with torch.cuda.stream(stream):
+            flush.zero_()
+
+    for _ in range(args.warmup):
+        flush_l2()
+        step()
+    torch.cuda.synchronize()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush_l2()  # outside the events: every timed step starts with a cold L2
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if dist:
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = T * world * args.steps / (total_ms / 1000.0)
+
+    # result check against a finite output (parity is the tests' job)
+    out = out_dev.cpu().numpy()
+    assert np.all(np.isfinite(out))
+
+    # end to end through the host-memory C-ABI call (H2D x, layer, D2H out, synchronise)
+    e2e_times = []
+    pinned_x = torch.from_numpy(x_host).pin_memory().numpy()
+    for i in range(max(3, args.steps)):
+        flush_l2()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        layer.forward(pinned_x)
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_value = T * world / statistics.mean(e2e_times)
+
+    # per-phase device time of the same forward (events inside the library, on its stream)
+    layer.set_profiling(True)
+    phases = {p: [] for p in layer.PHASES}
+    for _ in range(args.steps):
+        flush_l2()
+        step()
+        for p, v in layer.phase_times().items():
+            phases[p].append(v)
+    layer.set_profiling(False)
+    phase_ms = {p: statistics.mean(v) for p, v in phases.items()}
+    idx, w, offsets, pt, ps = layer.last_route(T)
+    pb = phase_bytes(spec, W, layer, T, offsets)
+    hbm, peak_kind = load_peaks()
+    dom = max(("gate_up", "down"), key=lambda p: phase_ms[p])
+    achieved = pb[dom] / (phase_ms[dom] / 1000.0) / 1e9
+    kernel_name = {"gate_up": "expert_kernel<true>", "down": "expert_kernel<false>"}[dom]
+    traffic = traffic_from_profiles(kernel_name)
+    layer_bytes = pb["route"] + pb["gate_up"] + pb["down"] + pb["combine"]
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded; configuration distributions, no checkpoint)",
+        "config": {
+            "workload": f"cfg1-v4flash-decode-T{T}",
+            "hidden": spec.hidden, "intermediate": spec.intermediate, "experts": spec.experts,
+            "top_k": spec.top_k, "shared_experts": 1, "tokens_per_gpu": T,
+            "routed_type": "IQ2_XXS", "shared_type": "Q8_0", "routing": "sqrt_softplus+bias, renorm",
+            "parallelism": "replicas" if world > 1 else "single",
+            "l2": "flushed (256 MiB write) before every timed step",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1),
+            "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+            "peak_kind": peak_kind, "traffic": traffic,
+            "algorithmic_bytes": pb[dom], "kernel_ms": round(phase_ms[dom], 5),
+        },
+        "layer_roofline": {
+            "bytes": layer_bytes, "achieved_gbs": round(layer_bytes / (ms_per_step / 1000.0) / 1e9, 1),
+            "frac": round(layer_bytes / (ms_per_step / 1000.0) / 1e9 / hbm, 4),
+            "active_experts": pb["active_experts"],
+        },
+        "phase_ms": {p: round(v, 5) for p, v in phase_ms.items()},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(out.nbytes),
+                "timing": "host wall clock around the synchronous C-ABI call"},
+        "clocks": clk,
+        "gpu_launches": 6 * args.steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget)
+    layer.destroy()
+    dev.close()
+    return result
+
+
+def cpu_baseline(W, x, budget_s: float, threads: int | None = None):
+    """The reference's own CPU path (oracle/_ref) on a bounded sample of the same batch."""
+    from oracle.oracle import Reference
+
+    if not Reference.available():
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref is not built"}
+    ref = Reference()
+    cores = os.cpu_count() or 1
+    # RowWorkPool has hardware_concurrency()/2 workers plus the caller (ggml_quantization.cpp:761)
+    threads = threads or max(1, cores // 2 + 1)
+    t0 = time.perf_counter()
+    ref.moe_forward(W, x[:1], threads=threads)
+    t1 = time.perf_counter() - t0
+    n = int(max(1, min(x.shape[0], budget_s / max(t1, 1e-6))))
+    t0 = time.perf_counter()
+    ref.moe_forward(W, x[:n], threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"first {n} of the {x.shape[0]} batch tokens through the reference's layer loop "
+                      f"({dt:.1f} s, max_threads={threads} of {cores} host threads)"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU implementation of the same layer and batch."""
+    from vastloom_b200 import synth
+    from oracle.oracle import Reference
+
+    if rank != 0:
+        return None
+    if not Reference.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref (reference compiled from source) is not built"}
+    spec = synth.config(1)
+    T = args.tokens
+    W = synth.layer_weights(spec, seed=1)
+    x, _, _ = synth.activations(spec, T, seed=2)
+    ref = Reference()
+    cores = os.cpu_count() or 1
+    threads = max(1, cores // 2 + 1)
+    per_step = max(1, args.ref_tokens_per_step)
+    for i in range(args.warmup):
+        ref.moe_forward(W, x[i % T: i % T + 1], threads=threads)
+    times = []
+    for i in range(args.steps):
+        lo = (i * per_step) % T
+        t0 = time.perf_counter()
+        ref.moe_forward(W, x[lo: lo + per_step], threads=threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = per_step * args.steps / total
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * total / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (f64 accumulation)",
+        "data": "synthetic (seeded; configuration distributions, no checkpoint)",
+        "config": {"workload": f"cfg1-v4flash-decode-T{T}", "tokens_per_step": per_step},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"{per_step} token(s) of the {T}-token batch per step"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--ref-tokens-per-step", type=int, default=1)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    res = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

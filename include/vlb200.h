@@ -1,0 +1,227 @@
+/*
+ * vlb200 - C ABI of the B200 (sm_100a) MoE routed-expert library.
+ *
+ * This is the boundary that replaces vastloom's CUDA driver / matvec-accelerator seam:
+ *   - src/cuda/cuda_driver.cpp (DynamicCudaBackend: dlopen of libcuda, embedded scalar PTX,
+ *     *_with_transfer launches; include/vastloom/cuda/cuda_driver.hpp:41-344), and
+ *   - src/cuda/cuda_matvec_accelerator.cpp (CudaMatvecAccelerator, the implementation of
+ *     DeepseekV4MatvecAccelerator, include/vastloom/inference/deepseek_v4_reference.hpp:440-451).
+ * A C++ adapter (vastloom_b200/host/b200_matvec_accelerator.hpp) implements the reference's
+ * DeepseekV4MatvecAccelerator interface on top of these entry points.
+ *
+ * Conventions (mirroring include/vastloom/core/status.hpp:10-21 and cuda_driver.cpp:2727-2738):
+ *   - every entry point returns an int status: VLB_OK (0) or VLB_ERR_* = vastloom ErrorCode + 1;
+ *   - VLB_DECLINED is the accelerator's "false": the call was refused, outputs are untouched and
+ *     the caller runs its CPU path (deepseek_v4_reference.hpp:440-451);
+ *   - the message of the last failure is kept per handle (vlb_last_error) and per thread
+ *     (vlb_thread_error) for calls that have no handle yet;
+ *   - nothing aborts or throws across this boundary; device-side waits are bounded and surface as
+ *     VLB_ERR_IO_ERROR.
+ * Threading: calls on one handle are serialised by the handle's mutex; each handle owns one CUDA
+ * stream on one device (the reference serialises its backend the same way, cuda_driver.cpp:2093).
+ * Memory: every device allocation the library makes is first reserved through the caller's
+ * governor callbacks (CudaDriver::allocate reserves before cuMemAlloc, cuda_driver.cpp:2929-3005).
+ */
+#ifndef VLB200_H
+#define VLB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VLB_ABI_VERSION 1
+
+/* Status codes: 0 = success; 1..10 = vastloom::ErrorCode + 1 (status.hpp:10-21). */
+enum {
+    VLB_OK = 0,
+    VLB_ERR_INVALID_ARGUMENT = 1,
+    VLB_ERR_INVALID_FORMAT = 2,
+    VLB_ERR_NOT_FOUND = 3,
+    VLB_ERR_PERMISSION_DENIED = 4,
+    VLB_ERR_IO_ERROR = 5,
+    VLB_ERR_INTEGRITY_ERROR = 6,
+    VLB_ERR_UNSAFE_PATH = 7,
+    VLB_ERR_UNSUPPORTED = 8,
+    VLB_ERR_RESOURCE_EXHAUSTED = 9,
+    VLB_ERR_INTERNAL_ERROR = 10,
+    VLB_DECLINED = 100
+};
+
+/* ggml storage types the device path accepts (ggml_quantization.hpp:35-46). */
+enum {
+    VLB_TYPE_F32 = 0,
+    VLB_TYPE_Q8_0 = 8,
+    VLB_TYPE_IQ2_XXS = 16,
+    VLB_TYPE_IQ3_XXS = 18,
+    VLB_TYPE_IQ1_S = 19
+};
+
+/* Router scoring (deepseek_v4_reference.cpp:65-69 sqrt_softplus; olmoe_runtime.cpp:1120-1127
+ * softmax; sigmoid has no reference router and is an extra mode). */
+enum { VLB_SCORE_SQRT_SOFTPLUS = 0, VLB_SCORE_SIGMOID = 1, VLB_SCORE_SOFTMAX = 2 };
+
+typedef struct vlb_handle vlb_handle;
+typedef struct vlb_matrix vlb_matrix;
+typedef struct vlb_layer vlb_layer;
+
+/* Governor hooks (include/vastloom/safety/resource_governor.hpp:60-113). reserve() is called with
+ * the exact byte count BEFORE each device allocation and must return 0 to allow it; release() is
+ * called after the matching free, or when the allocation failed after a successful reserve. A
+ * NULL governor means "no accounting" (tests only). */
+typedef struct vlb_governor {
+    void* ctx;
+    int (*reserve)(void* ctx, uint64_t bytes, const char* tag);
+    void (*release)(void* ctx, uint64_t bytes, const char* tag);
+} vlb_governor;
+
+typedef struct vlb_device_info {
+    int ordinal;
+    int sm_count;
+    int cc_major;
+    int cc_minor;
+    uint64_t total_bytes;
+    uint64_t free_bytes;
+    char name[96];
+} vlb_device_info;
+
+/* ---- library / device ------------------------------------------------------------------- */
+int vlb_abi_version(void);
+/* Thread-local message of the last failure of a call that had no handle (e.g. vlb_open). */
+int vlb_thread_error(char* buf, size_t cap);
+/* CudaDriverBackend::probe (cuda_driver.hpp:41-60): device count and one device's properties. */
+int vlb_device_count(int* count);
+int vlb_probe(int ordinal, vlb_device_info* info);
+
+/* Opens a handle on one device with its own stream. min_free_after: allocations that would
+ * leave less than this many free bytes on the device are refused (CudaMatvecAcceleratorOptions::
+ * minimum_free_vram_after, cuda_matvec_accelerator.hpp:17-30). */
+int vlb_open(int ordinal, const vlb_governor* governor, uint64_t min_free_after,
+             vlb_handle** out);
+void vlb_close(vlb_handle* h);
+int vlb_last_error(const vlb_handle* h, char* buf, size_t cap);
+/* The handle's CUDA stream (a cudaStream_t), for callers that enqueue their own work on it. */
+void* vlb_stream(vlb_handle* h);
+int vlb_synchronize(vlb_handle* h);
+
+/* ---- codebooks -------------------------------------------------------------------------- */
+/* Installs the IQ codebook for one type from the caller's table (the reference passes
+ * iq1_s_grid_table() / iq2_xxs_grid_table() / iq3_xxs_grid_table(), ggml_quantization.hpp:
+ * 63-76). The table's FNV-1a fingerprint must equal the reference's pinned value
+ * (ggml_quantization.cpp:60,73,99) or VLB_ERR_INTEGRITY_ERROR is returned. */
+int vlb_set_codebook(vlb_handle* h, uint32_t ggml_type, const void* table, size_t bytes);
+
+/* ---- governed device buffers (CudaDriver::allocate / CudaAllocation) ---------------------- */
+int vlb_alloc(vlb_handle* h, size_t bytes, const char* tag, void** dev_ptr);
+int vlb_free(vlb_handle* h, void* dev_ptr);
+int vlb_memcpy_h2d(vlb_handle* h, void* dst_dev, const void* src_host, size_t bytes);
+int vlb_memcpy_d2h(vlb_handle* h, void* dst_host, const void* src_dev, size_t bytes);
+/* Bytes currently allocated by this handle (resident matrices, layers, scratch). */
+uint64_t vlb_allocated_bytes(const vlb_handle* h);
+
+/* ---- resident packed matrices (DeepseekV4PackedMatrix, deepseek_v4_reference.hpp:104-141) --
+ * Uploads one ggml matrix (rows x storage_cols, consecutive little-endian blocks, exactly the
+ * reference's payload bytes) into device memory under its cache identity (never a host address;
+ * deepseek_v4_reference.hpp:125-132). The device copy is re-laid out for the kernels (per-block
+ * fp16 scales split from 16-byte-aligned block bodies); bytes per weight are unchanged. Every
+ * block scale must be finite (validate_block_scales, ggml_quantization.cpp:205-215). */
+int vlb_upload_matrix(vlb_handle* h, uint64_t cache_identity, uint32_t ggml_type, size_t rows,
+                      size_t storage_cols, const void* payload, size_t payload_bytes,
+                      vlb_matrix** out);
+int vlb_release_matrix(vlb_handle* h, vlb_matrix* m);
+/* Resident bytes of a matrix (scales + bodies). */
+uint64_t vlb_matrix_bytes(const vlb_matrix* m);
+
+/* The per-row operator seam: DeepseekV4MatvecAccelerator::matvec (deepseek_v4_reference.hpp:
+ * 440-451) for a resident matrix, host input (storage_cols floats, zero-padded by the caller)
+ * and host output (rows floats). Synchronous, like matvec_*_with_transfer
+ * (cuda_driver.cpp:2083-2171). */
+int vlb_matvec(vlb_handle* h, const vlb_matrix* m, const float* x_host, float* y_host);
+/* Device form over n_tokens rows of x (row stride x_stride floats) into y (n_tokens x rows,
+ * row stride y_stride floats), enqueued on `stream` (NULL = the handle's stream). */
+int vlb_matvec_device(vlb_handle* h, const vlb_matrix* m, const float* x_dev, size_t n_tokens,
+                      size_t x_stride, float* y_dev, size_t y_stride, void* stream);
+/* Dequantizes the whole matrix to f32 rows x storage_cols on the device (bit-exact with the
+ * reference's dequantize_*; ggml_quantization.cpp:217-435). */
+int vlb_dequantize_device(vlb_handle* h, const vlb_matrix* m, float* out_dev, void* stream);
+
+/* ---- the batched MoE layer (moe_forward, deepseek_v4_graph.cpp:1902-2274; OLMoE forward,
+ * olmoe_runtime.cpp:1119-1290) ------------------------------------------------------------ */
+typedef struct vlb_moe_layer_desc {
+    uint32_t hidden;        /* H */
+    uint32_t intermediate;  /* I */
+    uint32_t experts;       /* E routed experts */
+    uint32_t top_k;         /* k */
+    int score;              /* VLB_SCORE_* */
+    int hash_routing;       /* 1: experts from tid2eid[token*k + slot] */
+    int weight_after_down;  /* 1: OLMoE semantics (float SwiGLU, rank-order combine w*down) */
+    float route_scale;
+    float routed_swiglu_limit;
+    float shared_swiglu_limit;
+    uint32_t max_tokens;    /* workspace bound for one forward call */
+    uint32_t vocab;         /* rows of tid2eid */
+    const float* router;    /* host f32 [E x H], copied at create */
+    const float* bias;      /* host f32 [E] (learned routing) or NULL */
+    const uint32_t* tid2eid;/* host u32 [vocab x k] (hash routing) or NULL */
+    vlb_matrix* const* w1;  /* [E] gate (I x H) */
+    vlb_matrix* const* w3;  /* [E] up   (I x H) */
+    vlb_matrix* const* w2;  /* [E] down (H x I) */
+    vlb_matrix* shared_w1;  /* NULL: no shared expert */
+    vlb_matrix* shared_w3;
+    vlb_matrix* shared_w2;
+} vlb_moe_layer_desc;
+
+int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* desc, vlb_layer** out);
+int vlb_layer_destroy(vlb_handle* h, vlb_layer* layer);
+
+/* Device-resident forward: x_dev f32 [T x H], token_ids_dev u32 [T] (hash routing; may be NULL
+ * otherwise), optional logits_dev f32 [T x E] replacing the router projection, out_dev f32
+ * [T x H]. Enqueued on `stream` (NULL = handle stream); no host synchronisation. */
+int vlb_layer_forward_device(vlb_handle* h, vlb_layer* layer, const float* x_dev,
+                             const uint32_t* token_ids_dev, const float* logits_dev, uint32_t T,
+                             float* out_dev, void* stream);
+/* Host form (the end-to-end call): copies x / token ids / logits in, runs the layer, copies the
+ * output back, synchronises. */
+int vlb_layer_forward(vlb_handle* h, vlb_layer* layer, const float* x_host,
+                      const uint32_t* token_ids_host, const float* logits_host, uint32_t T,
+                      float* out_host);
+
+/* Route of the last forward on this layer, for parity checks: idx / weights [T x k] in rank
+ * order; offsets [E + 1]; pair_token / pair_slot [T x k] = the dispatch permutation (pairs
+ * sorted by expert ascending, then token, then slot - the reference's visit order,
+ * deepseek_v4_graph.cpp:2134-2223). Any pointer may be NULL. */
+int vlb_layer_last_route(vlb_handle* h, vlb_layer* layer, uint32_t T, uint32_t* idx,
+                         float* weights, uint32_t* offsets, uint32_t* pair_token,
+                         uint32_t* pair_slot);
+
+/* Bytes of weights a forward of the last route read (router + every selected expert's three
+ * matrices + the shared expert), the algorithmic numerator of the HBM roofline. */
+uint64_t vlb_layer_last_weight_bytes(vlb_handle* h, vlb_layer* layer);
+
+/* Phase timing of the layer forward (CUDA events on the launching stream, recorded only while
+ * enabled): ms[0] routing (router projection, scores, top-k), ms[1] dispatch, ms[2] gate/up +
+ * SwiGLU, ms[3] down, ms[4] combine, for the last forward. n must be >= 5. */
+int vlb_layer_set_profiling(vlb_handle* h, vlb_layer* layer, int enable);
+int vlb_layer_phase_times(vlb_handle* h, vlb_layer* layer, float* ms, int n);
+
+/* ---- standalone routing operators (deepseek_v4_route_*_logits, deepseek_v4_reference.hpp:
+ * 634-650) on device buffers ---------------------------------------------------------------- */
+int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* logits_dev,
+                     const float* bias_dev, const uint32_t* token_ids_dev,
+                     const uint32_t* tid2eid_dev, uint32_t vocab, uint32_t T, uint32_t E,
+                     uint32_t k, float route_scale, uint32_t* idx_dev, float* weights_dev,
+                     void* stream);
+/* Router projection logits[T x E] = f32(sum double(x) double(w)) (deepseek_v4_graph.cpp:
+ * 735-767). */
+int vlb_router_logits_device(vlb_handle* h, const float* x_dev, const float* w_dev, uint32_t T,
+                             uint32_t H, uint32_t E, float* logits_dev, void* stream);
+/* deepseek_v4_rms_norm (deepseek_v4_reference.cpp:170-206) on device rows. */
+int vlb_rms_norm_device(vlb_handle* h, const float* x_dev, const float* w_dev, uint32_t rows,
+                        uint32_t width, float eps, float* out_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VLB200_H */

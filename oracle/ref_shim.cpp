@@ -1,0 +1,263 @@
+// TEST INFRASTRUCTURE ONLY - extern "C" entry points over the vastloom reference library itself,
+// which oracle/Makefile compiles from the reference's own sources into oracle/_ref/. Used by the
+// tests to pin the C restatement (vlb_oracle.c) and by bench.py's reference/cpu_baseline legs.
+//
+// Everything arithmetic here is the reference's own code (matvec_*_f32, dequantize_*,
+// deepseek_v4_route_*_logits, deepseek_v4_rms_norm). The only restated piece is the MoE layer
+// loop, which is file-static in the reference (deepseek_v4_graph.cpp:1826-2274 execute_expert /
+// moe_forward; olmoe_runtime.cpp:1119-1290); vlr_moe_forward below follows that loop order
+// exactly and calls the reference's public kernels for every product.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <span>
+#include <vector>
+
+#include "vastloom/inference/deepseek_v4_reference.hpp"
+#include "vastloom/inference/ggml_quantization.hpp"
+
+namespace vi = vastloom::inference;
+
+extern "C" {
+
+struct vlr_matrix {
+    uint32_t type;
+    size_t rows;
+    size_t cols;
+    const uint8_t* data;
+};
+
+struct vlr_moe_layer {
+    size_t hidden, intermediate, experts, top_k;
+    int score;  // 0 sqrt_softplus, 1 sigmoid (no reference router: unsupported here), 2 softmax
+    int hash_routing;
+    int weight_after_down;
+    float route_scale, routed_swiglu_limit, shared_swiglu_limit;
+    const float* router;
+    const float* bias;
+    const uint32_t* tid2eid;
+    size_t vocab;
+    const vlr_matrix* w1;
+    const vlr_matrix* w3;
+    const vlr_matrix* w2;
+    const vlr_matrix* shared_w1;
+    const vlr_matrix* shared_w3;
+    const vlr_matrix* shared_w2;
+};
+
+static std::span<const std::byte> bytes_of(const vlr_matrix& m, size_t nbytes) {
+    return {reinterpret_cast<const std::byte*>(m.data), nbytes};
+}
+
+static size_t matrix_bytes(uint32_t type, size_t rows, size_t cols) {
+    auto b = vi::ggml_storage_bytes(type, rows, cols, vi::QuantizedKernelLimits{1ull << 40, 1});
+    return b ? b.value() : 0;
+}
+
+// Copies a reference codebook (iq*_grid_table) into caller storage; returns its byte size.
+size_t vlr_grid(uint32_t type, void* out, size_t cap) {
+    std::span<const std::byte> g;
+    if (type == vi::kGgmlTypeIq1S) g = std::as_bytes(vi::iq1_s_grid_table());
+    else if (type == vi::kGgmlTypeIq2Xxs) g = std::as_bytes(vi::iq2_xxs_grid_table());
+    else if (type == vi::kGgmlTypeIq3Xxs) g = std::as_bytes(vi::iq3_xxs_grid_table());
+    else return 0;
+    if (out && cap >= g.size()) std::memcpy(out, g.data(), g.size());
+    return g.size();
+}
+
+int vlr_dequantize(uint32_t type, const uint8_t* enc, size_t nbytes, float* out, size_t n) {
+    std::span<const std::byte> e(reinterpret_cast<const std::byte*>(enc), nbytes);
+    std::span<float> o(out, n);
+    vi::QuantizedKernelLimits lim{1ull << 40, 1};
+    vastloom::Result<void> r;
+    switch (type) {
+        case vi::kGgmlTypeQ8_0: r = vi::dequantize_q8_0(e, o, lim); break;
+        case vi::kGgmlTypeIq2Xxs: r = vi::dequantize_iq2_xxs(e, o, lim); break;
+        case vi::kGgmlTypeIq3Xxs: r = vi::dequantize_iq3_xxs(e, o, lim); break;
+        case vi::kGgmlTypeIq1S: r = vi::dequantize_iq1_s(e, o, lim); break;
+        default: return -2;
+    }
+    return r ? 0 : -1;
+}
+
+int vlr_matvec(uint32_t type, const uint8_t* enc, size_t rows, size_t cols, const float* x,
+               float* y, unsigned threads) {
+    const size_t nb = matrix_bytes(type, rows, cols);
+    if (nb == 0) return -2;
+    std::span<const std::byte> e(reinterpret_cast<const std::byte*>(enc), nb);
+    std::vector<float> scratch(rows);
+    vi::QuantizedKernelLimits lim{1ull << 40, threads == 0 ? 1u : threads};
+    auto r = vi::matvec_ggml_f32_transactional(type, e, rows, cols, {x, cols}, scratch,
+                                               {y, rows}, lim);
+    return r ? 0 : -1;
+}
+
+int vlr_quantize_q8_0(const float* m, size_t rows, size_t lc, size_t sc, uint8_t* out) {
+    auto r = vi::quantize_q8_0_reference({m, rows * lc}, rows, lc, sc);
+    if (!r) return -1;
+    std::memcpy(out, r.value().data(), r.value().size());
+    return 0;
+}
+
+static int copy_route(const vastloom::Result<vi::DeepseekV4RouteResult>& r, uint32_t* idx,
+                      float* w) {
+    if (!r) return -1;
+    std::memcpy(idx, r.value().indices.data(), r.value().indices.size() * sizeof(uint32_t));
+    std::memcpy(w, r.value().weights.data(), r.value().weights.size() * sizeof(float));
+    return 0;
+}
+
+int vlr_route_learned(const float* logits, const float* bias, size_t T, size_t E, size_t k,
+                      float route_scale, uint32_t* idx, float* w) {
+    return copy_route(vi::deepseek_v4_route_learned_logits({logits, T * E}, {bias, E}, T, E, k,
+                                                           route_scale),
+                      idx, w);
+}
+
+int vlr_route_hash(const float* logits, const uint32_t* token_ids, const uint32_t* table,
+                   size_t T, size_t V, size_t E, size_t k, float route_scale, uint32_t* idx,
+                   float* w) {
+    return copy_route(vi::deepseek_v4_route_hash_logits({logits, T * E}, {token_ids, T},
+                                                        {table, V * k}, T, V, E, k,
+                                                        route_scale),
+                      idx, w);
+}
+
+int vlr_rms_norm(const float* x, const float* w, size_t rows, size_t width, float eps,
+                 float* out) {
+    auto r = vi::deepseek_v4_rms_norm({x, rows * width}, {w, width}, rows, width, eps);
+    if (!r) return -1;
+    std::memcpy(out, r.value().data(), rows * width * sizeof(float));
+    return 0;
+}
+
+// Router projection as the reference graph computes it (linear, deepseek_v4_graph.cpp:735-767).
+static std::vector<float> router_logits(const vlr_moe_layer& L, const float* x, size_t T) {
+    std::vector<float> logits(T * L.experts);
+    for (size_t t = 0; t < T; ++t)
+        for (size_t e = 0; e < L.experts; ++e) {
+            double s = 0.0;
+            for (size_t c = 0; c < L.hidden; ++c)
+                s += static_cast<double>(x[t * L.hidden + c]) *
+                     static_cast<double>(L.router[e * L.hidden + c]);
+            logits[t * L.experts + e] = static_cast<float>(s);
+        }
+    return logits;
+}
+
+static int mv(const vlr_matrix& m, const float* x, float* y, std::vector<float>& scratch,
+              unsigned threads) {
+    const size_t nb = matrix_bytes(m.type, m.rows, m.cols);
+    scratch.resize(m.rows);
+    vi::QuantizedKernelLimits lim{1ull << 40, threads == 0 ? 1u : threads};
+    auto r = vi::matvec_ggml_f32_transactional(m.type, bytes_of(m, nb), m.rows, m.cols,
+                                               {x, m.cols}, scratch, {y, m.rows}, lim);
+    return r ? 0 : -1;
+}
+
+// The layer loop of moe_forward/execute_expert (DeepSeek V4) or of the OLMoE forward, with the
+// reference's own products. threads = QuantizedKernelLimits::max_threads for every matvec (the
+// reference's RowWorkPool row split, bit-identical to serial). Optional logits_in replaces the
+// router projection. Returns 0 on success.
+int vlr_moe_forward(const vlr_moe_layer* Lp, const float* x, const uint32_t* token_ids,
+                    size_t T, const float* logits_in, float* out, uint32_t* idx, float* weights,
+                    unsigned threads) {
+    const auto& L = *Lp;
+    const size_t H = L.hidden, I = L.intermediate, E = L.experts, k = L.top_k;
+    std::vector<float> logits = logits_in ? std::vector<float>(logits_in, logits_in + T * E)
+                                          : router_logits(L, x, T);
+    std::vector<float> gate(I), up(I), act(I), eo(H), scratch;
+    if (L.score == 2) {
+        // OLMoE router and combine, olmoe_runtime.cpp:1120-1137 and :1276-1286.
+        std::vector<float> p(E);
+        std::vector<uint32_t> order(E);
+        for (size_t t = 0; t < T; ++t) {
+            const float* l = logits.data() + t * E;
+            float mx = l[0];
+            for (size_t e = 1; e < E; ++e) mx = std::max(mx, l[e]);
+            double den = 0.0;
+            for (size_t e = 0; e < E; ++e) {
+                p[e] = std::exp(l[e] - mx);
+                den += static_cast<double>(p[e]);
+                order[e] = static_cast<uint32_t>(e);
+            }
+            for (auto& v : p) v /= static_cast<float>(den);
+            std::partial_sort(order.begin(), order.begin() + static_cast<std::ptrdiff_t>(k),
+                              order.end(), [&](uint32_t a, uint32_t b) {
+                                  if (p[a] != p[b]) return p[a] > p[b];
+                                  return a < b;
+                              });
+            for (size_t s = 0; s < k; ++s) {
+                idx[t * k + s] = order[s];
+                weights[t * k + s] = p[order[s]];
+            }
+        }
+        std::memset(out, 0, T * H * sizeof(float));
+        for (size_t t = 0; t < T; ++t)
+            for (size_t s = 0; s < k; ++s) {
+                const uint32_t e = idx[t * k + s];
+                if (mv(L.w1[e], x + t * H, gate.data(), scratch, threads) ||
+                    mv(L.w3[e], x + t * H, up.data(), scratch, threads))
+                    return -1;
+                for (size_t c = 0; c < I; ++c)
+                    act[c] = (gate[c] / (1.0F + std::exp(-gate[c]))) * up[c];
+                if (mv(L.w2[e], act.data(), eo.data(), scratch, threads)) return -1;
+                const float w = weights[t * k + s];
+                for (size_t c = 0; c < H; ++c) out[t * H + c] += w * eo[c];
+            }
+        return 0;
+    }
+    if (L.score != 0) return -2;  // the reference has no sigmoid router
+    {
+        vastloom::Result<vi::DeepseekV4RouteResult> route =
+            L.hash_routing
+                ? vi::deepseek_v4_route_hash_logits(logits, {token_ids, T},
+                                                    {L.tid2eid, L.vocab * k}, T, L.vocab, E, k,
+                                                    L.route_scale)
+                : vi::deepseek_v4_route_learned_logits(logits, {L.bias, E}, T, E, k,
+                                                       L.route_scale);
+        if (copy_route(route, idx, weights)) return -1;
+    }
+    // execute_expert, deepseek_v4_graph.cpp:1826-1895
+    const auto expert = [&](const vlr_matrix& w1, const vlr_matrix& w3, const vlr_matrix& w2,
+                            const float* xt, const float* rw, float limit, float* o) {
+        if (mv(w1, xt, gate.data(), scratch, threads) || mv(w3, xt, up.data(), scratch, threads))
+            return -1;
+        for (size_t c = 0; c < I; ++c) {
+            double g = static_cast<double>(gate[c]);
+            double u = static_cast<double>(up[c]);
+            if (limit > 0.0F) {
+                g = std::min(g, static_cast<double>(limit));
+                u = std::clamp(u, -static_cast<double>(limit), static_cast<double>(limit));
+            }
+            double v = g / (1.0 + std::exp(-g)) * u;
+            if (rw) v *= static_cast<double>(*rw);
+            act[c] = static_cast<float>(v);
+        }
+        return mv(w2, act.data(), o, scratch, threads);
+    };
+    std::vector<float> shared;
+    if (L.shared_w1) {
+        shared.resize(T * H);
+        for (size_t t = 0; t < T; ++t)
+            if (expert(*L.shared_w1, *L.shared_w3, *L.shared_w2, x + t * H, nullptr,
+                       L.shared_swiglu_limit, shared.data() + t * H))
+                return -1;
+    }
+    std::memset(out, 0, T * H * sizeof(float));
+    for (size_t e = 0; e < E; ++e)
+        for (size_t t = 0; t < T; ++t)
+            for (size_t s = 0; s < k; ++s) {
+                if (idx[t * k + s] != e) continue;
+                if (expert(L.w1[e], L.w3[e], L.w2[e], x + t * H, &weights[t * k + s],
+                           L.routed_swiglu_limit, eo.data()))
+                    return -1;
+                for (size_t c = 0; c < H; ++c) out[t * H + c] += eo[c];
+            }
+    if (!shared.empty())
+        for (size_t i = 0; i < T * H; ++i) out[i] += shared[i];
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,509 @@
+/*
+ * TEST INFRASTRUCTURE ONLY - CPU restatement of the vastloom reference arithmetic for the MoE
+ * routed-expert path (see vlb_oracle.h). Built with -O2 -ffp-contract=off so that every float
+ * operation rounds exactly where the reference's does (the reference is built for x86-64 without
+ * FMA, so it never contracts a multiply into an add).
+ *
+ * Citations are vastloom source paths (file:line).
+ */
+#include "vlb_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ggml_quantization.hpp:12-31 */
+int vlo_block_layout(uint32_t type, size_t* block_elems, size_t* block_bytes) {
+    switch (type) {
+        case VLO_TYPE_F32: *block_elems = 1; *block_bytes = 4; return 0;
+        case VLO_TYPE_Q8_0: *block_elems = 32; *block_bytes = 34; return 0;
+        case VLO_TYPE_IQ2_XXS: *block_elems = 256; *block_bytes = 66; return 0;
+        case VLO_TYPE_IQ3_XXS: *block_elems = 256; *block_bytes = 98; return 0;
+        case VLO_TYPE_IQ1_S: *block_elems = 256; *block_bytes = 50; return 0;
+        default: return -1;
+    }
+}
+
+static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* fp16_to_float, ggml_quantization.cpp:101-124: IEEE half with subnormals normalised by hand. */
+float vlo_fp16_to_float(uint16_t value) {
+    uint32_t sign = (uint32_t)(value & 0x8000u) << 16;
+    uint32_t exponent = (value >> 10) & 0x1fu;
+    uint32_t mantissa = value & 0x03ffu;
+    uint32_t bits = sign;
+    if (exponent == 0u) {
+        if (mantissa != 0u) {
+            exponent = 113u;
+            while ((mantissa & 0x0400u) == 0u) { mantissa <<= 1; --exponent; }
+            mantissa &= 0x03ffu;
+            bits |= exponent << 23;
+            bits |= mantissa << 13;
+        }
+    } else if (exponent == 0x1fu) {
+        bits |= 0x7f800000u | (mantissa << 13);
+    } else {
+        bits |= (exponent + 112u) << 23;
+        bits |= mantissa << 13;
+    }
+    return u2f(bits);
+}
+
+/* float_to_fp16, ggml_quantization.cpp:126-145: round-to-nearest-even through the
+ * scale-to-infinity / scale-to-zero construction. */
+uint16_t vlo_float_to_fp16(float value) {
+    const float scale_to_infinity = 0x1.0p+112f;
+    const float scale_to_zero = 0x1.0p-110f;
+    float base = (fabsf(value) * scale_to_infinity) * scale_to_zero;
+    const uint32_t word = f2u(value);
+    const uint32_t shifted = word + word;
+    const uint32_t sign = word & 0x80000000u;
+    uint32_t bias = shifted & 0xff000000u;
+    if (bias < 0x71000000u) bias = 0x71000000u;
+    base = u2f((bias >> 1) + 0x07800000u) + base;
+    const uint32_t bits = f2u(base);
+    const uint32_t exponent = (bits >> 13) & 0x00007c00u;
+    const uint32_t mantissa = bits & 0x00000fffu;
+    const uint32_t non_sign = exponent + mantissa;
+    return (uint16_t)((sign >> 16) | (shifted > 0xff000000u ? 0x7e00u : non_sign));
+}
+
+uint64_t vlo_fnv1a_bytes(const void* v, size_t n) {
+    const uint8_t* p = (const uint8_t*)v;
+    uint64_t h = 14695981039346656037ull;
+    for (size_t i = 0; i < n; ++i) { h ^= p[i]; h *= 1099511628211ull; }
+    return h;
+}
+
+/* The float fingerprint of tests/test_main.cpp:1332-1339: FNV-1a over each value's bits, low
+ * byte first. On a little-endian host that is the byte FNV of the array. */
+uint64_t vlo_fnv1a_f32(const float* v, size_t n) {
+    uint64_t h = 14695981039346656037ull;
+    for (size_t i = 0; i < n; ++i) {
+        uint32_t bits = f2u(v[i]);
+        for (unsigned s = 0; s < 32; s += 8) { h ^= (bits >> s) & 0xffu; h *= 1099511628211ull; }
+    }
+    return h;
+}
+
+static uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+static uint32_t rd32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+static int parity7(uint32_t v) { return __builtin_popcount(v) & 1; }
+
+/* decode_q8_0_block, ggml_quantization.cpp:419-435: w = d * float(int8 q) */
+static int decode_q8_0(const uint8_t* b, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b));
+    if (!isfinite(d)) return -1;
+    for (int i = 0; i < 32; ++i) out[i] = d * (float)(int8_t)b[2 + i];
+    return 0;
+}
+
+/* decode_iq2_xxs_block, ggml_quantization.cpp:250-283 */
+static int decode_iq2_xxs(const uint8_t* b, const uint64_t* grid, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b));
+    if (!isfinite(d)) return -1;
+    const uint8_t* q = b + 2;
+    for (int g = 0; g < 8; ++g) {
+        const uint8_t* packed = q + g * 8;
+        const uint32_t aux = rd32(packed + 4);
+        const float ls = d * (0.5f + (float)(aux >> 28)) * 0.25f;
+        for (int j = 0; j < 4; ++j) {
+            const uint64_t gv = grid[packed[j]];
+            const uint32_t si = (aux >> (7 * j)) & 127u;
+            const uint32_t signs = si | ((uint32_t)parity7(si) << 7);
+            for (int l = 0; l < 8; ++l) {
+                const uint8_t m = (uint8_t)((gv >> (8 * l)) & 0xffu);
+                const float s = (signs & (1u << l)) ? -1.0f : 1.0f;
+                out[g * 32 + j * 8 + l] = ls * (float)m * s;
+            }
+        }
+    }
+    return 0;
+}
+
+/* decode_iq3_xxs_block, ggml_quantization.cpp:336-379 */
+static int decode_iq3_xxs(const uint8_t* b, const uint32_t* grid, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b));
+    if (!isfinite(d)) return -1;
+    const uint8_t* q = b + 2;
+    const uint8_t* ss = q + 64;
+    for (int g = 0; g < 8; ++g) {
+        const uint32_t aux = rd32(ss + g * 4);
+        const float ls = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t si = (aux >> (7 * j)) & 127u;
+            const uint32_t signs = si | ((uint32_t)parity7(si) << 7);
+            const uint32_t g1 = grid[q[g * 8 + j * 2]];
+            const uint32_t g2 = grid[q[g * 8 + j * 2 + 1]];
+            for (int l = 0; l < 4; ++l) {
+                const float s1 = (signs & (1u << l)) ? -1.0f : 1.0f;
+                const float s2 = (signs & (1u << (l + 4))) ? -1.0f : 1.0f;
+                const uint8_t m1 = (uint8_t)((g1 >> (8 * l)) & 0xffu);
+                const uint8_t m2 = (uint8_t)((g2 >> (8 * l)) & 0xffu);
+                out[g * 32 + j * 8 + l] = ls * (float)m1 * s1;
+                out[g * 32 + j * 8 + l + 4] = ls * (float)m2 * s2;
+            }
+        }
+    }
+    return 0;
+}
+
+/* decode_iq1_s_block, ggml_quantization.cpp:217-248 */
+static int decode_iq1_s(const uint8_t* b, const uint64_t* grid, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b));
+    if (!isfinite(d)) return -1;
+    const uint8_t* qs = b + 2;
+    const uint8_t* qh = b + 34;
+    for (int g = 0; g < 8; ++g) {
+        const uint16_t h = rd16(qh + g * 2);
+        const float ls = d * (float)(2u * ((h >> 12) & 7u) + 1u);
+        const float delta = (h & 0x8000u) ? -0.125f : 0.125f;
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t idx = (uint32_t)qs[g * 4 + j] | ((uint32_t)((h >> (3 * j)) & 7u) << 8);
+            const uint64_t gv = grid[idx];
+            for (int l = 0; l < 8; ++l) {
+                const int8_t v = (int8_t)((gv >> (8 * l)) & 0xffu);
+                out[g * 32 + j * 8 + l] = ls * ((float)v + delta);
+            }
+        }
+    }
+    return 0;
+}
+
+static int decode_block(uint32_t type, const uint8_t* b, const void* grid, float* out) {
+    switch (type) {
+        case VLO_TYPE_Q8_0: return decode_q8_0(b, out);
+        case VLO_TYPE_IQ2_XXS: return decode_iq2_xxs(b, (const uint64_t*)grid, out);
+        case VLO_TYPE_IQ3_XXS: return decode_iq3_xxs(b, (const uint32_t*)grid, out);
+        case VLO_TYPE_IQ1_S: return decode_iq1_s(b, (const uint64_t*)grid, out);
+        case VLO_TYPE_F32: memcpy(out, b, 4); return isfinite(out[0]) ? 0 : -1;
+        default: return -2;
+    }
+}
+
+/* dequantize_blocked, ggml_quantization.cpp:600-628 */
+int vlo_dequantize(uint32_t type, const uint8_t* enc, size_t n_blocks, const void* grid,
+                   float* out) {
+    size_t be, bb;
+    if (vlo_block_layout(type, &be, &bb) != 0) return -2;
+    for (size_t i = 0; i < n_blocks; ++i) {
+        int st = decode_block(type, enc + i * bb, grid, out + i * be);
+        if (st) return st;
+    }
+    return 0;
+}
+
+/* matvec_blocked, ggml_quantization.cpp:768-809 (and the serial twins matvec_iq1_s_f32 :1331,
+ * matvec_iq3_xxs_f32 :1409): one double accumulator per row, columns in order, cast once. */
+int vlo_matvec(uint32_t type, const uint8_t* enc, size_t rows, size_t cols, const float* x,
+               float* y, const void* grid) {
+    size_t be, bb;
+    if (vlo_block_layout(type, &be, &bb) != 0 || cols % be) return -2;
+    float dec[256];
+    const size_t bpr = cols / be;
+    for (size_t r = 0; r < rows; ++r) {
+        double sum = 0.0;
+        for (size_t b = 0; b < bpr; ++b) {
+            int st = decode_block(type, enc + (r * bpr + b) * bb, grid, dec);
+            if (st) return st;
+            for (size_t c = 0; c < be; ++c) sum += (double)dec[c] * (double)x[b * be + c];
+        }
+        y[r] = (float)sum;
+        if (!isfinite(y[r])) return -3;
+    }
+    return 0;
+}
+
+/* quantize_q8_0_reference, ggml_quantization.cpp:944-1004 */
+int vlo_quantize_q8_0(const float* m, size_t rows, size_t lc, size_t sc, uint8_t* out) {
+    if (lc == 0 || lc > sc || sc % 32) return -1;
+    const size_t bpr = sc / 32;
+    for (size_t r = 0; r < rows; ++r) {
+        for (size_t b = 0; b < bpr; ++b) {
+            float v[32];
+            float maximum = 0.0f;
+            for (size_t i = 0; i < 32; ++i) {
+                const size_t c = b * 32 + i;
+                const float val = c < lc ? m[r * lc + c] : 0.0f;
+                if (!isfinite(val)) return -1;
+                v[i] = val;
+                maximum = fmaxf(maximum, fabsf(val));
+            }
+            const float scale = maximum / 127.0f;
+            const float inverse = scale != 0.0f ? 1.0f / scale : 0.0f;
+            uint8_t* o = out + (r * bpr + b) * 34;
+            const uint16_t es = vlo_float_to_fp16(scale);
+            if (!isfinite(vlo_fp16_to_float(es))) return -1;
+            o[0] = (uint8_t)(es & 0xffu);
+            o[1] = (uint8_t)(es >> 8);
+            for (size_t i = 0; i < 32; ++i) {
+                float rounded = roundf(v[i] * inverse);
+                if (rounded < -127.0f) rounded = -127.0f;
+                if (rounded > 127.0f) rounded = 127.0f;
+                o[2 + i] = (uint8_t)(int8_t)rounded;
+            }
+        }
+    }
+    return 0;
+}
+
+/* sqrt_softplus, deepseek_v4_reference.cpp:65-69 */
+float vlo_sqrt_softplus(float value) {
+    const double p = (double)value;
+    const double softplus = (p > 0.0 ? p : 0.0) + log1p(exp(-fabs(p)));
+    return (float)sqrt(softplus);
+}
+
+/* sigmoid, deepseek_v4_reference.cpp:71-78 */
+float vlo_sigmoid(float value) {
+    const double p = (double)value;
+    if (p >= 0.0) return (float)(1.0 / (1.0 + exp(-p)));
+    const double e = exp(p);
+    return (float)(e / (1.0 + e));
+}
+
+/* gate_logits, deepseek_v4_reference.cpp:123-160 (also linear, deepseek_v4_graph.cpp:735-767) */
+void vlo_router_logits(const float* x, const float* w, size_t T, size_t H, size_t E,
+                       float* logits) {
+    for (size_t t = 0; t < T; ++t)
+        for (size_t e = 0; e < E; ++e) {
+            double sum = 0.0;
+            for (size_t c = 0; c < H; ++c) sum += (double)x[t * H + c] * (double)w[e * H + c];
+            logits[t * E + e] = (float)sum;
+        }
+}
+
+/* Ordering used by every reference router: larger key first, ties to the lower expert id
+ * (deepseek_v4_reference.cpp:240-244, olmoe_runtime.cpp:1128-1137). */
+static void top_k_by_key(const float* key, size_t E, size_t k, uint32_t* out) {
+    /* selection sort of the first k: identical result to std::partial_sort with a strict
+     * total order (no NaN can reach here: inputs are finite). */
+    unsigned char* used = (unsigned char*)calloc(E, 1);
+    for (size_t s = 0; s < k; ++s) {
+        size_t best = E;
+        for (size_t e = 0; e < E; ++e) {
+            if (used[e]) continue;
+            if (best == E || key[e] > key[best]) best = e;
+        }
+        used[best] = 1;
+        out[s] = (uint32_t)best;
+    }
+    free(used);
+}
+
+/* route_from_indices, deepseek_v4_reference.cpp:80-121: weights are the UNBIASED scores of the
+ * chosen experts, normalised in double and multiplied by route_scale. */
+static int route_from_indices(const float* scores, const uint32_t* idx, size_t t, size_t E,
+                              size_t k, float route_scale, float* weights) {
+    double sum = 0.0;
+    for (size_t s = 0; s < k; ++s) {
+        if (idx[t * k + s] >= E) return -1;
+        const float v = scores[t * E + idx[t * k + s]];
+        weights[t * k + s] = v;
+        sum += (double)v;
+    }
+    if (!isfinite(sum) || sum <= 0.0) return -1;
+    for (size_t s = 0; s < k; ++s)
+        weights[t * k + s] = (float)((double)weights[t * k + s] / sum * (double)route_scale);
+    return 0;
+}
+
+static void score_logits(const float* logits, size_t n, int score, float* out) {
+    for (size_t i = 0; i < n; ++i)
+        out[i] = score == VLO_SCORE_SIGMOID ? vlo_sigmoid(logits[i]) : vlo_sqrt_softplus(logits[i]);
+}
+
+/* deepseek_v4_route_learned_logits, deepseek_v4_reference.cpp:223-255 */
+int vlo_route_learned(const float* logits, const float* bias, size_t T, size_t E, size_t k,
+                      float route_scale, int score, uint32_t* idx, float* weights) {
+    if (k == 0 || k > E || !(route_scale > 0.0f)) return -1;
+    float* scores = (float*)malloc(T * E * sizeof(float));
+    float* key = (float*)malloc(E * sizeof(float));
+    score_logits(logits, T * E, score, scores);
+    int st = 0;
+    for (size_t t = 0; t < T && !st; ++t) {
+        for (size_t e = 0; e < E; ++e) key[e] = scores[t * E + e] + bias[e];
+        top_k_by_key(key, E, k, idx + t * k);
+        st = route_from_indices(scores, idx, t, E, k, route_scale, weights);
+    }
+    free(scores);
+    free(key);
+    return st;
+}
+
+/* deepseek_v4_route_hash_logits, deepseek_v4_reference.cpp:275-307 */
+int vlo_route_hash(const float* logits, const uint32_t* token_ids, const uint32_t* table,
+                   size_t T, size_t V, size_t E, size_t k, float route_scale, int score,
+                   uint32_t* idx, float* weights) {
+    if (k == 0 || k > E || !(route_scale > 0.0f)) return -1;
+    float* scores = (float*)malloc(T * E * sizeof(float));
+    score_logits(logits, T * E, score, scores);
+    int st = 0;
+    for (size_t t = 0; t < T && !st; ++t) {
+        if (token_ids[t] >= V) { st = -1; break; }
+        for (size_t s = 0; s < k; ++s) idx[t * k + s] = table[(size_t)token_ids[t] * k + s];
+        st = route_from_indices(scores, idx, t, E, k, route_scale, weights);
+    }
+    free(scores);
+    return st;
+}
+
+/* OLMoE router, olmoe_runtime.cpp:1120-1137: float exp of (logit - max), double denominator,
+ * float division, top-k by probability, no renormalisation. */
+int vlo_route_softmax(const float* logits, size_t T, size_t E, size_t k, uint32_t* idx,
+                      float* weights) {
+    if (k == 0 || k > E) return -1;
+    float* p = (float*)malloc(E * sizeof(float));
+    for (size_t t = 0; t < T; ++t) {
+        const float* l = logits + t * E;
+        float mx = l[0];
+        for (size_t e = 1; e < E; ++e) if (l[e] > mx) mx = l[e];
+        double den = 0.0;
+        for (size_t e = 0; e < E; ++e) { p[e] = expf(l[e] - mx); den += (double)p[e]; }
+        for (size_t e = 0; e < E; ++e) p[e] /= (float)den;
+        top_k_by_key(p, E, k, idx + t * k);
+        for (size_t s = 0; s < k; ++s) weights[t * k + s] = p[idx[t * k + s]];
+    }
+    free(p);
+    return 0;
+}
+
+/* The dispatch permutation. The reference visits experts in ascending id, then tokens, then
+ * slots (deepseek_v4_graph.cpp:2134-2223); this is that visit order written out as a stable
+ * counting sort. */
+void vlo_dispatch(const uint32_t* idx, size_t T, size_t k, size_t E, uint32_t* offsets,
+                  uint32_t* pair_token, uint32_t* pair_slot) {
+    memset(offsets, 0, (E + 1) * sizeof(uint32_t));
+    for (size_t i = 0; i < T * k; ++i) offsets[idx[i] + 1]++;
+    for (size_t e = 0; e < E; ++e) offsets[e + 1] += offsets[e];
+    uint32_t* cursor = (uint32_t*)malloc(E * sizeof(uint32_t));
+    memcpy(cursor, offsets, E * sizeof(uint32_t));
+    for (size_t t = 0; t < T; ++t)
+        for (size_t s = 0; s < k; ++s) {
+            const uint32_t e = idx[t * k + s];
+            pair_token[cursor[e]] = (uint32_t)t;
+            pair_slot[cursor[e]] = (uint32_t)s;
+            cursor[e]++;
+        }
+    free(cursor);
+}
+
+/* deepseek_v4_rms_norm, deepseek_v4_reference.cpp:170-206 */
+int vlo_rms_norm(const float* x, const float* w, size_t rows, size_t width, float eps,
+                 float* out) {
+    for (size_t r = 0; r < rows; ++r) {
+        double sq = 0.0;
+        for (size_t c = 0; c < width; ++c) { const double v = x[r * width + c]; sq += v * v; }
+        const double inv = 1.0 / sqrt(sq / (double)width + (double)eps);
+        for (size_t c = 0; c < width; ++c)
+            out[r * width + c] = (float)((double)x[r * width + c] * inv * (double)w[c]);
+    }
+    return 0;
+}
+
+static const void* grid_for(const vlo_moe_layer* L, uint32_t type) {
+    switch (type) {
+        case VLO_TYPE_IQ1_S: return L->grid_iq1_s;
+        case VLO_TYPE_IQ2_XXS: return L->grid_iq2_xxs;
+        case VLO_TYPE_IQ3_XXS: return L->grid_iq3_xxs;
+        default: return NULL;
+    }
+}
+
+static int mv(const vlo_moe_layer* L, const vlo_matrix* m, const float* x, float* y) {
+    return vlo_matvec(m->type, m->data, m->rows, m->cols, x, y, grid_for(L, m->type));
+}
+
+/* execute_expert, deepseek_v4_graph.cpp:1826-1895, for one token: gate and up products, SwiGLU
+ * in double with the optional clamp, route weight applied BEFORE the down product. */
+static int v4_expert(const vlo_moe_layer* L, const vlo_matrix* w1, const vlo_matrix* w3,
+                     const vlo_matrix* w2, const float* x, const float* route_w, float limit,
+                     float* gate, float* up, float* act, float* out) {
+    int st = mv(L, w1, x, gate);
+    if (!st) st = mv(L, w3, x, up);
+    if (st) return st;
+    for (size_t c = 0; c < L->intermediate; ++c) {
+        double g = (double)gate[c];
+        double u = (double)up[c];
+        if (limit > 0.0f) {
+            if (g > (double)limit) g = (double)limit;
+            if (u < -(double)limit) u = -(double)limit;
+            if (u > (double)limit) u = (double)limit;
+        }
+        double v = g / (1.0 + exp(-g)) * u;
+        if (route_w) v *= (double)*route_w;
+        act[c] = (float)v;
+    }
+    return mv(L, w2, act, out);
+}
+
+/* OLMoE expert, olmoe_runtime.cpp:1276-1281: SwiGLU in float with expf. */
+static int olmoe_expert(const vlo_moe_layer* L, const vlo_matrix* w1, const vlo_matrix* w3,
+                        const vlo_matrix* w2, const float* x, float* gate, float* up,
+                        float* act, float* out) {
+    int st = mv(L, w1, x, gate);
+    if (!st) st = mv(L, w3, x, up);
+    if (st) return st;
+    for (size_t c = 0; c < L->intermediate; ++c)
+        act[c] = (gate[c] / (1.0f + expf(-gate[c]))) * up[c];
+    return mv(L, w2, act, out);
+}
+
+/* moe_forward, deepseek_v4_graph.cpp:1902-2274 (DeepSeek V4: route, shared expert over all
+ * tokens, routed experts in ascending id / token / slot order with float +=, shared added last),
+ * and the OLMoE layer loop, olmoe_runtime.cpp:1119-1290 (rank-order combine, weight after down,
+ * no shared expert). */
+int vlo_moe_forward(const vlo_moe_layer* L, const float* x, const uint32_t* token_ids,
+                    size_t T, const float* logits_in, float* out, uint32_t* idx,
+                    float* weights) {
+    const size_t H = L->hidden, I = L->intermediate, E = L->experts, k = L->top_k;
+    float* logits = (float*)malloc(T * E * sizeof(float));
+    float* gate = (float*)malloc(I * sizeof(float));
+    float* up = (float*)malloc(I * sizeof(float));
+    float* act = (float*)malloc(I * sizeof(float));
+    float* eo = (float*)malloc(H * sizeof(float));
+    int st = 0;
+    if (logits_in) memcpy(logits, logits_in, T * E * sizeof(float));
+    else vlo_router_logits(x, L->router, T, H, E, logits);
+    if (L->score == VLO_SCORE_SOFTMAX) st = vlo_route_softmax(logits, T, E, k, idx, weights);
+    else if (L->hash_routing)
+        st = vlo_route_hash(logits, token_ids, L->tid2eid, T, L->vocab, E, k, L->route_scale,
+                            L->score, idx, weights);
+    else
+        st = vlo_route_learned(logits, L->bias, T, E, k, L->route_scale, L->score, idx, weights);
+    memset(out, 0, T * H * sizeof(float));
+    if (!st && L->weight_after_down) {
+        for (size_t t = 0; t < T && !st; ++t)
+            for (size_t s = 0; s < k && !st; ++s) {
+                const uint32_t e = idx[t * k + s];
+                st = olmoe_expert(L, &L->w1[e], &L->w3[e], &L->w2[e], x + t * H, gate, up, act,
+                                  eo);
+                const float w = weights[t * k + s];
+                for (size_t c = 0; c < H && !st; ++c) out[t * H + c] += w * eo[c];
+            }
+    } else if (!st) {
+        float* shared = NULL;
+        if (L->shared_w1) {
+            shared = (float*)malloc(T * H * sizeof(float));
+            for (size_t t = 0; t < T && !st; ++t)
+                st = v4_expert(L, L->shared_w1, L->shared_w3, L->shared_w2, x + t * H, NULL,
+                               L->shared_swiglu_limit, gate, up, act, shared + t * H);
+        }
+        for (size_t e = 0; e < E && !st; ++e)
+            for (size_t t = 0; t < T && !st; ++t)
+                for (size_t s = 0; s < k && !st; ++s) {
+                    if (idx[t * k + s] != e) continue;
+                    st = v4_expert(L, &L->w1[e], &L->w3[e], &L->w2[e], x + t * H,
+                                   &weights[t * k + s], L->routed_swiglu_limit, gate, up, act, eo);
+                    for (size_t c = 0; c < H && !st; ++c) out[t * H + c] += eo[c];
+                }
+        if (shared && !st)
+            for (size_t i = 0; i < T * H; ++i) out[i] += shared[i];
+        free(shared);
+    }
+    free(logits); free(gate); free(up); free(act); free(eo);
+    return st;
+}

@@ -1,0 +1,528 @@
+"""vastloom_b200 - B200 (sm_100a) MoE routed-expert path behind the vlb200 C ABI.
+
+This package is the Python host mirror of vastloom's operator surface for the routed-expert hot
+path. Every call goes through the C ABI of ``libvlb200.so`` (``include/vlb200.h``); there is no
+CPU fallback: importing works without a GPU, but opening a device fails loudly when the CUDA
+library or a B200 is missing.
+
+Reference interfaces mirrored here (vastloom source paths):
+  * ``Device.matvec``            DeepseekV4MatvecAccelerator::matvec
+                                 (include/vastloom/inference/deepseek_v4_reference.hpp:440-451)
+  * ``Device.dequantize``        dequantize_q8_0/_iq2_xxs/_iq3_xxs/_iq1_s
+                                 (include/vastloom/inference/ggml_quantization.hpp:98-297)
+  * ``Device.route``             deepseek_v4_route_learned_logits / _hash_logits
+                                 (include/vastloom/inference/deepseek_v4_reference.hpp:634-650)
+  * ``MoeLayer.forward``         moe_forward (src/inference/deepseek_v4_graph.cpp:1902-2274) and
+                                 the OLMoE layer loop (src/inference/olmoe_runtime.cpp:1119-1290)
+Errors raise ``VlbError`` whose ``code`` names the reference ErrorCode
+(include/vastloom/core/status.hpp:10-21).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional, Sequence
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libvlb200.so"
+GRIDS_PATH = _PKG / "data" / "iq_grids.bin"
+
+TYPE_F32 = 0
+TYPE_Q8_0 = 8
+TYPE_IQ2_XXS = 16
+TYPE_IQ3_XXS = 18
+TYPE_IQ1_S = 19
+
+SCORE_SQRT_SOFTPLUS = 0
+SCORE_SIGMOID = 1
+SCORE_SOFTMAX = 2
+
+# (weights per block, ggml block bytes) - ggml_quantization.hpp:12-31
+BLOCK_LAYOUT = {
+    TYPE_Q8_0: (32, 34),
+    TYPE_IQ2_XXS: (256, 66),
+    TYPE_IQ3_XXS: (256, 98),
+    TYPE_IQ1_S: (256, 50),
+}
+
+ERROR_CODES = {
+    0: "ok",
+    1: "invalid_argument",
+    2: "invalid_format",
+    3: "not_found",
+    4: "permission_denied",
+    5: "io_error",
+    6: "integrity_error",
+    7: "unsafe_path",
+    8: "unsupported",
+    9: "resource_exhausted",
+    10: "internal_error",
+    100: "declined",
+}
+
+
+class VlbError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        self.status = status
+        self.code = ERROR_CODES.get(status, f"status_{status}")
+        super().__init__(f"{self.code}: {message}")
+
+
+def matrix_bytes(ggml_type: int, rows: int, cols: int) -> int:
+    be, bb = BLOCK_LAYOUT[ggml_type]
+    if cols % be:
+        raise ValueError("columns must be a multiple of the block size")
+    return rows * (cols // be) * bb
+
+
+class _DeviceInfo(C.Structure):
+    _fields_ = [
+        ("ordinal", C.c_int),
+        ("sm_count", C.c_int),
+        ("cc_major", C.c_int),
+        ("cc_minor", C.c_int),
+        ("total_bytes", C.c_uint64),
+        ("free_bytes", C.c_uint64),
+        ("name", C.c_char * 96),
+    ]
+
+
+RESERVE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_uint64, C.c_char_p)
+RELEASE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_uint64, C.c_char_p)
+
+
+class _Governor(C.Structure):
+    _fields_ = [("ctx", C.c_void_p), ("reserve", RESERVE_FN), ("release", RELEASE_FN)]
+
+
+class _LayerDesc(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_uint32),
+        ("intermediate", C.c_uint32),
+        ("experts", C.c_uint32),
+        ("top_k", C.c_uint32),
+        ("score", C.c_int),
+        ("hash_routing", C.c_int),
+        ("weight_after_down", C.c_int),
+        ("route_scale", C.c_float),
+        ("routed_swiglu_limit", C.c_float),
+        ("shared_swiglu_limit", C.c_float),
+        ("max_tokens", C.c_uint32),
+        ("vocab", C.c_uint32),
+        ("router", C.c_void_p),
+        ("bias", C.c_void_p),
+        ("tid2eid", C.c_void_p),
+        ("w1", C.c_void_p),
+        ("w3", C.c_void_p),
+        ("w2", C.c_void_p),
+        ("shared_w1", C.c_void_p),
+        ("shared_w3", C.c_void_p),
+        ("shared_w2", C.c_void_p),
+    ]
+
+
+_lib: Optional[C.CDLL] = None
+
+# exported symbols of include/vlb200.h (checked by the CPU test suite)
+EXPORTS = (
+    "vlb_abi_version vlb_thread_error vlb_device_count vlb_probe vlb_open vlb_close "
+    "vlb_last_error vlb_stream vlb_synchronize vlb_set_codebook vlb_alloc vlb_free "
+    "vlb_memcpy_h2d vlb_memcpy_d2h vlb_allocated_bytes vlb_upload_matrix vlb_release_matrix "
+    "vlb_matrix_bytes vlb_matvec vlb_matvec_device vlb_dequantize_device vlb_layer_create "
+    "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
+    "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_route_device vlb_router_logits_device vlb_rms_norm_device"
+).split()
+
+
+def load_library() -> C.CDLL:
+    """Loads libvlb200.so. Raises when it has not been built: there is no fallback path."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m vastloom_b200.build` "
+            "(the MoE path has no CPU fallback)")
+    lib = C.CDLL(str(LIB_PATH))
+    P, U32, U64, SZ, I, F = C.c_void_p, C.c_uint32, C.c_uint64, C.c_size_t, C.c_int, C.c_float
+    sig = {
+        "vlb_abi_version": (I, []),
+        "vlb_thread_error": (I, [C.c_char_p, SZ]),
+        "vlb_device_count": (I, [C.POINTER(C.c_int)]),
+        "vlb_probe": (I, [I, C.POINTER(_DeviceInfo)]),
+        "vlb_open": (I, [I, P, U64, C.POINTER(P)]),
+        "vlb_close": (None, [P]),
+        "vlb_last_error": (I, [P, C.c_char_p, SZ]),
+        "vlb_stream": (P, [P]),
+        "vlb_synchronize": (I, [P]),
+        "vlb_set_codebook": (I, [P, U32, P, SZ]),
+        "vlb_alloc": (I, [P, SZ, C.c_char_p, C.POINTER(P)]),
+        "vlb_free": (I, [P, P]),
+        "vlb_memcpy_h2d": (I, [P, P, P, SZ]),
+        "vlb_memcpy_d2h": (I, [P, P, P, SZ]),
+        "vlb_allocated_bytes": (U64, [P]),
+        "vlb_upload_matrix": (I, [P, U64, U32, SZ, SZ, P, SZ, C.POINTER(P)]),
+        "vlb_release_matrix": (I, [P, P]),
+        "vlb_matrix_bytes": (U64, [P]),
+        "vlb_matvec": (I, [P, P, P, P]),
+        "vlb_matvec_device": (I, [P, P, P, SZ, SZ, P, SZ, P]),
+        "vlb_dequantize_device": (I, [P, P, P, P]),
+        "vlb_layer_create": (I, [P, C.POINTER(_LayerDesc), C.POINTER(P)]),
+        "vlb_layer_destroy": (I, [P, P]),
+        "vlb_layer_forward_device": (I, [P, P, P, P, P, U32, P, P]),
+        "vlb_layer_forward": (I, [P, P, P, P, P, U32, P]),
+        "vlb_layer_last_route": (I, [P, P, U32, P, P, P, P, P]),
+        "vlb_layer_last_weight_bytes": (U64, [P, P]),
+        "vlb_layer_set_profiling": (I, [P, P, I]),
+        "vlb_layer_phase_times": (I, [P, P, C.POINTER(C.c_float), I]),
+        "vlb_route_device": (I, [P, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
+        "vlb_router_logits_device": (I, [P, P, P, U32, U32, U32, P, P]),
+        "vlb_rms_norm_device": (I, [P, P, P, U32, U32, F, P, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    assert a.flags["C_CONTIGUOUS"]
+    return C.c_void_p(a.ctypes.data)
+
+
+def read_codebooks(path: Path = GRIDS_PATH) -> dict[int, bytes]:
+    """Reads the codebook data file written at build time (see csrc/gen_codebooks.cpp)."""
+    raw = Path(path).read_bytes()
+    if raw[:8] != b"VLBGRID1":
+        raise VlbError(2, f"{path} is not a codebook file")
+    (count,) = struct.unpack_from("<I", raw, 8)
+    off = 12
+    out = {}
+    for _ in range(count):
+        t, n, _fp = struct.unpack_from("<IIQ", raw, off)
+        off += 16
+        out[t] = raw[off: off + n]
+        off += n
+    return out
+
+
+def device_count() -> int:
+    lib = load_library()
+    n = C.c_int(0)
+    st = lib.vlb_device_count(C.byref(n))
+    return n.value if st == 0 else 0
+
+
+@dataclass
+class Matrix:
+    ptr: C.c_void_p
+    ggml_type: int
+    rows: int
+    cols: int
+    identity: int
+    payload_bytes: int
+
+
+class DeviceBuffer:
+    """A governed device allocation owned by a Device."""
+
+    def __init__(self, dev: "Device", nbytes: int, tag: str = "py-buffer"):
+        self.dev = dev
+        self.nbytes = nbytes
+        p = C.c_void_p()
+        dev._check(dev.lib.vlb_alloc(dev.h, nbytes, tag.encode(), C.byref(p)))
+        self.ptr = p
+
+    @property
+    def address(self) -> int:
+        return self.ptr.value or 0
+
+    def upload(self, a: np.ndarray) -> "DeviceBuffer":
+        a = np.ascontiguousarray(a)
+        assert a.nbytes <= self.nbytes
+        self.dev._check(self.dev.lib.vlb_memcpy_h2d(self.dev.h, self.ptr, _ptr(a), a.nbytes))
+        return self
+
+    def download(self, dtype, count: int) -> np.ndarray:
+        out = np.empty(count, dtype=dtype)
+        self.dev._check(self.dev.lib.vlb_memcpy_d2h(self.dev.h, _ptr(out), self.ptr, out.nbytes))
+        return out
+
+    def free(self) -> None:
+        if self.ptr:
+            self.dev._check(self.dev.lib.vlb_free(self.dev.h, self.ptr))
+            self.ptr = C.c_void_p()
+
+
+class Device:
+    """One vlb200 handle on one GPU (cf. CudaMatvecAccelerator::create,
+    src/cuda/cuda_matvec_accelerator.cpp:68-90)."""
+
+    def __init__(self, ordinal: int = 0, governor=None, min_free_after: int = 0,
+                 install_codebooks: bool = True):
+        self.lib = load_library()
+        self._gov_keep = None
+        gov_ptr = None
+        if governor is not None:
+            # governor: object with reserve(bytes, tag) -> bool and release(bytes, tag)
+            def _res(_ctx, n, tag):
+                return 0 if governor.reserve(int(n), tag.decode() if tag else "") else 1
+
+            def _rel(_ctx, n, tag):
+                governor.release(int(n), tag.decode() if tag else "")
+
+            g = _Governor(None, RESERVE_FN(_res), RELEASE_FN(_rel))
+            self._gov_keep = g
+            gov_ptr = C.byref(g)
+        h = C.c_void_p()
+        st = self.lib.vlb_open(ordinal, gov_ptr, min_free_after, C.byref(h))
+        if st != 0:
+            buf = C.create_string_buffer(512)
+            self.lib.vlb_thread_error(buf, 512)
+            raise VlbError(st, buf.value.decode())
+        self.h = h
+        self.ordinal = ordinal
+        if install_codebooks:
+            for t, table in read_codebooks().items():
+                self.set_codebook(t, table)
+
+    # -- plumbing --
+    def _check(self, st: int) -> None:
+        if st != 0:
+            buf = C.create_string_buffer(1024)
+            self.lib.vlb_last_error(self.h, buf, 1024)
+            raise VlbError(st, buf.value.decode())
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.vlb_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def stream(self) -> int:
+        return self.lib.vlb_stream(self.h) or 0
+
+    def synchronize(self) -> None:
+        self._check(self.lib.vlb_synchronize(self.h))
+
+    def allocated_bytes(self) -> int:
+        return int(self.lib.vlb_allocated_bytes(self.h))
+
+    def buffer(self, nbytes: int, tag: str = "py-buffer") -> DeviceBuffer:
+        return DeviceBuffer(self, nbytes, tag)
+
+    def to_device(self, a: np.ndarray, tag: str = "py-buffer") -> DeviceBuffer:
+        a = np.ascontiguousarray(a)
+        return DeviceBuffer(self, max(a.nbytes, 4), tag).upload(a)
+
+    # -- operators --
+    def set_codebook(self, ggml_type: int, table: bytes) -> None:
+        b = (C.c_char * len(table)).from_buffer_copy(table)
+        self._check(self.lib.vlb_set_codebook(self.h, ggml_type, C.cast(b, C.c_void_p), len(table)))
+
+    def upload_matrix(self, ggml_type: int, rows: int, cols: int, payload, identity: int = 1) -> Matrix:
+        payload = np.ascontiguousarray(np.frombuffer(payload, dtype=np.uint8) if isinstance(payload, (bytes, bytearray)) else payload)
+        m = C.c_void_p()
+        self._check(self.lib.vlb_upload_matrix(self.h, identity, ggml_type, rows, cols, _ptr(payload),
+                                               payload.nbytes, C.byref(m)))
+        return Matrix(m, ggml_type, rows, cols, identity, int(payload.nbytes))
+
+    def release_matrix(self, m: Matrix) -> None:
+        if m.ptr:
+            self._check(self.lib.vlb_release_matrix(self.h, m.ptr))
+            m.ptr = C.c_void_p()
+
+    def matvec(self, m: Matrix, x: np.ndarray) -> np.ndarray:
+        """The per-row seam (host input of storage_cols floats, host output of rows floats)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.shape != (m.cols,):
+            raise ValueError("input must have storage_columns elements")
+        y = np.empty(m.rows, dtype=np.float32)
+        self._check(self.lib.vlb_matvec(self.h, m.ptr, _ptr(x), _ptr(y)))
+        return y
+
+    def matvec_tokens(self, m: Matrix, x: np.ndarray) -> np.ndarray:
+        """Multi-token product through the device entry point: x [n, cols] -> y [n, rows]."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n = x.shape[0]
+        xb = self.to_device(x, "py-x")
+        yb = self.buffer(n * m.rows * 4, "py-y")
+        try:
+            self._check(self.lib.vlb_matvec_device(self.h, m.ptr, xb.ptr, n, m.cols, yb.ptr, m.rows, None))
+            return yb.download(np.float32, n * m.rows).reshape(n, m.rows)
+        finally:
+            xb.free()
+            yb.free()
+
+    def dequantize(self, m: Matrix) -> np.ndarray:
+        ob = self.buffer(m.rows * m.cols * 4, "py-dequant")
+        try:
+            self._check(self.lib.vlb_dequantize_device(self.h, m.ptr, ob.ptr, None))
+            return ob.download(np.float32, m.rows * m.cols).reshape(m.rows, m.cols)
+        finally:
+            ob.free()
+
+    def route(self, logits: np.ndarray, top_k: int, route_scale: float = 1.0,
+              score: int = SCORE_SQRT_SOFTPLUS, bias: Optional[np.ndarray] = None,
+              token_ids: Optional[np.ndarray] = None, tid2eid: Optional[np.ndarray] = None):
+        """deepseek_v4_route_learned_logits / deepseek_v4_route_hash_logits (and the OLMoE
+        softmax router with score=SCORE_SOFTMAX) on the device. Returns (indices, weights)."""
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        T, E = logits.shape
+        bufs = [self.to_device(logits, "py-logits")]
+        bias_b = tok_b = tab_b = None
+        if bias is not None:
+            bias_b = self.to_device(np.ascontiguousarray(bias, dtype=np.float32), "py-bias")
+            bufs.append(bias_b)
+        hashing = tid2eid is not None
+        vocab = 0
+        if hashing:
+            tab = np.ascontiguousarray(tid2eid, dtype=np.uint32)
+            vocab = tab.size // top_k
+            tok_b = self.to_device(np.ascontiguousarray(token_ids, dtype=np.uint32), "py-tokens")
+            tab_b = self.to_device(tab, "py-tid2eid")
+            bufs += [tok_b, tab_b]
+        idx_b = self.buffer(T * top_k * 4, "py-idx")
+        w_b = self.buffer(T * top_k * 4, "py-w")
+        bufs += [idx_b, w_b]
+        try:
+            self._check(self.lib.vlb_route_device(
+                self.h, score, 1 if hashing else 0, bufs[0].ptr, bias_b.ptr if bias_b else None,
+                tok_b.ptr if tok_b else None, tab_b.ptr if tab_b else None, vocab, T, E, top_k,
+                route_scale, idx_b.ptr, w_b.ptr, None))
+            idx = idx_b.download(np.uint32, T * top_k).reshape(T, top_k)
+            w = w_b.download(np.float32, T * top_k).reshape(T, top_k)
+            return idx, w
+        finally:
+            for b in bufs:
+                b.free()
+
+    def router_logits(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        T, H = x.shape
+        E = w.shape[0]
+        xb, wb, lb = self.to_device(x), self.to_device(w), self.buffer(T * E * 4)
+        try:
+            self._check(self.lib.vlb_router_logits_device(self.h, xb.ptr, wb.ptr, T, H, E, lb.ptr, None))
+            return lb.download(np.float32, T * E).reshape(T, E)
+        finally:
+            for b in (xb, wb, lb):
+                b.free()
+
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, width = x.shape
+        xb, wb, ob = self.to_device(x), self.to_device(np.ascontiguousarray(w, dtype=np.float32)), self.buffer(x.nbytes)
+        try:
+            self._check(self.lib.vlb_rms_norm_device(self.h, xb.ptr, wb.ptr, rows, width, eps, ob.ptr, None))
+            self.synchronize()
+            return ob.download(np.float32, rows * width).reshape(rows, width)
+        finally:
+            for b in (xb, wb, ob):
+                b.free()
+
+
+class MoeLayer:
+    """One resident MoE layer (router, routed experts, optional shared expert)."""
+
+    def __init__(self, dev: Device, *, hidden: int, intermediate: int, experts: int, top_k: int,
+                 router: np.ndarray, w1: Sequence[Matrix], w3: Sequence[Matrix],
+                 w2: Sequence[Matrix], score: int = SCORE_SQRT_SOFTPLUS,
+                 bias: Optional[np.ndarray] = None, route_scale: float = 1.0,
+                 hash_table: Optional[np.ndarray] = None, weight_after_down: bool = False,
+                 routed_swiglu_limit: float = 0.0, shared_swiglu_limit: float = 0.0,
+                 shared: Optional[tuple[Matrix, Matrix, Matrix]] = None, max_tokens: int = 64):
+        self.dev = dev
+        self.H, self.I, self.E, self.k = hidden, intermediate, experts, top_k
+        self.max_tokens = max_tokens
+        self._router = np.ascontiguousarray(router, dtype=np.float32)
+        self._bias = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._table = None if hash_table is None else np.ascontiguousarray(hash_table, dtype=np.uint32)
+        arr = C.c_void_p * experts
+        self._w1 = arr(*[m.ptr.value for m in w1])
+        self._w3 = arr(*[m.ptr.value for m in w3])
+        self._w2 = arr(*[m.ptr.value for m in w2])
+        d = _LayerDesc()
+        d.hidden, d.intermediate, d.experts, d.top_k = hidden, intermediate, experts, top_k
+        d.score = score
+        d.hash_routing = 1 if hash_table is not None else 0
+        d.weight_after_down = 1 if weight_after_down else 0
+        d.route_scale = route_scale
+        d.routed_swiglu_limit = routed_swiglu_limit
+        d.shared_swiglu_limit = shared_swiglu_limit
+        d.max_tokens = max_tokens
+        d.vocab = 0 if self._table is None else self._table.size // top_k
+        d.router = self._router.ctypes.data
+        d.bias = None if self._bias is None else self._bias.ctypes.data
+        d.tid2eid = None if self._table is None else self._table.ctypes.data
+        d.w1 = C.cast(self._w1, C.c_void_p)
+        d.w3 = C.cast(self._w3, C.c_void_p)
+        d.w2 = C.cast(self._w2, C.c_void_p)
+        if shared is not None:
+            d.shared_w1, d.shared_w3, d.shared_w2 = (m.ptr.value for m in shared)
+        p = C.c_void_p()
+        dev._check(dev.lib.vlb_layer_create(dev.h, C.byref(d), C.byref(p)))
+        self.ptr = p
+
+    def forward(self, x: np.ndarray, token_ids: Optional[np.ndarray] = None,
+                logits: Optional[np.ndarray] = None) -> np.ndarray:
+        """Host-memory forward (H2D inputs, layer, D2H output) - the end-to-end call."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        out = np.empty((T, self.H), dtype=np.float32)
+        tok = None if token_ids is None else np.ascontiguousarray(token_ids, dtype=np.uint32)
+        lg = None if logits is None else np.ascontiguousarray(logits, dtype=np.float32)
+        self.dev._check(self.dev.lib.vlb_layer_forward(
+            self.dev.h, self.ptr, _ptr(x), None if tok is None else _ptr(tok),
+            None if lg is None else _ptr(lg), T, _ptr(out)))
+        return out
+
+    def forward_device(self, x_ptr: int, T: int, out_ptr: int, token_ids_ptr: int = 0,
+                       logits_ptr: int = 0, stream: int = 0) -> None:
+        """Device-resident forward on raw device pointers, enqueued on `stream`."""
+        self.dev._check(self.dev.lib.vlb_layer_forward_device(
+            self.dev.h, self.ptr, C.c_void_p(x_ptr), C.c_void_p(token_ids_ptr or None),
+            C.c_void_p(logits_ptr or None), T, C.c_void_p(out_ptr), C.c_void_p(stream or None)))
+
+    def last_route(self, T: int):
+        n = T * self.k
+        idx = np.empty(n, np.uint32)
+        w = np.empty(n, np.float32)
+        off = np.empty(self.E + 1, np.uint32)
+        pt = np.empty(n, np.uint32)
+        ps = np.empty(n, np.uint32)
+        self.dev._check(self.dev.lib.vlb_layer_last_route(self.dev.h, self.ptr, T, _ptr(idx), _ptr(w),
+                                                          _ptr(off), _ptr(pt), _ptr(ps)))
+        return idx.reshape(T, self.k), w.reshape(T, self.k), off, pt, ps
+
+    PHASES = ("route", "dispatch", "gate_up", "down", "combine")
+
+    def set_profiling(self, enable: bool) -> None:
+        self.dev._check(self.dev.lib.vlb_layer_set_profiling(self.dev.h, self.ptr, 1 if enable else 0))
+
+    def phase_times(self) -> dict:
+        ms = (C.c_float * 5)()
+        self.dev._check(self.dev.lib.vlb_layer_phase_times(self.dev.h, self.ptr, ms, 5))
+        return dict(zip(self.PHASES, [float(v) for v in ms]))
+
+    def last_weight_bytes(self) -> int:
+        return int(self.dev.lib.vlb_layer_last_weight_bytes(self.dev.h, self.ptr))
+
+    def destroy(self) -> None:
+        if self.ptr:
+            self.dev._check(self.dev.lib.vlb_layer_destroy(self.dev.h, self.ptr))
+            self.ptr = C.c_void_p()

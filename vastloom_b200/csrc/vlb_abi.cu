@@ -1,0 +1,781 @@
+// Host side of the vlb200 C ABI (include/vlb200.h): device handles, governed allocations,
+// codebook installation, resident matrices, MoE layer objects and their forward calls.
+//
+// Replaces the reference's driver boundary (src/cuda/cuda_driver.cpp) and the device half of
+// its accelerator (src/cuda/cuda_matvec_accelerator.cpp); see the header for the contract.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "vlb_launch.h"
+
+using namespace vlb;
+
+namespace {
+
+thread_local std::string t_error;
+
+int copy_message(const std::string& msg, char* buf, size_t cap) {
+    if (!buf || cap == 0) return VLB_ERR_INVALID_ARGUMENT;
+    const size_t n = msg.size() < cap - 1 ? msg.size() : cap - 1;
+    std::memcpy(buf, msg.data(), n);
+    buf[n] = '\0';
+    return VLB_OK;
+}
+
+// Pinned codebook fingerprints: FNV-1a over the table bytes, ggml_quantization.cpp:49-99.
+constexpr uint64_t kFpIq1S = 0x6703ed863501ae2eull;
+constexpr uint64_t kFpIq2Xxs = 0xbb4ee025b5ac6e8eull;
+constexpr uint64_t kFpIq3Xxs = 0xdfa5dc83d6a155d5ull;
+
+uint64_t fnv1a(const void* p, size_t n) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    uint64_t h = 14695981039346656037ull;
+    for (size_t i = 0; i < n; ++i) {
+        h ^= b[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+// CUDA failures become io_error with the call and CUDA's own description (the reference's
+// cuda_error, cuda_driver.cpp:2727-2738).
+std::string cuda_msg(const char* op, cudaError_t e) {
+    return std::string("CUDA call failed: ") + op + " (status=" + std::to_string((int)e) + ", " +
+           cudaGetErrorName(e) + ": " + cudaGetErrorString(e) + ")";
+}
+
+}  // namespace
+
+struct vlb_handle {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    vlb_governor gov{};
+    bool has_gov = false;
+    uint64_t min_free_after = 0;
+    std::mutex mu;
+    std::string err;
+    uint64_t* grid_iq1s = nullptr;
+    uint64_t* grid_iq2xxs = nullptr;
+    uint32_t* grid_iq3xxs = nullptr;
+    struct Alloc {
+        size_t bytes;
+        std::string tag;
+    };
+    std::unordered_map<void*, Alloc> allocs;
+    uint64_t allocated = 0;
+    float* seam_x = nullptr;
+    float* seam_y = nullptr;
+    size_t seam_x_cap = 0, seam_y_cap = 0;
+
+    int fail(int code, std::string msg) {
+        err = std::move(msg);
+        return code;
+    }
+    int cuda_fail(const char* op, cudaError_t e) {
+        (void)cudaGetLastError();  // clear a sticky launch error so the handle stays usable
+        return fail(VLB_ERR_IO_ERROR, cuda_msg(op, e));
+    }
+    Grids grids() const { return Grids{grid_iq1s, grid_iq2xxs, grid_iq3xxs}; }
+    cudaStream_t pick(void* s) const { return s ? static_cast<cudaStream_t>(s) : stream; }
+
+    // Governor-first allocation (CudaDriver::allocate, cuda_driver.cpp:2929-3005): reserve the
+    // exact bytes, check live free memory against the configured floor, then allocate; every
+    // failure after a successful reserve releases it again.
+    int galloc(size_t bytes, const char* tag, void** out) {
+        *out = nullptr;
+        if (bytes == 0) return fail(VLB_ERR_INVALID_ARGUMENT, "zero-byte device allocation");
+        if (has_gov && gov.reserve && gov.reserve(gov.ctx, bytes, tag) != 0)
+            return fail(VLB_ERR_RESOURCE_EXHAUSTED,
+                        std::string("governor refused the device reservation: ") + tag);
+        size_t free_b = 0, total_b = 0;
+        cudaError_t e = cudaMemGetInfo(&free_b, &total_b);
+        if (e != cudaSuccess) {
+            if (has_gov && gov.release) gov.release(gov.ctx, bytes, tag);
+            return cuda_fail("cudaMemGetInfo", e);
+        }
+        if ((uint64_t)free_b < (uint64_t)bytes + min_free_after) {
+            if (has_gov && gov.release) gov.release(gov.ctx, bytes, tag);
+            return fail(VLB_ERR_RESOURCE_EXHAUSTED,
+                        std::string("device allocation would cross the free-memory floor: ") + tag);
+        }
+        e = cudaMalloc(out, bytes);
+        if (e != cudaSuccess) {
+            *out = nullptr;
+            if (has_gov && gov.release) gov.release(gov.ctx, bytes, tag);
+            return cuda_fail("cudaMalloc", e);
+        }
+        allocs[*out] = Alloc{bytes, tag};
+        allocated += bytes;
+        return VLB_OK;
+    }
+    int gfree(void* p) {
+        if (!p) return VLB_OK;
+        auto it = allocs.find(p);
+        if (it == allocs.end()) return fail(VLB_ERR_NOT_FOUND, "pointer is not a live allocation");
+        cudaError_t e = cudaFree(p);
+        if (e != cudaSuccess) {
+            // Keep it accounted: a failed release must not hand the bytes back
+            // (cuda_driver.cpp:2881-2894).
+            return cuda_fail("cudaFree", e);
+        }
+        if (has_gov && gov.release) gov.release(gov.ctx, it->second.bytes, it->second.tag.c_str());
+        allocated -= it->second.bytes;
+        allocs.erase(it);
+        return VLB_OK;
+    }
+};
+
+struct vlb_matrix {
+    vlb_handle* owner = nullptr;
+    uint64_t identity = 0;
+    uint32_t type = 0;
+    size_t rows = 0, cols = 0;
+    uint32_t bpr = 0;
+    void* mem = nullptr;
+    size_t bytes = 0;  // resident bytes (scales + bodies)
+    size_t payload_bytes = 0;
+    DevMat dm{};
+};
+
+struct vlb_layer {
+    vlb_moe_layer_desc desc{};
+    bool has_shared = false;
+    float* router = nullptr;
+    float* bias = nullptr;
+    uint32_t* tid2eid = nullptr;
+    DevMat* mats = nullptr;
+    std::vector<const vlb_matrix*> host_mats;  // [3 x (E+1)]
+    // workspace
+    void* ws = nullptr;
+    MoeParams p{};
+    uint32_t last_T = 0;
+    bool last_logits_given = false;
+    // staging for the host-memory forward
+    float* x_dev = nullptr;
+    uint32_t* tok_dev = nullptr;
+    float* logits_dev = nullptr;
+    float* out_dev = nullptr;
+    // optional phase timing (vlb_layer_set_profiling)
+    bool profiling = false;
+    cudaEvent_t ev[kMoePhases + 1] = {};
+};
+
+#define VLB_LOCK(h)                                                                     \
+    if (!(h)) {                                                                          \
+        t_error = "null handle";                                                         \
+        return VLB_ERR_INVALID_ARGUMENT;                                                 \
+    }                                                                                    \
+    std::lock_guard<std::mutex> _vlb_lock((h)->mu);                                      \
+    {                                                                                    \
+        cudaError_t _e = cudaSetDevice((h)->device);                                     \
+        if (_e != cudaSuccess) return (h)->cuda_fail("cudaSetDevice", _e);               \
+    }
+
+#define VLB_CUDA(h, call)                                    \
+    do {                                                     \
+        cudaError_t _e = (call);                             \
+        if (_e != cudaSuccess) return (h)->cuda_fail(#call, _e); \
+    } while (0)
+
+extern "C" {
+
+int vlb_abi_version(void) { return VLB_ABI_VERSION; }
+
+int vlb_thread_error(char* buf, size_t cap) { return copy_message(t_error, buf, cap); }
+
+int vlb_device_count(int* count) {
+    if (!count) return VLB_ERR_INVALID_ARGUMENT;
+    *count = 0;
+    cudaError_t e = cudaGetDeviceCount(count);
+    if (e != cudaSuccess) {
+        *count = 0;
+        (void)cudaGetLastError();
+        t_error = cuda_msg("cudaGetDeviceCount", e);
+        return VLB_ERR_NOT_FOUND;
+    }
+    return VLB_OK;
+}
+
+int vlb_probe(int ordinal, vlb_device_info* info) {
+    if (!info) return VLB_ERR_INVALID_ARGUMENT;
+    int n = 0;
+    if (vlb_device_count(&n) != VLB_OK || ordinal < 0 || ordinal >= n) {
+        t_error = "CUDA device ordinal is not present";
+        return VLB_ERR_NOT_FOUND;
+    }
+    cudaDeviceProp prop{};
+    cudaError_t e = cudaGetDeviceProperties(&prop, ordinal);
+    if (e != cudaSuccess) {
+        t_error = cuda_msg("cudaGetDeviceProperties", e);
+        return VLB_ERR_IO_ERROR;
+    }
+    std::memset(info, 0, sizeof(*info));
+    info->ordinal = ordinal;
+    info->sm_count = prop.multiProcessorCount;
+    info->cc_major = prop.major;
+    info->cc_minor = prop.minor;
+    info->total_bytes = prop.totalGlobalMem;
+    std::snprintf(info->name, sizeof(info->name), "%s", prop.name);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(ordinal) == cudaSuccess) {
+        size_t f = 0, t = 0;
+        if (cudaMemGetInfo(&f, &t) == cudaSuccess) info->free_bytes = f;
+        cudaSetDevice(prev);
+    }
+    return VLB_OK;
+}
+
+int vlb_open(int ordinal, const vlb_governor* governor, uint64_t min_free_after,
+             vlb_handle** out) {
+    if (!out) {
+        t_error = "null output handle";
+        return VLB_ERR_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    vlb_device_info info{};
+    int st = vlb_probe(ordinal, &info);
+    if (st != VLB_OK) return st;
+    if (info.cc_major != 10) {
+        t_error = "this library is built for sm_100a (B200); device compute capability is " +
+                  std::to_string(info.cc_major) + "." + std::to_string(info.cc_minor);
+        return VLB_ERR_UNSUPPORTED;
+    }
+    vlb_handle* h = new (std::nothrow) vlb_handle();
+    if (!h) {
+        t_error = "unable to allocate the handle";
+        return VLB_ERR_RESOURCE_EXHAUSTED;
+    }
+    h->device = ordinal;
+    h->min_free_after = min_free_after;
+    if (governor) {
+        h->gov = *governor;
+        h->has_gov = true;
+    }
+    cudaError_t e = cudaSetDevice(ordinal);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        t_error = cuda_msg("cudaStreamCreate", e);
+        delete h;
+        return VLB_ERR_IO_ERROR;
+    }
+    *out = h;
+    return VLB_OK;
+}
+
+void vlb_close(vlb_handle* h) {
+    if (!h) return;
+    {
+        std::lock_guard<std::mutex> lock(h->mu);
+        cudaSetDevice(h->device);
+        cudaStreamSynchronize(h->stream);
+        for (auto& kv : h->allocs) {
+            cudaFree(kv.first);
+            if (h->has_gov && h->gov.release)
+                h->gov.release(h->gov.ctx, kv.second.bytes, kv.second.tag.c_str());
+        }
+        h->allocs.clear();
+        cudaStreamDestroy(h->stream);
+    }
+    delete h;
+}
+
+int vlb_last_error(const vlb_handle* h, char* buf, size_t cap) {
+    if (!h) return copy_message(t_error, buf, cap);
+    return copy_message(h->err, buf, cap);
+}
+
+void* vlb_stream(vlb_handle* h) { return h ? (void*)h->stream : nullptr; }
+
+int vlb_synchronize(vlb_handle* h) {
+    VLB_LOCK(h);
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    return VLB_OK;
+}
+
+int vlb_set_codebook(vlb_handle* h, uint32_t type, const void* table, size_t bytes) {
+    VLB_LOCK(h);
+    if (!table) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null codebook");
+    size_t want = 0;
+    uint64_t fp = 0;
+    void** slot = nullptr;
+    switch (type) {
+        case VLB_TYPE_IQ1_S: want = 2048 * 8; fp = kFpIq1S; slot = (void**)&h->grid_iq1s; break;
+        case VLB_TYPE_IQ2_XXS: want = 256 * 8; fp = kFpIq2Xxs; slot = (void**)&h->grid_iq2xxs; break;
+        case VLB_TYPE_IQ3_XXS: want = 256 * 4; fp = kFpIq3Xxs; slot = (void**)&h->grid_iq3xxs; break;
+        default: return h->fail(VLB_ERR_UNSUPPORTED, "storage type has no codebook");
+    }
+    if (bytes != want) return h->fail(VLB_ERR_INVALID_FORMAT, "codebook has the wrong size");
+    if (fnv1a(table, bytes) != fp)
+        return h->fail(VLB_ERR_INTEGRITY_ERROR, "codebook fingerprint does not match the pinned ggml table");
+    if (!*slot) {
+        int st = h->galloc(bytes, "vlb-codebook", slot);
+        if (st != VLB_OK) return st;
+    }
+    VLB_CUDA(h, cudaMemcpy(*slot, table, bytes, cudaMemcpyHostToDevice));
+    return VLB_OK;
+}
+
+int vlb_alloc(vlb_handle* h, size_t bytes, const char* tag, void** dev_ptr) {
+    VLB_LOCK(h);
+    if (!dev_ptr) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null output pointer");
+    return h->galloc(bytes, tag ? tag : "vlb-buffer", dev_ptr);
+}
+
+int vlb_free(vlb_handle* h, void* p) {
+    VLB_LOCK(h);
+    return h->gfree(p);
+}
+
+int vlb_memcpy_h2d(vlb_handle* h, void* dst, const void* src, size_t bytes) {
+    VLB_LOCK(h);
+    VLB_CUDA(h, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, h->stream));
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    return VLB_OK;
+}
+
+int vlb_memcpy_d2h(vlb_handle* h, void* dst, const void* src, size_t bytes) {
+    VLB_LOCK(h);
+    VLB_CUDA(h, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, h->stream));
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    return VLB_OK;
+}
+
+uint64_t vlb_allocated_bytes(const vlb_handle* h) { return h ? h->allocated : 0; }
+
+// ---- matrices -------------------------------------------------------------------------------
+
+static bool half_is_finite(uint16_t bits) { return ((bits >> 10) & 0x1fu) != 0x1fu; }
+
+int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t rows,
+                      size_t cols, const void* payload, size_t payload_bytes, vlb_matrix** out) {
+    VLB_LOCK(h);
+    if (!out || !payload) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null matrix argument");
+    *out = nullptr;
+    TypeLayout L{};
+    if (!type_layout(type, &L))
+        return h->fail(VLB_ERR_UNSUPPORTED, "storage type has no device kernel");
+    if ((type == VLB_TYPE_IQ1_S && !h->grid_iq1s) || (type == VLB_TYPE_IQ2_XXS && !h->grid_iq2xxs) ||
+        (type == VLB_TYPE_IQ3_XXS && !h->grid_iq3xxs))
+        return h->fail(VLB_ERR_NOT_FOUND, "the codebook for this storage type is not installed");
+    if (rows == 0 || cols == 0 || cols % L.block_elems != 0 || rows > 0xffffffffu ||
+        cols > 0xffffffffu || cols % 32 != 0)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "matrix dimensions are invalid");
+    const size_t bpr = cols / L.block_elems;
+    const size_t nblocks = rows * bpr;
+    if (payload_bytes != nblocks * L.block_bytes)
+        return h->fail(VLB_ERR_INVALID_FORMAT, "matrix payload size does not match its shape");
+    const uint8_t* src = static_cast<const uint8_t*>(payload);
+    // validate_block_scales (ggml_quantization.cpp:205-215): every block scale finite
+    for (size_t b = 0; b < nblocks; ++b) {
+        const uint16_t d = (uint16_t)(src[b * L.block_bytes] | (src[b * L.block_bytes + 1] << 8));
+        if (!half_is_finite(d))
+            return h->fail(VLB_ERR_INVALID_FORMAT, "quantized block scale is not finite");
+    }
+    const size_t d_bytes = (nblocks * 2 + 255) / 256 * 256;
+    const size_t body_bytes = nblocks * L.body_bytes;
+    std::vector<uint8_t> staged;
+    try {
+        staged.assign(d_bytes + body_bytes, 0);
+    } catch (const std::bad_alloc&) {
+        return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the matrix on the host");
+    }
+    uint16_t* dst_d = reinterpret_cast<uint16_t*>(staged.data());
+    uint8_t* dst_b = staged.data() + d_bytes;
+    const size_t copy = L.block_bytes - 2;
+    for (size_t b = 0; b < nblocks; ++b) {
+        const uint8_t* blk = src + b * L.block_bytes;
+        dst_d[b] = (uint16_t)(blk[0] | (blk[1] << 8));
+        std::memcpy(dst_b + b * L.body_bytes, blk + 2, copy);
+    }
+    vlb_matrix* m = new (std::nothrow) vlb_matrix();
+    if (!m) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
+    int st = h->galloc(staged.size(), "vlb-resident-matrix", &m->mem);
+    if (st != VLB_OK) {
+        delete m;
+        return st;
+    }
+    cudaError_t e = cudaMemcpy(m->mem, staged.data(), staged.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        h->gfree(m->mem);
+        delete m;
+        return h->cuda_fail("cudaMemcpy(matrix)", e);
+    }
+    m->owner = h;
+    m->identity = identity;
+    m->type = type;
+    m->rows = rows;
+    m->cols = cols;
+    m->bpr = (uint32_t)bpr;
+    m->bytes = nblocks * 2 + body_bytes;
+    m->payload_bytes = payload_bytes;
+    m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr,
+                   reinterpret_cast<const uint16_t*>(m->mem),
+                   reinterpret_cast<const uint8_t*>(m->mem) + d_bytes};
+    *out = m;
+    return VLB_OK;
+}
+
+int vlb_release_matrix(vlb_handle* h, vlb_matrix* m) {
+    VLB_LOCK(h);
+    if (!m || m->owner != h) return h->fail(VLB_ERR_INVALID_ARGUMENT, "matrix does not belong to this handle");
+    int st = h->gfree(m->mem);
+    if (st != VLB_OK) return st;
+    delete m;
+    return VLB_OK;
+}
+
+uint64_t vlb_matrix_bytes(const vlb_matrix* m) { return m ? m->payload_bytes : 0; }
+
+int vlb_matvec(vlb_handle* h, const vlb_matrix* m, const float* x, float* y) {
+    VLB_LOCK(h);
+    if (!m || m->owner != h || !x || !y) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid matvec argument");
+    if (h->seam_x_cap < m->cols) {
+        if (h->seam_x) h->gfree(h->seam_x);
+        h->seam_x = nullptr;
+        h->seam_x_cap = 0;
+        int st = h->galloc(m->cols * sizeof(float), "vlb-seam-input", (void**)&h->seam_x);
+        if (st != VLB_OK) return st;
+        h->seam_x_cap = m->cols;
+    }
+    if (h->seam_y_cap < m->rows) {
+        if (h->seam_y) h->gfree(h->seam_y);
+        h->seam_y = nullptr;
+        h->seam_y_cap = 0;
+        int st = h->galloc(m->rows * sizeof(float), "vlb-seam-output", (void**)&h->seam_y);
+        if (st != VLB_OK) return st;
+        h->seam_y_cap = m->rows;
+    }
+    VLB_CUDA(h, cudaMemcpyAsync(h->seam_x, x, m->cols * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    VLB_CUDA(h, launch_gemv(m->dm, h->grids(), h->seam_x, 1, (uint32_t)m->cols, h->seam_y, (uint32_t)m->rows, h->stream));
+    VLB_CUDA(h, cudaMemcpyAsync(y, h->seam_y, m->rows * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    return VLB_OK;
+}
+
+int vlb_matvec_device(vlb_handle* h, const vlb_matrix* m, const float* x, size_t ntok,
+                      size_t xstride, float* y, size_t ystride, void* stream) {
+    VLB_LOCK(h);
+    if (!m || m->owner != h || !x || !y || xstride < m->cols || ystride < m->rows)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid matvec argument");
+    VLB_CUDA(h, launch_gemv(m->dm, h->grids(), x, (uint32_t)ntok, (uint32_t)xstride, y, (uint32_t)ystride, h->pick(stream)));
+    return VLB_OK;
+}
+
+int vlb_dequantize_device(vlb_handle* h, const vlb_matrix* m, float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!m || m->owner != h || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid dequantize argument");
+    VLB_CUDA(h, launch_dequant(m->dm, h->grids(), out, h->pick(stream)));
+    return VLB_OK;
+}
+
+// ---- layers ---------------------------------------------------------------------------------
+
+static uint32_t max_units_for(uint32_t T, uint32_t k, uint32_t E) {
+    return T * k / (uint32_t)kUnitTokens + E + T / (uint32_t)kUnitTokens + 8u;
+}
+
+static void free_layer(vlb_handle* h, vlb_layer* L) {
+    for (auto& e : L->ev)
+        if (e) cudaEventDestroy(e);
+    void* ptrs[] = {L->router, L->bias, L->tid2eid, L->mats, L->ws,
+                    L->x_dev, L->tok_dev, L->logits_dev, L->out_dev};
+    for (void* p : ptrs)
+        if (p) h->gfree(p);
+    delete L;
+}
+
+int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out) {
+    VLB_LOCK(h);
+    if (!d || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer argument");
+    *out = nullptr;
+    const uint32_t H = d->hidden, I = d->intermediate, E = d->experts, k = d->top_k;
+    if (H == 0 || I == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512 || H % 256 ||
+        I % 256 || d->max_tokens == 0 || !d->w1 || !d->w3 || !d->w2)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "MoE layer dimensions are invalid");
+    if (d->score != VLB_SCORE_SOFTMAX && !(d->route_scale > 0.f && std::isfinite(d->route_scale)))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "route scale must be finite and positive");
+    if (d->hash_routing && (!d->tid2eid || d->vocab == 0))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs a token-to-expert table");
+    if (!d->router) return h->fail(VLB_ERR_INVALID_ARGUMENT, "the router weight is required");
+    const bool has_shared = d->shared_w1 && d->shared_w3 && d->shared_w2;
+    std::vector<const vlb_matrix*> hm(3 * (E + 1), nullptr);
+    for (uint32_t e = 0; e < E; ++e) {
+        hm[e] = d->w1[e];
+        hm[(E + 1) + e] = d->w3[e];
+        hm[2 * (E + 1) + e] = d->w2[e];
+    }
+    if (has_shared) {
+        hm[E] = d->shared_w1;
+        hm[(E + 1) + E] = d->shared_w3;
+        hm[2 * (E + 1) + E] = d->shared_w2;
+    }
+    for (uint32_t e = 0; e < E + (has_shared ? 1u : 0u); ++e) {
+        const vlb_matrix* a = hm[e];
+        const vlb_matrix* b = hm[(E + 1) + e];
+        const vlb_matrix* c = hm[2 * (E + 1) + e];
+        if (!a || !b || !c || a->owner != h || b->owner != h || c->owner != h)
+            return h->fail(VLB_ERR_INVALID_ARGUMENT, "an expert matrix is missing or foreign");
+        if (a->rows != I || a->cols != H || b->rows != I || b->cols != H || c->rows != H ||
+            c->cols != I || a->type != b->type)
+            return h->fail(VLB_ERR_INVALID_FORMAT, "an expert matrix shape does not match the layer");
+    }
+    vlb_layer* L = new (std::nothrow) vlb_layer();
+    if (!L) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the layer record");
+    L->desc = *d;
+    L->has_shared = has_shared;
+    L->host_mats = hm;
+    int st = VLB_OK;
+#define TRY(expr)                 \
+    do {                          \
+        st = (expr);              \
+        if (st != VLB_OK) {       \
+            free_layer(h, L);     \
+            return st;            \
+        }                         \
+    } while (0)
+    TRY(h->galloc((size_t)E * H * 4, "vlb-router", (void**)&L->router));
+    VLB_CUDA(h, cudaMemcpy(L->router, d->router, (size_t)E * H * 4, cudaMemcpyHostToDevice));
+    if (d->bias) {
+        TRY(h->galloc((size_t)E * 4, "vlb-router-bias", (void**)&L->bias));
+        VLB_CUDA(h, cudaMemcpy(L->bias, d->bias, (size_t)E * 4, cudaMemcpyHostToDevice));
+    }
+    if (d->hash_routing) {
+        TRY(h->galloc((size_t)d->vocab * k * 4, "vlb-tid2eid", (void**)&L->tid2eid));
+        VLB_CUDA(h, cudaMemcpy(L->tid2eid, d->tid2eid, (size_t)d->vocab * k * 4, cudaMemcpyHostToDevice));
+    }
+    std::vector<DevMat> dm(3 * (E + 1));
+    for (size_t i = 0; i < dm.size(); ++i) dm[i] = hm[i] ? hm[i]->dm : DevMat{};
+    TRY(h->galloc(dm.size() * sizeof(DevMat), "vlb-expert-table", (void**)&L->mats));
+    VLB_CUDA(h, cudaMemcpy(L->mats, dm.data(), dm.size() * sizeof(DevMat), cudaMemcpyHostToDevice));
+    // workspace
+    const size_t T = d->max_tokens, P = T * k + T;
+    const uint32_t mu = max_units_for((uint32_t)T, k, E);
+    size_t off = 0;
+    auto carve = [&](size_t bytes) {
+        const size_t at = off;
+        off += (bytes + 255) / 256 * 256;
+        return at;
+    };
+    const size_t o_logits = carve(T * E * 4), o_scores = carve(T * E * 4), o_idx = carve(T * k * 4),
+                 o_w = carve(T * k * 4), o_off = carve((E + 2) * 4), o_pt = carve(P * 4),
+                 o_ps = carve(P * 4), o_pw = carve(P * 4), o_units = carve((size_t)mu * sizeof(Unit)),
+                 o_cnt = carve(16), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
+                 o_y = carve(P * H * 4);
+    TRY(h->galloc(off, "vlb-layer-workspace", &L->ws));
+    TRY(h->galloc(T * H * 4, "vlb-layer-x", (void**)&L->x_dev));
+    TRY(h->galloc(T * 4, "vlb-layer-tokens", (void**)&L->tok_dev));
+    TRY(h->galloc(T * E * 4, "vlb-layer-logits", (void**)&L->logits_dev));
+    TRY(h->galloc(T * H * 4, "vlb-layer-out", (void**)&L->out_dev));
+#undef TRY
+    char* ws = static_cast<char*>(L->ws);
+    MoeParams& p = L->p;
+    p.H = H; p.I = I; p.E = E; p.k = k; p.T = 0;
+    p.score = d->score;
+    p.hash_routing = d->hash_routing;
+    p.weight_after_down = d->weight_after_down;
+    p.route_scale = d->route_scale;
+    p.routed_limit = d->routed_swiglu_limit;
+    p.shared_limit = d->shared_swiglu_limit;
+    p.vocab = d->vocab;
+    p.has_shared = has_shared ? 1 : 0;
+    p.router = L->router;
+    p.bias = L->bias;
+    p.tid2eid = L->tid2eid;
+    p.mats = L->mats;
+    p.grids = h->grids();
+    p.logits = reinterpret_cast<float*>(ws + o_logits);
+    p.scores = reinterpret_cast<float*>(ws + o_scores);
+    p.idx = reinterpret_cast<uint32_t*>(ws + o_idx);
+    p.weights = reinterpret_cast<float*>(ws + o_w);
+    p.offsets = reinterpret_cast<uint32_t*>(ws + o_off);
+    p.pair_token = reinterpret_cast<uint32_t*>(ws + o_pt);
+    p.pair_slot = reinterpret_cast<uint32_t*>(ws + o_ps);
+    p.pair_weight = reinterpret_cast<float*>(ws + o_pw);
+    p.units = reinterpret_cast<Unit*>(ws + o_units);
+    p.counters = reinterpret_cast<uint32_t*>(ws + o_cnt);
+    p.combine_pairs = reinterpret_cast<uint32_t*>(ws + o_cp);
+    p.act = reinterpret_cast<float*>(ws + o_act);
+    p.y = reinterpret_cast<float*>(ws + o_y);
+    p.max_units = mu;
+    *out = L;
+    return VLB_OK;
+}
+
+int vlb_layer_destroy(vlb_handle* h, vlb_layer* L) {
+    VLB_LOCK(h);
+    if (!L) return VLB_OK;
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    free_layer(h, L);
+    return VLB_OK;
+}
+
+static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
+                          const float* logits, uint32_t T, float* out, cudaStream_t s) {
+    if (T == 0 || T > L->desc.max_tokens)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "token count is zero or above the layer's max_tokens");
+    if (L->desc.hash_routing && !tok)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs token ids");
+    MoeParams p = L->p;
+    p.T = T;
+    p.x = x;
+    p.token_ids = tok;
+    p.logits_in = logits;
+    p.out = out;
+    p.grids = h->grids();
+    VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, 16, s));
+    VLB_CUDA(h, launch_moe(p, s, L->profiling ? L->ev : nullptr));
+    L->last_T = T;
+    L->last_logits_given = logits != nullptr;
+    return VLB_OK;
+}
+
+int vlb_layer_forward_device(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
+                             const float* logits, uint32_t T, float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!L || !x || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
+    return forward_locked(h, L, x, tok, logits, T, out, h->pick(stream));
+}
+
+int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
+                      const float* logits, uint32_t T, float* out) {
+    VLB_LOCK(h);
+    if (!L || !x || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
+    if (T == 0 || T > L->desc.max_tokens)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "token count is zero or above the layer's max_tokens");
+    const uint32_t H = L->desc.hidden, E = L->desc.experts;
+    cudaStream_t s = h->stream;
+    VLB_CUDA(h, cudaMemcpyAsync(L->x_dev, x, (size_t)T * H * 4, cudaMemcpyHostToDevice, s));
+    if (tok) VLB_CUDA(h, cudaMemcpyAsync(L->tok_dev, tok, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+    if (logits) VLB_CUDA(h, cudaMemcpyAsync(L->logits_dev, logits, (size_t)T * E * 4, cudaMemcpyHostToDevice, s));
+    int st = forward_locked(h, L, L->x_dev, tok ? L->tok_dev : nullptr, logits ? L->logits_dev : nullptr,
+                            T, L->out_dev, s);
+    if (st != VLB_OK) return st;
+    VLB_CUDA(h, cudaMemcpyAsync(out, L->out_dev, (size_t)T * H * 4, cudaMemcpyDeviceToHost, s));
+    uint32_t flags = 0;
+    VLB_CUDA(h, cudaMemcpyAsync(&flags, L->p.counters + 3, 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
+    if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "router selected an out-of-range expert");
+    if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
+    return VLB_OK;
+}
+
+int vlb_layer_last_route(vlb_handle* h, vlb_layer* L, uint32_t T, uint32_t* idx, float* w,
+                         uint32_t* offsets, uint32_t* pt, uint32_t* ps) {
+    VLB_LOCK(h);
+    if (!L || T != L->last_T || T == 0) return h->fail(VLB_ERR_INVALID_ARGUMENT, "no route of that size");
+    const size_t n = (size_t)T * L->desc.top_k;
+    cudaStream_t s = h->stream;
+    if (idx) VLB_CUDA(h, cudaMemcpyAsync(idx, L->p.idx, n * 4, cudaMemcpyDeviceToHost, s));
+    if (w) VLB_CUDA(h, cudaMemcpyAsync(w, L->p.weights, n * 4, cudaMemcpyDeviceToHost, s));
+    if (offsets) VLB_CUDA(h, cudaMemcpyAsync(offsets, L->p.offsets, (L->desc.experts + 1) * 4, cudaMemcpyDeviceToHost, s));
+    if (pt) VLB_CUDA(h, cudaMemcpyAsync(pt, L->p.pair_token, n * 4, cudaMemcpyDeviceToHost, s));
+    if (ps) VLB_CUDA(h, cudaMemcpyAsync(ps, L->p.pair_slot, n * 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    return VLB_OK;
+}
+
+uint64_t vlb_layer_last_weight_bytes(vlb_handle* h, vlb_layer* L) {
+    if (!h || !L || L->last_T == 0) return 0;
+    std::lock_guard<std::mutex> lock(h->mu);
+    cudaSetDevice(h->device);
+    const uint32_t E = L->desc.experts;
+    std::vector<uint32_t> off(E + 1);
+    if (cudaMemcpyAsync(off.data(), L->p.offsets, (E + 1) * 4, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess ||
+        cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return 0;
+    uint64_t bytes = L->last_logits_given ? 0 : (uint64_t)E * L->desc.hidden * 4;
+    for (uint32_t e = 0; e < E; ++e)
+        if (off[e + 1] > off[e])
+            bytes += L->host_mats[e]->payload_bytes + L->host_mats[(E + 1) + e]->payload_bytes +
+                     L->host_mats[2 * (E + 1) + e]->payload_bytes;
+    if (L->has_shared)
+        bytes += L->host_mats[E]->payload_bytes + L->host_mats[(E + 1) + E]->payload_bytes +
+                 L->host_mats[2 * (E + 1) + E]->payload_bytes;
+    return bytes;
+}
+
+int vlb_layer_set_profiling(vlb_handle* h, vlb_layer* L, int enable) {
+    VLB_LOCK(h);
+    if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
+    if (enable && !L->ev[0])
+        for (auto& e : L->ev) VLB_CUDA(h, cudaEventCreate(&e));
+    L->profiling = enable != 0;
+    return VLB_OK;
+}
+
+int vlb_layer_phase_times(vlb_handle* h, vlb_layer* L, float* ms, int n) {
+    VLB_LOCK(h);
+    if (!L || !ms || n < kMoePhases || !L->profiling || L->last_T == 0)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "profiling is off or there is no forward to report");
+    VLB_CUDA(h, cudaEventSynchronize(L->ev[kMoePhases]));
+    for (int i = 0; i < kMoePhases; ++i) VLB_CUDA(h, cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]));
+    return VLB_OK;
+}
+
+int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* logits,
+                     const float* bias, const uint32_t* tok, const uint32_t* tid2eid,
+                     uint32_t vocab, uint32_t T, uint32_t E, uint32_t k, float route_scale,
+                     uint32_t* idx, float* weights, void* stream) {
+    VLB_LOCK(h);
+    if (!logits || !idx || !weights || T == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid route argument");
+    if (hash_routing && (!tok || !tid2eid || vocab == 0))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs token ids and a table");
+    cudaStream_t s = h->pick(stream);
+    float* scores = nullptr;
+    uint32_t* flag = nullptr;
+    int st = h->galloc((size_t)T * E * 4 + 256, "vlb-route-scratch", (void**)&scores);
+    if (st != VLB_OK) return st;
+    flag = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(scores) + (size_t)T * E * 4);
+    cudaError_t e = cudaMemsetAsync(flag, 0, 4, s);
+    if (e == cudaSuccess) e = launch_scores(logits, (size_t)T * E, score, scores, s);
+    if (e == cudaSuccess)
+        e = launch_route(scores, bias, tok, tid2eid, vocab, T, E, k, score, hash_routing,
+                         route_scale, idx, weights, flag, s);
+    uint32_t flags = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&flags, flag, 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    h->gfree(scores);
+    if (e != cudaSuccess) return h->cuda_fail("route", e);
+    if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
+    if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "route selects an out-of-range expert");
+    if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
+    return VLB_OK;
+}
+
+int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint32_t T,
+                             uint32_t H, uint32_t E, float* logits, void* stream) {
+    VLB_LOCK(h);
+    if (!x || !w || !logits || T == 0 || H == 0 || E == 0)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid router argument");
+    float* scores = nullptr;
+    int st = h->galloc((size_t)T * E * 4, "vlb-router-scratch", (void**)&scores);
+    if (st != VLB_OK) return st;
+    cudaStream_t s = h->pick(stream);
+    cudaError_t e = launch_router(x, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scores, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    h->gfree(scores);
+    if (e != cudaSuccess) return h->cuda_fail("router", e);
+    return VLB_OK;
+}
+
+int vlb_rms_norm_device(vlb_handle* h, const float* x, const float* w, uint32_t rows,
+                        uint32_t width, float eps, float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!x || !w || !out || rows == 0 || width == 0 || !(eps > 0.f))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid RMSNorm argument");
+    VLB_CUDA(h, launch_rms_norm(x, w, rows, width, eps, out, h->pick(stream)));
+    return VLB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,195 @@
+// Internal definitions shared by the vlb200 CUDA sources: the device matrix layout, the
+// bit-exact block decoders and the launch-side workspace structures.
+//
+// Device layout of a resident ggml matrix (chosen at upload, vlb_upload_matrix):
+//   d    : fp16 block scales, [rows x blocks_per_row] (the 2-byte header of every ggml block)
+//   body : the rest of each block, padded to a 16-byte multiple, [rows x blocks_per_row x body]
+//            Q8_0    : 32 int8 quants                                   (32 B)
+//            IQ2_XXS : 8 groups x (4 grid-index bytes, u32 signs/scale)  (64 B)
+//            IQ3_XXS : 64 grid-index bytes, then 8 x u32 signs/scale      (96 B)
+//            IQ1_S   : 32 low-index bytes, then 8 x u16 high bits/scale   (48 B)
+// The ggml block is 34/66/98/50 bytes, so splitting the scale off makes every body 16-byte
+// aligned (wide vector loads, TMA-friendly rows) without changing the bytes read per weight.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/vlb200.h"
+
+namespace vlb {
+
+constexpr uint32_t kTypeQ8_0 = VLB_TYPE_Q8_0;
+constexpr uint32_t kTypeIq2Xxs = VLB_TYPE_IQ2_XXS;
+constexpr uint32_t kTypeIq3Xxs = VLB_TYPE_IQ3_XXS;
+constexpr uint32_t kTypeIq1S = VLB_TYPE_IQ1_S;
+
+struct TypeLayout {
+    uint32_t block_elems;  // weights per ggml block
+    uint32_t block_bytes;  // ggml block size (file/payload layout)
+    uint32_t body_bytes;   // device body size (block minus the fp16 scale, 16-byte multiple)
+};
+
+__host__ __device__ inline bool type_layout(uint32_t type, TypeLayout* l) {
+    switch (type) {
+        case kTypeQ8_0: *l = {32u, 34u, 32u}; return true;
+        case kTypeIq2Xxs: *l = {256u, 66u, 64u}; return true;
+        case kTypeIq3Xxs: *l = {256u, 98u, 96u}; return true;
+        case kTypeIq1S: *l = {256u, 50u, 48u}; return true;
+        default: return false;
+    }
+}
+
+// Kernel-side view of a resident matrix.
+struct DevMat {
+    uint32_t type;
+    uint32_t rows;
+    uint32_t cols;
+    uint32_t bpr;  // blocks per row
+    const uint16_t* d;
+    const uint8_t* body;
+};
+
+struct Grids {
+    const uint64_t* iq1s;    // 2048 entries, 8 x int8
+    const uint64_t* iq2xxs;  // 256 entries, 8 x uint8 magnitudes
+    const uint32_t* iq3xxs;  // 256 entries, 4 x uint8 magnitudes
+};
+
+// fp16 -> f32. The hardware conversion is exact (every half, subnormals included, is a float),
+// so it equals the reference's bit-level fp16_to_float (ggml_quantization.cpp:101-124).
+__device__ __forceinline__ float h2f(uint16_t bits) {
+    return __half2float(__ushort_as_half(bits));
+}
+
+// The 8-bit sign mask of one 8-weight sub-block: seven stored bits plus an even-parity bit
+// (ggml_quantization.cpp:268-271 and :354-357).
+__device__ __forceinline__ uint32_t iq_signs(uint32_t aux, int sub) {
+    const uint32_t s7 = (aux >> (7 * sub)) & 127u;
+    return s7 | ((__popc(s7) & 1u) << 7);
+}
+
+// ---- bit-exact block decoders (one 32-weight group at a time) ------------------------------
+// Each writes the 32 weights of group g (0..7 for the 256-weight formats; 0 for Q8_0) exactly as
+// the reference's decode_*_block computes them: the same operations in the same order, every one
+// rounded to f32 (no contraction is possible: no product feeds an addition).
+
+// decode_q8_0_block, ggml_quantization.cpp:419-435
+__device__ __forceinline__ void decode_group_q8_0(float d, const uint8_t* body, float* w) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = __fmul_rn(d, (float)(int8_t)body[i]);
+}
+
+// decode_iq2_xxs_block, ggml_quantization.cpp:250-283
+__device__ __forceinline__ void decode_group_iq2_xxs(float d, const uint8_t* body, int g,
+                                                     const uint64_t* grid, float* w) {
+    const uint32_t idx4 = *reinterpret_cast<const uint32_t*>(body + g * 8);
+    const uint32_t aux = *reinterpret_cast<const uint32_t*>(body + g * 8 + 4);
+    const float ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.25f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint64_t gv = grid[(idx4 >> (8 * j)) & 0xffu];
+        const uint32_t signs = iq_signs(aux, j);
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            const float m = (float)((uint32_t)(gv >> (8 * l)) & 0xffu);
+            const float p = __fmul_rn(ls, m);
+            w[j * 8 + l] = (signs >> l) & 1u ? -p : p;
+        }
+    }
+}
+
+// decode_iq3_xxs_block, ggml_quantization.cpp:336-379
+__device__ __forceinline__ void decode_group_iq3_xxs(float d, const uint8_t* body, int g,
+                                                     const uint32_t* grid, float* w) {
+    const uint32_t aux = *reinterpret_cast<const uint32_t*>(body + 64 + g * 4);
+    const uint2 idx8 = *reinterpret_cast<const uint2*>(body + g * 8);
+    const float ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t word = j < 2 ? idx8.x : idx8.y;
+        const uint32_t g1 = grid[(word >> (16 * (j & 1))) & 0xffu];
+        const uint32_t g2 = grid[(word >> (16 * (j & 1) + 8)) & 0xffu];
+        const uint32_t signs = iq_signs(aux, j);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const float p1 = __fmul_rn(ls, (float)((g1 >> (8 * l)) & 0xffu));
+            const float p2 = __fmul_rn(ls, (float)((g2 >> (8 * l)) & 0xffu));
+            w[j * 8 + l] = (signs >> l) & 1u ? -p1 : p1;
+            w[j * 8 + l + 4] = (signs >> (l + 4)) & 1u ? -p2 : p2;
+        }
+    }
+}
+
+// decode_iq1_s_block, ggml_quantization.cpp:217-248
+__device__ __forceinline__ void decode_group_iq1_s(float d, const uint8_t* body, int g,
+                                                   const uint64_t* grid, float* w) {
+    const uint32_t qs4 = *reinterpret_cast<const uint32_t*>(body + g * 4);
+    const uint32_t h = *reinterpret_cast<const uint16_t*>(body + 32 + g * 2);
+    const float ls = __fmul_rn(d, (float)(2u * ((h >> 12) & 7u) + 1u));
+    const float delta = (h & 0x8000u) ? -0.125f : 0.125f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t idx = ((qs4 >> (8 * j)) & 0xffu) | (((h >> (3 * j)) & 7u) << 8);
+        const uint64_t gv = grid[idx];
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            const float q = (float)(int8_t)(uint8_t)((gv >> (8 * l)) & 0xffu);
+            w[j * 8 + l] = __fmul_rn(ls, __fadd_rn(q, delta));
+        }
+    }
+}
+
+// ---- workspace of one MoE layer forward ----------------------------------------------------
+// A "unit" is one expert's slice of at most kUnitTokens (token, slot) pairs; every (unit, row
+// tile) pair is one work item of the expert kernels. Units are ordered by expert id ascending
+// (the shared expert last), so a CTA walking consecutive items keeps the same activations.
+constexpr int kUnitTokens = 4;
+
+struct Unit {
+    uint32_t expert;      // routed expert id, or E for the shared expert
+    uint32_t pair_begin;  // first pair (row of the act/out workspaces)
+    uint32_t count;       // pairs in this unit (1..kUnitTokens)
+    uint32_t pad;
+};
+
+struct MoeParams {
+    uint32_t H, I, E, k, T;
+    int score;
+    int hash_routing;
+    int weight_after_down;
+    float route_scale;
+    float routed_limit;
+    float shared_limit;
+    uint32_t vocab;
+    int has_shared;
+    // weights
+    const float* router;     // [E x H]
+    const float* bias;       // [E]
+    const uint32_t* tid2eid; // [vocab x k]
+    const DevMat* mats;      // [3 x (E+1)]: w1[0..E], w3[0..E], w2[0..E]; index E = shared
+    Grids grids;
+    // per-call inputs
+    const float* x;          // [T x H]
+    const uint32_t* token_ids;
+    const float* logits_in;  // optional [T x E]
+    // workspace
+    float* logits;           // [T x E]
+    float* scores;           // [T x E]
+    uint32_t* idx;           // [T x k]
+    float* weights;          // [T x k]
+    uint32_t* offsets;       // [E + 2]
+    uint32_t* pair_token;    // [T*k + T]
+    uint32_t* pair_slot;     // [T*k + T]
+    float* pair_weight;      // [T*k + T]
+    Unit* units;             // [max_units]
+    uint32_t* counters;      // [4]: n_units, n_active, combine_ready, error
+    uint32_t* combine_pairs; // [T x k]: each token's pairs in (expert, slot) order
+    float* act;              // [(T*k + T) x I]
+    float* y;                // [(T*k + T) x H]
+    float* out;              // [T x H]
+    uint32_t max_units;
+};
+
+}  // namespace vlb

@@ -1,0 +1,738 @@
+// sm_100a kernels of the MoE routed-expert decode path, and their launchers.
+//
+//   dequant_kernel    bit-exact block decode (reference decode_*_block)
+//   gemv_kernel       multi-token dequant-matvec over one resident matrix (the operator seam)
+//   router_kernel     router projection in f64 accumulation + score function
+//   route_kernel      warp-per-token top-k (ties to the lower id) and route weights
+//   dispatch_kernel   stable counting sort of (token, slot) pairs by expert, work units
+//   gateup_kernel     persistent: gate and up rows of every selected expert + SwiGLU epilogue
+//   down_kernel       persistent: down rows of every selected expert
+//   combine_kernel    per-token deterministic combine in the reference's order + shared expert
+#include <cuda_runtime.h>
+
+#include "vlb_gemv.cuh"
+#include "vlb_launch.h"
+
+namespace vlb {
+
+constexpr uint32_t kGridSmemBytes = 2048u * 8u + 256u * 8u + 256u * 4u;  // 19,456
+
+__device__ __forceinline__ GridSmem stage_grids(const Grids& g, unsigned char* smem) {
+    uint64_t* s1 = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* s2 = s1 + 2048;
+    uint32_t* s3 = reinterpret_cast<uint32_t*>(s2 + 256);
+    if (g.iq1s)
+        for (uint32_t i = threadIdx.x; i < 2048u; i += blockDim.x) s1[i] = g.iq1s[i];
+    if (g.iq2xxs)
+        for (uint32_t i = threadIdx.x; i < 256u; i += blockDim.x) s2[i] = g.iq2xxs[i];
+    if (g.iq3xxs)
+        for (uint32_t i = threadIdx.x; i < 256u; i += blockDim.x) s3[i] = g.iq3xxs[i];
+    return GridSmem{s1, s2, s3};
+}
+
+// ---------------------------------------------------------------------------------------------
+// dequantize: one thread per 32-weight group
+__global__ void dequant_kernel(DevMat m, Grids g, float* __restrict__ out) {
+    const uint32_t ngroups = m.cols / 32u;
+    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (size_t)m.rows * ngroups) return;
+    const uint32_t row = (uint32_t)(gid / ngroups), grp = (uint32_t)(gid % ngroups);
+    float w[32];
+    if (m.type == kTypeQ8_0) {
+        decode_group_q8_0(h2f(m.d[(size_t)row * m.bpr + grp]),
+                          m.body + ((size_t)row * m.bpr + grp) * 32u, w);
+    } else {
+        const uint32_t blk = grp >> 3, gg = grp & 7u;
+        const float d = h2f(m.d[(size_t)row * m.bpr + blk]);
+        if (m.type == kTypeIq2Xxs)
+            decode_group_iq2_xxs(d, m.body + ((size_t)row * m.bpr + blk) * 64u, gg, g.iq2xxs, w);
+        else if (m.type == kTypeIq3Xxs)
+            decode_group_iq3_xxs(d, m.body + ((size_t)row * m.bpr + blk) * 96u, gg, g.iq3xxs, w);
+        else
+            decode_group_iq1_s(d, m.body + ((size_t)row * m.bpr + blk) * 48u, gg, g.iq1s, w);
+    }
+    float* o = out + (size_t)row * m.cols + (size_t)grp * 32u;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Standalone multi-token GEMV: CTA = 8 warps x 8 rows; tokens in chunks of TOKC.
+constexpr int kGemvRows = 8;
+constexpr int kGemvWarps = 8;
+
+template <uint32_t FMT, int TOKC>
+__global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const float* __restrict__ x,
+                                                   uint32_t ntok, uint32_t xstride,
+                                                   float* __restrict__ y, uint32_t ystride) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const GridSmem gs = stage_grids(grids, smem);
+    float* xs = reinterpret_cast<float*>(smem + kGridSmemBytes);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t row0 = blockIdx.x * (kGemvRows * kGemvWarps) + warp * kGemvRows;
+    const uint32_t ngroups = m.cols / 32u;
+    const uint32_t rbase = row0 < m.rows ? row0 : 0u;
+    for (uint32_t t0 = 0; t0 < ntok; t0 += TOKC) {
+        const float* rows[TOKC];
+#pragma unroll
+        for (int t = 0; t < TOKC; ++t) rows[t] = t0 + t < ntok ? x + (size_t)(t0 + t) * xstride : nullptr;
+        __syncthreads();
+        stage_x<TOKC>(xs, rows, m.cols);
+        __syncthreads();
+        if (row0 >= m.rows) continue;
+        float acc[kGemvRows][TOKC];
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+            for (int t = 0; t < TOKC; ++t) acc[r][t] = 0.f;
+        if (rbase + kGemvRows <= m.rows) {
+            warp_dot<FMT, kGemvRows, 0, TOKC>(m, m, rbase, 0u, xs, ngroups, gs, acc);
+        } else {
+            // tail: one row at a time
+            for (int r = 0; r < kGemvRows; ++r) {
+                if (rbase + r >= m.rows) break;
+                float a1[1][TOKC];
+#pragma unroll
+                for (int t = 0; t < TOKC; ++t) a1[0][t] = 0.f;
+                warp_dot<FMT, 1, 0, TOKC>(m, m, rbase + r, 0u, xs, ngroups, gs, a1);
+#pragma unroll
+                for (int t = 0; t < TOKC; ++t) acc[r][t] = a1[0][t];
+            }
+        }
+        warp_reduce<kGemvRows, TOKC>(acc);
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+            for (int t = 0; t < TOKC; ++t)
+                if (lane == (uint32_t)(r * TOKC + t) % 32u && rbase + r < m.rows && t0 + t < ntok)
+                    y[(size_t)(t0 + t) * ystride + rbase + r] = acc[r][t];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Router projection, f64 accumulation of exact f32 products (deepseek_v4_graph.cpp:735-767), and
+// the per-expert score (sqrt_softplus / sigmoid; softmax is applied per token in route_kernel).
+// CTA: 8 warps = 8 experts, a chunk of up to 8 tokens, columns staged 1024 at a time.
+constexpr int kRouterTok = 8;
+constexpr int kRouterChunk = 1024;
+
+__device__ __forceinline__ float sqrt_softplus_dev(float v) {
+    const double p = (double)v;
+    const double sp = fmax(p, 0.0) + log1p(exp(-fabs(p)));
+    return (float)sqrt(sp);
+}
+__device__ __forceinline__ float sigmoid_dev(float v) {
+    const double p = (double)v;
+    if (p >= 0.0) return (float)(1.0 / (1.0 + exp(-p)));
+    const double e = exp(p);
+    return (float)(e / (1.0 + e));
+}
+__device__ __forceinline__ float score_dev(int score, float logit) {
+    if (score == VLB_SCORE_SIGMOID) return sigmoid_dev(logit);
+    if (score == VLB_SCORE_SQRT_SOFTPLUS) return sqrt_softplus_dev(logit);
+    return logit;
+}
+
+__global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ x,
+                                                     const float* __restrict__ w, uint32_t T,
+                                                     uint32_t H, uint32_t E, int score,
+                                                     float* __restrict__ logits,
+                                                     float* __restrict__ scores) {
+    __shared__ __align__(16) float xs[kRouterTok][kRouterChunk];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t e = blockIdx.x * 8u + warp;
+    const uint32_t t0 = blockIdx.y * kRouterTok;
+    const uint32_t nt = min((uint32_t)kRouterTok, T - t0);
+    double acc[kRouterTok];
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
+    for (uint32_t c0 = 0; c0 < H; c0 += kRouterChunk) {
+        const uint32_t cn = min((uint32_t)kRouterChunk, H - c0);
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < kRouterTok * cn; i += blockDim.x) {
+            const uint32_t t = i / cn, c = i % cn;
+            xs[t][c] = t < nt ? x[(size_t)(t0 + t) * H + c0 + c] : 0.f;
+        }
+        __syncthreads();
+        if (e < E) {
+            for (uint32_t c = lane; c < cn; c += 32u) {
+                const double wv = (double)__ldg(w + (size_t)e * H + c0 + c);
+#pragma unroll
+                for (int t = 0; t < kRouterTok; ++t) acc[t] = fma(wv, (double)xs[t][c], acc[t]);
+            }
+        }
+    }
+    if (e >= E) return;
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) {
+        double v = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[t] = v;
+    }
+    if (lane < nt) {
+        double v = 0.0;
+#pragma unroll
+        for (int t = 0; t < kRouterTok; ++t) if ((uint32_t)t == lane) v = acc[t];
+        const float lg = (float)v;
+        logits[(size_t)(t0 + lane) * E + e] = lg;
+        scores[(size_t)(t0 + lane) * E + e] = score_dev(score, lg);
+    }
+}
+
+__global__ void score_kernel(const float* __restrict__ logits, size_t n, int score,
+                             float* __restrict__ scores) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) scores[i] = score_dev(score, logits[i]);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Top-k routing, one warp per token (deepseek_v4_route_learned_logits / _hash_logits,
+// deepseek_v4_reference.cpp:223-307; OLMoE softmax router, olmoe_runtime.cpp:1120-1137).
+// Selection key: learned = score + bias (f32 add), softmax = probability; larger first, ties to
+// the lower expert id (std::partial_sort with that strict order). E <= 32 * kMaxPerLane.
+constexpr int kMaxPerLane = 16;  // E <= 512
+
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ scores,
+                                                    const float* __restrict__ bias,
+                                                    const uint32_t* __restrict__ token_ids,
+                                                    const uint32_t* __restrict__ tid2eid,
+                                                    uint32_t vocab, uint32_t T, uint32_t E,
+                                                    uint32_t k, int score, int hash_routing,
+                                                    float route_scale, uint32_t* __restrict__ idx,
+                                                    float* __restrict__ weights,
+                                                    uint32_t* __restrict__ error_flag) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t t = blockIdx.x * 8u + warp;
+    if (t >= T) return;
+    const float* s = scores + (size_t)t * E;
+    float key[kMaxPerLane];
+    float val[kMaxPerLane];
+    if (score == VLB_SCORE_SOFTMAX) {
+        // p_e = float exp of (logit - max); double denominator; float division (no renorm)
+        float mx = -INFINITY;
+        for (uint32_t e = lane; e < E; e += 32u) mx = fmaxf(mx, s[e]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        double den = 0.0;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            const uint32_t e = lane + 32u * i;
+            float p = 0.f;
+            if (e < E) p = (float)exp((double)__fsub_rn(s[e], mx));
+            val[i] = p;
+            den += (double)p;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+        const float fden = (float)den;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            val[i] = __fdiv_rn(val[i], fden);
+            key[i] = lane + 32u * i < E ? val[i] : -INFINITY;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            const uint32_t e = lane + 32u * i;
+            if (e < E) {
+                val[i] = s[e];
+                key[i] = hash_routing ? 0.f : __fadd_rn(s[e], bias ? bias[e] : 0.f);
+            } else {
+                val[i] = 0.f;
+                key[i] = -INFINITY;
+            }
+        }
+    }
+    uint32_t sel[16];
+    float selv[16];
+    if (hash_routing) {
+        const uint32_t tok = token_ids[t];
+        if (tok >= vocab) {
+            if (lane == 0) atomicOr(error_flag, 1u);
+            return;
+        }
+        for (uint32_t j = 0; j < k; ++j) {
+            const uint32_t e = tid2eid[(size_t)tok * k + j];
+            if (e >= E) {
+                if (lane == 0) atomicOr(error_flag, 2u);
+                return;
+            }
+            sel[j] = e;
+            // fetch val of expert e from its owner lane
+            const uint32_t owner = e & 31u, slot = e >> 5;
+            float mine = 0.f;
+#pragma unroll
+            for (int i = 0; i < kMaxPerLane; ++i) if ((uint32_t)i == slot) mine = val[i];
+            selv[j] = __shfl_sync(0xffffffffu, mine, owner);
+        }
+    } else {
+        uint32_t removed = 0;  // bit i: this lane's entry i has been selected already
+        for (uint32_t j = 0; j < k; ++j) {
+            // lane-local best: larger key, ties to the lower id (= lower i within a lane)
+            float bk = 0.f;
+            uint32_t be = 0xffffffffu;
+#pragma unroll
+            for (int i = 0; i < kMaxPerLane; ++i) {
+                const uint32_t e = lane + 32u * i;
+                if (e < E && !((removed >> i) & 1u) && (be == 0xffffffffu || key[i] > bk)) {
+                    bk = key[i];
+                    be = e;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+                const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, o);
+                if (oe != 0xffffffffu && (be == 0xffffffffu || ok > bk || (ok == bk && oe < be))) {
+                    bk = ok;
+                    be = oe;
+                }
+            }
+            sel[j] = be;
+            const uint32_t owner = be & 31u, slot = be >> 5;
+            float mine = 0.f;
+#pragma unroll
+            for (int i = 0; i < kMaxPerLane; ++i) if ((uint32_t)i == slot) mine = val[i];
+            selv[j] = __shfl_sync(0xffffffffu, mine, owner);
+            if (lane == owner) removed |= 1u << slot;
+        }
+    }
+    if (lane == 0) {
+        if (score == VLB_SCORE_SOFTMAX) {
+            for (uint32_t j = 0; j < k; ++j) {
+                idx[(size_t)t * k + j] = sel[j];
+                weights[(size_t)t * k + j] = selv[j];
+            }
+        } else {
+            // route_from_indices, deepseek_v4_reference.cpp:80-121
+            double sum = 0.0;
+            for (uint32_t j = 0; j < k; ++j) sum += (double)selv[j];
+            if (!(sum > 0.0) || isinf(sum)) atomicOr(error_flag, 4u);
+            for (uint32_t j = 0; j < k; ++j) {
+                idx[(size_t)t * k + j] = sel[j];
+                weights[(size_t)t * k + j] =
+                    (float)((double)selv[j] / sum * (double)route_scale);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Dispatch: one CTA. Stable counting sort of the T*k (token, slot) elements by expert; the
+// shared expert's T pairs are appended at [T*k, T*k + T). Builds the work units (<= kUnitTokens
+// pairs of one expert each, experts ascending, shared last) and each token's combine list.
+constexpr int kDispatchThreads = 1024;
+
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p) {
+    extern __shared__ uint32_t dsm[];
+    const uint32_t E = p.E, k = p.k, T = p.T, n = T * k;
+    uint32_t* cnt = dsm;              // [E]
+    uint32_t* base = cnt + E;         // [E + 1]
+    uint32_t* wcnt = base + E + 1;    // [32 warps x E] per-warp counts of the current chunk
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    for (uint32_t e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (uint32_t i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[p.idx[i]], 1u);
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t acc = 0;
+        for (uint32_t e = 0; e < E; ++e) { base[e] = acc; acc += cnt[e]; }
+        base[E] = acc;
+    }
+    __syncthreads();
+    for (uint32_t e = tid; e <= E; e += blockDim.x) p.offsets[e] = base[e];
+    if (tid == 0) p.offsets[E + 1] = n + (p.has_shared ? T : 0u);
+    // stable placement, chunk by chunk in element order
+    for (uint32_t c0 = 0; c0 < n; c0 += blockDim.x) {
+        const uint32_t i = c0 + tid;
+        const bool valid = i < n;
+        const uint32_t e = valid ? p.idx[i] : 0xffffffffu;
+        for (uint32_t q = tid; q < 32u * E; q += blockDim.x) wcnt[q] = 0;
+        __syncthreads();
+        const uint32_t peers = __match_any_sync(0xffffffffu, e);
+        const uint32_t rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+        const uint32_t leader = __ffs(peers) - 1u;
+        if (valid && lane == leader) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        uint32_t before = 0;
+        if (valid) for (uint32_t w = 0; w < warp; ++w) before += wcnt[w * E + e];
+        __syncthreads();
+        if (valid) {
+            const uint32_t pos = base[e] + before + rank_in_warp;
+            p.pair_token[pos] = i / k;
+            p.pair_slot[pos] = i % k;
+            p.pair_weight[pos] = p.weights[i];
+            p.combine_pairs[i] = pos;  // element -> pair position (reordered below)
+        }
+        __syncthreads();
+        // advance bases by this chunk's counts
+        for (uint32_t ee = tid; ee < E; ee += blockDim.x) {
+            uint32_t s = 0;
+            for (uint32_t w = 0; w < kDispatchThreads / 32u; ++w) s += wcnt[w * E + ee];
+            base[ee] += s;
+        }
+        __syncthreads();
+    }
+    if (p.has_shared)
+        for (uint32_t t = tid; t < T; t += blockDim.x) {
+            p.pair_token[n + t] = t;
+            p.pair_slot[n + t] = 0;
+            p.pair_weight[n + t] = 1.f;
+        }
+    // combine order per token: V4 sums its pairs in pair order (expert ascending, then slot);
+    // OLMoE keeps rank order.
+    if (!p.weight_after_down)
+        for (uint32_t t = tid; t < T; t += blockDim.x) {
+            uint32_t* c = p.combine_pairs + (size_t)t * k;
+            for (uint32_t a = 1; a < k; ++a) {
+                const uint32_t v = c[a];
+                uint32_t b = a;
+                while (b > 0 && c[b - 1] > v) { c[b] = c[b - 1]; --b; }
+                c[b] = v;
+            }
+        }
+    __syncthreads();
+    // work units: restore per-expert counts from offsets and split into <= kUnitTokens pairs
+    if (tid == 0) {
+        uint32_t nu = 0, na = 0;
+        const uint32_t ne = E + (p.has_shared ? 1u : 0u);
+        for (uint32_t e = 0; e < ne; ++e) {
+            const uint32_t b = e < E ? p.offsets[e] : n;
+            const uint32_t c = e < E ? p.offsets[e + 1] - p.offsets[e] : T;
+            if (c == 0) continue;
+            ++na;
+            for (uint32_t s = 0; s < c && nu < p.max_units; s += kUnitTokens) {
+                p.units[nu].expert = e;
+                p.units[nu].pair_begin = b + s;
+                p.units[nu].count = min((uint32_t)kUnitTokens, c - s);
+                p.units[nu].pad = 0;
+                ++nu;
+            }
+        }
+        p.counters[0] = nu;
+        p.counters[1] = na;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Expert kernels. Persistent CTAs walk a contiguous range of work items; an item is one unit
+// (<= 4 pairs of one expert) x one row tile. Gate/up: a warp takes 4 gate rows and the same 4
+// up rows, so the SwiGLU epilogue needs nothing from other warps.
+constexpr int kGuRowsPerWarp = 4;
+constexpr int kGuRowsPerCta = kGuRowsPerWarp * 8;  // 32 intermediate rows per item
+constexpr int kDnRowsPerWarp = 8;
+constexpr int kDnRowsPerCta = kDnRowsPerWarp * 8;  // 64 hidden rows per item
+
+template <uint32_t FMT, int TOKC>
+__device__ __forceinline__ void gateup_rows(const MoeParams& p, const DevMat& w1, const DevMat& w3,
+                                            uint32_t row, const float* xs, const GridSmem& gs,
+                                            const Unit& u, uint32_t e) {
+    float acc[2 * kGuRowsPerWarp][TOKC];
+#pragma unroll
+    for (int r = 0; r < 2 * kGuRowsPerWarp; ++r)
+#pragma unroll
+        for (int t = 0; t < TOKC; ++t) acc[r][t] = 0.f;
+    warp_dot<FMT, kGuRowsPerWarp, kGuRowsPerWarp, TOKC>(w1, w3, row, row, xs, p.H / 32u, gs, acc);
+    warp_reduce<2 * kGuRowsPerWarp, TOKC>(acc);
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool shared = e == p.E;
+    const float limit = shared ? p.shared_limit : p.routed_limit;
+#pragma unroll
+    for (int r = 0; r < kGuRowsPerWarp; ++r)
+#pragma unroll
+        for (int t = 0; t < TOKC; ++t) {
+            if (lane != (uint32_t)(r * TOKC + t) % 32u || (uint32_t)t >= u.count) continue;
+            const uint32_t pair = u.pair_begin + t;
+            const float g = acc[r][t], up = acc[kGuRowsPerWarp + r][t];
+            float a;
+            if (p.weight_after_down) {
+                // OLMoE: float SwiGLU with expf (olmoe_runtime.cpp:1279)
+                a = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
+            } else {
+                // execute_expert: double SwiGLU, optional clamp, route weight before down
+                // (deepseek_v4_graph.cpp:1865-1890)
+                double gv = (double)g, uv = (double)up;
+                if (limit > 0.f) {
+                    gv = fmin(gv, (double)limit);
+                    uv = fmin(fmax(uv, -(double)limit), (double)limit);
+                }
+                double v = gv / (1.0 + exp(-gv)) * uv;
+                if (!shared) v *= (double)p.pair_weight[pair];
+                a = (float)v;
+            }
+            p.act[(size_t)pair * p.I + row + r] = a;
+        }
+}
+
+template <uint32_t FMT, int TOKC>
+__device__ __forceinline__ void down_rows(const MoeParams& p, const DevMat& w2, uint32_t row,
+                                          const float* xs, const GridSmem& gs, const Unit& u) {
+    float acc[kDnRowsPerWarp][TOKC];
+#pragma unroll
+    for (int r = 0; r < kDnRowsPerWarp; ++r)
+#pragma unroll
+        for (int t = 0; t < TOKC; ++t) acc[r][t] = 0.f;
+    warp_dot<FMT, kDnRowsPerWarp, 0, TOKC>(w2, w2, row, 0u, xs, p.I / 32u, gs, acc);
+    warp_reduce<kDnRowsPerWarp, TOKC>(acc);
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int r = 0; r < kDnRowsPerWarp; ++r)
+#pragma unroll
+        for (int t = 0; t < TOKC; ++t)
+            if (lane == (uint32_t)(r * TOKC + t) % 32u && (uint32_t)t < u.count)
+                p.y[(size_t)(u.pair_begin + t) * p.H + row + r] = acc[r][t];
+}
+
+template <int TOKC>
+__device__ __forceinline__ void gateup_dispatch(const MoeParams& p, const DevMat& w1,
+                                                const DevMat& w3, uint32_t row, const float* xs,
+                                                const GridSmem& gs, const Unit& u, uint32_t e) {
+    switch (w1.type) {
+        case kTypeIq2Xxs: gateup_rows<kTypeIq2Xxs, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeQ8_0: gateup_rows<kTypeQ8_0, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeIq3Xxs: gateup_rows<kTypeIq3Xxs, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        default: gateup_rows<kTypeIq1S, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+    }
+}
+
+template <int TOKC>
+__device__ __forceinline__ void down_dispatch(const MoeParams& p, const DevMat& w2, uint32_t row,
+                                              const float* xs, const GridSmem& gs, const Unit& u) {
+    switch (w2.type) {
+        case kTypeIq2Xxs: down_rows<kTypeIq2Xxs, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeQ8_0: down_rows<kTypeQ8_0, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeIq3Xxs: down_rows<kTypeIq3Xxs, TOKC>(p, w2, row, xs, gs, u); break;
+        default: down_rows<kTypeIq1S, TOKC>(p, w2, row, xs, gs, u); break;
+    }
+}
+
+template <bool GATEUP>
+__global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const GridSmem gs = stage_grids(p.grids, smem);
+    float* xs = reinterpret_cast<float*>(smem + kGridSmemBytes);
+    const uint32_t n_units = p.counters[0];
+    const uint32_t rows_per_item = GATEUP ? kGuRowsPerCta : kDnRowsPerCta;
+    const uint32_t tiles = (GATEUP ? p.I : p.H) / rows_per_item;
+    const uint32_t cols = GATEUP ? p.H : p.I;
+    const uint64_t n_items = (uint64_t)n_units * tiles;
+    const uint64_t begin = n_items * blockIdx.x / gridDim.x;
+    const uint64_t end = n_items * (blockIdx.x + 1) / gridDim.x;
+    const uint32_t warp = threadIdx.x >> 5;
+    uint32_t staged = 0xffffffffu;
+    for (uint64_t item = begin; item < end; ++item) {
+        const uint32_t ui = (uint32_t)(item / tiles), tile = (uint32_t)(item % tiles);
+        const Unit u = p.units[ui];
+        if (ui != staged) {
+            const float* rows[kUnitTokens];
+#pragma unroll
+            for (int t = 0; t < kUnitTokens; ++t) {
+                const uint32_t pair = u.pair_begin + t;
+                rows[t] = (uint32_t)t < u.count
+                              ? (GATEUP ? p.x + (size_t)p.pair_token[pair] * p.H
+                                        : p.act + (size_t)pair * p.I)
+                              : nullptr;
+            }
+            __syncthreads();
+            stage_x<kUnitTokens>(xs, rows, cols);
+            __syncthreads();
+            staged = ui;
+        }
+        const uint32_t row = tile * rows_per_item + warp * (GATEUP ? kGuRowsPerWarp : kDnRowsPerWarp);
+        if (GATEUP) {
+            const DevMat w1 = p.mats[u.expert];
+            const DevMat w3 = p.mats[(p.E + 1) + u.expert];
+            if (u.count == 1) gateup_dispatch<1>(p, w1, w3, row, xs, gs, u, u.expert);
+            else if (u.count == 2) gateup_dispatch<2>(p, w1, w3, row, xs, gs, u, u.expert);
+            else gateup_dispatch<4>(p, w1, w3, row, xs, gs, u, u.expert);
+        } else {
+            const DevMat w2 = p.mats[2 * (p.E + 1) + u.expert];
+            if (u.count == 1) down_dispatch<1>(p, w2, row, xs, gs, u);
+            else if (u.count == 2) down_dispatch<2>(p, w2, row, xs, gs, u);
+            else down_dispatch<4>(p, w2, row, xs, gs, u);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Combine (deepseek_v4_graph.cpp:2214-2227, :2263-2266; olmoe_runtime.cpp:1282-1285).
+__global__ void __launch_bounds__(256) combine_kernel(MoeParams p) {
+    const uint32_t t = blockIdx.y;
+    const uint32_t c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
+    if (c4 >= p.H) return;
+    const uint32_t* cp = p.combine_pairs + (size_t)t * p.k;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t j = 0; j < p.k; ++j) {
+        const uint32_t pair = cp[j];
+        const float4 v = *reinterpret_cast<const float4*>(p.y + (size_t)pair * p.H + c4);
+        if (p.weight_after_down) {
+            const float w = p.pair_weight[pair];
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        } else {
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+    }
+    if (p.has_shared) {
+        const float4 v = *reinterpret_cast<const float4*>(p.y + (size_t)(p.T * p.k + t) * p.H + c4);
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+    }
+    *reinterpret_cast<float4*>(p.out + (size_t)t * p.H + c4) = acc;
+}
+
+// ---------------------------------------------------------------------------------------------
+// RMSNorm (deepseek_v4_reference.cpp:170-206), one CTA per row.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ w,
+                                                       uint32_t width, float eps,
+                                                       float* __restrict__ out) {
+    __shared__ double part[8];
+    const float* xr = x + (size_t)blockIdx.x * width;
+    double sq = 0.0;
+    for (uint32_t c = threadIdx.x; c < width; c += blockDim.x) {
+        const double v = (double)xr[c];
+        sq = fma(v, v, sq);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((threadIdx.x & 31u) == 0) part[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    double total = 0.0;
+    for (int i = 0; i < 8; ++i) total += part[i];
+    const double inv = 1.0 / sqrt(total / (double)width + (double)eps);
+    for (uint32_t c = threadIdx.x; c < width; c += blockDim.x)
+        out[(size_t)blockIdx.x * width + c] = (float)((double)xr[c] * inv * (double)w[c]);
+}
+
+// =============================================================================================
+// launchers
+static int g_num_sms = 0;
+static int num_sms() {
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+cudaError_t launch_dequant(const DevMat& m, const Grids& g, float* out, cudaStream_t s) {
+    const size_t groups = (size_t)m.rows * (m.cols / 32u);
+    dequant_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, s>>>(m, g, out);
+    return cudaGetLastError();
+}
+
+template <uint32_t FMT, int TOKC>
+static cudaError_t gemv_launch(const DevMat& m, const Grids& g, const float* x, uint32_t ntok,
+                               uint32_t xs, float* y, uint32_t ys, cudaStream_t s) {
+    const size_t smem = kGridSmemBytes + (size_t)TOKC * m.cols * sizeof(float);
+    auto kern = gemv_kernel<FMT, TOKC>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const unsigned grid = (m.rows + kGemvRows * kGemvWarps - 1) / (kGemvRows * kGemvWarps);
+    kern<<<grid, 256, smem, s>>>(m, g, x, ntok, xs, y, ys);
+    return cudaGetLastError();
+}
+
+template <int TOKC>
+static cudaError_t gemv_type(const DevMat& m, const Grids& g, const float* x, uint32_t ntok,
+                             uint32_t xs, float* y, uint32_t ys, cudaStream_t s) {
+    switch (m.type) {
+        case kTypeQ8_0: return gemv_launch<kTypeQ8_0, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeIq2Xxs: return gemv_launch<kTypeIq2Xxs, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeIq3Xxs: return gemv_launch<kTypeIq3Xxs, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeIq1S: return gemv_launch<kTypeIq1S, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_t ntok,
+                        uint32_t xstride, float* y, uint32_t ystride, cudaStream_t s) {
+    if (ntok == 0) return cudaSuccess;
+    if (ntok == 1) return gemv_type<1>(m, g, x, ntok, xstride, y, ystride, s);
+    if (ntok == 2) return gemv_type<2>(m, g, x, ntok, xstride, y, ystride, s);
+    return gemv_type<4>(m, g, x, ntok, xstride, y, ystride, s);
+}
+
+cudaError_t launch_router(const float* x, const float* w, uint32_t T, uint32_t H, uint32_t E,
+                          int score, float* logits, float* scores, cudaStream_t s) {
+    dim3 grid((E + 7) / 8, (T + kRouterTok - 1) / kRouterTok);
+    router_kernel<<<grid, 256, 0, s>>>(x, w, T, H, E, score, logits, scores);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scores(const float* logits, size_t n, int score, float* scores,
+                          cudaStream_t s) {
+    score_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(logits, n, score, scores);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route(const float* scores, const float* bias, const uint32_t* token_ids,
+                         const uint32_t* tid2eid, uint32_t vocab, uint32_t T, uint32_t E,
+                         uint32_t k, int score, int hash_routing, float route_scale,
+                         uint32_t* idx, float* weights, uint32_t* error_flag, cudaStream_t s) {
+    route_kernel<<<(T + 7) / 8, 256, 0, s>>>(scores, bias, token_ids, tid2eid, vocab, T, E, k,
+                                             score, hash_routing, route_scale, idx, weights,
+                                             error_flag);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
+    cudaError_t e;
+    if (ev) cudaEventRecord(ev[0], s);
+    // routing: router projection (or supplied logits) -> scores -> top-k
+    if (p.logits_in) {
+        e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
+    } else {
+        e = launch_router(p.x, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
+    }
+    if (e != cudaSuccess) return e;
+    e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
+                     p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
+    if (e != cudaSuccess) return e;
+    if (ev) cudaEventRecord(ev[1], s);
+    const size_t dsmem = ((size_t)p.E * 2 + 1 + 32u * p.E) * sizeof(uint32_t);
+    e = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsmem);
+    if (e != cudaSuccess) return e;
+    dispatch_kernel<<<1, kDispatchThreads, dsmem, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (ev) cudaEventRecord(ev[2], s);
+    // experts
+    const int ctas_per_sm = 2;
+    const unsigned grid = (unsigned)(num_sms() * ctas_per_sm);
+    const size_t gu_smem = kGridSmemBytes + (size_t)kUnitTokens * p.H * sizeof(float);
+    e = cudaFuncSetAttribute(expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gu_smem);
+    if (e != cudaSuccess) return e;
+    expert_kernel<true><<<grid, 256, gu_smem, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (ev) cudaEventRecord(ev[3], s);
+    const size_t dn_smem = kGridSmemBytes + (size_t)kUnitTokens * p.I * sizeof(float);
+    e = cudaFuncSetAttribute(expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem);
+    if (e != cudaSuccess) return e;
+    expert_kernel<false><<<grid, 256, dn_smem, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (ev) cudaEventRecord(ev[4], s);
+    dim3 cg((p.H / 4 + 255) / 256, p.T);
+    combine_kernel<<<cg, 256, 0, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (ev) cudaEventRecord(ev[5], s);
+    return cudaSuccess;
+}
+
+cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
+                            float eps, float* out, cudaStream_t s) {
+    rms_norm_kernel<<<rows, 256, 0, s>>>(x, w, width, eps, out);
+    return cudaGetLastError();
+}
+
+}  // namespace vlb

@@ -1,0 +1,29 @@
+// Host-side launchers of the vlb200 kernels (implemented in vlb_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "vlb_internal.cuh"
+
+namespace vlb {
+
+cudaError_t launch_dequant(const DevMat& m, const Grids& g, float* out, cudaStream_t s);
+cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_t ntok,
+                        uint32_t xstride, float* y, uint32_t ystride, cudaStream_t s);
+cudaError_t launch_router(const float* x, const float* w, uint32_t T, uint32_t H, uint32_t E,
+                          int score, float* logits, float* scores, cudaStream_t s);
+cudaError_t launch_scores(const float* logits, size_t n, int score, float* scores,
+                          cudaStream_t s);
+cudaError_t launch_route(const float* scores, const float* bias, const uint32_t* token_ids,
+                         const uint32_t* tid2eid, uint32_t vocab, uint32_t T, uint32_t E,
+                         uint32_t k, int score, int hash_routing, float route_scale,
+                         uint32_t* idx, float* weights, uint32_t* error_flag, cudaStream_t s);
+// The whole decode layer: routing, dispatch, gate/up + SwiGLU, down, combine.
+// ev: optional 6 events recorded at the phase boundaries (start, routed, dispatched, gate/up done,
+// down done, combined).
+constexpr int kMoePhases = 5;
+cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev = nullptr);
+cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
+                            float eps, float* out, cudaStream_t s);
+
+}  // namespace vlb
