@@ -213,6 +213,24 @@ int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* lo
                      const uint32_t* tid2eid_dev, uint32_t vocab, uint32_t T, uint32_t E,
                      uint32_t k, float route_scale, uint32_t* idx_dev, float* weights_dev,
                      void* stream);
+/* The same router as vlb_route_device for callers that cannot allocate device memory: code
+ * running inside a CUDA host callback (where CUDA API calls such as cudaMalloc are not
+ * permitted), a runtime whose ResourceGovernor is refusing new reservations under memory
+ * pressure, and decode loops that cannot take the synchronisation cudaMalloc/cudaFree may cause.
+ * This entry point has no counterpart in the reference. It allocates nothing: its score scratch
+ * is a fixed 1 MiB array inside the library, present on every GPU that loads the library until
+ * the process exits, so T*E may be at most 262,080 (larger requests return
+ * VLB_ERR_RESOURCE_EXHAUSTED). The caller passes device inputs and outputs as for
+ * vlb_route_device and the device ordinal to run on (made current for the call). The first call
+ * on each device also performs a one-time set-up (it looks up the array's device address), so
+ * make that first call before any stream capture. Every call uses the same array: calls that
+ * overlap on the GPU (other streams, other host threads) race on it; serialise them. Synchronous:
+ * returns after the route is written. */
+int vlb_route_device_noalloc(int ordinal, int score, int hash_routing, const float* logits_dev,
+                             const float* bias_dev, const uint32_t* token_ids_dev,
+                             const uint32_t* tid2eid_dev, uint32_t vocab, uint32_t T, uint32_t E,
+                             uint32_t k, float route_scale, uint32_t* idx_dev,
+                             float* weights_dev, void* stream);
 /* Router projection logits[T x E] = f32(sum double(x) double(w)) (deepseek_v4_graph.cpp:
  * 735-767). */
 int vlb_router_logits_device(vlb_handle* h, const float* x_dev, const float* w_dev, uint32_t T,

@@ -135,7 +135,7 @@ EXPORTS = (
     "vlb_memcpy_h2d vlb_memcpy_d2h vlb_allocated_bytes vlb_upload_matrix vlb_release_matrix "
     "vlb_matrix_bytes vlb_matvec vlb_matvec_device vlb_dequantize_device vlb_layer_create "
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
-    "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_route_device vlb_router_logits_device vlb_rms_norm_device"
+    "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
 ).split()
 
 
@@ -181,6 +181,7 @@ def load_library() -> C.CDLL:
         "vlb_layer_set_profiling": (I, [P, P, I]),
         "vlb_layer_phase_times": (I, [P, P, C.POINTER(C.c_float), I]),
         "vlb_route_device": (I, [P, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
+        "vlb_route_device_noalloc": (I, [I, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
         "vlb_router_logits_device": (I, [P, P, P, U32, U32, U32, P, P]),
         "vlb_rms_norm_device": (I, [P, P, P, U32, U32, F, P, P]),
     }

@@ -54,6 +54,11 @@ std::string cuda_msg(const char* op, cudaError_t e) {
 
 }  // namespace
 
+namespace vlb {
+// Lets other sources of the library report a failure through vlb_thread_error.
+void set_thread_error(const std::string& msg) { t_error = msg; }
+}  // namespace vlb
+
 struct vlb_handle {
     int device = 0;
     cudaStream_t stream = nullptr;
