@@ -45,51 +45,55 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled through NVML (read-only queries) every few
+    milliseconds while the timed region runs; falls back to nvidia-smi polling."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {  # nvmlClocksEventReason bits
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_s: float = 0.005):
         self.index = index
-        self.proc = None
-        self.file = None
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = False
+        self._thread = None
 
     def start(self):
+        import threading
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return
+
+        def run():
+            while not self._stop:
+                try:
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    self.reasons |= pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    pass
+                time.sleep(self.period)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self._thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
-        os.unlink(self.file.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            if len(r) < 9:
-                continue
-            for name, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        self._stop = True
+        self._thread.join(timeout=2)
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        names = sorted(n for n, bit in self.REASONS.items() if self.reasons & bit)
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples), "source": "nvml"}
 
 
 def phase_bytes(spec, W, layer, T, offsets):
@@ -252,7 +256,7 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(out.nbytes),
                 "timing": "host wall clock around the synchronous C-ABI call"},
         "clocks": clk,
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": 7 * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget)

@@ -198,8 +198,9 @@ def test_gpu_layer_full_cfg1_single_token(full_cfg1, oracle):
 
 def test_gpu_layer_full_cfg1_batch_properties(full_cfg1, oracle):
     """T=64 at full size: the route and permutation are bit-exact against the oracle (router in
-    f64 on the CPU), and every token's output is bit-identical to running it alone (the kernel's
-    per-token arithmetic does not depend on the batch)."""
+    f64 on the CPU); tokens taken from the batch match the oracle run on them alone; and every
+    token's output agrees with running it alone to 1e-6 (the kernels' column-split shape depends
+    on the batch size, so the f32 summation order - not the arithmetic - differs)."""
     spec, W, layer = full_cfg1
     x, _, _ = synth.activations(spec, 64, seed=6)
     out = layer.forward(x)
@@ -210,9 +211,12 @@ def test_gpu_layer_full_cfg1_batch_properties(full_cfg1, oracle):
     assert ulp_diff(w, rw) <= 1
     roff, rpt, rps = oracle.dispatch(ridx, spec.experts)
     assert np.array_equal(off, roff) and np.array_equal(pt, rpt) and np.array_equal(ps, rps)
+    for t in (0, 37):
+        ref, _, _ = oracle.moe_forward(W, x[t:t + 1])
+        assert rel_err(out[t:t + 1], ref) <= TOL
     for t in (0, 13, 63):
         single = layer.forward(x[t:t + 1])
-        assert single.tobytes() == out[t:t + 1].tobytes()
+        assert rel_err(single, out[t:t + 1]) <= 1e-6
     assert np.all(np.isfinite(out))
 
 

@@ -573,8 +573,9 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     const size_t o_logits = carve(T * E * 4), o_scores = carve(T * E * 4), o_idx = carve(T * k * 4),
                  o_w = carve(T * k * 4), o_off = carve((E + 2) * 4), o_pt = carve(P * 4),
                  o_ps = carve(P * 4), o_pw = carve(P * 4), o_units = carve((size_t)mu * sizeof(Unit)),
-                 o_cnt = carve(16), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
-                 o_y = carve(P * H * 4);
+                 o_cnt = carve(32), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
+                 o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
+                 o_xd = carve(T * H * 8);
     TRY(h->galloc(off, "vlb-layer-workspace", &L->ws));
     TRY(h->galloc(T * H * 4, "vlb-layer-x", (void**)&L->x_dev));
     TRY(h->galloc(T * 4, "vlb-layer-tokens", (void**)&L->tok_dev));
@@ -592,6 +593,13 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.shared_limit = d->shared_swiglu_limit;
     p.vocab = d->vocab;
     p.has_shared = has_shared ? 1 : 0;
+    p.has_legacy = 0;
+    p.has_mma = 0;
+    for (const vlb_matrix* m : hm) {
+        if (!m) continue;
+        if (m->type == VLB_TYPE_IQ2_XXS || m->type == VLB_TYPE_Q8_0) p.has_mma = 1;
+        else p.has_legacy = 1;
+    }
     p.router = L->router;
     p.bias = L->bias;
     p.tid2eid = L->tid2eid;
@@ -610,6 +618,9 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.combine_pairs = reinterpret_cast<uint32_t*>(ws + o_cp);
     p.act = reinterpret_cast<float*>(ws + o_act);
     p.y = reinterpret_cast<float*>(ws + o_y);
+    p.xscale = reinterpret_cast<float*>(ws + o_xs);
+    p.act_max = reinterpret_cast<uint32_t*>(ws + o_am);
+    p.xd = reinterpret_cast<double*>(ws + o_xd);
     p.max_units = mu;
     *out = L;
     return VLB_OK;
@@ -636,7 +647,7 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.logits_in = logits;
     p.out = out;
     p.grids = h->grids();
-    VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, 16, s));
+    VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, 32, s));
     VLB_CUDA(h, launch_moe(p, s, L->profiling ? L->ev : nullptr));
     L->last_T = T;
     L->last_logits_given = logits != nullptr;
@@ -761,15 +772,20 @@ int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* lo
 int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint32_t T,
                              uint32_t H, uint32_t E, float* logits, void* stream) {
     VLB_LOCK(h);
-    if (!x || !w || !logits || T == 0 || H == 0 || E == 0)
+    if (!x || !w || !logits || T == 0 || H == 0 || E == 0 || H % 4)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid router argument");
-    float* scores = nullptr;
-    int st = h->galloc((size_t)T * E * 4, "vlb-router-scratch", (void**)&scores);
+    float* scratch = nullptr;
+    const size_t sbytes = (size_t)T * E * 4 + (size_t)T * 4 + 255;
+    const size_t xbytes = (size_t)T * H * 8;
+    int st = h->galloc(sbytes + xbytes, "vlb-router-scratch", (void**)&scratch);
     if (st != VLB_OK) return st;
+    double* xd = reinterpret_cast<double*>(reinterpret_cast<char*>(scratch) + sbytes / 256 * 256);
+    float* xscale = scratch + (size_t)T * E;
     cudaStream_t s = h->pick(stream);
-    cudaError_t e = launch_router(x, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scores, s);
+    cudaError_t e = launch_prescale(x, T, H, xscale, xd, s);
+    if (e == cudaSuccess) e = launch_router(xd, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scratch, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    h->gfree(scores);
+    h->gfree(scratch);
     if (e != cudaSuccess) return h->cuda_fail("router", e);
     return VLB_OK;
 }

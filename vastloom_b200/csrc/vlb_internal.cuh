@@ -164,6 +164,8 @@ struct MoeParams {
     float shared_limit;
     uint32_t vocab;
     int has_shared;
+    int has_legacy;          // some expert uses a format the CUDA-core kernels serve (IQ3_XXS, IQ1_S)
+    int has_mma;             // some expert uses a format the tensor-core kernels serve (IQ2_XXS, Q8_0)
     // weights
     const float* router;     // [E x H]
     const float* bias;       // [E]
@@ -184,11 +186,14 @@ struct MoeParams {
     uint32_t* pair_slot;     // [T*k + T]
     float* pair_weight;      // [T*k + T]
     Unit* units;             // [max_units]
-    uint32_t* counters;      // [4]: n_units, n_active, combine_ready, error
+    uint32_t* counters;      // [8]: n_units, n_active, gate/up next item, error flags, down next item
     uint32_t* combine_pairs; // [T x k]: each token's pairs in (expert, slot) order
     float* act;              // [(T*k + T) x I]
     float* y;                // [(T*k + T) x H]
     float* out;              // [T x H]
+    float* xscale;           // [T]: power-of-two prescale of each token's activation row
+    double* xd;              // [T x H]: activations widened to f64 for the router projection
+    uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
     uint32_t max_units;
 };
 

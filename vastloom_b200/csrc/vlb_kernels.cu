@@ -10,8 +10,11 @@
 //   combine_kernel    per-token deterministic combine in the reference's order + shared expert
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "vlb_gemv.cuh"
 #include "vlb_launch.h"
+#include "vlb_mma.cuh"
 
 namespace vlb {
 
@@ -114,7 +117,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 // the per-expert score (sqrt_softplus / sigmoid; softmax is applied per token in route_kernel).
 // CTA: 8 warps = 8 experts, a chunk of up to 8 tokens, columns staged 1024 at a time.
 constexpr int kRouterTok = 8;
-constexpr int kRouterChunk = 1024;
 
 __device__ __forceinline__ float sqrt_softplus_dev(float v) {
     const double p = (double)v;
@@ -133,50 +135,63 @@ __device__ __forceinline__ float score_dev(int score, float logit) {
     return logit;
 }
 
-__global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(256) router_kernel(const double* __restrict__ xd,
                                                      const float* __restrict__ w, uint32_t T,
                                                      uint32_t H, uint32_t E, int score,
                                                      float* __restrict__ logits,
                                                      float* __restrict__ scores) {
-    __shared__ __align__(16) float xs[kRouterTok][kRouterChunk];
+    // One CTA per expert row; its 8 warps split the columns (H/8 each) and the partial sums are
+    // added in a fixed order through shared memory. The activations arrive widened to f64
+    // (token_prescale_kernel), so each router weight is converted once and reused for every token;
+    // the products are exact in f64. Tokens go kRouterTok at a time.
+    __shared__ double part[8][kRouterTok];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t e = blockIdx.x * 8u + warp;
-    const uint32_t t0 = blockIdx.y * kRouterTok;
-    const uint32_t nt = min((uint32_t)kRouterTok, T - t0);
-    double acc[kRouterTok];
+    const uint32_t e = blockIdx.x;
+    // columns of this warp: a multiple of 4 (H is), possibly empty for tiny H
+    const uint32_t span = ((H / 4u + 7u) / 8u) * 4u;
+    const uint32_t c0 = min(warp * span, H), c1 = min(c0 + span, H);
+    const float* wr = w + (size_t)e * H;
+    for (uint32_t t0 = 0; t0 < T; t0 += kRouterTok) {
+        const uint32_t nt = min((uint32_t)kRouterTok, T - t0);
+        double acc[kRouterTok];
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
-    for (uint32_t c0 = 0; c0 < H; c0 += kRouterChunk) {
-        const uint32_t cn = min((uint32_t)kRouterChunk, H - c0);
-        __syncthreads();
-        for (uint32_t i = threadIdx.x; i < kRouterTok * cn; i += blockDim.x) {
-            const uint32_t t = i / cn, c = i % cn;
-            xs[t][c] = t < nt ? x[(size_t)(t0 + t) * H + c0 + c] : 0.f;
-        }
-        __syncthreads();
-        if (e < E) {
-            for (uint32_t c = lane; c < cn; c += 32u) {
-                const double wv = (double)__ldg(w + (size_t)e * H + c0 + c);
+        for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
+        for (uint32_t c = c0 + lane * 4u; c < c1; c += 128u) {
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c));
+            const double w0 = wv.x, w1 = wv.y, w2 = wv.z, w3 = wv.w;
 #pragma unroll
-                for (int t = 0; t < kRouterTok; ++t) acc[t] = fma(wv, (double)xs[t][c], acc[t]);
+            for (int t = 0; t < kRouterTok; ++t) {
+                if ((uint32_t)t >= nt) break;
+                const double* xr = xd + (size_t)(t0 + t) * H + c;
+                const double2 a = __ldg(reinterpret_cast<const double2*>(xr));
+                const double2 b = __ldg(reinterpret_cast<const double2*>(xr + 2));
+                acc[t] = fma(w0, a.x, acc[t]);
+                acc[t] = fma(w1, a.y, acc[t]);
+                acc[t] = fma(w2, b.x, acc[t]);
+                acc[t] = fma(w3, b.y, acc[t]);
             }
         }
-    }
-    if (e >= E) return;
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
-        double v = acc[t];
+        for (int t = 0; t < kRouterTok; ++t) {
+            double v = acc[t];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        acc[t] = v;
-    }
-    if (lane < nt) {
-        double v = 0.0;
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            acc[t] = v;
+        }
+        if (lane == 0) {
 #pragma unroll
-        for (int t = 0; t < kRouterTok; ++t) if ((uint32_t)t == lane) v = acc[t];
-        const float lg = (float)v;
-        logits[(size_t)(t0 + lane) * E + e] = lg;
-        scores[(size_t)(t0 + lane) * E + e] = score_dev(score, lg);
+            for (int t = 0; t < kRouterTok; ++t) part[warp][t] = acc[t];
+        }
+        __syncthreads();
+        if (threadIdx.x < nt) {
+            const uint32_t t = threadIdx.x;
+            double v = 0.0;
+            for (int w8 = 0; w8 < 8; ++w8) v += part[w8][t];
+            const float lg = (float)v;
+            logits[(size_t)(t0 + t) * E + e] = lg;
+            scores[(size_t)(t0 + t) * E + e] = score_dev(score, lg);
+        }
+        __syncthreads();
     }
 }
 
@@ -324,25 +339,51 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
 // pairs of one expert each, experts ascending, shared last) and each token's combine list.
 constexpr int kDispatchThreads = 1024;
 
+// Exclusive scan of v[0..n) in shared memory by warp 0 (n <= a few thousand); returns the total.
+__device__ __forceinline__ uint32_t warp0_exclusive_scan(uint32_t* v, uint32_t n, uint32_t* total) {
+    if (threadIdx.x < 32u) {
+        const uint32_t lane = threadIdx.x;
+        uint32_t carry = 0;
+        for (uint32_t b = 0; b < n; b += 32u) {
+            const uint32_t i = b + lane;
+            const uint32_t x = i < n ? v[i] : 0u;
+            uint32_t incl = x;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= (uint32_t)o) incl += y;
+            }
+            if (i < n) v[i] = carry + incl - x;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) *total = carry;
+    }
+    __syncthreads();
+    return *total;
+}
+
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p) {
     extern __shared__ uint32_t dsm[];
     const uint32_t E = p.E, k = p.k, T = p.T, n = T * k;
-    uint32_t* cnt = dsm;              // [E]
-    uint32_t* base = cnt + E;         // [E + 1]
+    uint32_t* cnt = dsm;              // [E + 1]
+    uint32_t* off = cnt + E + 1;      // [E + 1] expert offsets (kept)
+    uint32_t* base = off + E + 1;     // [E + 1] running placement bases
     uint32_t* wcnt = base + E + 1;    // [32 warps x E] per-warp counts of the current chunk
+    __shared__ uint32_t total_s;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    for (uint32_t e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+    for (uint32_t e = tid; e <= E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (uint32_t i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[p.idx[i]], 1u);
     __syncthreads();
-    if (tid == 0) {
-        uint32_t acc = 0;
-        for (uint32_t e = 0; e < E; ++e) { base[e] = acc; acc += cnt[e]; }
-        base[E] = acc;
-    }
+    for (uint32_t e = tid; e <= E; e += blockDim.x) off[e] = cnt[e];
     __syncthreads();
-    for (uint32_t e = tid; e <= E; e += blockDim.x) p.offsets[e] = base[e];
+    warp0_exclusive_scan(off, E + 1, &total_s);  // off[E] = n (cnt[E] = 0)
+    for (uint32_t e = tid; e <= E; e += blockDim.x) {
+        base[e] = off[e];
+        p.offsets[e] = off[e];
+    }
     if (tid == 0) p.offsets[E + 1] = n + (p.has_shared ? T : 0u);
+    __syncthreads();
     // stable placement, chunk by chunk in element order
     for (uint32_t c0 = 0; c0 < n; c0 += blockDim.x) {
         const uint32_t i = c0 + tid;
@@ -366,7 +407,6 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p)
             p.combine_pairs[i] = pos;  // element -> pair position (reordered below)
         }
         __syncthreads();
-        // advance bases by this chunk's counts
         for (uint32_t ee = tid; ee < E; ee += blockDim.x) {
             uint32_t s = 0;
             for (uint32_t w = 0; w < kDispatchThreads / 32u; ++w) s += wcnt[w * E + ee];
@@ -374,6 +414,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p)
         }
         __syncthreads();
     }
+    for (uint32_t i = tid; i < n + (p.has_shared ? T : 0u); i += blockDim.x) p.act_max[i] = 0u;
     if (p.has_shared)
         for (uint32_t t = tid; t < T; t += blockDim.x) {
             p.pair_token[n + t] = t;
@@ -392,26 +433,35 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p)
                 c[b] = v;
             }
         }
+    // Work units: each expert's pairs split into <= kUnitTokens; the shared expert's units come
+    // first (they are the heaviest: every token, usually the widest storage type), so dynamically
+    // scheduled CTAs start on them and finish on light ones. Ordinal 0 = shared, e + 1 = expert e.
+    uint32_t* nu = base;  // reuse: units per ordinal, scanned to first unit index
+    for (uint32_t o = tid; o <= E; o += blockDim.x) {
+        uint32_t c = 0;
+        if (o == 0) c = p.has_shared ? T : 0u;
+        else c = off[o] - off[o - 1];
+        nu[o] = (c + kUnitTokens - 1) / kUnitTokens;
+    }
     __syncthreads();
-    // work units: restore per-expert counts from offsets and split into <= kUnitTokens pairs
-    if (tid == 0) {
-        uint32_t nu = 0, na = 0;
-        const uint32_t ne = E + (p.has_shared ? 1u : 0u);
-        for (uint32_t e = 0; e < ne; ++e) {
-            const uint32_t b = e < E ? p.offsets[e] : n;
-            const uint32_t c = e < E ? p.offsets[e + 1] - p.offsets[e] : T;
-            if (c == 0) continue;
-            ++na;
-            for (uint32_t s = 0; s < c && nu < p.max_units; s += kUnitTokens) {
-                p.units[nu].expert = e;
-                p.units[nu].pair_begin = b + s;
-                p.units[nu].count = min((uint32_t)kUnitTokens, c - s);
-                p.units[nu].pad = 0;
-                ++nu;
-            }
+    const uint32_t n_units = warp0_exclusive_scan(nu, E + 1, &total_s);
+    for (uint32_t o = tid; o <= E; o += blockDim.x) {
+        const uint32_t e = o == 0 ? E : o - 1u;
+        const uint32_t b = o == 0 ? n : off[e];
+        const uint32_t c = o == 0 ? (p.has_shared ? T : 0u) : off[e + 1] - off[e];
+        uint32_t u = nu[o];
+        for (uint32_t s = 0; s < c && u < p.max_units; s += kUnitTokens, ++u) {
+            p.units[u].expert = e;
+            p.units[u].pair_begin = b + s;
+            p.units[u].count = min((uint32_t)kUnitTokens, c - s);
+            p.units[u].pad = 0;
         }
-        p.counters[0] = nu;
-        p.counters[1] = na;
+    }
+    if (tid == 0) {
+        p.counters[0] = n_units < p.max_units ? n_units : p.max_units;
+        uint32_t na = 0;
+        for (uint32_t e = 0; e < E; ++e) na += off[e + 1] > off[e];
+        p.counters[1] = na + (p.has_shared ? 1u : 0u);
     }
 }
 
@@ -462,6 +512,7 @@ __device__ __forceinline__ void gateup_rows(const MoeParams& p, const DevMat& w1
                 a = (float)v;
             }
             p.act[(size_t)pair * p.I + row + r] = a;
+            atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
         }
 }
 
@@ -507,6 +558,8 @@ __device__ __forceinline__ void down_dispatch(const MoeParams& p, const DevMat& 
     }
 }
 
+__device__ __forceinline__ bool mma_type(uint32_t t) { return t == kTypeIq2Xxs || t == kTypeQ8_0; }
+
 template <bool GATEUP>
 __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -524,6 +577,7 @@ __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
     for (uint64_t item = begin; item < end; ++item) {
         const uint32_t ui = (uint32_t)(item / tiles), tile = (uint32_t)(item % tiles);
         const Unit u = p.units[ui];
+        if (mma_type(p.mats[(GATEUP ? 0u : 2u * (p.E + 1)) + u.expert].type)) continue;
         if (ui != staged) {
             const float* rows[kUnitTokens];
 #pragma unroll
@@ -553,6 +607,211 @@ __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
             else down_dispatch<4>(p, w2, row, xs, gs, u);
         }
     }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Tensor-core decode expert kernel (IQ2_XXS and Q8_0 experts; vlb_mma.cuh). CTA = 8 warps:
+// 4 row groups x 2 column halves. Gate/up: a warp owns 32 output rows (two 16-row tiles of the
+// gate matrix and the same two of the up matrix), a CTA 128; down: a warp owns 64 rows, a CTA
+// 256. The two column halves are summed through shared memory before the epilogue.
+constexpr uint32_t kMmaTabBytes = 256u * 8u * 16u;      // fp16 IQ2_XXS table, 8 replicas
+constexpr uint32_t kMmaRedBytes = 7u * 32u * 8u * 4u;   // partial sums of the column splits
+constexpr uint32_t kMmaChunk = 4;                        // max items per work-stealing grab
+
+__global__ void token_prescale_kernel(const float* __restrict__ x, uint32_t T, uint32_t H,
+                                      float* __restrict__ scale, double* __restrict__ xd) {
+    // per token: the power-of-two prescale of the tensor-core activation pieces, and the row
+    // widened to f64 for the router projection
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t t = blockIdx.x * 8u + warp;
+    if (t >= T) return;
+    float m = 0.f;
+    for (uint32_t c = lane * 4u; c < H; c += 128u) {
+        const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        if (xd) {
+            double* o = xd + (size_t)t * H + c;
+            *reinterpret_cast<double2*>(o) = make_double2(v.x, v.y);
+            *reinterpret_cast<double2*>(o + 2) = make_double2(v.z, v.w);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) scale[t] = mma::prescale_for(m);
+}
+
+// CTA shape: rg_count row groups x (8 / rg_count) column splits. A warp owns one 16-row tile of
+// the gate matrix and the same tile of the up matrix (gate/up: 16 output rows), or two 16-row
+// tiles of the down matrix (32 rows), over its share of the columns. Few tokens -> few units ->
+// narrow row groups and more column splits, so every SM has work.
+template <bool GATEUP>
+__global__ void __launch_bounds__(256, 2) expert_mma_kernel(MoeParams p, uint32_t rg_count) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint4* tab = reinterpret_cast<uint4*>(smem);
+    uint4* xs = reinterpret_cast<uint4*>(smem + kMmaTabBytes);
+    const uint32_t K = GATEUP ? p.H : p.I;
+    float* red = reinterpret_cast<float*>(smem + kMmaTabBytes + (size_t)8u * K * 2u);
+    mma::build_iq2_table(tab, p.grids.iq2xxs);
+    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) xs[i] = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t staged_count = 0;  // tokens whose pieces the staging buffer holds (the rest are zero)
+    const uint32_t n_units = p.counters[0];
+    const uint32_t ks_count = 8u / rg_count;
+    const uint32_t warp_rows = GATEUP ? 16u : 32u;
+    const uint32_t rows_per_item = warp_rows * rg_count;
+    const uint32_t tiles = (GATEUP ? p.I : p.H) / rows_per_item;
+    const uint64_t n_items = (uint64_t)n_units * tiles;
+    uint32_t chunk = (uint32_t)((n_items + 4ull * gridDim.x - 1) / (4ull * gridDim.x));
+    chunk = chunk < 1u ? 1u : (chunk > kMmaChunk ? kMmaChunk : chunk);
+    uint32_t* next_item = p.counters + (GATEUP ? 2 : 4);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rg = warp % rg_count, ks = warp / rg_count, g = lane >> 2, q = lane & 3u;
+    const uint32_t k_chunks = K / 8u;
+    const uint32_t kslice = K / ks_count;
+    const uint32_t mat_base = GATEUP ? 0u : 2u * (p.E + 1);
+    uint32_t staged = 0xffffffffu;
+    __shared__ float scale_s[kUnitTokens];
+    __shared__ uint32_t chunk_s;
+    __syncthreads();
+    // Work stealing in chunks of consecutive items (one unit's neighbouring row tiles, so the
+    // staged activations are reused within a chunk).
+    for (;;) {
+    if (threadIdx.x == 0) chunk_s = atomicAdd(next_item, chunk);
+    __syncthreads();
+    const uint64_t c0 = chunk_s;
+    __syncthreads();
+    if (c0 >= n_items) break;
+    const uint64_t c1 = c0 + chunk < n_items ? c0 + chunk : n_items;
+    for (uint64_t item = c0; item < c1; ++item) {
+        const uint32_t ui = (uint32_t)(item / tiles), tile = (uint32_t)(item % tiles);
+        const Unit u = p.units[ui];
+        const DevMat* ma = p.mats + mat_base + u.expert;
+        if (!mma_type(ma->type)) continue;
+        if (ui != staged) {
+            __syncthreads();
+            const float* rows[kUnitTokens];
+#pragma unroll
+            for (int t = 0; t < kUnitTokens; ++t) {
+                const uint32_t pair = u.pair_begin + t;
+                rows[t] = nullptr;
+                if ((uint32_t)t < u.count)
+                    rows[t] = GATEUP ? p.x + (size_t)p.pair_token[pair] * p.H : p.act + (size_t)pair * p.I;
+            }
+            if (threadIdx.x < kUnitTokens) {
+                const uint32_t t = threadIdx.x;
+                float sc = 1.f;
+                if (t < u.count)
+                    sc = GATEUP ? p.xscale[p.pair_token[u.pair_begin + t]]
+                                : mma::prescale_for(__uint_as_float(p.act_max[u.pair_begin + t]));
+                scale_s[t] = sc;
+            }
+            __syncthreads();
+            float sc[kUnitTokens];
+#pragma unroll
+            for (int t = 0; t < kUnitTokens; ++t) sc[t] = scale_s[t];
+            const uint32_t n_stage = u.count > staged_count ? u.count : staged_count;
+            mma::stage_pieces(xs, rows, sc, K, n_stage);
+            __syncthreads();
+            staged = ui;
+            staged_count = u.count;
+        }
+        // this warp's two 16-row tiles
+        const DevMat* mats[mma::kTiles];
+        uint32_t rlo[mma::kTiles], rhi[mma::kTiles];
+        const uint32_t out0 = tile * rows_per_item + rg * warp_rows;
+#pragma unroll
+        for (int i = 0; i < mma::kTiles; ++i) {
+            uint32_t base;
+            if (GATEUP) {
+                mats[i] = i == 0 ? ma : p.mats + (p.E + 1) + u.expert;
+                base = out0;
+            } else {
+                mats[i] = ma;
+                base = out0 + 16u * i;
+            }
+            rlo[i] = base + g;
+            rhi[i] = base + g + 8u;
+        }
+        float acc[mma::kTiles][4];
+#pragma unroll
+        for (int i = 0; i < mma::kTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        const uint32_t k0 = ks * kslice, k1 = k0 + kslice;
+        const bool iq2 = ma->type == kTypeIq2Xxs;
+        mma::TileRows tr;
+        mma::tile_rows(mats, rlo, rhi, iq2 ? 64u : 32u, tr);
+        if (iq2) mma::iq2_rows(tr, k0, k1, xs, k_chunks, tab, acc);
+        else mma::q8_rows(tr, k0, k1, xs, k_chunks, acc);
+        // sum the column splits: split ks > 0 parks its partial sums, split 0 adds them
+        if (ks > 0) {
+            float* mine = red + (((size_t)(ks - 1u) * rg_count + rg) * 32u + lane) * 8u;
+#pragma unroll
+            for (int i = 0; i < mma::kTiles; ++i)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) mine[i * 4 + c] = acc[i][c];
+        }
+        __syncthreads();
+        if (ks == 0 && q < u.count) {
+            for (uint32_t j = 1; j < ks_count; ++j) {
+                const float* other = red + (((size_t)(j - 1u) * rg_count + rg) * 32u + lane) * 8u;
+#pragma unroll
+                for (int i = 0; i < mma::kTiles; ++i)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[i][c] += other[i * 4 + c];
+            }
+            const uint32_t pair = u.pair_begin + q;
+            const float inv = 1.f / scale_s[q];  // exact: a power of two
+            if (GATEUP) {
+                const bool shared = u.expert == p.E;
+                const float limit = shared ? p.shared_limit : p.routed_limit;
+#pragma unroll
+                for (int hi = 0; hi < 2; ++hi) {  // fragment row g / g+8
+                    const float gv = (acc[0][2 * hi] + acc[0][2 * hi + 1]) * inv;
+                    const float uv = (acc[1][2 * hi] + acc[1][2 * hi + 1]) * inv;
+                    const uint32_t row = out0 + g + 8u * hi;
+                    float a;
+                    if (p.weight_after_down) {
+                        a = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                    } else {
+                        double gd = (double)gv, ud = (double)uv;
+                        if (limit > 0.f) {
+                            gd = fmin(gd, (double)limit);
+                            ud = fmin(fmax(ud, -(double)limit), (double)limit);
+                        }
+                        double v = gd / (1.0 + exp(-gd)) * ud;
+                        if (!shared) v *= (double)p.pair_weight[pair];
+                        a = (float)v;
+                    }
+                    p.act[(size_t)pair * p.I + row] = a;
+                    atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < mma::kTiles; ++i)
+#pragma unroll
+                    for (int hi = 0; hi < 2; ++hi) {
+                        const uint32_t row = out0 + 16u * i + g + 8u * hi;
+                        p.y[(size_t)pair * p.H + row] = (acc[i][2 * hi] + acc[i][2 * hi + 1]) * inv;
+                    }
+            }
+        }
+        __syncthreads();
+    }
+    }
+}
+
+// Row groups per CTA for a launch: the widest shape that still gives every CTA several items.
+static uint32_t pick_row_groups(uint32_t T, uint32_t k, uint32_t E, uint32_t rows, uint32_t warp_rows,
+                                uint32_t K, unsigned grid) {
+    // tuning override: VLB_ROW_GROUPS=1|2|4|8 forces the CTA shape
+    if (const char* env = getenv("VLB_ROW_GROUPS")) {
+        const uint32_t rg = (uint32_t)atoi(env);
+        if ((rg == 1 || rg == 2 || rg == 4 || rg == 8) && (K / (8u / rg)) % 256u == 0) return rg;
+    }
+    const uint32_t units = (T * k < E ? T * k : E) + (T + kUnitTokens - 1) / kUnitTokens;
+    for (uint32_t rg = 8; rg > 1; rg >>= 1) {
+        const uint64_t items = (uint64_t)units * (rows / (warp_rows * rg));
+        if ((K / (8u / rg)) % 256u == 0 && items >= 2ull * grid) return rg;
+    }
+    return 1;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -664,10 +923,16 @@ cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_
     return gemv_type<4>(m, g, x, ntok, xstride, y, ystride, s);
 }
 
-cudaError_t launch_router(const float* x, const float* w, uint32_t T, uint32_t H, uint32_t E,
+cudaError_t launch_router(const double* x, const float* w, uint32_t T, uint32_t H, uint32_t E,
                           int score, float* logits, float* scores, cudaStream_t s) {
-    dim3 grid((E + 7) / 8, (T + kRouterTok - 1) / kRouterTok);
-    router_kernel<<<grid, 256, 0, s>>>(x, w, T, H, E, score, logits, scores);
+    if (H % 4u) return cudaErrorInvalidValue;  // 16-byte rows
+    router_kernel<<<E, 256, 0, s>>>(x, w, T, H, E, score, logits, scores);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, float* scale, double* xd,
+                            cudaStream_t s) {
+    token_prescale_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, T, H, scale, xd);
     return cudaGetLastError();
 }
 
@@ -691,17 +956,20 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     cudaError_t e;
     if (ev) cudaEventRecord(ev[0], s);
     // routing: router projection (or supplied logits) -> scores -> top-k
+    token_prescale_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p.x, p.T, p.H, p.xscale,
+                                                         p.logits_in ? nullptr : p.xd);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (p.logits_in) {
         e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
     } else {
-        e = launch_router(p.x, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
+        e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
     }
     if (e != cudaSuccess) return e;
     e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
                      p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
     if (e != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[1], s);
-    const size_t dsmem = ((size_t)p.E * 2 + 1 + 32u * p.E) * sizeof(uint32_t);
+    const size_t dsmem = ((size_t)(p.E + 1) * 3 + 32u * p.E) * sizeof(uint32_t);
     e = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsmem);
     if (e != cudaSuccess) return e;
     dispatch_kernel<<<1, kDispatchThreads, dsmem, s>>>(p);
@@ -713,13 +981,27 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     const size_t gu_smem = kGridSmemBytes + (size_t)kUnitTokens * p.H * sizeof(float);
     e = cudaFuncSetAttribute(expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gu_smem);
     if (e != cudaSuccess) return e;
-    expert_kernel<true><<<grid, 256, gu_smem, s>>>(p);
+    if (p.has_legacy) expert_kernel<true><<<grid, 256, gu_smem, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t mg_smem = kMmaTabBytes + (size_t)8u * p.H * 2u + kMmaRedBytes;
+    e = cudaFuncSetAttribute(expert_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mg_smem);
+    if (e != cudaSuccess) return e;
+    if (p.has_mma)
+        expert_mma_kernel<true><<<grid, 256, mg_smem, s>>>(
+            p, pick_row_groups(p.T, p.k, p.E, p.I, 16u, p.H, grid));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[3], s);
     const size_t dn_smem = kGridSmemBytes + (size_t)kUnitTokens * p.I * sizeof(float);
     e = cudaFuncSetAttribute(expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem);
     if (e != cudaSuccess) return e;
-    expert_kernel<false><<<grid, 256, dn_smem, s>>>(p);
+    if (p.has_legacy) expert_kernel<false><<<grid, 256, dn_smem, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t md_smem = kMmaTabBytes + (size_t)8u * p.I * 2u + kMmaRedBytes;
+    e = cudaFuncSetAttribute(expert_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)md_smem);
+    if (e != cudaSuccess) return e;
+    if (p.has_mma)
+        expert_mma_kernel<false><<<grid, 256, md_smem, s>>>(
+            p, pick_row_groups(p.T, p.k, p.E, p.H, 32u, p.I, grid));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[4], s);
     dim3 cg((p.H / 4 + 255) / 256, p.T);
