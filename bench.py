@@ -256,7 +256,7 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(out.nbytes),
                 "timing": "host wall clock around the synchronous C-ABI call"},
         "clocks": clk,
-        "gpu_launches": 7 * args.steps,
+        "gpu_launches": (7 + (1 if ((spec.experts + 7) // 8) * ((T + 7) // 8) < 256 else 0)) * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget)

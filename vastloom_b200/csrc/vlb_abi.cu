@@ -168,6 +168,10 @@ struct vlb_layer {
     uint32_t* tok_dev = nullptr;
     float* logits_dev = nullptr;
     float* out_dev = nullptr;
+    // the forward captured as a CUDA graph for one input binding, replayed while it matches
+    cudaGraphExec_t gexec = nullptr;
+    const void* gkey[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    uint32_t gkey_T = 0;
     // optional phase timing (vlb_layer_set_profiling)
     bool profiling = false;
     cudaEvent_t ev[kMoePhases + 1] = {};
@@ -489,6 +493,7 @@ static uint32_t max_units_for(uint32_t T, uint32_t k, uint32_t E) {
 }
 
 static void free_layer(vlb_handle* h, vlb_layer* L) {
+    if (L->gexec) cudaGraphExecDestroy(L->gexec);
     for (auto& e : L->ev)
         if (e) cudaEventDestroy(e);
     void* ptrs[] = {L->router, L->bias, L->tid2eid, L->mats, L->ws,
@@ -573,9 +578,9 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     const size_t o_logits = carve(T * E * 4), o_scores = carve(T * E * 4), o_idx = carve(T * k * 4),
                  o_w = carve(T * k * 4), o_off = carve((E + 2) * 4), o_pt = carve(P * 4),
                  o_ps = carve(P * 4), o_pw = carve(P * 4), o_units = carve((size_t)mu * sizeof(Unit)),
-                 o_cnt = carve(32), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
+                 o_cnt = carve(32 + T * 4), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
                  o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
-                 o_xd = carve(T * H * 8);
+                 o_xd = carve(T * H * 8), o_rp = carve(8 * T * E * 8);
     TRY(h->galloc(off, "vlb-layer-workspace", &L->ws));
     TRY(h->galloc(T * H * 4, "vlb-layer-x", (void**)&L->x_dev));
     TRY(h->galloc(T * 4, "vlb-layer-tokens", (void**)&L->tok_dev));
@@ -618,9 +623,10 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.combine_pairs = reinterpret_cast<uint32_t*>(ws + o_cp);
     p.act = reinterpret_cast<float*>(ws + o_act);
     p.y = reinterpret_cast<float*>(ws + o_y);
-    p.xscale = reinterpret_cast<float*>(ws + o_xs);
+    p.xmax = reinterpret_cast<uint32_t*>(ws + o_cnt + 32);
     p.act_max = reinterpret_cast<uint32_t*>(ws + o_am);
     p.xd = reinterpret_cast<double*>(ws + o_xd);
+    p.router_partial = reinterpret_cast<double*>(ws + o_rp);
     p.max_units = mu;
     *out = L;
     return VLB_OK;
@@ -634,6 +640,11 @@ int vlb_layer_destroy(vlb_handle* h, vlb_layer* L) {
     return VLB_OK;
 }
 
+// One layer forward on stream s. Without profiling the whole launch sequence (a memset and seven
+// kernels) is captured once as a CUDA graph for this exact input binding and replayed afterwards:
+// at decode sizes the GPU work is short enough that per-kernel host submission would otherwise
+// leave the device idle between kernels. A stream that cannot be captured (the legacy default
+// stream) gets the same kernels launched directly.
 static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
                           const float* logits, uint32_t T, float* out, cudaStream_t s) {
     if (T == 0 || T > L->desc.max_tokens)
@@ -647,10 +658,44 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.logits_in = logits;
     p.out = out;
     p.grids = h->grids();
-    VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, 32, s));
-    VLB_CUDA(h, launch_moe(p, s, L->profiling ? L->ev : nullptr));
+    const size_t zero_bytes = 32 + (size_t)T * 4;  // counters and per-token max|x|
     L->last_T = T;
     L->last_logits_given = logits != nullptr;
+    if (L->profiling) {
+        VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, zero_bytes, s));
+        VLB_CUDA(h, launch_moe(p, s, L->ev));
+        return VLB_OK;
+    }
+    const void* key[5] = {x, tok, logits, out, s};
+    bool same = L->gexec && L->gkey_T == T;
+    for (int i = 0; same && i < 5; ++i) same = L->gkey[i] == key[i];
+    if (!same) {
+        if (L->gexec) {
+            cudaGraphExecDestroy(L->gexec);
+            L->gexec = nullptr;
+        }
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+        if (e == cudaSuccess) {
+            cudaError_t e1 = cudaMemsetAsync(p.counters, 0, zero_bytes, s);
+            cudaError_t e2 = e1 == cudaSuccess ? launch_moe(p, s) : e1;
+            e = cudaStreamEndCapture(s, &graph);
+            if (e2 != cudaSuccess) e = e2;
+        }
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&L->gexec, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (e != cudaSuccess) {
+            // not capturable here: launch directly
+            (void)cudaGetLastError();
+            L->gexec = nullptr;
+            VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, zero_bytes, s));
+            VLB_CUDA(h, launch_moe(p, s));
+            return VLB_OK;
+        }
+        for (int i = 0; i < 5; ++i) L->gkey[i] = key[i];
+        L->gkey_T = T;
+    }
+    VLB_CUDA(h, cudaGraphLaunch(L->gexec, s));
     return VLB_OK;
 }
 
@@ -774,16 +819,19 @@ int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint
     VLB_LOCK(h);
     if (!x || !w || !logits || T == 0 || H == 0 || E == 0 || H % 4)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid router argument");
-    float* scratch = nullptr;
-    const size_t sbytes = (size_t)T * E * 4 + (size_t)T * 4 + 255;
-    const size_t xbytes = (size_t)T * H * 8;
-    int st = h->galloc(sbytes + xbytes, "vlb-router-scratch", (void**)&scratch);
+    // scratch: scores [T x E] f32 | xmax [T] | x in f64 [T x H] | partial sums [8 x T x E] f64
+    const size_t sbytes = ((size_t)T * E * 4 + (size_t)T * 4 + 255) / 256 * 256;
+    const size_t xbytes = (size_t)T * H * 8, pbytes = (size_t)8 * T * E * 8;
+    char* scratch = nullptr;
+    int st = h->galloc(sbytes + xbytes + pbytes, "vlb-router-scratch", (void**)&scratch);
     if (st != VLB_OK) return st;
-    double* xd = reinterpret_cast<double*>(reinterpret_cast<char*>(scratch) + sbytes / 256 * 256);
-    float* xscale = scratch + (size_t)T * E;
+    float* scores = reinterpret_cast<float*>(scratch);
+    uint32_t* xmax = reinterpret_cast<uint32_t*>(scratch + (size_t)T * E * 4);
+    double* xd = reinterpret_cast<double*>(scratch + sbytes);
+    double* part = reinterpret_cast<double*>(scratch + sbytes + xbytes);
     cudaStream_t s = h->pick(stream);
-    cudaError_t e = launch_prescale(x, T, H, xscale, xd, s);
-    if (e == cudaSuccess) e = launch_router(xd, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scratch, s);
+    cudaError_t e = launch_prescale(x, T, H, xmax, xd, s);
+    if (e == cudaSuccess) e = launch_router(xd, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scores, part, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     h->gfree(scratch);
     if (e != cudaSuccess) return h->cuda_fail("router", e);

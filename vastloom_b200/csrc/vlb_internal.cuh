@@ -191,8 +191,9 @@ struct MoeParams {
     float* act;              // [(T*k + T) x I]
     float* y;                // [(T*k + T) x H]
     float* out;              // [T x H]
-    float* xscale;           // [T]: power-of-two prescale of each token's activation row
+    uint32_t* xmax;          // [T]: bits of max|x| per token (zeroed with the counters)
     double* xd;              // [T x H]: activations widened to f64 for the router projection
+    double* router_partial;  // [8 x T x E]: per-column-slice router partial sums
     uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
     uint32_t max_units;
 };

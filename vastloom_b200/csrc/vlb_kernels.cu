@@ -11,6 +11,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "vlb_gemv.cuh"
 #include "vlb_launch.h"
@@ -117,6 +120,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 // the per-expert score (sqrt_softplus / sigmoid; softmax is applied per token in route_kernel).
 // CTA: 8 warps = 8 experts, a chunk of up to 8 tokens, columns staged 1024 at a time.
 constexpr int kRouterTok = 8;
+constexpr uint32_t kRouterMaxSlices = 8;
 
 __device__ __forceinline__ float sqrt_softplus_dev(float v) {
     const double p = (double)v;
@@ -135,64 +139,98 @@ __device__ __forceinline__ float score_dev(int score, float logit) {
     return logit;
 }
 
-__global__ void __launch_bounds__(256) router_kernel(const double* __restrict__ xd,
-                                                     const float* __restrict__ w, uint32_t T,
+// Router projection on the FP64 tensor cores (mma.sync m8n8k4 f64): logits[t][e] =
+// f32(sum_k w[e][k] * x[t][k]) with f64 products and sums (f32 operands are exact in f64).
+// CTA tile = 8 experts x 8 tokens x one column slice (gridDim.z slices); the 8 warps split the
+// slice and their partial tiles are added in a fixed order through shared memory. With one slice
+// the tile is final; with several, each slice's partial tile goes to `partial` and
+// router_finish_kernel adds the slices in order. Router weights stay f32 (converted in
+// registers); activations arrive widened to f64 (token_prescale_kernel).
+__global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w,
+                                                     const double* __restrict__ xd, uint32_t T,
                                                      uint32_t H, uint32_t E, int score,
                                                      float* __restrict__ logits,
-                                                     float* __restrict__ scores) {
-    // One CTA per expert row; its 8 warps split the columns (H/8 each) and the partial sums are
-    // added in a fixed order through shared memory. The activations arrive widened to f64
-    // (token_prescale_kernel), so each router weight is converted once and reused for every token;
-    // the products are exact in f64. Tokens go kRouterTok at a time.
-    __shared__ double part[8][kRouterTok];
+                                                     float* __restrict__ scores,
+                                                     double* __restrict__ partial) {
+    __shared__ double part[8][32][2];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t e = blockIdx.x;
-    // columns of this warp: a multiple of 4 (H is), possibly empty for tiny H
-    const uint32_t span = ((H / 4u + 7u) / 8u) * 4u;
-    const uint32_t c0 = min(warp * span, H), c1 = min(c0 + span, H);
-    const float* wr = w + (size_t)e * H;
-    for (uint32_t t0 = 0; t0 < T; t0 += kRouterTok) {
-        const uint32_t nt = min((uint32_t)kRouterTok, T - t0);
-        double acc[kRouterTok];
+    const uint32_t g = lane >> 2, q = lane & 3u;
+    const uint32_t e0 = blockIdx.x * 8u, t0 = blockIdx.y * 8u;
+    const uint32_t slices = gridDim.z;
+    const uint32_t slice = ((H / 4u + slices - 1u) / slices) * 4u;
+    const uint32_t s0 = min(blockIdx.z * slice, H), s1 = min(s0 + slice, H);
+    const uint32_t span = (((s1 - s0) / 4u + 7u) / 8u) * 4u;
+    const uint32_t k0 = min(s0 + warp * span, s1), k1 = min(k0 + span, s1);
+    const float* wr = e0 + g < E ? w + (size_t)(e0 + g) * H : nullptr;
+    const double* xr = t0 + g < T ? xd + (size_t)(t0 + g) * H : nullptr;
+    // 8 independent accumulator chains (k-steps round-robin), summed in a fixed order after
+    constexpr int kChains = 8;
+    double c0[kChains], c1[kChains];
 #pragma unroll
-        for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0;
-        for (uint32_t c = c0 + lane * 4u; c < c1; c += 128u) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + c));
-            const double w0 = wv.x, w1 = wv.y, w2 = wv.z, w3 = wv.w;
+    for (int j = 0; j < kChains; ++j) c0[j] = c1[j] = 0.0;
+    uint32_t k = k0 + q;
+    for (; k + 4u * (kChains - 1) < k1; k += 4u * kChains) {
+        double a[kChains], b[kChains];
 #pragma unroll
-            for (int t = 0; t < kRouterTok; ++t) {
-                if ((uint32_t)t >= nt) break;
-                const double* xr = xd + (size_t)(t0 + t) * H + c;
-                const double2 a = __ldg(reinterpret_cast<const double2*>(xr));
-                const double2 b = __ldg(reinterpret_cast<const double2*>(xr + 2));
-                acc[t] = fma(w0, a.x, acc[t]);
-                acc[t] = fma(w1, a.y, acc[t]);
-                acc[t] = fma(w2, b.x, acc[t]);
-                acc[t] = fma(w3, b.y, acc[t]);
+        for (int j = 0; j < kChains; ++j) {
+            a[j] = wr ? (double)__ldg(wr + k + 4u * j) : 0.0;
+            b[j] = xr ? __ldg(xr + k + 4u * j) : 0.0;
+        }
+#pragma unroll
+        for (int j = 0; j < kChains; ++j)
+            asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                : "+d"(c0[j]), "+d"(c1[j])
+                : "d"(a[j]), "d"(b[j]));
+    }
+    for (; k < k1; k += 4u) {  // tail (slice not a multiple of 32 columns)
+        const double a = wr ? (double)__ldg(wr + k) : 0.0;
+        const double b = xr ? __ldg(xr + k) : 0.0;
+        asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+            : "+d"(c0[0]), "+d"(c1[0])
+            : "d"(a), "d"(b));
+    }
+    for (int j = 1; j < kChains; ++j) {
+        c0[0] += c0[j];
+        c1[0] += c1[j];
+    }
+    // lane holds C[g][2q], C[g][2q+1] = (expert e0 + g, tokens t0 + 2q and t0 + 2q + 1)
+    part[warp][lane][0] = c0[0];
+    part[warp][lane][1] = c1[0];
+    __syncthreads();
+    if (threadIdx.x < 64u) {
+        const uint32_t i = threadIdx.x, eg = i >> 3, tn = i & 7u;
+        const uint32_t src = eg * 4u + (tn >> 1), half = tn & 1u;
+        double v = 0.0;
+#pragma unroll
+        for (int w8 = 0; w8 < 8; ++w8) v += part[w8][src][half];
+        const uint32_t e = e0 + eg, t = t0 + tn;
+        if (e < E && t < T) {
+            if (slices == 1) {
+                const float lg = (float)v;
+                logits[(size_t)t * E + e] = lg;
+                scores[(size_t)t * E + e] = score_dev(score, lg);
+            } else {
+                partial[((size_t)blockIdx.z * T + t) * E + e] = v;
             }
         }
-#pragma unroll
-        for (int t = 0; t < kRouterTok; ++t) {
-            double v = acc[t];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            acc[t] = v;
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int t = 0; t < kRouterTok; ++t) part[warp][t] = acc[t];
-        }
-        __syncthreads();
-        if (threadIdx.x < nt) {
-            const uint32_t t = threadIdx.x;
-            double v = 0.0;
-            for (int w8 = 0; w8 < 8; ++w8) v += part[w8][t];
-            const float lg = (float)v;
-            logits[(size_t)(t0 + t) * E + e] = lg;
-            scores[(size_t)(t0 + t) * E + e] = score_dev(score, lg);
-        }
-        __syncthreads();
     }
+}
+
+__global__ void router_finish_kernel(const double* __restrict__ partial, uint32_t slices,
+                                     uint32_t T, uint32_t E, int score, float* __restrict__ logits,
+                                     float* __restrict__ scores) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)T * E) return;
+    double v = 0.0;
+    for (uint32_t z = 0; z < slices; ++z) v += partial[(size_t)z * T * E + i];
+    const float lg = (float)v;
+    logits[i] = lg;
+    scores[i] = score_dev(score, lg);
+}
+
+__global__ void widen_kernel(const float* __restrict__ src, size_t n, double* __restrict__ dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = (double)src[i];
 }
 
 __global__ void score_kernel(const float* __restrict__ logits, size_t n, int score,
@@ -618,17 +656,18 @@ constexpr uint32_t kMmaTabBytes = 256u * 8u * 16u;      // fp16 IQ2_XXS table, 8
 constexpr uint32_t kMmaRedBytes = 7u * 32u * 8u * 4u;   // partial sums of the column splits
 constexpr uint32_t kMmaChunk = 4;                        // max items per work-stealing grab
 
-__global__ void token_prescale_kernel(const float* __restrict__ x, uint32_t T, uint32_t H,
-                                      float* __restrict__ scale, double* __restrict__ xd) {
-    // per token: the power-of-two prescale of the tensor-core activation pieces, and the row
-    // widened to f64 for the router projection
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t t = blockIdx.x * 8u + warp;
-    if (t >= T) return;
+__global__ void __launch_bounds__(256) token_prescale_kernel(const float* __restrict__ x, uint32_t T,
+                                                             uint32_t H, uint32_t* __restrict__ xmax,
+                                                             double* __restrict__ xd) {
+    // grid (ceil(H / 1024), T): each thread takes 4 columns of one token; the token's max|x|
+    // (for the tensor-core activation prescale) is an atomic max over float bits (non-negative
+    // floats order as integers), and the row is widened to f64 for the router projection
+    const uint32_t t = blockIdx.y;
+    const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     float m = 0.f;
-    for (uint32_t c = lane * 4u; c < H; c += 128u) {
+    if (c < H) {
         const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         if (xd) {
             double* o = xd + (size_t)t * H + c;
             *reinterpret_cast<double2*>(o) = make_double2(v.x, v.y);
@@ -637,7 +676,7 @@ __global__ void token_prescale_kernel(const float* __restrict__ x, uint32_t T, u
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) scale[t] = mma::prescale_for(m);
+    if ((threadIdx.x & 31u) == 0 && m > 0.f) atomicMax(xmax + t, __float_as_uint(m));
 }
 
 // CTA shape: rg_count row groups x (8 / rg_count) column splits. A warp owns one 16-row tile of
@@ -700,8 +739,8 @@ __global__ void __launch_bounds__(256, 2) expert_mma_kernel(MoeParams p, uint32_
                 const uint32_t t = threadIdx.x;
                 float sc = 1.f;
                 if (t < u.count)
-                    sc = GATEUP ? p.xscale[p.pair_token[u.pair_begin + t]]
-                                : mma::prescale_for(__uint_as_float(p.act_max[u.pair_begin + t]));
+                    sc = mma::prescale_for(__uint_as_float(
+                        GATEUP ? p.xmax[p.pair_token[u.pair_begin + t]] : p.act_max[u.pair_begin + t]));
                 scale_s[t] = sc;
             }
             __syncthreads();
@@ -874,6 +913,20 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
 
 // =============================================================================================
 // launchers
+
+// Raises a kernel's dynamic shared-memory limit once per process and size (a host call that must
+// not sit on the per-forward path, and that graph capture would not record anyway).
+template <typename K>
+static cudaError_t set_smem_once(K kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, size_t>> done;
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& d : done)
+        if (d.first == (const void*)kernel && d.second >= bytes) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done.emplace_back((const void*)kernel, bytes);
+    return e;
+}
 static int g_num_sms = 0;
 static int num_sms() {
     if (g_num_sms == 0) {
@@ -896,7 +949,7 @@ static cudaError_t gemv_launch(const DevMat& m, const Grids& g, const float* x, 
                                uint32_t xs, float* y, uint32_t ys, cudaStream_t s) {
     const size_t smem = kGridSmemBytes + (size_t)TOKC * m.cols * sizeof(float);
     auto kern = gemv_kernel<FMT, TOKC>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = set_smem_once(kern, smem);
     if (e != cudaSuccess) return e;
     const unsigned grid = (m.rows + kGemvRows * kGemvWarps - 1) / (kGemvRows * kGemvWarps);
     kern<<<grid, 256, smem, s>>>(m, g, x, ntok, xs, y, ys);
@@ -923,16 +976,38 @@ cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_
     return gemv_type<4>(m, g, x, ntok, xstride, y, ystride, s);
 }
 
-cudaError_t launch_router(const double* x, const float* w, uint32_t T, uint32_t H, uint32_t E,
-                          int score, float* logits, float* scores, cudaStream_t s) {
-    if (H % 4u) return cudaErrorInvalidValue;  // 16-byte rows
-    router_kernel<<<E, 256, 0, s>>>(x, w, T, H, E, score, logits, scores);
+// Column slices: enough CTAs to cover the SMs when the expert x token tiles alone do not.
+static uint32_t router_slices(uint32_t T, uint32_t E, uint32_t H) {
+    const uint32_t tiles = ((E + 7) / 8) * ((T + 7) / 8);
+    uint32_t z = 1;
+    while (z < kRouterMaxSlices && tiles * z < 256u && H / (z * 2u) >= 256u) z *= 2u;
+    return z;
+}
+
+cudaError_t launch_router(const double* xd, const float* w, uint32_t T, uint32_t H, uint32_t E,
+                          int score, float* logits, float* scores, double* partial,
+                          cudaStream_t s) {
+    if (H % 4u) return cudaErrorInvalidValue;
+    const uint32_t z = partial ? router_slices(T, E, H) : 1u;
+    dim3 grid((E + 7) / 8, (T + 7) / 8, z);
+    router_kernel<<<grid, 256, 0, s>>>(w, xd, T, H, E, score, logits, scores, partial);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || z == 1) return e;
+    const size_t n = (size_t)T * E;
+    router_finish_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(partial, z, T, E, score, logits, scores);
     return cudaGetLastError();
 }
 
-cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, float* scale, double* xd,
+cudaError_t launch_widen(const float* src, size_t n, double* dst, cudaStream_t s) {
+    widen_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, n, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, double* xd,
                             cudaStream_t s) {
-    token_prescale_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, T, H, scale, xd);
+    cudaError_t e = cudaMemsetAsync(xmax, 0, (size_t)T * 4u, s);
+    if (e != cudaSuccess) return e;
+    token_prescale_kernel<<<dim3((H + 1023) / 1024, T), 256, 0, s>>>(x, T, H, xmax, xd);
     return cudaGetLastError();
 }
 
@@ -956,13 +1031,13 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     cudaError_t e;
     if (ev) cudaEventRecord(ev[0], s);
     // routing: router projection (or supplied logits) -> scores -> top-k
-    token_prescale_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p.x, p.T, p.H, p.xscale,
-                                                         p.logits_in ? nullptr : p.xd);
+    token_prescale_kernel<<<dim3((p.H + 1023) / 1024, p.T), 256, 0, s>>>(
+        p.x, p.T, p.H, p.xmax, p.logits_in ? nullptr : p.xd);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (p.logits_in) {
         e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
     } else {
-        e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
+        e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, p.router_partial, s);
     }
     if (e != cudaSuccess) return e;
     e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
@@ -970,8 +1045,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     if (e != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[1], s);
     const size_t dsmem = ((size_t)(p.E + 1) * 3 + 32u * p.E) * sizeof(uint32_t);
-    e = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsmem);
-    if (e != cudaSuccess) return e;
+    if ((e = set_smem_once(dispatch_kernel, dsmem)) != cudaSuccess) return e;
     dispatch_kernel<<<1, kDispatchThreads, dsmem, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[2], s);
@@ -979,26 +1053,22 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     const int ctas_per_sm = 2;
     const unsigned grid = (unsigned)(num_sms() * ctas_per_sm);
     const size_t gu_smem = kGridSmemBytes + (size_t)kUnitTokens * p.H * sizeof(float);
-    e = cudaFuncSetAttribute(expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gu_smem);
-    if (e != cudaSuccess) return e;
+    if (p.has_legacy && (e = set_smem_once(expert_kernel<true>, gu_smem)) != cudaSuccess) return e;
     if (p.has_legacy) expert_kernel<true><<<grid, 256, gu_smem, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t mg_smem = kMmaTabBytes + (size_t)8u * p.H * 2u + kMmaRedBytes;
-    e = cudaFuncSetAttribute(expert_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mg_smem);
-    if (e != cudaSuccess) return e;
+    if (p.has_mma && (e = set_smem_once(expert_mma_kernel<true>, mg_smem)) != cudaSuccess) return e;
     if (p.has_mma)
         expert_mma_kernel<true><<<grid, 256, mg_smem, s>>>(
             p, pick_row_groups(p.T, p.k, p.E, p.I, 16u, p.H, grid));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[3], s);
     const size_t dn_smem = kGridSmemBytes + (size_t)kUnitTokens * p.I * sizeof(float);
-    e = cudaFuncSetAttribute(expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem);
-    if (e != cudaSuccess) return e;
+    if (p.has_legacy && (e = set_smem_once(expert_kernel<false>, dn_smem)) != cudaSuccess) return e;
     if (p.has_legacy) expert_kernel<false><<<grid, 256, dn_smem, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t md_smem = kMmaTabBytes + (size_t)8u * p.I * 2u + kMmaRedBytes;
-    e = cudaFuncSetAttribute(expert_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)md_smem);
-    if (e != cudaSuccess) return e;
+    if (p.has_mma && (e = set_smem_once(expert_mma_kernel<false>, md_smem)) != cudaSuccess) return e;
     if (p.has_mma)
         expert_mma_kernel<false><<<grid, 256, md_smem, s>>>(
             p, pick_row_groups(p.T, p.k, p.E, p.H, 32u, p.I, grid));

@@ -10,9 +10,12 @@ namespace vlb {
 cudaError_t launch_dequant(const DevMat& m, const Grids& g, float* out, cudaStream_t s);
 cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_t ntok,
                         uint32_t xstride, float* y, uint32_t ystride, cudaStream_t s);
-cudaError_t launch_router(const double* x, const float* w, uint32_t T, uint32_t H, uint32_t E,
-                          int score, float* logits, float* scores, cudaStream_t s);
-cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, float* scale, double* xd,
+// partial: [8 x T x E] f64 scratch for column slices (null: a single slice)
+cudaError_t launch_router(const double* xd, const float* w, uint32_t T, uint32_t H, uint32_t E,
+                          int score, float* logits, float* scores, double* partial,
+                          cudaStream_t s);
+cudaError_t launch_widen(const float* src, size_t n, double* dst, cudaStream_t s);
+cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, double* xd,
                             cudaStream_t s);
 cudaError_t launch_scores(const float* logits, size_t n, int score, float* scores,
                           cudaStream_t s);
