@@ -188,6 +188,18 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* layer, const float* x_host,
                       const uint32_t* token_ids_host, const float* logits_host, uint32_t T,
                       float* out_host);
 
+/* Prefill mode. A forward of T >= min_tokens runs the expert products as grouped GEMMs on the
+ * tensor cores (tcgen05, fp16 operands with per-matrix / per-token / per-pair power-of-two scales,
+ * f32 accumulation): layer outputs then match the reference within 2e-2 relative (about 1e-3 in
+ * practice) instead of the decode path's 1e-5. Routing, dispatch and the combine order are the
+ * same on both paths; IQ3_XXS / IQ1_S experts stay on the CUDA-core kernels. min_tokens = 0
+ * restores the default (16 pairs per routed expert on average, at least 256 tokens);
+ * 0xFFFFFFFF keeps every forward on the decode path. vlb_layer_prefill_tokens returns the
+ * threshold in force (0 for a null argument). The prefill pipeline's waits are time-bounded: a
+ * wait that runs out makes vlb_layer_forward return VLB_ERR_INTERNAL_ERROR. */
+int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* layer, uint32_t min_tokens);
+uint32_t vlb_layer_prefill_tokens(vlb_handle* h, vlb_layer* layer);
+
 /* Route of the last forward on this layer, for parity checks: idx / weights [T x k] in rank
  * order; offsets [E + 1]; pair_token / pair_slot [T x k] = the dispatch permutation (pairs
  * sorted by expert ascending, then token, then slot - the reference's visit order,

@@ -135,7 +135,8 @@ EXPORTS = (
     "vlb_memcpy_h2d vlb_memcpy_d2h vlb_allocated_bytes vlb_upload_matrix vlb_release_matrix "
     "vlb_matrix_bytes vlb_matvec vlb_matvec_device vlb_dequantize_device vlb_layer_create "
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
-    "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
+    "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_layer_set_prefill_tokens "
+    "vlb_layer_prefill_tokens vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
 ).split()
 
 
@@ -180,6 +181,8 @@ def load_library() -> C.CDLL:
         "vlb_layer_last_weight_bytes": (U64, [P, P]),
         "vlb_layer_set_profiling": (I, [P, P, I]),
         "vlb_layer_phase_times": (I, [P, P, C.POINTER(C.c_float), I]),
+        "vlb_layer_set_prefill_tokens": (I, [P, P, U32]),
+        "vlb_layer_prefill_tokens": (U32, [P, P]),
         "vlb_route_device": (I, [P, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
         "vlb_route_device_noalloc": (I, [I, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
         "vlb_router_logits_device": (I, [P, P, P, U32, U32, U32, P, P]),
@@ -522,6 +525,16 @@ class MoeLayer:
 
     def last_weight_bytes(self) -> int:
         return int(self.dev.lib.vlb_layer_last_weight_bytes(self.dev.h, self.ptr))
+
+    PREFILL_NEVER = 0xFFFFFFFF
+
+    def set_prefill_tokens(self, min_tokens: int) -> None:
+        """Forwards of at least `min_tokens` tokens run the expert products on the tensor-core
+        prefill kernels (2e-2 contract); 0 = the default threshold, PREFILL_NEVER = never."""
+        self.dev._check(self.dev.lib.vlb_layer_set_prefill_tokens(self.dev.h, self.ptr, min_tokens))
+
+    def prefill_tokens(self) -> int:
+        return int(self.dev.lib.vlb_layer_prefill_tokens(self.dev.h, self.ptr))
 
     def destroy(self) -> None:
         if self.ptr:

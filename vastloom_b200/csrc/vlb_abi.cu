@@ -163,6 +163,8 @@ struct vlb_layer {
     MoeParams p{};
     uint32_t last_T = 0;
     bool last_logits_given = false;
+    // forwards of at least this many tokens run the expert products on the prefill kernels
+    uint32_t prefill_min_tokens = 0;
     // staging for the host-memory forward
     float* x_dev = nullptr;
     uint32_t* tok_dev = nullptr;
@@ -364,6 +366,56 @@ uint64_t vlb_allocated_bytes(const vlb_handle* h) { return h ? h->allocated : 0;
 
 static bool half_is_finite(uint16_t bits) { return ((bits >> 10) & 0x1fu) != 0x1fu; }
 
+static float half_bits_to_float(uint16_t bits) {
+    const uint32_t e = (bits >> 10) & 0x1fu, m = bits & 0x3ffu;
+    const float mag = e == 0 ? std::ldexp((float)m, -24) : std::ldexp((float)(m | 0x400u), (int)e - 25);
+    return (bits & 0x8000u) ? -mag : mag;
+}
+
+// TMA descriptor of a row-major fp16 matrix [rows x cols] read as 64-column x 16-row boxes with the
+// 128-byte swizzle of the UMMA K-major operand layout (cuTensorMapEncodeTiled, resolved through
+// the runtime so the library does not link the driver API).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+static bool encode_rows_fp16(CUtensorMap* map, void* base, size_t rows, size_t cols) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, prefill_box_rows()};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The power of two the prefill kernels scale a matrix's weights by before rounding them to fp16:
+// the largest possible |weight| (largest block scale x the format's largest factor: 128 for a
+// Q8_0 quant, 15.5 / 4 x 43 for an IQ2_XXS grid value) lands in [2^13, 2^14).
+static float prefill_scale(uint32_t type, float dmax) {
+    const float factor = type == VLB_TYPE_Q8_0 ? 128.f : type == VLB_TYPE_IQ2_XXS ? 167.f : 0.f;
+    const float bound = dmax * factor;
+    if (!(bound > 0.f)) return 1.f;
+    int e = 0;
+    std::frexp(bound, &e);  // bound = f * 2^e, f in [0.5, 1)
+    return std::ldexp(1.f, 14 - e);
+}
+
 int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t rows,
                       size_t cols, const void* payload, size_t payload_bytes, vlb_matrix** out) {
     VLB_LOCK(h);
@@ -384,13 +436,18 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
         return h->fail(VLB_ERR_INVALID_FORMAT, "matrix payload size does not match its shape");
     const uint8_t* src = static_cast<const uint8_t*>(payload);
     // validate_block_scales (ggml_quantization.cpp:205-215): every block scale finite
+    uint16_t dmax_bits = 0;  // largest |d| (fp16 magnitudes order as integers)
     for (size_t b = 0; b < nblocks; ++b) {
         const uint16_t d = (uint16_t)(src[b * L.block_bytes] | (src[b * L.block_bytes + 1] << 8));
         if (!half_is_finite(d))
             return h->fail(VLB_ERR_INVALID_FORMAT, "quantized block scale is not finite");
+        if ((d & 0x7fffu) > dmax_bits) dmax_bits = (uint16_t)(d & 0x7fffu);
     }
-    const size_t d_bytes = (nblocks * 2 + 255) / 256 * 256;
-    const size_t body_bytes = nblocks * L.body_bytes;
+    // tiled device layout (blk_index): rows padded to whole 128-row tiles with zero blocks
+    const size_t rows_padded = (rows + kTileRows - 1) / kTileRows * kTileRows;
+    const size_t nslots = rows_padded * bpr;
+    const size_t d_bytes = (nslots * 2 + 255) / 256 * 256;
+    const size_t body_bytes = nslots * L.body_bytes;
     std::vector<uint8_t> staged;
     try {
         staged.assign(d_bytes + body_bytes, 0);
@@ -400,11 +457,13 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     uint16_t* dst_d = reinterpret_cast<uint16_t*>(staged.data());
     uint8_t* dst_b = staged.data() + d_bytes;
     const size_t copy = L.block_bytes - 2;
-    for (size_t b = 0; b < nblocks; ++b) {
-        const uint8_t* blk = src + b * L.block_bytes;
-        dst_d[b] = (uint16_t)(blk[0] | (blk[1] << 8));
-        std::memcpy(dst_b + b * L.body_bytes, blk + 2, copy);
-    }
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < bpr; ++c) {
+            const uint8_t* blk = src + (r * bpr + c) * L.block_bytes;
+            const size_t at = blk_index((uint32_t)bpr, (uint32_t)r, (uint32_t)c);
+            dst_d[at] = (uint16_t)(blk[0] | (blk[1] << 8));
+            std::memcpy(dst_b + at * L.body_bytes, blk + 2, copy);
+        }
     vlb_matrix* m = new (std::nothrow) vlb_matrix();
     if (!m) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
     int st = h->galloc(staged.size(), "vlb-resident-matrix", &m->mem);
@@ -424,11 +483,12 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     m->rows = rows;
     m->cols = cols;
     m->bpr = (uint32_t)bpr;
-    m->bytes = nblocks * 2 + body_bytes;
+    m->bytes = nslots * 2 + body_bytes;
     m->payload_bytes = payload_bytes;
     m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr,
                    reinterpret_cast<const uint16_t*>(m->mem),
-                   reinterpret_cast<const uint8_t*>(m->mem) + d_bytes};
+                   reinterpret_cast<const uint8_t*>(m->mem) + d_bytes,
+                   prefill_scale(type, half_bits_to_float(dmax_bits))};
     *out = m;
     return VLB_OK;
 }
@@ -581,6 +641,8 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
                  o_cnt = carve(32 + T * 4), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
                  o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
                  o_xd = carve(T * H * 8), o_rp = carve(8 * T * E * 8);
+    const uint32_t mpt = prefill_max_tiles((uint32_t)T, k, E);
+    const size_t o_xh = carve(P * H * 2), o_acth = carve(P * I * 2), o_pt2 = carve((size_t)mpt * sizeof(Unit));
     TRY(h->galloc(off, "vlb-layer-workspace", &L->ws));
     TRY(h->galloc(T * H * 4, "vlb-layer-x", (void**)&L->x_dev));
     TRY(h->galloc(T * 4, "vlb-layer-tokens", (void**)&L->tok_dev));
@@ -628,6 +690,15 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.xd = reinterpret_cast<double*>(ws + o_xd);
     p.router_partial = reinterpret_cast<double*>(ws + o_rp);
     p.max_units = mu;
+    p.prefill = 0;
+    p.xperm = reinterpret_cast<__half*>(ws + o_xh);
+    p.act_h = reinterpret_cast<__half*>(ws + o_acth);
+    p.ptiles = reinterpret_cast<Unit*>(ws + o_pt2);
+    p.max_ptiles = mpt;
+    if (!encode_rows_fp16(&p.bmap_x, p.xperm, P, H) || !encode_rows_fp16(&p.bmap_act, p.act_h, P, I)) {
+        free_layer(h, L);
+        return h->fail(VLB_ERR_INTERNAL_ERROR, "unable to encode the prefill TMA descriptors");
+    }
     *out = L;
     return VLB_OK;
 }
@@ -638,6 +709,14 @@ int vlb_layer_destroy(vlb_handle* h, vlb_layer* L) {
     VLB_CUDA(h, cudaStreamSynchronize(h->stream));
     free_layer(h, L);
     return VLB_OK;
+}
+
+// Default prefill threshold: 16 pairs per routed expert on average, and never below 256 tokens.
+static uint32_t prefill_threshold(const vlb_layer* L) {
+    if (L->prefill_min_tokens) return L->prefill_min_tokens;
+    const uint32_t E = L->desc.experts, k = L->desc.top_k;
+    const uint32_t per_expert = (16u * E + k - 1u) / k;
+    return per_expert > 256u ? per_expert : 256u;
 }
 
 // One layer forward on stream s. Without profiling the whole launch sequence (a memset and seven
@@ -658,6 +737,7 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.logits_in = logits;
     p.out = out;
     p.grids = h->grids();
+    p.prefill = T >= prefill_threshold(L) ? 1 : 0;
     const size_t zero_bytes = 32 + (size_t)T * 4;  // counters and per-token max|x|
     L->last_T = T;
     L->last_logits_given = logits != nullptr;
@@ -727,7 +807,27 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_
     if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
     if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "router selected an out-of-range expert");
     if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
+    if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "a prefill pipeline wait ran out of time");
+    if (flags & 16u) return h->fail(VLB_ERR_INTERNAL_ERROR, "prefill shared memory is not 1 KB aligned");
     return VLB_OK;
+}
+
+int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* L, uint32_t min_tokens) {
+    VLB_LOCK(h);
+    if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
+    if (L->prefill_min_tokens != min_tokens && L->gexec) {
+        VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+        cudaGraphExecDestroy(L->gexec);
+        L->gexec = nullptr;
+    }
+    L->prefill_min_tokens = min_tokens;
+    return VLB_OK;
+}
+
+uint32_t vlb_layer_prefill_tokens(vlb_handle* h, vlb_layer* L) {
+    if (!h || !L) return 0;
+    std::lock_guard<std::mutex> lock(h->mu);
+    return prefill_threshold(L);
 }
 
 int vlb_layer_last_route(vlb_handle* h, vlb_layer* L, uint32_t T, uint32_t* idx, float* w,

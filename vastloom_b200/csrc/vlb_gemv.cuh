@@ -39,19 +39,19 @@ __device__ __forceinline__ void load_group(const DevMat& m, uint32_t row, uint32
                                            GroupRaw& r) {
     if constexpr (FMT == kTypeQ8_0) {
         // one 32-weight block per group; the 32 quants are loaded per sub-block pair below
-        r.ls = h2f(__ldg(m.d + (size_t)row * m.bpr + g));
+        r.ls = h2f(__ldg(m.d + blk_index(m.bpr, row, g)));
     } else if constexpr (FMT == kTypeIq2Xxs) {
         const uint32_t blk = g >> 3, gg = g & 7u;
-        const float d = h2f(__ldg(m.d + (size_t)row * m.bpr + blk));
+        const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(
-            m.body + ((size_t)row * m.bpr + blk) * 64u + gg * 8u));
+            m.body + blk_index(m.bpr, row, blk) * 64u + gg * 8u));
         r.a = v.x;
         r.b = v.y;
         r.ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(v.y >> 28))), 0.25f);
     } else if constexpr (FMT == kTypeIq3Xxs) {
         const uint32_t blk = g >> 3, gg = g & 7u;
-        const float d = h2f(__ldg(m.d + (size_t)row * m.bpr + blk));
-        const uint8_t* body = m.body + ((size_t)row * m.bpr + blk) * 96u;
+        const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
+        const uint8_t* body = m.body + blk_index(m.bpr, row, blk) * 96u;
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(body + gg * 8u));
         const uint32_t aux = __ldg(reinterpret_cast<const uint32_t*>(body + 64u + gg * 4u));
         r.a = v.x;
@@ -60,8 +60,8 @@ __device__ __forceinline__ void load_group(const DevMat& m, uint32_t row, uint32
         r.ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
     } else {  // IQ1_S
         const uint32_t blk = g >> 3, gg = g & 7u;
-        const float d = h2f(__ldg(m.d + (size_t)row * m.bpr + blk));
-        const uint8_t* body = m.body + ((size_t)row * m.bpr + blk) * 48u;
+        const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
+        const uint8_t* body = m.body + blk_index(m.bpr, row, blk) * 48u;
         const uint32_t qs4 = __ldg(reinterpret_cast<const uint32_t*>(body + gg * 4u));
         const uint32_t h = __ldg(reinterpret_cast<const uint16_t*>(body + 32u + gg * 2u));
         r.a = qs4;
@@ -78,7 +78,7 @@ __device__ __forceinline__ void decode_sub(const DevMat& m, uint32_t row, uint32
                                            float* w) {
     if constexpr (FMT == kTypeQ8_0) {
         const uint2 q = __ldg(reinterpret_cast<const uint2*>(
-            m.body + ((size_t)row * m.bpr + g) * 32u + j * 8u));
+            m.body + blk_index(m.bpr, row, g) * 32u + j * 8u));
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
             const uint32_t word = l < 4 ? q.x : q.y;

@@ -2,16 +2,21 @@
 // bit-exact block decoders and the launch-side workspace structures.
 //
 // Device layout of a resident ggml matrix (chosen at upload, vlb_upload_matrix):
-//   d    : fp16 block scales, [rows x blocks_per_row] (the 2-byte header of every ggml block)
-//   body : the rest of each block, padded to a 16-byte multiple, [rows x blocks_per_row x body]
+//   d    : fp16 block scales (the 2-byte header of every ggml block)
+//   body : the rest of each block, padded to a 16-byte multiple
 //            Q8_0    : 32 int8 quants                                   (32 B)
 //            IQ2_XXS : 8 groups x (4 grid-index bytes, u32 signs/scale)  (64 B)
 //            IQ3_XXS : 64 grid-index bytes, then 8 x u32 signs/scale      (96 B)
 //            IQ1_S   : 32 low-index bytes, then 8 x u16 high bits/scale   (48 B)
-// The ggml block is 34/66/98/50 bytes, so splitting the scale off makes every body 16-byte
-// aligned (wide vector loads, TMA-friendly rows) without changing the bytes read per weight.
+// both in 128-row tiles: entry (row, block) sits at ((row / 128) * blocks_per_row + block) * 128
+// + row % 128, so one block column of a tile (128 rows x one block) is contiguous. The ggml block
+// is 34/66/98/50 bytes, so splitting the scale off makes every body 16-byte aligned without
+// changing the bytes read per weight; the tiling makes the prefill GEMM's per-stage weight tile
+// one contiguous run (bulk copies) and a decode warp's 8 consecutive rows of a block 512
+// contiguous bytes. Rows are padded to a multiple of 128 (zero blocks).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -41,6 +46,14 @@ __host__ __device__ inline bool type_layout(uint32_t type, TypeLayout* l) {
     }
 }
 
+constexpr uint32_t kTileRows = 128;
+
+// Index of block `blk` of row `row` in the tiled d / body arrays of a matrix with `bpr` blocks per
+// row; consecutive blocks of one row are kTileRows entries apart.
+__host__ __device__ __forceinline__ size_t blk_index(uint32_t bpr, uint32_t row, uint32_t blk) {
+    return ((size_t)(row / kTileRows) * bpr + blk) * kTileRows + (row % kTileRows);
+}
+
 // Kernel-side view of a resident matrix.
 struct DevMat {
     uint32_t type;
@@ -49,6 +62,10 @@ struct DevMat {
     uint32_t bpr;  // blocks per row
     const uint16_t* d;
     const uint8_t* body;
+    // Power of two applied to the weights when the prefill kernels decode them to fp16: chosen at
+    // upload from the largest block scale so that every |weight| * pscale stays below 2^14 (no
+    // overflow) while small weights stay clear of the fp16 subnormal range.
+    float pscale;
 };
 
 struct Grids {
@@ -186,7 +203,8 @@ struct MoeParams {
     uint32_t* pair_slot;     // [T*k + T]
     float* pair_weight;      // [T*k + T]
     Unit* units;             // [max_units]
-    uint32_t* counters;      // [8]: n_units, n_active, gate/up next item, error flags, down next item
+    uint32_t* counters;      // [8]: n_units, n_active, gate/up next item, error flags, down next item,
+                             //      prefill gate/up next item, prefill down next item, n_ptiles
     uint32_t* combine_pairs; // [T x k]: each token's pairs in (expert, slot) order
     float* act;              // [(T*k + T) x I]
     float* y;                // [(T*k + T) x H]
@@ -196,6 +214,16 @@ struct MoeParams {
     double* router_partial;  // [8 x T x E]: per-column-slice router partial sums
     uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
     uint32_t max_units;
+    // prefill (tensor-core grouped GEMM) path
+    int prefill;             // 1: this forward runs the expert products on tcgen05 (fp16 operands)
+    __half* xperm;           // [(T*k + T) x H]: pair p's token row, fp16(x * 2^e_t) (the token's xmax power of two)
+    __half* act_h;           // [(T*k + T) x I]: fp16(act * 2^e_p), the per-pair power of two of act_max
+    Unit* ptiles;            // [max_ptiles]: (expert, first pair, pairs <= 256) GEMM column tiles
+    uint32_t max_ptiles;
+    // TMA descriptors of xperm and act_h (rows = max_tokens * (k + 1), 64 x 16 boxes, 128-byte
+    // swizzle): the prefill GEMMs' B operands
+    CUtensorMap bmap_x;
+    CUtensorMap bmap_act;
 };
 
 }  // namespace vlb

@@ -45,17 +45,17 @@ __global__ void dequant_kernel(DevMat m, Grids g, float* __restrict__ out) {
     const uint32_t row = (uint32_t)(gid / ngroups), grp = (uint32_t)(gid % ngroups);
     float w[32];
     if (m.type == kTypeQ8_0) {
-        decode_group_q8_0(h2f(m.d[(size_t)row * m.bpr + grp]),
-                          m.body + ((size_t)row * m.bpr + grp) * 32u, w);
+        decode_group_q8_0(h2f(m.d[blk_index(m.bpr, row, grp)]),
+                          m.body + blk_index(m.bpr, row, grp) * 32u, w);
     } else {
         const uint32_t blk = grp >> 3, gg = grp & 7u;
-        const float d = h2f(m.d[(size_t)row * m.bpr + blk]);
+        const float d = h2f(m.d[blk_index(m.bpr, row, blk)]);
         if (m.type == kTypeIq2Xxs)
-            decode_group_iq2_xxs(d, m.body + ((size_t)row * m.bpr + blk) * 64u, gg, g.iq2xxs, w);
+            decode_group_iq2_xxs(d, m.body + blk_index(m.bpr, row, blk) * 64u, gg, g.iq2xxs, w);
         else if (m.type == kTypeIq3Xxs)
-            decode_group_iq3_xxs(d, m.body + ((size_t)row * m.bpr + blk) * 96u, gg, g.iq3xxs, w);
+            decode_group_iq3_xxs(d, m.body + blk_index(m.bpr, row, blk) * 96u, gg, g.iq3xxs, w);
         else
-            decode_group_iq1_s(d, m.body + ((size_t)row * m.bpr + blk) * 48u, gg, g.iq1s, w);
+            decode_group_iq1_s(d, m.body + blk_index(m.bpr, row, blk) * 48u, gg, g.iq1s, w);
     }
     float* o = out + (size_t)row * m.cols + (size_t)grp * 32u;
 #pragma unroll
@@ -1052,27 +1052,34 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     // experts
     const int ctas_per_sm = 2;
     const unsigned grid = (unsigned)(num_sms() * ctas_per_sm);
+    if (p.prefill && (e = launch_prefill_plan(p, s)) != cudaSuccess) return e;
     const size_t gu_smem = kGridSmemBytes + (size_t)kUnitTokens * p.H * sizeof(float);
     if (p.has_legacy && (e = set_smem_once(expert_kernel<true>, gu_smem)) != cudaSuccess) return e;
     if (p.has_legacy) expert_kernel<true><<<grid, 256, gu_smem, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t mg_smem = kMmaTabBytes + (size_t)8u * p.H * 2u + kMmaRedBytes;
-    if (p.has_mma && (e = set_smem_once(expert_mma_kernel<true>, mg_smem)) != cudaSuccess) return e;
-    if (p.has_mma)
+    if (p.has_mma && p.prefill) {
+        if ((e = launch_prefill_gateup(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
+    } else if (p.has_mma) {
+        const size_t mg_smem = kMmaTabBytes + (size_t)8u * p.H * 2u + kMmaRedBytes;
+        if ((e = set_smem_once(expert_mma_kernel<true>, mg_smem)) != cudaSuccess) return e;
         expert_mma_kernel<true><<<grid, 256, mg_smem, s>>>(
             p, pick_row_groups(p.T, p.k, p.E, p.I, 16u, p.H, grid));
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
     if (ev) cudaEventRecord(ev[3], s);
     const size_t dn_smem = kGridSmemBytes + (size_t)kUnitTokens * p.I * sizeof(float);
     if (p.has_legacy && (e = set_smem_once(expert_kernel<false>, dn_smem)) != cudaSuccess) return e;
     if (p.has_legacy) expert_kernel<false><<<grid, 256, dn_smem, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t md_smem = kMmaTabBytes + (size_t)8u * p.I * 2u + kMmaRedBytes;
-    if (p.has_mma && (e = set_smem_once(expert_mma_kernel<false>, md_smem)) != cudaSuccess) return e;
-    if (p.has_mma)
+    if (p.has_mma && p.prefill) {
+        if ((e = launch_prefill_down(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
+    } else if (p.has_mma) {
+        const size_t md_smem = kMmaTabBytes + (size_t)8u * p.I * 2u + kMmaRedBytes;
+        if ((e = set_smem_once(expert_mma_kernel<false>, md_smem)) != cudaSuccess) return e;
         expert_mma_kernel<false><<<grid, 256, md_smem, s>>>(
             p, pick_row_groups(p.T, p.k, p.E, p.H, 32u, p.I, grid));
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
     if (ev) cudaEventRecord(ev[4], s);
     dim3 cg((p.H / 4 + 255) / 256, p.T);
     combine_kernel<<<cg, 256, 0, s>>>(p);

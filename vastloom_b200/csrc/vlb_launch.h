@@ -23,11 +23,19 @@ cudaError_t launch_route(const float* scores, const float* bias, const uint32_t*
                          const uint32_t* tid2eid, uint32_t vocab, uint32_t T, uint32_t E,
                          uint32_t k, int score, int hash_routing, float route_scale,
                          uint32_t* idx, float* weights, uint32_t* error_flag, cudaStream_t s);
-// The whole decode layer: routing, dispatch, gate/up + SwiGLU, down, combine.
+// The whole layer: routing, dispatch, gate/up + SwiGLU, down, combine (the expert products on the
+// decode kernels, or on the prefill kernels when p.prefill is set).
 // ev: optional 6 events recorded at the phase boundaries (start, routed, dispatched, gate/up done,
 // down done, combined).
 constexpr int kMoePhases = 5;
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev = nullptr);
+// Prefill path (vlb_prefill.cu): column-tile plan after dispatch, then the tcgen05 grouped GEMMs
+// (each preceded by the fp16 conversion of its activations).
+uint32_t prefill_max_tiles(uint32_t T, uint32_t k, uint32_t E);
+uint32_t prefill_box_rows();  // rows of the B operand's TMA box
+cudaError_t launch_prefill_plan(const MoeParams& p, cudaStream_t s);
+cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_t s);
+cudaError_t launch_prefill_down(const MoeParams& p, unsigned grid, cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
                             float eps, float* out, cudaStream_t s);
 

@@ -222,10 +222,10 @@ __device__ __forceinline__ void tile_rows(const DevMat* const (&mats)[kTiles],
 #pragma unroll
     for (int i = 0; i < kTiles; ++i) {
         const DevMat m = *mats[i];
-        tr.body_lo[i] = m.body + (size_t)rows_lo[i] * m.bpr * body_bytes;
-        tr.body_hi[i] = m.body + (size_t)rows_hi[i] * m.bpr * body_bytes;
-        tr.d_lo[i] = m.d + (size_t)rows_lo[i] * m.bpr;
-        tr.d_hi[i] = m.d + (size_t)rows_hi[i] * m.bpr;
+        tr.body_lo[i] = m.body + blk_index(m.bpr, rows_lo[i], 0) * body_bytes;
+        tr.body_hi[i] = m.body + blk_index(m.bpr, rows_hi[i], 0) * body_bytes;
+        tr.d_lo[i] = m.d + blk_index(m.bpr, rows_lo[i], 0);
+        tr.d_hi[i] = m.d + blk_index(m.bpr, rows_hi[i], 0);
     }
 }
 
@@ -240,10 +240,10 @@ __device__ __forceinline__ void load_iq2_block(const TileRows& tr, uint32_t blk,
                                                Iq2Block& r) {
 #pragma unroll
     for (int i = 0; i < kTiles; ++i) {
-        r.a[i] = ldg128(tr.body_lo[i] + blk * 64u + 16u * q);
-        r.b[i] = ldg128(tr.body_hi[i] + blk * 64u + 16u * q);
-        r.da[i] = h2f(__ldg(tr.d_lo[i] + blk));
-        r.db[i] = h2f(__ldg(tr.d_hi[i] + blk));
+        r.a[i] = ldg128(tr.body_lo[i] + (size_t)blk * (kTileRows * 64u) + 16u * q);
+        r.b[i] = ldg128(tr.body_hi[i] + (size_t)blk * (kTileRows * 64u) + 16u * q);
+        r.da[i] = h2f(__ldg(tr.d_lo[i] + (size_t)blk * kTileRows));
+        r.db[i] = h2f(__ldg(tr.d_hi[i] + (size_t)blk * kTileRows));
     }
 }
 
@@ -311,10 +311,10 @@ __device__ __forceinline__ void q8_rows(const TileRows& tr, uint32_t k0, uint32_
                     float (&yb)[kTiles]) {
 #pragma unroll
         for (int i = 0; i < kTiles; ++i) {
-            xa[i] = __ldg(reinterpret_cast<const uint2*>(tr.body_lo[i] + b * 32u + 8u * q));
-            xb[i] = __ldg(reinterpret_cast<const uint2*>(tr.body_hi[i] + b * 32u + 8u * q));
-            ya[i] = h2f(__ldg(tr.d_lo[i] + b));
-            yb[i] = h2f(__ldg(tr.d_hi[i] + b));
+            xa[i] = __ldg(reinterpret_cast<const uint2*>(tr.body_lo[i] + (size_t)b * (kTileRows * 32u) + 8u * q));
+            xb[i] = __ldg(reinterpret_cast<const uint2*>(tr.body_hi[i] + (size_t)b * (kTileRows * 32u) + 8u * q));
+            ya[i] = h2f(__ldg(tr.d_lo[i] + (size_t)b * kTileRows));
+            yb[i] = h2f(__ldg(tr.d_hi[i] + (size_t)b * kTileRows));
         }
     };
     if (b0 >= b1) return;

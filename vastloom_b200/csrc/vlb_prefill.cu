@@ -1,0 +1,687 @@
+// Prefill expert products: a grouped GEMM on the 5th-generation tensor cores (tcgen05.mma, f32
+// accumulators in tensor memory) with the block dequantization fused into the operand path.
+//
+// Reference semantics: the same expert loop as the decode path (deepseek_v4_graph.cpp:2134-2227,
+// olmoe_runtime.cpp:1226-1285): gate = W1 x, up = W3 x, act = SwiGLU(gate, up) (times the route
+// weight before the down projection for DeepSeek V4, after it for OLMoE), y = W2 act, combined per
+// token. The products here round their operands to fp16, so the layer output matches the
+// reference's f32/f64 sums to about 1e-3 relative (the contract for this path is 2e-2).
+//
+// Work decomposition. Dispatch sorts the (token, slot) pairs by expert; prefill_plan_kernel cuts
+// each expert's pairs into column tiles of at most 192 pairs (balanced, so 300 pairs -> 150 + 150).
+// One work item is (column tile, 128-row block): gate/up computes 128 rows of W1 AND the same 128
+// rows of W3 into two TMEM accumulators and applies SwiGLU in the epilogue; down computes two
+// 128-row tiles of W2 the same way. A persistent CTA per SM takes items from an atomic counter;
+// the shared expert's tiles come first (heaviest).
+//
+// Data path of one 64-column stage:
+//   packed weights: the stage's 128-row tile block column is contiguous in the tiled device
+//     layout (8 KB of Q8_0 per matrix; an IQ2_XXS 256-column block covers four stages), so the
+//     loader warp brings it into a shared-memory ring with one bulk copy per matrix;
+//   A (weights): the producer warps decode their rows from that ring to fp16 in registers and
+//     write them straight into tensor memory (tcgen05.st): the MMA reads A from TMEM;
+//   B (activations): N rows of the pair-ordered fp16 matrix (xperm for gate/up, act_h for down),
+//     TMA-loaded as 16-row boxes into a shared-memory ring (K-major, 128-byte swizzle).
+// CTA roles (608 threads, one CTA per SM):
+//   warps 0-15  producers: thread t owns half (t / 128 % 2) of the 64 stage columns of row t % 128
+//               of accumulator t / 256 (its TMEM lane is its row). Afterwards they are the
+//               epilogue: tcgen05.ld of the accumulators, scaling, SwiGLU, stores.
+//   warp 16     loader: lane 0 issues the packed-weight bulk copies.
+//   warp 17     TMA: lane 0 issues the B boxes.
+//   warp 18     MMA: lane 0 issues the MMAs (M = 128, N = tile, K = 16; 8 per stage), commits
+//               each stage's A and B slots back and the finished accumulators to the epilogue.
+// TMEM (512 columns): accumulators at columns 0 and 192 (N <= 192 each), A double buffer at
+// 384 + slot * 64 (+ 32 for the second accumulator's rows).
+// Every wait is bounded by a 2 s time limit; a wait that runs out sets error bit 8 of the layer's
+// flags and an abort word that makes every other wait of the CTA give up, so a fault in the
+// pipeline ends the kernel (and the host call reports it) instead of hanging the GPU.
+//
+// Operand scaling (exact powers of two, removed in the epilogue):
+//   weights:      fp16(w * pscale), pscale per matrix (upload time) keeps |w * pscale| < 2^14;
+//   activations:  fp16(x * s_t), s_t brings max|x| of token t into [2^14, 2^15) (xmax of the
+//                 routing prescale); act likewise per pair from act_max.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <utility>
+#include <vector>
+
+#include "vlb_launch.h"
+#include "vlb_mma.cuh"
+#include "vlb_tcgen05.cuh"
+
+namespace vlb {
+namespace {
+
+constexpr uint32_t kPfM = 128;                       // rows per accumulator (MMA M)
+constexpr uint32_t kPfMaxN = 192;                    // pairs per column tile (MMA N)
+constexpr uint32_t kPfKc = 64;                       // columns per stage: one 128-byte fp16 row
+constexpr uint32_t kPfProducerWarps = 16;
+constexpr uint32_t kPfProducers = kPfProducerWarps * 32;
+constexpr uint32_t kPfLoadWarp = kPfProducerWarps;
+constexpr uint32_t kPfTmaWarp = kPfProducerWarps + 1;
+constexpr uint32_t kPfMmaWarp = kPfProducerWarps + 2;
+constexpr uint32_t kPfThreads = kPfProducers + 96;
+constexpr uint32_t kPfBoxRows = 16;                  // B rows per TMA box
+// shared memory: B ring, packed-weight ring, IQ2 table, per-tile scalars, barriers
+constexpr uint32_t kPfBStages = 4;
+constexpr uint32_t kPfBStage = kPfMaxN * kPfKc * 2;  // 24 KB
+constexpr uint32_t kPfRawStages = 4;
+constexpr uint32_t kPfRawBody = kTileRows * 64u;     // 8 KB per matrix: one tile block column
+constexpr uint32_t kPfRawD = 512;                    // its block scales (<= 2 blocks x 128 rows)
+constexpr uint32_t kPfRawStage = 2 * kPfRawBody + 2 * kPfRawD;
+constexpr uint32_t kPfRawOff = kPfBStages * kPfBStage;
+constexpr uint32_t kPfTabOff = kPfRawOff + kPfRawStages * kPfRawStage;
+constexpr uint32_t kPfTabBytes = 256u * 8u * 16u;    // fp16 IQ2_XXS magnitudes, 8 replicas
+constexpr uint32_t kPfInvOff = kPfTabOff + kPfTabBytes;
+constexpr uint32_t kPfPwOff = kPfInvOff + kPfMaxN * 4;
+constexpr uint32_t kPfBarOff = kPfPwOff + kPfMaxN * 4;
+constexpr uint32_t kPfBars = 2 * kPfRawStages + 2 * kPfBStages + 2 * 2 + 1;
+constexpr uint32_t kPfSmemBytes = kPfBarOff + kPfBars * 8 + 32;
+// tensor memory
+constexpr uint32_t kPfTmemCols = 512;
+constexpr uint32_t kPfAcc1Col = kPfMaxN;             // second accumulator's first column
+constexpr uint32_t kPfACol = 2 * kPfMaxN;            // A slots
+constexpr uint64_t kPfWaitNs = 2000000000ull;        // 2 s: no wait in a healthy kernel comes close
+constexpr uint32_t kPfSleepNs = 20000;               // suspend hint of the mostly-waiting lanes
+constexpr uint32_t kPfErrTimeout = 8u;
+constexpr uint32_t kPfErrAlign = 16u;
+
+static_assert(kPfSmemBytes <= 232448, "prefill rings exceed the shared memory of a CTA");
+static_assert(kPfBStage % 1024 == 0 && kPfRawOff % 1024 == 0, "swizzle atoms must stay 1 KB aligned");
+static_assert(kPfBoxRows * 128 % 1024 == 0, "TMA boxes must start on swizzle-atom boundaries");
+static_assert(kPfACol + 2 * 64 <= kPfTmemCols, "TMEM budget");
+
+__device__ __forceinline__ bool pf_mma_type(uint32_t t) { return t == kTypeIq2Xxs || t == kTypeQ8_0; }
+
+// Waits for `parity` of `bar`; false when the CTA aborted or the time limit ran out. sleep_ns > 0
+// lets the hardware suspend the thread between tests.
+__device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+                                        uint32_t sleep_ns) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (sleep_ns ? tc::mbar_try_sleep(bar, parity, sleep_ns) : tc::mbar_try(bar, parity)) return true;
+        if (sleep_ns || (i & 63u) == 0) {
+            if (*abort) return false;
+            const uint64_t now = tc::global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > kPfWaitNs) return false;
+            if (i >= (1u << 30)) return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void pf_fail(uint32_t* flags, volatile uint32_t* abort) {
+    *abort = 1u;
+    atomicOr(flags, kPfErrTimeout);
+}
+
+// Position in a ring of n slots: slot and the parity of the slot's current use.
+struct PfPos {
+    uint32_t slot, ph;
+    __device__ __forceinline__ void next(uint32_t n) {
+        if (++slot == n) {
+            slot = 0;
+            ph ^= 1u;
+        }
+    }
+};
+
+__device__ __forceinline__ uint32_t h2_bits(float v) {
+    const uint32_t u = __half_as_ushort(__float2half_rn(v));
+    return u | (u << 16);
+}
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+struct PfBars {
+    uint64_t* raw_full;   // [kPfRawStages]  loader -> producers (bulk-copy bytes)
+    uint64_t* raw_empty;  // [kPfRawStages]  producers -> loader
+    uint64_t* b_full;     // [kPfBStages]    TMA bytes -> MMA
+    uint64_t* b_empty;    // [kPfBStages]    MMA commit -> TMA
+    uint64_t* a_full;     // [2]             producers (TMEM A slot written) -> MMA
+    uint64_t* a_empty;    // [2]             MMA commit -> producers
+    uint64_t* acc_full;   //                 MMA commit -> epilogue
+    volatile uint32_t* abort;
+};
+
+// ---- decode of one half-row stage to 16 fp16x2 words --------------------------------------------
+// Q8_0 (decode_q8_0_block, ggml_quantization.cpp:419-435): w = d * q. q is an exact fp16, d * pscale
+// too (a power-of-two scaling of an fp16); their product rounds once.
+__device__ __forceinline__ void pf_decode_q8(uint4 q0, uint4 q1, uint32_t dbits, float ps, uint32_t (&v)[16]) {
+    const uint32_t dh = h2_bits(h2f((uint16_t)dbits) * ps);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 q = j < 2 ? q0 : q1;
+        uint32_t t[4];
+        mma::decode_q8_sub((j & 1) ? q.z : q.x, (j & 1) ? q.w : q.y, t);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[4 * j + i] = mma::hmul2(t[i], dh);
+    }
+}
+
+// IQ2_XXS (decode_iq2_xxs_block, ggml_quantization.cpp:250-283): w = d * (0.5 + s) / 4 * m * sign.
+// The group factor fp16(d * pscale * (0.5 + s) / 4) rounds once, its product with the exact grid
+// magnitude m once more; the sign is a bit flip.
+__device__ __forceinline__ void pf_decode_iq2(uint32_t idx4, uint32_t aux, float d, const uint4* tab,
+                                              uint32_t lane7, uint32_t (&v)[16]) {
+    const uint32_t kk = h2_bits(d * (0.5f + (float)(aux >> 28)) * 0.25f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t t[4];
+        mma::decode_iq2_sub(tab, lane7, idx4, aux, (uint32_t)j, kk, t);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[4 * j + i] = t[i];
+    }
+}
+
+// Publishes one decoded half-row stage into TMEM A slot `a`: waits for the slot, stores, orders
+// the store before the arrival the MMA lane waits for.
+__device__ __forceinline__ bool pf_put_a(const PfBars& br, PfPos& a, uint32_t taddr, const uint32_t (&v)[16]) {
+    // warp-uniform outcome: tcgen05.st is a whole-warp instruction
+    if (!__all_sync(0xffffffffu, pf_wait(br.a_empty + a.slot, a.ph ^ 1u, br.abort, 0))) return false;
+    tc::fence_after_sync();
+    tc::tmem_st16(taddr + a.slot * 64u, v);
+    tc::tmem_wait_st();
+    tc::fence_before_sync();
+    tc::mbar_arrive(br.a_full + a.slot);
+    a.next(2);
+    return true;
+}
+
+// One producer thread's main loop over an item: packed weights from the shared ring, decoded,
+// into its TMEM lane.
+template <uint32_t FMT>
+__device__ __forceinline__ bool pf_produce(const PfBars& br, uint32_t smem, const uint4* tab, float ps,
+                                           uint32_t acc, uint32_t half, uint32_t r, uint32_t t_a,
+                                           uint32_t nk, PfPos& raw, PfPos& a) {
+    const uint32_t lane7 = threadIdx.x & 7u;
+    if constexpr (FMT == kTypeQ8_0) {
+        // one raw stage per operand stage: block `half` of the two, row r
+        for (uint32_t kc = 0; kc < nk; ++kc) {
+            if (!__all_sync(0xffffffffu, pf_wait(br.raw_full + raw.slot, raw.ph, br.abort, 0))) return false;
+            const uint32_t rs = smem + kPfRawOff + raw.slot * kPfRawStage;
+            const uint32_t body = rs + acc * kPfRawBody + (half * kTileRows + r) * 32u;
+            const uint4 q0 = lds_u4(body), q1 = lds_u4(body + 16u);
+            const uint32_t dbits = lds_u16(rs + 2u * kPfRawBody + acc * kPfRawD + (half * kTileRows + r) * 2u);
+            tc::mbar_arrive(br.raw_empty + raw.slot);
+            raw.next(kPfRawStages);
+            uint32_t v[16];
+            pf_decode_q8(q0, q1, dbits, ps, v);
+            if (!pf_put_a(br, a, t_a, v)) return false;
+        }
+    } else {
+        // one raw stage (a 256-column block) per four operand stages; this thread's groups are
+        // half, 2 + half, 4 + half, 6 + half
+        for (uint32_t kb = 0; kb < nk / 4u; ++kb) {
+            if (!__all_sync(0xffffffffu, pf_wait(br.raw_full + raw.slot, raw.ph, br.abort, 0))) return false;
+            const uint32_t rs = smem + kPfRawOff + raw.slot * kPfRawStage;
+            const uint32_t body = rs + acc * kPfRawBody + r * 64u;
+            const uint4 c0 = lds_u4(body), c1 = lds_u4(body + 16u), c2 = lds_u4(body + 32u), c3 = lds_u4(body + 48u);
+            const uint32_t dbits = lds_u16(rs + 2u * kPfRawBody + acc * kPfRawD + r * 2u);
+            tc::mbar_arrive(br.raw_empty + raw.slot);
+            raw.next(kPfRawStages);
+            const float d = h2f((uint16_t)dbits) * ps;
+#pragma unroll
+            for (uint32_t sub = 0; sub < 4u; ++sub) {
+                const uint4 c = sub == 0 ? c0 : sub == 1 ? c1 : sub == 2 ? c2 : c3;  // groups 2 sub, 2 sub + 1
+                uint32_t v[16];
+                pf_decode_iq2(half ? c.z : c.x, half ? c.w : c.y, d, tab, lane7, v);
+                if (!pf_put_a(br, a, t_a, v)) return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Loader lane: the item's packed weights, one bulk copy per matrix body and per scale run.
+__device__ __forceinline__ bool pf_load_raw(const PfBars& br, uint32_t smem, const DevMat& m0, const DevMat& m1,
+                                            uint32_t rt0, uint32_t rt1, uint32_t nk, PfPos& raw) {
+    const bool q8 = m0.type == kTypeQ8_0;
+    const uint32_t stages = q8 ? nk : nk / 4u;
+    const uint32_t dbytes = q8 ? 2u * kTileRows * 2u : kTileRows * 2u;
+    for (uint32_t rs = 0; rs < stages; ++rs) {
+        if (!pf_wait(br.raw_empty + raw.slot, raw.ph ^ 1u, br.abort, kPfSleepNs)) return false;
+        const uint32_t dst = smem + kPfRawOff + raw.slot * kPfRawStage;
+        tc::mbar_arrive_expect_tx(br.raw_full + raw.slot, 2u * (kPfRawBody + dbytes));
+        const uint32_t blk = q8 ? 2u * rs : rs;
+#pragma unroll
+        for (uint32_t i = 0; i < 2u; ++i) {
+            const DevMat& m = i ? m1 : m0;
+            const size_t at = blk_index(m.bpr, (i ? rt1 : rt0) * kTileRows, blk);
+            tc::bulk_load(dst + i * kPfRawBody, m.body + at * (q8 ? 32u : 64u), kPfRawBody, br.raw_full + raw.slot);
+            tc::bulk_load(dst + 2u * kPfRawBody + i * kPfRawD, m.d + at, dbytes, br.raw_full + raw.slot);
+        }
+        raw.next(kPfRawStages);
+    }
+    return true;
+}
+
+// TMA lane: per stage, the N B rows (pair order, starting at row0) as N / 16 boxes.
+__device__ __forceinline__ bool pf_load_b(const PfBars& br, uint32_t smem, const CUtensorMap* map,
+                                          uint32_t row0, uint32_t nk, uint32_t N, PfPos& b) {
+    for (uint32_t kc = 0; kc < nk; ++kc) {
+        if (!pf_wait(br.b_empty + b.slot, b.ph ^ 1u, br.abort, kPfSleepNs)) return false;
+        tc::mbar_arrive_expect_tx(br.b_full + b.slot, N * kPfKc * 2u);
+        const uint32_t dst = smem + b.slot * kPfBStage;
+        for (uint32_t j = 0; j < N / kPfBoxRows; ++j)
+            tc::tma_load_2d(dst + j * kPfBoxRows * 128u, map, (int32_t)(kc * kPfKc), (int32_t)(row0 + j * kPfBoxRows),
+                            br.b_full + b.slot);
+        b.next(kPfBStages);
+    }
+    return true;
+}
+
+// MMA lane: per stage, 4 K-steps x 2 accumulators with A from TMEM and B from shared memory.
+__device__ __forceinline__ bool pf_mma(const PfBars& br, uint32_t smem, uint32_t tmem, uint32_t nk, uint32_t N,
+                                       PfPos& a, PfPos& b, bool& pending) {
+    const uint32_t idesc = tc::idesc_f16(kPfM, N);
+    for (uint32_t kc = 0; kc < nk; ++kc) {
+        if (!pf_wait(br.b_full + b.slot, b.ph, br.abort, kPfSleepNs)) return false;
+        if (!pf_wait(br.a_full + a.slot, a.ph, br.abort, kPfSleepNs)) return false;
+        tc::fence_after_sync();
+        const uint32_t bs = smem + b.slot * kPfBStage;
+        const uint32_t ta = tmem + kPfACol + a.slot * 64u;
+        pending = true;
+#pragma unroll
+        for (uint32_t ks = 0; ks < kPfKc / 16u; ++ks) {
+            const uint64_t bd = tc::sw128_desc(bs + ks * 32u);
+            const uint32_t accumulate = (kc | ks) ? 1u : 0u;
+            tc::mma_f16_ts(tmem, ta + ks * 8u, bd, idesc, accumulate);
+            tc::mma_f16_ts(tmem + kPfAcc1Col, ta + 32u + ks * 8u, bd, idesc, accumulate);
+        }
+        tc::mma_commit(br.a_empty + a.slot);
+        tc::mma_commit(br.b_empty + b.slot);
+        a.next(2);
+        b.next(kPfBStages);
+    }
+    tc::mma_commit(br.acc_full);
+    pending = false;
+    return true;
+}
+
+// silu(g) * u from the definition g / (1 + e^-g), with the approximate exponential and reciprocal
+// (relative error ~1e-6, far inside the prefill tolerance); e^-g = inf gives 0.
+__device__ __forceinline__ float pf_silu_mul(float g, float u) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + __expf(-g)));
+    return g * r * u;
+}
+
+// Max over the 32 lanes of each of 8 columns, as a reduce-scatter: on return lane l holds the
+// maximum of column (l >> 2) & 7 (9 shuffles instead of 40).
+__device__ __forceinline__ float pf_colmax8(const float (&v)[8]) {
+    const uint32_t lane = threadIdx.x & 31u;
+    float a4[4], a2[2];
+    const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float mine = b4 ? v[4 + i] : v[i], other = b4 ? v[i] : v[4 + i];
+        a4[i] = fmaxf(mine, __shfl_xor_sync(0xffffffffu, other, 16));
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float mine = b3 ? a4[2 + i] : a4[i], other = b3 ? a4[i] : a4[2 + i];
+        a2[i] = fmaxf(mine, __shfl_xor_sync(0xffffffffu, other, 8));
+    }
+    float a1 = fmaxf(b2 ? a2[1] : a2[0], __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 4));
+    a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+    return fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+}
+
+// Gate/up epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (rows) and every fourth 8-column
+// chunk starting at w / 4; writes act (f32) and the per-pair max |act|.
+__device__ __forceinline__ void pf_epilogue_gateup(const MoeParams& p, uint32_t tmem, const Unit& tile,
+                                                   uint32_t N, uint32_t row0, float inv_ps0,
+                                                   float inv_ps1, const float* tok_inv,
+                                                   const float* pw) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, lq = warp & 3u;
+    const uint32_t row = row0 + 32u * lq + lane;
+    const uint32_t t_lane = tmem + ((32u * lq) << 16);
+    const bool shared = tile.expert == p.E;
+    const float limit = shared ? p.shared_limit : p.routed_limit;
+    const bool clamp = !p.weight_after_down && limit > 0.f;
+    const bool weigh = !p.weight_after_down && !shared;
+    for (uint32_t j = warp >> 2; 8u * j < N; j += 4u) {
+        float g[8], u[8];
+        tc::tmem_ld8(t_lane + 8u * j, g);
+        tc::tmem_ld8(t_lane + kPfAcc1Col + 8u * j, u);
+        tc::tmem_wait_ld();
+        const uint32_t n0 = 8u * j;
+        float m[8];
+#pragma unroll
+        for (uint32_t i = 0; i < 8u; ++i) {
+            m[i] = 0.f;
+            const uint32_t n = n0 + i;
+            if (n < tile.count) {
+                const float inv = tok_inv[n];
+                float gv = g[i] * inv * inv_ps0, uv = u[i] * inv * inv_ps1;
+                if (clamp) {
+                    gv = fminf(gv, limit);
+                    uv = fminf(fmaxf(uv, -limit), limit);
+                }
+                float a = pf_silu_mul(gv, uv);
+                if (weigh) a *= pw[n];
+                p.act[(size_t)(tile.pair_begin + n) * p.I + row] = a;
+                m[i] = fabsf(a);
+            }
+        }
+        const float cm = pf_colmax8(m);
+        const uint32_t col = (lane >> 2) & 7u;
+        if ((lane & 3u) == 0 && n0 + col < tile.count)
+            atomicMax(p.act_max + tile.pair_begin + n0 + col, __float_as_uint(cm));
+    }
+}
+
+// Down epilogue: the two accumulators are rows row0.. and row0 + 128.. of W2; y in f32.
+__device__ __forceinline__ void pf_epilogue_down(const MoeParams& p, uint32_t tmem, const Unit& tile,
+                                                 uint32_t N, uint32_t row0, float inv_ps,
+                                                 const float* tok_inv) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, lq = warp & 3u;
+    const uint32_t r0 = row0 + 32u * lq + lane, r1 = r0 + kPfM;
+    const uint32_t t_lane = tmem + ((32u * lq) << 16);
+    for (uint32_t j = warp >> 2; 8u * j < N; j += 4u) {
+        float a[8], b[8];
+        tc::tmem_ld8(t_lane + 8u * j, a);
+        tc::tmem_ld8(t_lane + kPfAcc1Col + 8u * j, b);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (uint32_t i = 0; i < 8u; ++i) {
+            const uint32_t n = 8u * j + i;
+            if (n < tile.count) {
+                const float inv = tok_inv[n] * inv_ps;
+                float* yr = p.y + (size_t)(tile.pair_begin + n) * p.H;
+                yr[r0] = a[i] * inv;
+                yr[r1] = b[i] * inv;
+            }
+        }
+    }
+}
+
+template <bool GATEUP>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(const __grid_constant__ MoeParams p) {
+    extern __shared__ __align__(1024) unsigned char pf_smem[];
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t smem = tc::smem_u32(pf_smem);
+    if (smem & 1023u) {  // the swizzle atoms need 1 KB alignment; uniform across the CTA
+        if (tid == 0) atomicOr(p.counters + 3, kPfErrAlign);
+        return;
+    }
+    const uint4* tab = reinterpret_cast<const uint4*>(pf_smem + kPfTabOff);
+    float* tok_inv = reinterpret_cast<float*>(pf_smem + kPfInvOff);
+    float* pw = reinterpret_cast<float*>(pf_smem + kPfPwOff);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(pf_smem + kPfBarOff);
+    uint32_t* misc = reinterpret_cast<uint32_t*>(bars + kPfBars);  // [0] TMEM base [1] item [2] abort
+    PfBars br;
+    br.raw_full = bars;
+    br.raw_empty = br.raw_full + kPfRawStages;
+    br.b_full = br.raw_empty + kPfRawStages;
+    br.b_empty = br.b_full + kPfBStages;
+    br.a_full = br.b_empty + kPfBStages;
+    br.a_empty = br.a_full + 2;
+    br.acc_full = br.a_empty + 2;
+    br.abort = misc + 2;
+    const CUtensorMap* bmap = GATEUP ? &p.bmap_x : &p.bmap_act;
+    if (warp == kPfMmaWarp) tc::tmem_alloc(misc, kPfTmemCols);
+    if (tid == 0) {
+        for (uint32_t i = 0; i < kPfRawStages; ++i) {
+            tc::mbar_init(br.raw_full + i, 1);
+            tc::mbar_init(br.raw_empty + i, kPfProducers);
+        }
+        for (uint32_t i = 0; i < kPfBStages; ++i) {
+            tc::mbar_init(br.b_full + i, 1);
+            tc::mbar_init(br.b_empty + i, 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            tc::mbar_init(br.a_full + i, kPfProducers);
+            tc::mbar_init(br.a_empty + i, 1);
+        }
+        tc::mbar_init(br.acc_full, 1);
+        misc[2] = 0;
+        tc::mbar_fence_init();
+    }
+    if (warp == kPfTmaWarp && lane == 0)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(bmap)) : "memory");
+    mma::build_iq2_table(reinterpret_cast<uint4*>(pf_smem + kPfTabOff), p.grids.iq2xxs);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = misc[0];
+
+    const uint32_t K = GATEUP ? p.H : p.I;
+    const uint32_t nk = K / kPfKc;
+    const uint32_t per_tile = GATEUP ? p.I / kPfM : p.H / (2u * kPfM);
+    const uint32_t n_items = p.counters[7] * per_tile;
+    uint32_t* next = p.counters + (GATEUP ? 5 : 6);
+    // producer geometry: row r of accumulator acc, column half `half` of each stage; its TMEM
+    // lane is r (warp % 4 == r / 32), its A columns 16 * half of the accumulator's 32 per slot
+    const uint32_t acc = tid >> 8, half = (tid >> 7) & 1u, r = tid & (kPfM - 1u);
+    const uint32_t t_a = tmem + ((32u * (warp & 3u)) << 16) + kPfACol + acc * 32u + half * 16u;
+    PfPos raw{0, 0}, bp{0, 0}, ap{0, 0};
+    uint32_t item_it = 0, pending_parity = 0;
+    bool pending = false, copies_dirty = false;
+    for (;;) {
+        __syncthreads();
+        if (tid == 0) misc[1] = *br.abort ? 0xffffffffu : atomicAdd(next, 1u);
+        __syncthreads();
+        const uint32_t item = misc[1];
+        if (item >= n_items) break;
+        const Unit tile = p.ptiles[item / per_tile];
+        const uint32_t mi = item % per_tile;
+        const DevMat* m0 = p.mats + (GATEUP ? 0u : 2u * (p.E + 1)) + tile.expert;
+        const DevMat* m1 = GATEUP ? p.mats + (p.E + 1) + tile.expert : m0;
+        const uint32_t type = m0->type;
+        if (!pf_mma_type(type)) continue;  // served by the CUDA-core expert kernels
+        const uint32_t N = (tile.count + 15u) & ~15u;
+        // row tiles (128 rows) of the two accumulators
+        const uint32_t rt0 = GATEUP ? mi : 2u * mi, rt1 = GATEUP ? mi : 2u * mi + 1u;
+        if (tid < tile.count) {
+            const uint32_t pair = tile.pair_begin + tid;
+            const uint32_t bits = GATEUP ? p.xmax[p.pair_token[pair]] : p.act_max[pair];
+            tok_inv[tid] = 1.f / mma::prescale_for(__uint_as_float(bits));
+            pw[tid] = p.pair_weight[pair];
+        }
+        __syncthreads();
+        if (warp < kPfProducerWarps) {
+            const float ps = (acc ? m1 : m0)->pscale;
+            bool ok = type == kTypeQ8_0
+                          ? pf_produce<kTypeQ8_0>(br, smem, tab, ps, acc, half, r, t_a, nk, raw, ap)
+                          : pf_produce<kTypeIq2Xxs>(br, smem, tab, ps, acc, half, r, t_a, nk, raw, ap);
+            if (ok) ok = pf_wait(br.acc_full, item_it & 1u, br.abort, 0);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is a whole-warp instruction
+            if (ok) {
+                tc::fence_after_sync();
+                if (GATEUP)
+                    pf_epilogue_gateup(p, tmem, tile, N, rt0 * kPfM, 1.f / m0->pscale, 1.f / m1->pscale, tok_inv, pw);
+                else
+                    pf_epilogue_down(p, tmem, tile, N, rt0 * kPfM, 1.f / m0->pscale, tok_inv);
+            } else {
+                pf_fail(p.counters + 3, br.abort);
+            }
+            tc::fence_before_sync();
+        } else if (warp == kPfLoadWarp) {
+            if (lane == 0) {
+                copies_dirty = true;
+                if (pf_load_raw(br, smem, *m0, *m1, rt0, rt1, nk, raw)) copies_dirty = false;
+                else pf_fail(p.counters + 3, br.abort);
+            }
+        } else if (warp == kPfTmaWarp) {
+            if (lane == 0) {
+                copies_dirty = true;
+                if (pf_load_b(br, smem, bmap, tile.pair_begin, nk, N, bp)) copies_dirty = false;
+                else pf_fail(p.counters + 3, br.abort);
+            }
+        } else if (lane == 0) {
+            pending_parity = item_it & 1u;
+            if (!pf_mma(br, smem, tmem, nk, N, ap, bp, pending)) pf_fail(p.counters + 3, br.abort);
+        }
+        ++item_it;
+    }
+    __syncthreads();
+    if ((warp == kPfLoadWarp || warp == kPfTmaWarp) && lane == 0 && copies_dirty) {
+        // after an abort, let copies already issued land before the CTA's shared memory goes away
+        const uint64_t t0 = tc::global_ns();
+        while (tc::global_ns() - t0 < 1000000ull) {
+        }
+    }
+    if (warp == kPfMmaWarp) {
+        // after an abort, MMAs already issued must finish before their TMEM is released
+        if (lane == 0 && pending) {
+            tc::mma_commit(br.acc_full);
+            const uint64_t t0 = tc::global_ns();
+            while (!tc::mbar_try(br.acc_full, pending_parity) && tc::global_ns() - t0 < kPfWaitNs) {
+            }
+        }
+        __syncwarp();
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kPfTmemCols);
+    }
+    __syncthreads();
+}
+
+// Column tiles of every expert's pairs (the shared expert first): an expert with c pairs gets
+// ceil(c / 256) tiles of balanced size. One CTA.
+__global__ void __launch_bounds__(512) prefill_plan_kernel(MoeParams p) {
+    __shared__ uint32_t nt[513];
+    __shared__ uint32_t warp_sum[16];
+    const uint32_t E = p.E, n = p.T * p.k, tid = threadIdx.x;
+    auto count_of = [&](uint32_t o, uint32_t* begin, uint32_t* expert) -> uint32_t {
+        if (o == 0) {
+            *begin = n;
+            *expert = E;
+            return p.has_shared ? p.T : 0u;
+        }
+        *begin = p.offsets[o - 1];
+        *expert = o - 1;
+        return p.offsets[o] - p.offsets[o - 1];
+    };
+    // exclusive scan of the tile counts over ordinals 0..E, blockDim.x ordinals per pass
+    uint32_t running = 0;
+    for (uint32_t base = 0; base <= E; base += blockDim.x) {
+        const uint32_t o = base + tid;
+        uint32_t b, e, c = 0;
+        if (o <= E) c = count_of(o, &b, &e);
+        const uint32_t v = (c + kPfMaxN - 1u) / kPfMaxN;
+        uint32_t incl = v;
+        const uint32_t lane = tid & 31u, w = tid >> 5;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= (uint32_t)d) incl += y;
+        }
+        if (lane == 31) warp_sum[w] = incl;
+        __syncthreads();
+        uint32_t before = running;
+        for (uint32_t i = 0; i < w; ++i) before += warp_sum[i];
+        if (o <= E) nt[o] = before + incl - v;  // exclusive
+        uint32_t total = 0;
+        for (uint32_t i = 0; i < blockDim.x / 32u; ++i) total += warp_sum[i];
+        __syncthreads();
+        running += total;
+    }
+    for (uint32_t o = tid; o <= E; o += blockDim.x) {
+        uint32_t b, e;
+        const uint32_t c = count_of(o, &b, &e);
+        const uint32_t tiles = (c + kPfMaxN - 1u) / kPfMaxN;
+        for (uint32_t j = 0; j < tiles; ++j) {
+            const uint32_t at = nt[o] + j;
+            if (at >= p.max_ptiles) break;
+            const uint32_t lo = (uint32_t)((uint64_t)c * j / tiles), hi = (uint32_t)((uint64_t)c * (j + 1) / tiles);
+            p.ptiles[at] = Unit{e, b + lo, hi - lo, 0u};
+        }
+    }
+    if (tid == 0) p.counters[7] = running < p.max_ptiles ? running : p.max_ptiles;
+}
+
+// Pair-ordered fp16 activations: xperm[pair] = fp16(x[token(pair)] * s_token). 4 columns a thread.
+__global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __restrict__ x,
+                                                             const uint32_t* __restrict__ pair_token,
+                                                             const uint32_t* __restrict__ xmax,
+                                                             uint32_t width, __half* __restrict__ dst) {
+    const uint32_t pr = blockIdx.y;
+    const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
+    if (c >= width) return;
+    const uint32_t t = pair_token[pr];
+    const float s = mma::prescale_for(__uint_as_float(xmax[t]));
+    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * width + c);
+    const __half2 a = __floats2half2_rn(v.x * s, v.y * s), b = __floats2half2_rn(v.z * s, v.w * s);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&a);
+    o.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(dst + (size_t)pr * width + c) = o;
+}
+
+// fp16(act * s) rows with s the power of two of each row's max (act_max); 4 columns a thread.
+__global__ void __launch_bounds__(256) prefill_half_kernel(const float* __restrict__ src,
+                                                           const uint32_t* __restrict__ rmax,
+                                                           uint32_t width, __half* __restrict__ dst) {
+    const uint32_t r = blockIdx.y;
+    const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
+    if (c >= width) return;
+    const float s = mma::prescale_for(__uint_as_float(rmax[r]));
+    const float4 v = *reinterpret_cast<const float4*>(src + (size_t)r * width + c);
+    const __half2 a = __floats2half2_rn(v.x * s, v.y * s), b = __floats2half2_rn(v.z * s, v.w * s);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&a);
+    o.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(dst + (size_t)r * width + c) = o;
+}
+
+template <typename Kern>
+cudaError_t pf_smem_once(Kern kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, size_t>> done;
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& d : done)
+        if (d.first == (const void*)kernel && d.second >= bytes) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done.emplace_back((const void*)kernel, bytes);
+    return e;
+}
+
+uint32_t pairs_of(const MoeParams& p) { return p.T * p.k + (p.has_shared ? p.T : 0u); }
+
+}  // namespace
+
+uint32_t prefill_max_tiles(uint32_t T, uint32_t k, uint32_t E) {
+    return (T * k + T) / kPfMaxN + E + 2u;
+}
+
+uint32_t prefill_box_rows() { return kPfBoxRows; }
+
+cudaError_t launch_prefill_plan(const MoeParams& p, cudaStream_t s) {
+    prefill_plan_kernel<<<1, 512, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_t s) {
+    prefill_gather_kernel<<<dim3((p.H / 4 + 255) / 256, pairs_of(p)), 256, 0, s>>>(p.x, p.pair_token, p.xmax,
+                                                                                    p.H, p.xperm);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if ((e = pf_smem_once(prefill_gemm_kernel<true>, kPfSmemBytes)) != cudaSuccess) return e;
+    prefill_gemm_kernel<true><<<grid, kPfThreads, kPfSmemBytes, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_down(const MoeParams& p, unsigned grid, cudaStream_t s) {
+    prefill_half_kernel<<<dim3((p.I / 4 + 255) / 256, pairs_of(p)), 256, 0, s>>>(p.act, p.act_max, p.I, p.act_h);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if ((e = pf_smem_once(prefill_gemm_kernel<false>, kPfSmemBytes)) != cudaSuccess) return e;
+    prefill_gemm_kernel<false><<<grid, kPfThreads, kPfSmemBytes, s>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace vlb
