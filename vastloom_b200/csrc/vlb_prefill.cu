@@ -8,7 +8,7 @@
 // reference's f32/f64 sums to about 1e-3 relative (the contract for this path is 2e-2).
 //
 // Work decomposition. Dispatch sorts the (token, slot) pairs by expert; prefill_plan_kernel cuts
-// each expert's pairs into column tiles of at most 192 pairs (balanced, so 300 pairs -> 150 + 150).
+// each expert's pairs into column tiles of at most 160 pairs (balanced, so 300 pairs -> 150 + 150).
 // One work item is (column tile, 128-row block): gate/up computes 128 rows of W1 AND the same 128
 // rows of W3 into two TMEM accumulators and applies SwiGLU in the epilogue; down computes two
 // 128-row tiles of W2 the same way. A persistent CTA per SM takes items from an atomic counter;
@@ -30,8 +30,8 @@
 //   warp 17     TMA: lane 0 issues the B boxes.
 //   warp 18     MMA: lane 0 issues the MMAs (M = 128, N = tile, K = 16; 8 per stage), commits
 //               each stage's A and B slots back and the finished accumulators to the epilogue.
-// TMEM (512 columns): accumulators at columns 0 and 192 (N <= 192 each), A double buffer at
-// 384 + slot * 64 (+ 32 for the second accumulator's rows).
+// TMEM (512 columns): accumulators at columns 0 and 160 (N <= 160 each), three A slots at
+// 320 + slot * 64 (+ 32 for the second accumulator's rows).
 // Every wait is bounded by a 2 s time limit; a wait that runs out sets error bit 8 of the layer's
 // flags and an abort word that makes every other wait of the CTA give up, so a fault in the
 // pipeline ends the kernel (and the host call reports it) instead of hanging the GPU.
@@ -55,7 +55,7 @@ namespace vlb {
 namespace {
 
 constexpr uint32_t kPfM = 128;                       // rows per accumulator (MMA M)
-constexpr uint32_t kPfMaxN = 192;                    // pairs per column tile (MMA N)
+constexpr uint32_t kPfMaxN = 160;                    // pairs per column tile (MMA N)
 constexpr uint32_t kPfKc = 64;                       // columns per stage: one 128-byte fp16 row
 constexpr uint32_t kPfProducerWarps = 16;
 constexpr uint32_t kPfProducers = kPfProducerWarps * 32;
@@ -64,10 +64,12 @@ constexpr uint32_t kPfTmaWarp = kPfProducerWarps + 1;
 constexpr uint32_t kPfMmaWarp = kPfProducerWarps + 2;
 constexpr uint32_t kPfThreads = kPfProducers + 96;
 constexpr uint32_t kPfBoxRows = 16;                  // B rows per TMA box
+constexpr uint32_t kPfASlots = 3;                    // A operand buffers in TMEM
 // shared memory: B ring, packed-weight ring, IQ2 table, per-tile scalars, barriers
-constexpr uint32_t kPfBStages = 4;
-constexpr uint32_t kPfBStage = kPfMaxN * kPfKc * 2;  // 24 KB
-constexpr uint32_t kPfRawStages = 4;
+constexpr uint32_t kPfBStages = 5;                   // B (activation) ring slots
+constexpr uint32_t kPfRing = 6;                      // stage barrier ring (>= A and B slots)
+constexpr uint32_t kPfBStage = kPfMaxN * kPfKc * 2;  // 20 KB
+constexpr uint32_t kPfRawStages = 5;                 // packed-weight ring: ~85 KB in flight
 constexpr uint32_t kPfRawBody = kTileRows * 64u;     // 8 KB per matrix: one tile block column
 constexpr uint32_t kPfRawD = 512;                    // its block scales (<= 2 blocks x 128 rows)
 constexpr uint32_t kPfRawStage = 2 * kPfRawBody + 2 * kPfRawD;
@@ -77,7 +79,7 @@ constexpr uint32_t kPfTabBytes = 256u * 8u * 16u;    // fp16 IQ2_XXS magnitudes,
 constexpr uint32_t kPfInvOff = kPfTabOff + kPfTabBytes;
 constexpr uint32_t kPfPwOff = kPfInvOff + kPfMaxN * 4;
 constexpr uint32_t kPfBarOff = kPfPwOff + kPfMaxN * 4;
-constexpr uint32_t kPfBars = 2 * kPfRawStages + 2 * kPfBStages + 2 * 2 + 1;
+constexpr uint32_t kPfBars = 2 * kPfRawStages + 2 * kPfRing + 1;
 constexpr uint32_t kPfSmemBytes = kPfBarOff + kPfBars * 8 + 32;
 // tensor memory
 constexpr uint32_t kPfTmemCols = 512;
@@ -85,24 +87,34 @@ constexpr uint32_t kPfAcc1Col = kPfMaxN;             // second accumulator's fir
 constexpr uint32_t kPfACol = 2 * kPfMaxN;            // A slots
 constexpr uint64_t kPfWaitNs = 2000000000ull;        // 2 s: no wait in a healthy kernel comes close
 constexpr uint32_t kPfSleepNs = 20000;               // suspend hint of the mostly-waiting lanes
+#ifndef VLB_PF_BACKOFF_NS
+#define VLB_PF_BACKOFF_NS 128
+#endif
+// Producer warps park between polls: a spinning lane 0 in each of 16 warps would take the issue
+// slots the decode and MMA lanes need.
+constexpr uint32_t kPfBackoffNs = VLB_PF_BACKOFF_NS;
 constexpr uint32_t kPfErrTimeout = 8u;
 constexpr uint32_t kPfErrAlign = 16u;
 
 static_assert(kPfSmemBytes <= 232448, "prefill rings exceed the shared memory of a CTA");
 static_assert(kPfBStage % 1024 == 0 && kPfRawOff % 1024 == 0, "swizzle atoms must stay 1 KB aligned");
 static_assert(kPfBoxRows * 128 % 1024 == 0, "TMA boxes must start on swizzle-atom boundaries");
-static_assert(kPfACol + 2 * 64 <= kPfTmemCols, "TMEM budget");
+static_assert(kPfACol + kPfASlots * 64 <= kPfTmemCols, "TMEM budget");
+static_assert(kPfRing >= kPfBStages + 1 && kPfRing >= kPfASlots + 1,
+              "a slot's waiter must never fall two phases behind on the stage barrier ring");
 
 __device__ __forceinline__ bool pf_mma_type(uint32_t t) { return t == kTypeIq2Xxs || t == kTypeQ8_0; }
 
 // Waits for `parity` of `bar`; false when the CTA aborted or the time limit ran out. sleep_ns > 0
-// lets the hardware suspend the thread between tests.
+// lets the hardware suspend the thread inside each test; backoff_ns > 0 parks the warp between
+// tests (a polling warp otherwise takes issue slots from the warps doing the work).
 __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
-                                        uint32_t sleep_ns) {
+                                        uint32_t sleep_ns, uint32_t backoff_ns = 0) {
     uint64_t t0 = 0;
     for (uint32_t i = 1;; ++i) {
         if (sleep_ns ? tc::mbar_try_sleep(bar, parity, sleep_ns) : tc::mbar_try(bar, parity)) return true;
-        if (sleep_ns || (i & 63u) == 0) {
+        if (backoff_ns) __nanosleep(backoff_ns);
+        if (sleep_ns || backoff_ns || (i & 63u) == 0) {
             if (*abort) return false;
             const uint64_t now = tc::global_ns();
             if (t0 == 0) t0 = now;
@@ -115,6 +127,20 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile
 __device__ __forceinline__ void pf_fail(uint32_t* flags, volatile uint32_t* abort) {
     *abort = 1u;
     atomicOr(flags, kPfErrTimeout);
+}
+
+// A producer warp's wait: lane 0 polls, the outcome is broadcast (and the warp reconverged).
+__device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
+    bool ok = true;
+    if ((threadIdx.x & 31u) == 0) ok = pf_wait(bar, parity, abort, 0, kPfBackoffNs);
+    return __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0;
+}
+
+// A producer warp's arrival: every lane's prior shared-memory reads and TMEM stores are ordered
+// before lane 0's (release) arrival by the warp barrier; the mbarrier counts warps.
+__device__ __forceinline__ void pf_arrive_warp(uint64_t* bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(bar);
 }
 
 // Position in a ring of n slots: slot and the parity of the slot's current use.
@@ -145,16 +171,27 @@ __device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
     return v;
 }
 
+// Operand stages are numbered globally across the CTA's items (g = 0, 1, ...). Stage g uses A slot
+// g % kPfASlots (TMEM), B slot g % kPfBStages (shared memory) and one pair of barriers, index
+// g % kPfRing: full (16 producer-warp arrivals + the TMA lane's transaction bytes) and empty (one
+// tcgen05.commit after the stage's MMAs, which frees both slots). One commit per stage matters:
+// every commit costs the tensor pipe a short drain. The producers reuse an A slot after stage
+// g - kPfASlots's commit, the TMA lane a B slot after stage g - kPfBStages's.
 struct PfBars {
     uint64_t* raw_full;   // [kPfRawStages]  loader -> producers (bulk-copy bytes)
     uint64_t* raw_empty;  // [kPfRawStages]  producers -> loader
-    uint64_t* b_full;     // [kPfBStages]    TMA bytes -> MMA
-    uint64_t* b_empty;    // [kPfBStages]    MMA commit -> TMA
-    uint64_t* a_full;     // [2]             producers (TMEM A slot written) -> MMA
-    uint64_t* a_empty;    // [2]             MMA commit -> producers
+    uint64_t* full;       // [kPfRing]       producers + TMA bytes -> MMA
+    uint64_t* empty;      // [kPfRing]       MMA commit -> producers, TMA
     uint64_t* acc_full;   //                 MMA commit -> epilogue
     volatile uint32_t* abort;
 };
+
+// Waits until stage g's commit (if g is a real stage: g >= 0) freed its slots.
+__device__ __forceinline__ bool pf_wait_freed(const PfBars& br, int64_t g, uint32_t sleep_ns, uint32_t backoff_ns = 0) {
+    if (g < 0) return true;
+    return pf_wait(br.empty + (uint32_t)(g % kPfRing), (uint32_t)((g / kPfRing) & 1), br.abort, sleep_ns,
+                   backoff_ns);
+}
 
 // ---- decode of one half-row stage to 16 fp16x2 words --------------------------------------------
 // Q8_0 (decode_q8_0_block, ggml_quantization.cpp:419-435): w = d * q. q is an exact fp16, d * pscale
@@ -186,59 +223,82 @@ __device__ __forceinline__ void pf_decode_iq2(uint32_t idx4, uint32_t aux, float
     }
 }
 
-// Publishes one decoded half-row stage into TMEM A slot `a`: waits for the slot, stores, orders
-// the store before the arrival the MMA lane waits for.
-__device__ __forceinline__ bool pf_put_a(const PfBars& br, PfPos& a, uint32_t taddr, const uint32_t (&v)[16]) {
-    // warp-uniform outcome: tcgen05.st is a whole-warp instruction
-    if (!__all_sync(0xffffffffu, pf_wait(br.a_empty + a.slot, a.ph ^ 1u, br.abort, 0))) return false;
+// Issues the TMEM store of one decoded half-row stage (32 fp16 = 16 columns) into the A slot of
+// global stage g once stage g - kPfASlots's MMAs released it. Completion is published later by
+// pf_publish_a, so the warp decodes the next stage while the store is in flight.
+__device__ __forceinline__ bool pf_store_a(const PfBars& br, uint32_t g, uint32_t taddr, const uint32_t (&v)[16]) {
+    bool ok = true;
+    if ((threadIdx.x & 31u) == 0) ok = pf_wait_freed(br, (int64_t)g - kPfASlots, 0, kPfBackoffNs);
+    if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0) return false;
     tc::fence_after_sync();
-    tc::tmem_st16(taddr + a.slot * 64u, v);
+    tc::tmem_st16(taddr + (g % kPfASlots) * 64u, v);
+    return true;
+}
+
+// Waits for the warp's outstanding TMEM store and arrives on stage g's full barrier.
+__device__ __forceinline__ void pf_publish_a(const PfBars& br, uint32_t g) {
     tc::tmem_wait_st();
     tc::fence_before_sync();
-    tc::mbar_arrive(br.a_full + a.slot);
-    a.next(2);
+    pf_arrive_warp(br.full + g % kPfRing);
+}
+
+// Q8_0 raw stage -> decoded half-row (block `half` of the stage's two, row r).
+__device__ __forceinline__ bool pf_fetch_q8(const PfBars& br, uint32_t smem, uint32_t rs, uint32_t acc, uint32_t half,
+                                            uint32_t r, float ps, uint32_t (&v)[16]) {
+    const uint32_t rslot = rs % kPfRawStages;
+    if (!pf_wait_warp(br.raw_full + rslot, (rs / kPfRawStages) & 1u, br.abort)) return false;
+    const uint32_t st = smem + kPfRawOff + rslot * kPfRawStage;
+    const uint32_t body = st + acc * kPfRawBody + (half * kTileRows + r) * 32u;
+    const uint4 q0 = lds_u4(body), q1 = lds_u4(body + 16u);
+    const uint32_t dbits = lds_u16(st + 2u * kPfRawBody + acc * kPfRawD + (half * kTileRows + r) * 2u);
+    pf_arrive_warp(br.raw_empty + rslot);
+    pf_decode_q8(q0, q1, dbits, ps, v);
     return true;
 }
 
 // One producer thread's main loop over an item: packed weights from the shared ring, decoded,
-// into its TMEM lane.
+// into its TMEM lane, software-pipelined so that stage kc + 1's decode overlaps stage kc's TMEM
+// store. g0 / rs0: global numbers of the item's first stage / raw stage.
 template <uint32_t FMT>
 __device__ __forceinline__ bool pf_produce(const PfBars& br, uint32_t smem, const uint4* tab, float ps,
                                            uint32_t acc, uint32_t half, uint32_t r, uint32_t t_a,
-                                           uint32_t nk, PfPos& raw, PfPos& a) {
+                                           uint32_t nk, uint32_t g0, uint32_t rs0) {
     const uint32_t lane7 = threadIdx.x & 7u;
     if constexpr (FMT == kTypeQ8_0) {
-        // one raw stage per operand stage: block `half` of the two, row r
+        // one raw stage per operand stage
+        uint32_t v[16];
+        if (!pf_fetch_q8(br, smem, rs0, acc, half, r, ps, v)) return false;
         for (uint32_t kc = 0; kc < nk; ++kc) {
-            if (!__all_sync(0xffffffffu, pf_wait(br.raw_full + raw.slot, raw.ph, br.abort, 0))) return false;
-            const uint32_t rs = smem + kPfRawOff + raw.slot * kPfRawStage;
-            const uint32_t body = rs + acc * kPfRawBody + (half * kTileRows + r) * 32u;
-            const uint4 q0 = lds_u4(body), q1 = lds_u4(body + 16u);
-            const uint32_t dbits = lds_u16(rs + 2u * kPfRawBody + acc * kPfRawD + (half * kTileRows + r) * 2u);
-            tc::mbar_arrive(br.raw_empty + raw.slot);
-            raw.next(kPfRawStages);
-            uint32_t v[16];
-            pf_decode_q8(q0, q1, dbits, ps, v);
-            if (!pf_put_a(br, a, t_a, v)) return false;
+            if (!pf_store_a(br, g0 + kc, t_a, v)) return false;
+            if (kc + 1u < nk && !pf_fetch_q8(br, smem, rs0 + kc + 1u, acc, half, r, ps, v)) {
+                tc::tmem_wait_st();
+                return false;
+            }
+            pf_publish_a(br, g0 + kc);
         }
     } else {
         // one raw stage (a 256-column block) per four operand stages; this thread's groups are
         // half, 2 + half, 4 + half, 6 + half
         for (uint32_t kb = 0; kb < nk / 4u; ++kb) {
-            if (!__all_sync(0xffffffffu, pf_wait(br.raw_full + raw.slot, raw.ph, br.abort, 0))) return false;
-            const uint32_t rs = smem + kPfRawOff + raw.slot * kPfRawStage;
-            const uint32_t body = rs + acc * kPfRawBody + r * 64u;
+            const uint32_t rs = rs0 + kb, rslot = rs % kPfRawStages;
+            if (!pf_wait_warp(br.raw_full + rslot, (rs / kPfRawStages) & 1u, br.abort)) return false;
+            const uint32_t st = smem + kPfRawOff + rslot * kPfRawStage;
+            const uint32_t body = st + acc * kPfRawBody + r * 64u;
             const uint4 c0 = lds_u4(body), c1 = lds_u4(body + 16u), c2 = lds_u4(body + 32u), c3 = lds_u4(body + 48u);
-            const uint32_t dbits = lds_u16(rs + 2u * kPfRawBody + acc * kPfRawD + r * 2u);
-            tc::mbar_arrive(br.raw_empty + raw.slot);
-            raw.next(kPfRawStages);
+            const uint32_t dbits = lds_u16(st + 2u * kPfRawBody + acc * kPfRawD + r * 2u);
+            pf_arrive_warp(br.raw_empty + rslot);
             const float d = h2f((uint16_t)dbits) * ps;
+            uint32_t v[16];
+            pf_decode_iq2(half ? c0.z : c0.x, half ? c0.w : c0.y, d, tab, lane7, v);
 #pragma unroll
-            for (uint32_t sub = 0; sub < 4u; ++sub) {
-                const uint4 c = sub == 0 ? c0 : sub == 1 ? c1 : sub == 2 ? c2 : c3;  // groups 2 sub, 2 sub + 1
-                uint32_t v[16];
-                pf_decode_iq2(half ? c.z : c.x, half ? c.w : c.y, d, tab, lane7, v);
-                if (!pf_put_a(br, a, t_a, v)) return false;
+            for (uint32_t sub = 0; sub < 4u; ++sub) {  // groups 2 sub, 2 sub + 1
+                const uint32_t g = g0 + 4u * kb + sub;
+                if (!pf_store_a(br, g, t_a, v)) return false;
+                if (sub < 3u) {
+                    const uint4 c = sub == 0 ? c1 : sub == 1 ? c2 : c3;
+                    pf_decode_iq2(half ? c.z : c.x, half ? c.w : c.y, d, tab, lane7, v);
+                }
+                pf_publish_a(br, g);
             }
         }
     }
@@ -270,29 +330,30 @@ __device__ __forceinline__ bool pf_load_raw(const PfBars& br, uint32_t smem, con
 
 // TMA lane: per stage, the N B rows (pair order, starting at row0) as N / 16 boxes.
 __device__ __forceinline__ bool pf_load_b(const PfBars& br, uint32_t smem, const CUtensorMap* map,
-                                          uint32_t row0, uint32_t nk, uint32_t N, PfPos& b) {
+                                          uint32_t row0, uint32_t nk, uint32_t N, uint32_t g0) {
     for (uint32_t kc = 0; kc < nk; ++kc) {
-        if (!pf_wait(br.b_empty + b.slot, b.ph ^ 1u, br.abort, kPfSleepNs)) return false;
-        tc::mbar_arrive_expect_tx(br.b_full + b.slot, N * kPfKc * 2u);
-        const uint32_t dst = smem + b.slot * kPfBStage;
+        const uint32_t g = g0 + kc, bar = g % kPfRing;
+        if (!pf_wait_freed(br, (int64_t)g - kPfBStages, kPfSleepNs)) return false;
+        tc::mbar_arrive_expect_tx(br.full + bar, N * kPfKc * 2u);
+        const uint32_t dst = smem + (g % kPfBStages) * kPfBStage;
         for (uint32_t j = 0; j < N / kPfBoxRows; ++j)
             tc::tma_load_2d(dst + j * kPfBoxRows * 128u, map, (int32_t)(kc * kPfKc), (int32_t)(row0 + j * kPfBoxRows),
-                            br.b_full + b.slot);
-        b.next(kPfBStages);
+                            br.full + bar);
     }
     return true;
 }
 
-// MMA lane: per stage, 4 K-steps x 2 accumulators with A from TMEM and B from shared memory.
+// MMA lane: per stage, 4 K-steps x 2 accumulators with A from TMEM and B from shared memory, then
+// one commit that frees the stage's slots.
 __device__ __forceinline__ bool pf_mma(const PfBars& br, uint32_t smem, uint32_t tmem, uint32_t nk, uint32_t N,
-                                       PfPos& a, PfPos& b, bool& pending) {
+                                       uint32_t g0, bool& pending) {
     const uint32_t idesc = tc::idesc_f16(kPfM, N);
     for (uint32_t kc = 0; kc < nk; ++kc) {
-        if (!pf_wait(br.b_full + b.slot, b.ph, br.abort, kPfSleepNs)) return false;
-        if (!pf_wait(br.a_full + a.slot, a.ph, br.abort, kPfSleepNs)) return false;
+        const uint32_t g = g0 + kc, bar = g % kPfRing;
+        if (!pf_wait(br.full + bar, (g / kPfRing) & 1u, br.abort, kPfSleepNs)) return false;
         tc::fence_after_sync();
-        const uint32_t bs = smem + b.slot * kPfBStage;
-        const uint32_t ta = tmem + kPfACol + a.slot * 64u;
+        const uint32_t bs = smem + (g % kPfBStages) * kPfBStage;
+        const uint32_t ta = tmem + kPfACol + (g % kPfASlots) * 64u;
         pending = true;
 #pragma unroll
         for (uint32_t ks = 0; ks < kPfKc / 16u; ++ks) {
@@ -301,10 +362,7 @@ __device__ __forceinline__ bool pf_mma(const PfBars& br, uint32_t smem, uint32_t
             tc::mma_f16_ts(tmem, ta + ks * 8u, bd, idesc, accumulate);
             tc::mma_f16_ts(tmem + kPfAcc1Col, ta + 32u + ks * 8u, bd, idesc, accumulate);
         }
-        tc::mma_commit(br.a_empty + a.slot);
-        tc::mma_commit(br.b_empty + b.slot);
-        a.next(2);
-        b.next(kPfBStages);
+        tc::mma_commit(br.empty + bar);
     }
     tc::mma_commit(br.acc_full);
     pending = false;
@@ -426,26 +484,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(const __gri
     PfBars br;
     br.raw_full = bars;
     br.raw_empty = br.raw_full + kPfRawStages;
-    br.b_full = br.raw_empty + kPfRawStages;
-    br.b_empty = br.b_full + kPfBStages;
-    br.a_full = br.b_empty + kPfBStages;
-    br.a_empty = br.a_full + 2;
-    br.acc_full = br.a_empty + 2;
+    br.full = br.raw_empty + kPfRawStages;
+    br.empty = br.full + kPfRing;
+    br.acc_full = br.empty + kPfRing;
     br.abort = misc + 2;
     const CUtensorMap* bmap = GATEUP ? &p.bmap_x : &p.bmap_act;
     if (warp == kPfMmaWarp) tc::tmem_alloc(misc, kPfTmemCols);
     if (tid == 0) {
         for (uint32_t i = 0; i < kPfRawStages; ++i) {
             tc::mbar_init(br.raw_full + i, 1);
-            tc::mbar_init(br.raw_empty + i, kPfProducers);
+            tc::mbar_init(br.raw_empty + i, kPfProducerWarps);
         }
-        for (uint32_t i = 0; i < kPfBStages; ++i) {
-            tc::mbar_init(br.b_full + i, 1);
-            tc::mbar_init(br.b_empty + i, 1);
-        }
-        for (uint32_t i = 0; i < 2; ++i) {
-            tc::mbar_init(br.a_full + i, kPfProducers);
-            tc::mbar_init(br.a_empty + i, 1);
+        for (uint32_t i = 0; i < kPfRing; ++i) {
+            tc::mbar_init(br.full + i, kPfProducerWarps + 1);  // producer warps + the TMA lane
+            tc::mbar_init(br.empty + i, 1);
         }
         tc::mbar_init(br.acc_full, 1);
         misc[2] = 0;
@@ -468,7 +520,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(const __gri
     // lane is r (warp % 4 == r / 32), its A columns 16 * half of the accumulator's 32 per slot
     const uint32_t acc = tid >> 8, half = (tid >> 7) & 1u, r = tid & (kPfM - 1u);
     const uint32_t t_a = tmem + ((32u * (warp & 3u)) << 16) + kPfACol + acc * 32u + half * 16u;
-    PfPos raw{0, 0}, bp{0, 0}, ap{0, 0};
+    PfPos raw{0, 0};
+    uint32_t gs0 = 0, rs0 = 0;  // global stage / raw-stage numbers of the item's first
     uint32_t item_it = 0, pending_parity = 0;
     bool pending = false, copies_dirty = false;
     for (;;) {
@@ -496,10 +549,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(const __gri
         if (warp < kPfProducerWarps) {
             const float ps = (acc ? m1 : m0)->pscale;
             bool ok = type == kTypeQ8_0
-                          ? pf_produce<kTypeQ8_0>(br, smem, tab, ps, acc, half, r, t_a, nk, raw, ap)
-                          : pf_produce<kTypeIq2Xxs>(br, smem, tab, ps, acc, half, r, t_a, nk, raw, ap);
-            if (ok) ok = pf_wait(br.acc_full, item_it & 1u, br.abort, 0);
-            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is a whole-warp instruction
+                          ? pf_produce<kTypeQ8_0>(br, smem, tab, ps, acc, half, r, t_a, nk, gs0, rs0)
+                          : pf_produce<kTypeIq2Xxs>(br, smem, tab, ps, acc, half, r, t_a, nk, gs0, rs0);
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) ok = pf_wait_warp(br.acc_full, item_it & 1u, br.abort);
             if (ok) {
                 tc::fence_after_sync();
                 if (GATEUP)
@@ -519,14 +572,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(const __gri
         } else if (warp == kPfTmaWarp) {
             if (lane == 0) {
                 copies_dirty = true;
-                if (pf_load_b(br, smem, bmap, tile.pair_begin, nk, N, bp)) copies_dirty = false;
+                if (pf_load_b(br, smem, bmap, tile.pair_begin, nk, N, gs0)) copies_dirty = false;
                 else pf_fail(p.counters + 3, br.abort);
             }
         } else if (lane == 0) {
             pending_parity = item_it & 1u;
-            if (!pf_mma(br, smem, tmem, nk, N, ap, bp, pending)) pf_fail(p.counters + 3, br.abort);
+            if (!pf_mma(br, smem, tmem, nk, N, gs0, pending)) pf_fail(p.counters + 3, br.abort);
         }
         ++item_it;
+        gs0 += nk;
+        rs0 += type == kTypeQ8_0 ? nk : nk / 4u;
     }
     __syncthreads();
     if ((warp == kPfLoadWarp || warp == kPfTmaWarp) && lane == 0 && copies_dirty) {
