@@ -4,9 +4,12 @@ Workload (default): the DeepSeek-V4-Flash-shaped decode layer of the benchmark c
 (config 1): H=4096, 256 routed IQ2_XXS experts + 1 Q8_0 shared expert, top-8 learned routing
 (sqrt-softplus + bias, renormalised), I=2048, a decode batch of 64 tokens. A step is one layer
 forward over the batch: router projection, top-k, dispatch, gate/up + SwiGLU, down, combine.
-All inputs are seeded synthetic data with the configuration's distributions (no checkpoint).
+The same line carries a "prefill" object: configuration 3 (the same shapes, 4096 tokens,
+N(0,1) routing logits, mixed IQ2_XXS / Q8_0 experts) through the tensor-core prefill path, with
+its tensor roofline. All inputs are seeded synthetic data with the configurations'
+distributions (no checkpoint).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--tokens T]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--tokens T] [--no-prefill]
 
 --impl reference times the reference's own CPU implementation (the vastloom library compiled
 from its sources into oracle/_ref, driven by the restated layer loop) on the host cores.
@@ -37,11 +40,23 @@ FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
 
 
+FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_BF16_SUSTAINED_TFLOPS = 1400.0
+
+
 def load_peaks():
     if PEAKS_FILE.exists():
         p = json.loads(PEAKS_FILE.read_text())
         return float(p["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_tensor_peaks():
+    """(burst, sustained) dense bf16 TFLOP/s; fp16 operands run at the same tensor rate."""
+    if PEAKS_FILE.exists():
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    return FALLBACK_BF16_TFLOPS, FALLBACK_BF16_SUSTAINED_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -193,11 +208,12 @@ def run_ours(args, rank, world, local_rank):
     # end to end through the host-memory C-ABI call (H2D x, layer, D2H out, synchronise)
     e2e_times = []
     pinned_x = torch.from_numpy(x_host).pin_memory().numpy()
+    pinned_out = torch.empty((T, spec.hidden), dtype=torch.float32).pin_memory().numpy()
     for i in range(max(3, args.steps)):
         flush_l2()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        layer.forward(pinned_x)
+        layer.forward(pinned_x, out=pinned_out)
         e2e_times.append(time.perf_counter() - t0)
     e2e_value = T * world / statistics.mean(e2e_times)
 
@@ -216,7 +232,7 @@ def run_ours(args, rank, world, local_rank):
     hbm, peak_kind = load_peaks()
     dom = max(("gate_up", "down"), key=lambda p: phase_ms[p])
     achieved = pb[dom] / (phase_ms[dom] / 1000.0) / 1e9
-    kernel_name = {"gate_up": "expert_kernel<true>", "down": "expert_kernel<false>"}[dom]
+    kernel_name = {"gate_up": "expert_mma_kernel<true>", "down": "expert_mma_kernel<false>"}[dom]
     traffic = traffic_from_profiles(kernel_name)
     layer_bytes = pb["route"] + pb["gate_up"] + pb["down"] + pb["combine"]
     result = {
@@ -261,11 +277,131 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget)
     layer.destroy()
+    for lst in layer.matrices.values():
+        for m in lst:
+            dev.release_matrix(m)
+    for m in layer.shared_matrices or ():
+        dev.release_matrix(m)
+    if not args.no_prefill:
+        result["prefill"] = run_prefill(args, dev, stream, flush_l2, rank, world, local_rank)
     dev.close()
     return result
 
 
-def cpu_baseline(W, x, budget_s: float, threads: int | None = None):
+def run_prefill(args, dev, stream, flush_l2, rank, world, local_rank):
+    """Configuration 3 at 4096 tokens per GPU through the tensor-core prefill path."""
+    import torch
+
+    from vastloom_b200 import synth
+
+    spec = synth.config(3)
+    T = args.prefill_tokens
+    W = synth.layer_weights(spec, seed=3)
+    layer = synth.upload_layer(dev, W, max_tokens=T)
+    assert layer.prefill_tokens() <= T
+    x_host, _, logits_host = synth.activations(spec, T, seed=33 + rank)
+    with torch.cuda.stream(stream):
+        x_dev = torch.from_numpy(x_host).cuda()
+        lg_dev = torch.from_numpy(logits_host).cuda()
+        out_dev = torch.empty((T, spec.hidden), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        layer.forward_device(x_dev.data_ptr(), T, out_dev.data_ptr(), logits_ptr=lg_dev.data_ptr(), stream=dev.stream)
+
+    for _ in range(args.warmup):
+        flush_l2()
+        step()
+    torch.cuda.synchronize()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    steps = args.prefill_steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush_l2()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if dist:
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / steps
+    value = T * world * steps / (total_ms / 1000.0)
+    out = out_dev.cpu().numpy()
+    assert np.all(np.isfinite(out))
+    # end to end: host x and logits in, host output back, per call
+    pinned_x = torch.from_numpy(x_host).pin_memory().numpy()
+    pinned_l = torch.from_numpy(logits_host).pin_memory().numpy()
+    pinned_out = torch.empty((T, spec.hidden), dtype=torch.float32).pin_memory().numpy()
+    e2e = []
+    for _ in range(3):
+        flush_l2()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        layer.forward(pinned_x, None, pinned_l, out=pinned_out)
+        e2e.append(time.perf_counter() - t0)
+    e2e_value = T * world / statistics.mean(e2e)
+    layer.set_profiling(True)
+    phases = {p: [] for p in layer.PHASES}
+    for _ in range(steps):
+        flush_l2()
+        step()
+        for p, v in layer.phase_times().items():
+            phases[p].append(v)
+    layer.set_profiling(False)
+    phase_ms = {p: statistics.mean(v) for p, v in phases.items()}
+    pairs = T * spec.top_k + T  # routed pairs + the shared expert's
+    flops = {"gate_up": 2.0 * 2 * spec.hidden * spec.intermediate * pairs,
+             "down": 2.0 * spec.hidden * spec.intermediate * pairs}
+    burst, sustained, kind = load_tensor_peaks()
+    dom = max(flops, key=lambda p: phase_ms[p])
+    achieved = flops[dom] / (phase_ms[dom] / 1000.0) / 1e12
+    layer_tflops = (flops["gate_up"] + flops["down"]) / (ms_per_step / 1000.0) / 1e12
+    res = {
+        "value": round(value, 1), "unit": "tokens/s", "ms_per_step": round(ms_per_step, 4), "steps": steps,
+        "dtype": "fp16 operands, f32 accumulation (tensor cores); routing f32/f64",
+        "config": {"workload": f"cfg3-prefill-mixed-T{T}", "hidden": spec.hidden,
+                   "intermediate": spec.intermediate, "experts": spec.experts, "top_k": spec.top_k,
+                   "shared_experts": 1, "tokens_per_gpu": T, "routed_types": "IQ2_XXS / Q8_0 (seeded coin)",
+                   "shared_type": "Q8_0", "routing": "given N(0,1) logits, sqrt_softplus+bias, renorm",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "roofline": {"bound": "tensor", "kernel": f"prefill_gemm_kernel<{'true' if dom == 'gate_up' else 'false'}>",
+                     "achieved": round(achieved, 1), "peak": sustained, "unit": "TFLOP/s",
+                     "frac": round(achieved / sustained, 4), "peak_kind": f"{kind} sustained bf16 (fp16 same rate)",
+                     "frac_of_burst": round(achieved / burst, 4), "traffic": traffic_from_profiles("prefill_gemm_kernel"),
+                     "algorithmic_flops": flops[dom], "kernel_ms": round(phase_ms[dom], 5)},
+        "layer_tflops": round(layer_tflops, 1),
+        "phase_ms": {p: round(v, 5) for p, v in phase_ms.items()},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x_host.nbytes + logits_host.nbytes), "d2h_bytes_per_step": int(out.nbytes),
+                "timing": "host wall clock around the synchronous C-ABI call"},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget / 2, logits=logits_host)
+    layer.destroy()
+    for lst in layer.matrices.values():
+        for m in lst:
+            dev.release_matrix(m)
+    for m in layer.shared_matrices or ():
+        dev.release_matrix(m)
+    return res
+
+
+def cpu_baseline(W, x, budget_s: float, threads: int | None = None, logits=None):
     """The reference's own CPU path (oracle/_ref) on a bounded sample of the same batch."""
     from oracle.oracle import Reference
 
@@ -276,12 +412,13 @@ def cpu_baseline(W, x, budget_s: float, threads: int | None = None):
     cores = os.cpu_count() or 1
     # RowWorkPool has hardware_concurrency()/2 workers plus the caller (ggml_quantization.cpp:761)
     threads = threads or max(1, cores // 2 + 1)
+    lg = (lambda a, b: None) if logits is None else (lambda a, b: logits[a:b])
     t0 = time.perf_counter()
-    ref.moe_forward(W, x[:1], threads=threads)
+    ref.moe_forward(W, x[:1], None, lg(0, 1), threads=threads)
     t1 = time.perf_counter() - t0
     n = int(max(1, min(x.shape[0], budget_s / max(t1, 1e-6))))
     t0 = time.perf_counter()
-    ref.moe_forward(W, x[:n], threads=threads)
+    ref.moe_forward(W, x[:n], None, lg(0, n), threads=threads)
     dt = time.perf_counter() - t0
     return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
             "sample": f"first {n} of the {x.shape[0]} batch tokens through the reference's layer loop "
@@ -338,6 +475,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--ref-tokens-per-step", type=int, default=1)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the configuration-3 prefill object")
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--prefill-steps", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -483,11 +483,15 @@ class MoeLayer:
         self.ptr = p
 
     def forward(self, x: np.ndarray, token_ids: Optional[np.ndarray] = None,
-                logits: Optional[np.ndarray] = None) -> np.ndarray:
-        """Host-memory forward (H2D inputs, layer, D2H output) - the end-to-end call."""
+                logits: Optional[np.ndarray] = None, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Host-memory forward (H2D inputs, layer, D2H output) - the end-to-end call. `out`
+        (f32 [T, H], C-contiguous) may be supplied, e.g. page-locked, to receive the output."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         T = x.shape[0]
-        out = np.empty((T, self.H), dtype=np.float32)
+        if out is None:
+            out = np.empty((T, self.H), dtype=np.float32)
+        elif out.dtype != np.float32 or out.shape != (T, self.H) or not out.flags["C_CONTIGUOUS"]:
+            raise ValueError("out must be a C-contiguous float32 array of shape (T, hidden)")
         tok = None if token_ids is None else np.ascontiguousarray(token_ids, dtype=np.uint32)
         lg = None if logits is None else np.ascontiguousarray(logits, dtype=np.float32)
         self.dev._check(self.dev.lib.vlb_layer_forward(

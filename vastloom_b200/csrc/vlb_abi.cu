@@ -643,6 +643,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
                  o_xd = carve(T * H * 8), o_rp = carve(8 * T * E * 8);
     const uint32_t mpt = prefill_max_tiles((uint32_t)T, k, E);
     const size_t o_xh = carve(P * H * 2), o_acth = carve(P * I * 2), o_pt2 = carve((size_t)mpt * sizeof(Unit));
+    const size_t o_dc = carve(((T * k + 1023) / 1024) * E * 4);
     TRY(h->galloc(off, "vlb-layer-workspace", &L->ws));
     TRY(h->galloc(T * H * 4, "vlb-layer-x", (void**)&L->x_dev));
     TRY(h->galloc(T * 4, "vlb-layer-tokens", (void**)&L->tok_dev));
@@ -695,6 +696,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.act_h = reinterpret_cast<__half*>(ws + o_acth);
     p.ptiles = reinterpret_cast<Unit*>(ws + o_pt2);
     p.max_ptiles = mpt;
+    p.disp_counts = reinterpret_cast<uint32_t*>(ws + o_dc);
     if (!encode_rows_fp16(&p.bmap_x, p.xperm, P, H) || !encode_rows_fp16(&p.bmap_act, p.act_h, P, I)) {
         free_layer(h, L);
         return h->fail(VLB_ERR_INTERNAL_ERROR, "unable to encode the prefill TMA descriptors");

@@ -214,6 +214,7 @@ struct MoeParams {
     double* router_partial;  // [8 x T x E]: per-column-slice router partial sums
     uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
     uint32_t max_units;
+    uint32_t* disp_counts;   // [ceil(T*k / 1024) x E]: per-chunk expert counts of the multi-CTA dispatch
     // prefill (tensor-core grouped GEMM) path
     int prefill;             // 1: this forward runs the expert products on tcgen05 (fp16 operands)
     __half* xperm;           // [(T*k + T) x H]: pair p's token row, fp16(x * 2^e_t) (the token's xmax power of two)

@@ -376,6 +376,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
 // shared expert's T pairs are appended at [T*k, T*k + T). Builds the work units (<= kUnitTokens
 // pairs of one expert each, experts ascending, shared last) and each token's combine list.
 constexpr int kDispatchThreads = 1024;
+constexpr uint32_t kMaxExperts = 512;  // vlb_layer_create bound
 
 // Exclusive scan of v[0..n) in shared memory by warp 0 (n <= a few thousand); returns the total.
 __device__ __forceinline__ uint32_t warp0_exclusive_scan(uint32_t* v, uint32_t n, uint32_t* total) {
@@ -400,58 +401,49 @@ __device__ __forceinline__ uint32_t warp0_exclusive_scan(uint32_t* v, uint32_t n
     return *total;
 }
 
-__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p) {
-    extern __shared__ uint32_t dsm[];
-    const uint32_t E = p.E, k = p.k, T = p.T, n = T * k;
-    uint32_t* cnt = dsm;              // [E + 1]
-    uint32_t* off = cnt + E + 1;      // [E + 1] expert offsets (kept)
-    uint32_t* base = off + E + 1;     // [E + 1] running placement bases
-    uint32_t* wcnt = base + E + 1;    // [32 warps x E] per-warp counts of the current chunk
-    __shared__ uint32_t total_s;
+// Stable placement of elements [c0, c0 + blockDim.x) (element i = token * k + slot): each goes to
+// base[e] + (its rank among this chunk's elements of expert e, in element order), which is the
+// reference's visit order (expert ascending, then token, then slot). base[] advances past the
+// chunk. wcnt: [32 warps x E] shared scratch.
+__device__ __forceinline__ void dispatch_place_chunk(const MoeParams& p, uint32_t c0, uint32_t* base,
+                                                     uint32_t* wcnt) {
+    const uint32_t E = p.E, k = p.k, n = p.T * p.k;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    for (uint32_t e = tid; e <= E; e += blockDim.x) cnt[e] = 0;
+    const uint32_t i = c0 + tid;
+    const bool valid = i < n;
+    const uint32_t e = valid ? p.idx[i] : 0xffffffffu;
+    for (uint32_t q = tid; q < 32u * E; q += blockDim.x) wcnt[q] = 0;
     __syncthreads();
-    for (uint32_t i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[p.idx[i]], 1u);
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const uint32_t rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+    const uint32_t leader = __ffs(peers) - 1u;
+    if (valid && lane == leader) wcnt[warp * E + e] = __popc(peers);
     __syncthreads();
-    for (uint32_t e = tid; e <= E; e += blockDim.x) off[e] = cnt[e];
+    uint32_t before = 0;
+    if (valid) for (uint32_t w = 0; w < warp; ++w) before += wcnt[w * E + e];
     __syncthreads();
-    warp0_exclusive_scan(off, E + 1, &total_s);  // off[E] = n (cnt[E] = 0)
-    for (uint32_t e = tid; e <= E; e += blockDim.x) {
-        base[e] = off[e];
-        p.offsets[e] = off[e];
+    if (valid) {
+        const uint32_t pos = base[e] + before + rank_in_warp;
+        p.pair_token[pos] = i / k;
+        p.pair_slot[pos] = i % k;
+        p.pair_weight[pos] = p.weights[i];
+        p.combine_pairs[i] = pos;  // element -> pair position (reordered by the tail)
     }
-    if (tid == 0) p.offsets[E + 1] = n + (p.has_shared ? T : 0u);
     __syncthreads();
-    // stable placement, chunk by chunk in element order
-    for (uint32_t c0 = 0; c0 < n; c0 += blockDim.x) {
-        const uint32_t i = c0 + tid;
-        const bool valid = i < n;
-        const uint32_t e = valid ? p.idx[i] : 0xffffffffu;
-        for (uint32_t q = tid; q < 32u * E; q += blockDim.x) wcnt[q] = 0;
-        __syncthreads();
-        const uint32_t peers = __match_any_sync(0xffffffffu, e);
-        const uint32_t rank_in_warp = __popc(peers & ((1u << lane) - 1u));
-        const uint32_t leader = __ffs(peers) - 1u;
-        if (valid && lane == leader) wcnt[warp * E + e] = __popc(peers);
-        __syncthreads();
-        uint32_t before = 0;
-        if (valid) for (uint32_t w = 0; w < warp; ++w) before += wcnt[w * E + e];
-        __syncthreads();
-        if (valid) {
-            const uint32_t pos = base[e] + before + rank_in_warp;
-            p.pair_token[pos] = i / k;
-            p.pair_slot[pos] = i % k;
-            p.pair_weight[pos] = p.weights[i];
-            p.combine_pairs[i] = pos;  // element -> pair position (reordered below)
-        }
-        __syncthreads();
-        for (uint32_t ee = tid; ee < E; ee += blockDim.x) {
-            uint32_t s = 0;
-            for (uint32_t w = 0; w < kDispatchThreads / 32u; ++w) s += wcnt[w * E + ee];
-            base[ee] += s;
-        }
-        __syncthreads();
+    for (uint32_t ee = tid; ee < E; ee += blockDim.x) {
+        uint32_t sum = 0;
+        for (uint32_t w = 0; w < blockDim.x / 32u; ++w) sum += wcnt[w * E + ee];
+        base[ee] += sum;
     }
+    __syncthreads();
+}
+
+// After placement (off[0..E] = expert offsets in shared memory, nu: [E + 1] shared scratch):
+// per-pair act_max reset, the shared expert's pairs, each token's combine order, the work units
+// and the counters.
+__device__ __forceinline__ void dispatch_tail(const MoeParams& p, const uint32_t* off, uint32_t* nu,
+                                              uint32_t* total_s) {
+    const uint32_t E = p.E, k = p.k, T = p.T, n = T * k, tid = threadIdx.x;
     for (uint32_t i = tid; i < n + (p.has_shared ? T : 0u); i += blockDim.x) p.act_max[i] = 0u;
     if (p.has_shared)
         for (uint32_t t = tid; t < T; t += blockDim.x) {
@@ -474,7 +466,6 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p)
     // Work units: each expert's pairs split into <= kUnitTokens; the shared expert's units come
     // first (they are the heaviest: every token, usually the widest storage type), so dynamically
     // scheduled CTAs start on them and finish on light ones. Ordinal 0 = shared, e + 1 = expert e.
-    uint32_t* nu = base;  // reuse: units per ordinal, scanned to first unit index
     for (uint32_t o = tid; o <= E; o += blockDim.x) {
         uint32_t c = 0;
         if (o == 0) c = p.has_shared ? T : 0u;
@@ -482,7 +473,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p)
         nu[o] = (c + kUnitTokens - 1) / kUnitTokens;
     }
     __syncthreads();
-    const uint32_t n_units = warp0_exclusive_scan(nu, E + 1, &total_s);
+    const uint32_t n_units = warp0_exclusive_scan(nu, E + 1, total_s);
     for (uint32_t o = tid; o <= E; o += blockDim.x) {
         const uint32_t e = o == 0 ? E : o - 1u;
         const uint32_t b = o == 0 ? n : off[e];
@@ -501,6 +492,86 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p)
         for (uint32_t e = 0; e < E; ++e) na += off[e + 1] > off[e];
         p.counters[1] = na + (p.has_shared ? 1u : 0u);
     }
+}
+
+// Small batches: the whole dispatch in one CTA (chunks of blockDim.x elements in order).
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p) {
+    extern __shared__ uint32_t dsm[];
+    const uint32_t E = p.E, T = p.T, n = T * p.k;
+    uint32_t* cnt = dsm;              // [E + 1]
+    uint32_t* off = cnt + E + 1;      // [E + 1] expert offsets (kept)
+    uint32_t* base = off + E + 1;     // [E + 1] running placement bases
+    uint32_t* wcnt = base + E + 1;    // [32 warps x E] per-warp counts of the current chunk
+    __shared__ uint32_t total_s;
+    const uint32_t tid = threadIdx.x;
+    for (uint32_t e = tid; e <= E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (uint32_t i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[p.idx[i]], 1u);
+    __syncthreads();
+    for (uint32_t e = tid; e <= E; e += blockDim.x) off[e] = cnt[e];
+    __syncthreads();
+    warp0_exclusive_scan(off, E + 1, &total_s);  // off[E] = n (cnt[E] = 0)
+    for (uint32_t e = tid; e <= E; e += blockDim.x) {
+        base[e] = off[e];
+        p.offsets[e] = off[e];
+    }
+    if (tid == 0) p.offsets[E + 1] = n + (p.has_shared ? T : 0u);
+    __syncthreads();
+    for (uint32_t c0 = 0; c0 < n; c0 += blockDim.x) dispatch_place_chunk(p, c0, base, wcnt);
+    dispatch_tail(p, off, base, &total_s);
+}
+
+// Large batches, three launches. (1) per-chunk expert counts, counts[chunk * E + e].
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_count_kernel(MoeParams p, uint32_t* counts) {
+    __shared__ uint32_t cnt[kMaxExperts];
+    const uint32_t E = p.E, n = p.T * p.k, tid = threadIdx.x;
+    for (uint32_t e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const uint32_t i = blockIdx.x * blockDim.x + tid;
+    if (i < n) atomicAdd(&cnt[p.idx[i]], 1u);
+    __syncthreads();
+    for (uint32_t e = tid; e < E; e += blockDim.x) counts[(size_t)blockIdx.x * E + e] = cnt[e];
+}
+
+// (2) each chunk's base per expert = offset of the expert + the counts of earlier chunks, then the
+// chunk's stable placement; block 0 publishes the offsets.
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_scatter_kernel(MoeParams p, const uint32_t* counts) {
+    extern __shared__ uint32_t dsm[];
+    const uint32_t E = p.E, T = p.T, n = T * p.k, tid = threadIdx.x, chunks = gridDim.x;
+    uint32_t* off = dsm;              // [E + 1]
+    uint32_t* base = off + E + 1;     // [E + 1]
+    uint32_t* wcnt = base + E + 1;    // [32 warps x E]
+    __shared__ uint32_t total_s;
+    for (uint32_t e = tid; e <= E; e += blockDim.x) {
+        uint32_t tot = 0, before = 0;
+        if (e < E)
+            for (uint32_t b = 0; b < chunks; ++b) {
+                const uint32_t c = counts[(size_t)b * E + e];
+                tot += c;
+                before += b < blockIdx.x ? c : 0u;
+            }
+        off[e] = tot;
+        base[e] = before;
+    }
+    __syncthreads();
+    warp0_exclusive_scan(off, E + 1, &total_s);
+    for (uint32_t e = tid; e <= E; e += blockDim.x) {
+        base[e] += off[e];
+        if (blockIdx.x == 0) p.offsets[e] = off[e];
+    }
+    if (blockIdx.x == 0 && tid == 0) p.offsets[E + 1] = n + (p.has_shared ? T : 0u);
+    __syncthreads();
+    dispatch_place_chunk(p, blockIdx.x * blockDim.x, base, wcnt);
+}
+
+// (3) the tail, one CTA, from the published offsets.
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_finish_kernel(MoeParams p) {
+    __shared__ uint32_t off[kMaxExperts + 1];
+    __shared__ uint32_t nu[kMaxExperts + 1];
+    __shared__ uint32_t total_s;
+    for (uint32_t e = threadIdx.x; e <= p.E; e += blockDim.x) off[e] = p.offsets[e];
+    __syncthreads();
+    dispatch_tail(p, off, nu, &total_s);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1044,9 +1115,21 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
                      p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
     if (e != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[1], s);
-    const size_t dsmem = ((size_t)(p.E + 1) * 3 + 32u * p.E) * sizeof(uint32_t);
-    if ((e = set_smem_once(dispatch_kernel, dsmem)) != cudaSuccess) return e;
-    dispatch_kernel<<<1, kDispatchThreads, dsmem, s>>>(p);
+    const uint32_t n_el = p.T * p.k;
+    if (n_el <= 4u * kDispatchThreads || !p.disp_counts) {
+        const size_t dsmem = ((size_t)(p.E + 1) * 3 + 32u * p.E) * sizeof(uint32_t);
+        if ((e = set_smem_once(dispatch_kernel, dsmem)) != cudaSuccess) return e;
+        dispatch_kernel<<<1, kDispatchThreads, dsmem, s>>>(p);
+    } else {
+        const unsigned chunks = (n_el + kDispatchThreads - 1) / kDispatchThreads;
+        dispatch_count_kernel<<<chunks, kDispatchThreads, 0, s>>>(p, p.disp_counts);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        const size_t ssmem = ((size_t)(p.E + 1) * 2 + 32u * p.E) * sizeof(uint32_t);
+        if ((e = set_smem_once(dispatch_scatter_kernel, ssmem)) != cudaSuccess) return e;
+        dispatch_scatter_kernel<<<chunks, kDispatchThreads, ssmem, s>>>(p, p.disp_counts);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        dispatch_finish_kernel<<<1, kDispatchThreads, 0, s>>>(p);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[2], s);
     // experts
