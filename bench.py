@@ -6,8 +6,10 @@ Workload (default): the DeepSeek-V4-Flash-shaped decode layer of the benchmark c
 forward over the batch: router projection, top-k, dispatch, gate/up + SwiGLU, down, combine.
 The same line carries a "prefill" object: configuration 3 (the same shapes, 4096 tokens,
 N(0,1) routing logits, mixed IQ2_XXS / Q8_0 experts) through the tensor-core prefill path, with
-its tensor roofline. All inputs are seeded synthetic data with the configurations'
-distributions (no checkpoint).
+its tensor roofline; and an "expert_parallel" object: configuration 4 (8192 tokens per GPU with
+Zipf-skewed routing, the 256 experts sharded over the N GPUs, NCCL all-to-all exchange), whose
+per-N values are the expert-parallel scaling. All inputs are seeded synthetic data with the
+configurations' distributions (no checkpoint).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--tokens T] [--no-prefill]
 
@@ -151,6 +153,19 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = vb.Device(local_rank)
+    if args.only_prefill:
+        stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local_rank))
+        with torch.cuda.stream(stream):
+            flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+        def flush_only():
+            with torch.cuda.stream(stream):
+                flush.zero_()
+
+        res = {"metric": METRIC, "n_gpus": world, "prefill": run_prefill(args, dev, stream, flush_only, rank, world,
+                                                                        local_rank)}
+        dev.close()
+        return res
     spec = synth.config(1)
     T = args.tokens
     W = synth.layer_weights(spec, seed=1)
@@ -284,8 +299,85 @@ def run_ours(args, rank, world, local_rank):
         dev.release_matrix(m)
     if not args.no_prefill:
         result["prefill"] = run_prefill(args, dev, stream, flush_l2, rank, world, local_rank)
+    if not args.no_ep:
+        result["expert_parallel"] = run_ep(args, dev, rank, world, local_rank)
     dev.close()
     return result
+
+
+def run_ep(args, dev, rank, world, local_rank):
+    """Configuration 4: 256 experts sharded over the N ranks (N = 1: all local), args.ep_tokens
+    tokens per rank with Zipf(1.1)-skewed routing logits, all-to-all dispatch and return over
+    NCCL. Device-timed per step (CUDA events on the library stream around the whole step), max
+    over ranks; also the per-rank expert-phase time, whose spread is the load imbalance."""
+    import torch
+
+    from vastloom_b200 import synth
+    from vastloom_b200.ep import TorchComm, make_device_layer
+
+    spec = synth.config(4)
+    T = args.ep_tokens
+    W = synth.layer_weights(spec, seed=4)
+    x_host, _, logits_host = synth.activations(spec, T, seed=44 + rank)
+    created_group = False
+    if world == 1 and not torch.distributed.is_initialized():
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29500 + (os.getpid() % 1000)))
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+        created_group = True
+    comm = TorchComm()
+    layer, ops = make_device_layer(dev, W, comm, max_tokens=T)
+    xd = torch.from_numpy(x_host).cuda()
+    ld = torch.from_numpy(logits_host).cuda()
+    for _ in range(args.warmup):
+        layer.forward(xd, ld, T)
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    steps = args.ep_steps
+    times, experts_s = [], []
+    for _ in range(steps):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(ops.stream)
+        layer.forward(xd, ld, T)
+        end.record(ops.stream)
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+        experts_s.append(layer.last["experts_s"])
+    torch.distributed.barrier()
+    ms = statistics.mean(times)
+    ms_max = comm.max_over_ranks(ms, xd)
+    ex = statistics.mean(experts_s) * 1000.0
+    ex_max = comm.max_over_ranks(ex, xd)
+    ex_min = comm.min_over_ranks(ex, xd)
+    recv = layer.last["received_rows"]
+    recv_max = comm.max_over_ranks(float(recv), xd)
+    recv_min = comm.min_over_ranks(float(recv), xd)
+    out = layer.forward(xd, ld, T).cpu().numpy()
+    assert np.all(np.isfinite(out))
+    res = {
+        "value": round(T * world / (ms_max / 1000.0), 1), "unit": "tokens/s", "ms_per_step": round(ms_max, 4),
+        "steps": steps, "scaling": "weak", "n_gpus": world,
+        "config": {"workload": f"cfg4-ep-zipf-T{T}x{world}", "hidden": spec.hidden,
+                   "intermediate": spec.intermediate, "experts": spec.experts, "experts_per_gpu": spec.experts // world,
+                   "top_k": spec.top_k, "tokens_per_gpu": T, "zipf_s": spec.zipf_s,
+                   "exchange": "NCCL all-to-all (rows f32, expert ids, weights), results back",
+                   "expert_path": "tensor-core prefill kernels on the received rows"},
+        "timing": "CUDA events on the library stream around each step, max over ranks",
+        "load_imbalance": {"experts_ms_max": round(ex_max, 4), "experts_ms_min": round(ex_min, 4),
+                           "imbalance_ms": round(ex_max - ex_min, 4), "received_rows_max": int(recv_max),
+                           "received_rows_min": int(recv_min), "rows_per_rank_balanced": T * spec.top_k},
+        "phases_ms_rank0": {k_: round(v * 1000.0, 4) for k_, v in layer.last.items() if k_.endswith("_s")},
+    }
+    ops.close()
+    if created_group:
+        torch.distributed.destroy_process_group()
+    return res
 
 
 def run_prefill(args, dev, stream, flush_l2, rank, world, local_rank):
@@ -295,6 +387,9 @@ def run_prefill(args, dev, stream, flush_l2, rank, world, local_rank):
     from vastloom_b200 import synth
 
     spec = synth.config(3)
+    if args.prefill_experts != spec.experts:  # smaller case of the same kernels (profiling)
+        import dataclasses
+        spec = dataclasses.replace(spec, experts=args.prefill_experts)
     T = args.prefill_tokens
     W = synth.layer_weights(spec, seed=3)
     layer = synth.upload_layer(dev, W, max_tokens=T)
@@ -478,6 +573,12 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the configuration-3 prefill object")
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--prefill-experts", type=int, default=256,
+                    help="routed experts of the prefill case (smaller = a profiling-sized case)")
+    ap.add_argument("--only-prefill", action="store_true", help="run the prefill object alone")
+    ap.add_argument("--no-ep", action="store_true", help="skip the configuration-4 expert-parallel object")
+    ap.add_argument("--ep-tokens", type=int, default=8192)
+    ap.add_argument("--ep-steps", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -200,6 +200,41 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* layer, const float* x_host,
 int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* layer, uint32_t min_tokens);
 uint32_t vlb_layer_prefill_tokens(vlb_handle* h, vlb_layer* layer);
 
+/* Given-routes forward (an expert-parallel group): idx_dev u32 [T x k] expert ids of this layer
+ * (< experts), weights_dev f32 [T x k]; the router and top-k are skipped, everything else is the
+ * layer forward (dispatch, experts, combine; the shared expert if the layer has one). An id out of
+ * range is reported by vlb_layer_status (VLB_ERR_INVALID_FORMAT) and never indexes past the
+ * expert table. Enqueued on `stream`. */
+int vlb_layer_forward_routes_device(vlb_handle* h, vlb_layer* layer, const float* x_dev,
+                                    const uint32_t* idx_dev, const float* weights_dev, uint32_t T,
+                                    float* out_dev, void* stream);
+/* Synchronises `stream` and reports the error bits the layer's last device forward left (hash
+ * token id out of its table, out-of-range expert, unnormalisable weights, prefill pipeline
+ * timeout), as vlb_layer_forward does for the host form. */
+int vlb_layer_status(vlb_handle* h, vlb_layer* layer, void* stream);
+
+/* ---- expert parallelism (configuration 4: experts sharded over GPUs, all-to-all exchange) ----
+ * Plan on the source rank: the T*k (token, slot) elements of idx_dev (global expert ids < E) in the
+ * dispatch's stable order (expert ascending, then token, then slot) - with experts sharded in
+ * contiguous ranges of experts_per_rank that is also destination-rank order; send_x_dev f32
+ * [T*k x H] their x rows, send_expert_dev their expert id local to the owning rank
+ * (id % experts_per_rank), send_weight_dev their route weight, elem_row_dev [T*k] element
+ * (t * k + slot) -> send row, offsets_dev u32 [E + 2] device and offsets_host [E + 1] host copies
+ * of the per-expert starts. ws_dev: vlb_ep_workspace_bytes(T, k, E) bytes of device scratch.
+ * Synchronises `stream` (the host offsets size the exchange). */
+size_t vlb_ep_workspace_bytes(uint32_t T, uint32_t k, uint32_t E);
+int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx_dev, const float* weights_dev, uint32_t T,
+                       uint32_t k, uint32_t E, uint32_t experts_per_rank, const float* x_dev, uint32_t H,
+                       void* ws_dev,
+                       uint32_t* offsets_dev, uint32_t* offsets_host, float* send_x_dev,
+                       uint32_t* send_expert_dev, float* send_weight_dev, uint32_t* elem_row_dev,
+                       void* stream);
+/* Combine on the source rank after the return exchange: out[t] = sum over its k slots of
+ * y_rows_dev[elem_row_dev[t * k + slot]] (slot order) + shared_rows_dev[t] (NULL: none). */
+int vlb_ep_combine_device(vlb_handle* h, const float* y_rows_dev, const uint32_t* elem_row_dev,
+                          uint32_t T, uint32_t k, const float* shared_rows_dev, uint32_t H,
+                          float* out_dev, void* stream);
+
 /* Route of the last forward on this layer, for parity checks: idx / weights [T x k] in rank
  * order; offsets [E + 1]; pair_token / pair_slot [T x k] = the dispatch permutation (pairs
  * sorted by expert ascending, then token, then slot - the reference's visit order,

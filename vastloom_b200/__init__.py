@@ -136,7 +136,8 @@ EXPORTS = (
     "vlb_matrix_bytes vlb_matvec vlb_matvec_device vlb_dequantize_device vlb_layer_create "
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
     "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_layer_set_prefill_tokens "
-    "vlb_layer_prefill_tokens vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
+    "vlb_layer_prefill_tokens vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
+    "vlb_ep_plan_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
 ).split()
 
 
@@ -182,6 +183,11 @@ def load_library() -> C.CDLL:
         "vlb_layer_set_profiling": (I, [P, P, I]),
         "vlb_layer_phase_times": (I, [P, P, C.POINTER(C.c_float), I]),
         "vlb_layer_set_prefill_tokens": (I, [P, P, U32]),
+        "vlb_layer_forward_routes_device": (I, [P, P, P, P, P, U32, P, P]),
+        "vlb_layer_status": (I, [P, P, P]),
+        "vlb_ep_workspace_bytes": (SZ, [U32, U32, U32]),
+        "vlb_ep_plan_device": (I, [P, P, P, U32, U32, U32, U32, P, U32, P, P, P, P, P, P, P, P]),
+        "vlb_ep_combine_device": (I, [P, P, P, U32, U32, P, U32, P, P]),
         "vlb_layer_prefill_tokens": (U32, [P, P]),
         "vlb_route_device": (I, [P, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
         "vlb_route_device_noalloc": (I, [I, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
@@ -529,6 +535,17 @@ class MoeLayer:
 
     def last_weight_bytes(self) -> int:
         return int(self.dev.lib.vlb_layer_last_weight_bytes(self.dev.h, self.ptr))
+
+    def forward_routes_device(self, x_ptr: int, idx_ptr: int, w_ptr: int, T: int, out_ptr: int,
+                              stream: int = 0) -> None:
+        """Forward with given routes (device u32 ids [T x k], f32 weights): router and top-k skipped."""
+        self.dev._check(self.dev.lib.vlb_layer_forward_routes_device(
+            self.dev.h, self.ptr, C.c_void_p(x_ptr), C.c_void_p(idx_ptr), C.c_void_p(w_ptr), T,
+            C.c_void_p(out_ptr), C.c_void_p(stream or None)))
+
+    def status(self, stream: int = 0) -> None:
+        """Raises the error the last device forward flagged (synchronises `stream`)."""
+        self.dev._check(self.dev.lib.vlb_layer_status(self.dev.h, self.ptr, C.c_void_p(stream or None)))
 
     PREFILL_NEVER = 0xFFFFFFFF
 

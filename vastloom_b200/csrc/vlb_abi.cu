@@ -172,7 +172,7 @@ struct vlb_layer {
     float* out_dev = nullptr;
     // the forward captured as a CUDA graph for one input binding, replayed while it matches
     cudaGraphExec_t gexec = nullptr;
-    const void* gkey[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    const void* gkey[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     uint32_t gkey_T = 0;
     // optional phase timing (vlb_layer_set_profiling)
     bool profiling = false;
@@ -713,6 +713,16 @@ int vlb_layer_destroy(vlb_handle* h, vlb_layer* L) {
     return VLB_OK;
 }
 
+// Error bits a layer forward leaves in its counters (route, given routes, prefill pipeline).
+static int check_layer_flags(vlb_handle* h, uint32_t flags) {
+    if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
+    if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
+    if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
+    if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "a prefill pipeline wait ran out of time");
+    if (flags & 16u) return h->fail(VLB_ERR_INTERNAL_ERROR, "prefill shared memory is not 1 KB aligned");
+    return VLB_OK;
+}
+
 // Default prefill threshold: 16 pairs per routed expert on average, and never below 256 tokens.
 static uint32_t prefill_threshold(const vlb_layer* L) {
     if (L->prefill_min_tokens) return L->prefill_min_tokens;
@@ -727,7 +737,8 @@ static uint32_t prefill_threshold(const vlb_layer* L) {
 // leave the device idle between kernels. A stream that cannot be captured (the legacy default
 // stream) gets the same kernels launched directly.
 static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
-                          const float* logits, uint32_t T, float* out, cudaStream_t s) {
+                          const float* logits, uint32_t T, float* out, cudaStream_t s,
+                          const uint32_t* routes_idx = nullptr, const float* routes_w = nullptr) {
     if (T == 0 || T > L->desc.max_tokens)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "token count is zero or above the layer's max_tokens");
     if (L->desc.hash_routing && !tok)
@@ -737,6 +748,8 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.x = x;
     p.token_ids = tok;
     p.logits_in = logits;
+    p.routes_idx = routes_idx;
+    p.routes_w = routes_w;
     p.out = out;
     p.grids = h->grids();
     p.prefill = T >= prefill_threshold(L) ? 1 : 0;
@@ -748,9 +761,9 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
         VLB_CUDA(h, launch_moe(p, s, L->ev));
         return VLB_OK;
     }
-    const void* key[5] = {x, tok, logits, out, s};
+    const void* key[7] = {x, tok, logits, out, s, routes_idx, routes_w};
     bool same = L->gexec && L->gkey_T == T;
-    for (int i = 0; same && i < 5; ++i) same = L->gkey[i] == key[i];
+    for (int i = 0; same && i < 7; ++i) same = L->gkey[i] == key[i];
     if (!same) {
         if (L->gexec) {
             cudaGraphExecDestroy(L->gexec);
@@ -774,7 +787,7 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
             VLB_CUDA(h, launch_moe(p, s));
             return VLB_OK;
         }
-        for (int i = 0; i < 5; ++i) L->gkey[i] = key[i];
+        for (int i = 0; i < 7; ++i) L->gkey[i] = key[i];
         L->gkey_T = T;
     }
     VLB_CUDA(h, cudaGraphLaunch(L->gexec, s));
@@ -786,6 +799,23 @@ int vlb_layer_forward_device(vlb_handle* h, vlb_layer* L, const float* x, const 
     VLB_LOCK(h);
     if (!L || !x || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
     return forward_locked(h, L, x, tok, logits, T, out, h->pick(stream));
+}
+
+int vlb_layer_forward_routes_device(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* idx,
+                                    const float* weights, uint32_t T, float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!L || !x || !out || !idx || !weights) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
+    return forward_locked(h, L, x, nullptr, nullptr, T, out, h->pick(stream), idx, weights);
+}
+
+int vlb_layer_status(vlb_handle* h, vlb_layer* L, void* stream) {
+    VLB_LOCK(h);
+    if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
+    cudaStream_t s = h->pick(stream);
+    uint32_t flags = 0;
+    VLB_CUDA(h, cudaMemcpyAsync(&flags, L->p.counters + 3, 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    return check_layer_flags(h, flags);
 }
 
 int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
@@ -806,12 +836,7 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_
     uint32_t flags = 0;
     VLB_CUDA(h, cudaMemcpyAsync(&flags, L->p.counters + 3, 4, cudaMemcpyDeviceToHost, s));
     VLB_CUDA(h, cudaStreamSynchronize(s));
-    if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
-    if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "router selected an out-of-range expert");
-    if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
-    if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "a prefill pipeline wait ran out of time");
-    if (flags & 16u) return h->fail(VLB_ERR_INTERNAL_ERROR, "prefill shared memory is not 1 KB aligned");
-    return VLB_OK;
+    return check_layer_flags(h, flags);
 }
 
 int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* L, uint32_t min_tokens) {
@@ -946,6 +971,67 @@ int vlb_rms_norm_device(vlb_handle* h, const float* x, const float* w, uint32_t 
     if (!x || !w || !out || rows == 0 || width == 0 || !(eps > 0.f))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid RMSNorm argument");
     VLB_CUDA(h, launch_rms_norm(x, w, rows, width, eps, out, h->pick(stream)));
+    return VLB_OK;
+}
+
+// ---- expert parallelism (configuration 4) ------------------------------------------------------
+
+size_t vlb_ep_workspace_bytes(uint32_t T, uint32_t k, uint32_t E) {
+    const size_t n = (size_t)T * k, chunks = (n + 1023) / 1024;
+    return 256 + 2 * ((n * 4 + 255) / 256 * 256) + (chunks * E * 4 + 255) / 256 * 256;
+}
+
+int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx, const float* weights, uint32_t T, uint32_t k,
+                       uint32_t E, uint32_t experts_per_rank, const float* x, uint32_t H, void* ws, uint32_t* offsets,
+                       uint32_t* offsets_host, float* send_x, uint32_t* send_expert, float* send_weight,
+                       uint32_t* elem_row, void* stream) {
+    VLB_LOCK(h);
+    if (!idx || !weights || !x || !ws || !offsets || !offsets_host || !send_x || !send_expert || !send_weight ||
+        !elem_row || k == 0 || E == 0 || E > 512 || H == 0 || H % 4 || experts_per_rank == 0 ||
+        E % experts_per_rank)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid expert-parallel plan argument");
+    cudaStream_t s = h->pick(stream);
+    const size_t n = (size_t)T * k;
+    char* w = static_cast<char*>(ws);
+    uint32_t* flag = reinterpret_cast<uint32_t*>(w);
+    uint32_t* pair_token = reinterpret_cast<uint32_t*>(w + 256);
+    uint32_t* pair_slot = reinterpret_cast<uint32_t*>(w + 256 + (n * 4 + 255) / 256 * 256);
+    uint32_t* counts = reinterpret_cast<uint32_t*>(w + 256 + 2 * ((n * 4 + 255) / 256 * 256));
+    // expert ids are validated before the counting sort indexes anything with them
+    uint32_t bad = 0;
+    VLB_CUDA(h, cudaMemsetAsync(flag, 0, 4, s));
+    VLB_CUDA(h, launch_ep_validate(idx, n, E, flag, s));
+    VLB_CUDA(h, cudaMemcpyAsync(&bad, flag, 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    if (bad) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
+    MoeParams p{};
+    p.T = T;
+    p.k = k;
+    p.E = E;
+    p.idx = const_cast<uint32_t*>(idx);
+    p.weights = const_cast<float*>(weights);
+    p.offsets = offsets;
+    p.pair_token = pair_token;
+    p.pair_slot = pair_slot;
+    p.pair_weight = send_weight;
+    p.combine_pairs = elem_row;
+    p.disp_counts = counts;
+    p.has_shared = 0;
+    VLB_CUDA(h, launch_stable_sort(p, s));
+    VLB_CUDA(h, launch_ep_gather(pair_token, pair_slot, idx, (uint32_t)n, k, experts_per_rank, x, H, send_x,
+                                 send_expert, s));
+    if (n == 0) VLB_CUDA(h, cudaMemsetAsync(offsets, 0, (E + 2) * 4, s));
+    VLB_CUDA(h, cudaMemcpyAsync(offsets_host, offsets, (E + 1) * 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    return VLB_OK;
+}
+
+int vlb_ep_combine_device(vlb_handle* h, const float* y_rows, const uint32_t* elem_row, uint32_t T, uint32_t k,
+                          const float* shared_rows, uint32_t H, float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!y_rows || !elem_row || !out || H == 0 || H % 4)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid expert-parallel combine argument");
+    VLB_CUDA(h, launch_ep_combine(y_rows, elem_row, T, k, shared_rows, H, out, h->pick(stream)));
     return VLB_OK;
 }
 

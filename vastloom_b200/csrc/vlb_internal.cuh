@@ -193,6 +193,8 @@ struct MoeParams {
     const float* x;          // [T x H]
     const uint32_t* token_ids;
     const float* logits_in;  // optional [T x E]
+    const uint32_t* routes_idx;  // optional [T x k]: given routes (skip the router and top-k)
+    const float* routes_w;       // [T x k] their weights
     // workspace
     float* logits;           // [T x E]
     float* scores;           // [T x E]

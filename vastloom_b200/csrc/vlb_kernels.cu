@@ -494,6 +494,23 @@ __device__ __forceinline__ void dispatch_tail(const MoeParams& p, const uint32_t
     }
 }
 
+// Given routes (expert-parallel groups): copies them into the layer's route arrays; an expert id
+// out of range is flagged (bit 2, "route selects an out-of-range expert") and replaced by 0 so
+// that nothing downstream indexes past the expert table.
+__global__ void routes_copy_kernel(const uint32_t* __restrict__ idx, const float* __restrict__ w, size_t n,
+                                   uint32_t E, uint32_t* __restrict__ idx_out, float* __restrict__ w_out,
+                                   uint32_t* flags) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t e = idx[i];
+    if (e >= E) {
+        atomicOr(flags, 2u);
+        e = 0;
+    }
+    idx_out[i] = e;
+    w_out[i] = w[i];
+}
+
 // Small batches: the whole dispatch in one CTA (chunks of blockDim.x elements in order).
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p) {
     extern __shared__ uint32_t dsm[];
@@ -1101,18 +1118,26 @@ cudaError_t launch_route(const float* scores, const float* bias, const uint32_t*
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     cudaError_t e;
     if (ev) cudaEventRecord(ev[0], s);
-    // routing: router projection (or supplied logits) -> scores -> top-k
+    // routing: router projection (or supplied logits) -> scores -> top-k; or given routes
+    const bool given = p.routes_idx != nullptr;
     token_prescale_kernel<<<dim3((p.H + 1023) / 1024, p.T), 256, 0, s>>>(
-        p.x, p.T, p.H, p.xmax, p.logits_in ? nullptr : p.xd);
+        p.x, p.T, p.H, p.xmax, (p.logits_in || given) ? nullptr : p.xd);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (p.logits_in) {
-        e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
+    if (given) {
+        const size_t n = (size_t)p.T * p.k;
+        routes_copy_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p.routes_idx, p.routes_w, n, p.E, p.idx,
+                                                                       p.weights, p.counters + 3);
+        e = cudaGetLastError();
     } else {
-        e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, p.router_partial, s);
+        if (p.logits_in) {
+            e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
+        } else {
+            e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, p.router_partial, s);
+        }
+        if (e != cudaSuccess) return e;
+        e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
+                         p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
     }
-    if (e != cudaSuccess) return e;
-    e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
-                     p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
     if (e != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[1], s);
     const uint32_t n_el = p.T * p.k;
@@ -1169,6 +1194,22 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[5], s);
     return cudaSuccess;
+}
+
+// Stable placement of p.idx's T*k elements by expert (offsets, pair_token / pair_slot /
+// pair_weight, combine_pairs = element -> position) without the layer tail: count + scatter.
+// p.idx must hold ids < p.E. p.disp_counts: [ceil(T*k / 1024) x E].
+cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s) {
+    const uint32_t n_el = p.T * p.k;
+    if (n_el == 0) return cudaSuccess;
+    const unsigned chunks = (n_el + kDispatchThreads - 1) / kDispatchThreads;
+    dispatch_count_kernel<<<chunks, kDispatchThreads, 0, s>>>(p, p.disp_counts);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t ssmem = ((size_t)(p.E + 1) * 2 + 32u * p.E) * sizeof(uint32_t);
+    if ((e = set_smem_once(dispatch_scatter_kernel, ssmem)) != cudaSuccess) return e;
+    dispatch_scatter_kernel<<<chunks, kDispatchThreads, ssmem, s>>>(p, p.disp_counts);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,

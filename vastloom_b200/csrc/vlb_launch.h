@@ -36,6 +36,14 @@ uint32_t prefill_box_rows();  // rows of the B operand's TMA box
 cudaError_t launch_prefill_plan(const MoeParams& p, cudaStream_t s);
 cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_t s);
 cudaError_t launch_prefill_down(const MoeParams& p, unsigned grid, cudaStream_t s);
+cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s);
+// Expert-parallel helpers (vlb_ep.cu)
+cudaError_t launch_ep_validate(const uint32_t* idx, size_t n, uint32_t E, uint32_t* flag, cudaStream_t s);
+cudaError_t launch_ep_gather(const uint32_t* pair_token, const uint32_t* pair_slot, const uint32_t* idx,
+                             uint32_t n, uint32_t k, uint32_t epr, const float* x, uint32_t H, float* send_x,
+                             uint32_t* send_expert, cudaStream_t s);
+cudaError_t launch_ep_combine(const float* y, const uint32_t* elem_row, uint32_t T, uint32_t k,
+                              const float* shared_rows, uint32_t H, float* out, cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
                             float eps, float* out, cudaStream_t s);
 

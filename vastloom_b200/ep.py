@@ -1,0 +1,286 @@
+"""Expert parallelism for the MoE layer (benchmark configuration 4): the routed experts are
+sharded in contiguous ranges over the ranks of a process group, every rank routes its own tokens,
+sends each (token, slot) pair's activation row to the rank that owns the expert (all-to-all),
+computes the pairs it received on its expert shard, and sends the results back for the combine.
+
+The layer math is the reference's (moe_forward, deepseek_v4_graph.cpp:1902-2274): route weights
+are applied before the down product, each token's pairs are summed and the shared expert's row is
+added. The shared expert is replicated: every rank computes it for its own tokens, as one more
+expert of its local group (weight 1).
+
+    rank r:  route (own logits) -> plan (stable order by expert = by owner rank, x rows gathered)
+             -> all-to-all counts, rows, expert ids, weights
+             -> group forward over [received rows ; own tokens for the shared expert]
+             -> all-to-all results back -> combine
+
+The orchestration is written once against two small interfaces: `ops` (the compute steps; the
+device implementation, DeviceEpOps, calls the vlb200 C ABI) and `comm` (the exchange;
+TorchComm wraps torch.distributed, NCCL on GPUs, gloo on CPU tensors).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import time
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+
+def owner_counts(offsets_host: np.ndarray, world: int, experts_per_rank: int) -> list:
+    """Pairs destined to each rank from the per-expert starts of a plan (expert-sorted order)."""
+    return [int(offsets_host[(r + 1) * experts_per_rank]) - int(offsets_host[r * experts_per_rank])
+            for r in range(world)]
+
+
+class TorchComm:
+    """All-to-all exchange through torch.distributed (NCCL for CUDA tensors, gloo for CPU)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def exchange_counts(self, send_counts: list, like) -> list:
+        import torch
+
+        s = torch.tensor(send_counts, dtype=torch.int64, device=like.device)
+        r = torch.empty_like(s)
+        self.dist.all_to_all_single(r, s, group=self.group)
+        return [int(v) for v in r.cpu().tolist()]
+
+    def all_to_all(self, out, inp, out_splits: list, in_splits: list) -> None:
+        self.dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def max_over_ranks(self, v: float, like) -> float:
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device=like.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group)
+        return float(t.item())
+
+    def min_over_ranks(self, v: float, like) -> float:
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device=like.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN, group=self.group)
+        return float(t.item())
+
+
+@dataclass
+class EpBuffers:
+    send_x: object
+    send_expert: object
+    send_w: object
+    elem_row: object
+    group_x: object
+    group_idx: object
+    group_w: object
+    group_y: object
+    back_y: object
+    out: object
+
+
+class ExpertParallelLayer:
+    """One rank's share of an expert-parallel MoE layer. `ops` provides route / plan / group
+    forward / combine on this rank's device (or host, for the CPU tests); `comm` the exchange."""
+
+    def __init__(self, ops, comm, experts: int, top_k: int, hidden: int, max_tokens: int):
+        if experts % comm.world:
+            raise ValueError("experts must divide evenly over the ranks")
+        self.ops = ops
+        self.comm = comm
+        self.E = experts
+        self.k = top_k
+        self.H = hidden
+        self.epr = experts // comm.world
+        self.max_tokens = max_tokens
+        n = max_tokens * top_k
+        self.buf = EpBuffers(
+            send_x=ops.empty((n, hidden), "f32"), send_expert=ops.empty((n,), "i32"),
+            send_w=ops.empty((n,), "f32"), elem_row=ops.empty((n,), "i32"),
+            group_x=None, group_idx=None, group_w=None, group_y=None,
+            back_y=ops.empty((n, hidden), "f32"), out=ops.empty((max_tokens, hidden), "f32"))
+        self.capacity = 0  # group rows the receive side is sized for (grown on demand)
+        self.last = {}
+
+    def _reserve(self, rows: int) -> None:
+        """Receive-side buffers for `rows` group rows (received pairs + own shared rows). The worst
+        case (every rank's pairs on this rank) is world x the balanced load, so capacity follows
+        the observed load with headroom instead."""
+        if rows <= self.capacity:
+            return
+        cap = int(rows * 1.25) + 16
+        b, ops = self.buf, self.ops
+        b.group_x = ops.empty((cap, self.H), "f32")
+        b.group_idx = ops.empty((cap,), "i32")
+        b.group_w = ops.empty((cap,), "f32")
+        b.group_y = ops.empty((cap, self.H), "f32")
+        ops.reserve_group(cap)
+        self.capacity = cap
+
+    def forward(self, x, logits, T: int):
+        """x [T, H] f32 and logits [T, E] f32 of this rank's tokens (in the ops' memory); returns
+        out [T, H]. Records the phase times of this rank in self.last."""
+        if T > self.max_tokens:
+            raise ValueError("more tokens than the layer was sized for")
+        ops, comm, b, k = self.ops, self.comm, self.buf, self.k
+        n = T * k
+        t0 = time.perf_counter()
+        idx, w = ops.route(logits, T)
+        offsets = ops.plan(idx, w, x, T, self.epr, b)
+        send_counts = owner_counts(offsets, comm.world, self.epr)
+        recv_counts = comm.exchange_counts(send_counts, b.send_x)
+        R = sum(recv_counts)
+        self._reserve(R + T)
+        t1 = ops.sync_time()
+        comm.all_to_all(b.group_x[:R], b.send_x[:n], recv_counts, send_counts)
+        comm.all_to_all(b.group_idx[:R], b.send_expert[:n], recv_counts, send_counts)
+        comm.all_to_all(b.group_w[:R], b.send_w[:n], recv_counts, send_counts)
+        ops.append_shared_rows(b, R, x, T, self.epr)
+        t2 = ops.sync_time()
+        ops.group_forward(b, R + T)
+        t3 = ops.sync_time()
+        comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts)
+        t4 = ops.sync_time()
+        out = ops.combine(b, T, k, R)
+        t5 = ops.sync_time()
+        self.last = {"plan_s": t1 - t0, "dispatch_s": t2 - t1, "experts_s": t3 - t2, "return_s": t4 - t3,
+                     "combine_s": t5 - t4, "received_rows": R, "sent_rows": n}
+        return out
+
+
+class DeviceEpOps:
+    """The compute steps on this rank's GPU through the vlb200 C ABI (buffers are torch CUDA
+    tensors on the handle's stream). The local group layer holds the rank's routed experts plus
+    the shared expert as local expert `experts_per_rank`."""
+
+    def __init__(self, dev, group_mats, spec, bias, score: int, route_scale: float, experts: int, top_k: int,
+                 hidden: int, max_tokens: int):
+        import torch
+
+        self.torch = torch
+        self.dev = dev
+        self.lib = dev.lib
+        self.group_mats = group_mats
+        self.spec = spec
+        self.group = None
+        self.score = score
+        self.route_scale = route_scale
+        self.E = experts
+        self.k = top_k
+        self.H = hidden
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.stream = torch.cuda.ExternalStream(dev.stream, device=self.device)
+        self.bias = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias, np.float32)).to(self.device)
+        n = max_tokens * top_k
+        self.idx = torch.empty((n,), dtype=torch.int32, device=self.device)
+        self.w = torch.empty((n,), dtype=torch.float32, device=self.device)
+        self.offsets = torch.empty((experts + 2,), dtype=torch.int32, device=self.device)
+        self.offsets_host = np.zeros(experts + 1, np.uint32)
+        self.ws = torch.empty((int(self.lib.vlb_ep_workspace_bytes(max_tokens, top_k, experts)),),
+                              dtype=torch.uint8, device=self.device)
+
+    def reserve_group(self, rows: int) -> None:
+        """(Re)creates the local group layer with a workspace for `rows` given-route rows."""
+        from . import MoeLayer
+
+        if self.group is not None:
+            self.group.destroy()
+        m = self.group_mats
+        spec = self.spec
+        e_local = len(m["w1"])
+        self.group = MoeLayer(self.dev, hidden=spec.hidden, intermediate=spec.intermediate, experts=e_local,
+                              top_k=1, router=np.zeros((e_local, spec.hidden), np.float32), w1=m["w1"],
+                              w3=m["w3"], w2=m["w2"], score=spec.score, bias=None, route_scale=1.0,
+                              weight_after_down=spec.weight_after_down, shared=None, max_tokens=rows)
+
+    def close(self) -> None:
+        if self.group is not None:
+            self.group.destroy()
+            self.group = None
+        for lst in self.group_mats.values():
+            for mtx in lst:
+                self.dev.release_matrix(mtx)
+
+    def empty(self, shape, kind):
+        dt = {"f32": self.torch.float32, "i32": self.torch.int32}[kind]
+        return self.torch.empty(shape, dtype=dt, device=self.device)
+
+    @staticmethod
+    def _p(t):
+        return C.c_void_p(t.data_ptr())
+
+    def sync_time(self) -> float:
+        self.torch.cuda.current_stream(self.device).synchronize()
+        self.stream.synchronize()
+        return time.perf_counter()
+
+    def route(self, logits, T):
+        self.dev._check(self.lib.vlb_route_device(
+            self.dev.h, self.score, 0, self._p(logits), None if self.bias is None else self._p(self.bias), None, None,
+            0, T, self.E, self.k, self.route_scale, self._p(self.idx), self._p(self.w), C.c_void_p(self.dev.stream)))
+        return self.idx, self.w
+
+    def plan(self, idx, w, x, T, epr, b):
+        self.dev._check(self.lib.vlb_ep_plan_device(
+            self.dev.h, self._p(idx), self._p(w), T, self.k, self.E, epr, self._p(x), self.H, self._p(self.ws),
+            self._p(self.offsets), self.offsets_host.ctypes.data_as(C.c_void_p), self._p(b.send_x),
+            self._p(b.send_expert), self._p(b.send_w), self._p(b.elem_row), C.c_void_p(self.dev.stream)))
+        return self.offsets_host
+
+    def append_shared_rows(self, b, R, x, T, epr):
+        with self.torch.cuda.stream(self.stream):
+            b.group_x[R:R + T].copy_(x[:T])
+            b.group_idx[R:R + T].fill_(epr)
+            b.group_w[R:R + T].fill_(1.0)
+
+    def group_forward(self, b, rows):
+        # the collectives ran on torch's stream; the library's stream must see their results
+        self.torch.cuda.current_stream(self.device).synchronize()
+        self.group.forward_routes_device(b.group_x.data_ptr(), b.group_idx.data_ptr(), b.group_w.data_ptr(), rows,
+                                         b.group_y.data_ptr(), stream=self.dev.stream)
+        self.group.status(stream=self.dev.stream)
+
+    def combine(self, b, T, k, R):
+        self.dev._check(self.lib.vlb_ep_combine_device(
+            self.dev.h, self._p(b.back_y), self._p(b.elem_row), T, k, self._p(b.group_y[R:R + T]), self.H,
+            self._p(b.out), C.c_void_p(self.dev.stream)))
+        return b.out[:T]
+
+
+def upload_group(dev, W, rank: int, world: int, layer_index: int = 0) -> dict:
+    """This rank's expert group matrices: routed experts [rank * E/world, (rank + 1) * E/world)
+    plus the shared expert as local expert E/world (w1 / w3 / w2 lists)."""
+    spec = W.spec
+    E, H, I = spec.experts, spec.hidden, spec.intermediate
+    epr = E // world
+    lo = rank * epr
+
+    def ident(e, role):
+        return ((layer_index * 1_000_003 + e) * 4 + role) * 2 + 1
+
+    mats = {"w1": [], "w3": [], "w2": []}
+    for e in range(lo, lo + epr):
+        for role, (name, rows, cols) in enumerate((("w1", I, H), ("w3", I, H), ("w2", H, I))):
+            t, blob = getattr(W, name)[e]
+            mats[name].append(dev.upload_matrix(t, rows, cols, blob, identity=ident(e, role)))
+    if W.shared is None:
+        raise ValueError("the expert-parallel layer expects a shared expert")
+    for role, ((t, blob), (rows, cols), name) in enumerate(zip(W.shared, ((I, H), (I, H), (H, I)), ("w1", "w3", "w2"))):
+        mats[name].append(dev.upload_matrix(t, rows, cols, blob, identity=ident(E, role)))
+    return mats
+
+
+def make_device_layer(dev, W, comm, max_tokens: int):
+    """The expert-parallel layer of this rank on device `dev` (weights W of the whole layer; only
+    this rank's shard and the shared expert are uploaded)."""
+    spec = W.spec
+    mats = upload_group(dev, W, comm.rank, comm.world)
+    ops = DeviceEpOps(dev, mats, spec, W.bias, spec.score, spec.route_scale, spec.experts, spec.top_k,
+                      spec.hidden, max_tokens)
+    return ExpertParallelLayer(ops, comm, spec.experts, spec.top_k, spec.hidden, max_tokens), ops
