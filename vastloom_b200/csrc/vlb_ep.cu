@@ -30,30 +30,32 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const uint32_t* __restri
     for (uint32_t c = threadIdx.x; c < H / 4u; c += blockDim.x) dst[c] = src[c];
 }
 
-// out[t] = sum over slots of y[elem_row[t * k + slot]] (slot order), + shared[t].
+// out[t] = sum over slots of y[elem_row[t * k + slot]] (slot order), + shared[t]; rows strided over
+// gridDim.y (limited to 65535).
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ y,
-                                                         const uint32_t* __restrict__ elem_row, uint32_t k,
+                                                         const uint32_t* __restrict__ elem_row, uint32_t T, uint32_t k,
                                                          const float* __restrict__ shared, uint32_t H,
                                                          float* __restrict__ out) {
-    const uint32_t t = blockIdx.y;
     const uint32_t c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     if (c4 >= H) return;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (uint32_t j = 0; j < k; ++j) {
-        const float4 v = *reinterpret_cast<const float4*>(y + (size_t)elem_row[(size_t)t * k + j] * H + c4);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    for (uint32_t t = blockIdx.y; t < T; t += gridDim.y) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t j = 0; j < k; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)elem_row[(size_t)t * k + j] * H + c4);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        if (shared) {
+            const float4 v = *reinterpret_cast<const float4*>(shared + (size_t)t * H + c4);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(out + (size_t)t * H + c4) = acc;
     }
-    if (shared) {
-        const float4 v = *reinterpret_cast<const float4*>(shared + (size_t)t * H + c4);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-    }
-    *reinterpret_cast<float4*>(out + (size_t)t * H + c4) = acc;
 }
 
 }  // namespace
@@ -75,7 +77,8 @@ cudaError_t launch_ep_gather(const uint32_t* pair_token, const uint32_t* pair_sl
 cudaError_t launch_ep_combine(const float* y, const uint32_t* elem_row, uint32_t T, uint32_t k,
                               const float* shared_rows, uint32_t H, float* out, cudaStream_t s) {
     if (T == 0) return cudaSuccess;
-    ep_combine_kernel<<<dim3((H / 4 + 255) / 256, T), 256, 0, s>>>(y, elem_row, k, shared_rows, H, out);
+    ep_combine_kernel<<<dim3((H / 4 + 255) / 256, T < 65535u ? T : 65535u), 256, 0, s>>>(y, elem_row, T, k,
+                                                                                       shared_rows, H, out);
     return cudaGetLastError();
 }
 

@@ -747,24 +747,26 @@ constexpr uint32_t kMmaChunk = 4;                        // max items per work-s
 __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __restrict__ x, uint32_t T,
                                                              uint32_t H, uint32_t* __restrict__ xmax,
                                                              double* __restrict__ xd) {
-    // grid (ceil(H / 1024), T): each thread takes 4 columns of one token; the token's max|x|
-    // (for the tensor-core activation prescale) is an atomic max over float bits (non-negative
-    // floats order as integers), and the row is widened to f64 for the router projection
-    const uint32_t t = blockIdx.y;
+    // grid (ceil(H / 1024), min(T, 65535)), rows strided over gridDim.y: each thread takes 4 columns
+    // of one token; the token's max|x| (for the tensor-core activation prescale) is an atomic max
+    // over float bits (non-negative floats order as integers), and the row is widened to f64 for
+    // the router projection
     const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
-    float m = 0.f;
-    if (c < H) {
-        const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
-        m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        if (xd) {
-            double* o = xd + (size_t)t * H + c;
-            *reinterpret_cast<double2*>(o) = make_double2(v.x, v.y);
-            *reinterpret_cast<double2*>(o + 2) = make_double2(v.z, v.w);
+    for (uint32_t t = blockIdx.y; t < T; t += gridDim.y) {
+        float m = 0.f;
+        if (c < H) {
+            const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
+            m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+            if (xd) {
+                double* o = xd + (size_t)t * H + c;
+                *reinterpret_cast<double2*>(o) = make_double2(v.x, v.y);
+                *reinterpret_cast<double2*>(o + 2) = make_double2(v.z, v.w);
+            }
         }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31u) == 0 && m > 0.f) atomicMax(xmax + t, __float_as_uint(m));
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((threadIdx.x & 31u) == 0 && m > 0.f) atomicMax(xmax + t, __float_as_uint(m));
+    }
 }
 
 // CTA shape: rg_count row groups x (8 / rg_count) column splits. A warp owns one 16-row tile of
@@ -944,35 +946,36 @@ static uint32_t pick_row_groups(uint32_t T, uint32_t k, uint32_t E, uint32_t row
 // ---------------------------------------------------------------------------------------------
 // Combine (deepseek_v4_graph.cpp:2214-2227, :2263-2266; olmoe_runtime.cpp:1282-1285).
 __global__ void __launch_bounds__(256) combine_kernel(MoeParams p) {
-    const uint32_t t = blockIdx.y;
     const uint32_t c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     if (c4 >= p.H) return;
-    const uint32_t* cp = p.combine_pairs + (size_t)t * p.k;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (uint32_t j = 0; j < p.k; ++j) {
-        const uint32_t pair = cp[j];
-        const float4 v = *reinterpret_cast<const float4*>(p.y + (size_t)pair * p.H + c4);
-        if (p.weight_after_down) {
-            const float w = p.pair_weight[pair];
-            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
-            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
-            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
-            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
-        } else {
+    for (uint32_t t = blockIdx.y; t < p.T; t += gridDim.y) {
+        const uint32_t* cp = p.combine_pairs + (size_t)t * p.k;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t j = 0; j < p.k; ++j) {
+            const uint32_t pair = cp[j];
+            const float4 v = *reinterpret_cast<const float4*>(p.y + (size_t)pair * p.H + c4);
+            if (p.weight_after_down) {
+                const float w = p.pair_weight[pair];
+                acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+            } else {
+                acc.x = __fadd_rn(acc.x, v.x);
+                acc.y = __fadd_rn(acc.y, v.y);
+                acc.z = __fadd_rn(acc.z, v.z);
+                acc.w = __fadd_rn(acc.w, v.w);
+            }
+        }
+        if (p.has_shared) {
+            const float4 v = *reinterpret_cast<const float4*>(p.y + (size_t)(p.T * p.k + t) * p.H + c4);
             acc.x = __fadd_rn(acc.x, v.x);
             acc.y = __fadd_rn(acc.y, v.y);
             acc.z = __fadd_rn(acc.z, v.z);
             acc.w = __fadd_rn(acc.w, v.w);
         }
+        *reinterpret_cast<float4*>(p.out + (size_t)t * p.H + c4) = acc;
     }
-    if (p.has_shared) {
-        const float4 v = *reinterpret_cast<const float4*>(p.y + (size_t)(p.T * p.k + t) * p.H + c4);
-        acc.x = __fadd_rn(acc.x, v.x);
-        acc.y = __fadd_rn(acc.y, v.y);
-        acc.z = __fadd_rn(acc.z, v.z);
-        acc.w = __fadd_rn(acc.w, v.w);
-    }
-    *reinterpret_cast<float4*>(p.out + (size_t)t * p.H + c4) = acc;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1015,6 +1018,8 @@ static cudaError_t set_smem_once(K kernel, size_t bytes) {
     if (e == cudaSuccess) done.emplace_back((const void*)kernel, bytes);
     return e;
 }
+// grid.y for row-strided kernels (gridDim.y is limited to 65535)
+static unsigned rows_grid(uint32_t rows) { return rows < 65535u ? (rows ? rows : 1u) : 65535u; }
 static int g_num_sms = 0;
 static int num_sms() {
     if (g_num_sms == 0) {
@@ -1095,7 +1100,7 @@ cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xm
                             cudaStream_t s) {
     cudaError_t e = cudaMemsetAsync(xmax, 0, (size_t)T * 4u, s);
     if (e != cudaSuccess) return e;
-    token_prescale_kernel<<<dim3((H + 1023) / 1024, T), 256, 0, s>>>(x, T, H, xmax, xd);
+    token_prescale_kernel<<<dim3((H + 1023) / 1024, rows_grid(T)), 256, 0, s>>>(x, T, H, xmax, xd);
     return cudaGetLastError();
 }
 
@@ -1120,7 +1125,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     if (ev) cudaEventRecord(ev[0], s);
     // routing: router projection (or supplied logits) -> scores -> top-k; or given routes
     const bool given = p.routes_idx != nullptr;
-    token_prescale_kernel<<<dim3((p.H + 1023) / 1024, p.T), 256, 0, s>>>(
+    token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(
         p.x, p.T, p.H, p.xmax, (p.logits_in || given) ? nullptr : p.xd);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (given) {
@@ -1189,7 +1194,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     if (ev) cudaEventRecord(ev[4], s);
-    dim3 cg((p.H / 4 + 255) / 256, p.T);
+    dim3 cg((p.H / 4 + 255) / 256, rows_grid(p.T));
     combine_kernel<<<cg, 256, 0, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[5], s);

@@ -659,38 +659,41 @@ __global__ void __launch_bounds__(512) prefill_plan_kernel(MoeParams p) {
     if (tid == 0) p.counters[7] = running < p.max_ptiles ? running : p.max_ptiles;
 }
 
-// Pair-ordered fp16 activations: xperm[pair] = fp16(x[token(pair)] * s_token). 4 columns a thread.
+// Pair-ordered fp16 activations: xperm[pair] = fp16(x[token(pair)] * s_token). 4 columns a thread;
+// rows strided over gridDim.y (limited to 65535).
 __global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __restrict__ x,
                                                              const uint32_t* __restrict__ pair_token,
-                                                             const uint32_t* __restrict__ xmax,
+                                                             const uint32_t* __restrict__ xmax, uint32_t rows,
                                                              uint32_t width, __half* __restrict__ dst) {
-    const uint32_t pr = blockIdx.y;
     const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     if (c >= width) return;
-    const uint32_t t = pair_token[pr];
-    const float s = mma::prescale_for(__uint_as_float(xmax[t]));
-    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * width + c);
-    const __half2 a = __floats2half2_rn(v.x * s, v.y * s), b = __floats2half2_rn(v.z * s, v.w * s);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&a);
-    o.y = *reinterpret_cast<const uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(dst + (size_t)pr * width + c) = o;
+    for (uint32_t pr = blockIdx.y; pr < rows; pr += gridDim.y) {
+        const uint32_t t = pair_token[pr];
+        const float s = mma::prescale_for(__uint_as_float(xmax[t]));
+        const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * width + c);
+        const __half2 a = __floats2half2_rn(v.x * s, v.y * s), b = __floats2half2_rn(v.z * s, v.w * s);
+        uint2 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&a);
+        o.y = *reinterpret_cast<const uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(dst + (size_t)pr * width + c) = o;
+    }
 }
 
 // fp16(act * s) rows with s the power of two of each row's max (act_max); 4 columns a thread.
 __global__ void __launch_bounds__(256) prefill_half_kernel(const float* __restrict__ src,
-                                                           const uint32_t* __restrict__ rmax,
+                                                           const uint32_t* __restrict__ rmax, uint32_t rows,
                                                            uint32_t width, __half* __restrict__ dst) {
-    const uint32_t r = blockIdx.y;
     const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     if (c >= width) return;
-    const float s = mma::prescale_for(__uint_as_float(rmax[r]));
-    const float4 v = *reinterpret_cast<const float4*>(src + (size_t)r * width + c);
-    const __half2 a = __floats2half2_rn(v.x * s, v.y * s), b = __floats2half2_rn(v.z * s, v.w * s);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&a);
-    o.y = *reinterpret_cast<const uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(dst + (size_t)r * width + c) = o;
+    for (uint32_t r = blockIdx.y; r < rows; r += gridDim.y) {
+        const float s = mma::prescale_for(__uint_as_float(rmax[r]));
+        const float4 v = *reinterpret_cast<const float4*>(src + (size_t)r * width + c);
+        const __half2 a = __floats2half2_rn(v.x * s, v.y * s), b = __floats2half2_rn(v.z * s, v.w * s);
+        uint2 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&a);
+        o.y = *reinterpret_cast<const uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(dst + (size_t)r * width + c) = o;
+    }
 }
 
 template <typename Kern>
@@ -707,6 +710,8 @@ cudaError_t pf_smem_once(Kern kernel, size_t bytes) {
 
 uint32_t pairs_of(const MoeParams& p) { return p.T * p.k + (p.has_shared ? p.T : 0u); }
 
+unsigned rows_grid(uint32_t rows) { return rows < 65535u ? (rows ? rows : 1u) : 65535u; }
+
 }  // namespace
 
 uint32_t prefill_max_tiles(uint32_t T, uint32_t k, uint32_t E) {
@@ -721,8 +726,8 @@ cudaError_t launch_prefill_plan(const MoeParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_t s) {
-    prefill_gather_kernel<<<dim3((p.H / 4 + 255) / 256, pairs_of(p)), 256, 0, s>>>(p.x, p.pair_token, p.xmax,
-                                                                                    p.H, p.xperm);
+    prefill_gather_kernel<<<dim3((p.H / 4 + 255) / 256, rows_grid(pairs_of(p))), 256, 0, s>>>(
+        p.x, p.pair_token, p.xmax, pairs_of(p), p.H, p.xperm);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if ((e = pf_smem_once(prefill_gemm_kernel<true>, kPfSmemBytes)) != cudaSuccess) return e;
@@ -731,7 +736,8 @@ cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_
 }
 
 cudaError_t launch_prefill_down(const MoeParams& p, unsigned grid, cudaStream_t s) {
-    prefill_half_kernel<<<dim3((p.I / 4 + 255) / 256, pairs_of(p)), 256, 0, s>>>(p.act, p.act_max, p.I, p.act_h);
+    prefill_half_kernel<<<dim3((p.I / 4 + 255) / 256, rows_grid(pairs_of(p))), 256, 0, s>>>(
+        p.act, p.act_max, pairs_of(p), p.I, p.act_h);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if ((e = pf_smem_once(prefill_gemm_kernel<false>, kPfSmemBytes)) != cudaSuccess) return e;
