@@ -446,23 +446,39 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     // tiled device layout (blk_index): rows padded to whole 128-row tiles with zero blocks
     const size_t rows_padded = (rows + kTileRows - 1) / kTileRows * kTileRows;
     const size_t nslots = rows_padded * bpr;
+    const bool iq2 = type == VLB_TYPE_IQ2_XXS;
     const size_t d_bytes = (nslots * 2 + 255) / 256 * 256;
+    const size_t sc_bytes = iq2 ? (nslots * 4 + 255) / 256 * 256 : 0;
     const size_t body_bytes = nslots * L.body_bytes;
     std::vector<uint8_t> staged;
     try {
-        staged.assign(d_bytes + body_bytes, 0);
+        staged.assign(d_bytes + sc_bytes + body_bytes, 0);
     } catch (const std::bad_alloc&) {
         return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the matrix on the host");
     }
     uint16_t* dst_d = reinterpret_cast<uint16_t*>(staged.data());
-    uint8_t* dst_b = staged.data() + d_bytes;
+    uint32_t* dst_sc = reinterpret_cast<uint32_t*>(staged.data() + d_bytes);
+    uint8_t* dst_b = staged.data() + d_bytes + sc_bytes;
     const size_t copy = L.block_bytes - 2;
     for (size_t r = 0; r < rows; ++r)
         for (size_t c = 0; c < bpr; ++c) {
             const uint8_t* blk = src + (r * bpr + c) * L.block_bytes;
             const size_t at = blk_index((uint32_t)bpr, (uint32_t)r, (uint32_t)c);
             dst_d[at] = (uint16_t)(blk[0] | (blk[1] << 8));
-            std::memcpy(dst_b + at * L.body_bytes, blk + 2, copy);
+            uint8_t* body = dst_b + at * L.body_bytes;
+            std::memcpy(body, blk + 2, copy);
+            if (iq2) {
+                // group words -> pair-layout sign words, scales gathered per block
+                uint32_t scales = 0;
+                for (uint32_t g = 0; g < 8; ++g) {
+                    uint32_t aux;
+                    std::memcpy(&aux, body + g * 8 + 4, 4);
+                    scales |= (aux >> 28) << (4 * g);
+                    const uint32_t sw = iq2_pair_signs(aux);
+                    std::memcpy(body + g * 8 + 4, &sw, 4);
+                }
+                dst_sc[at] = scales;
+            }
         }
     vlb_matrix* m = new (std::nothrow) vlb_matrix();
     if (!m) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
@@ -483,11 +499,13 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     m->rows = rows;
     m->cols = cols;
     m->bpr = (uint32_t)bpr;
-    m->bytes = nslots * 2 + body_bytes;
+    m->bytes = nslots * 2 + (iq2 ? nslots * 4 : 0) + body_bytes;
     m->payload_bytes = payload_bytes;
     m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr,
                    reinterpret_cast<const uint16_t*>(m->mem),
-                   reinterpret_cast<const uint8_t*>(m->mem) + d_bytes,
+                   reinterpret_cast<const uint8_t*>(m->mem) + d_bytes + sc_bytes,
+                   iq2 ? reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(m->mem) + d_bytes)
+                       : nullptr,
                    prefill_scale(type, half_bits_to_float(dmax_bits))};
     *out = m;
     return VLB_OK;

@@ -45,9 +45,10 @@ __device__ __forceinline__ void load_group(const DevMat& m, uint32_t row, uint32
         const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(
             m.body + blk_index(m.bpr, row, blk) * 64u + gg * 8u));
+        const uint32_t ls4 = (__ldg(m.scales + blk_index(m.bpr, row, blk)) >> (4u * gg)) & 15u;
         r.a = v.x;
-        r.b = v.y;
-        r.ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(v.y >> 28))), 0.25f);
+        r.b = v.y;  // pair-layout sign word
+        r.ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)ls4)), 0.25f);
     } else if constexpr (FMT == kTypeIq3Xxs) {
         const uint32_t blk = g >> 3, gg = g & 7u;
         const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
@@ -86,7 +87,7 @@ __device__ __forceinline__ void decode_sub(const DevMat& m, uint32_t row, uint32
         }
     } else if constexpr (FMT == kTypeIq2Xxs) {
         const uint64_t gv = gs.iq2xxs[(r.a >> (8 * j)) & 0xffu];
-        const uint32_t signs = iq_signs(r.b, j);
+        const uint32_t signs = iq2_sub_signs(r.b, j);
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
             const float p = __fmul_rn(r.ls, (float)((uint32_t)(gv >> (8 * l)) & 0xffu));

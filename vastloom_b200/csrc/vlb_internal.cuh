@@ -2,18 +2,27 @@
 // bit-exact block decoders and the launch-side workspace structures.
 //
 // Device layout of a resident ggml matrix (chosen at upload, vlb_upload_matrix):
-//   d    : fp16 block scales (the 2-byte header of every ggml block)
-//   body : the rest of each block, padded to a 16-byte multiple
+//   d      : fp16 block scales (the 2-byte header of every ggml block)
+//   scales : IQ2_XXS only: one u32 per block holding the 8 group scales (nibble g = group g's
+//            4-bit scale, the top nibble of the ggml group word)
+//   body   : the rest of each block, padded to a 16-byte multiple
 //            Q8_0    : 32 int8 quants                                   (32 B)
-//            IQ2_XXS : 8 groups x (4 grid-index bytes, u32 signs/scale)  (64 B)
+//            IQ2_XXS : 8 groups x (4 grid-index bytes, u32 sign word)    (64 B)
 //            IQ3_XXS : 64 grid-index bytes, then 8 x u32 signs/scale      (96 B)
 //            IQ1_S   : 32 low-index bytes, then 8 x u16 high bits/scale   (48 B)
-// both in 128-row tiles: entry (row, block) sits at ((row / 128) * blocks_per_row + block) * 128
-// + row % 128, so one block column of a tile (128 rows x one block) is contiguous. The ggml block
-// is 34/66/98/50 bytes, so splitting the scale off makes every body 16-byte aligned without
-// changing the bytes read per weight; the tiling makes the prefill GEMM's per-stage weight tile
-// one contiguous run (bulk copies) and a decode warp's 8 consecutive rows of a block 512
-// contiguous bytes. Rows are padded to a multiple of 128 (zero blocks).
+// all three in 128-row tiles: entry (row, block) sits at ((row / 128) * blocks_per_row + block) *
+// 128 + row % 128, so one block column of a tile (128 rows x one block) is contiguous. The ggml
+// block is 34/66/98/50 bytes, so splitting the scale off makes every body 16-byte aligned; the
+// tiling makes the GEMMs' per-stage weight tile one contiguous run (bulk copies) and a decode
+// warp's 8 consecutive rows of a block 512 contiguous bytes. Rows are padded to a multiple of 128
+// (zero blocks).
+//
+// IQ2_XXS sign word. The ggml group word holds four 7-bit sign fields (the eighth sign of each
+// 8-weight sub-block is the even parity of the seven) and the group scale. The upload rewrites it
+// with all 32 signs laid out in pairs: the signs of weights 2j and 2j + 1 of sub-block s are bits
+// 4 s + j and 4 s + j + 16. One shift then puts a pair's two signs on the sign bits (15, 31) of an
+// fp16x2 register, which is what the tensor-core decoders flip. The scale moves to `scales` (4
+// more bytes per 256 weights: 70 instead of 66).
 #pragma once
 
 #include <cuda.h>
@@ -62,6 +71,7 @@ struct DevMat {
     uint32_t bpr;  // blocks per row
     const uint16_t* d;
     const uint8_t* body;
+    const uint32_t* scales;  // IQ2_XXS group scales (one u32 per block, tiled like d); else null
     // Power of two applied to the weights when the prefill kernels decode them to fp16: chosen at
     // upload from the largest block scale so that every |weight| * pscale stays below 2^14 (no
     // overflow) while small weights stay clear of the fp16 subnormal range.
@@ -98,16 +108,41 @@ __device__ __forceinline__ void decode_group_q8_0(float d, const uint8_t* body, 
     for (int i = 0; i < 32; ++i) w[i] = __fmul_rn(d, (float)(int8_t)body[i]);
 }
 
-// decode_iq2_xxs_block, ggml_quantization.cpp:250-283
-__device__ __forceinline__ void decode_group_iq2_xxs(float d, const uint8_t* body, int g,
+// The IQ2_XXS sign word of one ggml group word `aux` (see the layout note at the top): the four
+// sub-blocks' 8-bit sign masks (seven stored bits plus even parity, ksigns_iq2xs semantics of
+// ggml_quantization.cpp:268-271) regrouped into weight pairs.
+__host__ __device__ inline uint32_t iq2_pair_signs(uint32_t aux) {
+    uint32_t s = 0;
+    for (uint32_t sub = 0; sub < 4; ++sub) {
+        uint32_t s7 = (aux >> (7 * sub)) & 127u, par = 0;
+        for (uint32_t b = 0; b < 7; ++b) par ^= (s7 >> b) & 1u;
+        const uint32_t s8 = s7 | (par << 7);
+        for (uint32_t l = 0; l < 8; ++l)
+            if ((s8 >> l) & 1u) s |= 1u << (4 * sub + (l >> 1) + 16 * (l & 1));
+    }
+    return s;
+}
+
+// The 8-bit sign mask (bit l = weight l negative) of sub-block `sub` from a pair-layout sign word.
+__device__ __forceinline__ uint32_t iq2_sub_signs(uint32_t sw, int sub) {
+    const uint32_t lo = (sw >> (4 * sub)) & 15u, hi = (sw >> (4 * sub + 16)) & 15u;
+    uint32_t r = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r |= (((lo >> j) & 1u) << (2 * j)) | (((hi >> j) & 1u) << (2 * j + 1));
+    return r;
+}
+
+// decode_iq2_xxs_block, ggml_quantization.cpp:250-283 (device layout: grid indices and the pair
+// sign word in the body, the 4-bit group scale `ls4` from the scales word)
+__device__ __forceinline__ void decode_group_iq2_xxs(float d, const uint8_t* body, int g, uint32_t ls4,
                                                      const uint64_t* grid, float* w) {
     const uint32_t idx4 = *reinterpret_cast<const uint32_t*>(body + g * 8);
-    const uint32_t aux = *reinterpret_cast<const uint32_t*>(body + g * 8 + 4);
-    const float ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.25f);
+    const uint32_t sw = *reinterpret_cast<const uint32_t*>(body + g * 8 + 4);
+    const float ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)ls4)), 0.25f);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint64_t gv = grid[(idx4 >> (8 * j)) & 0xffu];
-        const uint32_t signs = iq_signs(aux, j);
+        const uint32_t signs = iq2_sub_signs(sw, j);
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
             const float m = (float)((uint32_t)(gv >> (8 * l)) & 0xffu);

@@ -51,7 +51,8 @@ __global__ void dequant_kernel(DevMat m, Grids g, float* __restrict__ out) {
         const uint32_t blk = grp >> 3, gg = grp & 7u;
         const float d = h2f(m.d[blk_index(m.bpr, row, blk)]);
         if (m.type == kTypeIq2Xxs)
-            decode_group_iq2_xxs(d, m.body + blk_index(m.bpr, row, blk) * 64u, gg, g.iq2xxs, w);
+            decode_group_iq2_xxs(d, m.body + blk_index(m.bpr, row, blk) * 64u, gg,
+                                 (m.scales[blk_index(m.bpr, row, blk)] >> (4u * gg)) & 15u, g.iq2xxs, w);
         else if (m.type == kTypeIq3Xxs)
             decode_group_iq3_xxs(d, m.body + blk_index(m.bpr, row, blk) * 96u, gg, g.iq3xxs, w);
         else

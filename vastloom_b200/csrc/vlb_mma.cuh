@@ -10,7 +10,8 @@
 // Exactness of the operands (so the products are exact and only the f32 sums round):
 //   * IQ2_XXS weight = d * (0.5 + s)/4 * m * sign, m in {8, 25, 43}: the factor (1 + 2s) * m / 8
 //     has at most 11 significant bits, so A = sign * (0.5 + s)/4 * m is an exact fp16; the fp16
-//     block scale d is applied in f32 when a 256-column block's partial sums are read out.
+//     block scale d is applied in f32 when a 256-column block's partial sums are read out. The
+//     signs come from the pair-layout sign word (vlb_internal.cuh): one shift per fp16 pair.
 //   * Q8_0 weight = d * q: A = q (int8) is an exact fp16; d is applied per 32-column block.
 //   * Activations: x * 2^e (a per-token power of two bringing max|x| into [2^14, 2^15)) is split
 //     into hi = fp16(x') and lo = fp16(x' - hi), 22 significant bits; both pieces are B columns
@@ -160,39 +161,31 @@ __device__ __forceinline__ void build_iq2_table(uint4* tab, const uint64_t* grid
     }
 }
 
-// The sign masks of one 8-weight sub-block for the four fp16 pairs (0,1) (2,3) (4,5) (6,7):
-// bit 15 / bit 31 of mask j carry the signs of weights 2j / 2j+1. The eighth sign is the parity
-// of the seven stored bits (ggml_quantization.cpp:268-271).
-struct SignMasks {
-    uint32_t m[4];
-};
-__device__ __forceinline__ SignMasks sign_masks(uint32_t s7) {
-    SignMasks r;
-    r.m[0] = s7 * 0x40008000u;  // bit0 -> 15, bit1 -> 31
-    r.m[1] = s7 * 0x10002000u;  // bit2 -> 15, bit3 -> 31
-    r.m[2] = s7 * 0x04000800u;  // bit4 -> 15, bit5 -> 31
-    r.m[3] = s7 * 0x00000200u + ((uint32_t)__popc(s7) << 31);  // bit6 -> 15, parity -> 31
-    return r;
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// Decodes one IQ2_XXS sub-block of one row into 4 fp16x2 registers (pairs 0..3).
+// Decodes one IQ2_XXS sub-block of one row into 4 fp16x2 registers (pairs 0..3): magnitudes from
+// the table, times the group factor kk, signs flipped from the pair-layout sign word `sw` (the
+// signs of pair j of sub-block `sub` sit at bits 4 sub + j and 4 sub + j + 16, so shifting left by
+// 15 - 4 sub - j lands them on the fp16 sign bits 15 and 31).
 __device__ __forceinline__ void decode_iq2_sub(const uint4* tab, uint32_t lane7, uint32_t idx4,
-                                               uint32_t aux, uint32_t sub, uint32_t kk,
+                                               uint32_t sw, uint32_t sub, uint32_t kk,
                                                uint32_t (&v)[4]) {
-    const uint32_t idx = (idx4 >> (8u * sub)) & 0xffu;
+    const uint32_t idx = prmt(idx4, 0u, 0x4440u | sub);  // grid index byte `sub`
     const uint4 g = tab[idx * 8u + lane7];
-    const SignMasks sm = sign_masks((aux >> (7u * sub)) & 127u);
-    v[0] = flip_signs(hmul2(g.x, kk), sm.m[0]);
-    v[1] = flip_signs(hmul2(g.y, kk), sm.m[1]);
-    v[2] = flip_signs(hmul2(g.z, kk), sm.m[2]);
-    v[3] = flip_signs(hmul2(g.w, kk), sm.m[3]);
+    v[0] = flip_signs(hmul2(g.x, kk), sw << (15u - 4u * sub));
+    v[1] = flip_signs(hmul2(g.y, kk), sw << (14u - 4u * sub));
+    v[2] = flip_signs(hmul2(g.z, kk), sw << (13u - 4u * sub));
+    v[3] = flip_signs(hmul2(g.w, kk), sw << (12u - 4u * sub));
 }
 
-// (0.5 + s)/4 for the 4-bit group scale s, as a pair of equal fp16 values (exact).
-__device__ __forceinline__ uint32_t group_scale_h2(uint32_t aux) {
-    const __half h = __float2half_rn((0.5f + (float)(aux >> 28)) * 0.25f);
-    const uint32_t u = __half_as_ushort(h);
-    return u | (u << 16);
+// (0.5 + s)/4 for the 4-bit group scale s, as a pair of equal fp16 values (exact):
+// fp16(1024 + s) is built from its bits, then (1024 + s) / 4 - 255.875 rounds exactly.
+__device__ __forceinline__ uint32_t group_scale_h2(uint32_t s4) {
+    return hfma2((s4 * 0x10001u) | 0x64006400u, 0x34003400u, 0xdbffdbffu);
 }
 
 // Q8_0: 8 int8 quants (two words) -> 4 fp16x2 registers with the exact integer values.
@@ -213,6 +206,8 @@ struct TileRows {
     const uint8_t* body_hi[kTiles];
     const uint16_t* d_lo[kTiles];
     const uint16_t* d_hi[kTiles];
+    const uint32_t* s_lo[kTiles];  // IQ2_XXS group scale words
+    const uint32_t* s_hi[kTiles];
 };
 
 __device__ __forceinline__ void tile_rows(const DevMat* const (&mats)[kTiles],
@@ -226,6 +221,8 @@ __device__ __forceinline__ void tile_rows(const DevMat* const (&mats)[kTiles],
         tr.body_hi[i] = m.body + blk_index(m.bpr, rows_hi[i], 0) * body_bytes;
         tr.d_lo[i] = m.d + blk_index(m.bpr, rows_lo[i], 0);
         tr.d_hi[i] = m.d + blk_index(m.bpr, rows_hi[i], 0);
+        tr.s_lo[i] = m.scales ? m.scales + blk_index(m.bpr, rows_lo[i], 0) : nullptr;
+        tr.s_hi[i] = m.scales ? m.scales + blk_index(m.bpr, rows_hi[i], 0) : nullptr;
     }
 }
 
@@ -234,6 +231,7 @@ __device__ __forceinline__ void tile_rows(const DevMat* const (&mats)[kTiles],
 struct Iq2Block {
     uint4 a[kTiles], b[kTiles];
     float da[kTiles], db[kTiles];
+    uint32_t sa[kTiles], sb[kTiles];  // group scale words
 };
 
 __device__ __forceinline__ void load_iq2_block(const TileRows& tr, uint32_t blk, uint32_t q,
@@ -244,6 +242,8 @@ __device__ __forceinline__ void load_iq2_block(const TileRows& tr, uint32_t blk,
         r.b[i] = ldg128(tr.body_hi[i] + (size_t)blk * (kTileRows * 64u) + 16u * q);
         r.da[i] = h2f(__ldg(tr.d_lo[i] + (size_t)blk * kTileRows));
         r.db[i] = h2f(__ldg(tr.d_hi[i] + (size_t)blk * kTileRows));
+        r.sa[i] = __ldg(tr.s_lo[i] + (size_t)blk * kTileRows);
+        r.sb[i] = __ldg(tr.s_hi[i] + (size_t)blk * kTileRows);
     }
 }
 
@@ -268,8 +268,8 @@ __device__ __forceinline__ void iq2_rows(const TileRows& tr, uint32_t k0, uint32
             uint32_t kka[kTiles], kkb[kTiles];
 #pragma unroll
             for (int i = 0; i < kTiles; ++i) {
-                kka[i] = group_scale_h2(half ? cur.a[i].w : cur.a[i].y);
-                kkb[i] = group_scale_h2(half ? cur.b[i].w : cur.b[i].y);
+                kka[i] = group_scale_h2((cur.sa[i] >> (4u * (2u * q + half))) & 15u);
+                kkb[i] = group_scale_h2((cur.sb[i] >> (4u * (2u * q + half))) & 15u);
             }
 #pragma unroll
             for (int sub = 0; sub < 4; ++sub) {

@@ -72,7 +72,8 @@ constexpr uint32_t kPfBStage = kPfMaxN * kPfKc * 2;  // 20 KB
 constexpr uint32_t kPfRawStages = 5;                 // packed-weight ring: ~85 KB in flight
 constexpr uint32_t kPfRawBody = kTileRows * 64u;     // 8 KB per matrix: one tile block column
 constexpr uint32_t kPfRawD = 512;                    // its block scales (<= 2 blocks x 128 rows)
-constexpr uint32_t kPfRawStage = 2 * kPfRawBody + 2 * kPfRawD;
+constexpr uint32_t kPfRawSc = kTileRows * 4u;        // IQ2_XXS group scale words (128 rows x u32)
+constexpr uint32_t kPfRawStage = 2 * kPfRawBody + 2 * kPfRawD + 2 * kPfRawSc;
 constexpr uint32_t kPfRawOff = kPfBStages * kPfBStage;
 constexpr uint32_t kPfTabOff = kPfRawOff + kPfRawStages * kPfRawStage;
 constexpr uint32_t kPfTabBytes = 256u * 8u * 16u;    // fp16 IQ2_XXS magnitudes, 8 replicas
@@ -165,6 +166,12 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
     return v;
 }
 
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -210,14 +217,14 @@ __device__ __forceinline__ void pf_decode_q8(uint4 q0, uint4 q1, uint32_t dbits,
 
 // IQ2_XXS (decode_iq2_xxs_block, ggml_quantization.cpp:250-283): w = d * (0.5 + s) / 4 * m * sign.
 // The group factor fp16(d * pscale * (0.5 + s) / 4) rounds once, its product with the exact grid
-// magnitude m once more; the sign is a bit flip.
-__device__ __forceinline__ void pf_decode_iq2(uint32_t idx4, uint32_t aux, float d, const uint4* tab,
+// magnitude m once more; the sign is a bit flip (pair-layout sign word `sw`, 4-bit scale `s4`).
+__device__ __forceinline__ void pf_decode_iq2(uint32_t idx4, uint32_t sw, uint32_t s4, float d, const uint4* tab,
                                               uint32_t lane7, uint32_t (&v)[16]) {
-    const uint32_t kk = h2_bits(d * (0.5f + (float)(aux >> 28)) * 0.25f);
+    const uint32_t kk = h2_bits(d * (0.5f + (float)s4) * 0.25f);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         uint32_t t[4];
-        mma::decode_iq2_sub(tab, lane7, idx4, aux, (uint32_t)j, kk, t);
+        mma::decode_iq2_sub(tab, lane7, idx4, sw, (uint32_t)j, kk, t);
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[4 * j + i] = t[i];
     }
@@ -286,17 +293,19 @@ __device__ __forceinline__ bool pf_produce(const PfBars& br, uint32_t smem, cons
             const uint32_t body = st + acc * kPfRawBody + r * 64u;
             const uint4 c0 = lds_u4(body), c1 = lds_u4(body + 16u), c2 = lds_u4(body + 32u), c3 = lds_u4(body + 48u);
             const uint32_t dbits = lds_u16(st + 2u * kPfRawBody + acc * kPfRawD + r * 2u);
+            const uint32_t scw = lds_u32(st + 2u * kPfRawBody + 2u * kPfRawD + acc * kPfRawSc + r * 4u);
             pf_arrive_warp(br.raw_empty + rslot);
             const float d = h2f((uint16_t)dbits) * ps;
             uint32_t v[16];
-            pf_decode_iq2(half ? c0.z : c0.x, half ? c0.w : c0.y, d, tab, lane7, v);
+            pf_decode_iq2(half ? c0.z : c0.x, half ? c0.w : c0.y, (scw >> (4u * half)) & 15u, d, tab, lane7, v);
 #pragma unroll
             for (uint32_t sub = 0; sub < 4u; ++sub) {  // groups 2 sub, 2 sub + 1
                 const uint32_t g = g0 + 4u * kb + sub;
                 if (!pf_store_a(br, g, t_a, v)) return false;
                 if (sub < 3u) {
                     const uint4 c = sub == 0 ? c1 : sub == 1 ? c2 : c3;
-                    pf_decode_iq2(half ? c.z : c.x, half ? c.w : c.y, d, tab, lane7, v);
+                    pf_decode_iq2(half ? c.z : c.x, half ? c.w : c.y, (scw >> (4u * (2u * sub + 2u + half))) & 15u, d,
+                                  tab, lane7, v);
                 }
                 pf_publish_a(br, g);
             }
@@ -314,7 +323,7 @@ __device__ __forceinline__ bool pf_load_raw(const PfBars& br, uint32_t smem, con
     for (uint32_t rs = 0; rs < stages; ++rs) {
         if (!pf_wait(br.raw_empty + raw.slot, raw.ph ^ 1u, br.abort, kPfSleepNs)) return false;
         const uint32_t dst = smem + kPfRawOff + raw.slot * kPfRawStage;
-        tc::mbar_arrive_expect_tx(br.raw_full + raw.slot, 2u * (kPfRawBody + dbytes));
+        tc::mbar_arrive_expect_tx(br.raw_full + raw.slot, 2u * (kPfRawBody + dbytes + (q8 ? 0u : kPfRawSc)));
         const uint32_t blk = q8 ? 2u * rs : rs;
 #pragma unroll
         for (uint32_t i = 0; i < 2u; ++i) {
@@ -322,6 +331,9 @@ __device__ __forceinline__ bool pf_load_raw(const PfBars& br, uint32_t smem, con
             const size_t at = blk_index(m.bpr, (i ? rt1 : rt0) * kTileRows, blk);
             tc::bulk_load(dst + i * kPfRawBody, m.body + at * (q8 ? 32u : 64u), kPfRawBody, br.raw_full + raw.slot);
             tc::bulk_load(dst + 2u * kPfRawBody + i * kPfRawD, m.d + at, dbytes, br.raw_full + raw.slot);
+            if (!q8)
+                tc::bulk_load(dst + 2u * kPfRawBody + 2u * kPfRawD + i * kPfRawSc, m.scales + at, kPfRawSc,
+                              br.raw_full + raw.slot);
         }
         raw.next(kPfRawStages);
     }
