@@ -247,7 +247,7 @@ def run_ours(args, rank, world, local_rank):
     hbm, peak_kind = load_peaks()
     dom = max(("gate_up", "down"), key=lambda p: phase_ms[p])
     achieved = pb[dom] / (phase_ms[dom] / 1000.0) / 1e9
-    kernel_name = {"gate_up": "expert_mma_kernel<true>", "down": "expert_mma_kernel<false>"}[dom]
+    kernel_name = {"gate_up": "decode_experts_kernel<true>", "down": "decode_experts_kernel<false>"}[dom]
     traffic = traffic_from_profiles(kernel_name)
     layer_bytes = pb["route"] + pb["gate_up"] + pb["down"] + pb["combine"]
     result = {

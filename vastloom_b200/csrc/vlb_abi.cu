@@ -736,7 +736,7 @@ static int check_layer_flags(vlb_handle* h, uint32_t flags) {
     if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
     if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
     if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
-    if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "a prefill pipeline wait ran out of time");
+    if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "an expert-kernel pipeline wait ran out of time");
     if (flags & 16u) return h->fail(VLB_ERR_INTERNAL_ERROR, "prefill shared memory is not 1 KB aligned");
     return VLB_OK;
 }

@@ -1,0 +1,587 @@
+// Decode expert products (one to four tokens per expert unit) for the IQ2_XXS and Q8_0 formats:
+// warp-level tensor-core MMAs (mma.sync m16n8k16, exact fp16 operands, f32 accumulation; see
+// vlb_mma.cuh for the exactness argument) fed by a bulk-copy ring in shared memory.
+//
+// Reference semantics: the expert loop of moe_forward (deepseek_v4_graph.cpp:2134-2227,
+// execute_expert :1826-1895) and of the OLMoE layer (olmoe_runtime.cpp:1226-1285): gate = W1 x,
+// up = W3 x, act = SwiGLU(gate, up) (route weight before the down product for DeepSeek V4, after
+// it for OLMoE), y = W2 act, each row a sum of double(w) * double(x) in the reference. Here every
+// product is exact and only the f32 sums round: ~1e-7 relative per row, inside the 1e-5 layer
+// tolerance.
+//
+// Why this shape. A decode step reads every selected expert's weights once, with a handful of
+// tokens each, so the kernel is a stream of weights through the SMs: each weight is decoded once
+// into an A-fragment register and multiplied against 4 tokens x (hi, lo) activation pieces. The
+// SM-side cost per weight (table lookup, scale, sign flip) is what bounds it, so nothing else may
+// stall the decoding warps: one loader lane per CTA moves the packed weights with bulk copies into
+// a 3-stage ring (110 KB in flight per SM), and 16 consumer warps only decode and multiply.
+//
+// Work decomposition. A unit (<= 4 pairs of one expert, ordered by expert) and a row group form
+// an item: gate/up items cover 256 rows of W1 and the same 256 rows of W3, down items 512 rows of
+// W2. A stage is one K-chunk of the item: four 128-row tile block columns ("slices", 8 KB of
+// packed weights each: 256 IQ2_XXS or 64 Q8_0 columns) with their block scales. Consumer warp w
+// owns 16 rows of two slices (gate: W1 and W3 of tile w / 8; down: tiles w / 8 and 2 + w / 8), so
+// every warp reads every stage and finishes its rows' sums itself: no cross-warp reduction. The
+// loader takes items from a global counter in chunks of neighbouring items (same unit: the staged
+// activations are reused) and tells the consumers what each stage holds through a stage header.
+//
+// Every wait is bounded by a 2 s limit; one that runs out sets error bit 8 of the layer flags and
+// an abort word that ends every other wait of the CTA, so a broken pipeline ends the kernel with
+// an error instead of hanging the GPU.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <vector>
+
+#include "vlb_launch.h"
+#include "vlb_mma.cuh"
+#include "vlb_tcgen05.cuh"
+
+namespace vlb {
+namespace {
+
+constexpr uint32_t kDcConsumerWarps = 16;
+constexpr uint32_t kDcConsumers = kDcConsumerWarps * 32;
+constexpr uint32_t kDcThreads = kDcConsumers + 32;             // + the loader warp
+constexpr uint32_t kDcSlices = 4;
+constexpr uint32_t kDcBody = kTileRows * 64u;                  // 8 KB of packed weights per slice
+constexpr uint32_t kDcD = 512;                                 // fp16 block scales (<= 2 blocks)
+constexpr uint32_t kDcSc = kTileRows * 4u;                     // IQ2_XXS group scale words
+constexpr uint32_t kDcSlice = kDcBody + kDcD + kDcSc;
+constexpr uint32_t kDcStage = kDcSlices * kDcSlice;            // 36 KB
+constexpr uint32_t kDcRing = 3;
+constexpr uint32_t kDcTabBytes = 256u * 8u * 16u;              // fp16 IQ2_XXS magnitudes, 8 replicas
+constexpr uint32_t kDcRingOff = kDcTabBytes;
+constexpr uint32_t kDcHdrOff = kDcRingOff + kDcRing * kDcStage;
+constexpr uint32_t kDcBarOff = kDcHdrOff + kDcRing * 16u;
+constexpr uint32_t kDcMiscOff = kDcBarOff + 64u;              // abort word, token scales
+constexpr uint32_t kDcXsOff = (kDcMiscOff + 64u + 127u) / 128u * 128u;
+constexpr uint64_t kDcWaitNs = 2000000000ull;
+constexpr uint32_t kDcErrTimeout = 8u;
+constexpr uint32_t kDcEnd = 0xffffffffu;
+constexpr uint32_t kDcMaxChunk = 4;
+
+static_assert(kDcXsOff % 16 == 0 && kDcStage % 1024 == 0, "shared-memory carve alignment");
+static_assert((2u * kDcRing + 1u) * 8u <= 64u, "barriers fit their slot");
+
+// Activation staging: 8 B columns (n = 2 token + piece, piece 0 = hi, 1 = lo) of K fp16 values.
+// Two layouts, each free of bank conflicts for its format's read pattern (8 lanes of a 16-byte
+// load phase: n in {2m, 2m+1} x q in 0..3):
+//   IQ2_XXS: lane q reads chunk c = 32 b + 8 q + j (block b, k-step pair j): stored at 16-byte
+//            position 32 b + 4 j + q of a column whose stride is K * 2 + 64 bytes, so the four q
+//            are consecutive and the column parity shifts by half a bank row; j is an immediate.
+//   Q8_0:    lane q reads chunk c = 4 b' + q (32-column block b'): stored at position
+//            c ^ (((c >> 3) & 3) | ((n & 1) << 2)) of a column of K * 2 bytes.
+__host__ __device__ constexpr uint32_t dc_xs_bytes(uint32_t K) { return 8u * (K * 2u + 64u); }
+
+__device__ __forceinline__ uint32_t dc_xs_offset(bool iq2, uint32_t n, uint32_t c, uint32_t K) {
+    if (iq2) return n * (K * 2u + 64u) + ((c & ~31u) + 4u * (c & 7u) + ((c >> 3) & 3u)) * 16u;
+    return (n * (K / 8u) + (c ^ (((c >> 3) & 3u) | ((n & 1u) << 2)))) * 16u;
+}
+
+// Stages the unit's activation rows (f32, scaled by the token's power of two) as hi/lo fp16
+// pieces. Consumer threads only.
+__device__ __forceinline__ void dc_stage_xs(unsigned char* xs, const float* const (&rows)[kUnitTokens],
+                                            const float (&scale)[kUnitTokens], uint32_t K, uint32_t n_tokens,
+                                            bool iq2) {
+    const uint32_t k_chunks = K / 8u, total = n_tokens * k_chunks;
+    for (uint32_t i = threadIdx.x; i < total; i += kDcConsumers) {
+        const uint32_t t = i / k_chunks, c = i % k_chunks;
+        const float4 a = *reinterpret_cast<const float4*>(rows[t] + c * 8u);
+        const float4 b = *reinterpret_cast<const float4*>(rows[t] + c * 8u + 4u);
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const float s = scale[t];
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float x0 = v[2 * w] * s, x1 = v[2 * w + 1] * s;  // exact: s is a power of two
+            const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+            const __half l0 = __float2half_rn(x0 - __half2float(h0));
+            const __half l1 = __float2half_rn(x1 - __half2float(h1));
+            hi[w] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lo[w] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        *reinterpret_cast<uint4*>(xs + dc_xs_offset(iq2, 2u * t, c, K)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(xs + dc_xs_offset(iq2, 2u * t + 1u, c, K)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// One bounded test loop on an mbarrier phase; false on abort or after the time limit.
+__device__ __forceinline__ bool dc_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (tc::mbar_try(bar, parity)) return true;
+        if ((i & 63u) == 0) {
+            if (*abort) return false;
+            const uint64_t now = tc::global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > kDcWaitNs) return false;
+            if (i >= (1u << 30)) return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void dc_fail(uint32_t* flags, volatile uint32_t* abort) {
+    *abort = 1u;
+    atomicOr(flags, kDcErrTimeout);
+}
+
+// A barrier of the 16 consumer warps on an mbarrier (so that it is bounded like every other wait:
+// a hardware named barrier would wait forever for a warp that left after an abort). Every lane
+// waits on the phase itself, which orders the other warps' shared-memory writes before its reads.
+__device__ __forceinline__ bool dc_consumer_sync(uint64_t* cbar, uint32_t& phase, volatile uint32_t* abort) {
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(cbar);
+    const bool ok = dc_wait(cbar, phase & 1u, abort);
+    ++phase;
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Item geometry shared by the loader and the consumers.
+struct DcItem {
+    uint32_t unit, group;       // unit index, row group
+    const DevMat* m[kDcSlices];  // matrix of each slice
+    uint32_t tile[kDcSlices];    // 128-row tile of each slice
+    bool valid[kDcSlices];
+    bool iq2;
+    uint32_t stages;             // K-chunks
+};
+
+template <bool GATEUP>
+__device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uint32_t groups) {
+    DcItem it;
+    it.unit = item / groups;
+    it.group = item % groups;
+    const Unit u = p.units[it.unit];
+    const uint32_t rows = GATEUP ? p.I : p.H;
+    const uint32_t tiles = (rows + kTileRows - 1u) / kTileRows;
+#pragma unroll
+    for (uint32_t s = 0; s < kDcSlices; ++s) {
+        if (GATEUP) {
+            it.m[s] = p.mats + (s < 2u ? 0u : (p.E + 1u)) + u.expert;  // W1 for slices 0-1, W3 for 2-3
+            it.tile[s] = 2u * it.group + (s & 1u);
+        } else {
+            it.m[s] = p.mats + 2u * (p.E + 1u) + u.expert;
+            it.tile[s] = 4u * it.group + s;
+        }
+        it.valid[s] = it.tile[s] < tiles;
+    }
+    const uint32_t K = GATEUP ? p.H : p.I;
+    it.iq2 = it.m[0]->type == kTypeIq2Xxs;
+    it.stages = it.iq2 ? K / 256u : (K / 32u + 1u) / 2u;
+    return it;
+}
+
+// The consumer warp's view of an item: its two slices' tiles (scalars, no indexed arrays).
+struct DcWarpItem {
+    uint32_t unit;
+    uint32_t tile0, tile1;  // tiles of slices s0 and s1
+    bool valid0, valid1;
+    bool iq2;
+    uint32_t bpr;
+};
+
+template <bool GATEUP>
+__device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t item, uint32_t groups, uint32_t s0,
+                                                   uint32_t s1) {
+    DcWarpItem w;
+    w.unit = item / groups;
+    const uint32_t group = item % groups;
+    const Unit u = p.units[w.unit];
+    const uint32_t rows = GATEUP ? p.I : p.H;
+    const uint32_t tiles = (rows + kTileRows - 1u) / kTileRows;
+    w.tile0 = GATEUP ? 2u * group + (s0 & 1u) : 4u * group + s0;
+    w.tile1 = GATEUP ? 2u * group + (s1 & 1u) : 4u * group + s1;
+    w.valid0 = w.tile0 < tiles;
+    w.valid1 = w.tile1 < tiles;
+    const DevMat& m = p.mats[(GATEUP ? 0u : 2u * (p.E + 1u)) + u.expert];
+    w.iq2 = m.type == kTypeIq2Xxs;
+    w.bpr = m.bpr;
+    return w;
+}
+
+// ---- loader lane --------------------------------------------------------------------------------
+template <bool GATEUP>
+__device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t groups, uint64_t n_items,
+                          uint32_t chunk, volatile uint32_t* abort) {
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDcBarOff);
+    uint64_t* empty = full + kDcRing;
+    uint4* hdr = reinterpret_cast<uint4*>(smem + kDcHdrOff);
+    uint32_t* next_item = p.counters + (GATEUP ? 2 : 4);
+    const uint32_t mat_off = GATEUP ? 0u : 2u * (p.E + 1u);
+    uint32_t g = 0;
+    bool ok = true;
+    auto acquire = [&](uint32_t slot) -> bool {
+        if (g >= kDcRing && !dc_wait(empty + slot, ((g / kDcRing) - 1u) & 1u, abort)) {
+            dc_fail(p.counters + 3, abort);
+            return false;
+        }
+        return true;
+    };
+    while (ok) {
+        // chunks of neighbouring items (one unit's row groups share the staged activations) while
+        // much work is left, single items towards the end so that the CTAs finish together
+        const uint64_t seen = *reinterpret_cast<volatile uint32_t*>(next_item);
+        uint32_t take = seen < n_items ? (uint32_t)((n_items - seen) / (2ull * gridDim.x)) : 1u;
+        take = take < 1u ? 1u : (take > chunk ? chunk : take);
+        const uint64_t c0 = atomicAdd(next_item, take);
+        if (c0 >= n_items) break;
+        const uint64_t c1 = c0 + take < n_items ? c0 + take : n_items;
+        for (uint64_t ord = c0; ord < c1 && ok; ++ord) {
+            // heaviest first: the units are in expert order with the shared expert (many units of
+            // one matrix) last, so items are taken from the end
+            const uint64_t item = n_items - 1u - ord;
+            const Unit u = p.units[(uint32_t)(item / groups)];
+            const uint32_t t = p.mats[mat_off + u.expert].type;
+            if (t != kTypeIq2Xxs && t != kTypeQ8_0) continue;  // served by the CUDA-core kernels
+            const DcItem it = dc_item<GATEUP>(p, (uint32_t)item, groups);
+            for (uint32_t st = 0; st < it.stages; ++st, ++g) {
+                const uint32_t slot = g % kDcRing;
+                if (!(ok = acquire(slot))) break;
+                // Q8_0: blocks 2 st and 2 st + 1 (the second may be past the row end)
+                const uint32_t nblk = it.iq2 ? 1u : (2u * st + 1u < it.m[0]->bpr ? 2u : 1u);
+                const uint32_t body = it.iq2 ? kDcBody : nblk * kTileRows * 32u;
+                const uint32_t dbytes = nblk * kTileRows * 2u;
+                uint32_t bytes = 0;
+#pragma unroll
+                for (uint32_t s = 0; s < kDcSlices; ++s)
+                    if (it.valid[s]) bytes += body + dbytes + (it.iq2 ? kDcSc : 0u);
+                hdr[slot] = make_uint4((uint32_t)item, st, it.stages, 0u);
+                tc::mbar_arrive_expect_tx(full + slot, bytes);
+                const uint32_t dst = tc::smem_u32(smem + kDcRingOff + slot * kDcStage);
+                const uint32_t blk = it.iq2 ? st : 2u * st;
+#pragma unroll
+                for (uint32_t s = 0; s < kDcSlices; ++s) {
+                    if (!it.valid[s]) continue;
+                    const DevMat& m = *it.m[s];
+                    const size_t at = blk_index(m.bpr, it.tile[s] * kTileRows, blk);
+                    const uint32_t sd = dst + s * kDcSlice;
+                    tc::bulk_load(sd, m.body + at * (it.iq2 ? 64u : 32u), body, full + slot);
+                    tc::bulk_load(sd + kDcBody, m.d + at, dbytes, full + slot);
+                    if (it.iq2) tc::bulk_load(sd + kDcBody + kDcD, m.scales + at, kDcSc, full + slot);
+                }
+            }
+        }
+    }
+    if (ok) {  // end marker: a stage with no copies
+        const uint32_t slot = g % kDcRing;
+        if (acquire(slot)) {
+            hdr[slot] = make_uint4(kDcEnd, 0u, 0u, 0u);
+            tc::mbar_arrive(full + slot);
+            ++g;
+        }
+    }
+    // no bulk copy may still be landing in shared memory when the CTA exits
+    for (uint32_t j = g > kDcRing ? g - kDcRing : 0u; j < g; ++j)
+        if (!dc_wait(full + j % kDcRing, (j / kDcRing) & 1u, abort)) break;
+}
+
+// ---- consumer warps -------------------------------------------------------------------------------
+// IQ2_XXS stage: one 256-column block of this warp's two slices (rows rt + gq and rt + gq + 8).
+__device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
+                                             uint32_t gq, uint32_t q, uint32_t xrow, const uint4* tab,
+                                             uint32_t lane7, uint64_t* empty_bar, float (&acc)[2][4]) {
+    uint4 ra[2], rb[2];
+    float da[2], db[2];
+    uint32_t sa[2], sb[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t sl = st_addr + (i ? s1 : s0) * kDcSlice;
+        const uint32_t ba = sl + (rt + gq) * 64u + 16u * q, bb = ba + 8u * 64u;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(ra[i].x), "=r"(ra[i].y), "=r"(ra[i].z), "=r"(ra[i].w) : "r"(ba));
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(rb[i].x), "=r"(rb[i].y), "=r"(rb[i].z), "=r"(rb[i].w) : "r"(bb));
+        unsigned short ha, hb;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ha) : "r"(sl + kDcBody + (rt + gq) * 2u));
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hb) : "r"(sl + kDcBody + (rt + gq + 8u) * 2u));
+        da[i] = h2f(ha);
+        db[i] = h2f(hb);
+        uint32_t wa, wb;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wa) : "r"(sl + kDcBody + kDcD + (rt + gq) * 4u));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wb) : "r"(sl + kDcBody + kDcD + (rt + gq + 8u) * 4u));
+        sa[i] = wa >> (8u * q);  // this lane's groups 2q, 2q + 1 in the low byte
+        sb[i] = wb >> (8u * q);
+    }
+    // the slot is free once every lane has its words
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
+    float D[2][4] = {}, E[2][4] = {};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t kka[2], kkb[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            kka[i] = mma::group_scale_h2((sa[i] >> (4 * half)) & 15u);
+            kkb[i] = mma::group_scale_h2((sb[i] >> (4 * half)) & 15u);
+        }
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+            uint4 xb;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(xb.x), "=r"(xb.y), "=r"(xb.z), "=r"(xb.w)
+                         : "r"(xrow + (uint32_t)(4 * half + sub) * 64u));
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                uint32_t va[4], vb[4];
+                mma::decode_iq2_sub(tab, lane7, half ? ra[i].z : ra[i].x, half ? ra[i].w : ra[i].y, (uint32_t)sub,
+                                    kka[i], va);
+                mma::decode_iq2_sub(tab, lane7, half ? rb[i].z : rb[i].x, half ? rb[i].w : rb[i].y, (uint32_t)sub,
+                                    kkb[i], vb);
+                float (&A)[4] = (sub & 1) ? E[i] : D[i];
+                mma::mma16816(A, va[0], vb[0], va[1], vb[1], xb.x, xb.y);
+                mma::mma16816(A, va[2], vb[2], va[3], vb[3], xb.z, xb.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        acc[i][0] = fmaf(da[i], D[i][0] + E[i][0], acc[i][0]);
+        acc[i][1] = fmaf(da[i], D[i][1] + E[i][1], acc[i][1]);
+        acc[i][2] = fmaf(db[i], D[i][2] + E[i][2], acc[i][2]);
+        acc[i][3] = fmaf(db[i], D[i][3] + E[i][3], acc[i][3]);
+    }
+}
+
+// Q8_0 stage: 32-column blocks 2 st and 2 st + 1 (nblk of them) of the warp's two slices.
+__device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt, uint32_t gq,
+                                            uint32_t q, uint32_t n, const unsigned char* xs, uint32_t K,
+                                            uint32_t blk0, uint32_t nblk, uint64_t* empty_bar,
+                                            float (&acc)[2][4]) {
+    uint2 qa[2][2], qb[2][2];
+    float da[2][2], db[2][2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t sl = st_addr + (i ? s1 : s0) * kDcSlice;
+            const uint32_t ba = sl + j * (kTileRows * 32u) + (rt + gq) * 32u + 8u * q, bb = ba + 8u * 32u;
+            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(qa[i][j].x), "=r"(qa[i][j].y) : "r"(ba));
+            asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(qb[i][j].x), "=r"(qb[i][j].y) : "r"(bb));
+            unsigned short ha, hb;
+            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ha) : "r"(sl + kDcBody + j * (kTileRows * 2u) + (rt + gq) * 2u));
+            asm volatile("ld.shared.u16 %0, [%1];"
+                         : "=h"(hb)
+                         : "r"(sl + kDcBody + j * (kTileRows * 2u) + (rt + gq + 8u) * 2u));
+            da[i][j] = h2f(ha);
+            db[i][j] = h2f(hb);
+        }
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
+#pragma unroll
+    for (uint32_t j = 0; j < 2; ++j) {
+        if (j >= nblk) break;
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + dc_xs_offset(false, n, (blk0 + j) * 4u + q, K));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            uint32_t va[4], vb[4];
+            mma::decode_q8_sub(qa[i][j].x, qa[i][j].y, va);
+            mma::decode_q8_sub(qb[i][j].x, qb[i][j].y, vb);
+            float D[4] = {0.f, 0.f, 0.f, 0.f};
+            mma::mma16816(D, va[0], vb[0], va[1], vb[1], xv.x, xv.y);
+            mma::mma16816(D, va[2], vb[2], va[3], vb[3], xv.z, xv.w);
+            acc[i][0] = fmaf(da[i][j], D[0], acc[i][0]);
+            acc[i][1] = fmaf(da[i][j], D[1], acc[i][1]);
+            acc[i][2] = fmaf(db[i][j], D[2], acc[i][2]);
+            acc[i][3] = fmaf(db[i][j], D[3], acc[i][3]);
+        }
+    }
+}
+
+template <bool GATEUP>
+__global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __grid_constant__ MoeParams p,
+                                                                       uint32_t chunk) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kDcMiscOff);
+    float* tok_scale = reinterpret_cast<float*>(smem + kDcMiscOff + 16u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDcBarOff);
+    uint64_t* empty = full + kDcRing;
+    const uint32_t K = GATEUP ? p.H : p.I;
+    unsigned char* xs = smem + kDcXsOff;
+    const uint4* tab = reinterpret_cast<const uint4*>(smem);
+    mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
+    for (uint32_t i = threadIdx.x; i < dc_xs_bytes(K) / 16u; i += blockDim.x)
+        reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kDcRing; ++s) {
+            tc::mbar_init(full + s, 1);
+            tc::mbar_init(empty + s, kDcConsumerWarps);
+        }
+        tc::mbar_init(empty + kDcRing, kDcConsumerWarps);  // the consumers' own barrier
+        *abort = 0u;
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+    const uint32_t rows = GATEUP ? p.I : p.H;
+    const uint32_t groups = (rows + (GATEUP ? 255u : 511u)) / (GATEUP ? 256u : 512u);
+    const uint64_t n_items = (uint64_t)p.counters[0] * groups;
+    if (warp == kDcConsumerWarps) {
+        if (lane == 0) dc_loader<GATEUP>(p, smem, groups, n_items, chunk, abort);
+        return;
+    }
+    // consumer warp: 16 rows of slices (w / 8) and (2 + w / 8)
+    const uint32_t s0 = warp >> 3, s1 = 2u + (warp >> 3), rt = (warp & 7u) * 16u;
+    const uint32_t gq = lane >> 2, q = lane & 3u, n = lane >> 2, lane7 = lane & 7u;
+    const uint4* hdr = reinterpret_cast<const uint4*>(smem + kDcHdrOff);
+    const uint32_t xs_iq2_lane = tc::smem_u32(xs) + n * (K * 2u + 64u) + q * 16u;
+    uint64_t* cbar = empty + kDcRing;
+    uint32_t cphase = 0;
+    uint32_t staged_unit = 0xffffffffu;
+    bool staged_iq2 = false;
+    float acc[2][4] = {};
+    DcWarpItem it{};
+    for (uint32_t g = 0;; ++g) {
+        const uint32_t slot = g % kDcRing;
+        const bool ok = dc_wait(full + slot, (g / kDcRing) & 1u, abort);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) dc_fail(p.counters + 3, abort);
+            break;
+        }
+        const uint4 h = hdr[slot];
+        if (h.x == kDcEnd) break;
+        if (h.y == 0) {  // first stage of an item
+            it = dc_warp_item<GATEUP>(p, h.x, groups, s0, s1);
+            if (it.unit != staged_unit || it.iq2 != staged_iq2) {
+                const Unit u = p.units[it.unit];
+                // every warp is done with the previous unit's activations and token scales
+                if (!dc_consumer_sync(cbar, cphase, abort)) {
+                    if (lane == 0) dc_fail(p.counters + 3, abort);
+                    break;
+                }
+                if (threadIdx.x < (uint32_t)kUnitTokens) {
+                    float sc = 1.f;
+                    if (threadIdx.x < u.count)
+                        sc = mma::prescale_for(__uint_as_float(GATEUP ? p.xmax[p.pair_token[u.pair_begin + threadIdx.x]]
+                                                                      : p.act_max[u.pair_begin + threadIdx.x]));
+                    tok_scale[threadIdx.x] = sc;
+                }
+                if (!dc_consumer_sync(cbar, cphase, abort)) {
+                    if (lane == 0) dc_fail(p.counters + 3, abort);
+                    break;
+                }
+                const float* rws[kUnitTokens];
+                float scl[kUnitTokens];
+#pragma unroll
+                for (int t = 0; t < kUnitTokens; ++t) {
+                    const uint32_t pair = u.pair_begin + (uint32_t)t;
+                    rws[t] = (uint32_t)t < u.count
+                                 ? (GATEUP ? p.x + (size_t)p.pair_token[pair] * p.H : p.act + (size_t)pair * p.I)
+                                 : nullptr;
+                    scl[t] = tok_scale[t];
+                }
+                dc_stage_xs(xs, rws, scl, K, u.count, it.iq2);
+                if (!dc_consumer_sync(cbar, cphase, abort)) {
+                    if (lane == 0) dc_fail(p.counters + 3, abort);
+                    break;
+                }
+                staged_unit = it.unit;
+                staged_iq2 = it.iq2;
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        }
+        const uint32_t st_addr = tc::smem_u32(smem + kDcRingOff + slot * kDcStage);
+        if (it.iq2) {
+            dc_iq2_stage(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab, lane7, empty + slot, acc);
+        } else {
+            const uint32_t blk0 = 2u * h.y;
+            const uint32_t nblk = blk0 + 1u < it.bpr ? 2u : 1u;
+            dc_q8_stage(st_addr, s0, s1, rt, gq, q, n, xs, K, blk0, nblk, empty + slot, acc);
+        }
+        if (h.y + 1u == h.z) {  // last stage: this warp's rows are complete
+            const Unit u = p.units[it.unit];
+            if (q < u.count) {
+                const uint32_t pair = u.pair_begin + q;
+                const float inv = 1.f / tok_scale[q];  // exact: a power of two
+                if (GATEUP) {
+                    const bool shared = u.expert == p.E;
+                    const float limit = shared ? p.shared_limit : p.routed_limit;
+                    const uint32_t row_base = it.tile0 * kTileRows + rt + gq;
+#pragma unroll
+                    for (int hi = 0; hi < 2; ++hi) {  // fragment row gq / gq + 8
+                        const uint32_t row = row_base + 8u * hi;
+                        if (!it.valid0 || row >= p.I) continue;
+                        const float gv = (acc[0][2 * hi] + acc[0][2 * hi + 1]) * inv;
+                        const float uv = (acc[1][2 * hi] + acc[1][2 * hi + 1]) * inv;
+                        float a;
+                        if (p.weight_after_down) {
+                            // OLMoE: float SwiGLU with expf (olmoe_runtime.cpp:1279)
+                            a = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+                        } else {
+                            // execute_expert: double SwiGLU, optional clamp, route weight before
+                            // the down product (deepseek_v4_graph.cpp:1865-1890)
+                            double gd = (double)gv, ud = (double)uv;
+                            if (limit > 0.f) {
+                                gd = fmin(gd, (double)limit);
+                                ud = fmin(fmax(ud, -(double)limit), (double)limit);
+                            }
+                            double v = gd / (1.0 + exp(-gd)) * ud;
+                            if (!shared) v *= (double)p.pair_weight[pair];
+                            a = (float)v;
+                        }
+                        p.act[(size_t)pair * p.I + row] = a;
+                        atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        if (!(i ? it.valid1 : it.valid0)) continue;
+#pragma unroll
+                        for (int hi = 0; hi < 2; ++hi) {
+                            const uint32_t row = (i ? it.tile1 : it.tile0) * kTileRows + rt + gq + 8u * hi;
+                            if (row < p.H) p.y[(size_t)pair * p.H + row] = (acc[i][2 * hi] + acc[i][2 * hi + 1]) * inv;
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <bool GATEUP>
+cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
+    const uint32_t K = GATEUP ? p.H : p.I;
+    const size_t smem = kDcXsOff + dc_xs_bytes(K);
+    static std::mutex mu;
+    static std::vector<size_t> configured;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (configured.size() <= (size_t)dev) configured.resize((size_t)dev + 1, 0);
+        if (configured[(size_t)dev] < smem) {
+            int optin = 0;
+            if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+                return e;
+            if (smem > (size_t)optin) return cudaErrorInvalidValue;  // hidden size beyond this kernel's staging
+            if ((e = cudaFuncSetAttribute(decode_experts_kernel<GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem)) != cudaSuccess)
+                return e;
+            configured[(size_t)dev] = smem;
+        }
+    }
+    // items ~ units x row groups; the host does not know the unit count (it is on the device), so
+    // the chunk follows the worst case of one unit per routed pair plus the shared expert's units
+    const uint32_t rows = GATEUP ? p.I : p.H;
+    const uint32_t groups = (rows + (GATEUP ? 255u : 511u)) / (GATEUP ? 256u : 512u);
+    const uint64_t est = (uint64_t)(p.T * p.k < p.E ? p.T * p.k : p.E) * groups;
+    uint32_t chunk = (uint32_t)((est + 4ull * n_sms - 1) / (4ull * n_sms));
+    chunk = chunk < 1u ? 1u : (chunk > kDcMaxChunk ? kDcMaxChunk : chunk);
+    decode_experts_kernel<GATEUP><<<n_sms, kDcThreads, smem, s>>>(p, chunk);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_decode_gateup(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
+    return launch_decode<true>(p, n_sms, s);
+}
+
+cudaError_t launch_decode_down(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
+    return launch_decode<false>(p, n_sms, s);
+}
+
+}  // namespace vlb

@@ -736,15 +736,6 @@ __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
     }
 }
 
-// ---------------------------------------------------------------------------------------------
-// Tensor-core decode expert kernel (IQ2_XXS and Q8_0 experts; vlb_mma.cuh). CTA = 8 warps:
-// 4 row groups x 2 column halves. Gate/up: a warp owns 32 output rows (two 16-row tiles of the
-// gate matrix and the same two of the up matrix), a CTA 128; down: a warp owns 64 rows, a CTA
-// 256. The two column halves are summed through shared memory before the epilogue.
-constexpr uint32_t kMmaTabBytes = 256u * 8u * 16u;      // fp16 IQ2_XXS table, 8 replicas
-constexpr uint32_t kMmaRedBytes = 7u * 32u * 8u * 4u;   // partial sums of the column splits
-constexpr uint32_t kMmaChunk = 4;                        // max items per work-stealing grab
-
 __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __restrict__ x, uint32_t T,
                                                              uint32_t H, uint32_t* __restrict__ xmax,
                                                              double* __restrict__ xd) {
@@ -768,180 +759,6 @@ __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __rest
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((threadIdx.x & 31u) == 0 && m > 0.f) atomicMax(xmax + t, __float_as_uint(m));
     }
-}
-
-// CTA shape: rg_count row groups x (8 / rg_count) column splits. A warp owns one 16-row tile of
-// the gate matrix and the same tile of the up matrix (gate/up: 16 output rows), or two 16-row
-// tiles of the down matrix (32 rows), over its share of the columns. Few tokens -> few units ->
-// narrow row groups and more column splits, so every SM has work.
-template <bool GATEUP>
-__global__ void __launch_bounds__(256, 2) expert_mma_kernel(MoeParams p, uint32_t rg_count) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    uint4* tab = reinterpret_cast<uint4*>(smem);
-    uint4* xs = reinterpret_cast<uint4*>(smem + kMmaTabBytes);
-    const uint32_t K = GATEUP ? p.H : p.I;
-    float* red = reinterpret_cast<float*>(smem + kMmaTabBytes + (size_t)8u * K * 2u);
-    mma::build_iq2_table(tab, p.grids.iq2xxs);
-    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) xs[i] = make_uint4(0u, 0u, 0u, 0u);
-    uint32_t staged_count = 0;  // tokens whose pieces the staging buffer holds (the rest are zero)
-    const uint32_t n_units = p.counters[0];
-    const uint32_t ks_count = 8u / rg_count;
-    const uint32_t warp_rows = GATEUP ? 16u : 32u;
-    const uint32_t rows_per_item = warp_rows * rg_count;
-    const uint32_t tiles = (GATEUP ? p.I : p.H) / rows_per_item;
-    const uint64_t n_items = (uint64_t)n_units * tiles;
-    uint32_t chunk = (uint32_t)((n_items + 4ull * gridDim.x - 1) / (4ull * gridDim.x));
-    chunk = chunk < 1u ? 1u : (chunk > kMmaChunk ? kMmaChunk : chunk);
-    uint32_t* next_item = p.counters + (GATEUP ? 2 : 4);
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t rg = warp % rg_count, ks = warp / rg_count, g = lane >> 2, q = lane & 3u;
-    const uint32_t k_chunks = K / 8u;
-    const uint32_t kslice = K / ks_count;
-    const uint32_t mat_base = GATEUP ? 0u : 2u * (p.E + 1);
-    uint32_t staged = 0xffffffffu;
-    __shared__ float scale_s[kUnitTokens];
-    __shared__ uint32_t chunk_s;
-    __syncthreads();
-    // Work stealing in chunks of consecutive items (one unit's neighbouring row tiles, so the
-    // staged activations are reused within a chunk).
-    for (;;) {
-    if (threadIdx.x == 0) chunk_s = atomicAdd(next_item, chunk);
-    __syncthreads();
-    const uint64_t c0 = chunk_s;
-    __syncthreads();
-    if (c0 >= n_items) break;
-    const uint64_t c1 = c0 + chunk < n_items ? c0 + chunk : n_items;
-    for (uint64_t item = c0; item < c1; ++item) {
-        const uint32_t ui = (uint32_t)(item / tiles), tile = (uint32_t)(item % tiles);
-        const Unit u = p.units[ui];
-        const DevMat* ma = p.mats + mat_base + u.expert;
-        if (!mma_type(ma->type)) continue;
-        if (ui != staged) {
-            __syncthreads();
-            const float* rows[kUnitTokens];
-#pragma unroll
-            for (int t = 0; t < kUnitTokens; ++t) {
-                const uint32_t pair = u.pair_begin + t;
-                rows[t] = nullptr;
-                if ((uint32_t)t < u.count)
-                    rows[t] = GATEUP ? p.x + (size_t)p.pair_token[pair] * p.H : p.act + (size_t)pair * p.I;
-            }
-            if (threadIdx.x < kUnitTokens) {
-                const uint32_t t = threadIdx.x;
-                float sc = 1.f;
-                if (t < u.count)
-                    sc = mma::prescale_for(__uint_as_float(
-                        GATEUP ? p.xmax[p.pair_token[u.pair_begin + t]] : p.act_max[u.pair_begin + t]));
-                scale_s[t] = sc;
-            }
-            __syncthreads();
-            float sc[kUnitTokens];
-#pragma unroll
-            for (int t = 0; t < kUnitTokens; ++t) sc[t] = scale_s[t];
-            const uint32_t n_stage = u.count > staged_count ? u.count : staged_count;
-            mma::stage_pieces(xs, rows, sc, K, n_stage);
-            __syncthreads();
-            staged = ui;
-            staged_count = u.count;
-        }
-        // this warp's two 16-row tiles
-        const DevMat* mats[mma::kTiles];
-        uint32_t rlo[mma::kTiles], rhi[mma::kTiles];
-        const uint32_t out0 = tile * rows_per_item + rg * warp_rows;
-#pragma unroll
-        for (int i = 0; i < mma::kTiles; ++i) {
-            uint32_t base;
-            if (GATEUP) {
-                mats[i] = i == 0 ? ma : p.mats + (p.E + 1) + u.expert;
-                base = out0;
-            } else {
-                mats[i] = ma;
-                base = out0 + 16u * i;
-            }
-            rlo[i] = base + g;
-            rhi[i] = base + g + 8u;
-        }
-        float acc[mma::kTiles][4];
-#pragma unroll
-        for (int i = 0; i < mma::kTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-        const uint32_t k0 = ks * kslice, k1 = k0 + kslice;
-        const bool iq2 = ma->type == kTypeIq2Xxs;
-        mma::TileRows tr;
-        mma::tile_rows(mats, rlo, rhi, iq2 ? 64u : 32u, tr);
-        if (iq2) mma::iq2_rows(tr, k0, k1, xs, k_chunks, tab, acc);
-        else mma::q8_rows(tr, k0, k1, xs, k_chunks, acc);
-        // sum the column splits: split ks > 0 parks its partial sums, split 0 adds them
-        if (ks > 0) {
-            float* mine = red + (((size_t)(ks - 1u) * rg_count + rg) * 32u + lane) * 8u;
-#pragma unroll
-            for (int i = 0; i < mma::kTiles; ++i)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) mine[i * 4 + c] = acc[i][c];
-        }
-        __syncthreads();
-        if (ks == 0 && q < u.count) {
-            for (uint32_t j = 1; j < ks_count; ++j) {
-                const float* other = red + (((size_t)(j - 1u) * rg_count + rg) * 32u + lane) * 8u;
-#pragma unroll
-                for (int i = 0; i < mma::kTiles; ++i)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[i][c] += other[i * 4 + c];
-            }
-            const uint32_t pair = u.pair_begin + q;
-            const float inv = 1.f / scale_s[q];  // exact: a power of two
-            if (GATEUP) {
-                const bool shared = u.expert == p.E;
-                const float limit = shared ? p.shared_limit : p.routed_limit;
-#pragma unroll
-                for (int hi = 0; hi < 2; ++hi) {  // fragment row g / g+8
-                    const float gv = (acc[0][2 * hi] + acc[0][2 * hi + 1]) * inv;
-                    const float uv = (acc[1][2 * hi] + acc[1][2 * hi + 1]) * inv;
-                    const uint32_t row = out0 + g + 8u * hi;
-                    float a;
-                    if (p.weight_after_down) {
-                        a = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
-                    } else {
-                        double gd = (double)gv, ud = (double)uv;
-                        if (limit > 0.f) {
-                            gd = fmin(gd, (double)limit);
-                            ud = fmin(fmax(ud, -(double)limit), (double)limit);
-                        }
-                        double v = gd / (1.0 + exp(-gd)) * ud;
-                        if (!shared) v *= (double)p.pair_weight[pair];
-                        a = (float)v;
-                    }
-                    p.act[(size_t)pair * p.I + row] = a;
-                    atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < mma::kTiles; ++i)
-#pragma unroll
-                    for (int hi = 0; hi < 2; ++hi) {
-                        const uint32_t row = out0 + 16u * i + g + 8u * hi;
-                        p.y[(size_t)pair * p.H + row] = (acc[i][2 * hi] + acc[i][2 * hi + 1]) * inv;
-                    }
-            }
-        }
-        __syncthreads();
-    }
-    }
-}
-
-// Row groups per CTA for a launch: the widest shape that still gives every CTA several items.
-static uint32_t pick_row_groups(uint32_t T, uint32_t k, uint32_t E, uint32_t rows, uint32_t warp_rows,
-                                uint32_t K, unsigned grid) {
-    // tuning override: VLB_ROW_GROUPS=1|2|4|8 forces the CTA shape
-    if (const char* env = getenv("VLB_ROW_GROUPS")) {
-        const uint32_t rg = (uint32_t)atoi(env);
-        if ((rg == 1 || rg == 2 || rg == 4 || rg == 8) && (K / (8u / rg)) % 256u == 0) return rg;
-    }
-    const uint32_t units = (T * k < E ? T * k : E) + (T + kUnitTokens - 1) / kUnitTokens;
-    for (uint32_t rg = 8; rg > 1; rg >>= 1) {
-        const uint64_t items = (uint64_t)units * (rows / (warp_rows * rg));
-        if ((K / (8u / rg)) % 256u == 0 && items >= 2ull * grid) return rg;
-    }
-    return 1;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1174,11 +991,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     if (p.has_mma && p.prefill) {
         if ((e = launch_prefill_gateup(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     } else if (p.has_mma) {
-        const size_t mg_smem = kMmaTabBytes + (size_t)8u * p.H * 2u + kMmaRedBytes;
-        if ((e = set_smem_once(expert_mma_kernel<true>, mg_smem)) != cudaSuccess) return e;
-        expert_mma_kernel<true><<<grid, 256, mg_smem, s>>>(
-            p, pick_row_groups(p.T, p.k, p.E, p.I, 16u, p.H, grid));
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_decode_gateup(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     }
     if (ev) cudaEventRecord(ev[3], s);
     const size_t dn_smem = kGridSmemBytes + (size_t)kUnitTokens * p.I * sizeof(float);
@@ -1188,11 +1001,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     if (p.has_mma && p.prefill) {
         if ((e = launch_prefill_down(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     } else if (p.has_mma) {
-        const size_t md_smem = kMmaTabBytes + (size_t)8u * p.I * 2u + kMmaRedBytes;
-        if ((e = set_smem_once(expert_mma_kernel<false>, md_smem)) != cudaSuccess) return e;
-        expert_mma_kernel<false><<<grid, 256, md_smem, s>>>(
-            p, pick_row_groups(p.T, p.k, p.E, p.H, 32u, p.I, grid));
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_decode_down(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     }
     if (ev) cudaEventRecord(ev[4], s);
     dim3 cg((p.H / 4 + 255) / 256, rows_grid(p.T));

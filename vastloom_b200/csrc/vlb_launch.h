@@ -37,6 +37,10 @@ cudaError_t launch_prefill_plan(const MoeParams& p, cudaStream_t s);
 cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_t s);
 cudaError_t launch_prefill_down(const MoeParams& p, unsigned grid, cudaStream_t s);
 cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s);
+// Decode path (vlb_decode.cu): IQ2_XXS / Q8_0 expert products on mma.sync fed by a bulk-copy ring,
+// one CTA per SM.
+cudaError_t launch_decode_gateup(const MoeParams& p, unsigned n_sms, cudaStream_t s);
+cudaError_t launch_decode_down(const MoeParams& p, unsigned n_sms, cudaStream_t s);
 // Expert-parallel helpers (vlb_ep.cu)
 cudaError_t launch_ep_validate(const uint32_t* idx, size_t n, uint32_t E, uint32_t* flag, cudaStream_t s);
 cudaError_t launch_ep_gather(const uint32_t* pair_token, const uint32_t* pair_slot, const uint32_t* idx,
