@@ -366,7 +366,7 @@ def run_ep(args, dev, rank, world, local_rank):
         "config": {"workload": f"cfg4-ep-zipf-T{T}x{world}", "hidden": spec.hidden,
                    "intermediate": spec.intermediate, "experts": spec.experts, "experts_per_gpu": spec.experts // world,
                    "top_k": spec.top_k, "tokens_per_gpu": T, "zipf_s": spec.zipf_s,
-                   "exchange": "NCCL all-to-all (rows f32, expert ids, weights), results back",
+                   "exchange": "NCCL all-to-all: fp16 rows + (expert, weight, max|x|) words out, f32 results back",
                    "expert_path": "tensor-core prefill kernels on the received rows"},
         "timing": "CUDA events on the library stream around each step, max over ranks",
         "load_imbalance": {"experts_ms_max": round(ex_max, 4), "experts_ms_min": round(ex_min, 4),

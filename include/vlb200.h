@@ -208,8 +208,18 @@ uint32_t vlb_layer_prefill_tokens(vlb_handle* h, vlb_layer* layer);
 int vlb_layer_forward_routes_device(vlb_handle* h, vlb_layer* layer, const float* x_dev,
                                     const uint32_t* idx_dev, const float* weights_dev, uint32_t T,
                                     float* out_dev, void* stream);
+/* Forward of half rows with one route each (a layer of top_k 1 whose experts are IQ2_XXS /
+ * Q8_0, hidden % 8 == 0): rows_dev fp16 [T x H] = fp16(x * 2^e) with 2^e the power of two that
+ * brings the row's max|x| into [2^14, 2^15), meta_dev u32 [T x 3] = (expert id, route weight as
+ * f32 bits, max|x| as f32 bits), as vlb_ep_plan_half_device produces them. Always the tensor-core
+ * prefill path (its operands are these rows; 2e-2 contract); out_dev f32 [T x H]. No counterpart
+ * in the reference, whose expert-parallel exchange is not part of this path: it is the receiving
+ * side of the half-row exchange below. Enqueued on `stream`. */
+int vlb_layer_forward_rows_half_device(vlb_handle* h, vlb_layer* layer, const uint16_t* rows_dev,
+                                       const uint32_t* meta_dev, uint32_t T, float* out_dev,
+                                       void* stream);
 /* Synchronises `stream` and reports the error bits the layer's last device forward left (hash
- * token id out of its table, out-of-range expert, unnormalisable weights, prefill pipeline
+ * token id out of its table, out-of-range expert, unnormalisable weights, expert-kernel pipeline
  * timeout), as vlb_layer_forward does for the host form. */
 int vlb_layer_status(vlb_handle* h, vlb_layer* layer, void* stream);
 
@@ -229,6 +239,16 @@ int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx_dev, const float* weig
                        uint32_t* offsets_dev, uint32_t* offsets_host, float* send_x_dev,
                        uint32_t* send_expert_dev, float* send_weight_dev, uint32_t* elem_row_dev,
                        void* stream);
+/* The same plan with half rows for the exchange (half the bytes of f32 rows): send_rows_dev fp16
+ * [T*k x H] in plan order, send_meta_dev u32 [T*k x 3] = (local expert id, route weight bits,
+ * token max|x| bits), and the rank's own tokens for its shared expert, own_rows_dev fp16 [T x H]
+ * with own_meta_dev [T x 3] = (experts_per_rank, 1.0f bits, max|x| bits): the inputs of
+ * vlb_layer_forward_rows_half_device on the receiving rank. H % 8 == 0. */
+int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx_dev, const float* weights_dev, uint32_t T,
+                            uint32_t k, uint32_t E, uint32_t experts_per_rank, const float* x_dev, uint32_t H,
+                            void* ws_dev, uint32_t* offsets_dev, uint32_t* offsets_host,
+                            uint16_t* send_rows_dev, uint32_t* send_meta_dev, uint32_t* elem_row_dev,
+                            uint16_t* own_rows_dev, uint32_t* own_meta_dev, void* stream);
 /* Combine on the source rank after the return exchange: out[t] = sum over its k slots of
  * y_rows_dev[elem_row_dev[t * k + slot]] (slot order) + shared_rows_dev[t] (NULL: none). */
 int vlb_ep_combine_device(vlb_handle* h, const float* y_rows_dev, const uint32_t* elem_row_dev,

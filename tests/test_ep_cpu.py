@@ -59,12 +59,24 @@ class NumpyEpOps:
         self.epr = self.spec.experts // world
 
     def empty(self, shape, kind):
-        return torch.zeros(shape, dtype={"f32": torch.float64, "i32": torch.int32}[kind])
+        return torch.zeros(shape, dtype={"f32": torch.float64, "i32": torch.int32, "rows": torch.float64,
+                                         "meta": torch.float64}[kind])
 
-    def sync_time(self):
+    def mark(self):
         import time
 
         return time.perf_counter()
+
+    def elapsed(self, marks):
+        return [marks[i + 1] - marks[i] for i in range(len(marks) - 1)]
+
+    def comm_scope(self):
+        import contextlib
+
+        return contextlib.nullcontext()
+
+    def check(self):
+        pass
 
     def reserve_group(self, rows):
         pass
@@ -79,9 +91,9 @@ class NumpyEpOps:
         flat = idx.reshape(-1).astype(np.int64)
         order = np.argsort(flat, kind="stable")  # expert ascending, then element (token, slot)
         n = flat.size
-        b.send_x[:n] = torch.from_numpy(x.numpy()[order // k].astype(np.float64))
-        b.send_expert[:n] = torch.from_numpy((flat[order] % epr).astype(np.int32))
-        b.send_w[:n] = torch.from_numpy(w.reshape(-1)[order].astype(np.float64))
+        b.send_rows[:n] = torch.from_numpy(x.numpy()[order // k].astype(np.float64))
+        b.send_meta[:n, 0] = torch.from_numpy((flat[order] % epr).astype(np.float64))
+        b.send_meta[:n, 1] = torch.from_numpy(w.reshape(-1)[order].astype(np.float64))
         rows = np.empty(n, np.int32)
         rows[order] = np.arange(n, dtype=np.int32)
         b.elem_row[:n] = torch.from_numpy(rows)
@@ -89,16 +101,16 @@ class NumpyEpOps:
         return np.concatenate([[0], np.cumsum(counts)]).astype(np.uint32)
 
     def append_shared_rows(self, b, R, x, T, epr):
-        b.group_x[R:R + T] = torch.from_numpy(x.numpy().astype(np.float64))
-        b.group_idx[R:R + T] = epr
-        b.group_w[R:R + T] = 1.0
+        b.group_rows[R:R + T] = torch.from_numpy(x.numpy().astype(np.float64))
+        b.group_meta[R:R + T, 0] = epr
+        b.group_meta[R:R + T, 1] = 1.0
 
     def group_forward(self, b, rows):
         lo = self.rank * self.epr
         for r in range(rows):
-            e = int(b.group_idx[r])
+            e = int(b.group_meta[r, 0])
             mats = self.ex.shared if e == self.epr else self.ex.w[lo + e]
-            b.group_y[r] = torch.from_numpy(self.ex.apply(mats, b.group_x[r].numpy(), float(b.group_w[r])))
+            b.group_y[r] = torch.from_numpy(self.ex.apply(mats, b.group_rows[r].numpy(), float(b.group_meta[r, 1])))
 
     def combine(self, b, T, k, R):
         y = b.back_y.numpy()

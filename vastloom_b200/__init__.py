@@ -137,7 +137,7 @@ EXPORTS = (
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
     "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_layer_set_prefill_tokens "
     "vlb_layer_prefill_tokens vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
-    "vlb_ep_plan_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
+    "vlb_ep_plan_device vlb_ep_plan_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
 ).split()
 
 
@@ -188,6 +188,8 @@ def load_library() -> C.CDLL:
         "vlb_ep_workspace_bytes": (SZ, [U32, U32, U32]),
         "vlb_ep_plan_device": (I, [P, P, P, U32, U32, U32, U32, P, U32, P, P, P, P, P, P, P, P]),
         "vlb_ep_combine_device": (I, [P, P, P, U32, U32, P, U32, P, P]),
+        "vlb_ep_plan_half_device": (I, [P, P, P, U32, U32, U32, U32, P, U32, P, P, P, P, P, P, P, P, P]),
+        "vlb_layer_forward_rows_half_device": (I, [P, P, P, P, U32, P, P]),
         "vlb_layer_prefill_tokens": (U32, [P, P]),
         "vlb_route_device": (I, [P, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
         "vlb_route_device_noalloc": (I, [I, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
@@ -542,6 +544,12 @@ class MoeLayer:
         self.dev._check(self.dev.lib.vlb_layer_forward_routes_device(
             self.dev.h, self.ptr, C.c_void_p(x_ptr), C.c_void_p(idx_ptr), C.c_void_p(w_ptr), T,
             C.c_void_p(out_ptr), C.c_void_p(stream or None)))
+
+    def forward_rows_half_device(self, rows_ptr: int, meta_ptr: int, T: int, out_ptr: int, stream: int = 0) -> None:
+        """Forward of fp16 rows with one route each (meta u32 [T x 3]: expert, weight bits, max|x| bits)."""
+        self.dev._check(self.dev.lib.vlb_layer_forward_rows_half_device(
+            self.dev.h, self.ptr, C.c_void_p(rows_ptr), C.c_void_p(meta_ptr), T, C.c_void_p(out_ptr),
+            C.c_void_p(stream or None)))
 
     def status(self, stream: int = 0) -> None:
         """Raises the error the last device forward flagged (synchronises `stream`)."""

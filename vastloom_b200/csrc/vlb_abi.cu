@@ -756,10 +756,11 @@ static uint32_t prefill_threshold(const vlb_layer* L) {
 // stream) gets the same kernels launched directly.
 static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uint32_t* tok,
                           const float* logits, uint32_t T, float* out, cudaStream_t s,
-                          const uint32_t* routes_idx = nullptr, const float* routes_w = nullptr) {
+                          const uint32_t* routes_idx = nullptr, const float* routes_w = nullptr,
+                          const uint16_t* x_half = nullptr, const uint32_t* routes_meta = nullptr) {
     if (T == 0 || T > L->desc.max_tokens)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "token count is zero or above the layer's max_tokens");
-    if (L->desc.hash_routing && !tok)
+    if (L->desc.hash_routing && !tok && !routes_idx && !x_half)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs token ids");
     MoeParams p = L->p;
     p.T = T;
@@ -768,15 +769,22 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.logits_in = logits;
     p.routes_idx = routes_idx;
     p.routes_w = routes_w;
+    p.x_half = reinterpret_cast<const __half*>(x_half);
+    p.routes_meta = routes_meta;
     p.out = out;
     p.grids = h->grids();
-    p.prefill = T >= prefill_threshold(L) ? 1 : 0;
+    // half rows carry fp16 operands already: only the tensor-core prefill path consumes them
+    p.prefill = (x_half || T >= prefill_threshold(L)) ? 1 : 0;
+    const bool one_route = (routes_idx || x_half) && p.k == 1;
+    p.direct_out = one_route && !p.has_shared && !p.weight_after_down && !p.has_legacy ? 1 : 0;
     const size_t zero_bytes = 32 + (size_t)T * 4;  // counters and per-token max|x|
     L->last_T = T;
     L->last_logits_given = logits != nullptr;
-    if (L->profiling) {
+    // prefill-size forwards are long enough that launching directly costs nothing, and their
+    // token counts vary from call to call (a graph is keyed by T): no capture for them
+    if (L->profiling || p.prefill) {
         VLB_CUDA(h, cudaMemsetAsync(p.counters, 0, zero_bytes, s));
-        VLB_CUDA(h, launch_moe(p, s, L->ev));
+        VLB_CUDA(h, launch_moe(p, s, L->profiling ? L->ev : nullptr));
         return VLB_OK;
     }
     const void* key[7] = {x, tok, logits, out, s, routes_idx, routes_w};
@@ -824,6 +832,16 @@ int vlb_layer_forward_routes_device(vlb_handle* h, vlb_layer* L, const float* x,
     VLB_LOCK(h);
     if (!L || !x || !out || !idx || !weights) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
     return forward_locked(h, L, x, nullptr, nullptr, T, out, h->pick(stream), idx, weights);
+}
+
+int vlb_layer_forward_rows_half_device(vlb_handle* h, vlb_layer* L, const uint16_t* rows, const uint32_t* meta,
+                                       uint32_t T, float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!L || !rows || !meta || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
+    if (L->desc.top_k != 1 || L->p.has_legacy || L->desc.hidden % 8)
+        return h->fail(VLB_ERR_UNSUPPORTED,
+                       "half-row forwards need one route per row, tensor-core expert formats and hidden % 8 == 0");
+    return forward_locked(h, L, nullptr, nullptr, nullptr, T, out, h->pick(stream), nullptr, nullptr, rows, meta);
 }
 
 int vlb_layer_status(vlb_handle* h, vlb_layer* L, void* stream) {
@@ -994,9 +1012,13 @@ int vlb_rms_norm_device(vlb_handle* h, const float* x, const float* w, uint32_t 
 
 // ---- expert parallelism (configuration 4) ------------------------------------------------------
 
+// Plan workspace: flag | pair_token [n] | pair_slot [n] | per-chunk counts | sorted weights [n] |
+// per-token max|x| [T] (the last two only used by the half-row plan).
+static size_t ep_round(size_t b) { return (b + 255) / 256 * 256; }
+
 size_t vlb_ep_workspace_bytes(uint32_t T, uint32_t k, uint32_t E) {
     const size_t n = (size_t)T * k, chunks = (n + 1023) / 1024;
-    return 256 + 2 * ((n * 4 + 255) / 256 * 256) + (chunks * E * 4 + 255) / 256 * 256;
+    return 256 + 3 * ep_round(n * 4) + ep_round(chunks * E * 4) + ep_round((size_t)T * 4);
 }
 
 int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx, const float* weights, uint32_t T, uint32_t k,
@@ -1038,6 +1060,56 @@ int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx, const float* weights,
     VLB_CUDA(h, launch_stable_sort(p, s));
     VLB_CUDA(h, launch_ep_gather(pair_token, pair_slot, idx, (uint32_t)n, k, experts_per_rank, x, H, send_x,
                                  send_expert, s));
+    if (n == 0) VLB_CUDA(h, cudaMemsetAsync(offsets, 0, (E + 2) * 4, s));
+    VLB_CUDA(h, cudaMemcpyAsync(offsets_host, offsets, (E + 1) * 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    return VLB_OK;
+}
+
+int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx, const float* weights, uint32_t T, uint32_t k,
+                            uint32_t E, uint32_t experts_per_rank, const float* x, uint32_t H, void* ws,
+                            uint32_t* offsets, uint32_t* offsets_host, uint16_t* send_rows, uint32_t* send_meta,
+                            uint32_t* elem_row, uint16_t* own_rows, uint32_t* own_meta, void* stream) {
+    VLB_LOCK(h);
+    if (!idx || !weights || !x || !ws || !offsets || !offsets_host || !send_rows || !send_meta || !elem_row ||
+        !own_rows || !own_meta || k == 0 || E == 0 || E > 512 || H == 0 || H % 8 || experts_per_rank == 0 ||
+        E % experts_per_rank)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid expert-parallel plan argument");
+    cudaStream_t s = h->pick(stream);
+    const size_t n = (size_t)T * k, chunks = (n + 1023) / 1024;
+    char* w = static_cast<char*>(ws);
+    uint32_t* flag = reinterpret_cast<uint32_t*>(w);
+    uint32_t* pair_token = reinterpret_cast<uint32_t*>(w + 256);
+    uint32_t* pair_slot = reinterpret_cast<uint32_t*>(w + 256 + ep_round(n * 4));
+    uint32_t* counts = reinterpret_cast<uint32_t*>(w + 256 + 2 * ep_round(n * 4));
+    float* sorted_w = reinterpret_cast<float*>(w + 256 + 2 * ep_round(n * 4) + ep_round(chunks * E * 4));
+    uint32_t* xmax = reinterpret_cast<uint32_t*>(w + 256 + 3 * ep_round(n * 4) + ep_round(chunks * E * 4));
+    // expert ids are validated before the counting sort indexes anything with them
+    uint32_t bad = 0;
+    VLB_CUDA(h, cudaMemsetAsync(flag, 0, 4, s));
+    VLB_CUDA(h, launch_ep_validate(idx, n, E, flag, s));
+    VLB_CUDA(h, cudaMemcpyAsync(&bad, flag, 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
+    if (bad) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
+    VLB_CUDA(h, launch_prescale(x, T, H, xmax, nullptr, s));
+    MoeParams p{};
+    p.T = T;
+    p.k = k;
+    p.E = E;
+    p.idx = const_cast<uint32_t*>(idx);
+    p.weights = const_cast<float*>(weights);
+    p.offsets = offsets;
+    p.pair_token = pair_token;
+    p.pair_slot = pair_slot;
+    p.pair_weight = sorted_w;
+    p.combine_pairs = elem_row;
+    p.disp_counts = counts;
+    p.has_shared = 0;
+    VLB_CUDA(h, launch_stable_sort(p, s));
+    VLB_CUDA(h, launch_ep_gather_half(pair_token, pair_slot, idx, sorted_w, (uint32_t)n, k, experts_per_rank, x,
+                                      xmax, H, reinterpret_cast<__half*>(send_rows), send_meta, s));
+    VLB_CUDA(h, launch_ep_own_rows(x, xmax, T, H, experts_per_rank, reinterpret_cast<__half*>(own_rows), own_meta,
+                                   s));
     if (n == 0) VLB_CUDA(h, cudaMemsetAsync(offsets, 0, (E + 2) * 4, s));
     VLB_CUDA(h, cudaMemcpyAsync(offsets_host, offsets, (E + 1) * 4, cudaMemcpyDeviceToHost, s));
     VLB_CUDA(h, cudaStreamSynchronize(s));

@@ -525,13 +525,14 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
                         atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
                     }
                 } else {
+                    float* yrow = p.direct_out ? p.out + (size_t)p.pair_token[pair] * p.H : p.y + (size_t)pair * p.H;
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
                         if (!(i ? it.valid1 : it.valid0)) continue;
 #pragma unroll
                         for (int hi = 0; hi < 2; ++hi) {
                             const uint32_t row = (i ? it.tile1 : it.tile0) * kTileRows + rt + gq + 8u * hi;
-                            if (row < p.H) p.y[(size_t)pair * p.H + row] = (acc[i][2 * hi] + acc[i][2 * hi + 1]) * inv;
+                            if (row < p.H) yrow[row] = (acc[i][2 * hi] + acc[i][2 * hi + 1]) * inv;
                         }
                     }
                 }

@@ -4,9 +4,11 @@
 // global expert id (== by destination rank, experts being sharded in contiguous ranges) with the
 // same stable counting sort as the single-GPU dispatch, gathers their x rows, and after the
 // return exchange sums each token's rows and its shared-expert row.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "vlb_launch.h"
+#include "vlb_mma.cuh"
 
 namespace vlb {
 namespace {
@@ -28,6 +30,69 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const uint32_t* __restri
     const float4* src = reinterpret_cast<const float4*>(x + (size_t)t * H);
     float4* dst = reinterpret_cast<float4*>(send_x + (size_t)pos * H);
     for (uint32_t c = threadIdx.x; c < H / 4u; c += blockDim.x) dst[c] = src[c];
+}
+
+// fp16 rows for the exchange: send row pos = fp16(x[token] * s_token) (s the power of two of the
+// token's max|x|: exactly the row the receiver's tensor-core path would build from the f32 row),
+// meta = (local expert id, route weight bits, max|x| bits). One CTA per send row, 8 columns a
+// thread.
+__global__ void __launch_bounds__(256) ep_gather_half_kernel(const uint32_t* __restrict__ pair_token,
+                                                             const uint32_t* __restrict__ pair_slot,
+                                                             const uint32_t* __restrict__ idx,
+                                                             const float* __restrict__ sorted_w, uint32_t k,
+                                                             uint32_t epr, const float* __restrict__ x,
+                                                             const uint32_t* __restrict__ xmax, uint32_t H,
+                                                             __half* __restrict__ rows, uint32_t* __restrict__ meta) {
+    const uint32_t pos = blockIdx.x;
+    const uint32_t t = pair_token[pos];
+    const uint32_t xm = xmax[t];
+    if (threadIdx.x == 0) {
+        meta[3u * pos] = idx[(size_t)t * k + pair_slot[pos]] % epr;
+        meta[3u * pos + 1u] = __float_as_uint(sorted_w[pos]);
+        meta[3u * pos + 2u] = xm;
+    }
+    const float s = mma::prescale_for(__uint_as_float(xm));
+    const float* src = x + (size_t)t * H;
+    __half* dst = rows + (size_t)pos * H;
+    for (uint32_t c = threadIdx.x * 8u; c < H; c += blockDim.x * 8u) {
+        const float4 a = *reinterpret_cast<const float4*>(src + c);
+        const float4 b = *reinterpret_cast<const float4*>(src + c + 4u);
+        const __half2 h0 = __floats2half2_rn(a.x * s, a.y * s), h1 = __floats2half2_rn(a.z * s, a.w * s);
+        const __half2 h2 = __floats2half2_rn(b.x * s, b.y * s), h3 = __floats2half2_rn(b.z * s, b.w * s);
+        uint4 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&h0);
+        o.y = *reinterpret_cast<const uint32_t*>(&h1);
+        o.z = *reinterpret_cast<const uint32_t*>(&h2);
+        o.w = *reinterpret_cast<const uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(dst + c) = o;
+    }
+}
+
+// The rank's own tokens as fp16 rows for its shared expert (local expert `epr`, weight 1).
+__global__ void __launch_bounds__(256) ep_own_rows_kernel(const float* __restrict__ x,
+                                                          const uint32_t* __restrict__ xmax, uint32_t H,
+                                                          uint32_t epr, __half* __restrict__ rows,
+                                                          uint32_t* __restrict__ meta) {
+    const uint32_t t = blockIdx.x;
+    const uint32_t xm = xmax[t];
+    if (threadIdx.x == 0) {
+        meta[3u * t] = epr;
+        meta[3u * t + 1u] = __float_as_uint(1.0f);
+        meta[3u * t + 2u] = xm;
+    }
+    const float s = mma::prescale_for(__uint_as_float(xm));
+    for (uint32_t c = threadIdx.x * 8u; c < H; c += blockDim.x * 8u) {
+        const float4 a = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
+        const float4 b = *reinterpret_cast<const float4*>(x + (size_t)t * H + c + 4u);
+        const __half2 h0 = __floats2half2_rn(a.x * s, a.y * s), h1 = __floats2half2_rn(a.z * s, a.w * s);
+        const __half2 h2 = __floats2half2_rn(b.x * s, b.y * s), h3 = __floats2half2_rn(b.z * s, b.w * s);
+        uint4 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&h0);
+        o.y = *reinterpret_cast<const uint32_t*>(&h1);
+        o.z = *reinterpret_cast<const uint32_t*>(&h2);
+        o.w = *reinterpret_cast<const uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(rows + (size_t)t * H + c) = o;
+    }
 }
 
 // out[t] = sum over slots of y[elem_row[t * k + slot]] (slot order), + shared[t]; rows strided over
@@ -71,6 +136,21 @@ cudaError_t launch_ep_gather(const uint32_t* pair_token, const uint32_t* pair_sl
                              uint32_t* send_expert, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     ep_gather_kernel<<<n, 256, 0, s>>>(pair_token, pair_slot, idx, k, epr, x, H, send_x, send_expert);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_gather_half(const uint32_t* pair_token, const uint32_t* pair_slot, const uint32_t* idx,
+                                  const float* sorted_w, uint32_t n, uint32_t k, uint32_t epr, const float* x,
+                                  const uint32_t* xmax, uint32_t H, __half* rows, uint32_t* meta, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    ep_gather_half_kernel<<<n, 256, 0, s>>>(pair_token, pair_slot, idx, sorted_w, k, epr, x, xmax, H, rows, meta);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_own_rows(const float* x, const uint32_t* xmax, uint32_t T, uint32_t H, uint32_t epr,
+                               __half* rows, uint32_t* meta, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    ep_own_rows_kernel<<<T, 256, 0, s>>>(x, xmax, H, epr, rows, meta);
     return cudaGetLastError();
 }
 

@@ -230,6 +230,10 @@ struct MoeParams {
     const float* logits_in;  // optional [T x E]
     const uint32_t* routes_idx;  // optional [T x k]: given routes (skip the router and top-k)
     const float* routes_w;       // [T x k] their weights
+    // optional half-row input (one route per row): rows fp16(x * 2^e) with, per row, meta
+    // [expert id, route weight bits, max|x| bits]; replaces x, routes_idx and routes_w
+    const __half* x_half;        // [T x H]
+    const uint32_t* routes_meta; // [T x 3]
     // workspace
     float* logits;           // [T x E]
     float* scores;           // [T x E]
@@ -252,6 +256,10 @@ struct MoeParams {
     uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
     uint32_t max_units;
     uint32_t* disp_counts;   // [ceil(T*k / 1024) x E]: per-chunk expert counts of the multi-CTA dispatch
+    // 1: a one-route-per-row forward (k = 1, given routes) without a shared expert whose route
+    // weight is applied before the down product: each row's output is its single expert's down
+    // product, so the down kernels write it straight to out[token] and no combine pass runs
+    int direct_out;
     // prefill (tensor-core grouped GEMM) path
     int prefill;             // 1: this forward runs the expert products on tcgen05 (fp16 operands)
     __half* xperm;           // [(T*k + T) x H]: pair p's token row, fp16(x * 2^e_t) (the token's xmax power of two)

@@ -512,6 +512,23 @@ __global__ void routes_copy_kernel(const uint32_t* __restrict__ idx, const float
     w_out[i] = w[i];
 }
 
+// Half-row input: one route per row from its meta words (expert, weight bits, max|x| bits); the
+// row's max|x| goes where the prescale kernel would have put it. Out-of-range ids as above.
+__global__ void routes_meta_kernel(const uint32_t* __restrict__ meta, uint32_t n, uint32_t E,
+                                   uint32_t* __restrict__ idx_out, float* __restrict__ w_out,
+                                   uint32_t* __restrict__ xmax, uint32_t* flags) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t e = meta[3u * i];
+    if (e >= E) {
+        atomicOr(flags, 2u);
+        e = 0;
+    }
+    idx_out[i] = e;
+    w_out[i] = __uint_as_float(meta[3u * i + 1u]);
+    xmax[i] = meta[3u * i + 2u];
+}
+
 // Small batches: the whole dispatch in one CTA (chunks of blockDim.x elements in order).
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(MoeParams p) {
     extern __shared__ uint32_t dsm[];
@@ -941,25 +958,33 @@ cudaError_t launch_route(const float* scores, const float* bias, const uint32_t*
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
     cudaError_t e;
     if (ev) cudaEventRecord(ev[0], s);
-    // routing: router projection (or supplied logits) -> scores -> top-k; or given routes
+    // routing: router projection (or supplied logits) -> scores -> top-k; or given routes; or
+    // half rows that arrive with their max|x| and one route each
     const bool given = p.routes_idx != nullptr;
-    token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(
-        p.x, p.T, p.H, p.xmax, (p.logits_in || given) ? nullptr : p.xd);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (given) {
-        const size_t n = (size_t)p.T * p.k;
-        routes_copy_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p.routes_idx, p.routes_w, n, p.E, p.idx,
-                                                                       p.weights, p.counters + 3);
+    if (p.x_half) {
+        routes_meta_kernel<<<(p.T + 255) / 256, 256, 0, s>>>(p.routes_meta, p.T, p.E, p.idx, p.weights, p.xmax,
+                                                             p.counters + 3);
         e = cudaGetLastError();
     } else {
-        if (p.logits_in) {
-            e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
+        token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(
+            p.x, p.T, p.H, p.xmax, (p.logits_in || given) ? nullptr : p.xd);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (given) {
+            const size_t n = (size_t)p.T * p.k;
+            routes_copy_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p.routes_idx, p.routes_w, n, p.E,
+                                                                           p.idx, p.weights, p.counters + 3);
+            e = cudaGetLastError();
         } else {
-            e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, p.router_partial, s);
+            if (p.logits_in) {
+                e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
+            } else {
+                e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, p.router_partial,
+                                  s);
+            }
+            if (e != cudaSuccess) return e;
+            e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
+                             p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
         }
-        if (e != cudaSuccess) return e;
-        e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
-                         p.hash_routing, p.route_scale, p.idx, p.weights, p.counters + 3, s);
     }
     if (e != cudaSuccess) return e;
     if (ev) cudaEventRecord(ev[1], s);
@@ -1004,9 +1029,11 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
         if ((e = launch_decode_down(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     }
     if (ev) cudaEventRecord(ev[4], s);
-    dim3 cg((p.H / 4 + 255) / 256, rows_grid(p.T));
-    combine_kernel<<<cg, 256, 0, s>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (!p.direct_out) {
+        dim3 cg((p.H / 4 + 255) / 256, rows_grid(p.T));
+        combine_kernel<<<cg, 256, 0, s>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
     if (ev) cudaEventRecord(ev[5], s);
     return cudaSuccess;
 }

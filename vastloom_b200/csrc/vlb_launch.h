@@ -46,6 +46,12 @@ cudaError_t launch_ep_validate(const uint32_t* idx, size_t n, uint32_t E, uint32
 cudaError_t launch_ep_gather(const uint32_t* pair_token, const uint32_t* pair_slot, const uint32_t* idx,
                              uint32_t n, uint32_t k, uint32_t epr, const float* x, uint32_t H, float* send_x,
                              uint32_t* send_expert, cudaStream_t s);
+// Half-row exchange: fp16 send rows + (expert, weight, max|x|) meta, and the own tokens' rows.
+cudaError_t launch_ep_gather_half(const uint32_t* pair_token, const uint32_t* pair_slot, const uint32_t* idx,
+                                  const float* sorted_w, uint32_t n, uint32_t k, uint32_t epr, const float* x,
+                                  const uint32_t* xmax, uint32_t H, __half* rows, uint32_t* meta, cudaStream_t s);
+cudaError_t launch_ep_own_rows(const float* x, const uint32_t* xmax, uint32_t T, uint32_t H, uint32_t epr,
+                               __half* rows, uint32_t* meta, cudaStream_t s);
 cudaError_t launch_ep_combine(const float* y, const uint32_t* elem_row, uint32_t T, uint32_t k,
                               const float* shared_rows, uint32_t H, float* out, cudaStream_t s);
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,

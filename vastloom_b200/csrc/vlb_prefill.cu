@@ -471,7 +471,8 @@ __device__ __forceinline__ void pf_epilogue_down(const MoeParams& p, uint32_t tm
             const uint32_t n = 8u * j + i;
             if (n < tile.count) {
                 const float inv = tok_inv[n] * inv_ps;
-                float* yr = p.y + (size_t)(tile.pair_begin + n) * p.H;
+                const uint32_t pair = tile.pair_begin + n;
+                float* yr = p.direct_out ? p.out + (size_t)p.pair_token[pair] * p.H : p.y + (size_t)pair * p.H;
                 yr[r0] = a[i] * inv;
                 yr[r1] = b[i] * inv;
             }
@@ -691,6 +692,17 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __rest
     }
 }
 
+// Pair-ordered fp16 activations from half-row input (already fp16(x * s_token)): a row copy.
+__global__ void __launch_bounds__(256) prefill_copy_rows_kernel(const __half* __restrict__ src,
+                                                                const uint32_t* __restrict__ pair_token, uint32_t rows,
+                                                                uint32_t width, __half* __restrict__ dst) {
+    const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 8u;
+    if (c >= width) return;
+    for (uint32_t pr = blockIdx.y; pr < rows; pr += gridDim.y)
+        *reinterpret_cast<uint4*>(dst + (size_t)pr * width + c) =
+            *reinterpret_cast<const uint4*>(src + (size_t)pair_token[pr] * width + c);
+}
+
 // fp16(act * s) rows with s the power of two of each row's max (act_max); 4 columns a thread.
 __global__ void __launch_bounds__(256) prefill_half_kernel(const float* __restrict__ src,
                                                            const uint32_t* __restrict__ rmax, uint32_t rows,
@@ -738,8 +750,12 @@ cudaError_t launch_prefill_plan(const MoeParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_prefill_gateup(const MoeParams& p, unsigned grid, cudaStream_t s) {
-    prefill_gather_kernel<<<dim3((p.H / 4 + 255) / 256, rows_grid(pairs_of(p))), 256, 0, s>>>(
-        p.x, p.pair_token, p.xmax, pairs_of(p), p.H, p.xperm);
+    if (p.x_half)
+        prefill_copy_rows_kernel<<<dim3((p.H / 8 + 255) / 256, rows_grid(pairs_of(p))), 256, 0, s>>>(
+            p.x_half, p.pair_token, pairs_of(p), p.H, p.xperm);
+    else
+        prefill_gather_kernel<<<dim3((p.H / 4 + 255) / 256, rows_grid(pairs_of(p))), 256, 0, s>>>(
+            p.x, p.pair_token, p.xmax, pairs_of(p), p.H, p.xperm);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if ((e = pf_smem_once(prefill_gemm_kernel<true>, kPfSmemBytes)) != cudaSuccess) return e;

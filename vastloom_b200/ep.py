@@ -21,7 +21,6 @@ TorchComm wraps torch.distributed, NCCL on GPUs, gloo on CPU tensors).
 from __future__ import annotations
 
 import ctypes as C
-import time
 from dataclasses import dataclass
 from typing import Optional
 
@@ -73,21 +72,21 @@ class TorchComm:
 
 @dataclass
 class EpBuffers:
-    send_x: object
-    send_expert: object
-    send_w: object
-    elem_row: object
-    group_x: object
-    group_idx: object
-    group_w: object
-    group_y: object
-    back_y: object
-    out: object
+    send_rows: object   # [T*k, H] activation rows in send (plan) order; the ops choose the format
+    send_meta: object   # [T*k, 3] per row: local expert id, route weight, row scale information
+    elem_row: object    # [T*k] element (t * k + slot) -> send row
+    group_rows: object  # [capacity, H] received rows, then this rank's own rows for the shared expert
+    group_meta: object  # [capacity, 3]
+    group_y: object     # [capacity, H] f32 expert outputs of the group rows
+    back_y: object      # [T*k, H] f32 results returned to this rank, in send order
+    out: object         # [T, H] f32
 
 
 class ExpertParallelLayer:
     """One rank's share of an expert-parallel MoE layer. `ops` provides route / plan / group
-    forward / combine on this rank's device (or host, for the CPU tests); `comm` the exchange."""
+    forward / combine on this rank's device (or host, for the CPU tests); `comm` the exchange.
+    Rows travel in the format `ops` allocates for them (fp16 with per-row scale information on
+    GPUs: half the bytes of f32, and exactly the operands the tensor-core expert kernels use)."""
 
     def __init__(self, ops, comm, experts: int, top_k: int, hidden: int, max_tokens: int):
         if experts % comm.world:
@@ -101,12 +100,12 @@ class ExpertParallelLayer:
         self.max_tokens = max_tokens
         n = max_tokens * top_k
         self.buf = EpBuffers(
-            send_x=ops.empty((n, hidden), "f32"), send_expert=ops.empty((n,), "i32"),
-            send_w=ops.empty((n,), "f32"), elem_row=ops.empty((n,), "i32"),
-            group_x=None, group_idx=None, group_w=None, group_y=None,
+            send_rows=ops.empty((n, hidden), "rows"), send_meta=ops.empty((n, 3), "meta"),
+            elem_row=ops.empty((n,), "i32"), group_rows=None, group_meta=None, group_y=None,
             back_y=ops.empty((n, hidden), "f32"), out=ops.empty((max_tokens, hidden), "f32"))
         self.capacity = 0  # group rows the receive side is sized for (grown on demand)
-        self.last = {}
+        self._marks = None
+        self._rows = (0, 0)
 
     def _reserve(self, rows: int) -> None:
         """Receive-side buffers for `rows` group rows (received pairs + own shared rows). The worst
@@ -116,42 +115,56 @@ class ExpertParallelLayer:
             return
         cap = int(rows * 1.25) + 16
         b, ops = self.buf, self.ops
-        b.group_x = ops.empty((cap, self.H), "f32")
-        b.group_idx = ops.empty((cap,), "i32")
-        b.group_w = ops.empty((cap,), "f32")
+        b.group_rows = ops.empty((cap, self.H), "rows")
+        b.group_meta = ops.empty((cap, 3), "meta")
         b.group_y = ops.empty((cap, self.H), "f32")
         ops.reserve_group(cap)
         self.capacity = cap
 
     def forward(self, x, logits, T: int):
         """x [T, H] f32 and logits [T, E] f32 of this rank's tokens (in the ops' memory); returns
-        out [T, H]. Records the phase times of this rank in self.last."""
+        out [T, H]. The phase boundaries are marked on the device (no host synchronisation beyond
+        the two count read-backs the exchange sizes need); `last` reads them afterwards."""
         if T > self.max_tokens:
             raise ValueError("more tokens than the layer was sized for")
         ops, comm, b, k = self.ops, self.comm, self.buf, self.k
         n = T * k
-        t0 = time.perf_counter()
+        m0 = ops.mark()
         idx, w = ops.route(logits, T)
         offsets = ops.plan(idx, w, x, T, self.epr, b)
         send_counts = owner_counts(offsets, comm.world, self.epr)
-        recv_counts = comm.exchange_counts(send_counts, b.send_x)
+        with ops.comm_scope():
+            recv_counts = comm.exchange_counts(send_counts, b.out)
         R = sum(recv_counts)
         self._reserve(R + T)
-        t1 = ops.sync_time()
-        comm.all_to_all(b.group_x[:R], b.send_x[:n], recv_counts, send_counts)
-        comm.all_to_all(b.group_idx[:R], b.send_expert[:n], recv_counts, send_counts)
-        comm.all_to_all(b.group_w[:R], b.send_w[:n], recv_counts, send_counts)
+        m1 = ops.mark()
+        with ops.comm_scope():
+            comm.all_to_all(b.group_rows[:R], b.send_rows[:n], recv_counts, send_counts)
+            comm.all_to_all(b.group_meta[:R], b.send_meta[:n], recv_counts, send_counts)
         ops.append_shared_rows(b, R, x, T, self.epr)
-        t2 = ops.sync_time()
+        m2 = ops.mark()
         ops.group_forward(b, R + T)
-        t3 = ops.sync_time()
-        comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts)
-        t4 = ops.sync_time()
+        m3 = ops.mark()
+        with ops.comm_scope():
+            comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts)
+        m4 = ops.mark()
         out = ops.combine(b, T, k, R)
-        t5 = ops.sync_time()
-        self.last = {"plan_s": t1 - t0, "dispatch_s": t2 - t1, "experts_s": t3 - t2, "return_s": t4 - t3,
-                     "combine_s": t5 - t4, "received_rows": R, "sent_rows": n}
+        m5 = ops.mark()
+        ops.check()
+        self._marks = (m0, m1, m2, m3, m4, m5)
+        self._rows = (R, n)
         return out
+
+    @property
+    def last(self) -> dict:
+        """Phase times (seconds) and row counts of the last forward on this rank."""
+        if not getattr(self, "_marks", None):
+            return {}
+        t = self.ops.elapsed(self._marks)
+        names = ("plan_s", "dispatch_s", "experts_s", "return_s", "combine_s")
+        d = {name: t[i] for i, name in enumerate(names)}
+        d["received_rows"], d["sent_rows"] = self._rows
+        return d
 
 
 class DeviceEpOps:
@@ -184,6 +197,9 @@ class DeviceEpOps:
         self.offsets_host = np.zeros(experts + 1, np.uint32)
         self.ws = torch.empty((int(self.lib.vlb_ep_workspace_bytes(max_tokens, top_k, experts)),),
                               dtype=torch.uint8, device=self.device)
+        # this rank's own tokens as half rows for its shared expert (written by the plan)
+        self.own_rows = torch.empty((max_tokens, hidden), dtype=torch.float16, device=self.device)
+        self.own_meta = torch.empty((max_tokens, 3), dtype=torch.int32, device=self.device)
 
     def reserve_group(self, rows: int) -> None:
         """(Re)creates the local group layer with a workspace for `rows` given-route rows."""
@@ -208,17 +224,32 @@ class DeviceEpOps:
                 self.dev.release_matrix(mtx)
 
     def empty(self, shape, kind):
-        dt = {"f32": self.torch.float32, "i32": self.torch.int32}[kind]
+        # rows travel as fp16(x * 2^e); meta rows are u32 (expert, weight bits, max|x| bits)
+        dt = {"f32": self.torch.float32, "i32": self.torch.int32, "rows": self.torch.float16,
+              "meta": self.torch.int32}[kind]
         return self.torch.empty(shape, dtype=dt, device=self.device)
 
     @staticmethod
     def _p(t):
         return C.c_void_p(t.data_ptr())
 
-    def sync_time(self) -> float:
-        self.torch.cuda.current_stream(self.device).synchronize()
-        self.stream.synchronize()
-        return time.perf_counter()
+    def mark(self):
+        """A phase boundary: an event on the library stream (no host synchronisation)."""
+        ev = self.torch.cuda.Event(enable_timing=True)
+        ev.record(self.stream)
+        return ev
+
+    def elapsed(self, marks) -> list:
+        marks[-1].synchronize()
+        return [marks[i].elapsed_time(marks[i + 1]) / 1000.0 for i in range(len(marks) - 1)]
+
+    def comm_scope(self):
+        """The collectives run on the library stream, ordered with the kernels without host syncs."""
+        return self.torch.cuda.stream(self.stream)
+
+    def check(self) -> None:
+        """Raises the error the step's group forward flagged (one synchronisation per step)."""
+        self.group.status(stream=self.dev.stream)
 
     def route(self, logits, T):
         self.dev._check(self.lib.vlb_route_device(
@@ -227,24 +258,21 @@ class DeviceEpOps:
         return self.idx, self.w
 
     def plan(self, idx, w, x, T, epr, b):
-        self.dev._check(self.lib.vlb_ep_plan_device(
+        self.dev._check(self.lib.vlb_ep_plan_half_device(
             self.dev.h, self._p(idx), self._p(w), T, self.k, self.E, epr, self._p(x), self.H, self._p(self.ws),
-            self._p(self.offsets), self.offsets_host.ctypes.data_as(C.c_void_p), self._p(b.send_x),
-            self._p(b.send_expert), self._p(b.send_w), self._p(b.elem_row), C.c_void_p(self.dev.stream)))
+            self._p(self.offsets), self.offsets_host.ctypes.data_as(C.c_void_p), self._p(b.send_rows),
+            self._p(b.send_meta), self._p(b.elem_row), self._p(self.own_rows), self._p(self.own_meta),
+            C.c_void_p(self.dev.stream)))
         return self.offsets_host
 
     def append_shared_rows(self, b, R, x, T, epr):
         with self.torch.cuda.stream(self.stream):
-            b.group_x[R:R + T].copy_(x[:T])
-            b.group_idx[R:R + T].fill_(epr)
-            b.group_w[R:R + T].fill_(1.0)
+            b.group_rows[R:R + T].copy_(self.own_rows[:T])
+            b.group_meta[R:R + T].copy_(self.own_meta[:T])
 
     def group_forward(self, b, rows):
-        # the collectives ran on torch's stream; the library's stream must see their results
-        self.torch.cuda.current_stream(self.device).synchronize()
-        self.group.forward_routes_device(b.group_x.data_ptr(), b.group_idx.data_ptr(), b.group_w.data_ptr(), rows,
-                                         b.group_y.data_ptr(), stream=self.dev.stream)
-        self.group.status(stream=self.dev.stream)
+        self.group.forward_rows_half_device(b.group_rows.data_ptr(), b.group_meta.data_ptr(), rows,
+                                            b.group_y.data_ptr(), stream=self.dev.stream)
 
     def combine(self, b, T, k, R):
         self.dev._check(self.lib.vlb_ep_combine_device(
