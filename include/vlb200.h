@@ -274,7 +274,9 @@ int vlb_layer_set_profiling(vlb_handle* h, vlb_layer* layer, int enable);
 int vlb_layer_phase_times(vlb_handle* h, vlb_layer* layer, float* ms, int n);
 
 /* ---- standalone routing operators (deepseek_v4_route_*_logits, deepseek_v4_reference.hpp:
- * 634-650) on device buffers ---------------------------------------------------------------- */
+ * 634-650) on device buffers ----------------------------------------------------------------
+ * Both are synchronous (they synchronise `stream` to report errors) and keep their scratch in a
+ * grow-only buffer of the handle (released by vlb_close), so repeated calls allocate nothing. */
 int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* logits_dev,
                      const float* bias_dev, const uint32_t* token_ids_dev,
                      const uint32_t* tid2eid_dev, uint32_t vocab, uint32_t T, uint32_t E,

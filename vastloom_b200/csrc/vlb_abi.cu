@@ -79,10 +79,28 @@ struct vlb_handle {
     float* seam_x = nullptr;
     float* seam_y = nullptr;
     size_t seam_x_cap = 0, seam_y_cap = 0;
+    // grow-only scratch of the synchronous helper entry points (routing, router logits): a
+    // device allocation per call would cost more than the kernels themselves
+    char* scratch = nullptr;
+    size_t scratch_cap = 0;
 
     int fail(int code, std::string msg) {
         err = std::move(msg);
         return code;
+    }
+    // At least `bytes` of the helper scratch (callers hold the handle lock and synchronise their
+    // stream before returning, so the previous user is done with it).
+    int scratch_at_least(size_t bytes, char** out) {
+        if (scratch_cap < bytes) {
+            if (scratch) gfree(scratch);
+            scratch = nullptr;
+            scratch_cap = 0;
+            const int st = galloc(bytes, "vlb-call-scratch", reinterpret_cast<void**>(&scratch));
+            if (st != VLB_OK) return st;
+            scratch_cap = bytes;
+        }
+        *out = scratch;
+        return VLB_OK;
     }
     int cuda_fail(const char* op, cudaError_t e) {
         (void)cudaGetLastError();  // clear a sticky launch error so the handle stays usable
@@ -956,11 +974,11 @@ int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* lo
     if (hash_routing && (!tok || !tid2eid || vocab == 0))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs token ids and a table");
     cudaStream_t s = h->pick(stream);
-    float* scores = nullptr;
-    uint32_t* flag = nullptr;
-    int st = h->galloc((size_t)T * E * 4 + 256, "vlb-route-scratch", (void**)&scores);
+    char* scratch = nullptr;
+    int st = h->scratch_at_least((size_t)T * E * 4 + 256, &scratch);
     if (st != VLB_OK) return st;
-    flag = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(scores) + (size_t)T * E * 4);
+    float* scores = reinterpret_cast<float*>(scratch);
+    uint32_t* flag = reinterpret_cast<uint32_t*>(scratch + (size_t)T * E * 4);
     cudaError_t e = cudaMemsetAsync(flag, 0, 4, s);
     if (e == cudaSuccess) e = launch_scores(logits, (size_t)T * E, score, scores, s);
     if (e == cudaSuccess)
@@ -969,7 +987,6 @@ int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* lo
     uint32_t flags = 0;
     if (e == cudaSuccess) e = cudaMemcpyAsync(&flags, flag, 4, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    h->gfree(scores);
     if (e != cudaSuccess) return h->cuda_fail("route", e);
     if (flags & 1u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash route token id exceeds its table");
     if (flags & 2u) return h->fail(VLB_ERR_INVALID_FORMAT, "route selects an out-of-range expert");
@@ -986,7 +1003,7 @@ int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint
     const size_t sbytes = ((size_t)T * E * 4 + (size_t)T * 4 + 255) / 256 * 256;
     const size_t xbytes = (size_t)T * H * 8, pbytes = (size_t)8 * T * E * 8;
     char* scratch = nullptr;
-    int st = h->galloc(sbytes + xbytes + pbytes, "vlb-router-scratch", (void**)&scratch);
+    int st = h->scratch_at_least(sbytes + xbytes + pbytes, &scratch);
     if (st != VLB_OK) return st;
     float* scores = reinterpret_cast<float*>(scratch);
     uint32_t* xmax = reinterpret_cast<uint32_t*>(scratch + (size_t)T * E * 4);
@@ -996,7 +1013,6 @@ int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint
     cudaError_t e = launch_prescale(x, T, H, xmax, xd, s);
     if (e == cudaSuccess) e = launch_router(xd, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scores, part, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    h->gfree(scratch);
     if (e != cudaSuccess) return h->cuda_fail("router", e);
     return VLB_OK;
 }
