@@ -99,3 +99,58 @@ def test_gpu_ep_two_ranks_match_single_gpu_layer():
     for rank, rel, deterministic, received, sent in res:
         assert rel <= EXPECTED, (rank, rel)
         assert deterministic
+
+
+def _half_rows(x, idx, w):
+    """fp16(x * 2^e) rows (2^e brings each row's max|x| into [2^14, 2^15)) and their meta words."""
+    amax = np.max(np.abs(x), axis=1).astype(np.float32)
+    _, e = np.frexp(amax)
+    scale = np.ldexp(np.float32(1.0), 15 - e).astype(np.float32)
+    rows = (x * scale[:, None]).astype(np.float16)
+    meta = np.stack([idx.astype(np.uint32), w.astype(np.float32).view(np.uint32), amax.view(np.uint32)], axis=1)
+    return rows, np.ascontiguousarray(meta)
+
+
+def test_gpu_half_rows_forward_equals_given_routes_forward(device):
+    """The expert-parallel receiver's half-row forward (fp16 rows + expert / weight / max|x| words)
+    is bit-identical to the f32 given-routes forward on the same rows: the rows are exactly the
+    tensor-core operands the f32 path builds itself, and one-route rows go straight to out."""
+    import vastloom_b200 as vb
+    from vastloom_b200 import synth
+
+    spec = synth.config(4, "small")
+    W = synth.layer_weights(spec, seed=420)
+    T, E, H, I = 300, spec.experts, spec.hidden, spec.intermediate
+    rng = np.random.default_rng(421)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    idx = rng.integers(0, E, T).astype(np.uint32)
+    w = rng.uniform(0.05, 1.0, T).astype(np.float32)
+    mats = {"w1": [], "w3": [], "w2": []}
+    for e in range(E):
+        for role, (name, rows, cols) in enumerate((("w1", I, H), ("w3", I, H), ("w2", H, I))):
+            t, blob = getattr(W, name)[e]
+            mats[name].append(device.upload_matrix(t, rows, cols, blob, identity=2 * (4 * e + role) + 1))
+    layer = vb.MoeLayer(device, hidden=H, intermediate=I, experts=E, top_k=1, router=np.zeros((E, H), np.float32),
+                        w1=mats["w1"], w3=mats["w3"], w2=mats["w2"], score=spec.score, bias=None, route_scale=1.0,
+                        weight_after_down=False, shared=None, max_tokens=T)
+    try:
+        layer.set_prefill_tokens(1)
+        rows, meta = _half_rows(x, idx, w)
+        dx, didx, dw = (torch.from_numpy(a).cuda() for a in (x, idx.view(np.int32), w))
+        drows, dmeta = torch.from_numpy(rows).cuda(), torch.from_numpy(meta.view(np.int32)).cuda()
+        out_f32 = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        out_half = torch.empty_like(out_f32)
+        torch.cuda.synchronize()
+        layer.forward_routes_device(dx.data_ptr(), didx.data_ptr(), dw.data_ptr(), T, out_f32.data_ptr(),
+                                    stream=device.stream)
+        layer.status(stream=device.stream)
+        layer.forward_rows_half_device(drows.data_ptr(), dmeta.data_ptr(), T, out_half.data_ptr(), stream=device.stream)
+        layer.status(stream=device.stream)
+        a, b = out_f32.cpu().numpy(), out_half.cpu().numpy()
+        assert np.all(np.isfinite(a)) and np.abs(a).max() > 0
+        assert np.array_equal(a, b)
+    finally:
+        layer.destroy()
+        for lst in mats.values():
+            for m in lst:
+                device.release_matrix(m)
