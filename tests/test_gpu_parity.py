@@ -171,6 +171,46 @@ def test_gpu_layer_small_configs(device, oracle, cfg, T):
             device.release_matrix(m)
 
 
+RAGGED = {
+    # Q8_0, OLMoE semantics: 6 row tiles of W1/W3 and of W2 (gate/up row groups of 2 tiles fill
+    # exactly, down row groups of 4 tiles leave 2 empty)
+    "q8-olmoe": synth.LayerSpec("ragged-q8", 768, 768, 12, 3, synth.SCORE_SOFTMAX, synth.TYPE_Q8_0,
+                                synth.TYPE_Q8_0, weight_after_down=True),
+    # IQ2_XXS, 3 row tiles of W1/W3: the second gate/up row group has one empty slice
+    "iq2-odd-tiles": synth.LayerSpec("ragged-iq2-odd", 512, 768, 12, 3, synth.SCORE_SQRT_SOFTPLUS,
+                                     synth.TYPE_IQ2_XXS, synth.TYPE_IQ2_XXS),
+    # IQ2_XXS with a Q8_0 shared expert, DeepSeek-V4 semantics: 6 W2 tiles, 2 of the second down row
+    # group empty
+    "iq2-v4": synth.LayerSpec("ragged-iq2", 768, 512, 12, 3, synth.SCORE_SQRT_SOFTPLUS, synth.TYPE_IQ2_XXS,
+                              synth.TYPE_IQ2_XXS, shared_type=synth.TYPE_Q8_0),
+}
+
+
+@pytest.mark.parametrize("name", sorted(RAGGED))
+@pytest.mark.parametrize("T", [1, 9])
+def test_gpu_layer_ragged_tiles(device, oracle, name, T):
+    """Shapes whose row counts are not whole row groups of the decode kernel (row groups with
+    empty 128-row slices), for both tensor-core formats and both layer semantics."""
+    spec = RAGGED[name]
+    W = synth.layer_weights(spec, seed=500 + T)
+    x, tok, logits = synth.activations(spec, T, seed=510 + T)
+    layer = synth.upload_layer(device, W, max_tokens=16)
+    try:
+        out = layer.forward(x, tok, logits)
+        ref, ridx, _ = oracle.moe_forward(W, x, tok, logits)
+        idx, _, _, _, _ = layer.last_route(T)
+        assert np.array_equal(idx, ridx)
+        assert np.all(np.isfinite(out))
+        assert rel_err(out, ref) <= TOL
+    finally:
+        layer.destroy()
+        for lst in layer.matrices.values():
+            for m in lst:
+                device.release_matrix(m)
+        for m in layer.shared_matrices or ():
+            device.release_matrix(m)
+
+
 @pytest.fixture(scope="module")
 def full_cfg1(device):
     spec = synth.config(1)

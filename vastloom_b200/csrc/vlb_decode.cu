@@ -50,7 +50,10 @@ constexpr uint32_t kDcD = 512;                                 // fp16 block sca
 constexpr uint32_t kDcSc = kTileRows * 4u;                     // IQ2_XXS group scale words
 constexpr uint32_t kDcSlice = kDcBody + kDcD + kDcSc;
 constexpr uint32_t kDcStage = kDcSlices * kDcSlice;            // 36 KB
-constexpr uint32_t kDcRing = 3;
+#ifndef VLB_DC_RING
+#define VLB_DC_RING 3
+#endif
+constexpr uint32_t kDcRing = VLB_DC_RING;
 constexpr uint32_t kDcTabBytes = 256u * 8u * 16u;              // fp16 IQ2_XXS magnitudes, 8 replicas
 constexpr uint32_t kDcRingOff = kDcTabBytes;
 constexpr uint32_t kDcHdrOff = kDcRingOff + kDcRing * kDcStage;
@@ -60,7 +63,10 @@ constexpr uint32_t kDcXsOff = (kDcMiscOff + 64u + 127u) / 128u * 128u;
 constexpr uint64_t kDcWaitNs = 2000000000ull;
 constexpr uint32_t kDcErrTimeout = 8u;
 constexpr uint32_t kDcEnd = 0xffffffffu;
-constexpr uint32_t kDcMaxChunk = 4;
+#ifndef VLB_DC_MAX_CHUNK
+#define VLB_DC_MAX_CHUNK 4
+#endif
+constexpr uint32_t kDcMaxChunk = VLB_DC_MAX_CHUNK;
 
 static_assert(kDcXsOff % 16 == 0 && kDcStage % 1024 == 0, "shared-memory carve alignment");
 static_assert((2u * kDcRing + 1u) * 8u <= 64u, "barriers fit their slot");
