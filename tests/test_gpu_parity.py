@@ -147,12 +147,14 @@ def test_gpu_hash_route_rejects_out_of_range_token(device):
 # ---- the MoE layer ---------------------------------------------------------------------------
 
 @pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4])
-@pytest.mark.parametrize("T", [1, 5, 16])
+@pytest.mark.parametrize("T", [1, 5, 16, 37])
 def test_gpu_layer_small_configs(device, oracle, cfg, T):
+    """Every configuration's structure at small scale through the decode path; T = 37 gives the
+    Q8_0 shared expert three wide units (16 + 16 + 5 tokens)."""
     spec = synth.config(cfg, "small")
     W = synth.layer_weights(spec, seed=300 + cfg)
     x, tok, logits = synth.activations(spec, T, seed=400 + cfg + T)
-    layer = synth.upload_layer(device, W, max_tokens=16)
+    layer = synth.upload_layer(device, W, max_tokens=64)
     try:
         out = layer.forward(x, tok, logits)
         ref, ridx, rw = oracle.moe_forward(W, x, tok, logits)

@@ -207,10 +207,14 @@ __device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t 
     return w;
 }
 
-// ---- loader lane --------------------------------------------------------------------------------
+// ---- loader warp --------------------------------------------------------------------------------
+// Lane 0 takes the items and does the ring bookkeeping; the copies of a stage are issued by
+// different lanes at once (one copy per lane): a bulk copy costs its issuing thread a few hundred
+// cycles, so a single issuing lane would cap the stage rate well below HBM bandwidth.
 template <bool GATEUP>
 __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t groups, uint64_t n_items,
                           uint32_t chunk, volatile uint32_t* abort) {
+    const uint32_t lane = threadIdx.x & 31u;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDcBarOff);
     uint64_t* empty = full + kDcRing;
     uint4* hdr = reinterpret_cast<uint4*>(smem + kDcHdrOff);
@@ -218,26 +222,33 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
     const uint32_t mat_off = GATEUP ? 0u : 2u * (p.E + 1u);
     uint32_t g = 0;
     bool ok = true;
+    // every lane runs this (warp-uniform result)
     auto acquire = [&](uint32_t slot) -> bool {
-        if (g >= kDcRing && !dc_wait(empty + slot, ((g / kDcRing) - 1u) & 1u, abort)) {
+        bool got = true;
+        if (lane == 0 && g >= kDcRing && !dc_wait(empty + slot, ((g / kDcRing) - 1u) & 1u, abort)) {
             dc_fail(p.counters + 3, abort);
-            return false;
+            got = false;
         }
-        return true;
+        return __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0;
     };
     while (ok) {
         // chunks of neighbouring items (one unit's row groups share the staged activations) while
         // much work is left, single items towards the end so that the CTAs finish together
-        const uint64_t seen = *reinterpret_cast<volatile uint32_t*>(next_item);
-        uint32_t take = seen < n_items ? (uint32_t)((n_items - seen) / (2ull * gridDim.x)) : 1u;
-        take = take < 1u ? 1u : (take > chunk ? chunk : take);
-        const uint64_t c0 = atomicAdd(next_item, take);
+        uint64_t c0 = 0;
+        uint32_t take = 1;
+        if (lane == 0) {
+            const uint64_t seen = *reinterpret_cast<volatile uint32_t*>(next_item);
+            take = seen < n_items ? (uint32_t)((n_items - seen) / (2ull * gridDim.x)) : 1u;
+            take = take < 1u ? 1u : (take > chunk ? chunk : take);
+            c0 = atomicAdd(next_item, take);
+        }
+        c0 = __shfl_sync(0xffffffffu, (unsigned long long)c0, 0);
+        take = __shfl_sync(0xffffffffu, take, 0);
         if (c0 >= n_items) break;
         const uint64_t c1 = c0 + take < n_items ? c0 + take : n_items;
-        for (uint64_t ord = c0; ord < c1 && ok; ++ord) {
-            // heaviest first: the units are in expert order with the shared expert (many units of
-            // one matrix) last, so items are taken from the end
-            const uint64_t item = n_items - 1u - ord;
+        // the dispatch lists the shared expert's units first (the heaviest: every token, usually
+        // the widest storage type), so the CTAs start on them and finish on light routed items
+        for (uint64_t item = c0; item < c1 && ok; ++item) {
             const Unit u = p.units[(uint32_t)(item / groups)];
             const uint32_t t = p.mats[mat_off + u.expert].type;
             if (t != kTypeIq2Xxs && t != kTypeQ8_0) continue;  // served by the CUDA-core kernels
@@ -249,41 +260,73 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
                 const uint32_t nblk = it.iq2 ? 1u : (2u * st + 1u < it.m[0]->bpr ? 2u : 1u);
                 const uint32_t body = it.iq2 ? kDcBody : nblk * kTileRows * 32u;
                 const uint32_t dbytes = nblk * kTileRows * 2u;
-                uint32_t bytes = 0;
+                if (lane == 0) {
+                    uint32_t bytes = 0;
 #pragma unroll
-                for (uint32_t s = 0; s < kDcSlices; ++s)
-                    if (it.valid[s]) bytes += body + dbytes + (it.iq2 ? kDcSc : 0u);
-                hdr[slot] = make_uint4((uint32_t)item, st, it.stages, 0u);
-                tc::mbar_arrive_expect_tx(full + slot, bytes);
-                const uint32_t dst = tc::smem_u32(smem + kDcRingOff + slot * kDcStage);
-                const uint32_t blk = it.iq2 ? st : 2u * st;
-#pragma unroll
-                for (uint32_t s = 0; s < kDcSlices; ++s) {
-                    if (!it.valid[s]) continue;
-                    const DevMat& m = *it.m[s];
-                    const size_t at = blk_index(m.bpr, it.tile[s] * kTileRows, blk);
-                    const uint32_t sd = dst + s * kDcSlice;
-                    tc::bulk_load(sd, m.body + at * (it.iq2 ? 64u : 32u), body, full + slot);
-                    tc::bulk_load(sd + kDcBody, m.d + at, dbytes, full + slot);
-                    if (it.iq2) tc::bulk_load(sd + kDcBody + kDcD, m.scales + at, kDcSc, full + slot);
+                    for (uint32_t s = 0; s < kDcSlices; ++s)
+                        if (it.valid[s]) bytes += body + dbytes + (it.iq2 ? kDcSc : 0u);
+                    hdr[slot] = make_uint4((uint32_t)item, st, it.stages, 0u);
+                    tc::mbar_arrive_expect_tx(full + slot, bytes);
                 }
+                __syncwarp();
+                // lane 3 s + c: slice s, copy c (0 packed weights, 1 block scales, 2 group scales)
+                const uint32_t s = lane / 3u, c = lane % 3u;
+                const DevMat* ms = it.m[0];
+                uint32_t tile = 0;
+                bool valid = false;
+#pragma unroll
+                for (uint32_t k = 0; k < kDcSlices; ++k)  // constant indices keep the item in registers
+                    if (k == s) {
+                        ms = it.m[k];
+                        tile = it.tile[k];
+                        valid = it.valid[k];
+                    }
+                if (valid && (c < 2u || it.iq2)) {
+                    const DevMat& m = *ms;
+                    const uint32_t blk = it.iq2 ? st : 2u * st;
+                    const size_t at = blk_index(m.bpr, tile * kTileRows, blk);
+                    const uint32_t sd = tc::smem_u32(smem + kDcRingOff + slot * kDcStage) + s * kDcSlice;
+                    if (c == 0) tc::bulk_load(sd, m.body + at * (it.iq2 ? 64u : 32u), body, full + slot);
+                    else if (c == 1) tc::bulk_load(sd + kDcBody, m.d + at, dbytes, full + slot);
+                    else tc::bulk_load(sd + kDcBody + kDcD, m.scales + at, kDcSc, full + slot);
+                }
+                __syncwarp();
             }
         }
     }
     if (ok) {  // end marker: a stage with no copies
         const uint32_t slot = g % kDcRing;
         if (acquire(slot)) {
-            hdr[slot] = make_uint4(kDcEnd, 0u, 0u, 0u);
-            tc::mbar_arrive(full + slot);
+            if (lane == 0) {
+                hdr[slot] = make_uint4(kDcEnd, 0u, 0u, 0u);
+                tc::mbar_arrive(full + slot);
+            }
             ++g;
         }
     }
     // no bulk copy may still be landing in shared memory when the CTA exits
-    for (uint32_t j = g > kDcRing ? g - kDcRing : 0u; j < g; ++j)
-        if (!dc_wait(full + j % kDcRing, (j / kDcRing) & 1u, abort)) break;
+    if (lane == 0)
+        for (uint32_t j = g > kDcRing ? g - kDcRing : 0u; j < g; ++j)
+            if (!dc_wait(full + j % kDcRing, (j / kDcRing) & 1u, abort)) break;
 }
 
 // ---- consumer warps -------------------------------------------------------------------------------
+// One output of the gate/up epilogue: act = SwiGLU(gate, up), for DeepSeek V4 with the optional
+// clamp and the route weight before the down product (execute_expert, deepseek_v4_graph.cpp:
+// 1865-1890, double arithmetic), for OLMoE the float SwiGLU with expf (olmoe_runtime.cpp:1279).
+__device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, float uv, bool shared, uint32_t pair) {
+    if (p.weight_after_down) return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+    const float limit = shared ? p.shared_limit : p.routed_limit;
+    double gd = (double)gv, ud = (double)uv;
+    if (limit > 0.f) {
+        gd = fmin(gd, (double)limit);
+        ud = fmin(fmax(ud, -(double)limit), (double)limit);
+    }
+    double v = gd / (1.0 + exp(-gd)) * ud;
+    if (!shared) v *= (double)p.pair_weight[pair];
+    return (float)v;
+}
+
 // IQ2_XXS stage: one 256-column block of this warp's two slices (rows rt + gq and rt + gq + 8).
 __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
                                              uint32_t gq, uint32_t q, uint32_t xrow, const uint4* tab,
@@ -424,7 +467,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     const uint32_t groups = (rows + (GATEUP ? 255u : 511u)) / (GATEUP ? 256u : 512u);
     const uint64_t n_items = (uint64_t)p.counters[0] * groups;
     if (warp == kDcConsumerWarps) {
-        if (lane == 0) dc_loader<GATEUP>(p, smem, groups, n_items, chunk, abort);
+        dc_loader<GATEUP>(p, smem, groups, n_items, chunk, abort);
         return;
     }
     // consumer warp: 16 rows of slices (w / 8) and (2 + w / 8)
@@ -503,7 +546,6 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
                 const float inv = 1.f / tok_scale[q];  // exact: a power of two
                 if (GATEUP) {
                     const bool shared = u.expert == p.E;
-                    const float limit = shared ? p.shared_limit : p.routed_limit;
                     const uint32_t row_base = it.tile0 * kTileRows + rt + gq;
 #pragma unroll
                     for (int hi = 0; hi < 2; ++hi) {  // fragment row gq / gq + 8
@@ -511,22 +553,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
                         if (!it.valid0 || row >= p.I) continue;
                         const float gv = (acc[0][2 * hi] + acc[0][2 * hi + 1]) * inv;
                         const float uv = (acc[1][2 * hi] + acc[1][2 * hi + 1]) * inv;
-                        float a;
-                        if (p.weight_after_down) {
-                            // OLMoE: float SwiGLU with expf (olmoe_runtime.cpp:1279)
-                            a = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
-                        } else {
-                            // execute_expert: double SwiGLU, optional clamp, route weight before
-                            // the down product (deepseek_v4_graph.cpp:1865-1890)
-                            double gd = (double)gv, ud = (double)uv;
-                            if (limit > 0.f) {
-                                gd = fmin(gd, (double)limit);
-                                ud = fmin(fmax(ud, -(double)limit), (double)limit);
-                            }
-                            double v = gd / (1.0 + exp(-gd)) * ud;
-                            if (!shared) v *= (double)p.pair_weight[pair];
-                            a = (float)v;
-                        }
+                        const float a = dc_act_value(p, gv, uv, shared, pair);
                         p.act[(size_t)pair * p.I + row] = a;
                         atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
                     }
