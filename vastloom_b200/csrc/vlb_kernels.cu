@@ -5,9 +5,11 @@
 //   router_kernel     router projection in f64 accumulation + score function
 //   route_kernel      warp-per-token top-k (ties to the lower id) and route weights
 //   dispatch_kernel   stable counting sort of (token, slot) pairs by expert, work units
-//   gateup_kernel     persistent: gate and up rows of every selected expert + SwiGLU epilogue
-//   down_kernel       persistent: down rows of every selected expert
+//                     (dispatch_count / scatter / finish for large batches)
+//   expert_kernel     CUDA-core expert products for the IQ3_XXS / IQ1_S experts (bit-exact decode)
 //   combine_kernel    per-token deterministic combine in the reference's order + shared expert
+//   launch_moe        the whole layer: routing, dispatch, expert products (decode kernels in
+//                     vlb_decode.cu or the tcgen05 prefill GEMMs in vlb_prefill.cu), combine
 #include <cuda_runtime.h>
 
 #include <cstdlib>
