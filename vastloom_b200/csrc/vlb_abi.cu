@@ -390,9 +390,10 @@ static float half_bits_to_float(uint16_t bits) {
     return (bits & 0x8000u) ? -mag : mag;
 }
 
-// TMA descriptor of a row-major fp16 matrix [rows x cols] read as 64-column x 16-row boxes with the
-// 128-byte swizzle of the UMMA K-major operand layout (cuTensorMapEncodeTiled, resolved through
-// the runtime so the library does not link the driver API).
+// TMA descriptor of a row-major fp16 matrix [rows x cols] read as boxes of 64 columns x
+// prefill_box_rows() rows with the 128-byte swizzle of the UMMA K-major operand layout
+// (cuTensorMapEncodeTiled, resolved through the runtime so the library does not link the driver
+// API).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

@@ -21,12 +21,12 @@
 //   A (weights): the producer warps decode their rows from that ring to fp16 in registers and
 //     write them straight into tensor memory (tcgen05.st): the MMA reads A from TMEM;
 //   B (activations): N rows of the pair-ordered fp16 matrix (xperm for gate/up, act_h for down),
-//     TMA-loaded as 16-row boxes into a shared-memory ring (K-major, 128-byte swizzle).
+//     TMA-loaded as 80-row boxes into a shared-memory ring (K-major, 128-byte swizzle).
 // CTA roles (608 threads, one CTA per SM):
 //   warps 0-15  producers: thread t owns half (t / 128 % 2) of the 64 stage columns of row t % 128
 //               of accumulator t / 256 (its TMEM lane is its row). Afterwards they are the
 //               epilogue: tcgen05.ld of the accumulators, scaling, SwiGLU, stores.
-//   warp 16     loader: lane 0 issues the packed-weight bulk copies.
+//   warp 16     loader: lanes 0-5 issue the packed-weight bulk copies of a stage at once.
 //   warp 17     TMA: lane 0 issues the B boxes.
 //   warp 18     MMA: lane 0 issues the MMAs (M = 128, N = tile, K = 16; 8 per stage), commits
 //               each stage's A and B slots back and the finished accumulators to the epilogue.
@@ -63,7 +63,21 @@ constexpr uint32_t kPfLoadWarp = kPfProducerWarps;
 constexpr uint32_t kPfTmaWarp = kPfProducerWarps + 1;
 constexpr uint32_t kPfMmaWarp = kPfProducerWarps + 2;
 constexpr uint32_t kPfThreads = kPfProducers + 96;
-constexpr uint32_t kPfBoxRows = 16;                  // B rows per TMA box
+// B rows per TMA box. The TMA unit spends a fixed time per box besides the bytes (measured on
+// B200: a 160-row stage as ten 16-row boxes takes ~1,260 cycles, as two 80-row boxes ~750, the
+// time of the stage's MMAs), so a stage loads ceil(N / rows) large boxes and ignores the rows
+// past N.
+#ifndef VLB_PF_BOX_ROWS
+#define VLB_PF_BOX_ROWS 80
+#endif
+constexpr uint32_t kPfBoxRows = VLB_PF_BOX_ROWS;
+// The packed-weight copies of a stage are issued by separate lanes in one instruction (measured:
+// ~2% faster than one lane issuing them in turn; lanes that each take a branch of their own were
+// ~20% slower).
+#ifndef VLB_PF_RAW_LANES
+#define VLB_PF_RAW_LANES 1
+#endif
+constexpr bool kPfRawLanes = VLB_PF_RAW_LANES != 0;
 constexpr uint32_t kPfASlots = 3;                    // A operand buffers in TMEM
 // shared memory: B ring, packed-weight ring, IQ2 table, per-tile scalars, barriers
 constexpr uint32_t kPfBStages = 5;                   // B (activation) ring slots
@@ -100,6 +114,7 @@ constexpr uint32_t kPfErrAlign = 16u;
 static_assert(kPfSmemBytes <= 232448, "prefill rings exceed the shared memory of a CTA");
 static_assert(kPfBStage % 1024 == 0 && kPfRawOff % 1024 == 0, "swizzle atoms must stay 1 KB aligned");
 static_assert(kPfBoxRows * 128 % 1024 == 0, "TMA boxes must start on swizzle-atom boundaries");
+static_assert(kPfMaxN % kPfBoxRows == 0 && kPfBoxRows <= 256, "a stage's boxes must fill its B slot exactly");
 static_assert(kPfACol + kPfASlots * 64 <= kPfTmemCols, "TMEM budget");
 static_assert(kPfRing >= kPfBStages + 1 && kPfRing >= kPfASlots + 1,
               "a slot's waiter must never fall two phases behind on the stage barrier ring");
@@ -314,41 +329,68 @@ __device__ __forceinline__ bool pf_produce(const PfBars& br, uint32_t smem, cons
     return true;
 }
 
-// Loader lane: the item's packed weights, one bulk copy per matrix body and per scale run.
+// Loader warp: the item's packed weights, one bulk copy per matrix body and per scale run. Lane 0
+// waits for the ring slot and registers the stage's bytes; the copies are issued by lanes 2 c + i
+// (matrix i, copy c: 0 packed weights, 1 block scales, 2 group scales) at once, since a bulk copy
+// holds its issuing thread for a few hundred cycles. Every lane of the warp runs this.
 __device__ __forceinline__ bool pf_load_raw(const PfBars& br, uint32_t smem, const DevMat& m0, const DevMat& m1,
                                             uint32_t rt0, uint32_t rt1, uint32_t nk, PfPos& raw) {
+    const uint32_t lane = threadIdx.x & 31u;
     const bool q8 = m0.type == kTypeQ8_0;
     const uint32_t stages = q8 ? nk : nk / 4u;
     const uint32_t dbytes = q8 ? 2u * kTileRows * 2u : kTileRows * 2u;
     for (uint32_t rs = 0; rs < stages; ++rs) {
-        if (!pf_wait(br.raw_empty + raw.slot, raw.ph ^ 1u, br.abort, kPfSleepNs)) return false;
+        bool ok = true;
+        if (lane == 0) ok = pf_wait(br.raw_empty + raw.slot, raw.ph ^ 1u, br.abort, kPfSleepNs);
+        if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0) return false;
         const uint32_t dst = smem + kPfRawOff + raw.slot * kPfRawStage;
-        tc::mbar_arrive_expect_tx(br.raw_full + raw.slot, 2u * (kPfRawBody + dbytes + (q8 ? 0u : kPfRawSc)));
+        if (lane == 0)
+            tc::mbar_arrive_expect_tx(br.raw_full + raw.slot, 2u * (kPfRawBody + dbytes + (q8 ? 0u : kPfRawSc)));
+        __syncwarp();
         const uint32_t blk = q8 ? 2u * rs : rs;
+        if (kPfRawLanes) {
+            // lane 2 c + i: copy c of matrix i, all issued by one instruction
+            if (lane < (q8 ? 4u : 6u)) {
+                const uint32_t i = lane & 1u, c = lane >> 1;
+                const DevMat* m = i ? &m1 : &m0;
+                const size_t at = blk_index(m->bpr, (i ? rt1 : rt0) * kTileRows, blk);
+                const void* src = c == 0u ? (const void*)(m->body + at * (q8 ? 32u : 64u))
+                                  : c == 1u ? (const void*)(m->d + at) : (const void*)(m->scales + at);
+                const uint32_t to = c == 0u ? dst + i * kPfRawBody
+                                    : c == 1u ? dst + 2u * kPfRawBody + i * kPfRawD
+                                              : dst + 2u * kPfRawBody + 2u * kPfRawD + i * kPfRawSc;
+                const uint32_t bytes = c == 0u ? kPfRawBody : c == 1u ? dbytes : kPfRawSc;
+                tc::bulk_load(to, src, bytes, br.raw_full + raw.slot);
+            }
+        } else if (lane == 0) {
 #pragma unroll
-        for (uint32_t i = 0; i < 2u; ++i) {
-            const DevMat& m = i ? m1 : m0;
-            const size_t at = blk_index(m.bpr, (i ? rt1 : rt0) * kTileRows, blk);
-            tc::bulk_load(dst + i * kPfRawBody, m.body + at * (q8 ? 32u : 64u), kPfRawBody, br.raw_full + raw.slot);
-            tc::bulk_load(dst + 2u * kPfRawBody + i * kPfRawD, m.d + at, dbytes, br.raw_full + raw.slot);
-            if (!q8)
-                tc::bulk_load(dst + 2u * kPfRawBody + 2u * kPfRawD + i * kPfRawSc, m.scales + at, kPfRawSc,
-                              br.raw_full + raw.slot);
+            for (uint32_t i = 0; i < 2u; ++i) {
+                const DevMat& m = i ? m1 : m0;
+                const size_t at = blk_index(m.bpr, (i ? rt1 : rt0) * kTileRows, blk);
+                tc::bulk_load(dst + i * kPfRawBody, m.body + at * (q8 ? 32u : 64u), kPfRawBody, br.raw_full + raw.slot);
+                tc::bulk_load(dst + 2u * kPfRawBody + i * kPfRawD, m.d + at, dbytes, br.raw_full + raw.slot);
+                if (!q8)
+                    tc::bulk_load(dst + 2u * kPfRawBody + 2u * kPfRawD + i * kPfRawSc, m.scales + at, kPfRawSc,
+                                  br.raw_full + raw.slot);
+            }
         }
+        __syncwarp();
         raw.next(kPfRawStages);
     }
     return true;
 }
 
-// TMA lane: per stage, the N B rows (pair order, starting at row0) as N / 16 boxes.
+// TMA lane: per stage, the B rows of the tile (pair order, starting at row0) as ceil(N / box)
+// boxes; rows past N land in the slot unused (past the matrix end the TMA unit fills zeros).
 __device__ __forceinline__ bool pf_load_b(const PfBars& br, uint32_t smem, const CUtensorMap* map,
                                           uint32_t row0, uint32_t nk, uint32_t N, uint32_t g0) {
+    const uint32_t nbox = (N + kPfBoxRows - 1u) / kPfBoxRows;
     for (uint32_t kc = 0; kc < nk; ++kc) {
         const uint32_t g = g0 + kc, bar = g % kPfRing;
         if (!pf_wait_freed(br, (int64_t)g - kPfBStages, kPfSleepNs)) return false;
-        tc::mbar_arrive_expect_tx(br.full + bar, N * kPfKc * 2u);
+        tc::mbar_arrive_expect_tx(br.full + bar, nbox * kPfBoxRows * kPfKc * 2u);
         const uint32_t dst = smem + (g % kPfBStages) * kPfBStage;
-        for (uint32_t j = 0; j < N / kPfBoxRows; ++j)
+        for (uint32_t j = 0; j < nbox; ++j)
             tc::tma_load_2d(dst + j * kPfBoxRows * 128u, map, (int32_t)(kc * kPfKc), (int32_t)(row0 + j * kPfBoxRows),
                             br.full + bar);
     }
@@ -577,11 +619,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_gemm_kernel(const __gri
             }
             tc::fence_before_sync();
         } else if (warp == kPfLoadWarp) {
-            if (lane == 0) {
-                copies_dirty = true;
-                if (pf_load_raw(br, smem, *m0, *m1, rt0, rt1, nk, raw)) copies_dirty = false;
-                else pf_fail(p.counters + 3, br.abort);
-            }
+            copies_dirty = true;
+            if (pf_load_raw(br, smem, *m0, *m1, rt0, rt1, nk, raw)) copies_dirty = false;
+            else if (lane == 0) pf_fail(p.counters + 3, br.abort);
         } else if (warp == kPfTmaWarp) {
             if (lane == 0) {
                 copies_dirty = true;
