@@ -180,3 +180,95 @@ def test_ep_orchestration_matches_single_process(grids, world, T):
 def test_owner_counts_split_expert_sorted_offsets():
     offsets = np.array([0, 2, 2, 5, 9, 9, 12, 12, 13], np.uint32)  # 8 experts, 2 per rank
     assert owner_counts(offsets, 4, 2) == [2, 7, 3, 1]
+
+
+class _InjectedFailure(RuntimeError):
+    pass
+
+
+class FailingEpOps(NumpyEpOps):
+    """NumpyEpOps whose rank raises at one step (a host-side stand-in for a rank that fails)."""
+
+    def __init__(self, *args, fail_at=None):
+        super().__init__(*args)
+        self.fail_at = fail_at
+
+    def plan(self, *args):
+        if self.fail_at == "plan":
+            raise _InjectedFailure("injected failure before the first exchange")
+        return super().plan(*args)
+
+    def group_forward(self, *args):
+        if self.fail_at == "group_forward":
+            raise _InjectedFailure("injected failure between the dispatch and the return exchange")
+        return super().group_forward(*args)
+
+
+def _failure_rank_main(rank, world, port, mode, grids, result_q):
+    """Rank world - 1 fails (raises at `mode`, or never reaches the layer when mode is "absent");
+    the other ranks must end their forward with EpExchangeError instead of waiting for it."""
+    import datetime
+    import time
+
+    from vastloom_b200.ep import EpExchangeError
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    failing = rank == world - 1
+    if failing and mode == "absent":
+        time.sleep(12)  # alive but never joins an exchange; longer than the group's timeout
+        os._exit(0)
+    from oracle.oracle import Oracle
+
+    oracle = Oracle(grids)
+    spec = synth.config(4, "small")
+    W = synth.layer_weights(spec, seed=91)
+    T = 3
+    x, _, logits = synth.activations(spec, T, seed=92 + rank)
+    ops = FailingEpOps(oracle, W, rank, world, fail_at=mode if failing else None)
+    layer = ExpertParallelLayer(ops, TorchComm(), spec.experts, spec.top_k, spec.hidden, max_tokens=T)
+    if failing:
+        layer.forward(torch.from_numpy(x), torch.from_numpy(logits), T)  # raises: the process ends with it
+        os._exit(5)  # not reached
+    t0 = time.perf_counter()
+    try:
+        layer.forward(torch.from_numpy(x), torch.from_numpy(logits), T)
+        outcome = ("no error", None)
+    except EpExchangeError as e:
+        outcome = ("EpExchangeError", e.phase)
+    elapsed = time.perf_counter() - t0
+    try:  # the layer refuses further forwards at once
+        t1 = time.perf_counter()
+        layer.forward(torch.from_numpy(x), torch.from_numpy(logits), T)
+        again = ("no error", None, 0.0)
+    except EpExchangeError as e:
+        again = ("EpExchangeError", e.phase, time.perf_counter() - t1)
+    result_q.put((rank, outcome, elapsed, again))
+    result_q.close()
+    result_q.join_thread()
+    os._exit(0)  # no destroy_process_group: a peer is gone
+
+
+@pytest.mark.parametrize("mode,phase", [("plan", "counts"), ("group_forward", "return"), ("absent", "counts")])
+def test_ep_failed_rank_ends_the_step_with_an_error(grids, mode, phase):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failure_rank_main, args=(r, world, port, mode, grids, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes[0] == 0, codes
+    assert codes[1] == (0 if mode == "absent" else 1), codes
+    rank, outcome, elapsed, again = q.get(timeout=10)
+    assert rank == 0
+    assert outcome == ("EpExchangeError", phase), outcome
+    assert elapsed < 60.0, elapsed
+    assert again[:2] == ("EpExchangeError", phase) and again[2] < 1.0, again

@@ -16,6 +16,12 @@ expert of its local group (weight 1).
 The orchestration is written once against two small interfaces: `ops` (the compute steps; the
 device implementation, DeviceEpOps, calls the vlb200 C ABI) and `comm` (the exchange;
 TorchComm wraps torch.distributed, NCCL on GPUs, gloo on CPU tensors).
+
+Failure detection is the process group's: give it a short timeout. A rank that fails, leaves or
+never reaches an exchange makes the exchange raise on its peers (after the timeout, or at once
+when its connections close); the layer turns that into EpExchangeError naming the exchange and
+refuses further forwards, since the peers' state is unknown. Rebuild the group and the layer to
+continue.
 """
 
 from __future__ import annotations
@@ -25,6 +31,15 @@ from dataclasses import dataclass
 from typing import Optional
 
 import numpy as np
+
+
+class EpExchangeError(RuntimeError):
+    """An exchange of the expert-parallel layer failed: a peer rank failed, left the group or did
+    not join within the process group's timeout. `phase` is "counts", "dispatch" or "return"."""
+
+    def __init__(self, phase: str, cause: BaseException):
+        super().__init__(f"expert-parallel {phase} exchange failed: {cause}")
+        self.phase = phase
 
 
 def owner_counts(offsets_host: np.ndarray, world: int, experts_per_rank: int) -> list:
@@ -106,6 +121,17 @@ class ExpertParallelLayer:
         self.capacity = 0  # group rows the receive side is sized for (grown on demand)
         self._marks = None
         self._rows = (0, 0)
+        self.failed: Optional[str] = None  # the exchange that failed, once one has
+
+    def _exchange(self, phase: str, fn):
+        """Runs one exchange step; a failure of the process group becomes EpExchangeError and
+        marks the layer failed."""
+        try:
+            with self.ops.comm_scope():
+                return fn()
+        except Exception as e:  # torch.distributed raises RuntimeError (or a subclass) here
+            self.failed = phase
+            raise EpExchangeError(phase, e) from e
 
     def _reserve(self, rows: int) -> None:
         """Receive-side buffers for `rows` group rows (received pairs + own shared rows). The worst
@@ -127,26 +153,28 @@ class ExpertParallelLayer:
         the two count read-backs the exchange sizes need); `last` reads them afterwards."""
         if T > self.max_tokens:
             raise ValueError("more tokens than the layer was sized for")
+        if self.failed:
+            raise EpExchangeError(self.failed, RuntimeError("an earlier exchange of this layer failed"))
         ops, comm, b, k = self.ops, self.comm, self.buf, self.k
         n = T * k
         m0 = ops.mark()
         idx, w = ops.route(logits, T)
         offsets = ops.plan(idx, w, x, T, self.epr, b)
         send_counts = owner_counts(offsets, comm.world, self.epr)
-        with ops.comm_scope():
-            recv_counts = comm.exchange_counts(send_counts, b.out)
+        recv_counts = self._exchange("counts", lambda: comm.exchange_counts(send_counts, b.out))
         R = sum(recv_counts)
         self._reserve(R + T)
         m1 = ops.mark()
-        with ops.comm_scope():
+        def dispatch():
             comm.all_to_all(b.group_rows[:R], b.send_rows[:n], recv_counts, send_counts)
             comm.all_to_all(b.group_meta[:R], b.send_meta[:n], recv_counts, send_counts)
+
+        self._exchange("dispatch", dispatch)
         ops.append_shared_rows(b, R, x, T, self.epr)
         m2 = ops.mark()
         ops.group_forward(b, R + T)
         m3 = ops.mark()
-        with ops.comm_scope():
-            comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts)
+        self._exchange("return", lambda: comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts))
         m4 = ops.mark()
         out = ops.combine(b, T, k, R)
         m5 = ops.mark()
