@@ -121,8 +121,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 // ---------------------------------------------------------------------------------------------
 // Router projection, f64 accumulation of exact f32 products (deepseek_v4_graph.cpp:735-767), and
 // the per-expert score (sqrt_softplus / sigmoid; softmax is applied per token in route_kernel).
-// CTA: 8 warps = 8 experts, a chunk of up to 8 tokens, columns staged 1024 at a time.
-constexpr int kRouterTok = 8;
 constexpr uint32_t kRouterMaxSlices = 8;
 
 __device__ __forceinline__ float sqrt_softplus_dev(float v) {
