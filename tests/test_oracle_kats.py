@@ -145,14 +145,16 @@ def test_oracle_matches_reference_rms_norm(oracle, reference):
     assert oracle.rms_norm(x, w, 1e-6).tobytes() == reference.rms_norm(x, w, 1e-6).tobytes()
 
 
-@pytest.mark.parametrize("cfg", [0, 1, 2, 3])
-def test_oracle_layer_matches_reference_layer(oracle, reference, cfg):
-    """The restated MoE layer loop against the reference-kernel layer loop: bit-identical."""
+@pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("T", [1, 5, 13])
+def test_oracle_layer_matches_reference_layer(oracle, reference, cfg, T):
+    """The restated MoE layer loop against the reference-kernel layer loop: bit-identical, for a
+    single token and ragged batches."""
     from vastloom_b200 import synth
 
     spec = synth.config(cfg, "small")
     W = synth.layer_weights(spec, seed=100 + cfg)
-    x, tok, logits = synth.activations(spec, 5, seed=200 + cfg)
+    x, tok, logits = synth.activations(spec, T, seed=200 + cfg + 10 * T)
     a = oracle.moe_forward(W, x, tok, logits)
     b = reference.moe_forward(W, x, tok, logits)
     assert np.array_equal(a[1], b[1])
