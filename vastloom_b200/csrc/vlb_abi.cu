@@ -649,20 +649,28 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
             return st;            \
         }                         \
     } while (0)
+#define TRY_CUDA(call)                          \
+    do {                                        \
+        const cudaError_t e_ = (call);          \
+        if (e_ != cudaSuccess) {                \
+            free_layer(h, L);                   \
+            return h->cuda_fail(#call, e_);     \
+        }                                       \
+    } while (0)
     TRY(h->galloc((size_t)E * H * 4, "vlb-router", (void**)&L->router));
-    VLB_CUDA(h, cudaMemcpy(L->router, d->router, (size_t)E * H * 4, cudaMemcpyHostToDevice));
+    TRY_CUDA(cudaMemcpy(L->router, d->router, (size_t)E * H * 4, cudaMemcpyHostToDevice));
     if (d->bias) {
         TRY(h->galloc((size_t)E * 4, "vlb-router-bias", (void**)&L->bias));
-        VLB_CUDA(h, cudaMemcpy(L->bias, d->bias, (size_t)E * 4, cudaMemcpyHostToDevice));
+        TRY_CUDA(cudaMemcpy(L->bias, d->bias, (size_t)E * 4, cudaMemcpyHostToDevice));
     }
     if (d->hash_routing) {
         TRY(h->galloc((size_t)d->vocab * k * 4, "vlb-tid2eid", (void**)&L->tid2eid));
-        VLB_CUDA(h, cudaMemcpy(L->tid2eid, d->tid2eid, (size_t)d->vocab * k * 4, cudaMemcpyHostToDevice));
+        TRY_CUDA(cudaMemcpy(L->tid2eid, d->tid2eid, (size_t)d->vocab * k * 4, cudaMemcpyHostToDevice));
     }
     std::vector<DevMat> dm(3 * (E + 1));
     for (size_t i = 0; i < dm.size(); ++i) dm[i] = hm[i] ? hm[i]->dm : DevMat{};
     TRY(h->galloc(dm.size() * sizeof(DevMat), "vlb-expert-table", (void**)&L->mats));
-    VLB_CUDA(h, cudaMemcpy(L->mats, dm.data(), dm.size() * sizeof(DevMat), cudaMemcpyHostToDevice));
+    TRY_CUDA(cudaMemcpy(L->mats, dm.data(), dm.size() * sizeof(DevMat), cudaMemcpyHostToDevice));
     // workspace
     const size_t T = d->max_tokens, P = T * k + T;
     const uint32_t mu = max_units_for((uint32_t)T, k, E);
@@ -687,6 +695,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     TRY(h->galloc(T * E * 4, "vlb-layer-logits", (void**)&L->logits_dev));
     TRY(h->galloc(T * H * 4, "vlb-layer-out", (void**)&L->out_dev));
 #undef TRY
+#undef TRY_CUDA
     char* ws = static_cast<char*>(L->ws);
     MoeParams& p = L->p;
     p.H = H; p.I = I; p.E = E; p.k = k; p.T = 0;
