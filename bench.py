@@ -563,7 +563,8 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    # long enough timed regions for the clock sampler to see the load (~0.1 s of decode steps)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=64)
@@ -572,7 +573,7 @@ def main():
     ap.add_argument("--ref-tokens-per-step", type=int, default=1)
     ap.add_argument("--no-prefill", action="store_true", help="skip the configuration-3 prefill object")
     ap.add_argument("--prefill-tokens", type=int, default=4096)
-    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--prefill-experts", type=int, default=256,
                     help="routed experts of the prefill case (smaller = a profiling-sized case)")
     ap.add_argument("--only-prefill", action="store_true", help="run the prefill object alone")
