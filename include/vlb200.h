@@ -59,9 +59,25 @@ enum {
     VLB_TYPE_IQ1_S = 19
 };
 
-/* Router scoring (deepseek_v4_reference.cpp:65-69 sqrt_softplus; olmoe_runtime.cpp:1120-1127
- * softmax; sigmoid has no reference router and is an extra mode). */
-enum { VLB_SCORE_SQRT_SOFTPLUS = 0, VLB_SCORE_SIGMOID = 1, VLB_SCORE_SOFTMAX = 2 };
+/* Router scoring:
+ *   VLB_SCORE_SQRT_SOFTPLUS   sqrt_softplus scores, bias-selected top-k, renormalised weights times
+ *                             route_scale (deepseek_v4_reference.cpp:65-69, 80-121, 223-307);
+ *   VLB_SCORE_SIGMOID         the same with a sigmoid score (no reference router: an extra mode);
+ *   VLB_SCORE_SOFTMAX         OLMoE: f32 softmax probabilities, top-k, no renormalisation
+ *                             (olmoe_runtime.cpp:1120-1137);
+ *   VLB_SCORE_SOFTMAX_F64     Qwen: f64 softmax, top-k by probability, weights f32(prob)
+ *                             (qwen38_moe_route, qwen3_8_flash_next_reference.cpp:1186-1239 with
+ *                             norm_topk_prob = false);
+ *   VLB_SCORE_SOFTMAX_F64_NORM the same with norm_topk_prob = true (weights rescaled by the inverse
+ *                             of the selected probabilities' sum).
+ * The softmax modes ignore bias and route_scale. */
+enum {
+    VLB_SCORE_SQRT_SOFTPLUS = 0,
+    VLB_SCORE_SIGMOID = 1,
+    VLB_SCORE_SOFTMAX = 2,
+    VLB_SCORE_SOFTMAX_F64 = 3,
+    VLB_SCORE_SOFTMAX_F64_NORM = 4
+};
 
 typedef struct vlb_handle vlb_handle;
 typedef struct vlb_matrix vlb_matrix;
@@ -198,6 +214,17 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* layer, const float* x_host,
  * threshold in force (0 for a null argument). The prefill pipeline's waits are time-bounded: a
  * wait that runs out makes vlb_layer_forward return VLB_ERR_INTERNAL_ERROR. */
 int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* layer, uint32_t min_tokens);
+
+/* Residual-block entry and exit. With an input norm set (weight: host f32 [hidden], copied; eps >
+ * 0), every forward of plain token rows computes
+ *     out = x + MoE(RMSNorm(x))
+ * RMSNorm is deepseek_v4_rms_norm (deepseek_v4_reference.cpp:170-206: sequential f64 sum of
+ * squares, bit-identical) fused with the entry step of the layer, the router and the experts run
+ * on the normalised rows, and the residual is one f32 addition fused into the combine - the
+ * composition between the MoE layers of a hash-routed chain (configuration 2). weight = NULL
+ * removes it. Rows must be 16-byte aligned; given-routes and half-row forwards are refused while
+ * it is set. */
+int vlb_layer_set_input_norm(vlb_handle* h, vlb_layer* layer, const float* weight, float eps);
 uint32_t vlb_layer_prefill_tokens(vlb_handle* h, vlb_layer* layer);
 
 /* Given-routes forward (an expert-parallel group): idx_dev u32 [T x k] expert ids of this layer
@@ -282,19 +309,20 @@ int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* lo
                      const uint32_t* tid2eid_dev, uint32_t vocab, uint32_t T, uint32_t E,
                      uint32_t k, float route_scale, uint32_t* idx_dev, float* weights_dev,
                      void* stream);
-/* The same router as vlb_route_device for callers that cannot allocate device memory: code
- * running inside a CUDA host callback (where CUDA API calls such as cudaMalloc are not
- * permitted), a runtime whose ResourceGovernor is refusing new reservations under memory
- * pressure, and decode loops that cannot take the synchronisation cudaMalloc/cudaFree may cause.
+/* The same router as vlb_route_device for callers that cannot allocate device memory: a runtime
+ * whose ResourceGovernor is refusing new reservations under memory pressure, callers that may not
+ * call cudaMalloc at all, and decode loops that cannot take the synchronisation cudaMalloc/cudaFree
+ * may cause (vlb_route_device grows its handle's scratch with cudaMalloc when a call needs more).
  * This entry point has no counterpart in the reference. It allocates nothing: its score scratch
  * is a fixed 1 MiB array inside the library, present on every GPU that loads the library until
  * the process exits, so T*E may be at most 262,080 (larger requests return
  * VLB_ERR_RESOURCE_EXHAUSTED). The caller passes device inputs and outputs as for
- * vlb_route_device and the device ordinal to run on (made current for the call). The first call
- * on each device also performs a one-time set-up (it looks up the array's device address), so
- * make that first call before any stream capture. Every call uses the same array: calls that
- * overlap on the GPU (other streams, other host threads) race on it; serialise them. Synchronous:
- * returns after the route is written. */
+ * vlb_route_device and the device ordinal to run on (made current for the call, the caller's
+ * device restored after). The first call on each device also performs a one-time set-up (it
+ * looks up the array's device address). Every call uses the same array: calls that overlap on
+ * the GPU (other streams, other host threads) race on it; serialise them. It is ordinary host
+ * code: it synchronises `stream` before returning (the route is written then), so it must not be
+ * called from a CUDA host callback or while a stream capture is open. */
 int vlb_route_device_noalloc(int ordinal, int score, int hash_routing, const float* logits_dev,
                              const float* bias_dev, const uint32_t* token_ids_dev,
                              const uint32_t* tid2eid_dev, uint32_t vocab, uint32_t T, uint32_t E,

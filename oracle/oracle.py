@@ -76,8 +76,8 @@ class _LayerBuilder:
         L.hash_routing = 1 if s.hash_routing else 0
         L.weight_after_down = 1 if s.weight_after_down else 0
         L.route_scale = s.route_scale
-        L.routed_swiglu_limit = 0.0
-        L.shared_swiglu_limit = 0.0
+        L.routed_swiglu_limit = s.routed_swiglu_limit
+        L.shared_swiglu_limit = s.shared_swiglu_limit
         self.keep += [W.router, W.bias, W.tid2eid]
         L.router = W.router.ctypes.data
         L.bias = None if W.bias is None else W.bias.ctypes.data
@@ -138,6 +138,8 @@ class Oracle:
         L.vlo_route_learned.argtypes = [P, P, SZ, SZ, SZ, F, I, P, P]
         L.vlo_route_hash.argtypes = [P, P, P, SZ, SZ, SZ, SZ, F, I, P, P]
         L.vlo_route_softmax.argtypes = [P, SZ, SZ, SZ, P, P]
+        L.vlo_route_softmax_f64.argtypes = [P, SZ, SZ, SZ, I, P, P]
+        L.vlo_expert_swiglu.argtypes = [P, P, P, P, P, SZ, SZ, SZ, F, P]
         L.vlo_dispatch.argtypes = [P, SZ, SZ, SZ, P, P, P]
         L.vlo_dispatch.restype = None
         L.vlo_rms_norm.argtypes = [P, P, SZ, SZ, F, P]
@@ -208,6 +210,29 @@ class Oracle:
         self.lib.vlo_route_softmax(_p(logits), T, E, k, _p(idx), _p(w))
         return idx, w
 
+    def route_softmax_f64(self, logits, k, norm=True):
+        """qwen38_moe_route on given logits (f64 softmax, top-k, optional norm_topk_prob)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        T, E = logits.shape
+        idx = np.empty((T, k), np.uint32)
+        w = np.empty((T, k), np.float32)
+        if self.lib.vlo_route_softmax_f64(_p(logits), T, E, k, 1 if norm else 0, _p(idx), _p(w)):
+            raise ValueError("oracle f64 softmax route failed")
+        return idx, w
+
+    def expert_swiglu(self, x, gate_w, down_w, up_w, routing_weights, limit):
+        """deepseek_v4_expert_swiglu on float weights (gate/up [I, H], down [H, I])."""
+        x = np.ascontiguousarray(x, np.float32)
+        T, H = x.shape
+        I = gate_w.shape[0]
+        out = np.empty((T, H), np.float32)
+        rw = None if routing_weights is None else np.ascontiguousarray(routing_weights, np.float32)
+        if self.lib.vlo_expert_swiglu(_p(x), _p(np.ascontiguousarray(gate_w, np.float32)),
+                                      _p(np.ascontiguousarray(down_w, np.float32)),
+                                      _p(np.ascontiguousarray(up_w, np.float32)), _p(rw), T, H, I, limit, _p(out)):
+            raise ValueError("oracle expert_swiglu failed")
+        return out
+
     def dispatch(self, idx, E):
         idx = np.ascontiguousarray(idx, np.uint32)
         T, k = idx.shape
@@ -240,6 +265,30 @@ class Oracle:
         return out, idx, w
 
 
+def per_token(forward, W, x, token_ids=None, logits=None, threads: int = 0):
+    """Runs a layer forward one token at a time on a thread pool and stacks the results.
+
+    Every reference router and layer loop treats the tokens of a batch independently (per-token
+    routing; each token's output is the sum of its own expert outputs in a fixed order), so the
+    per-token results equal the batched call's. ctypes releases the GIL during the foreign call,
+    so the threads run in parallel; this keeps full-size parity checks to seconds."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    T = x.shape[0]
+    n = threads or min(T, os.cpu_count() or 1)
+
+    def one(t):
+        tok = None if token_ids is None else token_ids[t:t + 1]
+        lg = None if logits is None else logits[t:t + 1]
+        return forward(W, x[t:t + 1], tok, lg)
+
+    with ThreadPoolExecutor(max_workers=max(1, n)) as ex:
+        parts = list(ex.map(one, range(T)))
+    return (np.concatenate([p[0] for p in parts]), np.concatenate([p[1] for p in parts]),
+            np.concatenate([p[2] for p in parts]))
+
+
 class Reference:
     """The vastloom reference compiled from its sources (oracle/_ref)."""
 
@@ -262,6 +311,8 @@ class Reference:
         L.vlr_route_hash.argtypes = [P, P, P, SZ, SZ, SZ, SZ, F, P, P]
         L.vlr_rms_norm.argtypes = [P, P, SZ, SZ, F, P]
         L.vlr_moe_forward.argtypes = [C.POINTER(_RefLayer), P, P, SZ, P, P, P, P, C.c_uint]
+        L.vlr_qwen_route.argtypes = [P, P, SZ, SZ, SZ, SZ, I, P, P, P]
+        L.vlr_expert_swiglu.argtypes = [P, P, P, P, P, SZ, SZ, SZ, F, P]
 
     def grid(self, t: int) -> bytes:
         n = self.lib.vlr_grid(t, None, 0)
@@ -309,6 +360,31 @@ class Reference:
                                    T, table.size // k, E, k, route_scale, _p(idx), _p(w)):
             raise ValueError("reference hash route failed")
         return idx, w
+
+    def qwen_route(self, hidden, router, k, norm=True):
+        """qwen38_moe_route per token: returns (logits, indices, weights)."""
+        hidden = np.ascontiguousarray(hidden, np.float32)
+        router = np.ascontiguousarray(router, np.float32)
+        T, H = hidden.shape
+        E = router.shape[0]
+        lg = np.empty((T, E), np.float32)
+        idx = np.empty((T, k), np.uint32)
+        w = np.empty((T, k), np.float32)
+        if self.lib.vlr_qwen_route(_p(hidden), _p(router), T, H, E, k, 1 if norm else 0, _p(lg), _p(idx), _p(w)):
+            raise ValueError("reference qwen route failed")
+        return lg, idx, w
+
+    def expert_swiglu(self, x, gate_w, down_w, up_w, routing_weights, limit):
+        x = np.ascontiguousarray(x, np.float32)
+        T, H = x.shape
+        I = gate_w.shape[0]
+        out = np.empty((T, H), np.float32)
+        rw = None if routing_weights is None else np.ascontiguousarray(routing_weights, np.float32)
+        if self.lib.vlr_expert_swiglu(_p(x), _p(np.ascontiguousarray(gate_w, np.float32)),
+                                      _p(np.ascontiguousarray(down_w, np.float32)),
+                                      _p(np.ascontiguousarray(up_w, np.float32)), _p(rw), T, H, I, limit, _p(out)):
+            raise ValueError("reference expert_swiglu failed")
+        return out
 
     def rms_norm(self, x, w, eps):
         x = np.ascontiguousarray(x, np.float32)

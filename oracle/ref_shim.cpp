@@ -16,6 +16,7 @@
 
 #include "vastloom/inference/deepseek_v4_reference.hpp"
 #include "vastloom/inference/ggml_quantization.hpp"
+#include "vastloom/inference/qwen3_8_flash_next_reference.hpp"
 
 namespace vi = vastloom::inference;
 
@@ -129,6 +130,35 @@ int vlr_rms_norm(const float* x, const float* w, size_t rows, size_t width, floa
     auto r = vi::deepseek_v4_rms_norm({x, rows * width}, {w, width}, rows, width, eps);
     if (!r) return -1;
     std::memcpy(out, r.value().data(), rows * width * sizeof(float));
+    return 0;
+}
+
+// qwen38_moe_route (qwen3_8_flash_next_reference.cpp:1186-1239) for T tokens: hidden [T x H],
+// router [E x H]; logits [T x E] (may be null), idx / w [T x k].
+int vlr_qwen_route(const float* hidden, const float* router, size_t T, size_t H, size_t E, size_t k,
+                   int norm, float* logits, uint32_t* idx, float* w) {
+    for (size_t t = 0; t < T; ++t) {
+        auto r = vi::qwen38_moe_route({hidden + t * H, H}, {router, E * H}, static_cast<uint32_t>(E),
+                                      static_cast<uint32_t>(k), norm != 0);
+        if (!r) return -1;
+        if (logits) std::memcpy(logits + t * E, r.value().logits.data(), E * sizeof(float));
+        std::memcpy(idx + t * k, r.value().indices.data(), k * sizeof(uint32_t));
+        std::memcpy(w + t * k, r.value().weights.data(), k * sizeof(float));
+    }
+    return 0;
+}
+
+// deepseek_v4_expert_swiglu (deepseek_v4_reference.cpp:309-385); routing_weights may be null.
+int vlr_expert_swiglu(const float* x, const float* gate_w, const float* down_w, const float* up_w,
+                      const float* routing_weights, size_t T, size_t width, size_t inter, float limit,
+                      float* out) {
+    auto r = vi::deepseek_v4_expert_swiglu({x, T * width}, {gate_w, inter * width}, {down_w, width * inter},
+                                           {up_w, inter * width},
+                                           routing_weights ? std::span<const float>(routing_weights, T)
+                                                           : std::span<const float>(),
+                                           T, width, inter, limit);
+    if (!r) return -1;
+    std::memcpy(out, r.value().data(), T * width * sizeof(float));
     return 0;
 }
 

@@ -371,6 +371,48 @@ int vlo_route_softmax(const float* logits, size_t T, size_t E, size_t k, uint32_
     return 0;
 }
 
+/* Qwen router, qwen38_moe_route (qwen3_8_flash_next_reference.cpp:1186-1239) on given logits:
+ * probs = exp(double(l) - max) in double, summed in expert order, prob = probs * (1 / sum); all
+ * experts ranked by prob (larger first, ties to the lower id); weights = f32(prob), and with
+ * norm_topk_prob each weight becomes f32(double(weight) * (1 / top_sum)) where top_sum adds the
+ * selected probs in rank order. */
+int vlo_route_softmax_f64(const float* logits, size_t T, size_t E, size_t k, int norm,
+                          uint32_t* idx, float* weights) {
+    if (k == 0 || k > E) return -1;
+    double* p = (double*)malloc(E * sizeof(double));
+    unsigned char* used = (unsigned char*)malloc(E);
+    for (size_t t = 0; t < T; ++t) {
+        const float* l = logits + t * E;
+        double mx = (double)l[0];
+        for (size_t e = 0; e < E; ++e) if ((double)l[e] > mx) mx = (double)l[e];
+        double sum = 0.0;
+        for (size_t e = 0; e < E; ++e) { p[e] = exp((double)l[e] - mx); sum += p[e]; }
+        const double inv = sum > 0.0 ? 1.0 / sum : 0.0;
+        for (size_t e = 0; e < E; ++e) p[e] = p[e] * inv;
+        memset(used, 0, E);
+        double top = 0.0;
+        for (size_t s = 0; s < k; ++s) {
+            size_t best = E;
+            for (size_t e = 0; e < E; ++e) {
+                if (used[e]) continue;
+                if (best == E || p[e] > p[best]) best = e;
+            }
+            used[best] = 1;
+            idx[t * k + s] = (uint32_t)best;
+            weights[t * k + s] = (float)p[best];
+            top += p[best];
+        }
+        if (norm && top > 0.0) {
+            const double sc = 1.0 / top;
+            for (size_t s = 0; s < k; ++s)
+                weights[t * k + s] = (float)((double)weights[t * k + s] * sc);
+        }
+    }
+    free(p);
+    free(used);
+    return 0;
+}
+
 /* The dispatch permutation. The reference visits experts in ascending id, then tokens, then
  * slots (deepseek_v4_graph.cpp:2134-2223); this is that visit order written out as a stable
  * counting sort. */
@@ -417,6 +459,51 @@ static int mv(const vlo_moe_layer* L, const vlo_matrix* m, const float* x, float
     return vlo_matvec(m->type, m->data, m->rows, m->cols, x, y, grid_for(L, m->type));
 }
 
+/* The DeepSeek V4 SwiGLU of one gate/up pair, in double: with a positive limit L the gate is
+ * clamped to min(g, L) and the up value to [-L, L]; silu(g) * u, times the route weight when one
+ * is given. Shared by execute_expert (deepseek_v4_graph.cpp:1865-1890) and
+ * deepseek_v4_expert_swiglu (deepseek_v4_reference.cpp:350-365), which differ only in where g and
+ * u come from (f32 matvec outputs there, f64 sums here). */
+static double v4_swiglu(double g, double u, float limit, const float* route_w) {
+    if (limit > 0.0f) {
+        if (g > (double)limit) g = (double)limit;
+        if (u < -(double)limit) u = -(double)limit;
+        if (u > (double)limit) u = (double)limit;
+    }
+    double v = g / (1.0 + exp(-g)) * u;
+    if (route_w) v *= (double)*route_w;
+    return v;
+}
+
+/* deepseek_v4_expert_swiglu, deepseek_v4_reference.cpp:309-385: float weights, gate and up kept in
+ * double (column-order sums), clamp and SwiGLU in double, activation rounded to f32, down product
+ * in double. routing_weights may be NULL. */
+int vlo_expert_swiglu(const float* x, const float* gate_w, const float* down_w, const float* up_w,
+                      const float* routing_weights, size_t T, size_t width, size_t inter,
+                      float limit, float* out) {
+    if (T == 0 || width == 0 || inter == 0 || !(limit >= 0.0f) || !isfinite(limit)) return -1;
+    float* act = (float*)malloc(T * inter * sizeof(float));
+    for (size_t t = 0; t < T; ++t)
+        for (size_t r = 0; r < inter; ++r) {
+            double g = 0.0, u = 0.0;
+            for (size_t c = 0; c < width; ++c) {
+                const double v = (double)x[t * width + c];
+                g += v * (double)gate_w[r * width + c];
+                u += v * (double)up_w[r * width + c];
+            }
+            act[t * inter + r] = (float)v4_swiglu(g, u, limit, routing_weights ? routing_weights + t : NULL);
+        }
+    for (size_t t = 0; t < T; ++t)
+        for (size_t r = 0; r < width; ++r) {
+            double sum = 0.0;
+            for (size_t c = 0; c < inter; ++c)
+                sum += (double)act[t * inter + c] * (double)down_w[r * inter + c];
+            out[t * width + r] = (float)sum;
+        }
+    free(act);
+    return 0;
+}
+
 /* execute_expert, deepseek_v4_graph.cpp:1826-1895, for one token: gate and up products, SwiGLU
  * in double with the optional clamp, route weight applied BEFORE the down product. */
 static int v4_expert(const vlo_moe_layer* L, const vlo_matrix* w1, const vlo_matrix* w3,
@@ -425,18 +512,8 @@ static int v4_expert(const vlo_moe_layer* L, const vlo_matrix* w1, const vlo_mat
     int st = mv(L, w1, x, gate);
     if (!st) st = mv(L, w3, x, up);
     if (st) return st;
-    for (size_t c = 0; c < L->intermediate; ++c) {
-        double g = (double)gate[c];
-        double u = (double)up[c];
-        if (limit > 0.0f) {
-            if (g > (double)limit) g = (double)limit;
-            if (u < -(double)limit) u = -(double)limit;
-            if (u > (double)limit) u = (double)limit;
-        }
-        double v = g / (1.0 + exp(-g)) * u;
-        if (route_w) v *= (double)*route_w;
-        act[c] = (float)v;
-    }
+    for (size_t c = 0; c < L->intermediate; ++c)
+        act[c] = (float)v4_swiglu((double)gate[c], (double)up[c], limit, route_w);
     return mv(L, w2, act, out);
 }
 
@@ -469,6 +546,8 @@ int vlo_moe_forward(const vlo_moe_layer* L, const float* x, const uint32_t* toke
     if (logits_in) memcpy(logits, logits_in, T * E * sizeof(float));
     else vlo_router_logits(x, L->router, T, H, E, logits);
     if (L->score == VLO_SCORE_SOFTMAX) st = vlo_route_softmax(logits, T, E, k, idx, weights);
+    else if (L->score == VLO_SCORE_SOFTMAX_F64 || L->score == VLO_SCORE_SOFTMAX_F64_NORM)
+        st = vlo_route_softmax_f64(logits, T, E, k, L->score == VLO_SCORE_SOFTMAX_F64_NORM, idx, weights);
     else if (L->hash_routing)
         st = vlo_route_hash(logits, token_ids, L->tid2eid, T, L->vocab, E, k, L->route_scale,
                             L->score, idx, weights);

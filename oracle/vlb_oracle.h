@@ -34,6 +34,8 @@ extern "C" {
 #define VLO_SCORE_SQRT_SOFTPLUS 0
 #define VLO_SCORE_SIGMOID 1
 #define VLO_SCORE_SOFTMAX 2
+#define VLO_SCORE_SOFTMAX_F64 3      /* Qwen: qwen38_moe_route, norm_topk_prob = false */
+#define VLO_SCORE_SOFTMAX_F64_NORM 4 /* Qwen: qwen38_moe_route, norm_topk_prob = true */
 
 int vlo_block_layout(uint32_t type, size_t* block_elems, size_t* block_bytes);
 float vlo_fp16_to_float(uint16_t v);
@@ -62,6 +64,12 @@ int vlo_route_hash(const float* logits, const uint32_t* token_ids, const uint32_
                    uint32_t* idx, float* weights);
 int vlo_route_softmax(const float* logits, size_t T, size_t E, size_t k, uint32_t* idx,
                       float* weights);
+int vlo_route_softmax_f64(const float* logits, size_t T, size_t E, size_t k, int norm,
+                          uint32_t* idx, float* weights);
+/* deepseek_v4_expert_swiglu on float weights (gate/up [inter x width], down [width x inter]). */
+int vlo_expert_swiglu(const float* x, const float* gate_w, const float* down_w, const float* up_w,
+                      const float* routing_weights, size_t T, size_t width, size_t inter,
+                      float limit, float* out);
 /* Stable counting sort of (token, slot) pairs by expert: offsets[E+1], pair_token/pair_slot[T*k]
  * ordered by expert ascending, then token, then slot. */
 void vlo_dispatch(const uint32_t* idx, size_t T, size_t k, size_t E, uint32_t* offsets,

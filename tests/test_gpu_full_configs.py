@@ -1,0 +1,286 @@
+"""Full-size parity on every benchmark configuration, plus the router, RMSNorm and SwiGLU-clamp
+pieces the configurations depend on, through the vlb200 C ABI against the CPU oracle.
+
+Bit-exact: router logits (sequential f64 sums), RMSNorm rows, routing indices, permutation maps.
+Route weights: within 1 ulp (the only difference left is CUDA's double exp / log1p against
+glibc's; 2 ulp for the OLMoE router, whose CPU side uses glibc expf). Layer outputs: within 1e-5
+norm-wise relative error on the decode path (f32 accumulation of exact products against the
+reference's f64 sums) and 2e-2 on the tensor-core prefill path (4e-3 expected).
+
+The oracle runs per token on a thread pool (oracle.per_token): every router and layer loop of
+the reference treats the tokens of a batch independently, so this equals the batched call and
+keeps each full-size check to seconds."""
+
+from dataclasses import replace
+
+import numpy as np
+import pytest
+
+import vastloom_b200 as vb
+from conftest import rel_err
+from oracle.oracle import per_token
+from vastloom_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+PREFILL_EXPECTED = 4e-3
+
+
+def ulp_diff(a, b):
+    a = np.ascontiguousarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.ascontiguousarray(b, np.float32).view(np.int32).astype(np.int64)
+    return int(np.max(np.abs(a - b))) if a.size else 0
+
+
+def _release(device, layer):
+    layer.destroy()
+    for lst in layer.matrices.values():
+        for m in lst:
+            device.release_matrix(m)
+    for m in layer.shared_matrices or ():
+        device.release_matrix(m)
+
+
+def _check_layer(layer, oracle, W, x, tok=None, logits=None, tol=TOL):
+    """Forward on the device, oracle per token; routes and permutation bit-exact, outputs within
+    tol. Returns the device output."""
+    spec = W.spec
+    T = x.shape[0]
+    out = layer.forward(x, tok, logits)
+    ref, ridx, rw = per_token(oracle.moe_forward, W, x, tok, logits)
+    idx, w, off, pt, ps = layer.last_route(T)
+    assert np.array_equal(idx, ridx)
+    assert ulp_diff(w, rw) <= (2 if spec.score == vb.SCORE_SOFTMAX else 1)
+    roff, rpt, rps = oracle.dispatch(ridx, spec.experts)
+    assert np.array_equal(off, roff) and np.array_equal(pt, rpt) and np.array_equal(ps, rps)
+    assert np.all(np.isfinite(out))
+    assert rel_err(out, ref) <= tol, rel_err(out, ref)
+    return out
+
+
+# ---- router projection and RMSNorm: bit-exact ---------------------------------------------------
+
+@pytest.mark.parametrize("T,E,H", [(64, 256, 4096), (1, 64, 2048), (8, 256, 4096), (5, 17, 260),
+                                   (300, 64, 2048)])
+def test_gpu_router_logits_bit_exact(device, oracle, T, E, H):
+    """logits = f32(sum over columns in order of double(x) * double(w)) (deepseek_v4_graph.cpp:
+    735-767): the device walks each (token, expert) sum in column order, so every logit has the
+    reference's bits - not merely its value to an ulp."""
+    rng = np.random.default_rng(T * 7 + E + H)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    w = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    assert device.router_logits(x, w).tobytes() == oracle.router_logits(x, w).tobytes()
+
+
+@pytest.mark.parametrize("rows,width", [(1, 4096), (5, 4096), (3, 2048), (2, 260)])
+def test_gpu_rms_norm_bit_exact(device, oracle, rows, width):
+    rng = np.random.default_rng(rows + width)
+    x = (rng.standard_normal((rows, width)) * 3.0).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(width)).astype(np.float32)
+    assert device.rms_norm(x, w, 1e-6).tobytes() == oracle.rms_norm(x, w, 1e-6).tobytes()
+
+
+def test_gpu_rms_norm_fixture(device, oracle):
+    import json
+    from pathlib import Path
+
+    golden = json.loads((Path(__file__).parent / "golden" / "deepseek_v4_operators.json").read_text())
+    f = golden["rms_norm"]
+    x = np.array(f["input"], np.float32).reshape(f["rows"], f["width"])
+    w = np.array(f["weight"], np.float32)
+    out = device.rms_norm(x, w, f["epsilon"])
+    assert out.tobytes() == oracle.rms_norm(x, w, f["epsilon"]).tobytes()
+    assert np.max(np.abs(out.reshape(-1) - np.array(f["expected"]))) <= golden["absolute_tolerance"]
+
+
+# ---- the Qwen router (qwen38_moe_route) --------------------------------------------------------
+
+@pytest.mark.parametrize("score", [vb.SCORE_SOFTMAX_F64, vb.SCORE_SOFTMAX_F64_NORM])
+@pytest.mark.parametrize("T,E,k", [(64, 512, 10), (17, 64, 8), (3, 128, 16)])
+def test_gpu_qwen_route(device, oracle, score, T, E, k):
+    """f64 softmax, all experts ranked by probability (ties to the lower id), weights f32(prob),
+    renormalised by the rank-order sum with norm_topk_prob; the oracle is pinned bit for bit to
+    the reference's qwen38_moe_route (tests/test_oracle_kats.py)."""
+    rng = np.random.default_rng(T + E + k + score)
+    logits = (rng.standard_normal((T, E)) * 2.0).astype(np.float32)
+    logits[0, :4] = logits[0, 4]  # an exact tie in the top group
+    idx, w = device.route(logits, k, score=score)
+    ri, rw = oracle.route_softmax_f64(logits, k, norm=score == vb.SCORE_SOFTMAX_F64_NORM)
+    assert np.array_equal(idx, ri)
+    assert ulp_diff(w, rw) <= 1
+
+
+def test_gpu_qwen_route_reference_vector(device):
+    """tests/test_main.cpp:3966-3990 through the device router and route."""
+    x = np.array([[1.0, 0.0]], np.float32)
+    r = np.array([[1, 0], [0, 1], [1, 1]], np.float32)
+    logits = device.router_logits(np.pad(x, ((0, 0), (0, 2))), np.pad(r, ((0, 0), (0, 2))))
+    assert logits.tolist() == [[1.0, 0.0, 1.0]]
+    idx, w = device.route(logits, 2, score=vb.SCORE_SOFTMAX_F64_NORM)
+    assert idx.tolist() == [[0, 2]] and np.all(np.abs(w - 0.5) < 1e-5)
+
+
+def test_gpu_layer_qwen_router(device, oracle):
+    """A layer routed by the Qwen router (OLMoE-style combine): routes bit-exact, outputs 1e-5."""
+    spec = replace(synth.config(0, "small"), score=vb.SCORE_SOFTMAX_F64_NORM, name="qwen-router")
+    W = synth.layer_weights(spec, seed=77)
+    x, tok, logits = synth.activations(spec, 9, seed=78)
+    layer = synth.upload_layer(device, W, max_tokens=16)
+    try:
+        _check_layer(layer, oracle, W, x, tok, logits)
+    finally:
+        _release(device, layer)
+
+
+# ---- SwiGLU clamp ------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("limits", [(0.02, 0.05), (10.0, 10.0)])
+@pytest.mark.parametrize("prefill", [False, True])
+@pytest.mark.parametrize("cfg", [1, 2])
+def test_gpu_layer_swiglu_clamp(device, oracle, limits, prefill, cfg):
+    """execute_expert's clamp (deepseek_v4_graph.cpp:1878-1884: gate <= L, -L <= up <= L, in double)
+    on the decode kernels, the CUDA-core IQ3_XXS / IQ1_S kernels (config 2) and the prefill
+    epilogue. 10.0 is the real model's limit (tests/test_main.cpp:2836); 0.02 / 0.05 clamp most
+    gate and up values of these layers, so the test fails if any kernel skips or misplaces it."""
+    spec = replace(synth.config(cfg, "small"), routed_swiglu_limit=limits[0], shared_swiglu_limit=limits[1])
+    W = synth.layer_weights(spec, seed=700 + cfg)
+    x, tok, logits = synth.activations(spec, 37, seed=710 + cfg)
+    layer = synth.upload_layer(device, W, max_tokens=64)
+    try:
+        if prefill:
+            layer.set_prefill_tokens(1)
+        out = _check_layer(layer, oracle, W, x, tok, logits, tol=PREFILL_EXPECTED if prefill else TOL)
+        if limits[0] < 1.0:
+            unclamped, _, _ = oracle.moe_forward(replace(W, spec=replace(spec, routed_swiglu_limit=0.0,
+                                                                        shared_swiglu_limit=0.0)), x, tok, logits)
+            assert rel_err(out, unclamped) > 10 * (PREFILL_EXPECTED if prefill else TOL)
+    finally:
+        _release(device, layer)
+
+
+# ---- configuration 0: OLMoE-shaped, full size ----------------------------------------------------
+
+@pytest.fixture(scope="module")
+def full_cfg0(device):
+    spec = synth.config(0)
+    W = synth.layer_weights(spec, seed=10)
+    layer = synth.upload_layer(device, W, max_tokens=16)
+    yield W, layer
+    _release(device, layer)
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_gpu_full_cfg0(full_cfg0, oracle, T):
+    """H=2048, 64 Q8_0 experts of I=1024, top-8 softmax without renormalisation, rank-order
+    combine with the weight after the down product; batches of 1 and 16 tokens."""
+    W, layer = full_cfg0
+    x, _, _ = synth.activations(W.spec, T, seed=20 + T)
+    _check_layer(layer, oracle, W, x)
+
+
+# ---- configuration 1: DeepSeek-V4-Flash-shaped decode, full size ----------------------------------
+
+@pytest.fixture(scope="module")
+def full_cfg1(device):
+    spec = synth.config(1)
+    W = synth.layer_weights(spec, seed=1)
+    layer = synth.upload_layer(device, W, max_tokens=64)
+    yield W, layer
+    _release(device, layer)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_gpu_full_cfg1(full_cfg1, oracle, T):
+    """H=4096, 256 IQ2_XXS experts of I=2048 + the Q8_0 shared expert, sqrt-softplus top-8 with
+    bias and renormalisation; every token of the batch against the oracle."""
+    W, layer = full_cfg1
+    x, _, _ = synth.activations(W.spec, T, seed=30 + T)
+    _check_layer(layer, oracle, W, x)
+
+
+def test_gpu_full_cfg1_sigmoid(device, oracle, full_cfg1):
+    """BASELINE's wording of configuration 1: sigmoid gating (no reference router: parity against
+    the restatement only)."""
+    W, _ = full_cfg1
+    spec = replace(W.spec, score=vb.SCORE_SIGMOID)
+    Ws = replace(W, spec=spec)
+    layer = synth.upload_layer(device, Ws, max_tokens=8)
+    try:
+        x, _, _ = synth.activations(spec, 8, seed=39)
+        _check_layer(layer, oracle, Ws, x)
+    finally:
+        _release(device, layer)
+
+
+# ---- configuration 2: hash-routed three-layer chain, full size -----------------------------------
+
+@pytest.fixture(scope="module")
+def full_cfg2(device):
+    spec = synth.config(2)
+    Ws = [synth.layer_weights(spec, seed=40 + i) for i in range(3)]
+    layers = [synth.upload_layer(device, W, max_tokens=8, layer_index=i) for i, W in enumerate(Ws)]
+    yield Ws, layers
+    for layer in layers:
+        _release(device, layer)
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_gpu_full_cfg2_single_layer(full_cfg2, oracle, T):
+    """One layer of configuration 2: IQ1_S gate/up and IQ3_XXS down experts at 4096 x 2048, the
+    Q8_0 shared expert, token-id hash routing over the full 129,280-entry table (6 experts, equal
+    weights from the zero gate matrix)."""
+    Ws, layers = full_cfg2
+    W, layer = Ws[0], layers[0]
+    layer.set_input_norm(None)
+    x, tok, _ = synth.activations(W.spec, T, seed=50 + T)
+    assert int(np.max(tok)) > 1000  # ids beyond any small table
+    _check_layer(layer, oracle, W, x, tok)
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_gpu_full_cfg2_chain(device, full_cfg2, oracle, T):
+    """The three-layer chain x <- x + MoE(RMSNorm(x)) (unit weight, eps 1e-6) on the device (norm
+    fused into each layer's entry, residual into its combine, no host round trip between layers)
+    against the oracle's RMSNorm, layer loop and f32 residual addition."""
+    Ws, layers = full_cfg2
+    H = Ws[0].spec.hidden
+    x, tok, _ = synth.activations(Ws[0].spec, T, seed=60 + T)
+    for layer in layers:
+        layer.set_input_norm(np.ones(H, np.float32), 1e-6)
+    chain = vb.LayerChain(device, layers, max_tokens=8)
+    try:
+        out = chain.forward(x, tok)
+    finally:
+        chain.close()
+        for layer in layers:
+            layer.set_input_norm(None)
+    ref = x.copy()
+    for W in Ws:
+        xn = oracle.rms_norm(ref, np.ones(H, np.float32), 1e-6)
+        moe, _, _ = per_token(oracle.moe_forward, W, xn, tok)
+        ref = (ref + moe).astype(np.float32)
+    assert np.all(np.isfinite(out))
+    assert rel_err(out, ref) <= TOL, rel_err(out, ref)
+
+
+# ---- configuration 3: prefill at full size, more tokens against the oracle ----------------------
+
+def test_gpu_full_cfg3_prefill_sampled(device, oracle):
+    """4096 tokens through the tensor-core prefill path; 128 tokens spread over the batch (every
+    32nd) against the oracle, on top of the whole-batch comparisons in test_gpu_prefill.py."""
+    spec = synth.config(3)
+    W = synth.layer_weights(spec, seed=3)
+    layer = synth.upload_layer(device, W, max_tokens=4096)
+    try:
+        x, tok, logits = synth.activations(spec, 4096, seed=35)
+        out = layer.forward(x, tok, logits)
+        sel = np.arange(0, 4096, 32)
+        ref, ridx, _ = per_token(oracle.moe_forward, W, x[sel], None, logits[sel])
+        idx, *_ = layer.last_route(4096)
+        assert np.array_equal(idx[sel], ridx)
+        assert rel_err(out[sel], ref) <= PREFILL_EXPECTED
+        num = np.linalg.norm((out[sel] - ref).astype(np.float64), axis=1)
+        assert float(np.max(num / np.linalg.norm(ref.astype(np.float64), axis=1))) <= 1e-2
+    finally:
+        _release(device, layer)

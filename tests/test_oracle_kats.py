@@ -182,3 +182,83 @@ def test_routed_expert_zero_weights_give_zero(oracle):
     y = oracle.matvec(19, enc, 256, 256, np.full(256, 0.25, np.float32))
     assert np.all(y == 0.0)
     assert rel_err(y, y) == 0.0
+
+
+# ---- SwiGLU clamp and the Qwen router -----------------------------------------------------
+
+def test_oracle_expert_swiglu_fixture(oracle, reference):
+    """The clamped SwiGLU the layer loops share, pinned to the reference's `expert` fixture
+    (swiglu_limit 0.35, consumed by tests/test_main.cpp:4503-4516) and to the reference's
+    deepseek_v4_expert_swiglu itself, bit for bit."""
+    f = GOLDEN["expert"]
+    T, H, I = f["tokens"], f["width"], f["intermediate"]
+    x = np.array(f["input"], np.float32).reshape(T, H)
+    g = np.array(f["gate_weight"], np.float32).reshape(I, H)
+    u = np.array(f["up_weight"], np.float32).reshape(I, H)
+    d = np.array(f["down_weight"], np.float32).reshape(H, I)
+    rw = np.array(f["routing_weights"], np.float32)
+    out = oracle.expert_swiglu(x, g, d, u, rw, f["swiglu_limit"])
+    assert np.max(np.abs(out.reshape(-1) - np.array(f["expected"]))) <= GOLDEN["absolute_tolerance"]
+    assert out.tobytes() == reference.expert_swiglu(x, g, d, u, rw, f["swiglu_limit"]).tobytes()
+    # the clamp changes this fixture's result (the limit is active)
+    assert out.tobytes() != oracle.expert_swiglu(x, g, d, u, rw, 0.0).tobytes()
+
+
+@pytest.mark.parametrize("limit", [0.05, 0.35, 10.0])
+def test_oracle_expert_swiglu_matches_reference_random(oracle, reference, limit):
+    rng = np.random.default_rng(int(limit * 100))
+    T, H, I = 3, 64, 48
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    g, u = (rng.standard_normal((I, H)).astype(np.float32) for _ in range(2))
+    d = rng.standard_normal((H, I)).astype(np.float32)
+    rw = rng.random(T).astype(np.float32)
+    for w in (rw, None):
+        assert oracle.expert_swiglu(x, g, d, u, w, limit).tobytes() == \
+            reference.expert_swiglu(x, g, d, u, w, limit).tobytes()
+
+
+@pytest.mark.parametrize("cfg", [1, 2])
+@pytest.mark.parametrize("limits", [(0.01, 0.02), (10.0, 10.0)])
+def test_oracle_layer_with_clamp_matches_reference(oracle, reference, cfg, limits):
+    """The layer loops with the SwiGLU clamp on (routed and shared limits): 10.0 is the real
+    model's limit (tests/test_main.cpp:2836), 0.01 / 0.02 clamp most gate and up values of these
+    synthetic layers."""
+    from dataclasses import replace
+
+    from vastloom_b200 import synth
+
+    spec = replace(synth.config(cfg, "small"), routed_swiglu_limit=limits[0], shared_swiglu_limit=limits[1])
+    W = synth.layer_weights(spec, seed=600 + cfg)
+    x, tok, logits = synth.activations(spec, 5, seed=610 + cfg)
+    a = oracle.moe_forward(W, x, tok, logits)
+    b = reference.moe_forward(W, x, tok, logits)
+    assert np.array_equal(a[1], b[1]) and a[0].tobytes() == b[0].tobytes()
+    off = oracle.moe_forward(replace(W, spec=replace(spec, routed_swiglu_limit=0.0, shared_swiglu_limit=0.0)),
+                             x, tok, logits)[0]
+    if limits[0] < 1.0:
+        assert a[0].tobytes() != off.tobytes()  # the small limits do clamp
+
+
+def test_oracle_qwen_route_reference_test_vector(oracle):
+    """tests/test_main.cpp:3966-3990: hidden (1, 0), three experts, top-2 with renormalisation."""
+    x = np.array([[1.0, 0.0]], np.float32)
+    r = np.array([[1, 0], [0, 1], [1, 1]], np.float32)
+    logits = oracle.router_logits(x, r)
+    assert logits.tolist() == [[1.0, 0.0, 1.0]]
+    idx, w = oracle.route_softmax_f64(logits, 2, norm=True)
+    assert idx.tolist() == [[0, 2]]
+    assert np.all(np.abs(w - 0.5) < 1e-5)
+
+
+@pytest.mark.parametrize("norm", [True, False])
+@pytest.mark.parametrize("E,k", [(512, 10), (64, 8)])
+def test_oracle_qwen_route_matches_reference(oracle, reference, norm, E, k):
+    rng = np.random.default_rng(E + k + norm)
+    T, H = 6, 256
+    hidden = rng.standard_normal((T, H)).astype(np.float32)
+    router = (rng.standard_normal((E, H)) * 0.05).astype(np.float32)
+    logits = oracle.router_logits(hidden, router)
+    idx, w = oracle.route_softmax_f64(logits, k, norm=norm)
+    rl, ri, rw = reference.qwen_route(hidden, router, k, norm=norm)
+    assert logits.tobytes() == rl.tobytes()
+    assert np.array_equal(idx, ri) and w.tobytes() == rw.tobytes()

@@ -1,11 +1,13 @@
-"""vlb_route_device_noalloc: the router for callers that cannot allocate device memory (code in a
-CUDA host callback, a runtime whose memory governor refuses new reservations, decode loops that
-cannot take the synchronisation of cudaMalloc/cudaFree). Its scratch is a fixed array inside the
-library instead of a per-call allocation.
+"""vlb_route_device_noalloc: the router for callers that cannot allocate device memory (a runtime
+whose memory governor refuses new reservations, callers that may not call cudaMalloc, decode loops
+that cannot take the synchronisation of cudaMalloc/cudaFree). Its scratch is a fixed array inside
+the library instead of an allocation; it is called from ordinary host code (it synchronises its
+stream).
 
-Called through the C ABI and compared with the allocating entry point, vlb_route_device, on two
-calls in a row with different inputs (the shared scratch keeps the previous call's contents, so
-the second call checks that nothing leaks between calls). This file is collected last on purpose.
+Called through the C ABI and compared with the allocating entry point, vlb_route_device, and with
+the CPU oracle, on two calls in a row with different inputs (the shared scratch keeps the previous
+call's contents, so the second call checks that nothing leaks between calls). This file is
+collected last on purpose.
 """
 
 import ctypes as C
@@ -37,13 +39,20 @@ def _noalloc_route(dev, logits_b, bias_b, tok_b, tab_b, vocab, T, E, k, score, s
         w_b.free()
 
 
-@pytest.mark.parametrize("score", [vb.SCORE_SQRT_SOFTPLUS, vb.SCORE_SOFTMAX])
-def test_noalloc_route_matches_allocating_route_twice(device, score):
+def _ulp(a, b):
+    a = np.ascontiguousarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.ascontiguousarray(b, np.float32).view(np.int32).astype(np.int64)
+    return int(np.max(np.abs(a - b)))
+
+
+@pytest.mark.parametrize("score", [vb.SCORE_SQRT_SOFTPLUS, vb.SCORE_SIGMOID, vb.SCORE_SOFTMAX,
+                                   vb.SCORE_SOFTMAX_F64_NORM])
+def test_noalloc_route_matches_allocating_route_twice(device, oracle, score):
     rng = np.random.default_rng(1234 + score)
     for T, E, k in ((64, 256, 8), (7, 64, 4)):  # two calls in a row, different sizes and inputs
         logits = rng.standard_normal((T, E)).astype(np.float32)
         bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
-        use_bias = score != vb.SCORE_SOFTMAX
+        use_bias = score in (vb.SCORE_SQRT_SOFTPLUS, vb.SCORE_SIGMOID)
         want_idx, want_w = device.route(logits, k, 1.5, score=score, bias=bias if use_bias else None)
         lb = device.to_device(logits, "test-logits")
         bb = device.to_device(bias, "test-bias") if use_bias else None
@@ -55,6 +64,38 @@ def test_noalloc_route_matches_allocating_route_twice(device, score):
                 bb.free()
         assert np.array_equal(idx, want_idx)
         assert w.tobytes() == want_w.tobytes()
+        if score == vb.SCORE_SOFTMAX:
+            ri, rw = oracle.route_softmax(logits, k)
+        elif score == vb.SCORE_SOFTMAX_F64_NORM:
+            ri, rw = oracle.route_softmax_f64(logits, k, norm=True)
+        else:
+            ri, rw = oracle.route_learned(logits, bias, k, 1.5, score)
+        assert np.array_equal(idx, ri) and _ulp(w, rw) <= (2 if score == vb.SCORE_SOFTMAX else 1)
+
+
+def test_noalloc_route_on_another_device_restores_the_current_one():
+    """With two GPUs: device 0 current, a call for ordinal 1 runs there (its own copy of the fixed
+    array, looked up on its first call) and leaves device 0 current."""
+    if vb.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import ctypes
+
+    rt = ctypes.CDLL("libcudart.so.12")  # the runtime instance libvlb200.so is linked against
+    cur = ctypes.c_int(-1)
+    with vb.Device(1) as dev1:
+        rng = np.random.default_rng(5)
+        logits = rng.standard_normal((9, 64)).astype(np.float32)
+        bias = (rng.standard_normal(64) * 0.01).astype(np.float32)
+        want_idx, want_w = dev1.route(logits, 4, 1.0, bias=bias)
+        lb, bb = dev1.to_device(logits), dev1.to_device(bias)
+        try:
+            assert rt.cudaSetDevice(0) == 0
+            idx, w = _noalloc_route(dev1, lb, bb, None, None, 0, 9, 64, 4, vb.SCORE_SQRT_SOFTPLUS, 1.0)
+            assert rt.cudaGetDevice(ctypes.byref(cur)) == 0 and cur.value == 0
+        finally:
+            lb.free()
+            bb.free()
+        assert np.array_equal(idx, want_idx) and w.tobytes() == want_w.tobytes()
 
 
 def test_noalloc_hash_route_and_size_limit(device):

@@ -41,6 +41,8 @@ TYPE_IQ1_S = 19
 SCORE_SQRT_SOFTPLUS = 0
 SCORE_SIGMOID = 1
 SCORE_SOFTMAX = 2
+SCORE_SOFTMAX_F64 = 3       # Qwen router (qwen38_moe_route), norm_topk_prob = false
+SCORE_SOFTMAX_F64_NORM = 4  # Qwen router with norm_topk_prob = true
 
 # (weights per block, ggml block bytes) - ggml_quantization.hpp:12-31
 BLOCK_LAYOUT = {
@@ -136,7 +138,7 @@ EXPORTS = (
     "vlb_matrix_bytes vlb_matvec vlb_matvec_device vlb_dequantize_device vlb_layer_create "
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
     "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_layer_set_prefill_tokens "
-    "vlb_layer_prefill_tokens vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
+    "vlb_layer_prefill_tokens vlb_layer_set_input_norm vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
     "vlb_ep_plan_device vlb_ep_plan_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
 ).split()
 
@@ -183,6 +185,7 @@ def load_library() -> C.CDLL:
         "vlb_layer_set_profiling": (I, [P, P, I]),
         "vlb_layer_phase_times": (I, [P, P, C.POINTER(C.c_float), I]),
         "vlb_layer_set_prefill_tokens": (I, [P, P, U32]),
+        "vlb_layer_set_input_norm": (I, [P, P, P, F]),
         "vlb_layer_forward_routes_device": (I, [P, P, P, P, P, U32, P, P]),
         "vlb_layer_status": (I, [P, P, P]),
         "vlb_ep_workspace_bytes": (SZ, [U32, U32, U32]),
@@ -555,6 +558,19 @@ class MoeLayer:
         """Raises the error the last device forward flagged (synchronises `stream`)."""
         self.dev._check(self.dev.lib.vlb_layer_status(self.dev.h, self.ptr, C.c_void_p(stream or None)))
 
+    def set_input_norm(self, weight: Optional[np.ndarray], eps: float = 1e-6) -> None:
+        """Makes every forward a residual block out = x + MoE(RMSNorm(x)) (weight f32 [hidden]);
+        None removes the entry norm and the residual."""
+        if weight is None:
+            self.dev._check(self.dev.lib.vlb_layer_set_input_norm(self.dev.h, self.ptr, None, 0.0))
+            self._norm_w = None
+            return
+        w = np.ascontiguousarray(weight, dtype=np.float32)
+        if w.shape != (self.H,):
+            raise ValueError("the norm weight must have `hidden` elements")
+        self.dev._check(self.dev.lib.vlb_layer_set_input_norm(self.dev.h, self.ptr, _ptr(w), eps))
+        self._norm_w = w
+
     PREFILL_NEVER = 0xFFFFFFFF
 
     def set_prefill_tokens(self, min_tokens: int) -> None:
@@ -569,3 +585,41 @@ class MoeLayer:
         if self.ptr:
             self.dev._check(self.dev.lib.vlb_layer_destroy(self.dev.h, self.ptr))
             self.ptr = C.c_void_p()
+
+
+class LayerChain:
+    """Layers applied one after another on the device, x_{l+1} = layer_l(x_l), with one host copy
+    in and one out. With an input norm set on every layer (MoeLayer.set_input_norm) this is the
+    residual chain x <- x + MoE(RMSNorm(x)) of the hash-routed configuration; every layer reads the
+    same token ids (each with its own token-to-expert table)."""
+
+    def __init__(self, dev: Device, layers: Sequence[MoeLayer], max_tokens: int):
+        if not layers or any(l.H != layers[0].H for l in layers):
+            raise ValueError("a chain needs layers of one hidden size")
+        self.dev, self.layers, self.max_tokens = dev, list(layers), max_tokens
+        H = layers[0].H
+        self._bufs = [dev.buffer(max_tokens * H * 4, "chain-x0"), dev.buffer(max_tokens * H * 4, "chain-x1")]
+        self._tok = dev.buffer(max_tokens * 4, "chain-tokens")
+
+    def forward(self, x: np.ndarray, token_ids: Optional[np.ndarray] = None) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T, H = x.shape
+        if T == 0 or T > self.max_tokens or H != self.layers[0].H:
+            raise ValueError("chain input has the wrong shape")
+        self._bufs[0].upload(x)
+        tok_ptr = 0
+        if token_ids is not None:
+            self._tok.upload(np.ascontiguousarray(token_ids, dtype=np.uint32))
+            tok_ptr = self._tok.address
+        cur = 0
+        for layer in self.layers:
+            layer.forward_device(self._bufs[cur].address, T, self._bufs[1 - cur].address, token_ids_ptr=tok_ptr)
+            cur = 1 - cur
+        out = self._bufs[cur].download(np.float32, T * H).reshape(T, H)
+        for layer in self.layers:
+            layer.status()
+        return out
+
+    def close(self) -> None:
+        for b in self._bufs + [self._tok]:
+            b.free()

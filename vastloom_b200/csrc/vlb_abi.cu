@@ -176,6 +176,9 @@ struct vlb_layer {
     uint32_t* tid2eid = nullptr;
     DevMat* mats = nullptr;
     std::vector<const vlb_matrix*> host_mats;  // [3 x (E+1)]
+    // residual block entry (vlb_layer_set_input_norm): RMSNorm weight [H] and epsilon
+    float* norm_w = nullptr;
+    float norm_eps = 0.f;
     // workspace
     void* ws = nullptr;
     MoeParams p{};
@@ -594,7 +597,7 @@ static void free_layer(vlb_handle* h, vlb_layer* L) {
     for (auto& e : L->ev)
         if (e) cudaEventDestroy(e);
     void* ptrs[] = {L->router, L->bias, L->tid2eid, L->mats, L->ws,
-                    L->x_dev, L->tok_dev, L->logits_dev, L->out_dev};
+                    L->x_dev, L->tok_dev, L->logits_dev, L->out_dev, L->norm_w};
     for (void* p : ptrs)
         if (p) h->gfree(p);
     delete L;
@@ -608,7 +611,9 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     if (H == 0 || I == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512 || H % 256 ||
         I % 256 || d->max_tokens == 0 || !d->w1 || !d->w3 || !d->w2)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "MoE layer dimensions are invalid");
-    if (d->score != VLB_SCORE_SOFTMAX && !(d->route_scale > 0.f && std::isfinite(d->route_scale)))
+    if (d->score < VLB_SCORE_SQRT_SOFTPLUS || d->score > VLB_SCORE_SOFTMAX_F64_NORM)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "unknown router score mode");
+    if (d->score <= VLB_SCORE_SIGMOID && !(d->route_scale > 0.f && std::isfinite(d->route_scale)))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "route scale must be finite and positive");
     if (d->hash_routing && (!d->tid2eid || d->vocab == 0))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs a token-to-expert table");
@@ -685,7 +690,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
                  o_ps = carve(P * 4), o_pw = carve(P * 4), o_units = carve((size_t)mu * sizeof(Unit)),
                  o_cnt = carve(32 + T * 4), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
                  o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
-                 o_xd = carve(T * H * 8), o_rp = carve(8 * T * E * 8);
+                 o_xn = carve(T * H * 4);
     const uint32_t mpt = prefill_max_tiles((uint32_t)T, k, E);
     const size_t o_xh = carve(P * H * 2), o_acth = carve(P * I * 2), o_pt2 = carve((size_t)mpt * sizeof(Unit));
     const size_t o_dc = carve(((T * k + 1023) / 1024) * E * 4);
@@ -734,8 +739,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.y = reinterpret_cast<float*>(ws + o_y);
     p.xmax = reinterpret_cast<uint32_t*>(ws + o_cnt + 32);
     p.act_max = reinterpret_cast<uint32_t*>(ws + o_am);
-    p.xd = reinterpret_cast<double*>(ws + o_xd);
-    p.router_partial = reinterpret_cast<double*>(ws + o_rp);
+    p.x_norm = reinterpret_cast<float*>(ws + o_xn);
     p.max_units = mu;
     p.prefill = 0;
     p.xperm = reinterpret_cast<__half*>(ws + o_xh);
@@ -801,6 +805,12 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.routes_meta = routes_meta;
     p.out = out;
     p.grids = h->grids();
+    if (L->norm_w && (routes_idx || x_half))
+        return h->fail(VLB_ERR_UNSUPPORTED, "a layer with an input norm takes plain token rows only");
+    p.norm_w = L->norm_w;
+    p.norm_eps = L->norm_eps;
+    if (L->norm_w && ((reinterpret_cast<uintptr_t>(x) % 16u) || L->desc.hidden > kRmsMaxWidth))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "input rows of a normed layer must be 16-byte aligned");
     // half rows carry fp16 operands already: only the tensor-core prefill path consumes them
     p.prefill = (x_half || T >= prefill_threshold(L)) ? 1 : 0;
     const bool one_route = (routes_idx || x_half) && p.k == 1;
@@ -903,6 +913,35 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_
     return check_layer_flags(h, flags);
 }
 
+int vlb_layer_set_input_norm(vlb_handle* h, vlb_layer* L, const float* weight, float eps) {
+    VLB_LOCK(h);
+    if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
+    const uint32_t H = L->desc.hidden;
+    if (weight && !(eps > 0.f && std::isfinite(eps)))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "RMSNorm epsilon must be finite and positive");
+    if (weight && H > kRmsMaxWidth) return h->fail(VLB_ERR_UNSUPPORTED, "hidden size too large for the input norm");
+    if (weight)
+        for (uint32_t c = 0; c < H; ++c)
+            if (!std::isfinite(weight[c])) return h->fail(VLB_ERR_INVALID_ARGUMENT, "RMSNorm weight is not finite");
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    if (L->gexec) {  // the captured forward does not have the new entry step
+        cudaGraphExecDestroy(L->gexec);
+        L->gexec = nullptr;
+    }
+    if (!weight) {
+        if (L->norm_w) h->gfree(L->norm_w);
+        L->norm_w = nullptr;
+        return VLB_OK;
+    }
+    if (!L->norm_w) {
+        int st = h->galloc((size_t)H * 4, "vlb-input-norm", (void**)&L->norm_w);
+        if (st != VLB_OK) return st;
+    }
+    VLB_CUDA(h, cudaMemcpy(L->norm_w, weight, (size_t)H * 4, cudaMemcpyHostToDevice));
+    L->norm_eps = eps;
+    return VLB_OK;
+}
+
 int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* L, uint32_t min_tokens) {
     VLB_LOCK(h);
     if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
@@ -979,7 +1018,8 @@ int vlb_route_device(vlb_handle* h, int score, int hash_routing, const float* lo
                      uint32_t vocab, uint32_t T, uint32_t E, uint32_t k, float route_scale,
                      uint32_t* idx, float* weights, void* stream) {
     VLB_LOCK(h);
-    if (!logits || !idx || !weights || T == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512)
+    if (!logits || !idx || !weights || T == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512 ||
+        score < VLB_SCORE_SQRT_SOFTPLUS || score > VLB_SCORE_SOFTMAX_F64_NORM)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid route argument");
     if (hash_routing && (!tok || !tid2eid || vocab == 0))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs token ids and a table");
@@ -1009,19 +1049,15 @@ int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint
     VLB_LOCK(h);
     if (!x || !w || !logits || T == 0 || H == 0 || E == 0 || H % 4)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid router argument");
-    // scratch: scores [T x E] f32 | xmax [T] | x in f64 [T x H] | partial sums [8 x T x E] f64
-    const size_t sbytes = ((size_t)T * E * 4 + (size_t)T * 4 + 255) / 256 * 256;
-    const size_t xbytes = (size_t)T * H * 8, pbytes = (size_t)8 * T * E * 8;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) % 16u)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "router inputs must be 16-byte aligned");
+    if ((T + 3u) / 4u > 65535u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "too many router tokens for one call");
+    // scratch: the scores the kernel writes beside the logits
     char* scratch = nullptr;
-    int st = h->scratch_at_least(sbytes + xbytes + pbytes, &scratch);
+    int st = h->scratch_at_least((size_t)T * E * 4, &scratch);
     if (st != VLB_OK) return st;
-    float* scores = reinterpret_cast<float*>(scratch);
-    uint32_t* xmax = reinterpret_cast<uint32_t*>(scratch + (size_t)T * E * 4);
-    double* xd = reinterpret_cast<double*>(scratch + sbytes);
-    double* part = reinterpret_cast<double*>(scratch + sbytes + xbytes);
     cudaStream_t s = h->pick(stream);
-    cudaError_t e = launch_prescale(x, T, H, xmax, xd, s);
-    if (e == cudaSuccess) e = launch_router(xd, w, T, H, E, VLB_SCORE_SOFTMAX, logits, scores, part, s);
+    cudaError_t e = launch_router(x, w, T, H, E, VLB_SCORE_SOFTMAX, logits, reinterpret_cast<float*>(scratch), s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return h->cuda_fail("router", e);
     return VLB_OK;
@@ -1030,9 +1066,12 @@ int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint
 int vlb_rms_norm_device(vlb_handle* h, const float* x, const float* w, uint32_t rows,
                         uint32_t width, float eps, float* out, void* stream) {
     VLB_LOCK(h);
-    if (!x || !w || !out || rows == 0 || width == 0 || !(eps > 0.f))
+    if (!x || !w || !out || rows == 0 || width == 0 || !(eps > 0.f) || !std::isfinite(eps))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid RMSNorm argument");
-    VLB_CUDA(h, launch_rms_norm(x, w, rows, width, eps, out, h->pick(stream)));
+    if (width % 4u || width > kRmsMaxWidth || reinterpret_cast<uintptr_t>(x) % 16u)
+        return h->fail(VLB_ERR_UNSUPPORTED, "RMSNorm rows must be 16-byte aligned, width % 4 == 0 and width <= " +
+                                                std::to_string(kRmsMaxWidth));
+    VLB_CUDA(h, launch_rms_norm(x, w, rows, width, eps, out, nullptr, h->pick(stream)));
     return VLB_OK;
 }
 
@@ -1117,7 +1156,7 @@ int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx, const float* wei
     VLB_CUDA(h, cudaMemcpyAsync(&bad, flag, 4, cudaMemcpyDeviceToHost, s));
     VLB_CUDA(h, cudaStreamSynchronize(s));
     if (bad) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
-    VLB_CUDA(h, launch_prescale(x, T, H, xmax, nullptr, s));
+    VLB_CUDA(h, launch_prescale(x, T, H, xmax, s));
     MoeParams p{};
     p.T = T;
     p.k = k;

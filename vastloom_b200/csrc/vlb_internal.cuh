@@ -251,9 +251,13 @@ struct MoeParams {
     float* y;                // [(T*k + T) x H]
     float* out;              // [T x H]
     uint32_t* xmax;          // [T]: bits of max|x| per token (zeroed with the counters)
-    double* xd;              // [T x H]: activations widened to f64 for the router projection
-    double* router_partial;  // [8 x T x E]: per-column-slice router partial sums
     uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
+    // residual block (input norm set): the layer runs on xn = RMSNorm(x) (rows of x_norm) and the
+    // combine adds the original rows back: out = x + MoE(xn)
+    const float* norm_w;     // [H] or null
+    float norm_eps;
+    float* x_norm;           // [T x H] workspace
+    const float* x_residual; // set by launch_moe for a residual block: the original rows
     uint32_t max_units;
     uint32_t* disp_counts;   // [ceil(T*k / 1024) x E]: per-chunk expert counts of the multi-CTA dispatch
     // 1: a one-route-per-row forward (k = 1, given routes) without a shared expert whose route

@@ -2,7 +2,7 @@
 //
 //   dequant_kernel    bit-exact block decode (reference decode_*_block)
 //   gemv_kernel       multi-token dequant-matvec over one resident matrix (the operator seam)
-//   router_kernel     router projection in f64 accumulation + score function
+//   router_kernel     router projection (sequential f64 sums, bit-exact) + score function
 //   route_kernel      warp-per-token top-k (ties to the lower id) and route weights
 //   dispatch_kernel   stable counting sort of (token, slot) pairs by expert, work units
 //                     (dispatch_count / scatter / finish for large batches)
@@ -119,9 +119,22 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 }
 
 // ---------------------------------------------------------------------------------------------
-// Router projection, f64 accumulation of exact f32 products (deepseek_v4_graph.cpp:735-767), and
-// the per-expert score (sqrt_softplus / sigmoid; softmax is applied per token in route_kernel).
-constexpr uint32_t kRouterMaxSlices = 8;
+// Router projection (deepseek_v4_graph.cpp:735-767 `linear`; qwen3_8_flash_next_reference.cpp:311
+// `linear_f`): logits[t][e] = f32(sum over columns c = 0, 1, ... of double(x[t][c]) *
+// double(w[e][c])), one f64 rounding per added term, in column order. Every product of two f32
+// values is exact in f64, so fma(x, w, s) rounds exactly like s + x * w, and a thread that walks
+// the columns in order reproduces the reference's logit bit for bit. That order is the whole cost:
+// each logit is a chain of H dependent f64 additions, so the kernel is latency-bound (H times the
+// DFMA latency) and spends its effort on keeping every chain fed: a CTA computes a tile of 32
+// experts (the lanes) x 4 tokens (the warps), stages a column slice of the tile's weights and
+// activations in shared memory as f64 (each f32 converted once per CTA, not once per use), and
+// loads the next slice into registers while the chains consume the current one. (The slice is
+// 64 columns: the f64 copies of two slices then fit the 48 KB of static shared memory.)
+constexpr uint32_t kRtExperts = 32;
+constexpr uint32_t kRtTokens = 4;
+constexpr uint32_t kRtCols = 64;
+constexpr uint32_t kRtWStride = kRtCols + 2;  // doubles per staged weight row: 16-byte phase shift per row
+constexpr uint32_t kRtThreads = kRtExperts * kRtTokens;
 
 __device__ __forceinline__ float sqrt_softplus_dev(float v) {
     const double p = (double)v;
@@ -137,101 +150,84 @@ __device__ __forceinline__ float sigmoid_dev(float v) {
 __device__ __forceinline__ float score_dev(int score, float logit) {
     if (score == VLB_SCORE_SIGMOID) return sigmoid_dev(logit);
     if (score == VLB_SCORE_SQRT_SOFTPLUS) return sqrt_softplus_dev(logit);
-    return logit;
+    return logit;  // the softmax routers work on the logits themselves
 }
 
-// Router projection on the FP64 tensor cores (mma.sync m8n8k4 f64): logits[t][e] =
-// f32(sum_k w[e][k] * x[t][k]) with f64 products and sums (f32 operands are exact in f64).
-// CTA tile = 8 experts x 8 tokens x one column slice (gridDim.z slices); the 8 warps split the
-// slice and their partial tiles are added in a fixed order through shared memory. With one slice
-// the tile is final; with several, each slice's partial tile goes to `partial` and
-// router_finish_kernel adds the slices in order. Router weights stay f32 (converted in
-// registers); activations arrive widened to f64 (token_prescale_kernel).
-__global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w,
-                                                     const double* __restrict__ xd, uint32_t T,
-                                                     uint32_t H, uint32_t E, int score,
-                                                     float* __restrict__ logits,
-                                                     float* __restrict__ scores,
-                                                     double* __restrict__ partial) {
-    __shared__ double part[8][32][2];
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t g = lane >> 2, q = lane & 3u;
-    const uint32_t e0 = blockIdx.x * 8u, t0 = blockIdx.y * 8u;
-    const uint32_t slices = gridDim.z;
-    const uint32_t slice = ((H / 4u + slices - 1u) / slices) * 4u;
-    const uint32_t s0 = min(blockIdx.z * slice, H), s1 = min(s0 + slice, H);
-    const uint32_t span = (((s1 - s0) / 4u + 7u) / 8u) * 4u;
-    const uint32_t k0 = min(s0 + warp * span, s1), k1 = min(k0 + span, s1);
-    const float* wr = e0 + g < E ? w + (size_t)(e0 + g) * H : nullptr;
-    const double* xr = t0 + g < T ? xd + (size_t)(t0 + g) * H : nullptr;
-    // 8 independent accumulator chains (k-steps round-robin), summed in a fixed order after
-    constexpr int kChains = 8;
-    double c0[kChains], c1[kChains];
+__global__ void __launch_bounds__(kRtThreads) router_kernel(const float* __restrict__ w,
+                                                            const float* __restrict__ x, uint32_t T,
+                                                            uint32_t H, uint32_t E, int score,
+                                                            float* __restrict__ logits,
+                                                            float* __restrict__ scores) {
+    __shared__ __align__(16) double ws[2][kRtExperts * kRtWStride];
+    __shared__ __align__(16) double xs[2][kRtTokens * kRtCols];
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t e0 = blockIdx.x * kRtExperts, t0 = blockIdx.y * kRtTokens;
+    // staging roles: 512 weight float4s of a slice -> 4 per thread; 64 activation float4s -> one
+    // for each of the first 64 threads
+    constexpr int kWf = (int)(kRtExperts * kRtCols / 4u / kRtThreads);
+    float4 wr[kWf], xr = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool xrole = threadIdx.x < kRtTokens * kRtCols / 4u;
+    auto fetch = [&](uint32_t c0) {
 #pragma unroll
-    for (int j = 0; j < kChains; ++j) c0[j] = c1[j] = 0.0;
-    uint32_t k = k0 + q;
-    for (; k + 4u * (kChains - 1) < k1; k += 4u * kChains) {
-        double a[kChains], b[kChains];
-#pragma unroll
-        for (int j = 0; j < kChains; ++j) {
-            a[j] = wr ? (double)__ldg(wr + k + 4u * j) : 0.0;
-            b[j] = xr ? __ldg(xr + k + 4u * j) : 0.0;
+        for (int i = 0; i < kWf; ++i) {
+            const uint32_t f = threadIdx.x + (uint32_t)i * kRtThreads;  // float4 index in the slice
+            const uint32_t r = f / (kRtCols / 4u), c = c0 + (f % (kRtCols / 4u)) * 4u;
+            wr[i] = (e0 + r < E && c < H) ? __ldg(reinterpret_cast<const float4*>(w + (size_t)(e0 + r) * H + c))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        const uint32_t r = threadIdx.x / (kRtCols / 4u), c = c0 + (threadIdx.x % (kRtCols / 4u)) * 4u;
+        if (xrole)
+            xr = (t0 + r < T && c < H) ? __ldg(reinterpret_cast<const float4*>(x + (size_t)(t0 + r) * H + c))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto store = [&](int b) {
 #pragma unroll
-        for (int j = 0; j < kChains; ++j)
-            asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-                : "+d"(c0[j]), "+d"(c1[j])
-                : "d"(a[j]), "d"(b[j]));
-    }
-    for (; k < k1; k += 4u) {  // tail (slice not a multiple of 32 columns)
-        const double a = wr ? (double)__ldg(wr + k) : 0.0;
-        const double b = xr ? __ldg(xr + k) : 0.0;
-        asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-            : "+d"(c0[0]), "+d"(c1[0])
-            : "d"(a), "d"(b));
-    }
-    for (int j = 1; j < kChains; ++j) {
-        c0[0] += c0[j];
-        c1[0] += c1[j];
-    }
-    // lane holds C[g][2q], C[g][2q+1] = (expert e0 + g, tokens t0 + 2q and t0 + 2q + 1)
-    part[warp][lane][0] = c0[0];
-    part[warp][lane][1] = c1[0];
+        for (int i = 0; i < kWf; ++i) {
+            const uint32_t f = threadIdx.x + (uint32_t)i * kRtThreads;
+            double* d = &ws[b][(f / (kRtCols / 4u)) * kRtWStride + (f % (kRtCols / 4u)) * 4u];
+            *reinterpret_cast<double2*>(d) = make_double2(wr[i].x, wr[i].y);
+            *reinterpret_cast<double2*>(d + 2) = make_double2(wr[i].z, wr[i].w);
+        }
+        if (xrole) {
+            double* d = &xs[b][(threadIdx.x / (kRtCols / 4u)) * kRtCols + (threadIdx.x % (kRtCols / 4u)) * 4u];
+            *reinterpret_cast<double2*>(d) = make_double2(xr.x, xr.y);
+            *reinterpret_cast<double2*>(d + 2) = make_double2(xr.z, xr.w);
+        }
+    };
+    fetch(0);
+    store(0);
     __syncthreads();
-    if (threadIdx.x < 64u) {
-        const uint32_t i = threadIdx.x, eg = i >> 3, tn = i & 7u;
-        const uint32_t src = eg * 4u + (tn >> 1), half = tn & 1u;
-        double v = 0.0;
-#pragma unroll
-        for (int w8 = 0; w8 < 8; ++w8) v += part[w8][src][half];
-        const uint32_t e = e0 + eg, t = t0 + tn;
-        if (e < E && t < T) {
-            if (slices == 1) {
-                const float lg = (float)v;
-                logits[(size_t)t * E + e] = lg;
-                scores[(size_t)t * E + e] = score_dev(score, lg);
-            } else {
-                partial[((size_t)blockIdx.z * T + t) * E + e] = v;
-            }
+    double acc = 0.0;
+    const double* wrow0 = &ws[0][lane * kRtWStride];
+    const double* wrow1 = &ws[1][lane * kRtWStride];
+    const uint32_t slices = (H + kRtCols - 1u) / kRtCols;
+    for (uint32_t sl = 0; sl < slices; ++sl) {
+        const int b = (int)(sl & 1u);
+        if (sl + 1u < slices) fetch((sl + 1u) * kRtCols);  // in flight while the chain runs
+        const double* wrow = b ? wrow1 : wrow0;
+        const double* xrow = &xs[b][warp * kRtCols];
+        const uint32_t n = min(kRtCols, H - sl * kRtCols);  // a multiple of 4 (H % 4 == 0)
+        for (uint32_t c = 0; c < n; c += 4u) {
+            const double2 wa = *reinterpret_cast<const double2*>(wrow + c);
+            const double2 wb = *reinterpret_cast<const double2*>(wrow + c + 2u);
+            const double2 xa = *reinterpret_cast<const double2*>(xrow + c);
+            const double2 xb = *reinterpret_cast<const double2*>(xrow + c + 2u);
+            acc = __fma_rn(xa.x, wa.x, acc);
+            acc = __fma_rn(xa.y, wa.y, acc);
+            acc = __fma_rn(xb.x, wb.x, acc);
+            acc = __fma_rn(xb.y, wb.y, acc);
+        }
+        if (sl + 1u < slices) {
+            store(b ^ 1);  // the other buffer: its last readers finished before the previous barrier
+            __syncthreads();
         }
     }
-}
-
-__global__ void router_finish_kernel(const double* __restrict__ partial, uint32_t slices,
-                                     uint32_t T, uint32_t E, int score, float* __restrict__ logits,
-                                     float* __restrict__ scores) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (size_t)T * E) return;
-    double v = 0.0;
-    for (uint32_t z = 0; z < slices; ++z) v += partial[(size_t)z * T * E + i];
-    const float lg = (float)v;
-    logits[i] = lg;
-    scores[i] = score_dev(score, lg);
-}
-
-__global__ void widen_kernel(const float* __restrict__ src, size_t n, double* __restrict__ dst) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) dst[i] = (double)src[i];
+    const uint32_t e = e0 + lane, t = t0 + warp;
+    if (e < E && t < T) {
+        const float lg = (float)acc;
+        logits[(size_t)t * E + e] = lg;
+        scores[(size_t)t * E + e] = score_dev(score, lg);
+    }
 }
 
 __global__ void score_kernel(const float* __restrict__ logits, size_t n, int score,
@@ -242,10 +238,17 @@ __global__ void score_kernel(const float* __restrict__ logits, size_t n, int sco
 
 // ---------------------------------------------------------------------------------------------
 // Top-k routing, one warp per token (deepseek_v4_route_learned_logits / _hash_logits,
-// deepseek_v4_reference.cpp:223-307; OLMoE softmax router, olmoe_runtime.cpp:1120-1137).
-// Selection key: learned = score + bias (f32 add), softmax = probability; larger first, ties to
-// the lower expert id (std::partial_sort with that strict order). E <= 32 * kMaxPerLane.
+// deepseek_v4_reference.cpp:223-307; OLMoE softmax router, olmoe_runtime.cpp:1120-1137; Qwen
+// router, qwen3_8_flash_next_reference.cpp:1186-1239). Selection key: learned = score + bias (f32
+// add), OLMoE softmax = f32 probability, Qwen softmax = f64 probability; larger first, ties to the
+// lower expert id (std::partial_sort / std::sort with that strict order). Keys are held as f64
+// (every f32 key converts exactly, so the order and the ties are the f32 ones). E <= 32 *
+// kMaxPerLane.
 constexpr int kMaxPerLane = 16;  // E <= 512
+
+__device__ __forceinline__ bool f64_softmax(int score) {
+    return score == VLB_SCORE_SOFTMAX_F64 || score == VLB_SCORE_SOFTMAX_F64_NORM;
+}
 
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ scores,
                                                     const float* __restrict__ bias,
@@ -260,29 +263,52 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
     const uint32_t t = blockIdx.x * 8u + warp;
     if (t >= T) return;
     const float* s = scores + (size_t)t * E;
-    float key[kMaxPerLane];
-    float val[kMaxPerLane];
+    double key[kMaxPerLane];
+    double val[kMaxPerLane];
     if (score == VLB_SCORE_SOFTMAX) {
         // p_e = float exp of (logit - max); double denominator; float division (no renorm)
         float mx = -INFINITY;
         for (uint32_t e = lane; e < E; e += 32u) mx = fmaxf(mx, s[e]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float p[kMaxPerLane];
         double den = 0.0;
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
             const uint32_t e = lane + 32u * i;
-            float p = 0.f;
-            if (e < E) p = (float)exp((double)__fsub_rn(s[e], mx));
-            val[i] = p;
-            den += (double)p;
+            p[i] = e < E ? (float)exp((double)__fsub_rn(s[e], mx)) : 0.f;
+            den += (double)p[i];
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
         const float fden = (float)den;
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
-            val[i] = __fdiv_rn(val[i], fden);
+            val[i] = (double)__fdiv_rn(p[i], fden);
+            key[i] = lane + 32u * i < E ? val[i] : -INFINITY;
+        }
+    } else if (f64_softmax(score)) {
+        // probs[e] = exp(double(l_e) - max) in double, summed in expert order (the reference's
+        // sequential loop: each lane's values join the sum in turn), prob = probs[e] * (1 / sum)
+        double mx = -INFINITY;
+        for (uint32_t e = lane; e < E; e += 32u) mx = fmax(mx, (double)s[e]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            const uint32_t e = lane + 32u * i;
+            val[i] = e < E ? exp(__dsub_rn((double)s[e], mx)) : 0.0;
+        }
+        double sum = 0.0;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            if (32u * (uint32_t)i >= E) break;
+            for (uint32_t l = 0; l < 32u && 32u * i + l < E; ++l) sum = __dadd_rn(sum, __shfl_sync(0xffffffffu, val[i], l));
+        }
+        const double inv = sum > 0.0 ? 1.0 / sum : 0.0;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            val[i] = __dmul_rn(val[i], inv);
             key[i] = lane + 32u * i < E ? val[i] : -INFINITY;
         }
     } else {
@@ -290,16 +316,16 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
         for (int i = 0; i < kMaxPerLane; ++i) {
             const uint32_t e = lane + 32u * i;
             if (e < E) {
-                val[i] = s[e];
-                key[i] = hash_routing ? 0.f : __fadd_rn(s[e], bias ? bias[e] : 0.f);
+                val[i] = (double)s[e];
+                key[i] = hash_routing ? 0.0 : (double)__fadd_rn(s[e], bias ? bias[e] : 0.f);
             } else {
-                val[i] = 0.f;
+                val[i] = 0.0;
                 key[i] = -INFINITY;
             }
         }
     }
     uint32_t sel[16];
-    float selv[16];
+    double selv[16];
     if (hash_routing) {
         const uint32_t tok = token_ids[t];
         if (tok >= vocab) {
@@ -315,7 +341,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
             sel[j] = e;
             // fetch val of expert e from its owner lane
             const uint32_t owner = e & 31u, slot = e >> 5;
-            float mine = 0.f;
+            double mine = 0.0;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) if ((uint32_t)i == slot) mine = val[i];
             selv[j] = __shfl_sync(0xffffffffu, mine, owner);
@@ -324,7 +350,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
         uint32_t removed = 0;  // bit i: this lane's entry i has been selected already
         for (uint32_t j = 0; j < k; ++j) {
             // lane-local best: larger key, ties to the lower id (= lower i within a lane)
-            float bk = 0.f;
+            double bk = 0.0;
             uint32_t be = 0xffffffffu;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) {
@@ -336,7 +362,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
-                const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+                const double ok = __shfl_xor_sync(0xffffffffu, bk, o);
                 const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, o);
                 if (oe != 0xffffffffu && (be == 0xffffffffu || ok > bk || (ok == bk && oe < be))) {
                     bk = ok;
@@ -345,7 +371,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
             }
             sel[j] = be;
             const uint32_t owner = be & 31u, slot = be >> 5;
-            float mine = 0.f;
+            double mine = 0.0;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) if ((uint32_t)i == slot) mine = val[i];
             selv[j] = __shfl_sync(0xffffffffu, mine, owner);
@@ -356,17 +382,28 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
         if (score == VLB_SCORE_SOFTMAX) {
             for (uint32_t j = 0; j < k; ++j) {
                 idx[(size_t)t * k + j] = sel[j];
-                weights[(size_t)t * k + j] = selv[j];
+                weights[(size_t)t * k + j] = (float)selv[j];
+            }
+        } else if (f64_softmax(score)) {
+            // weights = f32(prob); with norm_topk_prob each is rescaled by 1 / (the rank-order
+            // f64 sum of the selected probabilities)
+            double top = 0.0;
+            for (uint32_t j = 0; j < k; ++j) top = __dadd_rn(top, selv[j]);
+            const bool norm = score == VLB_SCORE_SOFTMAX_F64_NORM && top > 0.0;
+            const double sc = norm ? 1.0 / top : 1.0;
+            for (uint32_t j = 0; j < k; ++j) {
+                idx[(size_t)t * k + j] = sel[j];
+                const float w = (float)selv[j];
+                weights[(size_t)t * k + j] = norm ? (float)__dmul_rn((double)w, sc) : w;
             }
         } else {
             // route_from_indices, deepseek_v4_reference.cpp:80-121
             double sum = 0.0;
-            for (uint32_t j = 0; j < k; ++j) sum += (double)selv[j];
+            for (uint32_t j = 0; j < k; ++j) sum += selv[j];
             if (!(sum > 0.0) || isinf(sum)) atomicOr(error_flag, 4u);
             for (uint32_t j = 0; j < k; ++j) {
                 idx[(size_t)t * k + j] = sel[j];
-                weights[(size_t)t * k + j] =
-                    (float)((double)selv[j] / sum * (double)route_scale);
+                weights[(size_t)t * k + j] = (float)(selv[j] / sum * (double)route_scale);
             }
         }
     }
@@ -754,23 +791,16 @@ __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
 }
 
 __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __restrict__ x, uint32_t T,
-                                                             uint32_t H, uint32_t* __restrict__ xmax,
-                                                             double* __restrict__ xd) {
+                                                             uint32_t H, uint32_t* __restrict__ xmax) {
     // grid (ceil(H / 1024), min(T, 65535)), rows strided over gridDim.y: each thread takes 4 columns
     // of one token; the token's max|x| (for the tensor-core activation prescale) is an atomic max
-    // over float bits (non-negative floats order as integers), and the row is widened to f64 for
-    // the router projection
+    // over float bits (non-negative floats order as integers)
     const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     for (uint32_t t = blockIdx.y; t < T; t += gridDim.y) {
         float m = 0.f;
         if (c < H) {
             const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
             m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-            if (xd) {
-                double* o = xd + (size_t)t * H + c;
-                *reinterpret_cast<double2*>(o) = make_double2(v.x, v.y);
-                *reinterpret_cast<double2*>(o + 2) = make_double2(v.z, v.w);
-            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -809,32 +839,66 @@ __global__ void __launch_bounds__(256) combine_kernel(MoeParams p) {
             acc.z = __fadd_rn(acc.z, v.z);
             acc.w = __fadd_rn(acc.w, v.w);
         }
+        if (p.x_residual) {  // residual block: x + MoE(RMSNorm(x)), one f32 addition
+            const float4 v = *reinterpret_cast<const float4*>(p.x_residual + (size_t)t * p.H + c4);
+            acc.x = __fadd_rn(v.x, acc.x);
+            acc.y = __fadd_rn(v.y, acc.y);
+            acc.z = __fadd_rn(v.z, acc.z);
+            acc.w = __fadd_rn(v.w, acc.w);
+        }
         *reinterpret_cast<float4*>(p.out + (size_t)t * p.H + c4) = acc;
     }
 }
 
 // ---------------------------------------------------------------------------------------------
-// RMSNorm (deepseek_v4_reference.cpp:170-206), one CTA per row.
+// RMSNorm (deepseek_v4_reference.cpp:170-206), one CTA per row: out = f32(double(x) * inv *
+// double(w)) with inv = 1 / sqrt(sum(double(x)^2) / width + eps). The sum of squares is the
+// reference's sequential f64 sum (each square of an f32 is exact in f64, so fma(v, v, s) rounds
+// like s + v * v): one thread walks the row, staged in shared memory, in column order, so the
+// result is bit-identical; division and square root are IEEE-rounded in CUDA as on the host.
+// With xmax non-null the kernel is also the layer's entry step: it records max|out| of the row
+// (bits of a non-negative float, for the tensor-core activation prescale).
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x,
                                                        const float* __restrict__ w,
                                                        uint32_t width, float eps,
-                                                       float* __restrict__ out) {
-    __shared__ double part[8];
+                                                       float* __restrict__ out,
+                                                       uint32_t* __restrict__ xmax) {
+    extern __shared__ __align__(16) float row[];
+    __shared__ double inv_s;
+    __shared__ float wmax[8];
     const float* xr = x + (size_t)blockIdx.x * width;
-    double sq = 0.0;
-    for (uint32_t c = threadIdx.x; c < width; c += blockDim.x) {
-        const double v = (double)xr[c];
-        sq = fma(v, v, sq);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((threadIdx.x & 31u) == 0) part[threadIdx.x >> 5] = sq;
+    for (uint32_t c = threadIdx.x * 4u; c < width; c += blockDim.x * 4u)
+        *reinterpret_cast<float4*>(row + c) = *reinterpret_cast<const float4*>(xr + c);
     __syncthreads();
-    double total = 0.0;
-    for (int i = 0; i < 8; ++i) total += part[i];
-    const double inv = 1.0 / sqrt(total / (double)width + (double)eps);
-    for (uint32_t c = threadIdx.x; c < width; c += blockDim.x)
-        out[(size_t)blockIdx.x * width + c] = (float)((double)xr[c] * inv * (double)w[c]);
+    if (threadIdx.x == 0) {
+        double sq = 0.0;
+        for (uint32_t c = 0; c < width; c += 4u) {
+            const float4 v = *reinterpret_cast<const float4*>(row + c);
+            sq = __fma_rn((double)v.x, (double)v.x, sq);
+            sq = __fma_rn((double)v.y, (double)v.y, sq);
+            sq = __fma_rn((double)v.z, (double)v.z, sq);
+            sq = __fma_rn((double)v.w, (double)v.w, sq);
+        }
+        inv_s = 1.0 / sqrt(sq / (double)width + (double)eps);
+    }
+    __syncthreads();
+    const double inv = inv_s;
+    float m = 0.f;
+    for (uint32_t c = threadIdx.x; c < width; c += blockDim.x) {
+        const float o = (float)(__dmul_rn(__dmul_rn((double)row[c], inv), (double)w[c]));
+        out[(size_t)blockIdx.x * width + c] = o;
+        m = fmaxf(m, fabsf(o));
+    }
+    if (!xmax) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31u) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = 0.f;
+        for (uint32_t i = 0; i < blockDim.x / 32u; ++i) mm = fmaxf(mm, wmax[i]);
+        xmax[blockIdx.x] = __float_as_uint(mm);
+    }
 }
 
 // =============================================================================================
@@ -904,38 +968,19 @@ cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_
     return gemv_type<4>(m, g, x, ntok, xstride, y, ystride, s);
 }
 
-// Column slices: enough CTAs to cover the SMs when the expert x token tiles alone do not.
-static uint32_t router_slices(uint32_t T, uint32_t E, uint32_t H) {
-    const uint32_t tiles = ((E + 7) / 8) * ((T + 7) / 8);
-    uint32_t z = 1;
-    while (z < kRouterMaxSlices && tiles * z < 256u && H / (z * 2u) >= 256u) z *= 2u;
-    return z;
-}
-
-cudaError_t launch_router(const double* xd, const float* w, uint32_t T, uint32_t H, uint32_t E,
-                          int score, float* logits, float* scores, double* partial,
-                          cudaStream_t s) {
+cudaError_t launch_router(const float* x, const float* w, uint32_t T, uint32_t H, uint32_t E, int score,
+                          float* logits, float* scores, cudaStream_t s) {
     if (H % 4u) return cudaErrorInvalidValue;
-    const uint32_t z = partial ? router_slices(T, E, H) : 1u;
-    dim3 grid((E + 7) / 8, (T + 7) / 8, z);
-    router_kernel<<<grid, 256, 0, s>>>(w, xd, T, H, E, score, logits, scores, partial);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess || z == 1) return e;
-    const size_t n = (size_t)T * E;
-    router_finish_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(partial, z, T, E, score, logits, scores);
+    const dim3 grid((E + kRtExperts - 1u) / kRtExperts, (T + kRtTokens - 1u) / kRtTokens);
+    if (grid.y > 65535u) return cudaErrorInvalidValue;
+    router_kernel<<<grid, kRtThreads, 0, s>>>(w, x, T, H, E, score, logits, scores);
     return cudaGetLastError();
 }
 
-cudaError_t launch_widen(const float* src, size_t n, double* dst, cudaStream_t s) {
-    widen_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, n, dst);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, double* xd,
-                            cudaStream_t s) {
+cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, cudaStream_t s) {
     cudaError_t e = cudaMemsetAsync(xmax, 0, (size_t)T * 4u, s);
     if (e != cudaSuccess) return e;
-    token_prescale_kernel<<<dim3((H + 1023) / 1024, rows_grid(T)), 256, 0, s>>>(x, T, H, xmax, xd);
+    token_prescale_kernel<<<dim3((H + 1023) / 1024, rows_grid(T)), 256, 0, s>>>(x, T, H, xmax);
     return cudaGetLastError();
 }
 
@@ -955,9 +1000,10 @@ cudaError_t launch_route(const float* scores, const float* bias, const uint32_t*
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
+cudaError_t launch_moe(const MoeParams& p_in, cudaStream_t s, cudaEvent_t* ev) {
     cudaError_t e;
     if (ev) cudaEventRecord(ev[0], s);
+    MoeParams p = p_in;
     // routing: router projection (or supplied logits) -> scores -> top-k; or given routes; or
     // half rows that arrive with their max|x| and one route each
     const bool given = p.routes_idx != nullptr;
@@ -966,9 +1012,17 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
                                                              p.counters + 3);
         e = cudaGetLastError();
     } else {
-        token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(
-            p.x, p.T, p.H, p.xmax, (p.logits_in || given) ? nullptr : p.xd);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (p.norm_w) {
+            // residual block entry: xn = RMSNorm(x) with each row's max|xn| (the prescale); the
+            // layer then runs on xn and the combine adds x back
+            if ((e = launch_rms_norm(p.x, p.norm_w, p.T, p.H, p.norm_eps, p.x_norm, p.xmax, s)) != cudaSuccess)
+                return e;
+            p.x_residual = p.x;
+            p.x = p.x_norm;
+        } else {
+            token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(p.x, p.T, p.H, p.xmax);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
         if (given) {
             const size_t n = (size_t)p.T * p.k;
             routes_copy_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p.routes_idx, p.routes_w, n, p.E,
@@ -978,8 +1032,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t s, cudaEvent_t* ev) {
             if (p.logits_in) {
                 e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
             } else {
-                e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, p.router_partial,
-                                  s);
+                e = launch_router(p.x, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
             }
             if (e != cudaSuccess) return e;
             e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
@@ -1055,8 +1108,12 @@ cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
-                            float eps, float* out, cudaStream_t s) {
-    rms_norm_kernel<<<rows, 256, 0, s>>>(x, w, width, eps, out);
+                            float eps, float* out, uint32_t* xmax, cudaStream_t s) {
+    if (width % 4u || (size_t)width * 4u > kRmsMaxWidth * 4u) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)width * 4u;
+    cudaError_t e = set_smem_once(rms_norm_kernel, smem);
+    if (e != cudaSuccess) return e;
+    rms_norm_kernel<<<rows, 256, smem, s>>>(x, w, width, eps, out, xmax);
     return cudaGetLastError();
 }
 

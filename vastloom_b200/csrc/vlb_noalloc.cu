@@ -1,12 +1,17 @@
 // vlb_route_device_noalloc: the device router (sqrt-softplus / sigmoid / softmax scores, top-k,
 // route weights) for callers that cannot allocate device memory.
 //
-// Who cannot allocate: code that runs inside a CUDA host callback (cudaLaunchHostFunc), where
-// CUDA API calls such as cudaMalloc are not permitted; a runtime whose ResourceGovernor has
-// entered its pressure or critical state and refuses every new reservation, yet must still route
-// the tokens already in flight; and decode loops that cannot afford the device-wide
-// synchronisation cudaMalloc/cudaFree may perform. vlb_route_device allocates its score scratch
-// for every call; this variant takes it from a fixed array compiled into the library instead.
+// Who cannot allocate: a runtime whose ResourceGovernor has entered its pressure or critical state
+// and refuses every new reservation, yet must still route the tokens already in flight; callers
+// that are not allowed to call cudaMalloc at all (an embedding application that owns the device
+// memory budget); and decode loops that cannot afford the device-wide synchronisation
+// cudaMalloc/cudaFree may perform. vlb_route_device keeps its score scratch in the handle and grows
+// it with cudaMalloc when a call needs more than the handle holds; this variant never allocates:
+// its scratch is a fixed array compiled into the library.
+//
+// The call is ordinary host code: it launches kernels and then synchronises the stream to read the
+// route's error flag, so it must not be made from a CUDA host callback or while a stream capture
+// is open.
 //
 // The scratch is one file-scope __device__ array of kNoAllocScratchBytes (1 MiB). Every GPU that
 // loads the library holds it until the process exits. In host code the array's name is only a
@@ -70,7 +75,8 @@ extern "C" int vlb_route_device_noalloc(int ordinal, int score, int hash_routing
                                         void* stream) {
     if (ordinal < 0 || ordinal >= kMaxDevices)
         return fail(VLB_ERR_INVALID_ARGUMENT, "device ordinal is out of range");
-    if (!logits || !idx || !weights || T == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512)
+    if (!logits || !idx || !weights || T == 0 || E == 0 || k == 0 || k > E || k > 16 || E > 512 ||
+        score < VLB_SCORE_SQRT_SOFTPLUS || score > VLB_SCORE_SOFTMAX_F64_NORM)
         return fail(VLB_ERR_INVALID_ARGUMENT, "invalid route argument");
     if (hash_routing && (!token_ids || !tid2eid || vocab == 0))
         return fail(VLB_ERR_INVALID_ARGUMENT, "hash routing needs token ids and a table");
@@ -108,6 +114,7 @@ extern "C" int vlb_route_device_noalloc(int ordinal, int score, int hash_routing
         else if (flags & 2u) st = fail(VLB_ERR_INVALID_FORMAT, "route selects an out-of-range expert");
         else if (flags & 4u) st = fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
     }
-    if (prev != ordinal) cudaSetDevice(prev);
+    if (prev != ordinal && (e = cudaSetDevice(prev)) != cudaSuccess && st == VLB_OK)
+        st = cuda_fail("cudaSetDevice (restoring the caller's device)", e);
     return st;
 }

@@ -72,6 +72,8 @@ class LayerSpec:
     mixed_types: bool = False      # config 3: experts alternate IQ2_XXS / Q8_0 by seeded coin
     logits_given: bool = False     # config 3/4: routing logits are an input
     zipf_s: float = 0.0            # config 4: Zipf-skewed popularity of the given logits
+    routed_swiglu_limit: float = 0.0   # SwiGLU clamp of the routed / shared experts (0: off)
+    shared_swiglu_limit: float = 0.0
 
 
 def config(n: int, scale: str = "full") -> LayerSpec:
@@ -122,12 +124,16 @@ def layer_weights(spec: LayerSpec, seed: int) -> LayerWeights:
     else:
         router = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
     bias = None
-    if not spec.hash_routing and spec.score != SCORE_SOFTMAX:
+    if not spec.hash_routing and spec.score in (SCORE_SQRT_SOFTPLUS, SCORE_SIGMOID):
         bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
     tid2eid = None
     if spec.hash_routing:
-        # distinct experts per row: the first k of a random permutation (argsort of uniforms)
-        tid2eid = np.argsort(rng.random((spec.vocab, E)), axis=1)[:, :k].astype(np.uint32)
+        # distinct experts per row: the first k of a random permutation (argsort of uniforms),
+        # drawn in row chunks (the same stream as one draw) to bound the memory at full vocabulary
+        tid2eid = np.empty((spec.vocab, k), np.uint32)
+        for r0 in range(0, spec.vocab, 8192):
+            r1 = min(spec.vocab, r0 + 8192)
+            tid2eid[r0:r1] = np.argsort(rng.random((r1 - r0, E)), axis=1)[:, :k]
     W = LayerWeights(spec, router, bias, tid2eid)
     for e in range(E):
         gt, dt = spec.gate_type, spec.down_type
@@ -187,7 +193,8 @@ def upload_layer(dev, W: LayerWeights, max_tokens: int, layer_index: int = 0):
     layer = MoeLayer(dev, hidden=H, intermediate=I, experts=spec.experts, top_k=spec.top_k,
                      router=W.router, w1=mats["w1"], w3=mats["w3"], w2=mats["w2"], score=spec.score,
                      bias=W.bias, route_scale=spec.route_scale, hash_table=W.tid2eid,
-                     weight_after_down=spec.weight_after_down, shared=shared, max_tokens=max_tokens)
+                     weight_after_down=spec.weight_after_down, shared=shared, max_tokens=max_tokens,
+                     routed_swiglu_limit=spec.routed_swiglu_limit, shared_swiglu_limit=spec.shared_swiglu_limit)
     layer.matrices = mats
     layer.shared_matrices = shared
     return layer
