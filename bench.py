@@ -63,7 +63,8 @@ def load_tensor_peaks():
 
 class ClockSampler:
     """SM clocks and throttle reasons sampled through NVML (read-only queries) every few
-    milliseconds while the timed region runs; falls back to nvidia-smi polling."""
+    milliseconds while the timed region runs. Without NVML (pynvml missing or failing) nothing is
+    sampled and stop() returns {"samples": 0, "source": "unavailable: ..."}."""
 
     REASONS = {  # nvmlClocksEventReason bits
         "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
@@ -78,6 +79,7 @@ class ClockSampler:
         self.max_mhz = None
         self._stop = False
         self._thread = None
+        self.unavailable = None
 
     def start(self):
         import threading
@@ -86,7 +88,8 @@ class ClockSampler:
             pynvml.nvmlInit()
             h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
-        except Exception:
+        except Exception as e:  # noqa: BLE001 - any NVML failure means no clock record
+            self.unavailable = f"unavailable: NVML ({type(e).__name__})"
             return
 
         def run():
@@ -103,11 +106,11 @@ class ClockSampler:
 
     def stop(self):
         if self._thread is None:
-            return None
+            return {"samples": 0, "source": self.unavailable or "unavailable: sampler not started"}
         self._stop = True
         self._thread.join(timeout=2)
         if not self.samples:
-            return None
+            return {"samples": 0, "source": "nvml (no sample inside the timed region)"}
         names = sorted(n for n, bit in self.REASONS.items() if self.reasons & bit)
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
                 "reasons": names, "samples": len(self.samples), "source": "nvml"}
@@ -287,10 +290,12 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(out.nbytes),
                 "timing": "host wall clock around the synchronous C-ABI call"},
         "clocks": clk,
-        "gpu_launches": (7 + (1 if ((spec.experts + 7) // 8) * ((T + 7) // 8) < 256 else 0)) * args.steps,
+        "gpu_launches": kernels_per_forward(spec, T) * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget)
+    if not args.no_configs:
+        result["configs"] = run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=(W, layer))
     layer.destroy()
     for lst in layer.matrices.values():
         for m in lst:
@@ -338,7 +343,7 @@ def run_ep(args, dev, rank, world, local_rank):
         layer.forward(xd, ld, T)
     torch.cuda.synchronize()
     torch.distributed.barrier()
-    steps = args.ep_steps
+    steps = args.ep_steps or max(3, min(args.steps, 20))
     times, experts_s = [], []
     for _ in range(steps):
         start = torch.cuda.Event(enable_timing=True)
@@ -360,6 +365,8 @@ def run_ep(args, dev, rank, world, local_rank):
     recv_min = comm.min_over_ranks(float(recv), xd)
     out = layer.forward(xd, ld, T).cpu().numpy()
     assert np.all(np.isfinite(out))
+    check = ep_parity_check(dev, W, x_host, logits_host, out)
+    check_max = comm.max_over_ranks(check["max_rel_err"], xd)
     res = {
         "value": round(T * world / (ms_max / 1000.0), 1), "unit": "tokens/s", "ms_per_step": round(ms_max, 4),
         "steps": steps, "scaling": "weak", "n_gpus": world,
@@ -373,11 +380,41 @@ def run_ep(args, dev, rank, world, local_rank):
                            "imbalance_ms": round(ex_max - ex_min, 4), "received_rows_max": int(recv_max),
                            "received_rows_min": int(recv_min), "rows_per_rank_balanced": T * spec.top_k},
         "phases_ms_rank0": {k_: round(v * 1000.0, 4) for k_, v in layer.last.items() if k_.endswith("_s")},
+        "check": {"max_rel_err": check_max, "rank0": check, "bound": 4e-3,
+                  "against": "the same tokens through one GPU holding all experts, exact decode path"},
     }
+    assert check_max <= 4e-3, f"expert-parallel output differs from the single-GPU layer: {check_max}"
     ops.close()
     if created_group:
         torch.distributed.destroy_process_group()
     return res
+
+
+def ep_parity_check(dev, W, x_host, logits_host, out_ep):
+    """The expert-parallel output of this rank's tokens against the same tokens through a
+    single-GPU layer holding all experts on the exact decode path (f32 accumulation of exact
+    products; itself held to 1e-5 against the oracle by the tests). The exchange carries fp16
+    rows and the group forward runs the tensor-core path, so ~1e-3 is expected."""
+    import vastloom_b200 as vb
+    from vastloom_b200 import synth
+
+    T = x_host.shape[0]
+    full = synth.upload_layer(dev, W, max_tokens=T)
+    try:
+        full.set_prefill_tokens(vb.MoeLayer.PREFILL_NEVER)
+        ref = full.forward(x_host, None, logits_host)
+    finally:
+        full.destroy()
+        for lst in full.matrices.values():
+            for m in lst:
+                dev.release_matrix(m)
+        for m in full.shared_matrices or ():
+            dev.release_matrix(m)
+    diff = np.abs(out_ep.astype(np.float64) - ref.astype(np.float64))
+    num = np.linalg.norm(out_ep.astype(np.float64) - ref.astype(np.float64), axis=1)
+    den = np.maximum(np.linalg.norm(ref.astype(np.float64), axis=1), 1e-30)
+    return {"max_rel_err": float(np.max(diff) / max(float(np.max(np.abs(ref))), 1e-30)),
+            "max_token_rel_err": float(np.max(num / den)), "tokens": int(T)}
 
 
 def run_prefill(args, dev, stream, flush_l2, rank, world, local_rank):
@@ -474,9 +511,11 @@ def run_prefill(args, dev, stream, flush_l2, rank, world, local_rank):
                    "shared_type": "Q8_0", "routing": "given N(0,1) logits, sqrt_softplus+bias, renorm",
                    "l2": "flushed (256 MiB write) before every timed step"},
         "roofline": {"bound": "tensor", "kernel": f"prefill_gemm_kernel<{'true' if dom == 'gate_up' else 'false'}>",
-                     "achieved": round(achieved, 1), "peak": sustained, "unit": "TFLOP/s",
-                     "frac": round(achieved / sustained, 4), "peak_kind": f"{kind} sustained bf16 (fp16 same rate)",
-                     "frac_of_burst": round(achieved / burst, 4), "traffic": traffic_from_profiles("prefill_gemm_kernel"),
+                     "achieved": round(achieved, 1), "peak": burst, "unit": "TFLOP/s",
+                     "frac": round(achieved / burst, 4),
+                     "peak_kind": f"{kind} burst bf16 (a kernel of a few ms timed alone; fp16 runs at the same rate)",
+                     "frac_of_sustained": round(achieved / sustained, 4), "peak_sustained": sustained,
+                     "traffic": traffic_from_profiles(f"prefill_gemm_kernel<{'true' if dom == 'gate_up' else 'false'}>"),
                      "algorithmic_flops": flops[dom], "kernel_ms": round(phase_ms[dom], 5)},
         "layer_tflops": round(layer_tflops, 1),
         "phase_ms": {p: round(v, 5) for p, v in phase_ms.items()},
@@ -496,7 +535,7 @@ def run_prefill(args, dev, stream, flush_l2, rank, world, local_rank):
     return res
 
 
-def cpu_baseline(W, x, budget_s: float, threads: int | None = None, logits=None):
+def cpu_baseline(W, x, budget_s: float, threads: int | None = None, logits=None, token_ids=None):
     """The reference's own CPU path (oracle/_ref) on a bounded sample of the same batch."""
     from oracle.oracle import Reference
 
@@ -508,16 +547,247 @@ def cpu_baseline(W, x, budget_s: float, threads: int | None = None, logits=None)
     # RowWorkPool has hardware_concurrency()/2 workers plus the caller (ggml_quantization.cpp:761)
     threads = threads or max(1, cores // 2 + 1)
     lg = (lambda a, b: None) if logits is None else (lambda a, b: logits[a:b])
+    tk = (lambda a, b: None) if token_ids is None else (lambda a, b: token_ids[a:b])
     t0 = time.perf_counter()
-    ref.moe_forward(W, x[:1], None, lg(0, 1), threads=threads)
+    ref.moe_forward(W, x[:1], tk(0, 1), lg(0, 1), threads=threads)
     t1 = time.perf_counter() - t0
     n = int(max(1, min(x.shape[0], budget_s / max(t1, 1e-6))))
     t0 = time.perf_counter()
-    ref.moe_forward(W, x[:n], None, lg(0, n), threads=threads)
+    ref.moe_forward(W, x[:n], tk(0, n), lg(0, n), threads=threads)
     dt = time.perf_counter() - t0
     return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
             "sample": f"first {n} of the {x.shape[0]} batch tokens through the reference's layer loop "
                       f"({dt:.1f} s, max_threads={threads} of {cores} host threads)"}
+
+
+# ---- decode-size objects of the other benchmark configurations ---------------------------------
+
+MMA_TYPES = (8, 16)  # Q8_0, IQ2_XXS: the tensor-core decode kernels; IQ3_XXS / IQ1_S: CUDA cores
+
+
+def kernels_per_forward(spec, T, logits_given=False, norm=False):
+    """Kernel launches of one layer forward (the library's launch sequence for this shape)."""
+    types = {spec.gate_type, spec.down_type} | ({spec.shared_type} if spec.shared_type is not None else set())
+    n = 1  # token prescale, or the RMSNorm entry step of a residual block
+    n += 1 if logits_given else 1  # score kernel on given logits, or the router projection
+    n += 1  # top-k route
+    n += 1 if T * spec.top_k <= 4096 else 3  # dispatch
+    if any(t in MMA_TYPES for t in types):
+        n += 2
+    if any(t not in MMA_TYPES for t in types):
+        n += 2
+    return n + 1  # combine
+
+
+def expert_kernel_name(spec, phase):
+    t = spec.gate_type if phase == "gate_up" else spec.down_type
+    flag = "true" if phase == "gate_up" else "false"
+    return f"decode_experts_kernel<{flag}>" if t in MMA_TYPES else f"expert_kernel<{flag}>"
+
+
+def measure_decode_object(dev, stream, flush_l2, Ws, layers, T, x_host, tok_host, args, rank, world, workload,
+                          chain=False, cpu_budget=5.0):
+    """One decode-size workload: a single layer (chain=False) or the layers applied in sequence as
+    residual blocks (chain=True). Device-timed steps with a cold L2, the host-memory C-ABI call
+    end to end, per-phase times, the HBM roofline of the dominant expert kernel, and the
+    reference CPU path on a bounded sample."""
+    import torch
+
+    import vastloom_b200 as vb
+
+    spec = Ws[0].spec
+    H = spec.hidden
+    with torch.cuda.stream(stream):
+        bufs = [torch.from_numpy(x_host).cuda(), torch.empty((T, H), dtype=torch.float32, device="cuda")]
+        if chain:
+            bufs.append(torch.empty((T, H), dtype=torch.float32, device="cuda"))
+        tok_dev = torch.from_numpy(tok_host.astype(np.uint32).view(np.int32)).cuda() if tok_host is not None else None
+    torch.cuda.synchronize()
+    tok_ptr = tok_dev.data_ptr() if tok_dev is not None else 0
+
+    def step():
+        if not chain:
+            layers[0].forward_device(bufs[0].data_ptr(), T, bufs[1].data_ptr(), token_ids_ptr=tok_ptr, stream=dev.stream)
+            return
+        src = 0
+        for i, layer in enumerate(layers):
+            dst = 1 if i % 2 == 0 else 2
+            layer.forward_device(bufs[src].data_ptr(), T, bufs[dst].data_ptr(), token_ids_ptr=tok_ptr, stream=dev.stream)
+            src = dst
+
+    for _ in range(args.warmup):
+        flush_l2()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    steps = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush_l2()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    total_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms = total_ms / steps
+    for layer in layers:
+        layer.status()
+    # end to end through the public host-memory calls
+    pinned_x = torch.from_numpy(x_host).pin_memory().numpy()
+    e2e = []
+    if chain:
+        lc = vb.LayerChain(dev, layers, max_tokens=T)
+        try:
+            for _ in range(max(3, min(steps, 20))):
+                flush_l2()
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                out = lc.forward(pinned_x, tok_host)
+                e2e.append(time.perf_counter() - t0)
+        finally:
+            lc.close()
+    else:
+        out = torch.empty((T, H), dtype=torch.float32).pin_memory().numpy()
+        for _ in range(max(3, min(steps, 20))):
+            flush_l2()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            layers[0].forward(pinned_x, tok_host, out=out)
+            e2e.append(time.perf_counter() - t0)
+    assert np.all(np.isfinite(out))
+    # phases (summed over the layers of a chain) and algorithmic bytes
+    phase_sum = {p: 0.0 for p in vb.MoeLayer.PHASES}
+    bytes_sum = {"route": 0, "gate_up": 0, "down": 0, "combine": 0}
+    active = []
+    for layer in layers:
+        layer.set_profiling(True)
+    reps = max(3, min(steps, 20))
+    for _ in range(reps):
+        flush_l2()
+        step()
+        for layer in layers:
+            for p, v in layer.phase_times().items():
+                phase_sum[p] += v / reps
+    for W, layer in zip(Ws, layers):
+        layer.set_profiling(False)
+        _, _, offsets, _, _ = layer.last_route(T)
+        pb = phase_bytes(W.spec, W, layer, T, offsets)
+        for p in bytes_sum:
+            bytes_sum[p] += pb[p]
+        active.append(pb["active_experts"])
+    hbm, peak_kind = load_peaks()
+    dom = max(("gate_up", "down"), key=lambda p: phase_sum[p])
+    achieved = bytes_sum[dom] / (phase_sum[dom] / 1000.0) / 1e9
+    layer_bytes = sum(bytes_sum.values())
+    res = {
+        "value": round(T * world / (ms / 1000.0), 1), "unit": "tokens/s", "ms_per_step": round(ms, 5),
+        "steps": steps, "tokens_per_gpu": T, "workload": workload,
+        "roofline": {"bound": "hbm", "kernel": expert_kernel_name(spec, dom), "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                     "traffic": None, "algorithmic_bytes": bytes_sum[dom], "kernel_ms": round(phase_sum[dom], 5)},
+        "layer_roofline": {"bytes": layer_bytes, "achieved_gbs": round(layer_bytes / (ms / 1000.0) / 1e9, 1),
+                           "frac": round(layer_bytes / (ms / 1000.0) / 1e9 / hbm, 4), "active_experts": active},
+        "phase_ms": {p: round(v, 5) for p, v in phase_sum.items()},
+        "e2e": {"value": round(T * world / statistics.mean(e2e), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x_host.nbytes + (0 if tok_host is None else 4 * T)),
+                "d2h_bytes_per_step": int(T * H * 4),
+                "timing": "host wall clock around the synchronous host-memory call"},
+        "gpu_launches": sum(kernels_per_forward(W.spec, T, norm=chain) for W in Ws) * steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_chain(Ws, x_host, tok_host, cpu_budget) if chain else \
+            cpu_baseline(Ws[0], x_host, budget_s=cpu_budget, token_ids=tok_host)
+    return res
+
+
+def cpu_baseline_chain(Ws, x, tok, budget_s):
+    """The reference's CPU path for the residual chain: its RMSNorm and its layer loop per layer,
+    f32 residual addition, on the first n tokens of the batch."""
+    from oracle.oracle import Reference
+
+    if not Reference.available():
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref is not built"}
+    ref = Reference()
+    cores = os.cpu_count() or 1
+    threads = max(1, cores // 2 + 1)
+    H = Ws[0].spec.hidden
+    ones = np.ones(H, np.float32)
+
+    def run(n):
+        h = x[:n].copy()
+        for W in Ws:
+            o, _, _ = ref.moe_forward(W, ref.rms_norm(h, ones, 1e-6), None if tok is None else tok[:n],
+                                      threads=threads)
+            h = (h + o).astype(np.float32)
+        return h
+
+    t0 = time.perf_counter()
+    run(1)
+    t1 = time.perf_counter() - t0
+    n = int(max(1, min(x.shape[0], budget_s / max(t1, 1e-6))))
+    t0 = time.perf_counter()
+    run(n)
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"first {n} of the {x.shape[0]} prompt tokens through the reference's RMSNorm and layer loop, "
+                      f"{len(Ws)} layers ({dt:.1f} s, max_threads={threads} of {cores} host threads)"}
+
+
+def run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=None):
+    """Decode-size numbers of configurations 0 (T = 1, 16), 1 (T = 1, 8; the headline is T = 64)
+    and 2 (the three-layer residual chain, prompts of 1 and 5 tokens)."""
+    from vastloom_b200 import synth
+
+    out = {}
+    budget = args.cpu_budget / 4
+
+    def release(layer):
+        layer.destroy()
+        for lst in layer.matrices.values():
+            for m in lst:
+                dev.release_matrix(m)
+        for m in layer.shared_matrices or ():
+            dev.release_matrix(m)
+
+    spec0 = synth.config(0)
+    W0 = synth.layer_weights(spec0, seed=10)
+    L0 = synth.upload_layer(dev, W0, max_tokens=16)
+    try:
+        for T in (1, 16):
+            x, _, _ = synth.activations(spec0, T, seed=20 + T + 100 * rank)
+            out[f"cfg0-T{T}"] = measure_decode_object(dev, stream, flush_l2, [W0], [L0], T, x, None, args, rank, world,
+                                                     f"cfg0-olmoe-q8_0-T{T}", cpu_budget=budget)
+    finally:
+        release(L0)
+    if cfg1 is not None:
+        W1, L1 = cfg1
+        for T in (1, 8):
+            x, _, _ = synth.activations(W1.spec, T, seed=30 + T + 100 * rank)
+            out[f"cfg1-T{T}"] = measure_decode_object(dev, stream, flush_l2, [W1], [L1], T, x, None, args, rank, world,
+                                                     f"cfg1-v4flash-decode-T{T}", cpu_budget=budget)
+    spec2 = synth.config(2)
+    W2 = [synth.layer_weights(spec2, seed=40 + i) for i in range(3)]
+    L2 = [synth.upload_layer(dev, W, max_tokens=8, layer_index=i) for i, W in enumerate(W2)]
+    try:
+        for layer in L2:
+            layer.set_input_norm(np.ones(spec2.hidden, np.float32), 1e-6)
+        for T in (1, 5):
+            x, tok, _ = synth.activations(spec2, T, seed=60 + T + 100 * rank)
+            out[f"cfg2-chain-T{T}"] = measure_decode_object(dev, stream, flush_l2, W2, L2, T, x, tok, args, rank, world,
+                                                           f"cfg2-hash-chain-3x-T{T}", chain=True, cpu_budget=budget)
+    finally:
+        for layer in L2:
+            release(layer)
+    return out
 
 
 def run_reference(args, rank, world):
@@ -578,8 +848,10 @@ def main():
                     help="routed experts of the prefill case (smaller = a profiling-sized case)")
     ap.add_argument("--only-prefill", action="store_true", help="run the prefill object alone")
     ap.add_argument("--no-ep", action="store_true", help="skip the configuration-4 expert-parallel object")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the decode objects of configurations 0, 1 (T = 1, 8) and 2 (chain)")
     ap.add_argument("--ep-tokens", type=int, default=8192)
-    ap.add_argument("--ep-steps", type=int, default=5)
+    ap.add_argument("--ep-steps", type=int, default=0, help="0: min(--steps, 20), at least 3")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

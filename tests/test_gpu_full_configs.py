@@ -24,6 +24,7 @@ from vastloom_b200 import synth
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-5
+PREFILL_CONTRACT = 2e-2
 PREFILL_EXPECTED = 4e-3
 
 
@@ -148,13 +149,17 @@ def test_gpu_layer_swiglu_clamp(device, oracle, limits, prefill, cfg):
     x, tok, logits = synth.activations(spec, 37, seed=710 + cfg)
     layer = synth.upload_layer(device, W, max_tokens=64)
     try:
+        # The prefill path's error is absolute at the scale of the gate/up rows (fp16 operands);
+        # limits far below that scale turn those rows into activations near zero, where the same
+        # absolute error is a larger relative one: the contract (2e-2) is the bound there.
+        tol = TOL if not prefill else (PREFILL_CONTRACT if limits[0] < 1.0 else PREFILL_EXPECTED)
         if prefill:
             layer.set_prefill_tokens(1)
-        out = _check_layer(layer, oracle, W, x, tok, logits, tol=PREFILL_EXPECTED if prefill else TOL)
+        out = _check_layer(layer, oracle, W, x, tok, logits, tol=tol)
         if limits[0] < 1.0:
             unclamped, _, _ = oracle.moe_forward(replace(W, spec=replace(spec, routed_swiglu_limit=0.0,
                                                                         shared_swiglu_limit=0.0)), x, tok, logits)
-            assert rel_err(out, unclamped) > 10 * (PREFILL_EXPECTED if prefill else TOL)
+            assert rel_err(out, unclamped) > 10 * tol
     finally:
         _release(device, layer)
 

@@ -20,6 +20,7 @@
 #include "vlb_gemv.cuh"
 #include "vlb_launch.h"
 #include "vlb_mma.cuh"
+#include "vlb_tcgen05.cuh"
 
 namespace vlb {
 
@@ -125,16 +126,18 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 // values is exact in f64, so fma(x, w, s) rounds exactly like s + x * w, and a thread that walks
 // the columns in order reproduces the reference's logit bit for bit. That order is the whole cost:
 // each logit is a chain of H dependent f64 additions, so the kernel is latency-bound (H times the
-// DFMA latency) and spends its effort on keeping every chain fed: a CTA computes a tile of 32
-// experts (the lanes) x 4 tokens (the warps), stages a column slice of the tile's weights and
-// activations in shared memory as f64 (each f32 converted once per CTA, not once per use), and
-// loads the next slice into registers while the chains consume the current one. (The slice is
-// 64 columns: the f64 copies of two slices then fit the 48 KB of static shared memory.)
+// DFMA latency) and is built to keep every chain fed: a CTA computes a tile of 32 experts (the
+// lanes) x 4 tokens (the warps); 64-column slices of the tile's f32 weights and activations stream
+// into a 4-stage shared-memory ring with cp.async (three slices in flight while the chains consume
+// the fourth), and each slice's 64 steps are unrolled so that its shared-memory loads run ahead of
+// the dependent DFMAs.
 constexpr uint32_t kRtExperts = 32;
 constexpr uint32_t kRtTokens = 4;
 constexpr uint32_t kRtCols = 64;
-constexpr uint32_t kRtWStride = kRtCols + 2;  // doubles per staged weight row: 16-byte phase shift per row
+constexpr uint32_t kRtStages = 4;
+constexpr uint32_t kRtWStride = kRtCols + 4;  // floats per staged weight row: a 16-byte phase shift per row
 constexpr uint32_t kRtThreads = kRtExperts * kRtTokens;
+constexpr uint32_t kRtStageFloats = kRtExperts * kRtWStride + kRtTokens * kRtCols;
 
 __device__ __forceinline__ float sqrt_softplus_dev(float v) {
     const double p = (double)v;
@@ -158,70 +161,65 @@ __global__ void __launch_bounds__(kRtThreads) router_kernel(const float* __restr
                                                             uint32_t H, uint32_t E, int score,
                                                             float* __restrict__ logits,
                                                             float* __restrict__ scores) {
-    __shared__ __align__(16) double ws[2][kRtExperts * kRtWStride];
-    __shared__ __align__(16) double xs[2][kRtTokens * kRtCols];
+    __shared__ __align__(16) float ring[kRtStages * kRtStageFloats];
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t e0 = blockIdx.x * kRtExperts, t0 = blockIdx.y * kRtTokens;
-    // staging roles: 512 weight float4s of a slice -> 4 per thread; 64 activation float4s -> one
-    // for each of the first 64 threads
-    constexpr int kWf = (int)(kRtExperts * kRtCols / 4u / kRtThreads);
-    float4 wr[kWf], xr = make_float4(0.f, 0.f, 0.f, 0.f);
-    const bool xrole = threadIdx.x < kRtTokens * kRtCols / 4u;
-    auto fetch = [&](uint32_t c0) {
-#pragma unroll
-        for (int i = 0; i < kWf; ++i) {
-            const uint32_t f = threadIdx.x + (uint32_t)i * kRtThreads;  // float4 index in the slice
-            const uint32_t r = f / (kRtCols / 4u), c = c0 + (f % (kRtCols / 4u)) * 4u;
-            wr[i] = (e0 + r < E && c < H) ? __ldg(reinterpret_cast<const float4*>(w + (size_t)(e0 + r) * H + c))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        const uint32_t r = threadIdx.x / (kRtCols / 4u), c = c0 + (threadIdx.x % (kRtCols / 4u)) * 4u;
-        if (xrole)
-            xr = (t0 + r < T && c < H) ? __ldg(reinterpret_cast<const float4*>(x + (size_t)(t0 + r) * H + c))
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-    };
-    auto store = [&](int b) {
-#pragma unroll
-        for (int i = 0; i < kWf; ++i) {
-            const uint32_t f = threadIdx.x + (uint32_t)i * kRtThreads;
-            double* d = &ws[b][(f / (kRtCols / 4u)) * kRtWStride + (f % (kRtCols / 4u)) * 4u];
-            *reinterpret_cast<double2*>(d) = make_double2(wr[i].x, wr[i].y);
-            *reinterpret_cast<double2*>(d + 2) = make_double2(wr[i].z, wr[i].w);
-        }
-        if (xrole) {
-            double* d = &xs[b][(threadIdx.x / (kRtCols / 4u)) * kRtCols + (threadIdx.x % (kRtCols / 4u)) * 4u];
-            *reinterpret_cast<double2*>(d) = make_double2(xr.x, xr.y);
-            *reinterpret_cast<double2*>(d + 2) = make_double2(xr.z, xr.w);
-        }
-    };
-    fetch(0);
-    store(0);
-    __syncthreads();
-    double acc = 0.0;
-    const double* wrow0 = &ws[0][lane * kRtWStride];
-    const double* wrow1 = &ws[1][lane * kRtWStride];
     const uint32_t slices = (H + kRtCols - 1u) / kRtCols;
-    for (uint32_t sl = 0; sl < slices; ++sl) {
-        const int b = (int)(sl & 1u);
-        if (sl + 1u < slices) fetch((sl + 1u) * kRtCols);  // in flight while the chain runs
-        const double* wrow = b ? wrow1 : wrow0;
-        const double* xrow = &xs[b][warp * kRtCols];
-        const uint32_t n = min(kRtCols, H - sl * kRtCols);  // a multiple of 4 (H % 4 == 0)
-        for (uint32_t c = 0; c < n; c += 4u) {
-            const double2 wa = *reinterpret_cast<const double2*>(wrow + c);
-            const double2 wb = *reinterpret_cast<const double2*>(wrow + c + 2u);
-            const double2 xa = *reinterpret_cast<const double2*>(xrow + c);
-            const double2 xb = *reinterpret_cast<const double2*>(xrow + c + 2u);
-            acc = __fma_rn(xa.x, wa.x, acc);
-            acc = __fma_rn(xa.y, wa.y, acc);
-            acc = __fma_rn(xb.x, wb.x, acc);
-            acc = __fma_rn(xb.y, wb.y, acc);
+    // slice `sl` into stage sl % kRtStages: 512 weight float4s (4 per thread) and 64 activation
+    // float4s (threads 0..63); rows past E / T and columns past H are zero-filled
+    auto issue = [&](uint32_t sl) {
+        float* st = ring + (sl % kRtStages) * kRtStageFloats;
+        const uint32_t c0 = sl * kRtCols;
+#pragma unroll
+        for (uint32_t i = 0; i < kRtExperts * kRtCols / 4u / kRtThreads; ++i) {
+            const uint32_t f = threadIdx.x + i * kRtThreads;
+            const uint32_t r = f / (kRtCols / 4u), c = (f % (kRtCols / 4u)) * 4u;
+            const bool ok = e0 + r < E && c0 + c < H;
+            tc::cp_async16(st + r * kRtWStride + c, ok ? w + (size_t)(e0 + r) * H + c0 + c : w, ok ? 16u : 0u);
         }
-        if (sl + 1u < slices) {
-            store(b ^ 1);  // the other buffer: its last readers finished before the previous barrier
-            __syncthreads();
+        if (threadIdx.x < kRtTokens * kRtCols / 4u) {
+            const uint32_t r = threadIdx.x / (kRtCols / 4u), c = (threadIdx.x % (kRtCols / 4u)) * 4u;
+            const bool ok = t0 + r < T && c0 + c < H;
+            tc::cp_async16(st + kRtExperts * kRtWStride + r * kRtCols + c, ok ? x + (size_t)(t0 + r) * H + c0 + c : x,
+                           ok ? 16u : 0u);
+        }
+    };
+    for (uint32_t sl = 0; sl < kRtStages - 1u; ++sl) {
+        if (sl < slices) issue(sl);
+        tc::cp_async_commit();  // (an empty group past the last slice keeps the count uniform)
+    }
+    double acc = 0.0;
+    for (uint32_t sl = 0; sl < slices; ++sl) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kRtStages - 2u) : "memory");  // slice sl has landed
+        __syncthreads();  // ... for every thread; and every thread is done with slice sl - 1's stage
+        if (sl + kRtStages - 1u < slices) issue(sl + kRtStages - 1u);
+        tc::cp_async_commit();
+        const float* st = ring + (sl % kRtStages) * kRtStageFloats;
+        const float* wr = st + lane * kRtWStride;
+        const float* xr = st + kRtExperts * kRtWStride + warp * kRtCols;
+        const uint32_t n = H - sl * kRtCols;  // a multiple of 4 (H % 4 == 0)
+        if (n >= kRtCols) {
+#pragma unroll
+            for (uint32_t c = 0; c < kRtCols; c += 4u) {
+                const float4 wv = *reinterpret_cast<const float4*>(wr + c);
+                const float4 xv = *reinterpret_cast<const float4*>(xr + c);
+                acc = __fma_rn((double)xv.x, (double)wv.x, acc);
+                acc = __fma_rn((double)xv.y, (double)wv.y, acc);
+                acc = __fma_rn((double)xv.z, (double)wv.z, acc);
+                acc = __fma_rn((double)xv.w, (double)wv.w, acc);
+            }
+        } else {
+            for (uint32_t c = 0; c < n; c += 4u) {
+                const float4 wv = *reinterpret_cast<const float4*>(wr + c);
+                const float4 xv = *reinterpret_cast<const float4*>(xr + c);
+                acc = __fma_rn((double)xv.x, (double)wv.x, acc);
+                acc = __fma_rn((double)xv.y, (double)wv.y, acc);
+                acc = __fma_rn((double)xv.z, (double)wv.z, acc);
+                acc = __fma_rn((double)xv.w, (double)wv.w, acc);
+            }
         }
     }
+    tc::cp_async_wait_all();
     const uint32_t e = e0 + lane, t = t0 + warp;
     if (e < E && t < T) {
         const float lg = (float)acc;
