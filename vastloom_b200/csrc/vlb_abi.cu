@@ -171,7 +171,7 @@ struct vlb_matrix {
 struct vlb_layer {
     vlb_moe_layer_desc desc{};
     bool has_shared = false;
-    float* router = nullptr;
+    double* router = nullptr;  // f64 widening of the f32 router weights
     float* bias = nullptr;
     uint32_t* tid2eid = nullptr;
     DevMat* mats = nullptr;
@@ -662,8 +662,17 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
             return h->cuda_fail(#call, e_);     \
         }                                       \
     } while (0)
-    TRY(h->galloc((size_t)E * H * 4, "vlb-router", (void**)&L->router));
-    TRY_CUDA(cudaMemcpy(L->router, d->router, (size_t)E * H * 4, cudaMemcpyHostToDevice));
+    {  // the router's f32 weights as f64: the sequential router chains consume f64 operands
+        std::vector<double> wd;
+        try {
+            wd.assign(d->router, d->router + (size_t)E * H);
+        } catch (const std::bad_alloc&) {
+            free_layer(h, L);
+            return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the router weights");
+        }
+        TRY(h->galloc((size_t)E * H * 8, "vlb-router", (void**)&L->router));
+        TRY_CUDA(cudaMemcpy(L->router, wd.data(), (size_t)E * H * 8, cudaMemcpyHostToDevice));
+    }
     if (d->bias) {
         TRY(h->galloc((size_t)E * 4, "vlb-router-bias", (void**)&L->bias));
         TRY_CUDA(cudaMemcpy(L->bias, d->bias, (size_t)E * 4, cudaMemcpyHostToDevice));
@@ -690,7 +699,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
                  o_ps = carve(P * 4), o_pw = carve(P * 4), o_units = carve((size_t)mu * sizeof(Unit)),
                  o_cnt = carve(32 + T * 4), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
                  o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
-                 o_xn = carve(T * H * 4);
+                 o_xn = carve(T * H * 4), o_xd = carve(T * H * 8);
     const uint32_t mpt = prefill_max_tiles((uint32_t)T, k, E);
     const size_t o_xh = carve(P * H * 2), o_acth = carve(P * I * 2), o_pt2 = carve((size_t)mpt * sizeof(Unit));
     const size_t o_dc = carve(((T * k + 1023) / 1024) * E * 4);
@@ -740,6 +749,7 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.xmax = reinterpret_cast<uint32_t*>(ws + o_cnt + 32);
     p.act_max = reinterpret_cast<uint32_t*>(ws + o_am);
     p.x_norm = reinterpret_cast<float*>(ws + o_xn);
+    p.xd = reinterpret_cast<double*>(ws + o_xd);
     p.max_units = mu;
     p.prefill = 0;
     p.xperm = reinterpret_cast<__half*>(ws + o_xh);
@@ -1052,12 +1062,18 @@ int vlb_router_logits_device(vlb_handle* h, const float* x, const float* w, uint
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) % 16u)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "router inputs must be 16-byte aligned");
     if ((T + 3u) / 4u > 65535u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "too many router tokens for one call");
-    // scratch: the scores the kernel writes beside the logits
+    // scratch: scores [T x E] f32 | x as f64 [T x H] | w as f64 [E x H]
+    const size_t sbytes = ((size_t)T * E * 4 + 255) / 256 * 256, xbytes = (size_t)T * H * 8;
     char* scratch = nullptr;
-    int st = h->scratch_at_least((size_t)T * E * 4, &scratch);
+    int st = h->scratch_at_least(sbytes + xbytes + (size_t)E * H * 8, &scratch);
     if (st != VLB_OK) return st;
+    double* xd = reinterpret_cast<double*>(scratch + sbytes);
+    double* wd = reinterpret_cast<double*>(scratch + sbytes + xbytes);
     cudaStream_t s = h->pick(stream);
-    cudaError_t e = launch_router(x, w, T, H, E, VLB_SCORE_SOFTMAX, logits, reinterpret_cast<float*>(scratch), s);
+    cudaError_t e = launch_widen(x, (size_t)T * H, xd, s);
+    if (e == cudaSuccess) e = launch_widen(w, (size_t)E * H, wd, s);
+    if (e == cudaSuccess)
+        e = launch_router(xd, wd, T, H, E, VLB_SCORE_SOFTMAX, logits, reinterpret_cast<float*>(scratch), s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return h->cuda_fail("router", e);
     return VLB_OK;
@@ -1071,7 +1087,7 @@ int vlb_rms_norm_device(vlb_handle* h, const float* x, const float* w, uint32_t 
     if (width % 4u || width > kRmsMaxWidth || reinterpret_cast<uintptr_t>(x) % 16u)
         return h->fail(VLB_ERR_UNSUPPORTED, "RMSNorm rows must be 16-byte aligned, width % 4 == 0 and width <= " +
                                                 std::to_string(kRmsMaxWidth));
-    VLB_CUDA(h, launch_rms_norm(x, w, rows, width, eps, out, nullptr, h->pick(stream)));
+    VLB_CUDA(h, launch_rms_norm(x, w, rows, width, eps, out, nullptr, nullptr, h->pick(stream)));
     return VLB_OK;
 }
 
@@ -1156,7 +1172,7 @@ int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx, const float* wei
     VLB_CUDA(h, cudaMemcpyAsync(&bad, flag, 4, cudaMemcpyDeviceToHost, s));
     VLB_CUDA(h, cudaStreamSynchronize(s));
     if (bad) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
-    VLB_CUDA(h, launch_prescale(x, T, H, xmax, s));
+    VLB_CUDA(h, launch_prescale(x, T, H, xmax, nullptr, s));
     MoeParams p{};
     p.T = T;
     p.k = k;

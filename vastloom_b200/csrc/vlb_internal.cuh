@@ -219,7 +219,7 @@ struct MoeParams {
     int has_legacy;          // some expert uses a format the CUDA-core kernels serve (IQ3_XXS, IQ1_S)
     int has_mma;             // some expert uses a format the tensor-core kernels serve (IQ2_XXS, Q8_0)
     // weights
-    const float* router;     // [E x H]
+    const double* router;    // [E x H], the f32 router weights widened to f64 at layer creation
     const float* bias;       // [E]
     const uint32_t* tid2eid; // [vocab x k]
     const DevMat* mats;      // [3 x (E+1)]: w1[0..E], w3[0..E], w2[0..E]; index E = shared
@@ -251,6 +251,7 @@ struct MoeParams {
     float* y;                // [(T*k + T) x H]
     float* out;              // [T x H]
     uint32_t* xmax;          // [T]: bits of max|x| per token (zeroed with the counters)
+    double* xd;              // [T x H]: the router's input rows widened to f64
     uint32_t* act_max;       // [T*k + T]: bits of max|act| per pair (non-negative floats order as ints)
     // residual block (input norm set): the layer runs on xn = RMSNorm(x) (rows of x_norm) and the
     // combine adds the original rows back: out = x + MoE(xn)

@@ -126,18 +126,22 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 // values is exact in f64, so fma(x, w, s) rounds exactly like s + x * w, and a thread that walks
 // the columns in order reproduces the reference's logit bit for bit. That order is the whole cost:
 // each logit is a chain of H dependent f64 additions, so the kernel is latency-bound (H times the
-// DFMA latency) and is built to keep every chain fed: a CTA computes a tile of 32 experts (the
-// lanes) x 4 tokens (the warps); 64-column slices of the tile's f32 weights and activations stream
-// into a 4-stage shared-memory ring with cp.async (three slices in flight while the chains consume
-// the fourth), and each slice's 64 steps are unrolled so that its shared-memory loads run ahead of
-// the dependent DFMAs.
+// 8-cycle DFMA latency) and is built to keep every chain fed:
+//   * the operands arrive already widened to f64 (the layer keeps its router weights as f64; the
+//     activations are widened by the entry step): an f32 -> f64 conversion per use would cost
+//     more issue time than the DFMA chain itself;
+//   * a CTA computes a tile of 32 experts (the lanes) x 4 tokens (the warps); 32-column slices of
+//     the tile's weights and activations stream into a 4-stage shared-memory ring with cp.async
+//     (three slices in flight while the chains consume the fourth), and each slice's steps are
+//     unrolled so that the shared-memory loads run ahead of the dependent DFMAs.
 constexpr uint32_t kRtExperts = 32;
 constexpr uint32_t kRtTokens = 4;
-constexpr uint32_t kRtCols = 64;
+constexpr uint32_t kRtCols = 32;
 constexpr uint32_t kRtStages = 4;
-constexpr uint32_t kRtWStride = kRtCols + 4;  // floats per staged weight row: a 16-byte phase shift per row
+constexpr uint32_t kRtWStride = kRtCols + 2;  // doubles per staged weight row: a 16-byte phase shift per row
 constexpr uint32_t kRtThreads = kRtExperts * kRtTokens;
-constexpr uint32_t kRtStageFloats = kRtExperts * kRtWStride + kRtTokens * kRtCols;
+constexpr uint32_t kRtStageDoubles = kRtExperts * kRtWStride + kRtTokens * kRtCols;
+constexpr size_t kRtSmemBytes = (size_t)kRtStages * kRtStageDoubles * 8u;
 
 __device__ __forceinline__ float sqrt_softplus_dev(float v) {
     const double p = (double)v;
@@ -156,31 +160,32 @@ __device__ __forceinline__ float score_dev(int score, float logit) {
     return logit;  // the softmax routers work on the logits themselves
 }
 
-__global__ void __launch_bounds__(kRtThreads) router_kernel(const float* __restrict__ w,
-                                                            const float* __restrict__ x, uint32_t T,
+// wd: f64 router weights [E x H]; xd: f64 activations [T x H]; H % 2 == 0.
+__global__ void __launch_bounds__(kRtThreads) router_kernel(const double* __restrict__ wd,
+                                                            const double* __restrict__ xd, uint32_t T,
                                                             uint32_t H, uint32_t E, int score,
                                                             float* __restrict__ logits,
                                                             float* __restrict__ scores) {
-    __shared__ __align__(16) float ring[kRtStages * kRtStageFloats];
+    extern __shared__ __align__(16) double ring[];
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t e0 = blockIdx.x * kRtExperts, t0 = blockIdx.y * kRtTokens;
     const uint32_t slices = (H + kRtCols - 1u) / kRtCols;
-    // slice `sl` into stage sl % kRtStages: 512 weight float4s (4 per thread) and 64 activation
-    // float4s (threads 0..63); rows past E / T and columns past H are zero-filled
+    // slice `sl` into stage sl % kRtStages: 512 weight double2s (4 per thread) and 64 activation
+    // double2s (threads 0..63); rows past E / T and columns past H are zero-filled
     auto issue = [&](uint32_t sl) {
-        float* st = ring + (sl % kRtStages) * kRtStageFloats;
+        double* st = ring + (sl % kRtStages) * kRtStageDoubles;
         const uint32_t c0 = sl * kRtCols;
 #pragma unroll
-        for (uint32_t i = 0; i < kRtExperts * kRtCols / 4u / kRtThreads; ++i) {
+        for (uint32_t i = 0; i < kRtExperts * kRtCols / 2u / kRtThreads; ++i) {
             const uint32_t f = threadIdx.x + i * kRtThreads;
-            const uint32_t r = f / (kRtCols / 4u), c = (f % (kRtCols / 4u)) * 4u;
+            const uint32_t r = f / (kRtCols / 2u), c = (f % (kRtCols / 2u)) * 2u;
             const bool ok = e0 + r < E && c0 + c < H;
-            tc::cp_async16(st + r * kRtWStride + c, ok ? w + (size_t)(e0 + r) * H + c0 + c : w, ok ? 16u : 0u);
+            tc::cp_async16(st + r * kRtWStride + c, ok ? wd + (size_t)(e0 + r) * H + c0 + c : wd, ok ? 16u : 0u);
         }
-        if (threadIdx.x < kRtTokens * kRtCols / 4u) {
-            const uint32_t r = threadIdx.x / (kRtCols / 4u), c = (threadIdx.x % (kRtCols / 4u)) * 4u;
+        if (threadIdx.x < kRtTokens * kRtCols / 2u) {
+            const uint32_t r = threadIdx.x / (kRtCols / 2u), c = (threadIdx.x % (kRtCols / 2u)) * 2u;
             const bool ok = t0 + r < T && c0 + c < H;
-            tc::cp_async16(st + kRtExperts * kRtWStride + r * kRtCols + c, ok ? x + (size_t)(t0 + r) * H + c0 + c : x,
+            tc::cp_async16(st + kRtExperts * kRtWStride + r * kRtCols + c, ok ? xd + (size_t)(t0 + r) * H + c0 + c : xd,
                            ok ? 16u : 0u);
         }
     };
@@ -194,28 +199,24 @@ __global__ void __launch_bounds__(kRtThreads) router_kernel(const float* __restr
         __syncthreads();  // ... for every thread; and every thread is done with slice sl - 1's stage
         if (sl + kRtStages - 1u < slices) issue(sl + kRtStages - 1u);
         tc::cp_async_commit();
-        const float* st = ring + (sl % kRtStages) * kRtStageFloats;
-        const float* wr = st + lane * kRtWStride;
-        const float* xr = st + kRtExperts * kRtWStride + warp * kRtCols;
-        const uint32_t n = H - sl * kRtCols;  // a multiple of 4 (H % 4 == 0)
+        const double* st = ring + (sl % kRtStages) * kRtStageDoubles;
+        const double* wr = st + lane * kRtWStride;
+        const double* xr = st + kRtExperts * kRtWStride + warp * kRtCols;
+        const uint32_t n = H - sl * kRtCols;  // even (H % 2 == 0)
         if (n >= kRtCols) {
 #pragma unroll
-            for (uint32_t c = 0; c < kRtCols; c += 4u) {
-                const float4 wv = *reinterpret_cast<const float4*>(wr + c);
-                const float4 xv = *reinterpret_cast<const float4*>(xr + c);
-                acc = __fma_rn((double)xv.x, (double)wv.x, acc);
-                acc = __fma_rn((double)xv.y, (double)wv.y, acc);
-                acc = __fma_rn((double)xv.z, (double)wv.z, acc);
-                acc = __fma_rn((double)xv.w, (double)wv.w, acc);
+            for (uint32_t c = 0; c < kRtCols; c += 2u) {
+                const double2 wv = *reinterpret_cast<const double2*>(wr + c);
+                const double2 xv = *reinterpret_cast<const double2*>(xr + c);
+                acc = __fma_rn(xv.x, wv.x, acc);
+                acc = __fma_rn(xv.y, wv.y, acc);
             }
         } else {
-            for (uint32_t c = 0; c < n; c += 4u) {
-                const float4 wv = *reinterpret_cast<const float4*>(wr + c);
-                const float4 xv = *reinterpret_cast<const float4*>(xr + c);
-                acc = __fma_rn((double)xv.x, (double)wv.x, acc);
-                acc = __fma_rn((double)xv.y, (double)wv.y, acc);
-                acc = __fma_rn((double)xv.z, (double)wv.z, acc);
-                acc = __fma_rn((double)xv.w, (double)wv.w, acc);
+            for (uint32_t c = 0; c < n; c += 2u) {
+                const double2 wv = *reinterpret_cast<const double2*>(wr + c);
+                const double2 xv = *reinterpret_cast<const double2*>(xr + c);
+                acc = __fma_rn(xv.x, wv.x, acc);
+                acc = __fma_rn(xv.y, wv.y, acc);
             }
         }
     }
@@ -226,6 +227,11 @@ __global__ void __launch_bounds__(kRtThreads) router_kernel(const float* __restr
         logits[(size_t)t * E + e] = lg;
         scores[(size_t)t * E + e] = score_dev(score, lg);
     }
+}
+
+__global__ void widen_kernel(const float* __restrict__ src, size_t n, double* __restrict__ dst) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = (double)src[i];
 }
 
 __global__ void score_kernel(const float* __restrict__ logits, size_t n, int score,
@@ -789,16 +795,23 @@ __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
 }
 
 __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __restrict__ x, uint32_t T,
-                                                             uint32_t H, uint32_t* __restrict__ xmax) {
+                                                             uint32_t H, uint32_t* __restrict__ xmax,
+                                                             double* __restrict__ xd) {
     // grid (ceil(H / 1024), min(T, 65535)), rows strided over gridDim.y: each thread takes 4 columns
     // of one token; the token's max|x| (for the tensor-core activation prescale) is an atomic max
-    // over float bits (non-negative floats order as integers)
+    // over float bits (non-negative floats order as integers); with xd the row is also widened to
+    // f64 for the router projection
     const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
     for (uint32_t t = blockIdx.y; t < T; t += gridDim.y) {
         float m = 0.f;
         if (c < H) {
             const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * H + c);
             m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+            if (xd) {
+                double* o = xd + (size_t)t * H + c;
+                *reinterpret_cast<double2*>(o) = make_double2(v.x, v.y);
+                *reinterpret_cast<double2*>(o + 2) = make_double2(v.z, v.w);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -852,39 +865,52 @@ __global__ void __launch_bounds__(256) combine_kernel(MoeParams p) {
 // RMSNorm (deepseek_v4_reference.cpp:170-206), one CTA per row: out = f32(double(x) * inv *
 // double(w)) with inv = 1 / sqrt(sum(double(x)^2) / width + eps). The sum of squares is the
 // reference's sequential f64 sum (each square of an f32 is exact in f64, so fma(v, v, s) rounds
-// like s + v * v): one thread walks the row, staged in shared memory, in column order, so the
-// result is bit-identical; division and square root are IEEE-rounded in CUDA as on the host.
-// With xmax non-null the kernel is also the layer's entry step: it records max|out| of the row
-// (bits of a non-negative float, for the tensor-core activation prescale).
+// like s + v * v): the CTA stages the row in shared memory as f64 (every thread converts a few
+// values: a conversion per chain step would cost more than the chain) and one thread walks it in
+// column order, so the result is bit-identical; division and square root are IEEE-rounded in CUDA
+// as on the host. With xmax non-null the kernel is also the layer's entry step: it records
+// max|out| of the row (bits of a non-negative float, for the tensor-core activation prescale), and
+// with out_d the normalised row widened to f64 (the router projection's input).
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x,
                                                        const float* __restrict__ w,
                                                        uint32_t width, float eps,
                                                        float* __restrict__ out,
-                                                       uint32_t* __restrict__ xmax) {
-    extern __shared__ __align__(16) float row[];
+                                                       uint32_t* __restrict__ xmax,
+                                                       double* __restrict__ out_d) {
+    extern __shared__ __align__(16) double rowd[];
     __shared__ double inv_s;
     __shared__ float wmax[8];
     const float* xr = x + (size_t)blockIdx.x * width;
-    for (uint32_t c = threadIdx.x * 4u; c < width; c += blockDim.x * 4u)
-        *reinterpret_cast<float4*>(row + c) = *reinterpret_cast<const float4*>(xr + c);
+    for (uint32_t c = threadIdx.x * 4u; c < width; c += blockDim.x * 4u) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + c);
+        *reinterpret_cast<double2*>(rowd + c) = make_double2(v.x, v.y);
+        *reinterpret_cast<double2*>(rowd + c + 2) = make_double2(v.z, v.w);
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
         double sq = 0.0;
-        for (uint32_t c = 0; c < width; c += 4u) {
-            const float4 v = *reinterpret_cast<const float4*>(row + c);
-            sq = __fma_rn((double)v.x, (double)v.x, sq);
-            sq = __fma_rn((double)v.y, (double)v.y, sq);
-            sq = __fma_rn((double)v.z, (double)v.z, sq);
-            sq = __fma_rn((double)v.w, (double)v.w, sq);
+        uint32_t c = 0;
+        for (; c + 8u <= width; c += 8u) {
+            double v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const double2 d2 = *reinterpret_cast<const double2*>(rowd + c + i);
+                v[i] = d2.x;
+                v[i + 1] = d2.y;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sq = __fma_rn(v[i], v[i], sq);
         }
+        for (; c < width; ++c) sq = __fma_rn(rowd[c], rowd[c], sq);
         inv_s = 1.0 / sqrt(sq / (double)width + (double)eps);
     }
     __syncthreads();
     const double inv = inv_s;
     float m = 0.f;
     for (uint32_t c = threadIdx.x; c < width; c += blockDim.x) {
-        const float o = (float)(__dmul_rn(__dmul_rn((double)row[c], inv), (double)w[c]));
+        const float o = (float)(__dmul_rn(__dmul_rn(rowd[c], inv), (double)w[c]));
         out[(size_t)blockIdx.x * width + c] = o;
+        if (out_d) out_d[(size_t)blockIdx.x * width + c] = (double)o;
         m = fmaxf(m, fabsf(o));
     }
     if (!xmax) return;
@@ -966,19 +992,28 @@ cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_
     return gemv_type<4>(m, g, x, ntok, xstride, y, ystride, s);
 }
 
-cudaError_t launch_router(const float* x, const float* w, uint32_t T, uint32_t H, uint32_t E, int score,
+cudaError_t launch_router(const double* xd, const double* wd, uint32_t T, uint32_t H, uint32_t E, int score,
                           float* logits, float* scores, cudaStream_t s) {
-    if (H % 4u) return cudaErrorInvalidValue;
+    if (H % 2u) return cudaErrorInvalidValue;
     const dim3 grid((E + kRtExperts - 1u) / kRtExperts, (T + kRtTokens - 1u) / kRtTokens);
     if (grid.y > 65535u) return cudaErrorInvalidValue;
-    router_kernel<<<grid, kRtThreads, 0, s>>>(w, x, T, H, E, score, logits, scores);
+    cudaError_t e = set_smem_once(router_kernel, kRtSmemBytes);
+    if (e != cudaSuccess) return e;
+    router_kernel<<<grid, kRtThreads, kRtSmemBytes, s>>>(wd, xd, T, H, E, score, logits, scores);
     return cudaGetLastError();
 }
 
-cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, cudaStream_t s) {
+cudaError_t launch_widen(const float* src, size_t n, double* dst, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const size_t blocks = (n + 255) / 256;
+    widen_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(src, n, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, double* xd, cudaStream_t s) {
     cudaError_t e = cudaMemsetAsync(xmax, 0, (size_t)T * 4u, s);
     if (e != cudaSuccess) return e;
-    token_prescale_kernel<<<dim3((H + 1023) / 1024, rows_grid(T)), 256, 0, s>>>(x, T, H, xmax);
+    token_prescale_kernel<<<dim3((H + 1023) / 1024, rows_grid(T)), 256, 0, s>>>(x, T, H, xmax, xd);
     return cudaGetLastError();
 }
 
@@ -1013,12 +1048,14 @@ cudaError_t launch_moe(const MoeParams& p_in, cudaStream_t s, cudaEvent_t* ev) {
         if (p.norm_w) {
             // residual block entry: xn = RMSNorm(x) with each row's max|xn| (the prescale); the
             // layer then runs on xn and the combine adds x back
-            if ((e = launch_rms_norm(p.x, p.norm_w, p.T, p.H, p.norm_eps, p.x_norm, p.xmax, s)) != cudaSuccess)
+            if ((e = launch_rms_norm(p.x, p.norm_w, p.T, p.H, p.norm_eps, p.x_norm, p.xmax,
+                                     (p.logits_in || given) ? nullptr : p.xd, s)) != cudaSuccess)
                 return e;
             p.x_residual = p.x;
             p.x = p.x_norm;
         } else {
-            token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(p.x, p.T, p.H, p.xmax);
+            token_prescale_kernel<<<dim3((p.H + 1023) / 1024, rows_grid(p.T)), 256, 0, s>>>(
+                p.x, p.T, p.H, p.xmax, (p.logits_in || given) ? nullptr : p.xd);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         if (given) {
@@ -1030,7 +1067,7 @@ cudaError_t launch_moe(const MoeParams& p_in, cudaStream_t s, cudaEvent_t* ev) {
             if (p.logits_in) {
                 e = launch_scores(p.logits_in, (size_t)p.T * p.E, p.score, p.scores, s);
             } else {
-                e = launch_router(p.x, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
+                e = launch_router(p.xd, p.router, p.T, p.H, p.E, p.score, p.logits, p.scores, s);
             }
             if (e != cudaSuccess) return e;
             e = launch_route(p.scores, p.bias, p.token_ids, p.tid2eid, p.vocab, p.T, p.E, p.k, p.score,
@@ -1106,12 +1143,12 @@ cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
-                            float eps, float* out, uint32_t* xmax, cudaStream_t s) {
-    if (width % 4u || (size_t)width * 4u > kRmsMaxWidth * 4u) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)width * 4u;
+                            float eps, float* out, uint32_t* xmax, double* out_d, cudaStream_t s) {
+    if (width % 4u || width > kRmsMaxWidth) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)width * 8u;
     cudaError_t e = set_smem_once(rms_norm_kernel, smem);
     if (e != cudaSuccess) return e;
-    rms_norm_kernel<<<rows, 256, smem, s>>>(x, w, width, eps, out, xmax);
+    rms_norm_kernel<<<rows, 256, smem, s>>>(x, w, width, eps, out, xmax, out_d);
     return cudaGetLastError();
 }
 

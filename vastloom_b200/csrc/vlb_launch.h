@@ -10,10 +10,13 @@ namespace vlb {
 cudaError_t launch_dequant(const DevMat& m, const Grids& g, float* out, cudaStream_t s);
 cudaError_t launch_gemv(const DevMat& m, const Grids& g, const float* x, uint32_t ntok,
                         uint32_t xstride, float* y, uint32_t ystride, cudaStream_t s);
-// logits[t][e] = f32(sequential f64 sum of x[t][c] * w[e][c]), scores = score function of them
-cudaError_t launch_router(const float* x, const float* w, uint32_t T, uint32_t H, uint32_t E, int score,
+// logits[t][e] = f32(sequential f64 sum of xd[t][c] * wd[e][c]), scores = score function of them;
+// xd / wd are the f64 widenings of the f32 activations / router weights (H % 2 == 0)
+cudaError_t launch_router(const double* xd, const double* wd, uint32_t T, uint32_t H, uint32_t E, int score,
                           float* logits, float* scores, cudaStream_t s);
-cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, cudaStream_t s);
+cudaError_t launch_widen(const float* src, size_t n, double* dst, cudaStream_t s);
+// per-token max|x| bits; with xd non-null also the rows widened to f64
+cudaError_t launch_prescale(const float* x, uint32_t T, uint32_t H, uint32_t* xmax, double* xd, cudaStream_t s);
 cudaError_t launch_scores(const float* logits, size_t n, int score, float* scores,
                           cudaStream_t s);
 cudaError_t launch_route(const float* scores, const float* bias, const uint32_t* token_ids,
@@ -51,10 +54,11 @@ cudaError_t launch_ep_own_rows(const float* x, const uint32_t* xmax, uint32_t T,
                                __half* rows, uint32_t* meta, cudaStream_t s);
 cudaError_t launch_ep_combine(const float* y, const uint32_t* elem_row, uint32_t T, uint32_t k,
                               const float* shared_rows, uint32_t H, float* out, cudaStream_t s);
-// RMSNorm rows (bit-exact); xmax non-null: also each row's max|out| bits. width % 4 == 0 and
+// RMSNorm rows (bit-exact); xmax non-null: also each row's max|out| bits; out_d: the rows as f64.
+// width % 4 == 0 and
 // width <= kRmsMaxWidth (the row is staged in shared memory).
-constexpr uint32_t kRmsMaxWidth = 49152;
+constexpr uint32_t kRmsMaxWidth = 24576;  // the row staged as f64 in shared memory
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
-                            float eps, float* out, uint32_t* xmax, cudaStream_t s);
+                            float eps, float* out, uint32_t* xmax, double* out_d, cudaStream_t s);
 
 }  // namespace vlb
