@@ -61,6 +61,7 @@ constexpr uint32_t kDcBarOff = kDcHdrOff + kDcRing * 16u;
 constexpr uint32_t kDcMiscOff = kDcBarOff + 64u;              // abort word, token scales
 constexpr uint32_t kDcXsOff = (kDcMiscOff + 64u + 127u) / 128u * 128u;
 constexpr uint64_t kDcWaitNs = 2000000000ull;
+constexpr uint32_t kDcSleepNs = 1000;  // suspend hint of one barrier test
 constexpr uint32_t kDcErrTimeout = 8u;
 constexpr uint32_t kDcEnd = 0xffffffffu;
 #ifndef VLB_DC_MAX_CHUNK
@@ -113,19 +114,17 @@ __device__ __forceinline__ void dc_stage_xs(unsigned char* xs, const float* cons
     }
 }
 
-// One bounded test loop on an mbarrier phase; false on abort or after the time limit.
+// One bounded wait on an mbarrier phase; false on abort or after the time limit. After a first
+// test the thread suspends in the barrier (woken when the phase completes) instead of spinning.
 __device__ __forceinline__ bool dc_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
-    uint64_t t0 = 0;
-    for (uint32_t i = 1;; ++i) {
-        if (tc::mbar_try(bar, parity)) return true;
-        if ((i & 63u) == 0) {
-            if (*abort) return false;
-            const uint64_t now = tc::global_ns();
-            if (t0 == 0) t0 = now;
-            else if (now - t0 > kDcWaitNs) return false;
-            if (i >= (1u << 30)) return false;
-        }
+    if (tc::mbar_try(bar, parity)) return true;
+    const uint64_t t0 = tc::global_ns();
+    for (uint32_t i = 1; i < (1u << 30); ++i) {
+        if (tc::mbar_try_sleep(bar, parity, kDcSleepNs)) return true;
+        if (*abort) return false;
+        if (tc::global_ns() - t0 > kDcWaitNs) return false;
     }
+    return false;
 }
 
 __device__ __forceinline__ void dc_fail(uint32_t* flags, volatile uint32_t* abort) {
@@ -329,8 +328,8 @@ __device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, floa
 
 // IQ2_XXS stage: one 256-column block of this warp's two slices (rows rt + gq and rt + gq + 8).
 __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
-                                             uint32_t gq, uint32_t q, uint32_t xrow, const uint4* tab,
-                                             uint32_t lane7, uint64_t* empty_bar, float (&acc)[2][4]) {
+                                             uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab_lane,
+                                             uint64_t* empty_bar, float (&acc)[2][4]) {
     uint4 ra[2], rb[2];
     float da[2], db[2];
     uint32_t sa[2], sb[2];
@@ -374,10 +373,10 @@ __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 uint32_t va[4], vb[4];
-                mma::decode_iq2_sub(tab, lane7, half ? ra[i].z : ra[i].x, half ? ra[i].w : ra[i].y, (uint32_t)sub,
-                                    kka[i], va);
-                mma::decode_iq2_sub(tab, lane7, half ? rb[i].z : rb[i].x, half ? rb[i].w : rb[i].y, (uint32_t)sub,
-                                    kkb[i], vb);
+                mma::decode_iq2_sub_lane(tab_lane, half ? ra[i].z : ra[i].x, half ? ra[i].w : ra[i].y,
+                                         (uint32_t)sub, kka[i], va);
+                mma::decode_iq2_sub_lane(tab_lane, half ? rb[i].z : rb[i].x, half ? rb[i].w : rb[i].y,
+                                         (uint32_t)sub, kkb[i], vb);
                 float (&A)[4] = (sub & 1) ? E[i] : D[i];
                 mma::mma16816(A, va[0], vb[0], va[1], vb[1], xb.x, xb.y);
                 mma::mma16816(A, va[2], vb[2], va[3], vb[3], xb.z, xb.w);
@@ -449,7 +448,6 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     uint64_t* empty = full + kDcRing;
     const uint32_t K = GATEUP ? p.H : p.I;
     unsigned char* xs = smem + kDcXsOff;
-    const uint4* tab = reinterpret_cast<const uint4*>(smem);
     mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
     for (uint32_t i = threadIdx.x; i < dc_xs_bytes(K) / 16u; i += blockDim.x)
         reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -475,6 +473,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     const uint32_t gq = lane >> 2, q = lane & 3u, n = lane >> 2, lane7 = lane & 7u;
     const uint4* hdr = reinterpret_cast<const uint4*>(smem + kDcHdrOff);
     const uint32_t xs_iq2_lane = tc::smem_u32(xs) + n * (K * 2u + 64u) + q * 16u;
+    const uint32_t tab_lane = tc::smem_u32(smem) + lane7 * 16u;  // this lane's table replica
     uint64_t* cbar = empty + kDcRing;
     uint32_t cphase = 0;
     uint32_t staged_unit = 0xffffffffu;
@@ -533,7 +532,7 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
         }
         const uint32_t st_addr = tc::smem_u32(smem + kDcRingOff + slot * kDcStage);
         if (it.iq2) {
-            dc_iq2_stage(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab, lane7, empty + slot, acc);
+            dc_iq2_stage(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
         } else {
             const uint32_t blk0 = 2u * h.y;
             const uint32_t nblk = blk0 + 1u < it.bpr ? 2u : 1u;
