@@ -318,7 +318,7 @@ def run_ep(args, dev, rank, world, local_rank):
     import torch
 
     from vastloom_b200 import synth
-    from vastloom_b200.ep import TorchComm, make_device_layer
+    from vastloom_b200.ep import TorchComm, balanced_slots, make_device_layer
 
     spec = synth.config(4)
     T = args.ep_tokens
@@ -336,7 +336,17 @@ def run_ep(args, dev, rank, world, local_rank):
                                 device_id=torch.device("cuda", local_rank))
         created_group = True
     comm = TorchComm()
-    layer, ops = make_device_layer(dev, W, comm, max_tokens=T)
+    # expert placement balanced by the measured load: every rank routes its own batch once, the
+    # per-expert counts are summed over the ranks, and every rank computes the same placement
+    idx0, _ = dev.route(logits_host, spec.top_k, spec.route_scale, score=spec.score, bias=W.bias)
+    counts = torch.from_numpy(np.bincount(idx0.ravel(), minlength=spec.experts).astype(np.float64)).cuda()
+    torch.distributed.all_reduce(counts)
+    slots = balanced_slots(counts.cpu().numpy(), world)
+    epr = spec.experts // world
+    load_contig = counts.cpu().numpy().reshape(world, epr).sum(axis=1)
+    load_bal = np.zeros(world)
+    np.add.at(load_bal, slots // epr, counts.cpu().numpy())
+    layer, ops = make_device_layer(dev, W, comm, max_tokens=T, slots=slots)
     xd = torch.from_numpy(x_host).cuda()
     ld = torch.from_numpy(logits_host).cuda()
     for _ in range(args.warmup):
@@ -373,8 +383,12 @@ def run_ep(args, dev, rank, world, local_rank):
         "config": {"workload": f"cfg4-ep-zipf-T{T}x{world}", "hidden": spec.hidden,
                    "intermediate": spec.intermediate, "experts": spec.experts, "experts_per_gpu": spec.experts // world,
                    "top_k": spec.top_k, "tokens_per_gpu": T, "zipf_s": spec.zipf_s,
-                   "exchange": "NCCL all-to-all: fp16 rows + (expert, weight, max|x|) words out, f32 results back",
+                   "exchange": "NCCL all-to-all: fp16 rows + (expert, weight, max|x|) words out, fp16 results "
+                               "with a per-row power-of-two scale back",
+                   "placement": "balanced by the measured expert load (longest-processing-time greedy, E/N per GPU)",
                    "expert_path": "tensor-core prefill kernels on the received rows"},
+        "expected_rows_per_rank": {"contiguous_max": int(load_contig.max()), "balanced_max": int(load_bal.max()),
+                                   "mean": int(load_bal.mean())},
         "timing": "CUDA events on the library stream around each step, max over ranks",
         "load_imbalance": {"experts_ms_max": round(ex_max, 4), "experts_ms_min": round(ex_min, 4),
                            "imbalance_ms": round(ex_max - ex_min, 4), "received_rows_max": int(recv_max),

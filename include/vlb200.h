@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define VLB_ABI_VERSION 1
+#define VLB_ABI_VERSION 2
 
 /* Status codes: 0 = success; 1..10 = vastloom::ErrorCode + 1 (status.hpp:10-21). */
 enum {
@@ -270,12 +270,28 @@ int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx_dev, const float* weig
  * [T*k x H] in plan order, send_meta_dev u32 [T*k x 3] = (local expert id, route weight bits,
  * token max|x| bits), and the rank's own tokens for its shared expert, own_rows_dev fp16 [T x H]
  * with own_meta_dev [T x 3] = (experts_per_rank, 1.0f bits, max|x| bits): the inputs of
- * vlb_layer_forward_rows_half_device on the receiving rank. H % 8 == 0. */
+ * vlb_layer_forward_rows_half_device on the receiving rank. H % 8 == 0. expert_slot_dev (u32 [E],
+ * NULL = identity) places the experts on the ranks: expert e is local expert slot % epr of rank
+ * slot / epr, slot = expert_slot_dev[e], a permutation of [0, E) - a placement balanced by expert
+ * load instead of contiguous ranges. The pairs are ordered by slot (expert order within a rank)
+ * and offsets are per slot. An expert id >= E returns VLB_ERR_INVALID_FORMAT. One host
+ * synchronisation (the offsets size the exchange). */
 int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx_dev, const float* weights_dev, uint32_t T,
-                            uint32_t k, uint32_t E, uint32_t experts_per_rank, const float* x_dev, uint32_t H,
-                            void* ws_dev, uint32_t* offsets_dev, uint32_t* offsets_host,
-                            uint16_t* send_rows_dev, uint32_t* send_meta_dev, uint32_t* elem_row_dev,
-                            uint16_t* own_rows_dev, uint32_t* own_meta_dev, void* stream);
+                            uint32_t k, uint32_t E, uint32_t experts_per_rank, const uint32_t* expert_slot_dev,
+                            const float* x_dev, uint32_t H, void* ws_dev, uint32_t* offsets_dev,
+                            uint32_t* offsets_host, uint16_t* send_rows_dev, uint32_t* send_meta_dev,
+                            uint32_t* elem_row_dev, uint16_t* own_rows_dev, uint32_t* own_meta_dev, void* stream);
+/* Expert outputs as fp16 rows for the return exchange: half_rows_dev [rows x H] = fp16(y * 2^e_r),
+ * 2^e_r the power of two bringing row r's max|y| into [2^14, 2^15), row_scale_dev[r] = 2^-e_r.
+ * Half the bytes of the f32 rows; each element keeps 11 significant bits. H % 8 == 0. */
+int vlb_ep_pack_half_device(vlb_handle* h, const float* y_rows_dev, uint32_t rows, uint32_t H,
+                            uint16_t* half_rows_dev, float* row_scale_dev, void* stream);
+/* vlb_ep_combine_device on returned half rows: out[t] = sum over its k slots of
+ * half_rows_dev[elem_row] * row_scale_dev[elem_row] (slot order) + shared_rows_dev[t] (f32; NULL:
+ * none). */
+int vlb_ep_combine_half_device(vlb_handle* h, const uint16_t* half_rows_dev, const float* row_scale_dev,
+                               const uint32_t* elem_row_dev, uint32_t T, uint32_t k, const float* shared_rows_dev,
+                               uint32_t H, float* out_dev, void* stream);
 /* Combine on the source rank after the return exchange: out[t] = sum over its k slots of
  * y_rows_dev[elem_row_dev[t * k + slot]] (slot order) + shared_rows_dev[t] (NULL: none). */
 int vlb_ep_combine_device(vlb_handle* h, const float* y_rows_dev, const uint32_t* elem_row_dev,

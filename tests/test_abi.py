@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_mapping():
     lib = vb.load_library()
-    assert lib.vlb_abi_version() == 1
+    assert lib.vlb_abi_version() == 2
     # ErrorCode order of include/vastloom/core/status.hpp:10-21, shifted by one
     assert [vb.ERROR_CODES[i] for i in range(1, 11)] == [
         "invalid_argument", "invalid_format", "not_found", "permission_denied", "io_error",

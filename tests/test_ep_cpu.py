@@ -272,3 +272,29 @@ def test_ep_failed_rank_ends_the_step_with_an_error(grids, mode, phase):
     assert outcome == ("EpExchangeError", phase), outcome
     assert elapsed < 60.0, elapsed
     assert again[:2] == ("EpExchangeError", phase) and again[2] < 1.0, again
+
+
+@pytest.mark.parametrize("zipf", [0.6, 1.1])
+def test_balanced_slots_is_a_balanced_permutation(zipf):
+    """LPT placement: a permutation of the expert ids, E / world experts per rank, Zipf loads
+    spread within a few percent of the mean when no expert outweighs a rank's share, and the
+    heaviest rank no heavier than the heaviest expert plus the lightest others when one does;
+    always better than contiguous ranges."""
+    from vastloom_b200.ep import balanced_slots
+
+    E, world = 256, 8
+    epr = E // world
+    ranks = np.random.default_rng(3).permutation(E) + 1
+    loads = ranks.astype(np.float64) ** -zipf * 1e6
+    slots = balanced_slots(loads, world)
+    assert sorted(slots.tolist()) == list(range(E))
+    assert np.bincount(slots // epr, minlength=world).tolist() == [epr] * world
+    per_rank = np.zeros(world)
+    for e in range(E):
+        per_rank[slots[e] // epr] += loads[e]
+    mean = per_rank.mean()
+    bound = max(1.05 * mean, loads.max() + np.sort(loads)[:epr - 1].sum())
+    assert per_rank.max() <= bound * (1 + 1e-12)
+    contiguous = loads.reshape(world, -1).sum(axis=1)
+    assert contiguous.max() > per_rank.max()
+    assert np.array_equal(slots, balanced_slots(loads, world))  # deterministic

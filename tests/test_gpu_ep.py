@@ -47,7 +47,15 @@ def _rank_main(rank, world, port, args, q):
         x, _, logits = synth.activations(spec, T, seed=args["seed"] + 1 + rank)
         dev = vb.Device(rank)
         comm = TorchComm()
-        layer, ops = make_device_layer(dev, W, comm, max_tokens=T)
+        slots = None
+        if args.get("balanced"):
+            # one placement on every rank: loads from rank 0's batch (top-k of its logits)
+            from vastloom_b200.ep import balanced_slots
+
+            _, _, lg0 = synth.activations(spec, T, seed=args["seed"] + 1)
+            top = np.argsort(-lg0, axis=1, kind="stable")[:, :spec.top_k]
+            slots = balanced_slots(np.bincount(top.ravel(), minlength=spec.experts), world)
+        layer, ops = make_device_layer(dev, W, comm, max_tokens=T, slots=slots)
         xd = torch.from_numpy(x).cuda()
         ld = torch.from_numpy(logits).cuda()
         out = layer.forward(xd, ld, T).cpu().numpy()
@@ -92,9 +100,17 @@ def test_gpu_ep_single_rank_matches_single_gpu_layer(scale, T):
     assert deterministic
 
 
+def test_gpu_ep_single_rank_balanced_placement():
+    """A balanced placement permutes the local expert order; the result is the same layer."""
+    res = _run(1, {"scale": "full", "T": 1024, "seed": 402, "balanced": True})
+    rank, rel, deterministic, received, sent = res[0]
+    assert received == sent and rel <= EXPECTED and deterministic
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_gpu_ep_two_ranks_match_single_gpu_layer():
-    res = _run(2, {"scale": "full", "T": 1024, "seed": 401})
+@pytest.mark.parametrize("balanced", [False, True])
+def test_gpu_ep_two_ranks_match_single_gpu_layer(balanced):
+    res = _run(2, {"scale": "full", "T": 1024, "seed": 401, "balanced": balanced})
     assert sum(r[3] for r in res) == sum(r[4] for r in res)
     for rank, rel, deterministic, received, sent in res:
         assert rel <= EXPECTED, (rank, rel)

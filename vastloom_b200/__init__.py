@@ -139,7 +139,7 @@ EXPORTS = (
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
     "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_layer_set_prefill_tokens "
     "vlb_layer_prefill_tokens vlb_layer_set_input_norm vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
-    "vlb_ep_plan_device vlb_ep_plan_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
+    "vlb_ep_plan_device vlb_ep_plan_half_device vlb_ep_pack_half_device vlb_ep_combine_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
 ).split()
 
 
@@ -191,7 +191,9 @@ def load_library() -> C.CDLL:
         "vlb_ep_workspace_bytes": (SZ, [U32, U32, U32]),
         "vlb_ep_plan_device": (I, [P, P, P, U32, U32, U32, U32, P, U32, P, P, P, P, P, P, P, P]),
         "vlb_ep_combine_device": (I, [P, P, P, U32, U32, P, U32, P, P]),
-        "vlb_ep_plan_half_device": (I, [P, P, P, U32, U32, U32, U32, P, U32, P, P, P, P, P, P, P, P, P]),
+        "vlb_ep_plan_half_device": (I, [P, P, P, U32, U32, U32, U32, P, P, U32, P, P, P, P, P, P, P, P, P]),
+        "vlb_ep_pack_half_device": (I, [P, P, U32, U32, P, P, P]),
+        "vlb_ep_combine_half_device": (I, [P, P, P, P, U32, U32, P, U32, P, P]),
         "vlb_layer_forward_rows_half_device": (I, [P, P, P, P, U32, P, P]),
         "vlb_layer_prefill_tokens": (U32, [P, P]),
         "vlb_route_device": (I, [P, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),

@@ -1099,7 +1099,7 @@ static size_t ep_round(size_t b) { return (b + 255) / 256 * 256; }
 
 size_t vlb_ep_workspace_bytes(uint32_t T, uint32_t k, uint32_t E) {
     const size_t n = (size_t)T * k, chunks = (n + 1023) / 1024;
-    return 256 + 3 * ep_round(n * 4) + ep_round(chunks * E * 4) + ep_round((size_t)T * 4);
+    return 256 + 4 * ep_round(n * 4) + ep_round(chunks * E * 4) + ep_round((size_t)T * 4);
 }
 
 int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx, const float* weights, uint32_t T, uint32_t k,
@@ -1148,9 +1148,10 @@ int vlb_ep_plan_device(vlb_handle* h, const uint32_t* idx, const float* weights,
 }
 
 int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx, const float* weights, uint32_t T, uint32_t k,
-                            uint32_t E, uint32_t experts_per_rank, const float* x, uint32_t H, void* ws,
-                            uint32_t* offsets, uint32_t* offsets_host, uint16_t* send_rows, uint32_t* send_meta,
-                            uint32_t* elem_row, uint16_t* own_rows, uint32_t* own_meta, void* stream) {
+                            uint32_t E, uint32_t experts_per_rank, const uint32_t* expert_slot, const float* x,
+                            uint32_t H, void* ws, uint32_t* offsets, uint32_t* offsets_host, uint16_t* send_rows,
+                            uint32_t* send_meta, uint32_t* elem_row, uint16_t* own_rows, uint32_t* own_meta,
+                            void* stream) {
     VLB_LOCK(h);
     if (!idx || !weights || !x || !ws || !offsets || !offsets_host || !send_rows || !send_meta || !elem_row ||
         !own_rows || !own_meta || k == 0 || E == 0 || E > 512 || H == 0 || H % 8 || experts_per_rank == 0 ||
@@ -1165,19 +1166,19 @@ int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx, const float* wei
     uint32_t* counts = reinterpret_cast<uint32_t*>(w + 256 + 2 * ep_round(n * 4));
     float* sorted_w = reinterpret_cast<float*>(w + 256 + 2 * ep_round(n * 4) + ep_round(chunks * E * 4));
     uint32_t* xmax = reinterpret_cast<uint32_t*>(w + 256 + 3 * ep_round(n * 4) + ep_round(chunks * E * 4));
-    // expert ids are validated before the counting sort indexes anything with them
-    uint32_t bad = 0;
+    uint32_t* slots = reinterpret_cast<uint32_t*>(w + 256 + 3 * ep_round(n * 4) + ep_round(chunks * E * 4) +
+                                                  ep_round((size_t)T * 4));
+    // routes -> exchange slots (an out-of-range id is flagged and made harmless), then the stable
+    // sort by slot = by destination rank; one host synchronisation at the end reads the offsets that
+    // size the exchange, and the flag
     VLB_CUDA(h, cudaMemsetAsync(flag, 0, 4, s));
-    VLB_CUDA(h, launch_ep_validate(idx, n, E, flag, s));
-    VLB_CUDA(h, cudaMemcpyAsync(&bad, flag, 4, cudaMemcpyDeviceToHost, s));
-    VLB_CUDA(h, cudaStreamSynchronize(s));
-    if (bad) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
+    VLB_CUDA(h, launch_ep_slots(idx, n, E, expert_slot, slots, flag, s));
     VLB_CUDA(h, launch_prescale(x, T, H, xmax, nullptr, s));
     MoeParams p{};
     p.T = T;
     p.k = k;
     p.E = E;
-    p.idx = const_cast<uint32_t*>(idx);
+    p.idx = slots;
     p.weights = const_cast<float*>(weights);
     p.offsets = offsets;
     p.pair_token = pair_token;
@@ -1187,13 +1188,36 @@ int vlb_ep_plan_half_device(vlb_handle* h, const uint32_t* idx, const float* wei
     p.disp_counts = counts;
     p.has_shared = 0;
     VLB_CUDA(h, launch_stable_sort(p, s));
-    VLB_CUDA(h, launch_ep_gather_half(pair_token, pair_slot, idx, sorted_w, (uint32_t)n, k, experts_per_rank, x,
+    VLB_CUDA(h, launch_ep_gather_half(pair_token, pair_slot, slots, sorted_w, (uint32_t)n, k, experts_per_rank, x,
                                       xmax, H, reinterpret_cast<__half*>(send_rows), send_meta, s));
     VLB_CUDA(h, launch_ep_own_rows(x, xmax, T, H, experts_per_rank, reinterpret_cast<__half*>(own_rows), own_meta,
                                    s));
     if (n == 0) VLB_CUDA(h, cudaMemsetAsync(offsets, 0, (E + 2) * 4, s));
+    uint32_t bad = 0;
     VLB_CUDA(h, cudaMemcpyAsync(offsets_host, offsets, (E + 1) * 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaMemcpyAsync(&bad, flag, 4, cudaMemcpyDeviceToHost, s));
     VLB_CUDA(h, cudaStreamSynchronize(s));
+    if (bad) return h->fail(VLB_ERR_INVALID_FORMAT, "a route selects an out-of-range expert");
+    return VLB_OK;
+}
+
+int vlb_ep_pack_half_device(vlb_handle* h, const float* y_rows, uint32_t rows, uint32_t H, uint16_t* half_rows,
+                            float* row_scale, void* stream) {
+    VLB_LOCK(h);
+    if ((rows && (!y_rows || !half_rows || !row_scale)) || H == 0 || H % 8)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid expert-parallel pack argument");
+    VLB_CUDA(h, launch_ep_pack_half(y_rows, rows, H, reinterpret_cast<__half*>(half_rows), row_scale, h->pick(stream)));
+    return VLB_OK;
+}
+
+int vlb_ep_combine_half_device(vlb_handle* h, const uint16_t* half_rows, const float* row_scale,
+                               const uint32_t* elem_row, uint32_t T, uint32_t k, const float* shared_rows, uint32_t H,
+                               float* out, void* stream) {
+    VLB_LOCK(h);
+    if (!half_rows || !row_scale || !elem_row || !out || H == 0 || H % 4)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid expert-parallel combine argument");
+    VLB_CUDA(h, launch_ep_combine_half(reinterpret_cast<const __half*>(half_rows), row_scale, elem_row, T, k,
+                                       shared_rows, H, out, h->pick(stream)));
     return VLB_OK;
 }
 

@@ -126,20 +126,28 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
 // values is exact in f64, so fma(x, w, s) rounds exactly like s + x * w, and a thread that walks
 // the columns in order reproduces the reference's logit bit for bit. That order is the whole cost:
 // each logit is a chain of H dependent f64 additions, so the kernel is latency-bound (H times the
-// 8-cycle DFMA latency) and is built to keep every chain fed:
+// 8-cycle DFMA latency) and, with many tokens, by the FP64 pipe (measured on B200: about 8 DFMA
+// per clock per SM). It is built to keep every chain fed:
 //   * the operands arrive already widened to f64 (the layer keeps its router weights as f64; the
 //     activations are widened by the entry step): an f32 -> f64 conversion per use would cost
 //     more issue time than the DFMA chain itself;
-//   * a CTA computes a tile of 32 experts (the lanes) x 4 tokens (the warps); 32-column slices of
-//     the tile's weights and activations stream into a 4-stage shared-memory ring with cp.async
-//     (three slices in flight while the chains consume the fourth), and each slice's steps are
-//     unrolled so that the shared-memory loads run ahead of the dependent DFMAs.
+//   * a CTA computes a tile of 32 experts (the lanes) x 4 warps x kRtChains tokens; 128-column
+//     slices of the tile's weights and activations stream into a 4-stage shared-memory ring with
+//     cp.async: three slices (about 1.9 us of chain steps) in flight, more than the memory latency,
+//     so the chains do not wait for their operands;
+//   * warps whose tokens are all past T skip the chain (they only help stage), which leaves the
+//     SM's FP64 pipe to the chains that count.
+#ifndef VLB_RT_CHAINS
+#define VLB_RT_CHAINS 1
+#endif
 constexpr uint32_t kRtExperts = 32;
-constexpr uint32_t kRtTokens = 4;
-constexpr uint32_t kRtCols = 32;
+constexpr uint32_t kRtWarps = 4;
+constexpr uint32_t kRtChains = VLB_RT_CHAINS;          // tokens per warp: independent chains per thread
+constexpr uint32_t kRtTokens = kRtWarps * kRtChains;  // tokens per CTA
+constexpr uint32_t kRtCols = 128;
 constexpr uint32_t kRtStages = 4;
 constexpr uint32_t kRtWStride = kRtCols + 2;  // doubles per staged weight row: a 16-byte phase shift per row
-constexpr uint32_t kRtThreads = kRtExperts * kRtTokens;
+constexpr uint32_t kRtThreads = kRtExperts * kRtWarps;
 constexpr uint32_t kRtStageDoubles = kRtExperts * kRtWStride + kRtTokens * kRtCols;
 constexpr size_t kRtSmemBytes = (size_t)kRtStages * kRtStageDoubles * 8u;
 
@@ -160,6 +168,12 @@ __device__ __forceinline__ float score_dev(int score, float logit) {
     return logit;  // the softmax routers work on the logits themselves
 }
 
+__device__ __forceinline__ double2 lds_f64x2(uint32_t addr) {
+    double2 v;
+    asm("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(addr));
+    return v;
+}
+
 // wd: f64 router weights [E x H]; xd: f64 activations [T x H]; H % 2 == 0.
 __global__ void __launch_bounds__(kRtThreads) router_kernel(const double* __restrict__ wd,
                                                             const double* __restrict__ xd, uint32_t T,
@@ -170,8 +184,8 @@ __global__ void __launch_bounds__(kRtThreads) router_kernel(const double* __rest
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t e0 = blockIdx.x * kRtExperts, t0 = blockIdx.y * kRtTokens;
     const uint32_t slices = (H + kRtCols - 1u) / kRtCols;
-    // slice `sl` into stage sl % kRtStages: 512 weight double2s (4 per thread) and 64 activation
-    // double2s (threads 0..63); rows past E / T and columns past H are zero-filled
+    // slice `sl` into stage sl % kRtStages: the weight tile's double2s and the token rows' double2s,
+    // spread over the threads; rows past E / T and columns past H are zero-filled
     auto issue = [&](uint32_t sl) {
         double* st = ring + (sl % kRtStages) * kRtStageDoubles;
         const uint32_t c0 = sl * kRtCols;
@@ -182,8 +196,11 @@ __global__ void __launch_bounds__(kRtThreads) router_kernel(const double* __rest
             const bool ok = e0 + r < E && c0 + c < H;
             tc::cp_async16(st + r * kRtWStride + c, ok ? wd + (size_t)(e0 + r) * H + c0 + c : wd, ok ? 16u : 0u);
         }
-        if (threadIdx.x < kRtTokens * kRtCols / 2u) {
-            const uint32_t r = threadIdx.x / (kRtCols / 2u), c = (threadIdx.x % (kRtCols / 2u)) * 2u;
+#pragma unroll
+        for (uint32_t i = 0; i < (kRtTokens * kRtCols / 2u + kRtThreads - 1u) / kRtThreads; ++i) {
+            const uint32_t f = threadIdx.x + i * kRtThreads;
+            if (f >= kRtTokens * kRtCols / 2u) break;
+            const uint32_t r = f / (kRtCols / 2u), c = (f % (kRtCols / 2u)) * 2u;
             const bool ok = t0 + r < T && c0 + c < H;
             tc::cp_async16(st + kRtExperts * kRtWStride + r * kRtCols + c, ok ? xd + (size_t)(t0 + r) * H + c0 + c : xd,
                            ok ? 16u : 0u);
@@ -193,39 +210,53 @@ __global__ void __launch_bounds__(kRtThreads) router_kernel(const double* __rest
         if (sl < slices) issue(sl);
         tc::cp_async_commit();  // (an empty group past the last slice keeps the count uniform)
     }
-    double acc = 0.0;
+    double acc[kRtChains];
+#pragma unroll
+    for (uint32_t h = 0; h < kRtChains; ++h) acc[h] = 0.0;
+    const uint32_t ring_a = tc::smem_u32(ring);
     for (uint32_t sl = 0; sl < slices; ++sl) {
         asm volatile("cp.async.wait_group %0;" ::"n"(kRtStages - 2u) : "memory");  // slice sl has landed
         __syncthreads();  // ... for every thread; and every thread is done with slice sl - 1's stage
         if (sl + kRtStages - 1u < slices) issue(sl + kRtStages - 1u);
         tc::cp_async_commit();
-        const double* st = ring + (sl % kRtStages) * kRtStageDoubles;
-        const double* wr = st + lane * kRtWStride;
-        const double* xr = st + kRtExperts * kRtWStride + warp * kRtCols;
+        const uint32_t st = ring_a + (sl % kRtStages) * kRtStageDoubles * 8u;
+        const uint32_t wa = st + lane * kRtWStride * 8u;
+        const uint32_t xa = st + (kRtExperts * kRtWStride + warp * kRtChains * kRtCols) * 8u;
         const uint32_t n = H - sl * kRtCols;  // even (H % 2 == 0)
+        if (t0 + warp * kRtChains >= T) continue;  // no valid token in this warp: keep the FP64 pipe free
         if (n >= kRtCols) {
 #pragma unroll
             for (uint32_t c = 0; c < kRtCols; c += 2u) {
-                const double2 wv = *reinterpret_cast<const double2*>(wr + c);
-                const double2 xv = *reinterpret_cast<const double2*>(xr + c);
-                acc = __fma_rn(xv.x, wv.x, acc);
-                acc = __fma_rn(xv.y, wv.y, acc);
+                const double2 wv = lds_f64x2(wa + 8u * c);
+#pragma unroll
+                for (uint32_t h = 0; h < kRtChains; ++h) {
+                    const double2 xv = lds_f64x2(xa + 8u * (h * kRtCols + c));
+                    acc[h] = __fma_rn(xv.x, wv.x, acc[h]);
+                    acc[h] = __fma_rn(xv.y, wv.y, acc[h]);
+                }
             }
         } else {
             for (uint32_t c = 0; c < n; c += 2u) {
-                const double2 wv = *reinterpret_cast<const double2*>(wr + c);
-                const double2 xv = *reinterpret_cast<const double2*>(xr + c);
-                acc = __fma_rn(xv.x, wv.x, acc);
-                acc = __fma_rn(xv.y, wv.y, acc);
+                const double2 wv = lds_f64x2(wa + 8u * c);
+#pragma unroll
+                for (uint32_t h = 0; h < kRtChains; ++h) {
+                    const double2 xv = lds_f64x2(xa + 8u * (h * kRtCols + c));
+                    acc[h] = __fma_rn(xv.x, wv.x, acc[h]);
+                    acc[h] = __fma_rn(xv.y, wv.y, acc[h]);
+                }
             }
         }
     }
     tc::cp_async_wait_all();
-    const uint32_t e = e0 + lane, t = t0 + warp;
-    if (e < E && t < T) {
-        const float lg = (float)acc;
-        logits[(size_t)t * E + e] = lg;
-        scores[(size_t)t * E + e] = score_dev(score, lg);
+    const uint32_t e = e0 + lane;
+#pragma unroll
+    for (uint32_t h = 0; h < kRtChains; ++h) {
+        const uint32_t t = t0 + warp * kRtChains + h;
+        if (e < E && t < T) {
+            const float lg = (float)acc[h];
+            logits[(size_t)t * E + e] = lg;
+            scores[(size_t)t * E + e] = score_dev(score, lg);
+        }
     }
 }
 

@@ -43,6 +43,13 @@ cudaError_t launch_decode_gateup(const MoeParams& p, unsigned n_sms, cudaStream_
 cudaError_t launch_decode_down(const MoeParams& p, unsigned n_sms, cudaStream_t s);
 // Expert-parallel helpers (vlb_ep.cu)
 cudaError_t launch_ep_validate(const uint32_t* idx, size_t n, uint32_t E, uint32_t* flag, cudaStream_t s);
+// expert ids -> exchange slots (slot_of null: identity); out-of-range ids flagged and replaced by 0
+cudaError_t launch_ep_slots(const uint32_t* idx, size_t n, uint32_t E, const uint32_t* slot_of, uint32_t* out,
+                            uint32_t* flag, cudaStream_t s);
+// f32 rows -> fp16 rows with a per-row power-of-two scale (scale[r] = the inverse factor)
+cudaError_t launch_ep_pack_half(const float* y, uint32_t rows, uint32_t H, __half* out, float* scale, cudaStream_t s);
+cudaError_t launch_ep_combine_half(const __half* rows, const float* scale, const uint32_t* elem_row, uint32_t T,
+                                   uint32_t k, const float* shared_rows, uint32_t H, float* out, cudaStream_t s);
 cudaError_t launch_ep_gather(const uint32_t* pair_token, const uint32_t* pair_slot, const uint32_t* idx,
                              uint32_t n, uint32_t k, uint32_t epr, const float* x, uint32_t H, float* send_x,
                              uint32_t* send_expert, cudaStream_t s);

@@ -1,7 +1,8 @@
 """Expert parallelism for the MoE layer (benchmark configuration 4): the routed experts are
-sharded in contiguous ranges over the ranks of a process group, every rank routes its own tokens,
-sends each (token, slot) pair's activation row to the rank that owns the expert (all-to-all),
-computes the pairs it received on its expert shard, and sends the results back for the combine.
+sharded over the ranks of a process group (contiguous ranges of ids, or a placement balanced by
+expert load), every rank routes its own tokens, sends each (token, slot) pair's activation row to
+the rank that owns the expert (all-to-all), computes the pairs it received on its expert shard,
+and sends the results back for the combine.
 
 The layer math is the reference's (moe_forward, deepseek_v4_graph.cpp:1902-2274): route weights
 are applied before the down product, each token's pairs are summed and the shared expert's row is
@@ -40,6 +41,29 @@ class EpExchangeError(RuntimeError):
     def __init__(self, phase: str, cause: BaseException):
         super().__init__(f"expert-parallel {phase} exchange failed: {cause}")
         self.phase = phase
+
+
+def balanced_slots(loads, world: int) -> np.ndarray:
+    """Expert placement balanced by load: slot[e] for every expert (rank slot // epr, local expert
+    slot % epr), experts_per_rank = E / world experts on every rank. Longest-processing-time
+    greedy: experts by load, heaviest first (ties to the lower id), each to the least-loaded rank
+    that still has room (ties to the lower rank); within a rank in assignment order. Every rank
+    computes the same placement from the same loads."""
+    loads = np.asarray(loads, dtype=np.float64)
+    E = loads.size
+    if E % world:
+        raise ValueError("experts must divide evenly over the ranks")
+    epr = E // world
+    order = sorted(range(E), key=lambda e: (-loads[e], e))
+    rank_load = [0.0] * world
+    fill = [0] * world
+    slot = np.empty(E, np.uint32)
+    for e in order:
+        r = min((r for r in range(world) if fill[r] < epr), key=lambda r: (rank_load[r], r))
+        slot[e] = r * epr + fill[r]
+        fill[r] += 1
+        rank_load[r] += loads[e]
+    return slot
 
 
 def owner_counts(offsets_host: np.ndarray, world: int, experts_per_rank: int) -> list:
@@ -93,8 +117,10 @@ class EpBuffers:
     group_rows: object  # [capacity, H] received rows, then this rank's own rows for the shared expert
     group_meta: object  # [capacity, 3]
     group_y: object     # [capacity, H] f32 expert outputs of the group rows
-    back_y: object      # [T*k, H] f32 results returned to this rank, in send order
+    back_y: object      # [T*k, H] results returned to this rank, in send order (the ops' format)
     out: object         # [T, H] f32
+    group_ys: object = None  # [capacity] per-row scales of packed return rows (ops with pack_return)
+    back_ys: object = None   # [T*k] their returned copies
 
 
 class ExpertParallelLayer:
@@ -114,10 +140,13 @@ class ExpertParallelLayer:
         self.epr = experts // comm.world
         self.max_tokens = max_tokens
         n = max_tokens * top_k
+        # ops with pack_return send the expert outputs back in their own (smaller) row format
+        self.packed = hasattr(ops, "pack_return")
         self.buf = EpBuffers(
             send_rows=ops.empty((n, hidden), "rows"), send_meta=ops.empty((n, 3), "meta"),
             elem_row=ops.empty((n,), "i32"), group_rows=None, group_meta=None, group_y=None,
-            back_y=ops.empty((n, hidden), "f32"), out=ops.empty((max_tokens, hidden), "f32"))
+            back_y=ops.empty((n, hidden), "rows" if self.packed else "f32"), out=ops.empty((max_tokens, hidden), "f32"),
+            back_ys=ops.empty((n,), "f32") if self.packed else None)
         self.capacity = 0  # group rows the receive side is sized for (grown on demand)
         self._marks = None
         self._rows = (0, 0)
@@ -144,6 +173,9 @@ class ExpertParallelLayer:
         b.group_rows = ops.empty((cap, self.H), "rows")
         b.group_meta = ops.empty((cap, 3), "meta")
         b.group_y = ops.empty((cap, self.H), "f32")
+        if self.packed:
+            b.group_yh = ops.empty((cap, self.H), "rows")
+            b.group_ys = ops.empty((cap,), "f32")
         ops.reserve_group(cap)
         self.capacity = cap
 
@@ -174,7 +206,16 @@ class ExpertParallelLayer:
         m2 = ops.mark()
         ops.group_forward(b, R + T)
         m3 = ops.mark()
-        self._exchange("return", lambda: comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts))
+        if self.packed:
+            ops.pack_return(b, R)
+
+            def ret():
+                comm.all_to_all(b.back_y[:n], b.group_yh[:R], send_counts, recv_counts)
+                comm.all_to_all(b.back_ys[:n], b.group_ys[:R], send_counts, recv_counts)
+
+            self._exchange("return", ret)
+        else:
+            self._exchange("return", lambda: comm.all_to_all(b.back_y[:n], b.group_y[:R], send_counts, recv_counts))
         m4 = ops.mark()
         out = ops.combine(b, T, k, R)
         m5 = ops.mark()
@@ -201,7 +242,7 @@ class DeviceEpOps:
     the shared expert as local expert `experts_per_rank`."""
 
     def __init__(self, dev, group_mats, spec, bias, score: int, route_scale: float, experts: int, top_k: int,
-                 hidden: int, max_tokens: int):
+                 hidden: int, max_tokens: int, slots: Optional[np.ndarray] = None):
         import torch
 
         self.torch = torch
@@ -218,6 +259,8 @@ class DeviceEpOps:
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.stream = torch.cuda.ExternalStream(dev.stream, device=self.device)
         self.bias = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias, np.float32)).to(self.device)
+        self.slots = None if slots is None else torch.from_numpy(
+            np.ascontiguousarray(slots, np.uint32).view(np.int32)).to(self.device)
         n = max_tokens * top_k
         self.idx = torch.empty((n,), dtype=torch.int32, device=self.device)
         self.w = torch.empty((n,), dtype=torch.float32, device=self.device)
@@ -287,7 +330,8 @@ class DeviceEpOps:
 
     def plan(self, idx, w, x, T, epr, b):
         self.dev._check(self.lib.vlb_ep_plan_half_device(
-            self.dev.h, self._p(idx), self._p(w), T, self.k, self.E, epr, self._p(x), self.H, self._p(self.ws),
+            self.dev.h, self._p(idx), self._p(w), T, self.k, self.E, epr,
+            None if self.slots is None else self._p(self.slots), self._p(x), self.H, self._p(self.ws),
             self._p(self.offsets), self.offsets_host.ctypes.data_as(C.c_void_p), self._p(b.send_rows),
             self._p(b.send_meta), self._p(b.elem_row), self._p(self.own_rows), self._p(self.own_meta),
             C.c_void_p(self.dev.stream)))
@@ -302,26 +346,38 @@ class DeviceEpOps:
         self.group.forward_rows_half_device(b.group_rows.data_ptr(), b.group_meta.data_ptr(), rows,
                                             b.group_y.data_ptr(), stream=self.dev.stream)
 
+    def pack_return(self, b, R):
+        """The received pairs' outputs as fp16 rows with a power-of-two scale per row: half the
+        bytes of the f32 rows on the return exchange (11 significant bits, like the operands)."""
+        self.dev._check(self.lib.vlb_ep_pack_half_device(
+            self.dev.h, self._p(b.group_y), R, self.H, self._p(b.group_yh), self._p(b.group_ys),
+            C.c_void_p(self.dev.stream)))
+
     def combine(self, b, T, k, R):
-        self.dev._check(self.lib.vlb_ep_combine_device(
-            self.dev.h, self._p(b.back_y), self._p(b.elem_row), T, k, self._p(b.group_y[R:R + T]), self.H,
-            self._p(b.out), C.c_void_p(self.dev.stream)))
+        self.dev._check(self.lib.vlb_ep_combine_half_device(
+            self.dev.h, self._p(b.back_y), self._p(b.back_ys), self._p(b.elem_row), T, k,
+            self._p(b.group_y[R:R + T]), self.H, self._p(b.out), C.c_void_p(self.dev.stream)))
         return b.out[:T]
 
 
-def upload_group(dev, W, rank: int, world: int, layer_index: int = 0) -> dict:
-    """This rank's expert group matrices: routed experts [rank * E/world, (rank + 1) * E/world)
-    plus the shared expert as local expert E/world (w1 / w3 / w2 lists)."""
+def upload_group(dev, W, rank: int, world: int, layer_index: int = 0, slots: Optional[np.ndarray] = None) -> dict:
+    """This rank's expert group matrices: the routed experts placed on it (slots [rank * E/world,
+    (rank + 1) * E/world) in slot order; without slots the contiguous range of ids) plus the shared
+    expert as local expert E/world (w1 / w3 / w2 lists)."""
     spec = W.spec
     E, H, I = spec.experts, spec.hidden, spec.intermediate
     epr = E // world
-    lo = rank * epr
+    if slots is None:
+        local = list(range(rank * epr, (rank + 1) * epr))
+    else:
+        by_slot = np.argsort(np.asarray(slots, np.int64))
+        local = [int(e) for e in by_slot[rank * epr:(rank + 1) * epr]]
 
     def ident(e, role):
         return ((layer_index * 1_000_003 + e) * 4 + role) * 2 + 1
 
     mats = {"w1": [], "w3": [], "w2": []}
-    for e in range(lo, lo + epr):
+    for e in local:
         for role, (name, rows, cols) in enumerate((("w1", I, H), ("w3", I, H), ("w2", H, I))):
             t, blob = getattr(W, name)[e]
             mats[name].append(dev.upload_matrix(t, rows, cols, blob, identity=ident(e, role)))
@@ -332,11 +388,12 @@ def upload_group(dev, W, rank: int, world: int, layer_index: int = 0) -> dict:
     return mats
 
 
-def make_device_layer(dev, W, comm, max_tokens: int):
+def make_device_layer(dev, W, comm, max_tokens: int, slots: Optional[np.ndarray] = None):
     """The expert-parallel layer of this rank on device `dev` (weights W of the whole layer; only
-    this rank's shard and the shared expert are uploaded)."""
+    this rank's shard and the shared expert are uploaded). `slots` places the experts (see
+    balanced_slots; None: contiguous ranges of ids)."""
     spec = W.spec
-    mats = upload_group(dev, W, comm.rank, comm.world)
+    mats = upload_group(dev, W, comm.rank, comm.world, slots=slots)
     ops = DeviceEpOps(dev, mats, spec, W.bias, spec.score, spec.route_scale, spec.experts, spec.top_k,
-                      spec.hidden, max_tokens)
+                      spec.hidden, max_tokens, slots=slots)
     return ExpertParallelLayer(ops, comm, spec.experts, spec.top_k, spec.hidden, max_tokens), ops
