@@ -27,7 +27,9 @@ def build(reference: Optional[str] = None, jobs: int = 8) -> None:
     """Builds liboracle.so, and _ref/libvlref.so when the reference tree is present."""
     args = ["make", "-C", str(HERE), f"-j{jobs}", "oracle"]
     subprocess.run(args, check=True, capture_output=True)
-    ref = Path(reference or "/root/reference")
+    from vastloom_b200.build import reference_root
+
+    ref = Path(reference) if reference else reference_root()
     if (ref / "src" / "inference" / "ggml_quantization.cpp").exists():
         subprocess.run(["make", "-C", str(HERE), f"-j{jobs}", "ref", f"REF={ref}"], check=True,
                        capture_output=True)

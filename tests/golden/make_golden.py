@@ -11,7 +11,10 @@ import json
 import sys
 from pathlib import Path
 
-ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+from vastloom_b200.build import reference_root  # noqa: E402
+
+ref = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
 src = json.loads((ref / "tests" / "fixtures" / "deepseek_v4_operators.json").read_text())
 keep = {k: src[k] for k in ("learned_route", "hash_route", "rms_norm", "expert", "absolute_tolerance",
                             "official_revision")}

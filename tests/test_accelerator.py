@@ -13,7 +13,9 @@ CPP = ROOT / "tests" / "cpp"
 def _binary(name: str) -> Path:
     exe = CPP / name
     if not exe.exists():
-        ref = Path("/root/reference/include")
+        from vastloom_b200.build import reference_root
+
+        ref = reference_root() / "include"
         if not ref.exists():
             pytest.skip(f"{name} is not built and the reference headers are absent")
         subprocess.run(["make", "-C", str(ROOT / "vastloom_b200" / "host")], check=True, capture_output=True)

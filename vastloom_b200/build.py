@@ -24,7 +24,14 @@ DATA = PKG / "data"
 GRIDS = DATA / "iq_grids.bin"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["vlb_kernels.cu", "vlb_decode.cu", "vlb_prefill.cu", "vlb_ep.cu", "vlb_abi.cu", "vlb_noalloc.cu"]
-DEFAULT_REFERENCE = Path("/root/reference")
+
+
+def reference_root() -> Path:
+    """The vastloom reference source tree the build-time tools read: $VLB_REFERENCE, else a
+    `reference` directory beside this repository. It is only needed here, in the build container;
+    the GPU box runs on the files built from it."""
+    env = os.environ.get("VLB_REFERENCE")
+    return Path(env) if env else ROOT.parent / "reference"
 
 
 def _nvcc() -> str:
@@ -76,7 +83,7 @@ def build_codebooks(reference: Path | None = None, force: bool = False) -> bool:
 
     Returns False (and leaves any existing file alone) when the reference tree is absent, as on
     the GPU box, which uses the file built here."""
-    ref = Path(os.environ.get("VLB_REFERENCE", reference or DEFAULT_REFERENCE))
+    ref = Path(reference) if reference else reference_root()
     inc = ref / "src" / "inference"
     if not (inc / "iq2xxs_grid.inc").exists():
         return GRIDS.exists()

@@ -588,6 +588,10 @@ int vlb_dequantize_device(vlb_handle* h, const vlb_matrix* m, float* out, void* 
 
 // ---- layers ---------------------------------------------------------------------------------
 
+// K-split items the decode kernels' scratch holds per layer (16 KB each): enough for about four
+// items per SM at decode sizes where the (unit, row group) items alone are too few.
+constexpr uint32_t kSplitItems = 640;
+
 static uint32_t max_units_for(uint32_t T, uint32_t k, uint32_t E) {
     return T * k / (uint32_t)kUnitTokens + E + T / (uint32_t)kUnitTokens + 8u;
 }
@@ -697,7 +701,8 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     const size_t o_logits = carve(T * E * 4), o_scores = carve(T * E * 4), o_idx = carve(T * k * 4),
                  o_w = carve(T * k * 4), o_off = carve((E + 2) * 4), o_pt = carve(P * 4),
                  o_ps = carve(P * 4), o_pw = carve(P * 4), o_units = carve((size_t)mu * sizeof(Unit)),
-                 o_cnt = carve(32 + T * 4), o_cp = carve(T * k * 4), o_act = carve(P * I * 4),
+                 o_cnt = carve(32 + T * 4 + (size_t)kSplitItems * 16 * 4), o_cp = carve(T * k * 4),
+                 o_act = carve(P * I * 4), o_sp = carve((size_t)kSplitItems * 16 * 32 * 8 * 4),
                  o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
                  o_xn = carve(T * H * 4), o_xd = carve(T * H * 8);
     const uint32_t mpt = prefill_max_tiles((uint32_t)T, k, E);
@@ -743,6 +748,9 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.pair_weight = reinterpret_cast<float*>(ws + o_pw);
     p.units = reinterpret_cast<Unit*>(ws + o_units);
     p.counters = reinterpret_cast<uint32_t*>(ws + o_cnt);
+    p.split_cnt = reinterpret_cast<uint32_t*>(ws + o_cnt + 32 + T * 4);
+    p.split_part = reinterpret_cast<float*>(ws + o_sp);
+    p.split_items = kSplitItems;
     p.combine_pairs = reinterpret_cast<uint32_t*>(ws + o_cp);
     p.act = reinterpret_cast<float*>(ws + o_act);
     p.y = reinterpret_cast<float*>(ws + o_y);
@@ -825,7 +833,8 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
     p.prefill = (x_half || T >= prefill_threshold(L)) ? 1 : 0;
     const bool one_route = (routes_idx || x_half) && p.k == 1;
     p.direct_out = one_route && !p.has_shared && !p.weight_after_down && !p.has_legacy ? 1 : 0;
-    const size_t zero_bytes = 32 + (size_t)T * 4;  // counters and per-token max|x|
+    // counters, per-token max|x| (the layer's max_tokens of them) and the K-split arrival counters
+    const size_t zero_bytes = 32 + (size_t)L->desc.max_tokens * 4 + (size_t)kSplitItems * 16 * 4;
     L->last_T = T;
     L->last_logits_given = logits != nullptr;
     // prefill-size forwards are long enough that launching directly costs nothing, and their

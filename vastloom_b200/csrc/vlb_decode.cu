@@ -68,6 +68,7 @@ constexpr uint32_t kDcEnd = 0xffffffffu;
 #define VLB_DC_MAX_CHUNK 4
 #endif
 constexpr uint32_t kDcMaxChunk = VLB_DC_MAX_CHUNK;
+constexpr uint32_t kDcMaxSplits = 8;
 
 static_assert(kDcXsOff % 16 == 0 && kDcStage % 1024 == 0, "shared-memory carve alignment");
 static_assert((2u * kDcRing + 1u) * 8u <= 64u, "barriers fit their slot");
@@ -150,14 +151,17 @@ struct DcItem {
     uint32_t tile[kDcSlices];    // 128-row tile of each slice
     bool valid[kDcSlices];
     bool iq2;
-    uint32_t stages;             // K-chunks
+    uint32_t st0, st1;           // this item's K-chunks: [st0, st1) of the row group's K
 };
 
+// Items are (unit, row group, K split): item = (unit * groups + group) * splits + split, so the
+// splits of one row group are neighbours (they share the staged activations).
 template <bool GATEUP>
-__device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uint32_t groups) {
+__device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uint32_t groups, uint32_t splits) {
     DcItem it;
-    it.unit = item / groups;
-    it.group = item % groups;
+    const uint32_t split = item % splits, rg = item / splits;
+    it.unit = rg / groups;
+    it.group = rg % groups;
     const Unit u = p.units[it.unit];
     const uint32_t rows = GATEUP ? p.I : p.H;
     const uint32_t tiles = (rows + kTileRows - 1u) / kTileRows;
@@ -174,7 +178,9 @@ __device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uin
     }
     const uint32_t K = GATEUP ? p.H : p.I;
     it.iq2 = it.m[0]->type == kTypeIq2Xxs;
-    it.stages = it.iq2 ? K / 256u : (K / 32u + 1u) / 2u;
+    const uint32_t stages = it.iq2 ? K / 256u : (K / 32u + 1u) / 2u;
+    it.st0 = (uint32_t)((uint64_t)stages * split / splits);
+    it.st1 = (uint32_t)((uint64_t)stages * (split + 1u) / splits);
     return it;
 }
 
@@ -188,11 +194,12 @@ struct DcWarpItem {
 };
 
 template <bool GATEUP>
-__device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t item, uint32_t groups, uint32_t s0,
-                                                   uint32_t s1) {
+__device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t item, uint32_t groups,
+                                                   uint32_t splits, uint32_t s0, uint32_t s1) {
     DcWarpItem w;
-    w.unit = item / groups;
-    const uint32_t group = item % groups;
+    const uint32_t rg = item / splits;
+    w.unit = rg / groups;
+    const uint32_t group = rg % groups;
     const Unit u = p.units[w.unit];
     const uint32_t rows = GATEUP ? p.I : p.H;
     const uint32_t tiles = (rows + kTileRows - 1u) / kTileRows;
@@ -211,8 +218,8 @@ __device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t 
 // different lanes at once (one copy per lane): a bulk copy costs its issuing thread a few hundred
 // cycles, so a single issuing lane would cap the stage rate well below HBM bandwidth.
 template <bool GATEUP>
-__device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t groups, uint64_t n_items,
-                          uint32_t chunk, volatile uint32_t* abort) {
+__device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t groups, uint32_t splits,
+                          uint64_t n_items, uint32_t chunk, volatile uint32_t* abort) {
     const uint32_t lane = threadIdx.x & 31u;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDcBarOff);
     uint64_t* empty = full + kDcRing;
@@ -248,11 +255,11 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
         // the dispatch lists the shared expert's units first (the heaviest: every token, usually
         // the widest storage type), so the CTAs start on them and finish on light routed items
         for (uint64_t item = c0; item < c1 && ok; ++item) {
-            const Unit u = p.units[(uint32_t)(item / groups)];
+            const Unit u = p.units[(uint32_t)(item / ((uint64_t)groups * splits))];
             const uint32_t t = p.mats[mat_off + u.expert].type;
             if (t != kTypeIq2Xxs && t != kTypeQ8_0) continue;  // served by the CUDA-core kernels
-            const DcItem it = dc_item<GATEUP>(p, (uint32_t)item, groups);
-            for (uint32_t st = 0; st < it.stages; ++st, ++g) {
+            const DcItem it = dc_item<GATEUP>(p, (uint32_t)item, groups, splits);
+            for (uint32_t st = it.st0; st < it.st1; ++st, ++g) {
                 const uint32_t slot = g % kDcRing;
                 if (!(ok = acquire(slot))) break;
                 // Q8_0: blocks 2 st and 2 st + 1 (the second may be past the row end)
@@ -264,7 +271,7 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
 #pragma unroll
                     for (uint32_t s = 0; s < kDcSlices; ++s)
                         if (it.valid[s]) bytes += body + dbytes + (it.iq2 ? kDcSc : 0u);
-                    hdr[slot] = make_uint4((uint32_t)item, st, it.stages, 0u);
+                    hdr[slot] = make_uint4((uint32_t)item, st, it.st1, it.st0);
                     tc::mbar_arrive_expect_tx(full + slot, bytes);
                 }
                 __syncwarp();
@@ -437,9 +444,42 @@ __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint3
     }
 }
 
+// K-split join. Every split of a row group writes its warp's partial sums (8 floats a lane) to the
+// layer's split scratch and counts itself in on the (row group, warp) counter; the warp that
+// arrives last adds the splits' partials in split order (the same sum whatever CTA ran which
+// split) and runs the epilogue, and resets the counter. Returns true for that last warp, with acc
+// holding the full sums.
+__device__ __forceinline__ bool dc_join_splits(const MoeParams& p, uint32_t item, uint32_t splits, uint32_t warp,
+                                               uint32_t lane, float (&acc)[2][4]) {
+    const uint32_t rg = item / splits;
+    float4* part = reinterpret_cast<float4*>(p.split_part);
+    const size_t mine = (((size_t)item * kDcConsumerWarps + warp) * 32u + lane) * 2u;
+    __stcg(part + mine, make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]));
+    __stcg(part + mine + 1, make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]));
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(p.split_cnt + (size_t)rg * kDcConsumerWarps + warp, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1u != splits) return false;
+    // every split has arrived: the counter goes back to zero for the next kernel (gate/up and down
+    // use the same counters, one after the other)
+    if (lane == 0) p.split_cnt[(size_t)rg * kDcConsumerWarps + warp] = 0u;
+    __threadfence();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (uint32_t sp = 0; sp < splits; ++sp) {
+        const size_t at = ((((size_t)rg * splits + sp) * kDcConsumerWarps + warp) * 32u + lane) * 2u;
+        const float4 a = __ldcg(part + at), b = __ldcg(part + at + 1);
+        acc[0][0] += a.x; acc[0][1] += a.y; acc[0][2] += a.z; acc[0][3] += a.w;
+        acc[1][0] += b.x; acc[1][1] += b.y; acc[1][2] += b.z; acc[1][3] += b.w;
+    }
+    return true;
+}
+
 template <bool GATEUP>
 __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __grid_constant__ MoeParams p,
-                                                                       uint32_t chunk) {
+                                                                       uint32_t chunk, uint32_t splits) {
     extern __shared__ __align__(1024) unsigned char smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kDcMiscOff);
@@ -463,9 +503,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     __syncthreads();
     const uint32_t rows = GATEUP ? p.I : p.H;
     const uint32_t groups = (rows + (GATEUP ? 255u : 511u)) / (GATEUP ? 256u : 512u);
-    const uint64_t n_items = (uint64_t)p.counters[0] * groups;
+    const uint64_t n_items = (uint64_t)p.counters[0] * groups * splits;
     if (warp == kDcConsumerWarps) {
-        dc_loader<GATEUP>(p, smem, groups, n_items, chunk, abort);
+        dc_loader<GATEUP>(p, smem, groups, splits, n_items, chunk, abort);
         return;
     }
     // consumer warp: 16 rows of slices (w / 8) and (2 + w / 8)
@@ -489,8 +529,8 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
         }
         const uint4 h = hdr[slot];
         if (h.x == kDcEnd) break;
-        if (h.y == 0) {  // first stage of an item
-            it = dc_warp_item<GATEUP>(p, h.x, groups, s0, s1);
+        if (h.y == h.w) {  // first stage of an item
+            it = dc_warp_item<GATEUP>(p, h.x, groups, splits, s0, s1);
             if (it.unit != staged_unit || it.iq2 != staged_iq2) {
                 const Unit u = p.units[it.unit];
                 // every warp is done with the previous unit's activations and token scales
@@ -538,7 +578,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
             const uint32_t nblk = blk0 + 1u < it.bpr ? 2u : 1u;
             dc_q8_stage(st_addr, s0, s1, rt, gq, q, n, xs, K, blk0, nblk, empty + slot, acc);
         }
-        if (h.y + 1u == h.z) {  // last stage: this warp's rows are complete
+        if (h.y + 1u == h.z) {  // last stage of the item
+            if (splits > 1u && !dc_join_splits(p, h.x, splits, warp, lane, acc)) continue;
+            // this warp's rows are complete
             const Unit u = p.units[it.unit];
             if (q < u.count) {
                 const uint32_t pair = u.pair_begin + q;
@@ -601,9 +643,22 @@ cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
     const uint32_t rows = GATEUP ? p.I : p.H;
     const uint32_t groups = (rows + (GATEUP ? 255u : 511u)) / (GATEUP ? 256u : 512u);
     const uint64_t est = (uint64_t)(p.T * p.k < p.E ? p.T * p.k : p.E) * groups;
-    uint32_t chunk = (uint32_t)((est + 4ull * n_sms - 1) / (4ull * n_sms));
+    // Small batches have fewer (unit, row group) items than SMs: split K so that about two items
+    // reach every SM. The unit count is bounded by one per routed pair plus the shared expert's.
+    const uint64_t max_items = ((uint64_t)p.T * p.k + (p.has_shared ? (p.T + kUnitTokens - 1u) / kUnitTokens : 0u)) *
+                               groups;
+    const uint32_t min_stages = K / 256u;  // an IQ2_XXS row group's K-chunks (Q8_0 has more)
+    uint32_t splits = 1;
+    if (p.split_part && max_items < 2ull * n_sms) {
+        splits = (uint32_t)((2ull * n_sms + max_items - 1) / max_items);
+        if (splits > kDcMaxSplits) splits = kDcMaxSplits;
+        if (splits > min_stages) splits = min_stages;
+        while (splits > 1u && max_items * splits > p.split_items) --splits;
+        if (splits < 1u) splits = 1;
+    }
+    uint32_t chunk = (uint32_t)((est * splits + 4ull * n_sms - 1) / (4ull * n_sms));
     chunk = chunk < 1u ? 1u : (chunk > kDcMaxChunk ? kDcMaxChunk : chunk);
-    decode_experts_kernel<GATEUP><<<n_sms, kDcThreads, smem, s>>>(p, chunk);
+    decode_experts_kernel<GATEUP><<<n_sms, kDcThreads, smem, s>>>(p, chunk, splits);
     return cudaGetLastError();
 }
 

@@ -261,6 +261,12 @@ struct MoeParams {
     const float* x_residual; // set by launch_moe for a residual block: the original rows
     uint32_t max_units;
     uint32_t* disp_counts;   // [ceil(T*k / 1024) x E]: per-chunk expert counts of the multi-CTA dispatch
+    // K-split scratch of the decode kernels (small batches): 16 warps x 32 lanes x 8 floats of
+    // partial sums per split item, and one arrival counter per (row group, warp), zeroed with the
+    // counters before each forward; null: no splitting
+    float* split_part;
+    uint32_t* split_cnt;
+    uint32_t split_items;    // split items the scratch holds
     // 1: a one-route-per-row forward (k = 1, given routes) without a shared expert whose route
     // weight is applied before the down product: each row's output is its single expert's down
     // product, so the down kernels write it straight to out[token] and no combine pass runs
