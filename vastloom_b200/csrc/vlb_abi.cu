@@ -468,9 +468,10 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     // tiled device layout (blk_index): rows padded to whole 128-row tiles with zero blocks
     const size_t rows_padded = (rows + kTileRows - 1) / kTileRows * kTileRows;
     const size_t nslots = rows_padded * bpr;
-    const bool iq2 = type == VLB_TYPE_IQ2_XXS;
+    const bool iq2 = type == VLB_TYPE_IQ2_XXS, iq3 = type == VLB_TYPE_IQ3_XXS;
+    const bool scaled = iq2 || iq3;  // sign words re-encoded, group scales gathered per block
     const size_t d_bytes = (nslots * 2 + 255) / 256 * 256;
-    const size_t sc_bytes = iq2 ? (nslots * 4 + 255) / 256 * 256 : 0;
+    const size_t sc_bytes = scaled ? (nslots * 4 + 255) / 256 * 256 : 0;
     const size_t body_bytes = nslots * L.body_bytes;
     std::vector<uint8_t> staged;
     try {
@@ -489,15 +490,17 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
             dst_d[at] = (uint16_t)(blk[0] | (blk[1] << 8));
             uint8_t* body = dst_b + at * L.body_bytes;
             std::memcpy(body, blk + 2, copy);
-            if (iq2) {
-                // group words -> pair-layout sign words, scales gathered per block
+            if (scaled) {
+                // group words (IQ2_XXS: after each group's 4 index bytes; IQ3_XXS: after the 64
+                // index bytes) -> pair-layout sign words, scales gathered per block
                 uint32_t scales = 0;
                 for (uint32_t g = 0; g < 8; ++g) {
+                    uint8_t* word = iq2 ? body + g * 8 + 4 : body + 64 + g * 4;
                     uint32_t aux;
-                    std::memcpy(&aux, body + g * 8 + 4, 4);
+                    std::memcpy(&aux, word, 4);
                     scales |= (aux >> 28) << (4 * g);
                     const uint32_t sw = iq2_pair_signs(aux);
-                    std::memcpy(body + g * 8 + 4, &sw, 4);
+                    std::memcpy(word, &sw, 4);
                 }
                 dst_sc[at] = scales;
             }
@@ -521,13 +524,13 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     m->rows = rows;
     m->cols = cols;
     m->bpr = (uint32_t)bpr;
-    m->bytes = nslots * 2 + (iq2 ? nslots * 4 : 0) + body_bytes;
+    m->bytes = nslots * 2 + (scaled ? nslots * 4 : 0) + body_bytes;
     m->payload_bytes = payload_bytes;
     m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr,
                    reinterpret_cast<const uint16_t*>(m->mem),
                    reinterpret_cast<const uint8_t*>(m->mem) + d_bytes + sc_bytes,
-                   iq2 ? reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(m->mem) + d_bytes)
-                       : nullptr,
+                   scaled ? reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(m->mem) + d_bytes)
+                          : nullptr,
                    prefill_scale(type, half_bits_to_float(dmax_bits))};
     *out = m;
     return VLB_OK;
@@ -728,10 +731,14 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
     p.has_shared = has_shared ? 1 : 0;
     p.has_legacy = 0;
     p.has_mma = 0;
-    for (const vlb_matrix* m : hm) {
+    p.fmt_gu = p.fmt_dn = 0;
+    for (size_t i = 0; i < hm.size(); ++i) {
+        const vlb_matrix* m = hm[i];
         if (!m) continue;
         if (m->type == VLB_TYPE_IQ2_XXS || m->type == VLB_TYPE_Q8_0) p.has_mma = 1;
         else p.has_legacy = 1;
+        if (i < 2 * (size_t)(E + 1)) p.fmt_gu |= fmt_bit(m->type);
+        else p.fmt_dn |= fmt_bit(m->type);
     }
     p.router = L->router;
     p.bias = L->bias;

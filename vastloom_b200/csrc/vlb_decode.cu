@@ -45,21 +45,30 @@ constexpr uint32_t kDcConsumerWarps = 16;
 constexpr uint32_t kDcConsumers = kDcConsumerWarps * 32;
 constexpr uint32_t kDcThreads = kDcConsumers + 32;             // + the loader warp
 constexpr uint32_t kDcSlices = 4;
-constexpr uint32_t kDcBody = kTileRows * 64u;                  // 8 KB of packed weights per slice
 constexpr uint32_t kDcD = 512;                                 // fp16 block scales (<= 2 blocks)
-constexpr uint32_t kDcSc = kTileRows * 4u;                     // IQ2_XXS group scale words
-constexpr uint32_t kDcSlice = kDcBody + kDcD + kDcSc;
-constexpr uint32_t kDcStage = kDcSlices * kDcSlice;            // 36 KB
+constexpr uint32_t kDcSc = kTileRows * 4u;                     // IQ2_XXS / IQ3_XXS group scale words
 #ifndef VLB_DC_RING
 #define VLB_DC_RING 3
 #endif
 constexpr uint32_t kDcRing = VLB_DC_RING;
-constexpr uint32_t kDcTabBytes = 256u * 8u * 16u;              // fp16 IQ2_XXS magnitudes, 8 replicas
-constexpr uint32_t kDcRingOff = kDcTabBytes;
-constexpr uint32_t kDcHdrOff = kDcRingOff + kDcRing * kDcStage;
-constexpr uint32_t kDcBarOff = kDcHdrOff + kDcRing * 16u;
-constexpr uint32_t kDcMiscOff = kDcBarOff + 64u;              // abort word, token scales
-constexpr uint32_t kDcXsOff = (kDcMiscOff + 64u + 127u) / 128u * 128u;
+constexpr uint32_t kDcTabBytes = 32768u;  // the IQ codebook in fp16 (layout per format: dc_build_table)
+// Stage carve for slices of BODY bytes of packed weights: 8 KB holds a 128-row tile block column
+// of IQ2_XXS (64 B a row), IQ1_S (48 B) or two Q8_0 blocks (2 x 32 B); IQ3_XXS (96 B a row) needs
+// 12 KB and is launched with the larger carve.
+constexpr uint32_t kDcBodySmall = kTileRows * 64u;
+constexpr uint32_t kDcBodyLarge = kTileRows * 96u;
+template <uint32_t BODY>
+struct DcL {
+    static constexpr uint32_t Body = BODY;
+    static constexpr uint32_t Slice = BODY + kDcD + kDcSc;
+    static constexpr uint32_t Stage = kDcSlices * Slice;
+    static constexpr uint32_t RingOff = kDcTabBytes;
+    static constexpr uint32_t HdrOff = RingOff + kDcRing * Stage;
+    static constexpr uint32_t BarOff = HdrOff + kDcRing * 16u;
+    static constexpr uint32_t MiscOff = BarOff + 64u;  // abort word, token scales
+    static constexpr uint32_t XsOff = (MiscOff + 64u + 127u) / 128u * 128u;
+    static_assert(XsOff % 16 == 0 && Stage % 1024 == 0, "shared-memory carve alignment");
+};
 constexpr uint64_t kDcWaitNs = 2000000000ull;
 constexpr uint32_t kDcSleepNs = 1000;  // suspend hint of one barrier test
 constexpr uint32_t kDcErrTimeout = 8u;
@@ -70,13 +79,13 @@ constexpr uint32_t kDcEnd = 0xffffffffu;
 constexpr uint32_t kDcMaxChunk = VLB_DC_MAX_CHUNK;
 constexpr uint32_t kDcMaxSplits = 8;
 
-static_assert(kDcXsOff % 16 == 0 && kDcStage % 1024 == 0, "shared-memory carve alignment");
 static_assert((2u * kDcRing + 1u) * 8u <= 64u, "barriers fit their slot");
 
 // Activation staging: 8 B columns (n = 2 token + piece, piece 0 = hi, 1 = lo) of K fp16 values.
 // Two layouts, each free of bank conflicts for its format's read pattern (8 lanes of a 16-byte
 // load phase: n in {2m, 2m+1} x q in 0..3):
-//   IQ2_XXS: lane q reads chunk c = 32 b + 8 q + j (block b, k-step pair j): stored at 16-byte
+//   256-column formats (IQ2_XXS, IQ3_XXS, IQ1_S):
+//            lane q reads chunk c = 32 b + 8 q + j (block b, k-step pair j): stored at 16-byte
 //            position 32 b + 4 j + q of a column whose stride is K * 2 + 64 bytes, so the four q
 //            are consecutive and the column parity shifts by half a bank row; j is an immediate.
 //   Q8_0:    lane q reads chunk c = 4 b' + q (32-column block b'): stored at position
@@ -150,9 +159,14 @@ struct DcItem {
     const DevMat* m[kDcSlices];  // matrix of each slice
     uint32_t tile[kDcSlices];    // 128-row tile of each slice
     bool valid[kDcSlices];
-    bool iq2;
+    uint32_t fmt;                // storage type of the item's matrices
     uint32_t st0, st1;           // this item's K-chunks: [st0, st1) of the row group's K
 };
+
+// Packed bytes per (row, block) of the device body, per type.
+__device__ __forceinline__ uint32_t dc_body_bytes(uint32_t fmt) {
+    return fmt == kTypeQ8_0 ? 32u : fmt == kTypeIq2Xxs ? 64u : fmt == kTypeIq1S ? 48u : 96u;
+}
 
 // Items are (unit, row group, K split): item = (unit * groups + group) * splits + split, so the
 // splits of one row group are neighbours (they share the staged activations).
@@ -177,8 +191,8 @@ __device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uin
         it.valid[s] = it.tile[s] < tiles;
     }
     const uint32_t K = GATEUP ? p.H : p.I;
-    it.iq2 = it.m[0]->type == kTypeIq2Xxs;
-    const uint32_t stages = it.iq2 ? K / 256u : (K / 32u + 1u) / 2u;
+    it.fmt = it.m[0]->type;
+    const uint32_t stages = it.fmt != kTypeQ8_0 ? K / 256u : (K / 32u + 1u) / 2u;
     it.st0 = (uint32_t)((uint64_t)stages * split / splits);
     it.st1 = (uint32_t)((uint64_t)stages * (split + 1u) / splits);
     return it;
@@ -189,7 +203,7 @@ struct DcWarpItem {
     uint32_t unit;
     uint32_t tile0, tile1;  // tiles of slices s0 and s1
     bool valid0, valid1;
-    bool iq2;
+    uint32_t fmt;
     uint32_t bpr;
 };
 
@@ -208,7 +222,7 @@ __device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t 
     w.valid0 = w.tile0 < tiles;
     w.valid1 = w.tile1 < tiles;
     const DevMat& m = p.mats[(GATEUP ? 0u : 2u * (p.E + 1u)) + u.expert];
-    w.iq2 = m.type == kTypeIq2Xxs;
+    w.fmt = m.type;
     w.bpr = m.bpr;
     return w;
 }
@@ -217,13 +231,14 @@ __device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t 
 // Lane 0 takes the items and does the ring bookkeeping; the copies of a stage are issued by
 // different lanes at once (one copy per lane): a bulk copy costs its issuing thread a few hundred
 // cycles, so a single issuing lane would cap the stage rate well below HBM bandwidth.
-template <bool GATEUP>
+template <bool GATEUP, uint32_t BODY>
 __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t groups, uint32_t splits,
-                          uint64_t n_items, uint32_t chunk, volatile uint32_t* abort) {
+                          uint64_t n_items, uint32_t chunk, uint32_t tfmt, volatile uint32_t* abort) {
+    using Lay = DcL<BODY>;
     const uint32_t lane = threadIdx.x & 31u;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDcBarOff);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::BarOff);
     uint64_t* empty = full + kDcRing;
-    uint4* hdr = reinterpret_cast<uint4*>(smem + kDcHdrOff);
+    uint4* hdr = reinterpret_cast<uint4*>(smem + Lay::HdrOff);
     uint32_t* next_item = p.counters + (GATEUP ? 2 : 4);
     const uint32_t mat_off = GATEUP ? 0u : 2u * (p.E + 1u);
     uint32_t g = 0;
@@ -257,20 +272,23 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
         for (uint64_t item = c0; item < c1 && ok; ++item) {
             const Unit u = p.units[(uint32_t)(item / ((uint64_t)groups * splits))];
             const uint32_t t = p.mats[mat_off + u.expert].type;
-            if (t != kTypeIq2Xxs && t != kTypeQ8_0) continue;  // served by the CUDA-core kernels
+            if (t != tfmt && t != kTypeQ8_0) continue;  // served by the CUDA-core kernels
             const DcItem it = dc_item<GATEUP>(p, (uint32_t)item, groups, splits);
             for (uint32_t st = it.st0; st < it.st1; ++st, ++g) {
                 const uint32_t slot = g % kDcRing;
                 if (!(ok = acquire(slot))) break;
                 // Q8_0: blocks 2 st and 2 st + 1 (the second may be past the row end)
-                const uint32_t nblk = it.iq2 ? 1u : (2u * st + 1u < it.m[0]->bpr ? 2u : 1u);
-                const uint32_t body = it.iq2 ? kDcBody : nblk * kTileRows * 32u;
+                const bool q8 = it.fmt == kTypeQ8_0;
+                const bool scaled = it.fmt == kTypeIq2Xxs || it.fmt == kTypeIq3Xxs;
+                const uint32_t nblk = q8 ? (2u * st + 1u < it.m[0]->bpr ? 2u : 1u) : 1u;
+                const uint32_t bb = dc_body_bytes(it.fmt);
+                const uint32_t body = nblk * kTileRows * bb;
                 const uint32_t dbytes = nblk * kTileRows * 2u;
                 if (lane == 0) {
                     uint32_t bytes = 0;
 #pragma unroll
                     for (uint32_t s = 0; s < kDcSlices; ++s)
-                        if (it.valid[s]) bytes += body + dbytes + (it.iq2 ? kDcSc : 0u);
+                        if (it.valid[s]) bytes += body + dbytes + (scaled ? kDcSc : 0u);
                     hdr[slot] = make_uint4((uint32_t)item, st, it.st1, it.st0);
                     tc::mbar_arrive_expect_tx(full + slot, bytes);
                 }
@@ -287,14 +305,14 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
                         tile = it.tile[k];
                         valid = it.valid[k];
                     }
-                if (valid && (c < 2u || it.iq2)) {
+                if (valid && (c < 2u || scaled)) {
                     const DevMat& m = *ms;
-                    const uint32_t blk = it.iq2 ? st : 2u * st;
+                    const uint32_t blk = q8 ? 2u * st : st;
                     const size_t at = blk_index(m.bpr, tile * kTileRows, blk);
-                    const uint32_t sd = tc::smem_u32(smem + kDcRingOff + slot * kDcStage) + s * kDcSlice;
-                    if (c == 0) tc::bulk_load(sd, m.body + at * (it.iq2 ? 64u : 32u), body, full + slot);
-                    else if (c == 1) tc::bulk_load(sd + kDcBody, m.d + at, dbytes, full + slot);
-                    else tc::bulk_load(sd + kDcBody + kDcD, m.scales + at, kDcSc, full + slot);
+                    const uint32_t sd = tc::smem_u32(smem + Lay::RingOff + slot * Lay::Stage) + s * Lay::Slice;
+                    if (c == 0) tc::bulk_load(sd, m.body + at * bb, body, full + slot);
+                    else if (c == 1) tc::bulk_load(sd + BODY, m.d + at, dbytes, full + slot);
+                    else tc::bulk_load(sd + BODY + kDcD, m.scales + at, kDcSc, full + slot);
                 }
                 __syncwarp();
             }
@@ -334,6 +352,7 @@ __device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, floa
 }
 
 // IQ2_XXS stage: one 256-column block of this warp's two slices (rows rt + gq and rt + gq + 8).
+template <uint32_t BODY>
 __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
                                              uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab_lane,
                                              uint64_t* empty_bar, float (&acc)[2][4]) {
@@ -342,20 +361,20 @@ __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint
     uint32_t sa[2], sb[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        const uint32_t sl = st_addr + (i ? s1 : s0) * kDcSlice;
+        const uint32_t sl = st_addr + (i ? s1 : s0) * DcL<BODY>::Slice;
         const uint32_t ba = sl + (rt + gq) * 64u + 16u * q, bb = ba + 8u * 64u;
         asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(ra[i].x), "=r"(ra[i].y), "=r"(ra[i].z), "=r"(ra[i].w) : "r"(ba));
         asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(rb[i].x), "=r"(rb[i].y), "=r"(rb[i].z), "=r"(rb[i].w) : "r"(bb));
         unsigned short ha, hb;
-        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ha) : "r"(sl + kDcBody + (rt + gq) * 2u));
-        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hb) : "r"(sl + kDcBody + (rt + gq + 8u) * 2u));
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ha) : "r"(sl + BODY + (rt + gq) * 2u));
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hb) : "r"(sl + BODY + (rt + gq + 8u) * 2u));
         da[i] = h2f(ha);
         db[i] = h2f(hb);
         uint32_t wa, wb;
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wa) : "r"(sl + kDcBody + kDcD + (rt + gq) * 4u));
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wb) : "r"(sl + kDcBody + kDcD + (rt + gq + 8u) * 4u));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wa) : "r"(sl + BODY + kDcD + (rt + gq) * 4u));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wb) : "r"(sl + BODY + kDcD + (rt + gq + 8u) * 4u));
         sa[i] = wa >> (8u * q);  // this lane's groups 2q, 2q + 1 in the low byte
         sb[i] = wb >> (8u * q);
     }
@@ -400,6 +419,7 @@ __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint
 }
 
 // Q8_0 stage: 32-column blocks 2 st and 2 st + 1 (nblk of them) of the warp's two slices.
+template <uint32_t BODY>
 __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt, uint32_t gq,
                                             uint32_t q, uint32_t n, const unsigned char* xs, uint32_t K,
                                             uint32_t blk0, uint32_t nblk, uint64_t* empty_bar,
@@ -410,15 +430,15 @@ __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint3
     for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            const uint32_t sl = st_addr + (i ? s1 : s0) * kDcSlice;
+            const uint32_t sl = st_addr + (i ? s1 : s0) * DcL<BODY>::Slice;
             const uint32_t ba = sl + j * (kTileRows * 32u) + (rt + gq) * 32u + 8u * q, bb = ba + 8u * 32u;
             asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(qa[i][j].x), "=r"(qa[i][j].y) : "r"(ba));
             asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(qb[i][j].x), "=r"(qb[i][j].y) : "r"(bb));
             unsigned short ha, hb;
-            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ha) : "r"(sl + kDcBody + j * (kTileRows * 2u) + (rt + gq) * 2u));
+            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(ha) : "r"(sl + BODY + j * (kTileRows * 2u) + (rt + gq) * 2u));
             asm volatile("ld.shared.u16 %0, [%1];"
                          : "=h"(hb)
-                         : "r"(sl + kDcBody + j * (kTileRows * 2u) + (rt + gq + 8u) * 2u));
+                         : "r"(sl + BODY + j * (kTileRows * 2u) + (rt + gq + 8u) * 2u));
             da[i][j] = h2f(ha);
             db[i][j] = h2f(hb);
         }
@@ -441,6 +461,141 @@ __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint3
             acc[i][2] = fmaf(db[i][j], D[2], acc[i][2]);
             acc[i][3] = fmaf(db[i][j], D[3], acc[i][3]);
         }
+    }
+}
+
+// IQ1_S stage: one 256-column block (48 bytes a row: 32 qs bytes, 8 qh words) of this warp's two
+// slices. Lane q owns groups 2q and 2q + 1 as for IQ2_XXS; the fp16 block scale d is applied per
+// block on the accumulators.
+template <uint32_t BODY>
+__device__ __forceinline__ void dc_iq1_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
+                                             uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab,
+                                             uint64_t* empty_bar, float (&acc)[2][4]) {
+    uint2 qa[2], qb[2];
+    uint32_t ha[2], hb[2];
+    float da[2], db[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t sl = st_addr + (i ? s1 : s0) * DcL<BODY>::Slice;
+        const uint32_t ba = sl + (rt + gq) * 48u, bb = ba + 8u * 48u;
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(qa[i].x), "=r"(qa[i].y) : "r"(ba + 8u * q));
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(qb[i].x), "=r"(qb[i].y) : "r"(bb + 8u * q));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(ha[i]) : "r"(ba + 32u + 4u * q));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(hb[i]) : "r"(bb + 32u + 4u * q));
+        unsigned short xa, xb;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(xa) : "r"(sl + BODY + (rt + gq) * 2u));
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(xb) : "r"(sl + BODY + (rt + gq + 8u) * 2u));
+        da[i] = h2f(xa);
+        db[i] = h2f(xb);
+    }
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
+    float D[2][4] = {}, E[2][4] = {};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t kka[2], dka[2], kkb[2], dkb[2], hga[2], hgb[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            hga[i] = (ha[i] >> (16 * half)) & 0xffffu;
+            hgb[i] = (hb[i] >> (16 * half)) & 0xffffu;
+            mma::iq1_group_factors(hga[i], kka[i], dka[i]);
+            mma::iq1_group_factors(hgb[i], kkb[i], dkb[i]);
+        }
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+            uint4 xv;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(xv.x), "=r"(xv.y), "=r"(xv.z), "=r"(xv.w)
+                         : "r"(xrow + (uint32_t)(4 * half + sub) * 64u));
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                uint32_t va[4], vb[4];
+                mma::decode_iq1_sub(tab, half ? qa[i].y : qa[i].x, hga[i], (uint32_t)sub, kka[i], dka[i], va);
+                mma::decode_iq1_sub(tab, half ? qb[i].y : qb[i].x, hgb[i], (uint32_t)sub, kkb[i], dkb[i], vb);
+                float (&A)[4] = (sub & 1) ? E[i] : D[i];
+                mma::mma16816(A, va[0], vb[0], va[1], vb[1], xv.x, xv.y);
+                mma::mma16816(A, va[2], vb[2], va[3], vb[3], xv.z, xv.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        acc[i][0] = fmaf(da[i], D[i][0] + E[i][0], acc[i][0]);
+        acc[i][1] = fmaf(da[i], D[i][1] + E[i][1], acc[i][1]);
+        acc[i][2] = fmaf(db[i], D[i][2] + E[i][2], acc[i][2]);
+        acc[i][3] = fmaf(db[i], D[i][3] + E[i][3], acc[i][3]);
+    }
+}
+
+// IQ3_XXS stage: one 256-column block (96 bytes a row: 64 grid-index bytes, 8 pair-layout sign
+// words; group scales in the stage's scale words) of this warp's two slices.
+template <uint32_t BODY>
+__device__ __forceinline__ void dc_iq3_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
+                                             uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab_lane,
+                                             uint64_t* empty_bar, float (&acc)[2][4]) {
+    uint4 ia[2], ib[2];
+    uint2 wa[2], wb[2];
+    uint32_t sca[2], scb[2];
+    float da[2], db[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t sl = st_addr + (i ? s1 : s0) * DcL<BODY>::Slice;
+        const uint32_t ba = sl + (rt + gq) * 96u, bb = ba + 8u * 96u;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(ia[i].x), "=r"(ia[i].y), "=r"(ia[i].z), "=r"(ia[i].w) : "r"(ba + 16u * q));
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(ib[i].x), "=r"(ib[i].y), "=r"(ib[i].z), "=r"(ib[i].w) : "r"(bb + 16u * q));
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(wa[i].x), "=r"(wa[i].y) : "r"(ba + 64u + 8u * q));
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(wb[i].x), "=r"(wb[i].y) : "r"(bb + 64u + 8u * q));
+        unsigned short xa, xb;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(xa) : "r"(sl + BODY + (rt + gq) * 2u));
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(xb) : "r"(sl + BODY + (rt + gq + 8u) * 2u));
+        da[i] = h2f(xa);
+        db[i] = h2f(xb);
+        uint32_t ta, tb;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(ta) : "r"(sl + BODY + kDcD + (rt + gq) * 4u));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tb) : "r"(sl + BODY + kDcD + (rt + gq + 8u) * 4u));
+        sca[i] = ta >> (8u * q);  // this lane's groups 2q, 2q + 1 in the low byte
+        scb[i] = tb >> (8u * q);
+    }
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
+    float D[2][4] = {}, E[2][4] = {};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t kka[2], kkb[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            kka[i] = mma::iq3_group_scale_h2((sca[i] >> (4 * half)) & 15u);
+            kkb[i] = mma::iq3_group_scale_h2((scb[i] >> (4 * half)) & 15u);
+        }
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+            uint4 xv;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(xv.x), "=r"(xv.y), "=r"(xv.z), "=r"(xv.w)
+                         : "r"(xrow + (uint32_t)(4 * half + sub) * 64u));
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                // the group's index words: (x, y) for group 2q, (z, w) for 2q + 1; sub-blocks 0-1
+                // in the first word, 2-3 in the second
+                const uint32_t wla = half ? (sub < 2 ? ia[i].z : ia[i].w) : (sub < 2 ? ia[i].x : ia[i].y);
+                const uint32_t wlb = half ? (sub < 2 ? ib[i].z : ib[i].w) : (sub < 2 ? ib[i].x : ib[i].y);
+                uint32_t va[4], vb[4];
+                mma::decode_iq3_sub(tab_lane, wla, half ? wa[i].y : wa[i].x, (uint32_t)sub, kka[i], va);
+                mma::decode_iq3_sub(tab_lane, wlb, half ? wb[i].y : wb[i].x, (uint32_t)sub, kkb[i], vb);
+                float (&A)[4] = (sub & 1) ? E[i] : D[i];
+                mma::mma16816(A, va[0], vb[0], va[1], vb[1], xv.x, xv.y);
+                mma::mma16816(A, va[2], vb[2], va[3], vb[3], xv.z, xv.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        acc[i][0] = fmaf(da[i], D[i][0] + E[i][0], acc[i][0]);
+        acc[i][1] = fmaf(da[i], D[i][1] + E[i][1], acc[i][1]);
+        acc[i][2] = fmaf(db[i], D[i][2] + E[i][2], acc[i][2]);
+        acc[i][3] = fmaf(db[i], D[i][3] + E[i][3], acc[i][3]);
     }
 }
 
@@ -477,18 +632,24 @@ __device__ __forceinline__ bool dc_join_splits(const MoeParams& p, uint32_t item
     return true;
 }
 
-template <bool GATEUP>
+// tfmt: the IQ storage type whose codebook the CTA holds (IQ2_XXS, IQ1_S or IQ3_XXS); items of
+// that type and of Q8_0 run here, any other type on the CUDA-core kernels.
+template <bool GATEUP, uint32_t BODY>
 __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __grid_constant__ MoeParams p,
-                                                                       uint32_t chunk, uint32_t splits) {
+                                                                       uint32_t chunk, uint32_t splits,
+                                                                       uint32_t tfmt) {
+    using Lay = DcL<BODY>;
     extern __shared__ __align__(1024) unsigned char smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + kDcMiscOff);
-    float* tok_scale = reinterpret_cast<float*>(smem + kDcMiscOff + 16u);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDcBarOff);
+    volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + Lay::MiscOff);
+    float* tok_scale = reinterpret_cast<float*>(smem + Lay::MiscOff + 16u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::BarOff);
     uint64_t* empty = full + kDcRing;
     const uint32_t K = GATEUP ? p.H : p.I;
-    unsigned char* xs = smem + kDcXsOff;
-    mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
+    unsigned char* xs = smem + Lay::XsOff;
+    if (tfmt == kTypeIq2Xxs) mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
+    else if (tfmt == kTypeIq1S) mma::build_iq1s_table(reinterpret_cast<uint4*>(smem), p.grids.iq1s);
+    else if (tfmt == kTypeIq3Xxs) mma::build_iq3_table(reinterpret_cast<uint2*>(smem), p.grids.iq3xxs);
     for (uint32_t i = threadIdx.x; i < dc_xs_bytes(K) / 16u; i += blockDim.x)
         reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
@@ -505,19 +666,20 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     const uint32_t groups = (rows + (GATEUP ? 255u : 511u)) / (GATEUP ? 256u : 512u);
     const uint64_t n_items = (uint64_t)p.counters[0] * groups * splits;
     if (warp == kDcConsumerWarps) {
-        dc_loader<GATEUP>(p, smem, groups, splits, n_items, chunk, abort);
+        dc_loader<GATEUP, BODY>(p, smem, groups, splits, n_items, chunk, tfmt, abort);
         return;
     }
     // consumer warp: 16 rows of slices (w / 8) and (2 + w / 8)
     const uint32_t s0 = warp >> 3, s1 = 2u + (warp >> 3), rt = (warp & 7u) * 16u;
     const uint32_t gq = lane >> 2, q = lane & 3u, n = lane >> 2, lane7 = lane & 7u;
-    const uint4* hdr = reinterpret_cast<const uint4*>(smem + kDcHdrOff);
+    const uint4* hdr = reinterpret_cast<const uint4*>(smem + Lay::HdrOff);
     const uint32_t xs_iq2_lane = tc::smem_u32(xs) + n * (K * 2u + 64u) + q * 16u;
-    const uint32_t tab_lane = tc::smem_u32(smem) + lane7 * 16u;  // this lane's table replica
+    const uint32_t tab = tc::smem_u32(smem);
+    const uint32_t tab_lane = tab + (tfmt == kTypeIq3Xxs ? (lane & 15u) * 8u : lane7 * 16u);  // this lane's replica
     uint64_t* cbar = empty + kDcRing;
     uint32_t cphase = 0;
     uint32_t staged_unit = 0xffffffffu;
-    bool staged_iq2 = false;
+    bool staged_iq = false;  // staged for the 256-column formats (else for Q8_0)
     float acc[2][4] = {};
     DcWarpItem it{};
     for (uint32_t g = 0;; ++g) {
@@ -531,7 +693,8 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
         if (h.x == kDcEnd) break;
         if (h.y == h.w) {  // first stage of an item
             it = dc_warp_item<GATEUP>(p, h.x, groups, splits, s0, s1);
-            if (it.unit != staged_unit || it.iq2 != staged_iq2) {
+            const bool iq = it.fmt != kTypeQ8_0;
+            if (it.unit != staged_unit || iq != staged_iq) {
                 const Unit u = p.units[it.unit];
                 // every warp is done with the previous unit's activations and token scales
                 if (!dc_consumer_sync(cbar, cphase, abort)) {
@@ -559,24 +722,28 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
                                  : nullptr;
                     scl[t] = tok_scale[t];
                 }
-                dc_stage_xs(xs, rws, scl, K, u.count, it.iq2);
+                dc_stage_xs(xs, rws, scl, K, u.count, iq);
                 if (!dc_consumer_sync(cbar, cphase, abort)) {
                     if (lane == 0) dc_fail(p.counters + 3, abort);
                     break;
                 }
                 staged_unit = it.unit;
-                staged_iq2 = it.iq2;
+                staged_iq = iq;
             }
 #pragma unroll
             for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
         }
-        const uint32_t st_addr = tc::smem_u32(smem + kDcRingOff + slot * kDcStage);
-        if (it.iq2) {
-            dc_iq2_stage(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
+        const uint32_t st_addr = tc::smem_u32(smem + Lay::RingOff + slot * Lay::Stage);
+        if (it.fmt == kTypeIq2Xxs) {
+            dc_iq2_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
+        } else if (it.fmt == kTypeIq1S) {
+            dc_iq1_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab, empty + slot, acc);
+        } else if (it.fmt == kTypeIq3Xxs) {
+            dc_iq3_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
         } else {
             const uint32_t blk0 = 2u * h.y;
             const uint32_t nblk = blk0 + 1u < it.bpr ? 2u : 1u;
-            dc_q8_stage(st_addr, s0, s1, rt, gq, q, n, xs, K, blk0, nblk, empty + slot, acc);
+            dc_q8_stage<BODY>(st_addr, s0, s1, rt, gq, q, n, xs, K, blk0, nblk, empty + slot, acc);
         }
         if (h.y + 1u == h.z) {  // last stage of the item
             if (splits > 1u && !dc_join_splits(p, h.x, splits, warp, lane, acc)) continue;
@@ -615,10 +782,41 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     }
 }
 
-template <bool GATEUP>
-cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
-    const uint32_t K = GATEUP ? p.H : p.I;
-    const size_t smem = kDcXsOff + dc_xs_bytes(K);
+// The phase's IQ type and its stage carve: IQ2_XXS, else IQ1_S, else IQ3_XXS (0: Q8_0 only); a
+// carve that does not fit the device's shared memory for this K leaves the IQ type to the
+// CUDA-core kernels.
+struct DcChoice {
+    uint32_t tfmt;
+    bool large;
+    size_t smem;
+};
+
+static int g_optin_smem = 0;
+
+static DcChoice dc_choice(const MoeParams& p, bool gateup) {
+    const uint32_t mask = gateup ? p.fmt_gu : p.fmt_dn;
+    const uint32_t K = gateup ? p.H : p.I;
+    DcChoice c{0u, false, 0};
+    if (mask & fmt_bit(kTypeIq2Xxs)) c.tfmt = kTypeIq2Xxs;
+    else if (mask & fmt_bit(kTypeIq1S)) c.tfmt = kTypeIq1S;
+    else if (mask & fmt_bit(kTypeIq3Xxs)) c.tfmt = kTypeIq3Xxs;
+    c.large = c.tfmt == kTypeIq3Xxs;
+    c.smem = (c.large ? DcL<kDcBodyLarge>::XsOff : DcL<kDcBodySmall>::XsOff) + dc_xs_bytes(K);
+    if (g_optin_smem == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_optin_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    }
+    if (c.large && c.smem > (size_t)g_optin_smem) {  // IQ3_XXS does not fit: CUDA cores take it
+        c.tfmt = 0;
+        c.large = false;
+        c.smem = DcL<kDcBodySmall>::XsOff + dc_xs_bytes(K);
+    }
+    return c;
+}
+
+template <bool GATEUP, uint32_t BODY>
+cudaError_t launch_decode_carve(const MoeParams& p, unsigned n_sms, uint32_t tfmt, size_t smem, cudaStream_t s) {
     static std::mutex mu;
     static std::vector<size_t> configured;
     int dev = 0;
@@ -632,12 +830,13 @@ cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
             if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
                 return e;
             if (smem > (size_t)optin) return cudaErrorInvalidValue;  // hidden size beyond this kernel's staging
-            if ((e = cudaFuncSetAttribute(decode_experts_kernel<GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem)) != cudaSuccess)
+            if ((e = cudaFuncSetAttribute(decode_experts_kernel<GATEUP, BODY>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
                 return e;
             configured[(size_t)dev] = smem;
         }
     }
+    const uint32_t K = GATEUP ? p.H : p.I;
     // items ~ units x row groups; the host does not know the unit count (it is on the device), so
     // the chunk follows the worst case of one unit per routed pair plus the shared expert's units
     const uint32_t rows = GATEUP ? p.I : p.H;
@@ -647,7 +846,7 @@ cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
     // reach every SM. The unit count is bounded by one per routed pair plus the shared expert's.
     const uint64_t max_items = ((uint64_t)p.T * p.k + (p.has_shared ? (p.T + kUnitTokens - 1u) / kUnitTokens : 0u)) *
                                groups;
-    const uint32_t min_stages = K / 256u;  // an IQ2_XXS row group's K-chunks (Q8_0 has more)
+    const uint32_t min_stages = K / 256u;  // a 256-column format's K-chunks (Q8_0 has more)
     uint32_t splits = 1;
     if (p.split_part && max_items < 2ull * n_sms) {
         splits = (uint32_t)((2ull * n_sms + max_items - 1) / max_items);
@@ -658,8 +857,15 @@ cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
     }
     uint32_t chunk = (uint32_t)((est * splits + 4ull * n_sms - 1) / (4ull * n_sms));
     chunk = chunk < 1u ? 1u : (chunk > kDcMaxChunk ? kDcMaxChunk : chunk);
-    decode_experts_kernel<GATEUP><<<n_sms, kDcThreads, smem, s>>>(p, chunk, splits);
+    decode_experts_kernel<GATEUP, BODY><<<n_sms, kDcThreads, smem, s>>>(p, chunk, splits, tfmt);
     return cudaGetLastError();
+}
+
+template <bool GATEUP>
+cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
+    const DcChoice c = dc_choice(p, GATEUP);
+    if (c.large) return launch_decode_carve<GATEUP, kDcBodyLarge>(p, n_sms, c.tfmt, c.smem, s);
+    return launch_decode_carve<GATEUP, kDcBodySmall>(p, n_sms, c.tfmt, c.smem, s);
 }
 
 }  // namespace
@@ -670,6 +876,11 @@ cudaError_t launch_decode_gateup(const MoeParams& p, unsigned n_sms, cudaStream_
 
 cudaError_t launch_decode_down(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
     return launch_decode<false>(p, n_sms, s);
+}
+
+uint32_t decode_ring_types(const MoeParams& p, bool gateup) {
+    const DcChoice c = dc_choice(p, gateup);
+    return fmt_bit(kTypeQ8_0) | (c.tfmt ? fmt_bit(c.tfmt) : 0u);
 }
 
 }  // namespace vlb

@@ -54,11 +54,11 @@ __device__ __forceinline__ void load_group(const DevMat& m, uint32_t row, uint32
         const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
         const uint8_t* body = m.body + blk_index(m.bpr, row, blk) * 96u;
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(body + gg * 8u));
-        const uint32_t aux = __ldg(reinterpret_cast<const uint32_t*>(body + 64u + gg * 4u));
+        const uint32_t ls4 = (__ldg(m.scales + blk_index(m.bpr, row, blk)) >> (4u * gg)) & 15u;
         r.a = v.x;
         r.b = v.y;
-        r.c = aux;
-        r.ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
+        r.c = __ldg(reinterpret_cast<const uint32_t*>(body + 64u + gg * 4u));  // pair-layout sign word
+        r.ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)ls4)), 0.5f);
     } else {  // IQ1_S
         const uint32_t blk = g >> 3, gg = g & 7u;
         const float d = h2f(__ldg(m.d + blk_index(m.bpr, row, blk)));
@@ -97,7 +97,7 @@ __device__ __forceinline__ void decode_sub(const DevMat& m, uint32_t row, uint32
         const uint32_t word = j < 2 ? r.a : r.b;
         const uint32_t g1 = gs.iq3xxs[(word >> (16 * (j & 1))) & 0xffu];
         const uint32_t g2 = gs.iq3xxs[(word >> (16 * (j & 1) + 8)) & 0xffu];
-        const uint32_t signs = iq_signs(r.c, j);
+        const uint32_t signs = iq2_sub_signs(r.c, j);
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
             const float p1 = __fmul_rn(r.ls, (float)((g1 >> (8 * l)) & 0xffu));

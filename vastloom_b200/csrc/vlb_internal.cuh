@@ -3,12 +3,12 @@
 //
 // Device layout of a resident ggml matrix (chosen at upload, vlb_upload_matrix):
 //   d      : fp16 block scales (the 2-byte header of every ggml block)
-//   scales : IQ2_XXS only: one u32 per block holding the 8 group scales (nibble g = group g's
-//            4-bit scale, the top nibble of the ggml group word)
+//   scales : IQ2_XXS and IQ3_XXS: one u32 per block holding the 8 group scales (nibble g = group
+//            g's 4-bit scale, the top nibble of the ggml group word)
 //   body   : the rest of each block, padded to a 16-byte multiple
 //            Q8_0    : 32 int8 quants                                   (32 B)
 //            IQ2_XXS : 8 groups x (4 grid-index bytes, u32 sign word)    (64 B)
-//            IQ3_XXS : 64 grid-index bytes, then 8 x u32 signs/scale      (96 B)
+//            IQ3_XXS : 64 grid-index bytes, then 8 x u32 pair sign words  (96 B)
 //            IQ1_S   : 32 low-index bytes, then 8 x u16 high bits/scale   (48 B)
 // all three in 128-row tiles: entry (row, block) sits at ((row / 128) * blocks_per_row + block) *
 // 128 + row % 128, so one block column of a tile (128 rows x one block) is contiguous. The ggml
@@ -17,12 +17,13 @@
 // warp's 8 consecutive rows of a block 512 contiguous bytes. Rows are padded to a multiple of 128
 // (zero blocks).
 //
-// IQ2_XXS sign word. The ggml group word holds four 7-bit sign fields (the eighth sign of each
-// 8-weight sub-block is the even parity of the seven) and the group scale. The upload rewrites it
-// with all 32 signs laid out in pairs: the signs of weights 2j and 2j + 1 of sub-block s are bits
-// 4 s + j and 4 s + j + 16. One shift then puts a pair's two signs on the sign bits (15, 31) of an
-// fp16x2 register, which is what the tensor-core decoders flip. The scale moves to `scales` (4
-// more bytes per 256 weights: 70 instead of 66).
+// IQ2_XXS / IQ3_XXS sign word. The ggml group word holds four 7-bit sign fields (the eighth sign
+// of each 8-weight sub-block is the even parity of the seven) and the group scale. The upload
+// rewrites it with all 32 signs laid out in pairs: the signs of weights 2j and 2j + 1 of sub-block
+// s are bits 4 s + j and 4 s + j + 16. One shift then puts a pair's two signs on the sign bits
+// (15, 31) of an fp16x2 register, which is what the tensor-core decoders flip. The scale moves to
+// `scales` (4 more bytes per 256 weights: 70 instead of 66 for IQ2_XXS, 102 instead of 98 for
+// IQ3_XXS).
 #pragma once
 
 #include <cuda.h>
@@ -71,7 +72,7 @@ struct DevMat {
     uint32_t bpr;  // blocks per row
     const uint16_t* d;
     const uint8_t* body;
-    const uint32_t* scales;  // IQ2_XXS group scales (one u32 per block, tiled like d); else null
+    const uint32_t* scales;  // IQ2_XXS / IQ3_XXS group scales (one u32 per block, tiled like d); else null
     // Power of two applied to the weights when the prefill kernels decode them to fp16: chosen at
     // upload from the largest block scale so that every |weight| * pscale stays below 2^14 (no
     // overflow) while small weights stay clear of the fp16 subnormal range.
@@ -90,11 +91,9 @@ __device__ __forceinline__ float h2f(uint16_t bits) {
     return __half2float(__ushort_as_half(bits));
 }
 
-// The 8-bit sign mask of one 8-weight sub-block: seven stored bits plus an even-parity bit
-// (ggml_quantization.cpp:268-271 and :354-357).
-__device__ __forceinline__ uint32_t iq_signs(uint32_t aux, int sub) {
-    const uint32_t s7 = (aux >> (7 * sub)) & 127u;
-    return s7 | ((__popc(s7) & 1u) << 7);
+// One bit per device storage type, for sets of types.
+__host__ __device__ constexpr uint32_t fmt_bit(uint32_t type) {
+    return type == kTypeQ8_0 ? 1u : type == kTypeIq2Xxs ? 2u : type == kTypeIq3Xxs ? 4u : type == kTypeIq1S ? 8u : 0u;
 }
 
 // ---- bit-exact block decoders (one 32-weight group at a time) ------------------------------
@@ -152,18 +151,19 @@ __device__ __forceinline__ void decode_group_iq2_xxs(float d, const uint8_t* bod
     }
 }
 
-// decode_iq3_xxs_block, ggml_quantization.cpp:336-379
-__device__ __forceinline__ void decode_group_iq3_xxs(float d, const uint8_t* body, int g,
+// decode_iq3_xxs_block, ggml_quantization.cpp:336-379 (device layout: grid indices and the pair
+// sign word in the body, the 4-bit group scale `ls4` from the scales word)
+__device__ __forceinline__ void decode_group_iq3_xxs(float d, const uint8_t* body, int g, uint32_t ls4,
                                                      const uint32_t* grid, float* w) {
-    const uint32_t aux = *reinterpret_cast<const uint32_t*>(body + 64 + g * 4);
+    const uint32_t sw = *reinterpret_cast<const uint32_t*>(body + 64 + g * 4);
     const uint2 idx8 = *reinterpret_cast<const uint2*>(body + g * 8);
-    const float ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
+    const float ls = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)ls4)), 0.5f);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t word = j < 2 ? idx8.x : idx8.y;
         const uint32_t g1 = grid[(word >> (16 * (j & 1))) & 0xffu];
         const uint32_t g2 = grid[(word >> (16 * (j & 1) + 8)) & 0xffu];
-        const uint32_t signs = iq_signs(aux, j);
+        const uint32_t signs = iq2_sub_signs(sw, j);
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
             const float p1 = __fmul_rn(ls, (float)((g1 >> (8 * l)) & 0xffu));
@@ -216,8 +216,9 @@ struct MoeParams {
     float shared_limit;
     uint32_t vocab;
     int has_shared;
-    int has_legacy;          // some expert uses a format the CUDA-core kernels serve (IQ3_XXS, IQ1_S)
-    int has_mma;             // some expert uses a format the tensor-core kernels serve (IQ2_XXS, Q8_0)
+    int has_legacy;          // some expert uses a format the prefill GEMMs do not serve (IQ3_XXS, IQ1_S)
+    int has_mma;             // some expert uses a format the prefill GEMMs serve (IQ2_XXS, Q8_0)
+    uint32_t fmt_gu, fmt_dn; // storage types present among the W1/W3 and the W2 matrices (fmt_bit)
     // weights
     const double* router;    // [E x H], the f32 router weights widened to f64 at layer creation
     const float* bias;       // [E]

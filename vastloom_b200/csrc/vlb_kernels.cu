@@ -57,7 +57,8 @@ __global__ void dequant_kernel(DevMat m, Grids g, float* __restrict__ out) {
             decode_group_iq2_xxs(d, m.body + blk_index(m.bpr, row, blk) * 64u, gg,
                                  (m.scales[blk_index(m.bpr, row, blk)] >> (4u * gg)) & 15u, g.iq2xxs, w);
         else if (m.type == kTypeIq3Xxs)
-            decode_group_iq3_xxs(d, m.body + blk_index(m.bpr, row, blk) * 96u, gg, g.iq3xxs, w);
+            decode_group_iq3_xxs(d, m.body + blk_index(m.bpr, row, blk) * 96u, gg,
+                                 (m.scales[blk_index(m.bpr, row, blk)] >> (4u * gg)) & 15u, g.iq3xxs, w);
         else
             decode_group_iq1_s(d, m.body + blk_index(m.bpr, row, blk) * 48u, gg, g.iq1s, w);
     }
@@ -774,10 +775,9 @@ __device__ __forceinline__ void down_dispatch(const MoeParams& p, const DevMat& 
     }
 }
 
-__device__ __forceinline__ bool mma_type(uint32_t t) { return t == kTypeIq2Xxs || t == kTypeQ8_0; }
-
+// skip: fmt_bit set of the storage types another kernel of the phase serves.
 template <bool GATEUP>
-__global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
+__global__ void __launch_bounds__(256) expert_kernel(MoeParams p, uint32_t skip) {
     extern __shared__ __align__(16) unsigned char smem[];
     const GridSmem gs = stage_grids(p.grids, smem);
     float* xs = reinterpret_cast<float*>(smem + kGridSmemBytes);
@@ -793,7 +793,7 @@ __global__ void __launch_bounds__(256) expert_kernel(MoeParams p) {
     for (uint64_t item = begin; item < end; ++item) {
         const uint32_t ui = (uint32_t)(item / tiles), tile = (uint32_t)(item % tiles);
         const Unit u = p.units[ui];
-        if (mma_type(p.mats[(GATEUP ? 0u : 2u * (p.E + 1)) + u.expert].type)) continue;
+        if (skip & fmt_bit(p.mats[(GATEUP ? 0u : 2u * (p.E + 1)) + u.expert].type)) continue;
         if (ui != staged) {
             const float* rows[kUnitTokens];
 #pragma unroll
@@ -1128,23 +1128,28 @@ cudaError_t launch_moe(const MoeParams& p_in, cudaStream_t s, cudaEvent_t* ev) {
     const int ctas_per_sm = 2;
     const unsigned grid = (unsigned)(num_sms() * ctas_per_sm);
     if (p.prefill && (e = launch_prefill_plan(p, s)) != cudaSuccess) return e;
+    // which kernel serves which storage type: the prefill GEMMs take IQ2_XXS and Q8_0; the decode
+    // kernels take Q8_0 and one IQ type per phase (decode_ring_types); the CUDA-core kernels the rest
+    const uint32_t pf_types = fmt_bit(kTypeIq2Xxs) | fmt_bit(kTypeQ8_0);
+    const uint32_t gu_fast = p.prefill ? pf_types : decode_ring_types(p, true);
+    const uint32_t dn_fast = p.prefill ? pf_types : decode_ring_types(p, false);
     const size_t gu_smem = kGridSmemBytes + (size_t)kUnitTokens * p.H * sizeof(float);
-    if (p.has_legacy && (e = set_smem_once(expert_kernel<true>, gu_smem)) != cudaSuccess) return e;
-    if (p.has_legacy) expert_kernel<true><<<grid, 256, gu_smem, s>>>(p);
+    if ((p.fmt_gu & ~gu_fast) && (e = set_smem_once(expert_kernel<true>, gu_smem)) != cudaSuccess) return e;
+    if (p.fmt_gu & ~gu_fast) expert_kernel<true><<<grid, 256, gu_smem, s>>>(p, gu_fast);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (p.has_mma && p.prefill) {
+    if ((p.fmt_gu & gu_fast) && p.prefill) {
         if ((e = launch_prefill_gateup(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
-    } else if (p.has_mma) {
+    } else if (p.fmt_gu & gu_fast) {
         if ((e = launch_decode_gateup(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     }
     if (ev) cudaEventRecord(ev[3], s);
     const size_t dn_smem = kGridSmemBytes + (size_t)kUnitTokens * p.I * sizeof(float);
-    if (p.has_legacy && (e = set_smem_once(expert_kernel<false>, dn_smem)) != cudaSuccess) return e;
-    if (p.has_legacy) expert_kernel<false><<<grid, 256, dn_smem, s>>>(p);
+    if ((p.fmt_dn & ~dn_fast) && (e = set_smem_once(expert_kernel<false>, dn_smem)) != cudaSuccess) return e;
+    if (p.fmt_dn & ~dn_fast) expert_kernel<false><<<grid, 256, dn_smem, s>>>(p, dn_fast);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (p.has_mma && p.prefill) {
+    if ((p.fmt_dn & dn_fast) && p.prefill) {
         if ((e = launch_prefill_down(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
-    } else if (p.has_mma) {
+    } else if (p.fmt_dn & dn_fast) {
         if ((e = launch_decode_down(p, (unsigned)num_sms(), s)) != cudaSuccess) return e;
     }
     if (ev) cudaEventRecord(ev[4], s);

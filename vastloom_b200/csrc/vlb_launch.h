@@ -40,6 +40,9 @@ cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s);
 // Decode path (vlb_decode.cu): IQ2_XXS / Q8_0 expert products on mma.sync fed by a bulk-copy ring,
 // one CTA per SM.
 cudaError_t launch_decode_gateup(const MoeParams& p, unsigned n_sms, cudaStream_t s);
+// fmt_bit set of the storage types the decode kernel of a phase serves: Q8_0 and the phase's IQ
+// type (IQ2_XXS before IQ1_S before IQ3_XXS when several are present) if its stage carve fits
+uint32_t decode_ring_types(const MoeParams& p, bool gateup);
 cudaError_t launch_decode_down(const MoeParams& p, unsigned n_sms, cudaStream_t s);
 // Expert-parallel helpers (vlb_ep.cu)
 cudaError_t launch_ep_validate(const uint32_t* idx, size_t n, uint32_t E, uint32_t* flag, cudaStream_t s);

@@ -142,6 +142,92 @@ __device__ __forceinline__ void decode_iq2_sub_lane(uint32_t tab_lane, uint32_t 
     v[3] = flip_signs(hmul2(g.w, kk), sw << (12u - 4u * sub));
 }
 
+// IQ1_S grid as fp16: entry e = its 8 values q in {-1, 0, 1} (16 bytes), one copy (2048 entries
+// fill 32 KB).
+__device__ __forceinline__ void build_iq1s_table(uint4* tab, const uint64_t* grid) {
+    if (!grid) return;
+    for (uint32_t i = threadIdx.x; i < 2048u; i += blockDim.x) {
+        const uint64_t gv = grid[i];
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half a = __int2half_rn((int)(int8_t)(uint8_t)(gv >> (16 * j)));
+            const __half b = __int2half_rn((int)(int8_t)(uint8_t)(gv >> (16 * j + 8)));
+            w[j] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+        }
+        tab[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// IQ3_XXS grid as fp16: entry e = its 4 magnitudes (8 bytes), replicated 16 times so that replica
+// r sits at byte 8 r of the entry's 128-byte row: the 16 lanes of an 8-byte load phase read
+// replicas lane % 16, free of bank conflicts.
+__device__ __forceinline__ void build_iq3_table(uint2* tab, const uint32_t* grid) {
+    if (!grid) return;
+    for (uint32_t i = threadIdx.x; i < 256u * 16u; i += blockDim.x) {
+        const uint32_t gv = grid[i >> 4];
+        uint32_t w[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const __half a = __uint2half_rn((gv >> (16 * j)) & 0xffu);
+            const __half b = __uint2half_rn((gv >> (16 * j + 8)) & 0xffu);
+            w[j] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+        }
+        tab[i] = make_uint2(w[0], w[1]);
+    }
+}
+
+// IQ1_S sub-block `sub` of one row: 11-bit grid index = qs byte `sub` | 3 bits of the group's qh
+// word, the 8 grid values q from the table, A = q * (2s + 1) + delta * (2s + 1) (kk, dk: those
+// factors as fp16 pairs) - an exact fp16 (at most 8 significant bits), the reference's weight
+// ls * (q + delta) without the fp16 block scale d.
+__device__ __forceinline__ void decode_iq1_sub(uint32_t tab, uint32_t qs4, uint32_t h, uint32_t sub, uint32_t kk,
+                                               uint32_t dk, uint32_t (&v)[4]) {
+    const uint32_t idx = prmt(qs4, 0u, 0x4440u | sub) | (((h >> (3u * sub)) & 7u) << 8);
+    uint32_t addr;
+    asm("mad.lo.u32 %0, %1, 16, %2;" : "=r"(addr) : "r"(idx), "r"(tab));
+    uint4 g;
+    asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(g.x), "=r"(g.y), "=r"(g.z), "=r"(g.w) : "r"(addr));
+    v[0] = hfma2(g.x, kk, dk);
+    v[1] = hfma2(g.y, kk, dk);
+    v[2] = hfma2(g.z, kk, dk);
+    v[3] = hfma2(g.w, kk, dk);
+}
+
+// (2s + 1, 2s + 1) and (delta (2s + 1), delta (2s + 1)) as fp16 pairs from an IQ1_S group word h
+// (s = bits 12-14, delta = -1/8 when bit 15 is set, else +1/8): exact.
+__device__ __forceinline__ void iq1_group_factors(uint32_t h, uint32_t& kk, uint32_t& dk) {
+    const uint32_t n = 2u * ((h >> 12) & 7u) + 1u;
+    kk = hsub2((n * 0x10001u) | 0x64006400u, 0x64006400u);
+    dk = hmul2(kk, (h & 0x8000u) ? 0xB000B000u : 0x30003000u);
+}
+
+// IQ3_XXS sub-block `sub` of one row: two grid indices (bytes 2 (sub & 1), 2 (sub & 1) + 1 of
+// `word`, the group's index word holding this sub-block), 4 magnitudes each from the replicated
+// table, times the group factor kk = (0.5 + s) / 2, signs from the pair-layout sign word `sw` as
+// for IQ2_XXS. A = sign * (0.5 + s) / 2 * m is an exact fp16 (at most 10 significant bits).
+__device__ __forceinline__ void decode_iq3_sub(uint32_t tab_lane, uint32_t word, uint32_t sw, uint32_t sub,
+                                               uint32_t kk, uint32_t (&v)[4]) {
+    const uint32_t i0 = prmt(word, 0u, 0x4440u | (2u * (sub & 1u)));
+    const uint32_t i1 = prmt(word, 0u, 0x4440u | (2u * (sub & 1u) + 1u));
+    uint32_t a0, a1;
+    asm("mad.lo.u32 %0, %1, 128, %2;" : "=r"(a0) : "r"(i0), "r"(tab_lane));
+    asm("mad.lo.u32 %0, %1, 128, %2;" : "=r"(a1) : "r"(i1), "r"(tab_lane));
+    uint2 A, B;
+    asm("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(A.x), "=r"(A.y) : "r"(a0));
+    asm("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(B.x), "=r"(B.y) : "r"(a1));
+    v[0] = flip_signs(hmul2(A.x, kk), sw << (15u - 4u * sub));
+    v[1] = flip_signs(hmul2(A.y, kk), sw << (14u - 4u * sub));
+    v[2] = flip_signs(hmul2(B.x, kk), sw << (13u - 4u * sub));
+    v[3] = flip_signs(hmul2(B.y, kk), sw << (12u - 4u * sub));
+}
+
+// (0.5 + s)/2 for the IQ3_XXS group scale s, as a pair of equal fp16 values (exact):
+// fp16(1024 + s) * 0.5 - 511.75.
+__device__ __forceinline__ uint32_t iq3_group_scale_h2(uint32_t s4) {
+    return hfma2((s4 * 0x10001u) | 0x64006400u, 0x38003800u, 0xDFFFDFFFu);
+}
+
 // (0.5 + s)/4 for the 4-bit group scale s, as a pair of equal fp16 values (exact):
 // fp16(1024 + s) is built from its bits, then (1024 + s) / 4 - 255.875 rounds exactly.
 __device__ __forceinline__ uint32_t group_scale_h2(uint32_t s4) {
