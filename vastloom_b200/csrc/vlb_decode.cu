@@ -604,7 +604,7 @@ __device__ __forceinline__ void dc_iq3_stage(uint32_t st_addr, uint32_t s0, uint
 // arrives last adds the splits' partials in split order (the same sum whatever CTA ran which
 // split) and runs the epilogue, and resets the counter. Returns true for that last warp, with acc
 // holding the full sums.
-__device__ __forceinline__ bool dc_join_splits(const MoeParams& p, uint32_t item, uint32_t splits, uint32_t warp,
+__device__ __noinline__ bool dc_join_splits(const MoeParams& p, uint32_t item, uint32_t splits, uint32_t warp,
                                                uint32_t lane, float (&acc)[2][4]) {
     const uint32_t rg = item / splits;
     float4* part = reinterpret_cast<float4*>(p.split_part);
@@ -632,12 +632,13 @@ __device__ __forceinline__ bool dc_join_splits(const MoeParams& p, uint32_t item
     return true;
 }
 
-// tfmt: the IQ storage type whose codebook the CTA holds (IQ2_XXS, IQ1_S or IQ3_XXS); items of
-// that type and of Q8_0 run here, any other type on the CUDA-core kernels.
-template <bool GATEUP, uint32_t BODY>
+// TFMT: the IQ storage type whose codebook the CTA holds (IQ2_XXS, IQ1_S or IQ3_XXS); items of
+// that type and of Q8_0 run here, any other type on the CUDA-core kernels. One instance per type
+// keeps each instance's register allocation to its own decoder.
+template <bool GATEUP, uint32_t BODY, uint32_t TFMT>
 __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __grid_constant__ MoeParams p,
-                                                                       uint32_t chunk, uint32_t splits,
-                                                                       uint32_t tfmt) {
+                                                                       uint32_t chunk, uint32_t splits) {
+    constexpr uint32_t tfmt = TFMT;
     using Lay = DcL<BODY>;
     extern __shared__ __align__(1024) unsigned char smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -647,9 +648,9 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     uint64_t* empty = full + kDcRing;
     const uint32_t K = GATEUP ? p.H : p.I;
     unsigned char* xs = smem + Lay::XsOff;
-    if (tfmt == kTypeIq2Xxs) mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
-    else if (tfmt == kTypeIq1S) mma::build_iq1s_table(reinterpret_cast<uint4*>(smem), p.grids.iq1s);
-    else if (tfmt == kTypeIq3Xxs) mma::build_iq3_table(reinterpret_cast<uint2*>(smem), p.grids.iq3xxs);
+    if constexpr (TFMT == kTypeIq2Xxs) mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
+    if constexpr (TFMT == kTypeIq1S) mma::build_iq1s_table(reinterpret_cast<uint4*>(smem), p.grids.iq1s);
+    if constexpr (TFMT == kTypeIq3Xxs) mma::build_iq3_table(reinterpret_cast<uint2*>(smem), p.grids.iq3xxs);
     for (uint32_t i = threadIdx.x; i < dc_xs_bytes(K) / 16u; i += blockDim.x)
         reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
@@ -734,12 +735,13 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
             for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
         }
         const uint32_t st_addr = tc::smem_u32(smem + Lay::RingOff + slot * Lay::Stage);
-        if (it.fmt == kTypeIq2Xxs) {
-            dc_iq2_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
-        } else if (it.fmt == kTypeIq1S) {
-            dc_iq1_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab, empty + slot, acc);
-        } else if (it.fmt == kTypeIq3Xxs) {
-            dc_iq3_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
+        if (it.fmt != kTypeQ8_0) {  // the CTA's IQ type (the loader sends no other)
+            if constexpr (TFMT == kTypeIq2Xxs)
+                dc_iq2_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
+            if constexpr (TFMT == kTypeIq1S)
+                dc_iq1_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab, empty + slot, acc);
+            if constexpr (TFMT == kTypeIq3Xxs)
+                dc_iq3_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
         } else {
             const uint32_t blk0 = 2u * h.y;
             const uint32_t nblk = blk0 + 1u < it.bpr ? 2u : 1u;
@@ -815,8 +817,8 @@ static DcChoice dc_choice(const MoeParams& p, bool gateup) {
     return c;
 }
 
-template <bool GATEUP, uint32_t BODY>
-cudaError_t launch_decode_carve(const MoeParams& p, unsigned n_sms, uint32_t tfmt, size_t smem, cudaStream_t s) {
+template <bool GATEUP, uint32_t BODY, uint32_t TFMT>
+cudaError_t launch_decode_carve(const MoeParams& p, unsigned n_sms, size_t smem, cudaStream_t s) {
     static std::mutex mu;
     static std::vector<size_t> configured;
     int dev = 0;
@@ -830,7 +832,7 @@ cudaError_t launch_decode_carve(const MoeParams& p, unsigned n_sms, uint32_t tfm
             if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
                 return e;
             if (smem > (size_t)optin) return cudaErrorInvalidValue;  // hidden size beyond this kernel's staging
-            if ((e = cudaFuncSetAttribute(decode_experts_kernel<GATEUP, BODY>,
+            if ((e = cudaFuncSetAttribute(decode_experts_kernel<GATEUP, BODY, TFMT>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
                 return e;
             configured[(size_t)dev] = smem;
@@ -857,15 +859,17 @@ cudaError_t launch_decode_carve(const MoeParams& p, unsigned n_sms, uint32_t tfm
     }
     uint32_t chunk = (uint32_t)((est * splits + 4ull * n_sms - 1) / (4ull * n_sms));
     chunk = chunk < 1u ? 1u : (chunk > kDcMaxChunk ? kDcMaxChunk : chunk);
-    decode_experts_kernel<GATEUP, BODY><<<n_sms, kDcThreads, smem, s>>>(p, chunk, splits, tfmt);
+    decode_experts_kernel<GATEUP, BODY, TFMT><<<n_sms, kDcThreads, smem, s>>>(p, chunk, splits);
     return cudaGetLastError();
 }
 
 template <bool GATEUP>
 cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
     const DcChoice c = dc_choice(p, GATEUP);
-    if (c.large) return launch_decode_carve<GATEUP, kDcBodyLarge>(p, n_sms, c.tfmt, c.smem, s);
-    return launch_decode_carve<GATEUP, kDcBodySmall>(p, n_sms, c.tfmt, c.smem, s);
+    if (c.tfmt == kTypeIq3Xxs) return launch_decode_carve<GATEUP, kDcBodyLarge, kTypeIq3Xxs>(p, n_sms, c.smem, s);
+    if (c.tfmt == kTypeIq1S) return launch_decode_carve<GATEUP, kDcBodySmall, kTypeIq1S>(p, n_sms, c.smem, s);
+    // IQ2_XXS, or Q8_0 alone (the IQ2_XXS instance builds no table without its codebook in use)
+    return launch_decode_carve<GATEUP, kDcBodySmall, kTypeIq2Xxs>(p, n_sms, c.smem, s);
 }
 
 }  // namespace

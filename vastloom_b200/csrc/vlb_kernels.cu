@@ -277,15 +277,16 @@ __global__ void score_kernel(const float* __restrict__ logits, size_t n, int sco
 // deepseek_v4_reference.cpp:223-307; OLMoE softmax router, olmoe_runtime.cpp:1120-1137; Qwen
 // router, qwen3_8_flash_next_reference.cpp:1186-1239). Selection key: learned = score + bias (f32
 // add), OLMoE softmax = f32 probability, Qwen softmax = f64 probability; larger first, ties to the
-// lower expert id (std::partial_sort / std::sort with that strict order). Keys are held as f64
-// (every f32 key converts exactly, so the order and the ties are the f32 ones). E <= 32 *
-// kMaxPerLane.
+// lower expert id (std::partial_sort / std::sort with that strict order). KT is the key type: f32
+// for the f32-keyed routers, f64 for the Qwen router (a one-warp selection in f64 costs several
+// times the f32 one on this GPU's FP64 pipe). E <= 32 * kMaxPerLane.
 constexpr int kMaxPerLane = 16;  // E <= 512
 
 __device__ __forceinline__ bool f64_softmax(int score) {
     return score == VLB_SCORE_SOFTMAX_F64 || score == VLB_SCORE_SOFTMAX_F64_NORM;
 }
 
+template <typename KT>
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ scores,
                                                     const float* __restrict__ bias,
                                                     const uint32_t* __restrict__ token_ids,
@@ -299,8 +300,8 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
     const uint32_t t = blockIdx.x * 8u + warp;
     if (t >= T) return;
     const float* s = scores + (size_t)t * E;
-    double key[kMaxPerLane];
-    double val[kMaxPerLane];
+    KT key[kMaxPerLane];
+    KT val[kMaxPerLane];
     if (score == VLB_SCORE_SOFTMAX) {
         // p_e = float exp of (logit - max); double denominator; float division (no renorm)
         float mx = -INFINITY;
@@ -320,8 +321,8 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
         const float fden = (float)den;
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
-            val[i] = (double)__fdiv_rn(p[i], fden);
-            key[i] = lane + 32u * i < E ? val[i] : -INFINITY;
+            val[i] = (KT)__fdiv_rn(p[i], fden);
+            key[i] = lane + 32u * i < E ? val[i] : (KT)-INFINITY;
         }
     } else if (f64_softmax(score)) {
         // probs[e] = exp(double(l_e) - max) in double, summed in expert order (the reference's
@@ -330,38 +331,40 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
         for (uint32_t e = lane; e < E; e += 32u) mx = fmax(mx, (double)s[e]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        double pv[kMaxPerLane];
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
             const uint32_t e = lane + 32u * i;
-            val[i] = e < E ? exp(__dsub_rn((double)s[e], mx)) : 0.0;
+            pv[i] = e < E ? exp(__dsub_rn((double)s[e], mx)) : 0.0;
         }
         double sum = 0.0;
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
             if (32u * (uint32_t)i >= E) break;
-            for (uint32_t l = 0; l < 32u && 32u * i + l < E; ++l) sum = __dadd_rn(sum, __shfl_sync(0xffffffffu, val[i], l));
+            for (uint32_t l = 0; l < 32u && 32u * i + l < E; ++l) sum = __dadd_rn(sum, __shfl_sync(0xffffffffu, pv[i], l));
         }
         const double inv = sum > 0.0 ? 1.0 / sum : 0.0;
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
-            val[i] = __dmul_rn(val[i], inv);
-            key[i] = lane + 32u * i < E ? val[i] : -INFINITY;
+            val[i] = (KT)__dmul_rn(pv[i], inv);
+            key[i] = lane + 32u * i < E ? val[i] : (KT)-INFINITY;
         }
     } else {
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
             const uint32_t e = lane + 32u * i;
             if (e < E) {
-                val[i] = (double)s[e];
-                key[i] = hash_routing ? 0.0 : (double)__fadd_rn(s[e], bias ? bias[e] : 0.f);
+                val[i] = (KT)s[e];
+                key[i] = hash_routing ? (KT)0 : (KT)__fadd_rn(s[e], bias ? bias[e] : 0.f);
             } else {
-                val[i] = 0.0;
-                key[i] = -INFINITY;
+                val[i] = (KT)0;
+                key[i] = (KT)-INFINITY;
             }
         }
     }
-    uint32_t sel[16];
-    double selv[16];
+    // slot j's expert and value end up in lane j (k <= 16 <= 32): no per-thread arrays
+    uint32_t msel = 0;
+    KT mval = (KT)0;
     if (hash_routing) {
         const uint32_t tok = token_ids[t];
         if (tok >= vocab) {
@@ -374,19 +377,22 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
                 if (lane == 0) atomicOr(error_flag, 2u);
                 return;
             }
-            sel[j] = e;
             // fetch val of expert e from its owner lane
             const uint32_t owner = e & 31u, slot = e >> 5;
-            double mine = 0.0;
+            KT mine = (KT)0;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) if ((uint32_t)i == slot) mine = val[i];
-            selv[j] = __shfl_sync(0xffffffffu, mine, owner);
+            const KT v = __shfl_sync(0xffffffffu, mine, owner);
+            if (lane == j) {
+                msel = e;
+                mval = v;
+            }
         }
     } else {
         uint32_t removed = 0;  // bit i: this lane's entry i has been selected already
         for (uint32_t j = 0; j < k; ++j) {
             // lane-local best: larger key, ties to the lower id (= lower i within a lane)
-            double bk = 0.0;
+            KT bk = (KT)0;
             uint32_t be = 0xffffffffu;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) {
@@ -398,49 +404,43 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ sc
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
-                const double ok = __shfl_xor_sync(0xffffffffu, bk, o);
+                const KT ok = __shfl_xor_sync(0xffffffffu, bk, o);
                 const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, o);
                 if (oe != 0xffffffffu && (be == 0xffffffffu || ok > bk || (ok == bk && oe < be))) {
                     bk = ok;
                     be = oe;
                 }
             }
-            sel[j] = be;
             const uint32_t owner = be & 31u, slot = be >> 5;
-            double mine = 0.0;
+            KT mine = (KT)0;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) if ((uint32_t)i == slot) mine = val[i];
-            selv[j] = __shfl_sync(0xffffffffu, mine, owner);
+            const KT v = __shfl_sync(0xffffffffu, mine, owner);
             if (lane == owner) removed |= 1u << slot;
+            if (lane == j) {
+                msel = be;
+                mval = v;
+            }
         }
     }
-    if (lane == 0) {
+    // the selected values' sum in slot order (the reference's sequential loop), every lane alike
+    double sum = 0.0;
+    for (uint32_t j = 0; j < k; ++j) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, mval, j));
+    if (lane < k) {
+        const size_t at = (size_t)t * k + lane;
+        idx[at] = msel;
         if (score == VLB_SCORE_SOFTMAX) {
-            for (uint32_t j = 0; j < k; ++j) {
-                idx[(size_t)t * k + j] = sel[j];
-                weights[(size_t)t * k + j] = (float)selv[j];
-            }
+            weights[at] = (float)mval;
         } else if (f64_softmax(score)) {
-            // weights = f32(prob); with norm_topk_prob each is rescaled by 1 / (the rank-order
-            // f64 sum of the selected probabilities)
-            double top = 0.0;
-            for (uint32_t j = 0; j < k; ++j) top = __dadd_rn(top, selv[j]);
-            const bool norm = score == VLB_SCORE_SOFTMAX_F64_NORM && top > 0.0;
-            const double sc = norm ? 1.0 / top : 1.0;
-            for (uint32_t j = 0; j < k; ++j) {
-                idx[(size_t)t * k + j] = sel[j];
-                const float w = (float)selv[j];
-                weights[(size_t)t * k + j] = norm ? (float)__dmul_rn((double)w, sc) : w;
-            }
+            // weights = f32(prob); with norm_topk_prob each is rescaled by 1 / (the rank-order f64
+            // sum of the selected probabilities)
+            const bool norm = score == VLB_SCORE_SOFTMAX_F64_NORM && sum > 0.0;
+            const float w = (float)mval;
+            weights[at] = norm ? (float)__dmul_rn((double)w, 1.0 / sum) : w;
         } else {
             // route_from_indices, deepseek_v4_reference.cpp:80-121
-            double sum = 0.0;
-            for (uint32_t j = 0; j < k; ++j) sum += selv[j];
-            if (!(sum > 0.0) || isinf(sum)) atomicOr(error_flag, 4u);
-            for (uint32_t j = 0; j < k; ++j) {
-                idx[(size_t)t * k + j] = sel[j];
-                weights[(size_t)t * k + j] = (float)(selv[j] / sum * (double)route_scale);
-            }
+            if (lane == 0 && (!(sum > 0.0) || isinf(sum))) atomicOr(error_flag, 4u);
+            weights[at] = (float)((double)mval / sum * (double)route_scale);
         }
     }
 }
@@ -1058,9 +1058,12 @@ cudaError_t launch_route(const float* scores, const float* bias, const uint32_t*
                          const uint32_t* tid2eid, uint32_t vocab, uint32_t T, uint32_t E,
                          uint32_t k, int score, int hash_routing, float route_scale,
                          uint32_t* idx, float* weights, uint32_t* error_flag, cudaStream_t s) {
-    route_kernel<<<(T + 7) / 8, 256, 0, s>>>(scores, bias, token_ids, tid2eid, vocab, T, E, k,
-                                             score, hash_routing, route_scale, idx, weights,
-                                             error_flag);
+    if (score == VLB_SCORE_SOFTMAX_F64 || score == VLB_SCORE_SOFTMAX_F64_NORM)
+        route_kernel<double><<<(T + 7) / 8, 256, 0, s>>>(scores, bias, token_ids, tid2eid, vocab, T, E, k, score,
+                                                         hash_routing, route_scale, idx, weights, error_flag);
+    else
+        route_kernel<float><<<(T + 7) / 8, 256, 0, s>>>(scores, bias, token_ids, tid2eid, vocab, T, E, k, score,
+                                                        hash_routing, route_scale, idx, weights, error_flag);
     return cudaGetLastError();
 }
 
