@@ -346,21 +346,34 @@ def run_ep(args, dev, rank, world, local_rank):
     load_contig = counts.cpu().numpy().reshape(world, epr).sum(axis=1)
     load_bal = np.zeros(world)
     np.add.at(load_bal, slots // epr, counts.cpu().numpy())
-    layer, ops = make_device_layer(dev, W, comm, max_tokens=T, slots=slots)
+    native = args.ep_driver == "native"
+    if native:
+        # the library's C++ driver with its own NCCL communicator (id made by rank 0, shared through
+        # the process group); torch.distributed carries only the set-up and the timing reductions
+        from vastloom_b200.ep import NativeEpComm, NativeEpLayer, native_unique_id
+
+        uid = [native_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        ncomm = NativeEpComm(dev, uid[0], rank, world, timeout_ms=120_000)
+        layer = NativeEpLayer(dev, ncomm, W, max_tokens=T, slots=slots)
+        lib_stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", torch.cuda.current_device()))
+    else:
+        layer, ops = make_device_layer(dev, W, comm, max_tokens=T, slots=slots)
+        lib_stream = ops.stream
     xd = torch.from_numpy(x_host).cuda()
     ld = torch.from_numpy(logits_host).cuda()
     for _ in range(args.warmup):
         layer.forward(xd, ld, T)
     torch.cuda.synchronize()
     torch.distributed.barrier()
-    steps = args.ep_steps or max(3, min(args.steps, 20))
+    steps = args.ep_steps or args.steps
     times, experts_s = [], []
     for _ in range(steps):
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
-        start.record(ops.stream)
+        start.record(lib_stream)
         layer.forward(xd, ld, T)
-        end.record(ops.stream)
+        end.record(lib_stream)
         torch.cuda.synchronize()
         times.append(start.elapsed_time(end))
         experts_s.append(layer.last["experts_s"])
@@ -385,6 +398,8 @@ def run_ep(args, dev, rank, world, local_rank):
                    "top_k": spec.top_k, "tokens_per_gpu": T, "zipf_s": spec.zipf_s,
                    "exchange": "NCCL all-to-all: fp16 rows + (expert, weight, max|x|) words out, fp16 results "
                                "with a per-row power-of-two scale back",
+                   "driver": ("C++ (vlb_ep_forward_device, the library's own NCCL communicator)" if native
+                              else "Python orchestration over torch.distributed"),
                    "placement": "balanced by the measured expert load (longest-processing-time greedy, E/N per GPU)",
                    "expert_path": "tensor-core prefill kernels on the received rows"},
         "expected_rows_per_rank": {"contiguous_max": int(load_contig.max()), "balanced_max": int(load_bal.max()),
@@ -398,7 +413,11 @@ def run_ep(args, dev, rank, world, local_rank):
                   "against": "the same tokens through one GPU holding all experts, exact decode path"},
     }
     assert check_max <= 4e-3, f"expert-parallel output differs from the single-GPU layer: {check_max}"
-    ops.close()
+    if native:
+        layer.close()
+        ncomm.close()
+    else:
+        ops.close()
     if created_group:
         torch.distributed.destroy_process_group()
     return res
@@ -865,7 +884,9 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the decode objects of configurations 0, 1 (T = 1, 8) and 2 (chain)")
     ap.add_argument("--ep-tokens", type=int, default=8192)
-    ap.add_argument("--ep-steps", type=int, default=0, help="0: min(--steps, 20), at least 3")
+    ap.add_argument("--ep-steps", type=int, default=0, help="0: --steps")
+    ap.add_argument("--ep-driver", default="native", choices=["native", "torch"],
+                    help="expert-parallel host side: the library's C++ driver or the Python orchestration")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

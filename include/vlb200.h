@@ -298,6 +298,81 @@ int vlb_ep_combine_device(vlb_handle* h, const float* y_rows_dev, const uint32_t
                           uint32_t T, uint32_t k, const float* shared_rows_dev, uint32_t H,
                           float* out_dev, void* stream);
 
+/* ---- expert-parallel driver over NCCL -------------------------------------------------------
+ * The whole configuration-4 step of one rank in one call, for a C or C++ host with one process
+ * (or host thread) and one handle per GPU. Communicator set-up from an ncclUniqueId that rank 0
+ * creates and the caller distributes (MPI, a key-value store, a file); then per step: route, plan,
+ * counts all-to-all, half-row dispatch, the rank's expert group (its routed experts and the shared
+ * expert) on the tensor-core path, fp16 results back, combine - grouped ncclSend/ncclRecv on the
+ * step's stream. NCCL (>= 2.18) is loaded when first needed: $VLB_NCCL_LIBRARY, else
+ * libnccl.so.2 (the copy the process has already loaded, if any); without it these entry points
+ * return VLB_ERR_UNSUPPORTED and the rest of the library is unaffected. A process holds one
+ * libnccl.so.2: one that also uses another NCCL user (PyTorch) loads that user first, so that the
+ * driver binds its copy.
+ *
+ * Waits are bounded: the communicator is non-blocking and every host wait (set-up, the count
+ * read-back, the end of a step) gives up after timeout_ms, aborts the communicator (ending this
+ * rank's NCCL kernels) and returns VLB_ERR_IO_ERROR naming the exchange ("counts", "dispatch",
+ * "return"). A layer whose exchange failed refuses every later forward; rebuild the communicator
+ * and the layer. Failure messages are read with vlb_thread_error. The reference has no
+ * expert-parallel exchange on this path, so none of these has a reference counterpart. */
+#define VLB_EP_UNIQUE_ID_BYTES 128
+typedef struct vlb_ep_comm vlb_ep_comm;
+typedef struct vlb_ep_layer vlb_ep_layer;
+
+/* NCCL's version code (e.g. 22703) of the library the driver loaded. */
+int vlb_ep_nccl_version(int* version);
+/* ncclGetUniqueId: rank 0 creates the id, every rank passes the same bytes to vlb_ep_comm_init. */
+int vlb_ep_unique_id(uint8_t* id /* [VLB_EP_UNIQUE_ID_BYTES] */);
+/* One rank's communicator on the handle's device (world ranks, ranks 0..world-1). Returns when
+ * every rank has joined, or VLB_ERR_IO_ERROR after timeout_ms. */
+int vlb_ep_comm_init(vlb_handle* h, const uint8_t* id, int rank, int world, uint32_t timeout_ms,
+                     vlb_ep_comm** out);
+/* Finalizes (bounded) and frees the communicator; an aborted one is only freed. */
+int vlb_ep_comm_destroy(vlb_ep_comm* comm);
+/* Aborts the communicator (a host-side decision that a peer is gone); later exchanges fail. */
+int vlb_ep_comm_abort(vlb_ep_comm* comm);
+/* Plain all-to-all of bytes: send_bytes[p] bytes to rank p from send_dev (peers in rank order),
+ * recv_bytes[p] from rank p into recv_dev; both arrays host [world]. Enqueued on `stream` (NULL =
+ * the handle's); returns once NCCL has issued it. The exchange the driver's steps use, exposed
+ * for measuring the link (an NVLink all-to-all microbenchmark) and for callers' own exchanges. */
+int vlb_ep_all_to_all_device(vlb_ep_comm* comm, const void* send_dev, const uint64_t* send_bytes,
+                             void* recv_dev, const uint64_t* recv_bytes, void* stream);
+
+typedef struct vlb_ep_layer_desc {
+    uint32_t hidden, intermediate;
+    uint32_t experts;           /* E routed experts over all ranks (a multiple of world) */
+    uint32_t top_k;
+    int score;                  /* VLB_SCORE_* (learned routing from given logits) */
+    int weight_after_down;
+    float route_scale;
+    float routed_swiglu_limit;  /* must equal shared_swiglu_limit (one limit per group layer) */
+    float shared_swiglu_limit;
+    uint32_t max_tokens;        /* tokens of this rank per step */
+    const float* bias;          /* host f32 [E] or NULL */
+    const uint32_t* expert_slot;/* host u32 [E], a permutation of [0, E): expert e lives on rank
+                                   slot / (E / world) as its local expert slot % (E / world);
+                                   NULL = contiguous ranges of ids */
+    /* this rank's E / world routed experts in local-slot order, then the shared expert: E/world+1
+     * matrices each (IQ2_XXS or Q8_0, the tensor-core types) */
+    vlb_matrix* const* w1;
+    vlb_matrix* const* w3;
+    vlb_matrix* const* w2;
+} vlb_ep_layer_desc;
+
+int vlb_ep_layer_create(vlb_handle* h, vlb_ep_comm* comm, const vlb_ep_layer_desc* desc,
+                        vlb_ep_layer** out);
+int vlb_ep_layer_destroy(vlb_handle* h, vlb_ep_layer* layer);
+/* One step: x_dev f32 [T x H] and logits_dev f32 [T x E] of this rank's tokens, out_dev f32
+ * [T x H] = its MoE output (routed experts wherever they live + the shared expert). Every rank
+ * calls it once per step (T may differ between ranks). Synchronises `stream` at the count
+ * read-back and at the end (the step's status). */
+int vlb_ep_forward_device(vlb_handle* h, vlb_ep_layer* layer, const float* x_dev,
+                          const float* logits_dev, uint32_t T, float* out_dev, void* stream);
+/* Device times (ms) of the last completed step: plan, dispatch, experts, return, combine;
+ * rows[0] = rows received for this rank's experts, rows[1] = rows sent (T * k). */
+int vlb_ep_last_phases(vlb_ep_layer* layer, float* ms /* [5] */, uint64_t* rows /* [2] or NULL */);
+
 /* Route of the last forward on this layer, for parity checks: idx / weights [T x k] in rank
  * order; offsets [E + 1]; pair_token / pair_slot [T x k] = the dispatch permutation (pairs
  * sorted by expert ascending, then token, then slot - the reference's visit order,

@@ -86,3 +86,22 @@ def test_hash_tables_have_distinct_experts_per_row():
 def test_codebook_file_roundtrip(grids):
     assert set(grids) == {16, 18, 19}
     assert len(grids[19]) == 2048 * 8 and len(grids[16]) == 256 * 8 and len(grids[18]) == 256 * 4
+
+
+def test_ep_driver_reports_the_nccl_it_binds():
+    """The expert-parallel driver loads NCCL at first use (after torch, whose copy it then binds)
+    and needs >= 2.18; no GPU is touched."""
+    import ctypes as C
+
+    import torch  # noqa: F401
+
+    lib = vb.load_library()
+    v = C.c_int(0)
+    st = lib.vlb_ep_nccl_version(C.byref(v))
+    if st == 8:  # VLB_ERR_UNSUPPORTED: no NCCL in this environment
+        pytest.skip("no NCCL library")
+    assert st == 0 and v.value >= 21800
+    buf = C.create_string_buffer(128)
+    assert lib.vlb_ep_comm_init(None, None, 0, 1, 1000, None) == 1  # invalid argument, not a crash
+    assert lib.vlb_ep_forward_device(None, None, None, None, 0, None, None) == 1
+    assert lib.vlb_ep_last_phases(None, None, None) == 1

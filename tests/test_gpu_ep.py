@@ -55,12 +55,29 @@ def _rank_main(rank, world, port, args, q):
             _, _, lg0 = synth.activations(spec, T, seed=args["seed"] + 1)
             top = np.argsort(-lg0, axis=1, kind="stable")[:, :spec.top_k]
             slots = balanced_slots(np.bincount(top.ravel(), minlength=spec.experts), world)
-        layer, ops = make_device_layer(dev, W, comm, max_tokens=T, slots=slots)
         xd = torch.from_numpy(x).cuda()
         ld = torch.from_numpy(logits).cuda()
+        layer, ops = make_device_layer(dev, W, comm, max_tokens=T, slots=slots)
         out = layer.forward(xd, ld, T).cpu().numpy()
         out2 = layer.forward(xd, ld, T).cpu().numpy()  # a second step reuses the reserved buffers
         ops.close()
+        native_same = None
+        if args.get("native"):
+            # the library's C++ driver (its own NCCL communicator) on the same tokens: the same
+            # kernels in the same order, so the same bytes as the torch.distributed orchestration
+            from vastloom_b200.ep import NativeEpComm, NativeEpLayer, native_unique_id
+
+            uid = [native_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            ncomm = NativeEpComm(dev, uid[0], rank, world, timeout_ms=60_000)
+            nlayer = NativeEpLayer(dev, ncomm, W, max_tokens=T, slots=slots)
+            o1 = nlayer.forward(xd, ld, T).cpu().numpy()
+            o2 = nlayer.forward(xd, ld, T).cpu().numpy()
+            last = nlayer.last
+            assert last["received_rows"] == layer.last["received_rows"], (last, layer.last)
+            native_same = bool(np.array_equal(o1, out) and np.array_equal(o2, out))
+            nlayer.close()
+            ncomm.close()
         # the same tokens through the single-GPU layer (every expert resident)
         single = synth.upload_layer(dev, W, max_tokens=T)
         single.set_prefill_tokens(1)
@@ -68,7 +85,8 @@ def _rank_main(rank, world, port, args, q):
         idx_ref, _, _, _, _ = single.last_route(T)
         single.destroy()
         rel = float(np.linalg.norm(out - ref) / np.linalg.norm(ref))
-        q.put((rank, rel, bool(np.array_equal(out, out2)), layer.last["received_rows"], layer.last["sent_rows"]))
+        q.put((rank, rel, bool(np.array_equal(out, out2)), layer.last["received_rows"], layer.last["sent_rows"],
+               native_same))
         dev.close()
     finally:
         dist.destroy_process_group()
@@ -93,28 +111,106 @@ def _run(world, args):
 
 @pytest.mark.parametrize("scale,T", [("small", 600), ("full", 1024)])
 def test_gpu_ep_single_rank_matches_single_gpu_layer(scale, T):
-    res = _run(1, {"scale": scale, "T": T, "seed": 400})
-    rank, rel, deterministic, received, sent = res[0]
+    res = _run(1, {"scale": scale, "T": T, "seed": 400, "native": True})
+    rank, rel, deterministic, received, sent, native_same = res[0]
     assert received == sent  # a single rank receives all of its own pairs
     assert rel <= EXPECTED
     assert deterministic
+    assert native_same  # the C++ driver gives the same bytes
 
 
 def test_gpu_ep_single_rank_balanced_placement():
     """A balanced placement permutes the local expert order; the result is the same layer."""
-    res = _run(1, {"scale": "full", "T": 1024, "seed": 402, "balanced": True})
-    rank, rel, deterministic, received, sent = res[0]
-    assert received == sent and rel <= EXPECTED and deterministic
+    res = _run(1, {"scale": "full", "T": 1024, "seed": 402, "balanced": True, "native": True})
+    rank, rel, deterministic, received, sent, native_same = res[0]
+    assert received == sent and rel <= EXPECTED and deterministic and native_same
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("balanced", [False, True])
 def test_gpu_ep_two_ranks_match_single_gpu_layer(balanced):
-    res = _run(2, {"scale": "full", "T": 1024, "seed": 401, "balanced": balanced})
+    res = _run(2, {"scale": "full", "T": 1024, "seed": 401, "balanced": balanced, "native": True})
     assert sum(r[3] for r in res) == sum(r[4] for r in res)
-    for rank, rel, deterministic, received, sent in res:
+    for rank, rel, deterministic, received, sent, native_same in res:
         assert rel <= EXPECTED, (rank, rel)
         assert deterministic
+        assert native_same, rank
+
+
+def _leave_main(rank, world, port, q):
+    """Rank 1 runs one step with rank 0 and then leaves (between steps, nothing of it in flight);
+    rank 0's next step must end with the library's bounded wait (EpExchangeError "counts") and
+    every later step must be refused. NVLS is off, so no NVLink multicast object is involved."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=__import__("datetime").timedelta(seconds=60))
+    import vastloom_b200 as vb
+    from vastloom_b200 import synth
+    from vastloom_b200.ep import EpExchangeError, NativeEpComm, NativeEpLayer, native_unique_id
+
+    if rank == 0:
+        store.set("uid", native_unique_id())
+    uid = store.get("uid")
+    spec = synth.config(4, "small")
+    W = synth.layer_weights(spec, seed=430)
+    T = 256
+    x, _, logits = synth.activations(spec, T, seed=431 + rank)
+    dev = vb.Device(rank)
+    comm = NativeEpComm(dev, uid, rank, world, timeout_ms=5000)
+    layer = NativeEpLayer(dev, comm, W, max_tokens=T)
+    xd, ld = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+    first = layer.forward(xd, ld, T).cpu().numpy()
+    torch.cuda.synchronize()
+    store.set(f"done{rank}", "1")
+    store.wait(["done0", "done1"])
+    if rank == 1:
+        q.put((rank, bool(np.all(np.isfinite(first))), None, None))
+        q.close()
+        q.join_thread()  # the result reaches the pipe before the process leaves
+        os._exit(0)  # leaves without finalizing: its peer finds out at its next exchange
+    import time
+
+    time.sleep(1.0)
+    phase = refused = None
+    t0 = time.time()
+    try:
+        layer.forward(xd, ld, T)
+    except EpExchangeError as e:
+        phase = e.phase
+    waited = time.time() - t0
+    try:
+        layer.forward(xd, ld, T)
+    except EpExchangeError as e:
+        refused = e.phase
+    layer.close()
+    comm.close()
+    dev.close()
+    q.put((rank, bool(np.all(np.isfinite(first))), phase, (refused, waited)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_gpu_ep_native_peer_leaves_between_steps():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leave_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    (_, ok0, phase, (refused, waited)), (_, ok1, _, _) = res
+    assert ok0 and ok1
+    assert phase == "counts"
+    assert refused == "counts"
+    assert waited < 30.0
 
 
 def _half_rows(x, idx, w):

@@ -175,6 +175,10 @@ RAGGED = {
     # group empty
     "iq2-v4": synth.LayerSpec("ragged-iq2", 768, 512, 12, 3, synth.SCORE_SQRT_SOFTPLUS, synth.TYPE_IQ2_XXS,
                               synth.TYPE_IQ2_XXS, shared_type=synth.TYPE_Q8_0),
+    # IQ1_S gate/up and IQ3_XXS down (configuration 2's types) with a Q8_0 shared expert: 6 W2
+    # tiles, 2 of the second down row group empty
+    "iq1-iq3-v4": synth.LayerSpec("ragged-iq1-iq3", 768, 512, 12, 3, synth.SCORE_SQRT_SOFTPLUS, synth.TYPE_IQ1_S,
+                                  synth.TYPE_IQ3_XXS, shared_type=synth.TYPE_Q8_0),
 }
 
 
@@ -182,7 +186,7 @@ RAGGED = {
 @pytest.mark.parametrize("T", [1, 9])
 def test_gpu_layer_ragged_tiles(device, oracle, name, T):
     """Shapes whose row counts are not whole row groups of the decode kernel (row groups with
-    empty 128-row slices), for both tensor-core formats and both layer semantics."""
+    empty 128-row slices), for every storage type and both layer semantics."""
     spec = RAGGED[name]
     W = synth.layer_weights(spec, seed=500 + T)
     x, tok, logits = synth.activations(spec, T, seed=510 + T)

@@ -139,7 +139,9 @@ EXPORTS = (
     "vlb_layer_destroy vlb_layer_forward_device vlb_layer_forward vlb_layer_last_route "
     "vlb_layer_last_weight_bytes vlb_layer_set_profiling vlb_layer_phase_times vlb_layer_set_prefill_tokens "
     "vlb_layer_prefill_tokens vlb_layer_set_input_norm vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
-    "vlb_ep_plan_device vlb_ep_plan_half_device vlb_ep_pack_half_device vlb_ep_combine_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device"
+    "vlb_ep_plan_device vlb_ep_plan_half_device vlb_ep_pack_half_device vlb_ep_combine_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device "
+    "vlb_ep_nccl_version vlb_ep_unique_id vlb_ep_comm_init vlb_ep_comm_destroy vlb_ep_comm_abort "
+    "vlb_ep_all_to_all_device vlb_ep_layer_create vlb_ep_layer_destroy vlb_ep_forward_device vlb_ep_last_phases"
 ).split()
 
 
@@ -200,6 +202,16 @@ def load_library() -> C.CDLL:
         "vlb_route_device_noalloc": (I, [I, I, I, P, P, P, P, U32, U32, U32, U32, F, P, P, P]),
         "vlb_router_logits_device": (I, [P, P, P, U32, U32, U32, P, P]),
         "vlb_rms_norm_device": (I, [P, P, P, U32, U32, F, P, P]),
+        "vlb_ep_nccl_version": (I, [C.POINTER(I)]),
+        "vlb_ep_unique_id": (I, [P]),
+        "vlb_ep_comm_init": (I, [P, P, I, I, U32, C.POINTER(P)]),
+        "vlb_ep_comm_destroy": (I, [P]),
+        "vlb_ep_comm_abort": (I, [P]),
+        "vlb_ep_all_to_all_device": (I, [P, P, P, P, P, P]),
+        "vlb_ep_layer_create": (I, [P, P, P, C.POINTER(P)]),
+        "vlb_ep_layer_destroy": (I, [P, P]),
+        "vlb_ep_forward_device": (I, [P, P, P, P, U32, P, P]),
+        "vlb_ep_last_phases": (I, [P, C.POINTER(C.c_float), C.POINTER(U64)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

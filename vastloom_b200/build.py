@@ -23,7 +23,7 @@ LIB = PKG / "libvlb200.so"
 DATA = PKG / "data"
 GRIDS = DATA / "iq_grids.bin"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["vlb_kernels.cu", "vlb_decode.cu", "vlb_prefill.cu", "vlb_ep.cu", "vlb_abi.cu", "vlb_noalloc.cu"]
+SOURCES = ["vlb_kernels.cu", "vlb_decode.cu", "vlb_prefill.cu", "vlb_ep.cu", "vlb_abi.cu", "vlb_noalloc.cu", "vlb_ep_driver.cu"]
 
 
 def reference_root() -> Path:

@@ -397,3 +397,166 @@ def make_device_layer(dev, W, comm, max_tokens: int, slots: Optional[np.ndarray]
     ops = DeviceEpOps(dev, mats, spec, W.bias, spec.score, spec.route_scale, spec.experts, spec.top_k,
                       spec.hidden, max_tokens, slots=slots)
     return ExpertParallelLayer(ops, comm, spec.experts, spec.top_k, spec.hidden, max_tokens), ops
+
+
+class _EpLayerDesc(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("experts", C.c_uint32), ("top_k", C.c_uint32),
+        ("score", C.c_int), ("weight_after_down", C.c_int), ("route_scale", C.c_float),
+        ("routed_swiglu_limit", C.c_float), ("shared_swiglu_limit", C.c_float), ("max_tokens", C.c_uint32),
+        ("bias", C.c_void_p), ("expert_slot", C.c_void_p), ("w1", C.c_void_p), ("w3", C.c_void_p),
+        ("w2", C.c_void_p),
+    ]
+
+
+def _native_check(lib, st: int, phase: Optional[str] = None) -> None:
+    if st != 0:
+        from . import VlbError
+
+        buf = C.create_string_buffer(1024)
+        lib.vlb_thread_error(buf, 1024)
+        msg = buf.value.decode()
+        if phase is not None:
+            raise EpExchangeError(phase, VlbError(st, msg))
+        raise VlbError(st, msg)
+
+
+def native_unique_id() -> bytes:
+    """ncclGetUniqueId through the library (rank 0 makes it; every rank passes the same bytes to
+    NativeEpComm)."""
+    import torch  # noqa: F401  (torch's NCCL first: see NativeEpComm)
+
+    from . import load_library
+
+    lib = load_library()
+    buf = (C.c_uint8 * 128)()
+    _native_check(lib, lib.vlb_ep_unique_id(buf))
+    return bytes(buf)
+
+
+class NativeEpComm:
+    """The library's own NCCL communicator for one rank (vlb_ep_comm_init): non-blocking, every
+    wait bounded by `timeout_ms`, aborted by the library when an exchange fails.
+
+    The library binds the NCCL copy already loaded in the process when there is one. torch is
+    imported before the first NCCL call, so that copy is torch's own: a process that loaded
+    another libnccl.so.2 first could no longer import torch (one soname per process)."""
+
+    def __init__(self, dev, unique_id: bytes, rank: int, world: int, timeout_ms: int = 120_000):
+        import torch  # noqa: F401
+
+        if len(unique_id) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        self.dev, self.lib, self.rank, self.world = dev, dev.lib, rank, world
+        uid = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        p = C.c_void_p()
+        _native_check(self.lib, self.lib.vlb_ep_comm_init(dev.h, uid, rank, world, timeout_ms, C.byref(p)))
+        self.ptr = p
+
+    def abort(self) -> None:
+        _native_check(self.lib, self.lib.vlb_ep_comm_abort(self.ptr))
+
+    def all_to_all(self, send_ptr: int, send_bytes, recv_ptr: int, recv_bytes, stream: int = 0) -> None:
+        sb = (C.c_uint64 * self.world)(*[int(v) for v in send_bytes])
+        rb = (C.c_uint64 * self.world)(*[int(v) for v in recv_bytes])
+        _native_check(self.lib, self.lib.vlb_ep_all_to_all_device(self.ptr, C.c_void_p(send_ptr), sb,
+                                                                  C.c_void_p(recv_ptr), rb, C.c_void_p(stream)))
+
+    def close(self) -> None:
+        if self.ptr:
+            st = self.lib.vlb_ep_comm_destroy(self.ptr)
+            self.ptr = C.c_void_p()
+            _native_check(self.lib, st)
+
+
+class NativeEpLayer:
+    """One rank's expert-parallel layer run by the library's C++ driver (vlb_ep_layer_create /
+    vlb_ep_forward_device): route, plan, the NCCL exchanges, the group forward and the combine in
+    one call per step. A failed exchange raises EpExchangeError with the phase the library names
+    and leaves the layer refusing further forwards."""
+
+    PHASES = ("plan_s", "dispatch_s", "experts_s", "return_s", "combine_s")
+
+    def __init__(self, dev, comm: NativeEpComm, W, max_tokens: int, slots: Optional[np.ndarray] = None,
+                 layer_index: int = 0):
+        spec = W.spec
+        self.dev, self.lib, self.comm, self.spec = dev, dev.lib, comm, spec
+        self.mats = upload_group(dev, W, comm.rank, comm.world, layer_index=layer_index, slots=slots)
+        self._keep = []
+
+        def arr(lst):
+            a = (C.c_void_p * len(lst))(*[m.ptr.value for m in lst])
+            self._keep.append(a)
+            return C.cast(a, C.c_void_p)
+
+        bias = None if W.bias is None else np.ascontiguousarray(W.bias, np.float32)
+        sl = None if slots is None else np.ascontiguousarray(slots, np.uint32)
+        self._keep += [bias, sl]
+        d = _EpLayerDesc(spec.hidden, spec.intermediate, spec.experts, spec.top_k, spec.score,
+                         spec.weight_after_down, spec.route_scale, spec.routed_swiglu_limit,
+                         spec.shared_swiglu_limit, max_tokens,
+                         None if bias is None else bias.ctypes.data, None if sl is None else sl.ctypes.data,
+                         arr(self.mats["w1"]), arr(self.mats["w3"]), arr(self.mats["w2"]))
+        p = C.c_void_p()
+        try:
+            _native_check(self.lib, self.lib.vlb_ep_layer_create(dev.h, comm.ptr, C.byref(d), C.byref(p)))
+        except Exception:
+            self._release_mats()
+            raise
+        self.ptr = p
+        self.max_tokens = max_tokens
+        self.failed: Optional[str] = None
+
+    def forward_device(self, x_ptr: int, logits_ptr: int, T: int, out_ptr: int, stream: int = 0) -> None:
+        """x [T, H] f32, logits [T, E] f32 and out [T, H] f32 device addresses."""
+        st = self.lib.vlb_ep_forward_device(self.dev.h, self.ptr, C.c_void_p(x_ptr), C.c_void_p(logits_ptr), T,
+                                            C.c_void_p(out_ptr), C.c_void_p(stream))
+        if st != 0:
+            buf = C.create_string_buffer(1024)
+            self.lib.vlb_thread_error(buf, 1024)
+            msg = buf.value.decode()
+            # the driver prefixes an exchange failure with its phase ("counts: ...") and refuses a
+            # failed layer with "an earlier exchange (<phase>) ..."
+            phase = next((p for p in ("counts", "dispatch", "return", "communicator")
+                          if msg.startswith(p + ":") or msg.startswith(f"an earlier exchange ({p})")), None)
+            if phase is not None:
+                from . import VlbError
+
+                self.failed = phase
+                raise EpExchangeError(phase, VlbError(st, msg))
+            _native_check(self.lib, st)
+
+    def forward(self, x, logits, T: int):
+        """torch CUDA tensors x [T, H], logits [T, E] (f32); returns out [T, H] on the library
+        stream's device."""
+        import torch
+
+        out = torch.empty((T, self.spec.hidden), dtype=torch.float32, device=x.device)
+        lib_stream = torch.cuda.ExternalStream(self.dev.stream, device=x.device)
+        lib_stream.wait_stream(torch.cuda.current_stream(x.device))  # inputs written on torch's stream
+        # the step ends with a synchronisation of the library stream (its status read), so `out`
+        # is complete when this returns
+        self.forward_device(x.data_ptr(), logits.data_ptr(), T, out.data_ptr(), self.dev.stream)
+        return out
+
+    @property
+    def last(self) -> dict:
+        ms = (C.c_float * 5)()
+        rows = (C.c_uint64 * 2)()
+        if self.lib.vlb_ep_last_phases(self.ptr, ms, rows) != 0:
+            return {}
+        d = {name: ms[i] / 1000.0 for i, name in enumerate(self.PHASES)}
+        d["received_rows"], d["sent_rows"] = int(rows[0]), int(rows[1])
+        return d
+
+    def _release_mats(self) -> None:
+        for lst in self.mats.values():
+            for m in lst:
+                self.dev.release_matrix(m)
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            st = self.lib.vlb_ep_layer_destroy(self.dev.h, self.ptr)
+            self.ptr = C.c_void_p()
+            self._release_mats()
+            _native_check(self.lib, st)
