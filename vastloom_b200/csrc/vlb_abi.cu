@@ -709,7 +709,10 @@ int vlb_layer_create(vlb_handle* h, const vlb_moe_layer_desc* d, vlb_layer** out
                  o_y = carve(P * H * 4), o_xs = carve(T * 4), o_am = carve(P * 4),
                  o_xn = carve(T * H * 4), o_xd = carve(T * H * 8);
     const uint32_t mpt = prefill_max_tiles((uint32_t)T, k, E);
-    const size_t o_xh = carve(P * H * 2), o_acth = carve(P * I * 2), o_pt2 = carve((size_t)mpt * sizeof(Unit));
+    // xperm (prefill operand rows, P x H fp16) doubles as the decode kernels' gate/up activation
+    // image (T rows of 4 H bytes) in a decode forward: room for the larger of the two
+    const size_t o_xh = carve(P * H * 2 > T * H * 4 ? P * H * 2 : T * H * 4), o_acth = carve(P * I * 2),
+                 o_pt2 = carve((size_t)mpt * sizeof(Unit));
     const size_t o_dc = carve(((T * k + 1023) / 1024) * E * 4);
     TRY(h->galloc(off, "vlb-layer-workspace", &L->ws));
     TRY(h->galloc(T * H * 4, "vlb-layer-x", (void**)&L->x_dev));

@@ -47,27 +47,32 @@ constexpr uint32_t kDcThreads = kDcConsumers + 32;             // + the loader w
 constexpr uint32_t kDcSlices = 4;
 constexpr uint32_t kDcD = 512;                                 // fp16 block scales (<= 2 blocks)
 constexpr uint32_t kDcSc = kTileRows * 4u;                     // IQ2_XXS / IQ3_XXS group scale words
-#ifndef VLB_DC_RING
-#define VLB_DC_RING 3
-#endif
-constexpr uint32_t kDcRing = VLB_DC_RING;
 constexpr uint32_t kDcTabBytes = 32768u;  // the IQ codebook in fp16 (layout per format: dc_build_table)
 // Stage carve for slices of BODY bytes of packed weights: 8 KB holds a 128-row tile block column
 // of IQ2_XXS (64 B a row), IQ1_S (48 B) or two Q8_0 blocks (2 x 32 B); IQ3_XXS (96 B a row) needs
 // 12 KB and is launched with the larger carve.
 constexpr uint32_t kDcBodySmall = kTileRows * 64u;
 constexpr uint32_t kDcBodyLarge = kTileRows * 96u;
+// A stage also holds the unit's activations for the stage's columns, streamed from the activation
+// image (below) with the weights: 8 columns n = 2 token + piece (piece 0 = hi, 1 = lo) of one
+// 512-byte block record each, 576 bytes apart (the 64-byte shift puts columns 2m and 2m + 1 in
+// different bank halves).
+constexpr uint32_t kDcXsCol = 576;
+constexpr uint32_t kDcXsStage = 8u * kDcXsCol;
 template <uint32_t BODY>
 struct DcL {
     static constexpr uint32_t Body = BODY;
+    static constexpr uint32_t Ring = BODY <= kDcBodySmall ? 4u : 3u;  // stages in flight
     static constexpr uint32_t Slice = BODY + kDcD + kDcSc;
-    static constexpr uint32_t Stage = kDcSlices * Slice;
+    static constexpr uint32_t XsOff = kDcSlices * Slice;  // the activations, within a stage
+    static constexpr uint32_t Stage = XsOff + kDcXsStage;
     static constexpr uint32_t RingOff = kDcTabBytes;
-    static constexpr uint32_t HdrOff = RingOff + kDcRing * Stage;
-    static constexpr uint32_t BarOff = HdrOff + kDcRing * 16u;
-    static constexpr uint32_t MiscOff = BarOff + 64u;  // abort word, token scales
-    static constexpr uint32_t XsOff = (MiscOff + 64u + 127u) / 128u * 128u;
-    static_assert(XsOff % 16 == 0 && Stage % 1024 == 0, "shared-memory carve alignment");
+    static constexpr uint32_t HdrOff = RingOff + Ring * Stage;
+    static constexpr uint32_t BarOff = HdrOff + Ring * 48u;  // three uint4 per stage header
+    static constexpr uint32_t MiscOff = BarOff + 64u;        // abort word
+    static constexpr uint32_t End = MiscOff + 16u;
+    static_assert(Stage % 128 == 0 && HdrOff % 16 == 0, "shared-memory carve alignment");
+    static_assert(2u * Ring * 8u <= 64u, "barriers fit their slot");
 };
 constexpr uint64_t kDcWaitNs = 2000000000ull;
 constexpr uint32_t kDcSleepNs = 1000;  // suspend hint of one barrier test
@@ -79,48 +84,40 @@ constexpr uint32_t kDcEnd = 0xffffffffu;
 constexpr uint32_t kDcMaxChunk = VLB_DC_MAX_CHUNK;
 constexpr uint32_t kDcMaxSplits = 8;
 
-static_assert((2u * kDcRing + 1u) * 8u <= 64u, "barriers fit their slot");
-
-// Activation staging: 8 B columns (n = 2 token + piece, piece 0 = hi, 1 = lo) of K fp16 values.
-// Two layouts, each free of bank conflicts for its format's read pattern (8 lanes of a 16-byte
-// load phase: n in {2m, 2m+1} x q in 0..3):
-//   256-column formats (IQ2_XXS, IQ3_XXS, IQ1_S):
-//            lane q reads chunk c = 32 b + 8 q + j (block b, k-step pair j): stored at 16-byte
-//            position 32 b + 4 j + q of a column whose stride is K * 2 + 64 bytes, so the four q
-//            are consecutive and the column parity shifts by half a bank row; j is an immediate.
-//   Q8_0:    lane q reads chunk c = 4 b' + q (32-column block b'): stored at position
-//            c ^ (((c >> 3) & 3) | ((n & 1) << 2)) of a column of K * 2 bytes.
-__host__ __device__ constexpr uint32_t dc_xs_bytes(uint32_t K) { return 8u * (K * 2u + 64u); }
-
-__device__ __forceinline__ uint32_t dc_xs_offset(bool iq2, uint32_t n, uint32_t c, uint32_t K) {
-    if (iq2) return n * (K * 2u + 64u) + ((c & ~31u) + 4u * (c & 7u) + ((c >> 3) & 3u)) * 16u;
-    return (n * (K / 8u) + (c ^ (((c >> 3) & 3u) | ((n & 1u) << 2)))) * 16u;
-}
-
-// Stages the unit's activation rows (f32, scaled by the token's power of two) as hi/lo fp16
-// pieces. Consumer threads only.
-__device__ __forceinline__ void dc_stage_xs(unsigned char* xs, const float* const (&rows)[kUnitTokens],
-                                            const float (&scale)[kUnitTokens], uint32_t K, uint32_t n_tokens,
-                                            bool iq2) {
-    const uint32_t k_chunks = K / 8u, total = n_tokens * k_chunks;
-    for (uint32_t i = threadIdx.x; i < total; i += kDcConsumers) {
-        const uint32_t t = i / k_chunks, c = i % k_chunks;
-        const float4 a = *reinterpret_cast<const float4*>(rows[t] + c * 8u);
-        const float4 b = *reinterpret_cast<const float4*>(rows[t] + c * 8u + 4u);
-        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        const float s = scale[t];
+// Activation image: the decode kernels' B operand, converted once per row (a token's x for
+// gate/up, a pair's act for down) instead of once per unit in every CTA. Row r is K / 256 records
+// of 1 KB, one per 256-column block: the fp16 hi pieces of the block's values x * s (s the row's
+// power-of-two prescale: max|x * s| in [2^14, 2^15)), then the lo pieces x * s - hi, each 32
+// 16-byte chunks with chunk c (columns 8 c .. 8 c + 7) at position 4 (c % 8) + c / 8. In that
+// order the consumer lanes' 16-byte loads are free of bank conflicts: in a 256-column stage lane
+// q reads chunk 8 q + j (j = 4 half + sub-block), at position 4 j + q. A row takes 4 K bytes, the
+// size of its f32 row, so the down phase converts act in place.
+__global__ void __launch_bounds__(256) dc_image_kernel(const float* src, uint32_t K, const uint32_t* __restrict__ maxbits,
+                                                       unsigned char* dst) {
+    extern __shared__ __align__(16) float row_s[];
+    const uint32_t r = blockIdx.x;
+    const float* row = src + (size_t)r * K;
+    // the whole row first: the down phase writes over its own input
+    for (uint32_t i = threadIdx.x; i < K / 4u; i += blockDim.x)
+        reinterpret_cast<float4*>(row_s)[i] = reinterpret_cast<const float4*>(row)[i];
+    const float s = mma::prescale_for(__uint_as_float(maxbits[r]));
+    __syncthreads();
+    unsigned char* out = dst + (size_t)r * K * 4u;
+    for (uint32_t c = threadIdx.x; c < K / 8u; c += blockDim.x) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            const float x0 = v[2 * w] * s, x1 = v[2 * w + 1] * s;  // exact: s is a power of two
+            const float x0 = row_s[8u * c + 2u * w] * s, x1 = row_s[8u * c + 2u * w + 1u] * s;  // exact: s is a power of two
             const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
             const __half l0 = __float2half_rn(x0 - __half2float(h0));
             const __half l1 = __float2half_rn(x1 - __half2float(h1));
             hi[w] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
             lo[w] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
         }
-        *reinterpret_cast<uint4*>(xs + dc_xs_offset(iq2, 2u * t, c, K)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(xs + dc_xs_offset(iq2, 2u * t + 1u, c, K)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        const uint32_t cb = c & 31u, pos = 4u * (cb & 7u) + (cb >> 3);
+        unsigned char* rec = out + (size_t)(c >> 5) * 1024u + pos * 16u;
+        *reinterpret_cast<uint4*>(rec) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(rec + 512u) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -142,17 +139,6 @@ __device__ __forceinline__ void dc_fail(uint32_t* flags, volatile uint32_t* abor
     atomicOr(flags, kDcErrTimeout);
 }
 
-// A barrier of the 16 consumer warps on an mbarrier (so that it is bounded like every other wait:
-// a hardware named barrier would wait forever for a warp that left after an abort). Every lane
-// waits on the phase itself, which orders the other warps' shared-memory writes before its reads.
-__device__ __forceinline__ bool dc_consumer_sync(uint64_t* cbar, uint32_t& phase, volatile uint32_t* abort) {
-    __syncwarp();
-    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(cbar);
-    const bool ok = dc_wait(cbar, phase & 1u, abort);
-    ++phase;
-    return __all_sync(0xffffffffu, ok);
-}
-
 // Item geometry shared by the loader and the consumers.
 struct DcItem {
     uint32_t unit, group;       // unit index, row group
@@ -171,12 +157,12 @@ __device__ __forceinline__ uint32_t dc_body_bytes(uint32_t fmt) {
 // Items are (unit, row group, K split): item = (unit * groups + group) * splits + split, so the
 // splits of one row group are neighbours (they share the staged activations).
 template <bool GATEUP>
-__device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uint32_t groups, uint32_t splits) {
+__device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, const Unit& u, uint32_t fmt,
+                                          uint32_t groups, uint32_t splits) {
     DcItem it;
     const uint32_t split = item % splits, rg = item / splits;
     it.unit = rg / groups;
     it.group = rg % groups;
-    const Unit u = p.units[it.unit];
     const uint32_t rows = GATEUP ? p.I : p.H;
     const uint32_t tiles = (rows + kTileRows - 1u) / kTileRows;
 #pragma unroll
@@ -191,7 +177,7 @@ __device__ __forceinline__ DcItem dc_item(const MoeParams& p, uint32_t item, uin
         it.valid[s] = it.tile[s] < tiles;
     }
     const uint32_t K = GATEUP ? p.H : p.I;
-    it.fmt = it.m[0]->type;
+    it.fmt = fmt;
     const uint32_t stages = it.fmt != kTypeQ8_0 ? K / 256u : (K / 32u + 1u) / 2u;
     it.st0 = (uint32_t)((uint64_t)stages * split / splits);
     it.st1 = (uint32_t)((uint64_t)stages * (split + 1u) / splits);
@@ -207,23 +193,23 @@ struct DcWarpItem {
     uint32_t bpr;
 };
 
+// Built from the stage header's second word (unit count | storage type << 8, first pair, expert,
+// blocks per row), which the loader writes: no global loads at an item boundary.
 template <bool GATEUP>
-__device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t item, uint32_t groups,
-                                                   uint32_t splits, uint32_t s0, uint32_t s1) {
+__device__ __forceinline__ DcWarpItem dc_warp_item(const MoeParams& p, uint32_t item, const uint4& h2,
+                                                   uint32_t groups, uint32_t splits, uint32_t s0, uint32_t s1) {
     DcWarpItem w;
     const uint32_t rg = item / splits;
     w.unit = rg / groups;
     const uint32_t group = rg % groups;
-    const Unit u = p.units[w.unit];
     const uint32_t rows = GATEUP ? p.I : p.H;
     const uint32_t tiles = (rows + kTileRows - 1u) / kTileRows;
     w.tile0 = GATEUP ? 2u * group + (s0 & 1u) : 4u * group + s0;
     w.tile1 = GATEUP ? 2u * group + (s1 & 1u) : 4u * group + s1;
     w.valid0 = w.tile0 < tiles;
     w.valid1 = w.tile1 < tiles;
-    const DevMat& m = p.mats[(GATEUP ? 0u : 2u * (p.E + 1u)) + u.expert];
-    w.fmt = m.type;
-    w.bpr = m.bpr;
+    w.fmt = (h2.x >> 8) & 0xffu;
+    w.bpr = h2.w;
     return w;
 }
 
@@ -235,94 +221,159 @@ template <bool GATEUP, uint32_t BODY>
 __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t groups, uint32_t splits,
                           uint64_t n_items, uint32_t chunk, uint32_t tfmt, volatile uint32_t* abort) {
     using Lay = DcL<BODY>;
+    constexpr uint32_t R = Lay::Ring;
     const uint32_t lane = threadIdx.x & 31u;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::BarOff);
-    uint64_t* empty = full + kDcRing;
+    uint64_t* empty = full + R;
     uint4* hdr = reinterpret_cast<uint4*>(smem + Lay::HdrOff);
     uint32_t* next_item = p.counters + (GATEUP ? 2 : 4);
     const uint32_t mat_off = GATEUP ? 0u : 2u * (p.E + 1u);
+    const uint32_t K = GATEUP ? p.H : p.I;
+    // the activation image: gate/up in the prefill operand buffer (idle in a decode forward), down
+    // in act (converted in place)
+    const unsigned char* image = GATEUP ? reinterpret_cast<const unsigned char*>(p.xperm)
+                                        : reinterpret_cast<const unsigned char*>(p.act);
     uint32_t g = 0;
     bool ok = true;
     // every lane runs this (warp-uniform result)
     auto acquire = [&](uint32_t slot) -> bool {
         bool got = true;
-        if (lane == 0 && g >= kDcRing && !dc_wait(empty + slot, ((g / kDcRing) - 1u) & 1u, abort)) {
+        if (lane == 0 && g >= R && !dc_wait(empty + slot, ((g / R) - 1u) & 1u, abort)) {
             dc_fail(p.counters + 3, abort);
             got = false;
         }
         return __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0;
     };
-    while (ok) {
-        // chunks of neighbouring items (one unit's row groups share the staged activations) while
-        // much work is left, single items towards the end so that the CTAs finish together
-        uint64_t c0 = 0;
+    // chunks of neighbouring items (one unit's row groups share the activation rows) while much work
+    // is left, single items towards the end so that the CTAs finish together; [c0, c1) is the chunk
+    auto claim = [&](uint64_t& c0, uint64_t& c1) {
+        uint64_t a = 0;
         uint32_t take = 1;
         if (lane == 0) {
             const uint64_t seen = *reinterpret_cast<volatile uint32_t*>(next_item);
             take = seen < n_items ? (uint32_t)((n_items - seen) / (2ull * gridDim.x)) : 1u;
             take = take < 1u ? 1u : (take > chunk ? chunk : take);
-            c0 = atomicAdd(next_item, take);
+            a = atomicAdd(next_item, take);
         }
-        c0 = __shfl_sync(0xffffffffu, (unsigned long long)c0, 0);
+        c0 = __shfl_sync(0xffffffffu, (unsigned long long)a, 0);
         take = __shfl_sync(0xffffffffu, take, 0);
-        if (c0 >= n_items) break;
-        const uint64_t c1 = c0 + take < n_items ? c0 + take : n_items;
-        // the dispatch lists the shared expert's units first (the heaviest: every token, usually
-        // the widest storage type), so the CTAs start on them and finish on light routed items
-        for (uint64_t item = c0; item < c1 && ok; ++item) {
-            const Unit u = p.units[(uint32_t)(item / ((uint64_t)groups * splits))];
-            const uint32_t t = p.mats[mat_off + u.expert].type;
-            if (t != tfmt && t != kTypeQ8_0) continue;  // served by the CUDA-core kernels
-            const DcItem it = dc_item<GATEUP>(p, (uint32_t)item, groups, splits);
+        c1 = c0 < n_items ? (c0 + take < n_items ? c0 + take : n_items) : c0;
+    };
+    // an item's scalars, loaded one item ahead so that their latency hides behind the stages issued
+    // meanwhile: its unit, storage type and, on lane 12 + 2 t + piece, token t's image row and
+    // (piece 0) the row's max-bits word
+    struct Pre {
+        Unit u;
+        uint32_t type;
+        uint32_t row, maxbits;
+    };
+    const uint32_t xt = (lane - 12u) >> 1, xpiece = (lane - 12u) & 1u;
+    auto fetch = [&](uint64_t item) -> Pre {
+        Pre f;
+        f.u = p.units[(uint32_t)(item / ((uint64_t)groups * splits))];
+        f.type = p.mats[mat_off + f.u.expert].type;
+        f.row = 0;
+        f.maxbits = 0;
+        if (lane >= 12u && lane < 12u + 2u * kUnitTokens && xt < f.u.count) {
+            const uint32_t pair = f.u.pair_begin + xt;
+            f.row = GATEUP ? p.pair_token[pair] : pair;
+            if (!xpiece) f.maxbits = GATEUP ? p.xmax[f.row] : p.act_max[pair];
+        }
+        return f;
+    };
+    uint64_t c0 = 0, c1 = 0;
+    claim(c0, c1);
+    uint64_t n0 = 0, n1 = 0;  // the next chunk, claimed while the current one's last item is issued
+    bool have_next = false;
+    uint64_t item = c0;
+    Pre cur{};
+    if (item < c1) cur = fetch(item);
+    while (ok && item < c1) {
+        // the next item: in this chunk, else the first of the next chunk (claimed now)
+        uint64_t nitem = item + 1;
+        if (nitem >= c1) {
+            claim(n0, n1);
+            have_next = n0 < n1;
+            nitem = n0;
+        }
+        Pre nxt{};
+        if (nitem < n_items && (nitem < c1 || have_next)) nxt = fetch(nitem);
+        const Unit u = cur.u;
+        const uint32_t t = cur.type;
+        if (t == tfmt || t == kTypeQ8_0) {  // else served by the CUDA-core kernels
+            const DcItem it = dc_item<GATEUP>(p, (uint32_t)item, u, t, groups, splits);
+            const bool xlane = lane >= 12u && lane < 12u + 2u * kUnitTokens && xt < u.count;
+            const unsigned char* xrow = xlane ? image + (size_t)cur.row * K * 4u + xpiece * 512u : nullptr;
+            const uint4 hmax = make_uint4(__shfl_sync(0xffffffffu, cur.maxbits, 12), __shfl_sync(0xffffffffu, cur.maxbits, 14),
+                                          __shfl_sync(0xffffffffu, cur.maxbits, 16), __shfl_sync(0xffffffffu, cur.maxbits, 18));
+            const uint32_t bpr = it.m[0]->bpr;
             for (uint32_t st = it.st0; st < it.st1; ++st, ++g) {
-                const uint32_t slot = g % kDcRing;
+                const uint32_t slot = g % R;
                 if (!(ok = acquire(slot))) break;
                 // Q8_0: blocks 2 st and 2 st + 1 (the second may be past the row end)
                 const bool q8 = it.fmt == kTypeQ8_0;
                 const bool scaled = it.fmt == kTypeIq2Xxs || it.fmt == kTypeIq3Xxs;
-                const uint32_t nblk = q8 ? (2u * st + 1u < it.m[0]->bpr ? 2u : 1u) : 1u;
+                const uint32_t nblk = q8 ? (2u * st + 1u < bpr ? 2u : 1u) : 1u;
                 const uint32_t bb = dc_body_bytes(it.fmt);
                 const uint32_t body = nblk * kTileRows * bb;
                 const uint32_t dbytes = nblk * kTileRows * 2u;
+                const uint32_t sbase = tc::smem_u32(smem + Lay::RingOff + slot * Lay::Stage);
                 if (lane == 0) {
-                    uint32_t bytes = 0;
+                    uint32_t bytes = u.count * 1024u;
 #pragma unroll
                     for (uint32_t s = 0; s < kDcSlices; ++s)
                         if (it.valid[s]) bytes += body + dbytes + (scaled ? kDcSc : 0u);
-                    hdr[slot] = make_uint4((uint32_t)item, st, it.st1, it.st0);
+                    hdr[3u * slot] = make_uint4((uint32_t)item, st, it.st1, it.st0);
+                    hdr[3u * slot + 1u] = make_uint4(u.count | (it.fmt << 8), u.pair_begin, u.expert, bpr);
+                    hdr[3u * slot + 2u] = hmax;
                     tc::mbar_arrive_expect_tx(full + slot, bytes);
                 }
                 __syncwarp();
-                // lane 3 s + c: slice s, copy c (0 packed weights, 1 block scales, 2 group scales)
-                const uint32_t s = lane / 3u, c = lane % 3u;
-                const DevMat* ms = it.m[0];
-                uint32_t tile = 0;
-                bool valid = false;
+                if (lane < 12u) {
+                    // lane 3 s + c: slice s, copy c (0 packed weights, 1 block scales, 2 group scales)
+                    const uint32_t s = lane / 3u, c = lane % 3u;
+                    const DevMat* ms = it.m[0];
+                    uint32_t tile = 0;
+                    bool valid = false;
 #pragma unroll
-                for (uint32_t k = 0; k < kDcSlices; ++k)  // constant indices keep the item in registers
-                    if (k == s) {
-                        ms = it.m[k];
-                        tile = it.tile[k];
-                        valid = it.valid[k];
+                    for (uint32_t k = 0; k < kDcSlices; ++k)  // constant indices keep the item in registers
+                        if (k == s) {
+                            ms = it.m[k];
+                            tile = it.tile[k];
+                            valid = it.valid[k];
+                        }
+                    if (valid && (c < 2u || scaled)) {
+                        const DevMat& m = *ms;
+                        const uint32_t blk = q8 ? 2u * st : st;
+                        const size_t at = blk_index(m.bpr, tile * kTileRows, blk);
+                        const uint32_t sd = sbase + s * Lay::Slice;
+                        if (c == 0) tc::bulk_load(sd, m.body + at * bb, body, full + slot);
+                        else if (c == 1) tc::bulk_load(sd + BODY, m.d + at, dbytes, full + slot);
+                        else tc::bulk_load(sd + BODY + kDcD, m.scales + at, kDcSc, full + slot);
                     }
-                if (valid && (c < 2u || scaled)) {
-                    const DevMat& m = *ms;
-                    const uint32_t blk = q8 ? 2u * st : st;
-                    const size_t at = blk_index(m.bpr, tile * kTileRows, blk);
-                    const uint32_t sd = tc::smem_u32(smem + Lay::RingOff + slot * Lay::Stage) + s * Lay::Slice;
-                    if (c == 0) tc::bulk_load(sd, m.body + at * bb, body, full + slot);
-                    else if (c == 1) tc::bulk_load(sd + BODY, m.d + at, dbytes, full + slot);
-                    else tc::bulk_load(sd + BODY + kDcD, m.scales + at, kDcSc, full + slot);
+                } else if (xlane) {
+                    // the 256-column block holding the stage's columns (a Q8_0 stage: a quarter of it)
+                    const uint32_t blk = q8 ? st >> 2 : st;
+                    tc::bulk_load(sbase + Lay::XsOff + (2u * xt + xpiece) * kDcXsCol, xrow + (size_t)blk * 1024u, 512u,
+                                  full + slot);
                 }
                 __syncwarp();
             }
         }
+        if (item + 1 >= c1) {  // move to the chunk claimed above
+            if (!have_next) break;
+            c0 = n0;
+            c1 = n1;
+            have_next = false;
+        }
+        item = nitem;
+        cur = nxt;
     }
     if (ok) {  // end marker: a stage with no copies
-        const uint32_t slot = g % kDcRing;
+        const uint32_t slot = g % R;
         if (acquire(slot)) {
             if (lane == 0) {
-                hdr[slot] = make_uint4(kDcEnd, 0u, 0u, 0u);
+                hdr[3u * slot] = make_uint4(kDcEnd, 0u, 0u, 0u);
                 tc::mbar_arrive(full + slot);
             }
             ++g;
@@ -330,15 +381,16 @@ __device__ void dc_loader(const MoeParams& p, unsigned char* smem, uint32_t grou
     }
     // no bulk copy may still be landing in shared memory when the CTA exits
     if (lane == 0)
-        for (uint32_t j = g > kDcRing ? g - kDcRing : 0u; j < g; ++j)
-            if (!dc_wait(full + j % kDcRing, (j / kDcRing) & 1u, abort)) break;
+        for (uint32_t j = g > R ? g - R : 0u; j < g; ++j)
+            if (!dc_wait(full + j % R, (j / R) & 1u, abort)) break;
 }
 
 // ---- consumer warps -------------------------------------------------------------------------------
 // One output of the gate/up epilogue: act = SwiGLU(gate, up), for DeepSeek V4 with the optional
 // clamp and the route weight before the down product (execute_expert, deepseek_v4_graph.cpp:
 // 1865-1890, double arithmetic), for OLMoE the float SwiGLU with expf (olmoe_runtime.cpp:1279).
-__device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, float uv, bool shared, uint32_t pair) {
+// pw: the pair's route weight (read when the item starts).
+__device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, float uv, bool shared, float pw) {
     if (p.weight_after_down) return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
     const float limit = shared ? p.shared_limit : p.routed_limit;
     double gd = (double)gv, ud = (double)uv;
@@ -347,7 +399,7 @@ __device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, floa
         ud = fmin(fmax(ud, -(double)limit), (double)limit);
     }
     double v = gd / (1.0 + exp(-gd)) * ud;
-    if (!shared) v *= (double)p.pair_weight[pair];
+    if (!shared) v *= (double)pw;
     return (float)v;
 }
 
@@ -355,7 +407,7 @@ __device__ __forceinline__ float dc_act_value(const MoeParams& p, float gv, floa
 template <uint32_t BODY>
 __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
                                              uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab_lane,
-                                             uint64_t* empty_bar, float (&acc)[2][4]) {
+                                             float (&acc)[2][4]) {
     uint4 ra[2], rb[2];
     float da[2], db[2];
     uint32_t sa[2], sb[2];
@@ -378,9 +430,6 @@ __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint
         sa[i] = wa >> (8u * q);  // this lane's groups 2q, 2q + 1 in the low byte
         sb[i] = wb >> (8u * q);
     }
-    // the slot is free once every lane has its words
-    __syncwarp();
-    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
     float D[2][4] = {}, E[2][4] = {};
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -420,10 +469,10 @@ __device__ __forceinline__ void dc_iq2_stage(uint32_t st_addr, uint32_t s0, uint
 
 // Q8_0 stage: 32-column blocks 2 st and 2 st + 1 (nblk of them) of the warp's two slices.
 template <uint32_t BODY>
+// xq: this lane's activations in the stage: column n's record holds chunk 4 j + q of the stage's
+// 64 columns at position 4 (4 j + q) + (stage % 4), i.e. xq + 256 j.
 __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt, uint32_t gq,
-                                            uint32_t q, uint32_t n, const unsigned char* xs, uint32_t K,
-                                            uint32_t blk0, uint32_t nblk, uint64_t* empty_bar,
-                                            float (&acc)[2][4]) {
+                                            uint32_t q, uint32_t xq, uint32_t nblk, float (&acc)[2][4]) {
     uint2 qa[2][2], qb[2][2];
     float da[2][2], db[2][2];
 #pragma unroll
@@ -442,12 +491,12 @@ __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint3
             da[i][j] = h2f(ha);
             db[i][j] = h2f(hb);
         }
-    __syncwarp();
-    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
 #pragma unroll
     for (uint32_t j = 0; j < 2; ++j) {
         if (j >= nblk) break;
-        const uint4 xv = *reinterpret_cast<const uint4*>(xs + dc_xs_offset(false, n, (blk0 + j) * 4u + q, K));
+        uint4 xv;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(xv.x), "=r"(xv.y), "=r"(xv.z), "=r"(xv.w)
+                     : "r"(xq + j * 256u));
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             uint32_t va[4], vb[4];
@@ -470,7 +519,7 @@ __device__ __forceinline__ void dc_q8_stage(uint32_t st_addr, uint32_t s0, uint3
 template <uint32_t BODY>
 __device__ __forceinline__ void dc_iq1_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
                                              uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab,
-                                             uint64_t* empty_bar, float (&acc)[2][4]) {
+                                             float (&acc)[2][4]) {
     uint2 qa[2], qb[2];
     uint32_t ha[2], hb[2];
     float da[2], db[2];
@@ -488,8 +537,6 @@ __device__ __forceinline__ void dc_iq1_stage(uint32_t st_addr, uint32_t s0, uint
         da[i] = h2f(xa);
         db[i] = h2f(xb);
     }
-    __syncwarp();
-    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
     float D[2][4] = {}, E[2][4] = {};
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -532,7 +579,7 @@ __device__ __forceinline__ void dc_iq1_stage(uint32_t st_addr, uint32_t s0, uint
 template <uint32_t BODY>
 __device__ __forceinline__ void dc_iq3_stage(uint32_t st_addr, uint32_t s0, uint32_t s1, uint32_t rt,
                                              uint32_t gq, uint32_t q, uint32_t xrow, uint32_t tab_lane,
-                                             uint64_t* empty_bar, float (&acc)[2][4]) {
+                                             float (&acc)[2][4]) {
     uint4 ia[2], ib[2];
     uint2 wa[2], wb[2];
     uint32_t sca[2], scb[2];
@@ -558,8 +605,6 @@ __device__ __forceinline__ void dc_iq3_stage(uint32_t st_addr, uint32_t s0, uint
         sca[i] = ta >> (8u * q);  // this lane's groups 2q, 2q + 1 in the low byte
         scb[i] = tb >> (8u * q);
     }
-    __syncwarp();
-    if ((threadIdx.x & 31u) == 0) tc::mbar_arrive(empty_bar);
     float D[2][4] = {}, E[2][4] = {};
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -640,25 +685,20 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
                                                                        uint32_t chunk, uint32_t splits) {
     constexpr uint32_t tfmt = TFMT;
     using Lay = DcL<BODY>;
+    constexpr uint32_t R = Lay::Ring;
     extern __shared__ __align__(1024) unsigned char smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     volatile uint32_t* abort = reinterpret_cast<volatile uint32_t*>(smem + Lay::MiscOff);
-    float* tok_scale = reinterpret_cast<float*>(smem + Lay::MiscOff + 16u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::BarOff);
-    uint64_t* empty = full + kDcRing;
-    const uint32_t K = GATEUP ? p.H : p.I;
-    unsigned char* xs = smem + Lay::XsOff;
+    uint64_t* empty = full + R;
     if constexpr (TFMT == kTypeIq2Xxs) mma::build_iq2_table(reinterpret_cast<uint4*>(smem), p.grids.iq2xxs);
     if constexpr (TFMT == kTypeIq1S) mma::build_iq1s_table(reinterpret_cast<uint4*>(smem), p.grids.iq1s);
     if constexpr (TFMT == kTypeIq3Xxs) mma::build_iq3_table(reinterpret_cast<uint2*>(smem), p.grids.iq3xxs);
-    for (uint32_t i = threadIdx.x; i < dc_xs_bytes(K) / 16u; i += blockDim.x)
-        reinterpret_cast<uint4*>(xs)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < kDcRing; ++s) {
+        for (uint32_t s = 0; s < R; ++s) {
             tc::mbar_init(full + s, 1);
             tc::mbar_init(empty + s, kDcConsumerWarps);
         }
-        tc::mbar_init(empty + kDcRing, kDcConsumerWarps);  // the consumers' own barrier
         *abort = 0u;
         tc::mbar_fence_init();
     }
@@ -674,62 +714,41 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
     const uint32_t s0 = warp >> 3, s1 = 2u + (warp >> 3), rt = (warp & 7u) * 16u;
     const uint32_t gq = lane >> 2, q = lane & 3u, n = lane >> 2, lane7 = lane & 7u;
     const uint4* hdr = reinterpret_cast<const uint4*>(smem + Lay::HdrOff);
-    const uint32_t xs_iq2_lane = tc::smem_u32(xs) + n * (K * 2u + 64u) + q * 16u;
+    // this lane's activation column n in a stage: its chunk q (256-column formats), or 64 q bytes
+    // further on for Q8_0
+    const uint32_t xs_lane = Lay::XsOff + n * kDcXsCol + q * 16u;
+    const uint32_t xs_lane_q8 = Lay::XsOff + n * kDcXsCol + q * 64u;
     const uint32_t tab = tc::smem_u32(smem);
     const uint32_t tab_lane = tab + (tfmt == kTypeIq3Xxs ? (lane & 15u) * 8u : lane7 * 16u);  // this lane's replica
-    uint64_t* cbar = empty + kDcRing;
-    uint32_t cphase = 0;
-    uint32_t staged_unit = 0xffffffffu;
-    bool staged_iq = false;  // staged for the 256-column formats (else for Q8_0)
     float acc[2][4] = {};
     DcWarpItem it{};
+    Unit u{};
+    float pw = 1.f;        // the pair's route weight (gate/up epilogue)
+    float inv = 1.f;       // 1 / the power-of-two prescale of the pair's activations
+    uint32_t out_row = 0;  // the pair's token (down epilogue writing out directly)
     for (uint32_t g = 0;; ++g) {
-        const uint32_t slot = g % kDcRing;
-        const bool ok = dc_wait(full + slot, (g / kDcRing) & 1u, abort);
+        const uint32_t slot = g % R;
+        const bool ok = dc_wait(full + slot, (g / R) & 1u, abort);
         if (!__all_sync(0xffffffffu, ok)) {
             if (lane == 0) dc_fail(p.counters + 3, abort);
             break;
         }
-        const uint4 h = hdr[slot];
+        const uint4 h = hdr[3u * slot];
         if (h.x == kDcEnd) break;
         if (h.y == h.w) {  // first stage of an item
-            it = dc_warp_item<GATEUP>(p, h.x, groups, splits, s0, s1);
-            const bool iq = it.fmt != kTypeQ8_0;
-            if (it.unit != staged_unit || iq != staged_iq) {
-                const Unit u = p.units[it.unit];
-                // every warp is done with the previous unit's activations and token scales
-                if (!dc_consumer_sync(cbar, cphase, abort)) {
-                    if (lane == 0) dc_fail(p.counters + 3, abort);
-                    break;
-                }
-                if (threadIdx.x < (uint32_t)kUnitTokens) {
-                    float sc = 1.f;
-                    if (threadIdx.x < u.count)
-                        sc = mma::prescale_for(__uint_as_float(GATEUP ? p.xmax[p.pair_token[u.pair_begin + threadIdx.x]]
-                                                                      : p.act_max[u.pair_begin + threadIdx.x]));
-                    tok_scale[threadIdx.x] = sc;
-                }
-                if (!dc_consumer_sync(cbar, cphase, abort)) {
-                    if (lane == 0) dc_fail(p.counters + 3, abort);
-                    break;
-                }
-                const float* rws[kUnitTokens];
-                float scl[kUnitTokens];
-#pragma unroll
-                for (int t = 0; t < kUnitTokens; ++t) {
-                    const uint32_t pair = u.pair_begin + (uint32_t)t;
-                    rws[t] = (uint32_t)t < u.count
-                                 ? (GATEUP ? p.x + (size_t)p.pair_token[pair] * p.H : p.act + (size_t)pair * p.I)
-                                 : nullptr;
-                    scl[t] = tok_scale[t];
-                }
-                dc_stage_xs(xs, rws, scl, K, u.count, iq);
-                if (!dc_consumer_sync(cbar, cphase, abort)) {
-                    if (lane == 0) dc_fail(p.counters + 3, abort);
-                    break;
-                }
-                staged_unit = it.unit;
-                staged_iq = iq;
+            const uint4 h2 = hdr[3u * slot + 1u];
+            const uint4 hmax = hdr[3u * slot + 2u];
+            it = dc_warp_item<GATEUP>(p, h.x, h2, groups, splits, s0, s1);
+            u.count = h2.x & 0xffu;
+            u.pair_begin = h2.y;
+            u.expert = h2.z;
+            // the epilogue's per-pair scalars, loaded now so that their latency hides behind the item
+            if (q < u.count) {
+                const uint32_t pair = u.pair_begin + q;
+                inv = 1.f / mma::prescale_for(__uint_as_float(q == 0u ? hmax.x : q == 1u ? hmax.y : q == 2u ? hmax.z
+                                                                                                      : hmax.w));  // exact
+                if (GATEUP) pw = (u.expert != p.E && !p.weight_after_down) ? p.pair_weight[pair] : 1.f;
+                else if (p.direct_out) out_row = p.pair_token[pair];
             }
 #pragma unroll
             for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -737,23 +756,24 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
         const uint32_t st_addr = tc::smem_u32(smem + Lay::RingOff + slot * Lay::Stage);
         if (it.fmt != kTypeQ8_0) {  // the CTA's IQ type (the loader sends no other)
             if constexpr (TFMT == kTypeIq2Xxs)
-                dc_iq2_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
+                dc_iq2_stage<BODY>(st_addr, s0, s1, rt, gq, q, st_addr + xs_lane, tab_lane, acc);
             if constexpr (TFMT == kTypeIq1S)
-                dc_iq1_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab, empty + slot, acc);
+                dc_iq1_stage<BODY>(st_addr, s0, s1, rt, gq, q, st_addr + xs_lane, tab, acc);
             if constexpr (TFMT == kTypeIq3Xxs)
-                dc_iq3_stage<BODY>(st_addr, s0, s1, rt, gq, q, xs_iq2_lane + h.y * 512u, tab_lane, empty + slot, acc);
+                dc_iq3_stage<BODY>(st_addr, s0, s1, rt, gq, q, st_addr + xs_lane, tab_lane, acc);
         } else {
-            const uint32_t blk0 = 2u * h.y;
-            const uint32_t nblk = blk0 + 1u < it.bpr ? 2u : 1u;
-            dc_q8_stage<BODY>(st_addr, s0, s1, rt, gq, q, n, xs, K, blk0, nblk, empty + slot, acc);
+            const uint32_t nblk = 2u * h.y + 1u < it.bpr ? 2u : 1u;
+            dc_q8_stage<BODY>(st_addr, s0, s1, rt, gq, q, st_addr + xs_lane_q8 + (h.y & 3u) * 16u, nblk, acc);
         }
+        // the slot goes back to the loader once this warp's loads of it (weights and activations)
+        // have completed: the MMAs that consume them have issued
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(empty + slot);
         if (h.y + 1u == h.z) {  // last stage of the item
             if (splits > 1u && !dc_join_splits(p, h.x, splits, warp, lane, acc)) continue;
             // this warp's rows are complete
-            const Unit u = p.units[it.unit];
             if (q < u.count) {
                 const uint32_t pair = u.pair_begin + q;
-                const float inv = 1.f / tok_scale[q];  // exact: a power of two
                 if (GATEUP) {
                     const bool shared = u.expert == p.E;
                     const uint32_t row_base = it.tile0 * kTileRows + rt + gq;
@@ -763,12 +783,12 @@ __global__ void __launch_bounds__(kDcThreads, 1) decode_experts_kernel(const __g
                         if (!it.valid0 || row >= p.I) continue;
                         const float gv = (acc[0][2 * hi] + acc[0][2 * hi + 1]) * inv;
                         const float uv = (acc[1][2 * hi] + acc[1][2 * hi + 1]) * inv;
-                        const float a = dc_act_value(p, gv, uv, shared, pair);
+                        const float a = dc_act_value(p, gv, uv, shared, pw);
                         p.act[(size_t)pair * p.I + row] = a;
                         atomicMax(p.act_max + pair, __float_as_uint(fabsf(a)));
                     }
                 } else {
-                    float* yrow = p.direct_out ? p.out + (size_t)p.pair_token[pair] * p.H : p.y + (size_t)pair * p.H;
+                    float* yrow = p.direct_out ? p.out + (size_t)out_row * p.H : p.y + (size_t)pair * p.H;
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
                         if (!(i ? it.valid1 : it.valid0)) continue;
@@ -803,7 +823,7 @@ static DcChoice dc_choice(const MoeParams& p, bool gateup) {
     else if (mask & fmt_bit(kTypeIq1S)) c.tfmt = kTypeIq1S;
     else if (mask & fmt_bit(kTypeIq3Xxs)) c.tfmt = kTypeIq3Xxs;
     c.large = c.tfmt == kTypeIq3Xxs;
-    c.smem = (c.large ? DcL<kDcBodyLarge>::XsOff : DcL<kDcBodySmall>::XsOff) + dc_xs_bytes(K);
+    c.smem = c.large ? DcL<kDcBodyLarge>::End : DcL<kDcBodySmall>::End;
     if (g_optin_smem == 0) {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -812,7 +832,7 @@ static DcChoice dc_choice(const MoeParams& p, bool gateup) {
     if (c.large && c.smem > (size_t)g_optin_smem) {  // IQ3_XXS does not fit: CUDA cores take it
         c.tfmt = 0;
         c.large = false;
-        c.smem = DcL<kDcBodySmall>::XsOff + dc_xs_bytes(K);
+        c.smem = DcL<kDcBodySmall>::End;
     }
     return c;
 }
@@ -863,8 +883,45 @@ cudaError_t launch_decode_carve(const MoeParams& p, unsigned n_sms, size_t smem,
     return cudaGetLastError();
 }
 
+// The phase's activation image (dc_image_kernel): gate/up converts the T token rows into the
+// prefill operand buffer, down converts the pairs' act rows in place (after every reader of act
+// as f32: the CUDA-core kernels of the phase run before).
+// One record of the image kernel's shared-memory limit per device (both phases launch it): it
+// only ever grows.
+static std::mutex g_image_mu;
+static std::vector<size_t> g_image_smem;
+
+template <bool GATEUP>
+cudaError_t launch_decode_image(const MoeParams& p, cudaStream_t s) {
+    const uint32_t K = GATEUP ? p.H : p.I;
+    const uint32_t rows = GATEUP ? p.T : p.T * p.k + (p.has_shared ? p.T : 0u);
+    if (rows == 0) return cudaSuccess;
+    const size_t smem = (size_t)K * sizeof(float);
+    std::mutex& mu = g_image_mu;
+    std::vector<size_t>& configured = g_image_smem;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (configured.size() <= (size_t)dev) configured.resize((size_t)dev + 1, 0);
+        if (configured[(size_t)dev] < smem) {
+            if ((e = cudaFuncSetAttribute(dc_image_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+                cudaSuccess)
+                return e;
+            configured[(size_t)dev] = smem;
+        }
+    }
+    dc_image_kernel<<<rows, 256, smem, s>>>(GATEUP ? p.x : p.act, K, GATEUP ? p.xmax : p.act_max,
+                                            GATEUP ? reinterpret_cast<unsigned char*>(p.xperm)
+                                                   : reinterpret_cast<unsigned char*>(p.act));
+    return cudaGetLastError();
+}
+
 template <bool GATEUP>
 cudaError_t launch_decode(const MoeParams& p, unsigned n_sms, cudaStream_t s) {
+    cudaError_t e = launch_decode_image<GATEUP>(p, s);
+    if (e != cudaSuccess) return e;
     const DcChoice c = dc_choice(p, GATEUP);
     if (c.tfmt == kTypeIq3Xxs) return launch_decode_carve<GATEUP, kDcBodyLarge, kTypeIq3Xxs>(p, n_sms, c.smem, s);
     if (c.tfmt == kTypeIq1S) return launch_decode_carve<GATEUP, kDcBodySmall, kTypeIq1S>(p, n_sms, c.smem, s);
