@@ -13,17 +13,21 @@
 // tokens each, so the kernel is a stream of weights through the SMs: each weight is decoded once
 // into an A-fragment register and multiplied against 4 tokens x (hi, lo) activation pieces. The
 // SM-side cost per weight (table lookup, scale, sign flip) is what bounds it, so nothing else may
-// stall the decoding warps: one loader lane per CTA moves the packed weights with bulk copies into
-// a 3-stage ring (110 KB in flight per SM), and 16 consumer warps only decode and multiply.
+// stall the decoding warps: one loader warp per CTA moves the packed weights and the unit's
+// activations for the same columns with bulk copies into a 4-stage ring (~160 KB in flight per
+// SM), and 16 consumer warps only decode and multiply. The activations come from an image that
+// dc_image_kernel writes once per token (gate/up) or pair (down) before the launch.
 //
 // Work decomposition. A unit (<= 4 pairs of one expert, ordered by expert) and a row group form
 // an item: gate/up items cover 256 rows of W1 and the same 256 rows of W3, down items 512 rows of
 // W2. A stage is one K-chunk of the item: four 128-row tile block columns ("slices", 8 KB of
-// packed weights each: 256 IQ2_XXS or 64 Q8_0 columns) with their block scales. Consumer warp w
-// owns 16 rows of two slices (gate: W1 and W3 of tile w / 8; down: tiles w / 8 and 2 + w / 8), so
-// every warp reads every stage and finishes its rows' sums itself: no cross-warp reduction. The
-// loader takes items from a global counter in chunks of neighbouring items (same unit: the staged
-// activations are reused) and tells the consumers what each stage holds through a stage header.
+// packed weights each: 256 IQ2_XXS or 64 Q8_0 columns) with their block scales, and the unit's
+// activation columns. Consumer warp w owns 16 rows of two slices (gate: W1 and W3 of tile w / 8;
+// down: tiles w / 8 and 2 + w / 8), so every warp reads every stage and finishes its rows' sums
+// itself: no cross-warp reduction. The loader takes items from a global counter in chunks of
+// neighbouring items, fetching each item's scalars one item ahead, and tells the consumers what a
+// stage holds through its stage header (item, K range, unit, storage type, the tokens' prescale
+// words): the consumers make no global loads at item boundaries.
 //
 // Every wait is bounded by a 2 s limit; one that runs out sets error bit 8 of the layer flags and
 // an abort word that ends every other wait of the CTA, so a broken pipeline ends the kernel with
