@@ -294,6 +294,9 @@ def run_ours(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(W, x_host, budget_s=args.cpu_budget)
+        # the same sample on one host thread (the reference's serial matvec path)
+        one = cpu_baseline(W, x_host, budget_s=args.cpu_budget / 3, threads=1)
+        result["cpu_baseline"]["single_thread"] = {"value": one["value"], "cores": 1, "sample": one["sample"]}
     if not args.no_configs:
         result["configs"] = run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=(W, layer))
     layer.destroy()
@@ -595,7 +598,7 @@ def cpu_baseline(W, x, budget_s: float, threads: int | None = None, logits=None,
 
 # ---- decode-size objects of the other benchmark configurations ---------------------------------
 
-MMA_TYPES = (8, 16)  # Q8_0, IQ2_XXS: the tensor-core decode kernels; IQ3_XXS / IQ1_S: CUDA cores
+MMA_TYPES = (8, 16, 18, 19)  # Q8_0, IQ2_XXS, IQ3_XXS, IQ1_S: all on the decode_experts_kernel instances
 
 
 def kernels_per_forward(spec, T, logits_given=False, norm=False):
@@ -606,7 +609,7 @@ def kernels_per_forward(spec, T, logits_given=False, norm=False):
     n += 1  # top-k route
     n += 1 if T * spec.top_k <= 4096 else 3  # dispatch
     if any(t in MMA_TYPES for t in types):
-        n += 2
+        n += 4  # per phase: the activation image, then the decode kernel
     if any(t not in MMA_TYPES for t in types):
         n += 2
     return n + 1  # combine
