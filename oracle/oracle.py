@@ -59,7 +59,7 @@ _LAYER_FIELDS = [
 
 class _OracleLayer(C.Structure):
     _fields_ = _LAYER_FIELDS + [("grid_iq1_s", C.c_void_p), ("grid_iq2_xxs", C.c_void_p),
-                                ("grid_iq3_xxs", C.c_void_p)]
+                                ("grid_iq3_xxs", C.c_void_p), ("grid_iq2_s", C.c_void_p)]
 
 
 class _RefLayer(C.Structure):
@@ -107,6 +107,8 @@ class _LayerBuilder:
             L.grid_iq1_s = gb[19].ctypes.data
             L.grid_iq2_xxs = gb[16].ctypes.data
             L.grid_iq3_xxs = gb[18].ctypes.data
+            if 22 in gb:
+                L.grid_iq2_s = gb[22].ctypes.data
         self.layer = L
 
 

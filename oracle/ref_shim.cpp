@@ -62,6 +62,7 @@ size_t vlr_grid(uint32_t type, void* out, size_t cap) {
     if (type == vi::kGgmlTypeIq1S) g = std::as_bytes(vi::iq1_s_grid_table());
     else if (type == vi::kGgmlTypeIq2Xxs) g = std::as_bytes(vi::iq2_xxs_grid_table());
     else if (type == vi::kGgmlTypeIq3Xxs) g = std::as_bytes(vi::iq3_xxs_grid_table());
+    else if (type == vi::kGgmlTypeIq2S) g = std::as_bytes(vi::iq2_s_grid_table());
     else return 0;
     if (out && cap >= g.size()) std::memcpy(out, g.data(), g.size());
     return g.size();
@@ -77,6 +78,11 @@ int vlr_dequantize(uint32_t type, const uint8_t* enc, size_t nbytes, float* out,
         case vi::kGgmlTypeIq2Xxs: r = vi::dequantize_iq2_xxs(e, o, lim); break;
         case vi::kGgmlTypeIq3Xxs: r = vi::dequantize_iq3_xxs(e, o, lim); break;
         case vi::kGgmlTypeIq1S: r = vi::dequantize_iq1_s(e, o, lim); break;
+        case vi::kGgmlTypeQ4K: r = vi::dequantize_q4_k(e, o, lim); break;
+        case vi::kGgmlTypeQ5K: r = vi::dequantize_q5_k(e, o, lim); break;
+        case vi::kGgmlTypeQ6K: r = vi::dequantize_q6_k(e, o, lim); break;
+        case vi::kGgmlTypeIq2S: r = vi::dequantize_iq2_s(e, o, lim); break;
+        case vi::kGgmlTypeMxfp4: r = vi::dequantize_mxfp4(e, o, lim); break;
         default: return -2;
     }
     return r ? 0 : -1;

@@ -20,6 +20,11 @@ int vlo_block_layout(uint32_t type, size_t* block_elems, size_t* block_bytes) {
         case VLO_TYPE_IQ2_XXS: *block_elems = 256; *block_bytes = 66; return 0;
         case VLO_TYPE_IQ3_XXS: *block_elems = 256; *block_bytes = 98; return 0;
         case VLO_TYPE_IQ1_S: *block_elems = 256; *block_bytes = 50; return 0;
+        case VLO_TYPE_Q4_K: *block_elems = 256; *block_bytes = 144; return 0;
+        case VLO_TYPE_Q5_K: *block_elems = 256; *block_bytes = 176; return 0;
+        case VLO_TYPE_Q6_K: *block_elems = 256; *block_bytes = 210; return 0;
+        case VLO_TYPE_IQ2_S: *block_elems = 256; *block_bytes = 82; return 0;
+        case VLO_TYPE_MXFP4: *block_elems = 32; *block_bytes = 17; return 0;
         default: return -1;
     }
 }
@@ -173,12 +178,137 @@ static int decode_iq1_s(const uint8_t* b, const uint64_t* grid, float* out) {
     return 0;
 }
 
+/* qk_scale_min, ggml_quantization.cpp:437-455: the 6-bit scale and minimum of sub-block j of a
+ * Q4_K / Q5_K block from its 12 packed bytes (j < 4: low six bits of bytes j and j + 4; else four
+ * bits of byte j + 4 and the top two bits of bytes j - 4 and j). */
+static void qk_scale_min(uint32_t j, const uint8_t* s, uint32_t* sc, uint32_t* mn) {
+    if (j < 4) {
+        *sc = s[j] & 63u;
+        *mn = s[j + 4] & 63u;
+    } else {
+        *sc = (s[j + 4] & 15u) | ((uint32_t)(s[j - 4] >> 6) << 4);
+        *mn = (s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+    }
+}
+
+/* decode_q4_k_block, ggml_quantization.cpp:457-493: d, dmin, 12 scale bytes, 128 nibble bytes; the
+ * 32 bytes of pair p hold sub-block 2p in their low nibbles and 2p + 1 in their high nibbles;
+ * w = d * sc - dmin * m rounded as (d * sc) * q - (dmin * m). */
+static int decode_q4_k(const uint8_t* b, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b)), dmin = vlo_fp16_to_float(rd16(b + 2));
+    if (!isfinite(d) || !isfinite(dmin)) return -1;
+    const uint8_t* q = b + 16;
+    for (uint32_t p = 0; p < 4; ++p) {
+        uint32_t s1, m1, s2, m2;
+        qk_scale_min(2 * p, b + 4, &s1, &m1);
+        qk_scale_min(2 * p + 1, b + 4, &s2, &m2);
+        const float d1 = d * (float)s1, n1 = dmin * (float)m1, d2 = d * (float)s2, n2 = dmin * (float)m2;
+        for (uint32_t l = 0; l < 32; ++l) {
+            out[64 * p + l] = d1 * (float)(q[32 * p + l] & 15u) - n1;
+            out[64 * p + 32 + l] = d2 * (float)(q[32 * p + l] >> 4) - n2;
+        }
+    }
+    return 0;
+}
+
+/* decode_q5_k_block, ggml_quantization.cpp:495-539: as Q4_K with a fifth bit per weight from the 32
+ * qh bytes: sub-block 2p takes bit 2p of qh[l], sub-block 2p + 1 bit 2p + 1. */
+static int decode_q5_k(const uint8_t* b, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b)), dmin = vlo_fp16_to_float(rd16(b + 2));
+    if (!isfinite(d) || !isfinite(dmin)) return -1;
+    const uint8_t* qh = b + 16;
+    const uint8_t* q = b + 48;
+    for (uint32_t p = 0; p < 4; ++p) {
+        uint32_t s1, m1, s2, m2;
+        qk_scale_min(2 * p, b + 4, &s1, &m1);
+        qk_scale_min(2 * p + 1, b + 4, &s2, &m2);
+        const float d1 = d * (float)s1, n1 = dmin * (float)m1, d2 = d * (float)s2, n2 = dmin * (float)m2;
+        for (uint32_t l = 0; l < 32; ++l) {
+            const uint32_t v1 = (q[32 * p + l] & 15u) + ((qh[l] >> (2 * p)) & 1u ? 16u : 0u);
+            const uint32_t v2 = (q[32 * p + l] >> 4) + ((qh[l] >> (2 * p + 1)) & 1u ? 16u : 0u);
+            out[64 * p + l] = d1 * (float)v1 - n1;
+            out[64 * p + 32 + l] = d2 * (float)v2 - n2;
+        }
+    }
+    return 0;
+}
+
+/* decode_q6_k_block, ggml_quantization.cpp:541-590: 128 low-nibble bytes, 64 high-bit bytes, 16
+ * int8 scales, then the fp16 d (last). Per half h of 128 weights and l < 32, the four weights
+ * h*128 + 32 i + l take nibble (i / 2) of low byte 64 h + 32 (i % 2) + l and bits 2 i of high byte
+ * 32 h + l, minus 32; w = (d * scale[8 h + l / 16 + 2 i]) * q. */
+static int decode_q6_k(const uint8_t* b, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b + 208));
+    if (!isfinite(d)) return -1;
+    for (uint32_t h = 0; h < 2; ++h) {
+        const uint8_t* lo = b + 64 * h;
+        const uint8_t* hi = b + 128 + 32 * h;
+        const int8_t* sc = (const int8_t*)(b + 192 + 8 * h);
+        for (uint32_t l = 0; l < 32; ++l) {
+            for (uint32_t i = 0; i < 4; ++i) {
+                const uint32_t byte = lo[32 * (i & 1) + l];
+                const int q = (int)((i < 2 ? byte & 15u : byte >> 4) | (((hi[l] >> (2 * i)) & 3u) << 4)) - 32;
+                out[128 * h + 32 * i + l] = d * (float)sc[l / 16 + 2 * i] * (float)q;
+            }
+        }
+    }
+    return 0;
+}
+
+/* decode_iq2_s_block, ggml_quantization.cpp:285-334: d, 32 grid-index bytes, 32 sign bytes, 8 qh
+ * bytes (two high index bits per sub-block), 8 scale bytes (low nibble for sub-blocks 0-1 of the
+ * group, high nibble for 2-3); w = ((d * (0.5 + s)) * 0.25) * m, negated where the sign bit is set. */
+static int decode_iq2_s(const uint8_t* b, const uint64_t* grid, float* out) {
+    const float d = vlo_fp16_to_float(rd16(b));
+    if (!isfinite(d)) return -1;
+    const uint8_t* qs = b + 2;
+    const uint8_t* signs = b + 34;
+    const uint8_t* qh = b + 66;
+    const uint8_t* scales = b + 74;
+    for (uint32_t g = 0; g < 8; ++g) {
+        const float lo = d * (0.5f + (float)(scales[g] & 15u)) * 0.25f;
+        const float hi = d * (0.5f + (float)(scales[g] >> 4)) * 0.25f;
+        for (uint32_t s = 0; s < 4; ++s) {
+            const float ls = s < 2 ? lo : hi;
+            const uint32_t idx = qs[4 * g + s] | (((uint32_t)qh[g] << (8 - 2 * s)) & 0x300u);
+            const uint64_t gv = grid[idx];
+            const uint32_t sg = signs[4 * g + s];
+            for (uint32_t l = 0; l < 8; ++l) {
+                const float m = ls * (float)((gv >> (8 * l)) & 0xffu);
+                out[32 * g + 8 * s + l] = (sg >> l) & 1u ? -m : m;
+            }
+        }
+    }
+    return 0;
+}
+
+/* e8m0_to_float_half, ggml_quantization.cpp:112-120, and decode_mxfp4_block :381-398: half the
+ * power of two of the E8M0 byte (bytes 0 and 1: the two smallest half-scaled powers) times the
+ * doubled E2M1 value of each nibble; byte i holds weight i (low nibble) and i + 16 (high). */
+static const int8_t kMxfp4[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+static int decode_mxfp4(const uint8_t* b, float* out) {
+    const uint32_t e = b[0];
+    const float scale = u2f(e < 2 ? 0x00200000u << e : (e - 1u) << 23);
+    for (uint32_t i = 0; i < 16; ++i) {
+        const float lo = (float)kMxfp4[b[1 + i] & 15u] * scale, hi = (float)kMxfp4[b[1 + i] >> 4] * scale;
+        if (!isfinite(lo) || !isfinite(hi)) return -1;
+        out[i] = lo;
+        out[i + 16] = hi;
+    }
+    return 0;
+}
+
 static int decode_block(uint32_t type, const uint8_t* b, const void* grid, float* out) {
     switch (type) {
         case VLO_TYPE_Q8_0: return decode_q8_0(b, out);
         case VLO_TYPE_IQ2_XXS: return decode_iq2_xxs(b, (const uint64_t*)grid, out);
         case VLO_TYPE_IQ3_XXS: return decode_iq3_xxs(b, (const uint32_t*)grid, out);
         case VLO_TYPE_IQ1_S: return decode_iq1_s(b, (const uint64_t*)grid, out);
+        case VLO_TYPE_Q4_K: return decode_q4_k(b, out);
+        case VLO_TYPE_Q5_K: return decode_q5_k(b, out);
+        case VLO_TYPE_Q6_K: return decode_q6_k(b, out);
+        case VLO_TYPE_IQ2_S: return decode_iq2_s(b, (const uint64_t*)grid, out);
+        case VLO_TYPE_MXFP4: return decode_mxfp4(b, out);
         case VLO_TYPE_F32: memcpy(out, b, 4); return isfinite(out[0]) ? 0 : -1;
         default: return -2;
     }
@@ -451,6 +581,7 @@ static const void* grid_for(const vlo_moe_layer* L, uint32_t type) {
         case VLO_TYPE_IQ1_S: return L->grid_iq1_s;
         case VLO_TYPE_IQ2_XXS: return L->grid_iq2_xxs;
         case VLO_TYPE_IQ3_XXS: return L->grid_iq3_xxs;
+        case VLO_TYPE_IQ2_S: return L->grid_iq2_s;
         default: return NULL;
     }
 }

@@ -27,6 +27,11 @@ extern "C" {
 #define VLO_TYPE_IQ2_XXS 16u
 #define VLO_TYPE_IQ3_XXS 18u
 #define VLO_TYPE_IQ1_S 19u
+#define VLO_TYPE_Q4_K 12u
+#define VLO_TYPE_Q5_K 13u
+#define VLO_TYPE_Q6_K 14u
+#define VLO_TYPE_IQ2_S 22u
+#define VLO_TYPE_MXFP4 39u
 
 /* Routing score functions. SQRT_SOFTPLUS and SOFTMAX are the reference's; SIGMOID has no
  * reference router (parity unpinned) and reuses route_from_indices semantics with a sigmoid
@@ -108,6 +113,7 @@ typedef struct vlo_moe_layer {
     const void* grid_iq1_s;
     const void* grid_iq2_xxs;
     const void* grid_iq3_xxs;
+    const void* grid_iq2_s;
 } vlo_moe_layer;
 
 /* One MoE layer over T tokens: out f32[T x H]; idx/weights [T x k] receive the route. Optional

@@ -87,6 +87,99 @@ def q8_0_encoder_source() -> np.ndarray:
             + (c % 5).astype(np.float32) * np.float32(0.00390625)).astype(np.float32)
 
 
+MIN_SCALES = (0x3800, 0xBC00, 0x3000, 0x3C00, 0x0001, 0x0400)  # tests/test_main.cpp:946-947
+
+
+def q4_k_blocks() -> np.ndarray:
+    """tests/test_main.cpp:976-989 (Q4_K part of test_trunk_storage_reference_kernels)."""
+    b = bytearray(len(SCALES) * 144)
+    for blk, s in enumerate(SCALES):
+        base = blk * 144
+        _put16(b, base, s)
+        _put16(b, base + 2, MIN_SCALES[blk])
+        for i in range(12):
+            b[base + 4 + i] = (blk * 29 + i * 47 + 7) & 0xFF
+        for i in range(128):
+            b[base + 16 + i] = (blk * 37 + i * 53 + 11) & 0xFF
+    return np.frombuffer(bytes(b), np.uint8).copy()
+
+
+def q5_k_blocks() -> np.ndarray:
+    """tests/test_main.cpp:1019-1037 (Q5_K part)."""
+    b = bytearray(len(SCALES) * 176)
+    for blk, s in enumerate(SCALES):
+        base = blk * 176
+        _put16(b, base, s)
+        _put16(b, base + 2, MIN_SCALES[blk])
+        for i in range(12):
+            b[base + 4 + i] = (blk * 29 + i * 47 + 7) & 0xFF
+        for i in range(32):
+            b[base + 16 + i] = (blk * 41 + i * 31 + 13) & 0xFF
+        for i in range(128):
+            b[base + 48 + i] = (blk * 37 + i * 53 + 11) & 0xFF
+    return np.frombuffer(bytes(b), np.uint8).copy()
+
+
+def q6_k_blocks() -> np.ndarray:
+    """tests/test_main.cpp:1057-1072 (Q6_K part)."""
+    b = bytearray(len(SCALES) * 210)
+    for blk, s in enumerate(SCALES):
+        base = blk * 210
+        for i in range(128):
+            b[base + i] = (blk * 37 + i * 53 + 11) & 0xFF
+        for i in range(64):
+            b[base + 128 + i] = (blk * 41 + i * 31 + 13) & 0xFF
+        for i in range(16):
+            b[base + 192 + i] = (blk * 59 + i * 43 + 17) & 0xFF
+        _put16(b, base + 208, s)
+    return np.frombuffer(bytes(b), np.uint8).copy()
+
+
+def iq2_s_blocks() -> np.ndarray:
+    """tests/test_main.cpp:1725-1753 (test_iq2_s_reference_kernel)."""
+    b = bytearray(len(SCALES) * 82)
+    for blk, s in enumerate(SCALES):
+        base = blk * 82
+        _put16(b, base, s)
+        for i in range(32):
+            b[base + 2 + i] = (blk * 733 + i * 977 + 0x1234) & 0xFF
+        for i in range(32):
+            b[base + 34 + i] = (blk * 251 + i * 131 + 0x5AA5) & 0xFF
+        for i in range(8):
+            b[base + 66 + i] = (blk * 97 + i * 43 + 0x3C) & 0xFF
+        for i in range(8):
+            b[base + 74 + i] = (blk * 61 + i * 29 + 0x17) & 0xFF
+    return np.frombuffer(bytes(b), np.uint8).copy()
+
+
+PARITY_MINIMUMS = (0x3800, 0x3555, 0xBC00, 0x0001, 0x4200, 0x0400)  # tests/test_main.cpp:1666-1667
+
+
+def q4_k_parity_blocks() -> np.ndarray:
+    """tests/test_main.cpp:1668-1683 (test_q4k_mxfp4_reference_parity, Q4_K part)."""
+    b = bytearray(len(SCALES) * 144)
+    for blk, s in enumerate(SCALES):
+        base = blk * 144
+        _put16(b, base, s)
+        _put16(b, base + 2, PARITY_MINIMUMS[blk])
+        for i in range(12):
+            b[base + 4 + i] = (blk * 37 + i * 53 + 0x2B) & 0xFF
+        for i in range(128):
+            b[base + 16 + i] = (blk * 733 + i * 977 + 0x1234) & 0xFF
+    return np.frombuffer(bytes(b), np.uint8).copy()
+
+
+def mxfp4_blocks() -> np.ndarray:
+    """tests/test_main.cpp:1701-1709 (test_q4k_mxfp4_reference_parity, MXFP4 part)."""
+    b = bytearray(len(SCALES) * 17)
+    for blk in range(len(SCALES)):
+        base = blk * 17
+        b[base] = 120 + blk * 3
+        for i in range(16):
+            b[base + 1 + i] = (blk * 91 + i * 167 + 0x5A) & 0xFF
+    return np.frombuffer(bytes(b), np.uint8).copy()
+
+
 # Pinned answers. (hash of all decoded f32 bits, selected decoded values, 3-row matvec outputs
 # with an absolute tolerance where the reference uses one.)
 ANSWERS = {
@@ -107,6 +200,34 @@ ANSWERS = {
         hash=0x25EDD1A40129EE99,
         values={0: 11.0, 7: 126.0, 8: -77.0, 31: 118.0, 32: -24.0, 63: 50.5, 127: -54.0},
         matvec=[(-168.55859375, 0.0), (-2.8284435272216797, 0.0), (0.0058367089368402958, 0.0)]),
+    "q4_k": dict(  # tests/test_main.cpp:992-1005
+        hash=0x84E8E84336EA0AD7,
+        values={0: 75.5, 7: 96.5, 8: 19.5, 31: 40.5, 32: -25.0, 63: 353.0, 127: 12.0, 255: 212.0, 256: 32.0,
+                511: -125.5},
+        matvec=[(281.6796875, 0.0), (-792.12872314453125, 0.0), (0.0096547976136207581, 0.0)]),
+    "q5_k": dict(  # tests/test_main.cpp:1040-1054
+        hash=0x3EC4A59589931118,
+        values={0: 187.5, 7: 96.5, 8: 131.5, 31: 40.5, 32: -25.0, 63: 1217.0, 127: 332.0, 255: 916.0,
+                256: 32.0, 511: -453.5},
+        matvec=[(668.2421875, 0.0), (1631.9100341796875, 0.0), (-0.046117834746837616, 0.0)]),
+    "q6_k": dict(  # tests/test_main.cpp:1074-1088
+        hash=0xCD39C3F1219AFBC9,
+        values={0: -85.0, 7: 238.0, 8: -221.0, 31: 360.0, 32: 2781.0, 63: -2420.0, 127: 1054.0, 255: -530.0,
+                511: 540.5},
+        matvec=[(-4684.79296875, 0.0), (7494.287109375, 0.0), (0.5950310230255127, 0.0)]),
+    "iq2_s": dict(  # tests/test_main.cpp:1766-1783
+        hash=0x785968D455DE0695,
+        values={0: -15.0, 7: -15.0, 8: 15.0, 31: 3.0, 32: -9.0, 63: 21.875, 127: 40.625, 255: -29.0,
+                256: -4.5, 511: -8.0625},
+        matvec=[(209.540527, 0.0), (274.050537, 0.0), (0.0192997903, 1e-9)]),
+    "q4_k_parity": dict(  # tests/test_main.cpp:1694-1699
+        hash=0x4A61F0F8094737CC,
+        values={0: 140.5, 1: 183.5, 31: 97.5, 32: 70.0, 127: 85.0, 255: 680.5},
+        matvec=None),
+    "mxfp4": dict(  # tests/test_main.cpp:1720-1722
+        hash=0xCE2B9AA19EF0E448,
+        values={0: -0.0078125, 1: 0.00390625, 2: 0.0, 3: -0.046875, 4: 0.03125},
+        matvec=None),
 }
 Q8_0_ENCODER_FINGERPRINT = 0x083A653165A92C21  # tests/test_main.cpp:920
 
@@ -116,6 +237,12 @@ KAT_SETS = {
     "iq2_xxs": (iq2_xxs_blocks, 16, 512),
     "iq3_xxs": (iq3_xxs_blocks, 18, 512),
     "q8_0": (q8_0_blocks, 8, 64),
+    "q4_k": (q4_k_blocks, 12, 512),
+    "q5_k": (q5_k_blocks, 13, 512),
+    "q6_k": (q6_k_blocks, 14, 512),
+    "iq2_s": (iq2_s_blocks, 22, 512),
+    "q4_k_parity": (q4_k_parity_blocks, 12, 512),
+    "mxfp4": (mxfp4_blocks, 39, 64),
 }
 
 

@@ -37,6 +37,11 @@ TYPE_Q8_0 = 8
 TYPE_IQ2_XXS = 16
 TYPE_IQ3_XXS = 18
 TYPE_IQ1_S = 19
+TYPE_Q4_K = 12
+TYPE_Q5_K = 13
+TYPE_Q6_K = 14
+TYPE_IQ2_S = 22
+TYPE_MXFP4 = 39
 
 SCORE_SQRT_SOFTPLUS = 0
 SCORE_SIGMOID = 1
@@ -50,6 +55,11 @@ BLOCK_LAYOUT = {
     TYPE_IQ2_XXS: (256, 66),
     TYPE_IQ3_XXS: (256, 98),
     TYPE_IQ1_S: (256, 50),
+    TYPE_Q4_K: (256, 144),
+    TYPE_Q5_K: (256, 176),
+    TYPE_Q6_K: (256, 210),
+    TYPE_IQ2_S: (256, 82),
+    TYPE_MXFP4: (32, 17),
 }
 
 ERROR_CODES = {

@@ -15,8 +15,8 @@ from typing import Optional
 
 import numpy as np
 
-from . import (BLOCK_LAYOUT, SCORE_SIGMOID, SCORE_SOFTMAX, SCORE_SQRT_SOFTPLUS, TYPE_IQ1_S,
-               TYPE_IQ2_XXS, TYPE_IQ3_XXS, TYPE_Q8_0)
+from . import (BLOCK_LAYOUT, SCORE_SIGMOID, SCORE_SOFTMAX, SCORE_SQRT_SOFTPLUS, TYPE_IQ1_S, TYPE_IQ2_S,
+               TYPE_IQ2_XXS, TYPE_IQ3_XXS, TYPE_MXFP4, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_0)
 
 
 def _fp16_bits(v: np.ndarray) -> np.ndarray:
@@ -30,16 +30,31 @@ def blocks(rng: np.random.Generator, ggml_type: int, n_blocks: int, d_scale: flo
     IQ2_XXS : d = |N(0,1)| * d_scale, 32 uniformly random u16 qs words         (66 B)
     IQ3_XXS : d = |N(0,1)| * d_scale, 96 random packed bytes                   (98 B)
     IQ1_S   : d = |N(0,1)| * d_scale, 32 random qs bytes, 8 random u16 qh      (50 B)
+    Q4_K/Q5_K: d and dmin = |N(0,1)| * d_scale, the rest random bytes       (144 / 176 B)
+    Q6_K    : 208 random bytes, then d = |N(0,1)| * d_scale                  (210 B)
+    IQ2_S   : d = |N(0,1)| * d_scale, 80 random bytes                        (82 B)
+    MXFP4   : an E8M0 scale byte in [118, 126] (2^-10 .. 2^-2), 16 random nibble bytes (17 B)
     """
     _, bb = BLOCK_LAYOUT[ggml_type]
     out = np.empty((n_blocks, bb), dtype=np.uint8)
+    if ggml_type == TYPE_MXFP4:
+        out[:, 0] = rng.integers(118, 127, size=n_blocks, dtype=np.uint8)
+        out[:, 1:] = rng.integers(0, 256, size=(n_blocks, bb - 1), dtype=np.uint8)
+        return out.reshape(-1)
     d = _fp16_bits(np.abs(rng.standard_normal(n_blocks)) * d_scale)
-    out[:, 0] = d & 0xFF
-    out[:, 1] = d >> 8
-    if ggml_type == TYPE_Q8_0:
+    at = 208 if ggml_type == TYPE_Q6_K else 0
+    if ggml_type == TYPE_Q6_K:
+        out[:, :208] = rng.integers(0, 256, size=(n_blocks, 208), dtype=np.uint8)
+    elif ggml_type == TYPE_Q8_0:
         out[:, 2:] = rng.integers(-127, 128, size=(n_blocks, 32), dtype=np.int16).astype(np.int8).view(np.uint8)
     else:
         out[:, 2:] = rng.integers(0, 256, size=(n_blocks, bb - 2), dtype=np.uint8)
+    out[:, at] = d & 0xFF
+    out[:, at + 1] = d >> 8
+    if ggml_type in (TYPE_Q4_K, TYPE_Q5_K):
+        dmin = _fp16_bits(np.abs(rng.standard_normal(n_blocks)) * d_scale)
+        out[:, 2] = dmin & 0xFF
+        out[:, 3] = dmin >> 8
     return out.reshape(-1)
 
 
@@ -48,7 +63,8 @@ def matrix(rng: np.random.Generator, ggml_type: int, rows: int, cols: int, d_sca
     return blocks(rng, ggml_type, rows * (cols // be), d_scale)
 
 
-D_SCALE = {TYPE_Q8_0: 0.002, TYPE_IQ2_XXS: 0.01, TYPE_IQ3_XXS: 0.01, TYPE_IQ1_S: 0.01}
+D_SCALE = {TYPE_Q8_0: 0.002, TYPE_IQ2_XXS: 0.01, TYPE_IQ3_XXS: 0.01, TYPE_IQ1_S: 0.01, TYPE_Q4_K: 0.001,
+           TYPE_Q5_K: 0.0005, TYPE_Q6_K: 0.0005, TYPE_IQ2_S: 0.01, TYPE_MXFP4: 1.0}
 
 
 @dataclass
