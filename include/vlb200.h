@@ -56,7 +56,13 @@ enum {
     VLB_TYPE_Q8_0 = 8,
     VLB_TYPE_IQ2_XXS = 16,
     VLB_TYPE_IQ3_XXS = 18,
-    VLB_TYPE_IQ1_S = 19
+    VLB_TYPE_IQ1_S = 19,
+    /* served on the CUDA cores (the per-row seam, dequantize and the expert kernels) */
+    VLB_TYPE_Q4_K = 12,
+    VLB_TYPE_Q5_K = 13,
+    VLB_TYPE_Q6_K = 14,
+    VLB_TYPE_IQ2_S = 22,
+    VLB_TYPE_MXFP4 = 39
 };
 
 /* Router scoring:

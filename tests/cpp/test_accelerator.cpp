@@ -130,7 +130,7 @@ void test_refusals() {
     experts_only.maximum_resident_bytes = 8U * vastloom::MiB;
     auto acc = vastloom::b200::B200MatvecAccelerator::create(governor, experts_only, kFake);
     CHECK(acc);
-    CHECK(fake.codebooks == 3);
+    CHECK(fake.codebooks == 4);
     DeepseekV4PackedMatrix recurring(8U, 1U, 32U, 32U, q8_payload(1, 32, 1));
     recurring.cache_identity = 11U;
     recurring.recurring = true;
@@ -150,12 +150,12 @@ void test_refusals() {
     r = acc2.value()->matvec(unsupported, input, output);
     CHECK(r && !r.value());
     CHECK(acc2.value()->stats().declined_by_type.at(999U) == 1U);
-    DeepseekV4PackedMatrix q4k(12U, 1U, 256U, 256U, std::vector<std::byte>(144));
-    q4k.cache_identity = 14U;
+    DeepseekV4PackedMatrix q2k(10U, 1U, 256U, 256U, std::vector<std::byte>(84));  // Q2_K
+    q2k.cache_identity = 14U;
     std::vector<float> in256(256, 0.f);
-    r = acc2.value()->matvec(q4k, in256, output);
-    CHECK(r && !r.value());  // a type the sm_100a kernels do not take is counted too
-    CHECK(acc2.value()->stats().declined_by_type.at(12U) == 1U);
+    r = acc2.value()->matvec(q2k, in256, output);
+    CHECK(r && !r.value());  // a ggml type the sm_100a kernels do not take is counted too
+    CHECK(acc2.value()->stats().declined_by_type.at(10U) == 1U);
 
     vastloom::b200::B200MatvecAcceleratorOptions tiny;
     tiny.maximum_resident_bytes = 1U;

@@ -51,16 +51,21 @@ def test_block_layouts_and_matrix_bytes():
     assert vb.matrix_bytes(vb.TYPE_Q8_0, 2048, 4096) == 8_912_896
     assert vb.matrix_bytes(vb.TYPE_IQ1_S, 2048, 4096) == 1_638_400
     assert vb.matrix_bytes(vb.TYPE_IQ3_XXS, 4096, 2048) == 3_211_264
+    assert vb.matrix_bytes(vb.TYPE_Q4_K, 2048, 4096) == 2048 * 16 * 144
+    assert vb.matrix_bytes(vb.TYPE_Q6_K, 2048, 4096) == 2048 * 16 * 210
+    assert vb.matrix_bytes(vb.TYPE_MXFP4, 2048, 4096) == 2048 * 128 * 17
     with pytest.raises(ValueError):
         vb.matrix_bytes(vb.TYPE_IQ2_XXS, 1, 100)
 
 
 def test_synthetic_blocks_follow_the_configuration():
     rng = np.random.default_rng(0)
-    for t in (vb.TYPE_Q8_0, vb.TYPE_IQ2_XXS, vb.TYPE_IQ3_XXS, vb.TYPE_IQ1_S):
+    for t in (vb.TYPE_Q8_0, vb.TYPE_IQ2_XXS, vb.TYPE_IQ3_XXS, vb.TYPE_IQ1_S, vb.TYPE_Q4_K, vb.TYPE_Q5_K,
+              vb.TYPE_Q6_K, vb.TYPE_IQ2_S):
         be, bb = vb.BLOCK_LAYOUT[t]
         b = synth.blocks(rng, t, 100, 0.01).reshape(100, bb)
-        d = (b[:, 0].astype(np.uint16) | (b[:, 1].astype(np.uint16) << 8)).view(np.float16)
+        at = 208 if t == vb.TYPE_Q6_K else 0  # the fp16 block scale
+        d = (b[:, at].astype(np.uint16) | (b[:, at + 1].astype(np.uint16) << 8)).view(np.float16)
         assert np.all(np.isfinite(d)) and np.all(d >= 0)
         if t == vb.TYPE_Q8_0:
             q = b[:, 2:].view(np.int8)
@@ -84,8 +89,9 @@ def test_hash_tables_have_distinct_experts_per_row():
 
 
 def test_codebook_file_roundtrip(grids):
-    assert set(grids) == {16, 18, 19}
+    assert set(grids) == {16, 18, 19, 22}
     assert len(grids[19]) == 2048 * 8 and len(grids[16]) == 256 * 8 and len(grids[18]) == 256 * 4
+    assert len(grids[22]) == 1024 * 8
 
 
 def test_ep_driver_reports_the_nccl_it_binds():

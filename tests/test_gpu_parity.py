@@ -30,7 +30,11 @@ def ulp_diff(a, b):
 
 # ---- dequant / matvec ------------------------------------------------------------------------
 
-@pytest.mark.parametrize("name", ["iq1_s", "iq2_xxs", "iq3_xxs", "q8_0"])
+KAT_NAMES = ["iq1_s", "iq2_xxs", "iq3_xxs", "q8_0", "q4_k", "q5_k", "q6_k", "iq2_s", "q4_k_parity", "mxfp4"]
+ALL_TYPES = [8, 16, 18, 19, 12, 13, 14, 22, 39]  # the four MoE formats, then Q4_K Q5_K Q6_K IQ2_S MXFP4
+
+
+@pytest.mark.parametrize("name", KAT_NAMES)
 def test_gpu_dequant_and_matvec_kats(device, oracle, name):
     make, t, cols = kat.KAT_SETS[name]
     enc = make()
@@ -38,16 +42,18 @@ def test_gpu_dequant_and_matvec_kats(device, oracle, name):
     try:
         dec = device.dequantize(m).reshape(-1)
         assert kat.fnv1a_f32(dec) == kat.ANSWERS[name]["hash"]
-        be = 32 if t == 8 else 256
+        be = vb.BLOCK_LAYOUT[t][0]
         assert dec.tobytes() == oracle.dequantize(t, enc, len(kat.SCALES), be).tobytes()
         y = device.matvec(m, kat.kat_input(cols))
-        want = np.array([v for v, _ in kat.ANSWERS[name]["matvec"]])
-        assert rel_err(y, want) <= TOL
+        if kat.ANSWERS[name]["matvec"] is not None:
+            want = np.array([v for v, _ in kat.ANSWERS[name]["matvec"]])
+            assert rel_err(y, want) <= TOL
+        assert rel_err(y, oracle.matvec(t, enc, 3, cols, kat.kat_input(cols))) <= TOL
     finally:
         device.release_matrix(m)
 
 
-@pytest.mark.parametrize("t", [8, 16, 18, 19])
+@pytest.mark.parametrize("t", ALL_TYPES)
 @pytest.mark.parametrize("shape", [(64, 512), (40, 1024), (7, 256)])
 def test_gpu_dequant_bit_exact_random(device, oracle, t, shape):
     rows, cols = shape
@@ -63,7 +69,7 @@ def test_gpu_dequant_bit_exact_random(device, oracle, t, shape):
         device.release_matrix(m)
 
 
-@pytest.mark.parametrize("t", [8, 16, 18, 19])
+@pytest.mark.parametrize("t", ALL_TYPES)
 @pytest.mark.parametrize("ntok", [1, 2, 3, 5, 9])
 def test_gpu_matvec_multi_token(device, oracle, t, ntok):
     rows, cols = 136, 1024
@@ -153,6 +159,41 @@ def test_gpu_layer_small_configs(device, oracle, cfg, T):
         assert ulp_diff(w, rw) <= 2
         roff, rpt, rps = oracle.dispatch(ridx, spec.experts)
         assert np.array_equal(off, roff) and np.array_equal(pt, rpt) and np.array_equal(ps, rps)
+        assert rel_err(out, ref) <= TOL
+    finally:
+        layer.destroy()
+        for lst in layer.matrices.values():
+            for m in lst:
+                device.release_matrix(m)
+        for m in layer.shared_matrices or ():
+            device.release_matrix(m)
+
+
+# Layers whose experts use the formats served on the CUDA cores only: Q4_K gate/up with Q6_K down
+# beside a Q8_0 shared expert (DeepSeek V4 semantics), IQ2_S and MXFP4 experts (OLMoE semantics),
+# Q5_K with IQ2_S down; against the oracle layer loop.
+WHOLE_BLOCK = {
+    "q4k-q6k-v4": synth.LayerSpec("wb-q4k-q6k", 512, 256, 12, 3, synth.SCORE_SQRT_SOFTPLUS, vb.TYPE_Q4_K,
+                                  vb.TYPE_Q6_K, shared_type=synth.TYPE_Q8_0),
+    "iq2s-mxfp4-olmoe": synth.LayerSpec("wb-iq2s-mxfp4", 512, 256, 12, 3, synth.SCORE_SOFTMAX, vb.TYPE_IQ2_S,
+                                        vb.TYPE_MXFP4, weight_after_down=True),
+    "q5k-iq2s-v4": synth.LayerSpec("wb-q5k-iq2s", 768, 512, 8, 2, synth.SCORE_SQRT_SOFTPLUS, vb.TYPE_Q5_K,
+                                   vb.TYPE_IQ2_S, shared_type=synth.TYPE_Q8_0),
+}
+
+
+@pytest.mark.parametrize("name", list(WHOLE_BLOCK))
+@pytest.mark.parametrize("T", [1, 9])
+def test_gpu_layer_whole_block_formats(device, oracle, name, T):
+    spec = WHOLE_BLOCK[name]
+    W = synth.layer_weights(spec, seed=700 + T)
+    x, tok, logits = synth.activations(spec, T, seed=710 + T)
+    layer = synth.upload_layer(device, W, max_tokens=16)
+    try:
+        out = layer.forward(x, tok, logits)
+        ref, ridx, _ = oracle.moe_forward(W, x, tok, logits)
+        idx, _, _, _, _ = layer.last_route(T)
+        assert np.array_equal(idx, ridx)
         assert rel_err(out, ref) <= TOL
     finally:
         layer.destroy()

@@ -5,6 +5,7 @@
 // its accelerator (src/cuda/cuda_matvec_accelerator.cpp); see the header for the contract.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -14,6 +15,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "vlb_formats.cuh"
 #include "vlb_launch.h"
 
 using namespace vlb;
@@ -34,6 +36,7 @@ int copy_message(const std::string& msg, char* buf, size_t cap) {
 constexpr uint64_t kFpIq1S = 0x6703ed863501ae2eull;
 constexpr uint64_t kFpIq2Xxs = 0xbb4ee025b5ac6e8eull;
 constexpr uint64_t kFpIq3Xxs = 0xdfa5dc83d6a155d5ull;
+constexpr uint64_t kFpIq2S = 0x123edd38a3b62b90ull;  // ggml_quantization.cpp:86
 
 uint64_t fnv1a(const void* p, size_t n) {
     const uint8_t* b = static_cast<const uint8_t*>(p);
@@ -70,6 +73,7 @@ struct vlb_handle {
     uint64_t* grid_iq1s = nullptr;
     uint64_t* grid_iq2xxs = nullptr;
     uint32_t* grid_iq3xxs = nullptr;
+    uint64_t* grid_iq2s = nullptr;
     struct Alloc {
         size_t bytes;
         std::string tag;
@@ -106,7 +110,7 @@ struct vlb_handle {
         (void)cudaGetLastError();  // clear a sticky launch error so the handle stays usable
         return fail(VLB_ERR_IO_ERROR, cuda_msg(op, e));
     }
-    Grids grids() const { return Grids{grid_iq1s, grid_iq2xxs, grid_iq3xxs}; }
+    Grids grids() const { return Grids{grid_iq1s, grid_iq2xxs, grid_iq3xxs, grid_iq2s}; }
     cudaStream_t pick(void* s) const { return s ? static_cast<cudaStream_t>(s) : stream; }
 
     // Governor-first allocation (CudaDriver::allocate, cuda_driver.cpp:2929-3005): reserve the
@@ -343,6 +347,7 @@ int vlb_set_codebook(vlb_handle* h, uint32_t type, const void* table, size_t byt
         case VLB_TYPE_IQ1_S: want = 2048 * 8; fp = kFpIq1S; slot = (void**)&h->grid_iq1s; break;
         case VLB_TYPE_IQ2_XXS: want = 256 * 8; fp = kFpIq2Xxs; slot = (void**)&h->grid_iq2xxs; break;
         case VLB_TYPE_IQ3_XXS: want = 256 * 4; fp = kFpIq3Xxs; slot = (void**)&h->grid_iq3xxs; break;
+        case VLB_TYPE_IQ2_S: want = 1024 * 8; fp = kFpIq2S; slot = (void**)&h->grid_iq2s; break;
         default: return h->fail(VLB_ERR_UNSUPPORTED, "storage type has no codebook");
     }
     if (bytes != want) return h->fail(VLB_ERR_INVALID_FORMAT, "codebook has the wrong size");
@@ -438,6 +443,90 @@ static float prefill_scale(uint32_t type, float dmax) {
     return std::ldexp(1.f, 14 - e);
 }
 
+// The whole-block formats (vlb_formats.cuh): validated as the reference's decoders validate
+// them, then stored one block per slot (the IQ2_S body two bytes further on, the MXFP4 scale byte
+// after its nibbles), tiled by 128 rows.
+static bool mxfp4_block_finite(const uint8_t* b) {
+    // decode_mxfp4_block (ggml_quantization.cpp:381-398) rejects a block with a non-finite value:
+    // the largest magnitude times the scale decides it
+    static const int kMag[8] = {0, 1, 2, 3, 4, 6, 8, 12};
+    int mx = 0;
+    for (int i = 0; i < 16; ++i) {
+        mx = std::max(mx, kMag[b[1 + i] & 7u]);
+        mx = std::max(mx, kMag[(b[1 + i] >> 4) & 7u]);
+    }
+    const uint32_t e = b[0];
+    const uint32_t bits = e < 2u ? 0x00200000u << e : (e - 1u) << 23;
+    float scale;
+    std::memcpy(&scale, &bits, 4);
+    return std::isfinite((float)mx * scale);
+}
+
+static int upload_raw(vlb_handle* h, uint64_t identity, uint32_t type, size_t rows, size_t cols,
+                      const uint8_t* src, size_t payload_bytes, const TypeLayout& L, vlb_matrix** out) {
+    const size_t bpr = cols / L.block_elems, nblocks = rows * bpr;
+    for (size_t b = 0; b < nblocks; ++b) {
+        const uint8_t* blk = src + b * L.block_bytes;
+        bool ok = true;
+        if (type == VLB_TYPE_Q4_K || type == VLB_TYPE_Q5_K)  // decode_q4_k_block / q5_k: d and dmin
+            ok = half_is_finite((uint16_t)(blk[0] | (blk[1] << 8))) && half_is_finite((uint16_t)(blk[2] | (blk[3] << 8)));
+        else if (type == VLB_TYPE_Q6_K)  // decode_q6_k_block: d after the quants
+            ok = half_is_finite((uint16_t)(blk[208] | (blk[209] << 8)));
+        else if (type == VLB_TYPE_IQ2_S)
+            ok = half_is_finite((uint16_t)(blk[0] | (blk[1] << 8)));
+        else
+            ok = mxfp4_block_finite(blk);
+        if (!ok) return h->fail(VLB_ERR_INVALID_FORMAT, "quantized block scale is not finite");
+    }
+    const size_t rows_padded = (rows + kTileRows - 1) / kTileRows * kTileRows;
+    const size_t nslots = rows_padded * bpr, slot = L.body_bytes;
+    std::vector<uint8_t> staged;
+    try {
+        staged.assign(nslots * slot, 0);
+    } catch (const std::bad_alloc&) {
+        return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the matrix on the host");
+    }
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < bpr; ++c) {
+            const uint8_t* blk = src + (r * bpr + c) * L.block_bytes;
+            uint8_t* dst = staged.data() + blk_index((uint32_t)bpr, (uint32_t)r, (uint32_t)c) * slot;
+            if (type == VLB_TYPE_IQ2_S) {
+                std::memcpy(dst, blk, 2);
+                std::memcpy(dst + 4, blk + 2, L.block_bytes - 2);
+            } else if (type == VLB_TYPE_MXFP4) {
+                std::memcpy(dst, blk + 1, 16);
+                dst[16] = blk[0];
+            } else {
+                std::memcpy(dst, blk, L.block_bytes);
+            }
+        }
+    vlb_matrix* m = new (std::nothrow) vlb_matrix();
+    if (!m) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
+    int st = h->galloc(staged.size(), "vlb-resident-matrix", &m->mem);
+    if (st != VLB_OK) {
+        delete m;
+        return st;
+    }
+    cudaError_t e = cudaMemcpy(m->mem, staged.data(), staged.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        h->gfree(m->mem);
+        delete m;
+        return h->cuda_fail("cudaMemcpy(matrix)", e);
+    }
+    m->owner = h;
+    m->identity = identity;
+    m->type = type;
+    m->rows = rows;
+    m->cols = cols;
+    m->bpr = (uint32_t)bpr;
+    m->bytes = staged.size();
+    m->payload_bytes = payload_bytes;
+    m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr, nullptr,
+                   reinterpret_cast<const uint8_t*>(m->mem), nullptr, 1.f};
+    *out = m;
+    return VLB_OK;
+}
+
 int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t rows,
                       size_t cols, const void* payload, size_t payload_bytes, vlb_matrix** out) {
     VLB_LOCK(h);
@@ -447,7 +536,7 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     if (!type_layout(type, &L))
         return h->fail(VLB_ERR_UNSUPPORTED, "storage type has no device kernel");
     if ((type == VLB_TYPE_IQ1_S && !h->grid_iq1s) || (type == VLB_TYPE_IQ2_XXS && !h->grid_iq2xxs) ||
-        (type == VLB_TYPE_IQ3_XXS && !h->grid_iq3xxs))
+        (type == VLB_TYPE_IQ3_XXS && !h->grid_iq3xxs) || (type == VLB_TYPE_IQ2_S && !h->grid_iq2s))
         return h->fail(VLB_ERR_NOT_FOUND, "the codebook for this storage type is not installed");
     if (rows == 0 || cols == 0 || cols % L.block_elems != 0 || rows > 0xffffffffu ||
         cols > 0xffffffffu || cols % 32 != 0)
@@ -457,6 +546,7 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     if (payload_bytes != nblocks * L.block_bytes)
         return h->fail(VLB_ERR_INVALID_FORMAT, "matrix payload size does not match its shape");
     const uint8_t* src = static_cast<const uint8_t*>(payload);
+    if (raw_type(type)) return upload_raw(h, identity, type, rows, cols, src, payload_bytes, L, out);
     // validate_block_scales (ggml_quantization.cpp:205-215): every block scale finite
     uint16_t dmax_bits = 0;  // largest |d| (fp16 magnitudes order as integers)
     for (size_t b = 0; b < nblocks; ++b) {

@@ -12,6 +12,7 @@
 //   xs[((t*4 + j)*2 + h)*ngroups + g][e] = x[t][g*32 + j*8 + h*4 + e]
 #pragma once
 
+#include "vlb_formats.cuh"
 #include "vlb_internal.cuh"
 
 namespace vlb {
@@ -20,6 +21,7 @@ struct GridSmem {
     const uint64_t* iq1s;
     const uint64_t* iq2xxs;
     const uint32_t* iq3xxs;
+    const uint64_t* iq2s;
 };
 
 __device__ __forceinline__ uint32_t xs_index(uint32_t t, uint32_t j, uint32_t h, uint32_t g,
@@ -116,13 +118,57 @@ __device__ __forceinline__ void decode_sub(const DevMat& m, uint32_t row, uint32
     }
 }
 
+// warp_dot for the whole-block formats (vlb_formats.cuh): the same column split and activation
+// layout, each group's scales read once per row, its weights decoded 8 at a time.
+template <uint32_t FMT, int RA, int RB, int TOKC>
+__device__ __forceinline__ void warp_dot_raw(const DevMat& ma, const DevMat& mb, uint32_t row_a,
+                                             uint32_t row_b, const float* __restrict__ xs,
+                                             uint32_t ngroups, const GridSmem& gs,
+                                             float (&acc)[RA + RB][TOKC]) {
+    constexpr int R = RA + RB;
+    constexpr uint32_t gpb = raw_groups(FMT), slot = raw_slot_bytes(FMT);
+    const uint32_t lane = threadIdx.x & 31u;
+    for (uint32_t g = lane; g < ngroups; g += 32u) {
+        const uint32_t blk = g / gpb, gg = g % gpb;
+        const uint8_t* pb[R];
+        RawGroup raw[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const DevMat& m = r < RA ? ma : mb;
+            const uint32_t row = r < RA ? row_a + r : row_b + (r - RA);
+            pb[r] = m.body + blk_index(m.bpr, row, blk) * slot;
+            raw[r] = raw_group<FMT>(pb[r], gg);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float xv[TOKC][8];
+#pragma unroll
+            for (int t = 0; t < TOKC; ++t) {
+                const float4 lo = *reinterpret_cast<const float4*>(xs + xs_index(t, j, 0, g, ngroups));
+                const float4 hi = *reinterpret_cast<const float4*>(xs + xs_index(t, j, 1, g, ngroups));
+                xv[t][0] = lo.x; xv[t][1] = lo.y; xv[t][2] = lo.z; xv[t][3] = lo.w;
+                xv[t][4] = hi.x; xv[t][5] = hi.y; xv[t][6] = hi.z; xv[t][7] = hi.w;
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float w[8];
+                raw_sub<FMT>(pb[r], raw[r], j, gs.iq2s, w);
+#pragma unroll
+                for (int t = 0; t < TOKC; ++t)
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) acc[r][t] = fmaf(w[l], xv[t][l], acc[r][t]);
+            }
+        }
+    }
+}
+
 // acc[r][t] += sum over this lane's columns of W[row_r][c] * x[t][c], for the R rows
 // rows[0..R) of matrix ma (first RA rows) and mb (the rest). Both matrices share the columns.
 template <uint32_t FMT, int RA, int RB, int TOKC>
-__device__ __forceinline__ void warp_dot(const DevMat& ma, const DevMat& mb, uint32_t row_a,
-                                         uint32_t row_b, const float* __restrict__ xs,
-                                         uint32_t ngroups, const GridSmem& gs,
-                                         float (&acc)[RA + RB][TOKC]) {
+__device__ __forceinline__ void warp_dot_split(const DevMat& ma, const DevMat& mb, uint32_t row_a,
+                                               uint32_t row_b, const float* __restrict__ xs,
+                                               uint32_t ngroups, const GridSmem& gs,
+                                               float (&acc)[RA + RB][TOKC]) {
     constexpr int R = RA + RB;
     const uint32_t lane = threadIdx.x & 31u;
     for (uint32_t g = lane; g < ngroups; g += 32u) {
@@ -154,6 +200,17 @@ __device__ __forceinline__ void warp_dot(const DevMat& ma, const DevMat& mb, uin
             }
         }
     }
+}
+
+template <uint32_t FMT, int RA, int RB, int TOKC>
+__device__ __forceinline__ void warp_dot(const DevMat& ma, const DevMat& mb, uint32_t row_a,
+                                         uint32_t row_b, const float* __restrict__ xs,
+                                         uint32_t ngroups, const GridSmem& gs,
+                                         float (&acc)[RA + RB][TOKC]) {
+    if constexpr (raw_type(FMT))
+        warp_dot_raw<FMT, RA, RB, TOKC>(ma, mb, row_a, row_b, xs, ngroups, gs, acc);
+    else
+        warp_dot_split<FMT, RA, RB, TOKC>(ma, mb, row_a, row_b, xs, ngroups, gs, acc);
 }
 
 template <int R, int TOKC>

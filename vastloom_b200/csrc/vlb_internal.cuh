@@ -39,6 +39,11 @@ constexpr uint32_t kTypeQ8_0 = VLB_TYPE_Q8_0;
 constexpr uint32_t kTypeIq2Xxs = VLB_TYPE_IQ2_XXS;
 constexpr uint32_t kTypeIq3Xxs = VLB_TYPE_IQ3_XXS;
 constexpr uint32_t kTypeIq1S = VLB_TYPE_IQ1_S;
+constexpr uint32_t kTypeQ4K = VLB_TYPE_Q4_K;
+constexpr uint32_t kTypeQ5K = VLB_TYPE_Q5_K;
+constexpr uint32_t kTypeQ6K = VLB_TYPE_Q6_K;
+constexpr uint32_t kTypeIq2S = VLB_TYPE_IQ2_S;
+constexpr uint32_t kTypeMxfp4 = VLB_TYPE_MXFP4;
 
 struct TypeLayout {
     uint32_t block_elems;  // weights per ggml block
@@ -52,6 +57,12 @@ __host__ __device__ inline bool type_layout(uint32_t type, TypeLayout* l) {
         case kTypeIq2Xxs: *l = {256u, 66u, 64u}; return true;
         case kTypeIq3Xxs: *l = {256u, 98u, 96u}; return true;
         case kTypeIq1S: *l = {256u, 50u, 48u}; return true;
+        // served on the CUDA cores from whole-block slots (vlb_formats.cuh)
+        case kTypeQ4K: *l = {256u, 144u, 144u}; return true;
+        case kTypeQ5K: *l = {256u, 176u, 176u}; return true;
+        case kTypeQ6K: *l = {256u, 210u, 212u}; return true;
+        case kTypeIq2S: *l = {256u, 82u, 84u}; return true;
+        case kTypeMxfp4: *l = {32u, 17u, 20u}; return true;
         default: return false;
     }
 }
@@ -83,6 +94,7 @@ struct Grids {
     const uint64_t* iq1s;    // 2048 entries, 8 x int8
     const uint64_t* iq2xxs;  // 256 entries, 8 x uint8 magnitudes
     const uint32_t* iq3xxs;  // 256 entries, 4 x uint8 magnitudes
+    const uint64_t* iq2s;    // 1024 entries, 8 x uint8 magnitudes
 };
 
 // fp16 -> f32. The hardware conversion is exact (every half, subnormals included, is a float),
@@ -93,7 +105,16 @@ __device__ __forceinline__ float h2f(uint16_t bits) {
 
 // One bit per device storage type, for sets of types.
 __host__ __device__ constexpr uint32_t fmt_bit(uint32_t type) {
-    return type == kTypeQ8_0 ? 1u : type == kTypeIq2Xxs ? 2u : type == kTypeIq3Xxs ? 4u : type == kTypeIq1S ? 8u : 0u;
+    return type == kTypeQ8_0    ? 1u
+           : type == kTypeIq2Xxs ? 2u
+           : type == kTypeIq3Xxs ? 4u
+           : type == kTypeIq1S   ? 8u
+           : type == kTypeQ4K    ? 16u
+           : type == kTypeQ5K    ? 32u
+           : type == kTypeQ6K    ? 64u
+           : type == kTypeIq2S   ? 128u
+           : type == kTypeMxfp4  ? 256u
+                                 : 0u;
 }
 
 // ---- bit-exact block decoders (one 32-weight group at a time) ------------------------------

@@ -24,19 +24,23 @@
 
 namespace vlb {
 
-constexpr uint32_t kGridSmemBytes = 2048u * 8u + 256u * 8u + 256u * 4u;  // 19,456
+constexpr uint32_t kGridSmemBytes = 2048u * 8u + 256u * 8u + 256u * 4u + 1024u * 8u;  // 27,648
 
-__device__ __forceinline__ GridSmem stage_grids(const Grids& g, unsigned char* smem) {
+// Copies the codebooks of the storage types in `need` (fmt_bit set) into shared memory.
+__device__ __forceinline__ GridSmem stage_grids(const Grids& g, unsigned char* smem, uint32_t need = ~0u) {
     uint64_t* s1 = reinterpret_cast<uint64_t*>(smem);
     uint64_t* s2 = s1 + 2048;
     uint32_t* s3 = reinterpret_cast<uint32_t*>(s2 + 256);
-    if (g.iq1s)
+    uint64_t* s4 = reinterpret_cast<uint64_t*>(s3 + 256);
+    if (g.iq2s && (need & fmt_bit(kTypeIq2S)))
+        for (uint32_t i = threadIdx.x; i < 1024u; i += blockDim.x) s4[i] = g.iq2s[i];
+    if (g.iq1s && (need & fmt_bit(kTypeIq1S)))
         for (uint32_t i = threadIdx.x; i < 2048u; i += blockDim.x) s1[i] = g.iq1s[i];
-    if (g.iq2xxs)
+    if (g.iq2xxs && (need & fmt_bit(kTypeIq2Xxs)))
         for (uint32_t i = threadIdx.x; i < 256u; i += blockDim.x) s2[i] = g.iq2xxs[i];
-    if (g.iq3xxs)
+    if (g.iq3xxs && (need & fmt_bit(kTypeIq3Xxs)))
         for (uint32_t i = threadIdx.x; i < 256u; i += blockDim.x) s3[i] = g.iq3xxs[i];
-    return GridSmem{s1, s2, s3};
+    return GridSmem{s1, s2, s3, s4};
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -47,7 +51,17 @@ __global__ void dequant_kernel(DevMat m, Grids g, float* __restrict__ out) {
     if (gid >= (size_t)m.rows * ngroups) return;
     const uint32_t row = (uint32_t)(gid / ngroups), grp = (uint32_t)(gid % ngroups);
     float w[32];
-    if (m.type == kTypeQ8_0) {
+    if (raw_type(m.type)) {
+        const uint32_t gpb = raw_groups(m.type), blk = grp / gpb, gg = grp % gpb;
+        const uint8_t* pb = m.body + blk_index(m.bpr, row, blk) * raw_slot_bytes(m.type);
+        switch (m.type) {
+            case kTypeQ4K: raw_decode_group<kTypeQ4K>(pb, gg, g.iq2s, w); break;
+            case kTypeQ5K: raw_decode_group<kTypeQ5K>(pb, gg, g.iq2s, w); break;
+            case kTypeQ6K: raw_decode_group<kTypeQ6K>(pb, gg, g.iq2s, w); break;
+            case kTypeIq2S: raw_decode_group<kTypeIq2S>(pb, gg, g.iq2s, w); break;
+            default: raw_decode_group<kTypeMxfp4>(pb, gg, g.iq2s, w); break;
+        }
+    } else if (m.type == kTypeQ8_0) {
         decode_group_q8_0(h2f(m.d[blk_index(m.bpr, row, grp)]),
                           m.body + blk_index(m.bpr, row, grp) * 32u, w);
     } else {
@@ -77,7 +91,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const 
                                                    uint32_t ntok, uint32_t xstride,
                                                    float* __restrict__ y, uint32_t ystride) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const GridSmem gs = stage_grids(grids, smem);
+    const GridSmem gs = stage_grids(grids, smem, fmt_bit(FMT));
     float* xs = reinterpret_cast<float*>(smem + kGridSmemBytes);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t row0 = blockIdx.x * (kGemvRows * kGemvWarps) + warp * kGemvRows;
@@ -760,6 +774,11 @@ __device__ __forceinline__ void gateup_dispatch(const MoeParams& p, const DevMat
         case kTypeIq2Xxs: gateup_rows<kTypeIq2Xxs, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
         case kTypeQ8_0: gateup_rows<kTypeQ8_0, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
         case kTypeIq3Xxs: gateup_rows<kTypeIq3Xxs, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeQ4K: gateup_rows<kTypeQ4K, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeQ5K: gateup_rows<kTypeQ5K, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeQ6K: gateup_rows<kTypeQ6K, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeIq2S: gateup_rows<kTypeIq2S, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
+        case kTypeMxfp4: gateup_rows<kTypeMxfp4, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
         default: gateup_rows<kTypeIq1S, TOKC>(p, w1, w3, row, xs, gs, u, e); break;
     }
 }
@@ -771,6 +790,11 @@ __device__ __forceinline__ void down_dispatch(const MoeParams& p, const DevMat& 
         case kTypeIq2Xxs: down_rows<kTypeIq2Xxs, TOKC>(p, w2, row, xs, gs, u); break;
         case kTypeQ8_0: down_rows<kTypeQ8_0, TOKC>(p, w2, row, xs, gs, u); break;
         case kTypeIq3Xxs: down_rows<kTypeIq3Xxs, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeQ4K: down_rows<kTypeQ4K, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeQ5K: down_rows<kTypeQ5K, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeQ6K: down_rows<kTypeQ6K, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeIq2S: down_rows<kTypeIq2S, TOKC>(p, w2, row, xs, gs, u); break;
+        case kTypeMxfp4: down_rows<kTypeMxfp4, TOKC>(p, w2, row, xs, gs, u); break;
         default: down_rows<kTypeIq1S, TOKC>(p, w2, row, xs, gs, u); break;
     }
 }
@@ -1011,6 +1035,11 @@ static cudaError_t gemv_type(const DevMat& m, const Grids& g, const float* x, ui
         case kTypeIq2Xxs: return gemv_launch<kTypeIq2Xxs, TOKC>(m, g, x, ntok, xs, y, ys, s);
         case kTypeIq3Xxs: return gemv_launch<kTypeIq3Xxs, TOKC>(m, g, x, ntok, xs, y, ys, s);
         case kTypeIq1S: return gemv_launch<kTypeIq1S, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeQ4K: return gemv_launch<kTypeQ4K, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeQ5K: return gemv_launch<kTypeQ5K, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeQ6K: return gemv_launch<kTypeQ6K, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeIq2S: return gemv_launch<kTypeIq2S, TOKC>(m, g, x, ntok, xs, y, ys, s);
+        case kTypeMxfp4: return gemv_launch<kTypeMxfp4, TOKC>(m, g, x, ntok, xs, y, ys, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -27,6 +27,11 @@ bool layout_for(std::uint32_t type, Layout* l) {
         case kTypeIq2Xxs: *l = {256U, 66U}; return true;
         case kTypeIq3Xxs: *l = {256U, 98U}; return true;
         case kTypeIq1S: *l = {256U, 50U}; return true;
+        case inference::kGgmlTypeQ4K: *l = {256U, 144U}; return true;
+        case inference::kGgmlTypeQ5K: *l = {256U, 176U}; return true;
+        case inference::kGgmlTypeQ6K: *l = {256U, 210U}; return true;
+        case inference::kGgmlTypeIq2S: *l = {256U, 82U}; return true;
+        case inference::kGgmlTypeMxfp4: *l = {32U, 17U}; return true;
         default: return false;
     }
 }
@@ -125,6 +130,7 @@ Result<std::unique_ptr<B200MatvecAccelerator>> B200MatvecAccelerator::create(
     if (auto s = install(kTypeIq1S, std::as_bytes(inference::iq1_s_grid_table())); !s) return s.error();
     if (auto s = install(kTypeIq2Xxs, std::as_bytes(inference::iq2_xxs_grid_table())); !s) return s.error();
     if (auto s = install(kTypeIq3Xxs, std::as_bytes(inference::iq3_xxs_grid_table())); !s) return s.error();
+    if (auto s = install(inference::kGgmlTypeIq2S, std::as_bytes(inference::iq2_s_grid_table())); !s) return s.error();
     return self;
 }
 
