@@ -64,14 +64,21 @@ def build_library(force: bool = False, verbose_ptxas: bool = False) -> str:
     out = []
     build_dir = PKG / "_build"
     build_dir.mkdir(exist_ok=True)
+    # the translation units compile in parallel (the expert kernels' format instances dominate)
+    procs = []
     for s in SOURCES:
         obj = build_dir / (Path(s).stem + ".o")
         cmd = [_nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
                "-I", str(ROOT / "include"), "-c", str(CSRC / s), "-o", str(obj)]
         if verbose_ptxas:
             cmd.insert(1, "-Xptxas=-v")
-        out.append(_run(cmd))
+        procs.append((cmd, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
         objs.append(str(obj))
+    for cmd, proc in procs:
+        so, se = proc.communicate()
+        if proc.returncode != 0:
+            raise RuntimeError(f"command failed ({proc.returncode}): {' '.join(cmd)}\n{so}\n{se}")
+        out.append(so + se)
     tmp = LIB.with_suffix(".so.tmp")
     _run([_nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart"])
     os.replace(tmp, LIB)
