@@ -299,6 +299,7 @@ def run_ours(args, rank, world, local_rank):
         result["cpu_baseline"]["single_thread"] = {"value": one["value"], "cores": 1, "sample": one["sample"]}
     if not args.no_configs:
         result["configs"] = run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=(W, layer))
+        result["formats"] = run_format_objects(args, dev, stream)
     layer.destroy()
     for lst in layer.matrices.values():
         for m in lst:
@@ -824,6 +825,61 @@ def run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=None):
         for layer in L2:
             release(layer)
     return out
+
+
+def run_format_objects(args, dev, stream):
+    """The operator seam's dequant-matvec (vlb_matvec_device) for every storage type on a 4096 x
+    4096 matrix, 1 and 4 tokens: 16 different matrices per type (more bytes than the L2) taken in
+    turn, CUDA events around 64 calls; bytes = the matrix's GGUF payload + activations + outputs,
+    against the HBM copy peak. The parity of each format is the test suite's."""
+    import ctypes as C
+
+    import torch
+
+    import vastloom_b200 as vb
+    from vastloom_b200 import synth
+
+    peak, peak_kind = load_peaks()
+    rows = cols = 4096
+    names = {vb.TYPE_Q8_0: "Q8_0", vb.TYPE_IQ2_XXS: "IQ2_XXS", vb.TYPE_IQ3_XXS: "IQ3_XXS", vb.TYPE_IQ1_S: "IQ1_S",
+             vb.TYPE_Q4_K: "Q4_K", vb.TYPE_Q5_K: "Q5_K", vb.TYPE_Q6_K: "Q6_K", vb.TYPE_IQ2_S: "IQ2_S",
+             vb.TYPE_MXFP4: "MXFP4"}
+    rng = np.random.default_rng(77)
+    x = torch.from_numpy(rng.standard_normal((4, cols)).astype(np.float32)).cuda()
+    y = torch.empty((4, rows), dtype=torch.float32, device="cuda")
+    ext = torch.cuda.ExternalStream(dev.stream, device=x.device)
+    out = {}
+    for t, name in names.items():
+        enc = synth.matrix(rng, t, rows, cols, synth.D_SCALE[t])
+        mats = [dev.upload_matrix(t, rows, cols, enc, identity=0x5000 + i) for i in range(16)]
+        try:
+            res = {"payload_bytes": int(enc.nbytes)}
+            for ntok in (1, 4):
+                def call(i):
+                    dev._check(dev.lib.vlb_matvec_device(dev.h, mats[i % 16].ptr, C.c_void_p(x.data_ptr()), ntok, cols,
+                                                         C.c_void_p(y.data_ptr()), rows, C.c_void_p(dev.stream)))
+                for i in range(16):
+                    call(i)
+                dev.synchronize()
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record(ext)
+                for i in range(64):
+                    call(i)
+                ev1.record(ext)
+                ev1.synchronize()
+                ms = ev0.elapsed_time(ev1) / 64
+                nbytes = enc.nbytes + ntok * cols * 4 + ntok * rows * 4
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                res[f"T{ntok}"] = {"us_per_call": round(ms * 1000, 2), "achieved_gbs": round(gbs, 1),
+                                   "frac": round(gbs / peak, 4), "weights_per_s": round(rows * cols / (ms * 1e-3), 1)}
+            res["roofline"] = {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                               "kernel": "gemv_kernel", "frac_T1": res["T1"]["frac"]}
+            out[name] = res
+        finally:
+            for m in mats:
+                dev.release_matrix(m)
+    return {"workload": "vlb_matvec_device, 4096 x 4096 matrix, 16 matrices in turn (> L2), 64 calls",
+            "timing": "CUDA events on the library stream", "by_type": out}
 
 
 def run_reference(args, rank, world):

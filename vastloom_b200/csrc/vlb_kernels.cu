@@ -82,14 +82,17 @@ __global__ void dequant_kernel(DevMat m, Grids g, float* __restrict__ out) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Standalone multi-token GEMV: CTA = 8 warps x 8 rows; tokens in chunks of TOKC.
-constexpr int kGemvRows = 8;
+// Standalone multi-token GEMV: CTA = 8 warps x gemv_rows(TOKC) rows; tokens in chunks of TOKC. A
+// warp's rows share each activation load; few rows per warp keep a single matrix spread over
+// every SM (a 4096-row matrix is 256 CTAs at one token).
 constexpr int kGemvWarps = 8;
+__host__ __device__ constexpr int gemv_rows(int tokc) { return tokc == 1 ? 2 : 4; }
 
 template <uint32_t FMT, int TOKC>
 __global__ void __launch_bounds__(256) gemv_kernel(DevMat m, Grids grids, const float* __restrict__ x,
                                                    uint32_t ntok, uint32_t xstride,
                                                    float* __restrict__ y, uint32_t ystride) {
+    constexpr int kGemvRows = gemv_rows(TOKC);
     extern __shared__ __align__(16) unsigned char smem[];
     const GridSmem gs = stage_grids(grids, smem, fmt_bit(FMT));
     float* xs = reinterpret_cast<float*>(smem + kGridSmemBytes);
@@ -1022,7 +1025,7 @@ static cudaError_t gemv_launch(const DevMat& m, const Grids& g, const float* x, 
     auto kern = gemv_kernel<FMT, TOKC>;
     cudaError_t e = set_smem_once(kern, smem);
     if (e != cudaSuccess) return e;
-    const unsigned grid = (m.rows + kGemvRows * kGemvWarps - 1) / (kGemvRows * kGemvWarps);
+    const unsigned grid = (m.rows + gemv_rows(TOKC) * kGemvWarps - 1) / (gemv_rows(TOKC) * kGemvWarps);
     kern<<<grid, 256, smem, s>>>(m, g, x, ntok, xs, y, ys);
     return cudaGetLastError();
 }
