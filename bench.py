@@ -300,6 +300,7 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_configs:
         result["configs"] = run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=(W, layer))
         result["formats"] = run_format_objects(args, dev, stream)
+        result["records"] = run_record_objects(args, dev)
     layer.destroy()
     for lst in layer.matrices.values():
         for m in lst:
@@ -880,6 +881,96 @@ def run_format_objects(args, dev, stream):
                 dev.release_matrix(m)
     return {"workload": "vlb_matvec_device, 4096 x 4096 matrix, 16 matrices in turn (> L2), 64 calls",
             "timing": "CUDA events on the library stream", "by_type": out}
+
+
+def run_record_objects(args, dev):
+    """Expert records to device: 32 config-1 expert records (IQ2_XXS W1 / W3 2048 x 4096 and W2
+    4096 x 2048, 6.49 MB each, as an expert pack stores them) from page-locked memory through
+    vlb_upload_record_async (one host-to-device copy per record, the re-layout on the device),
+    host wall clock from the first start to the last finish. Beside it: a plain host-to-device
+    copy of the same bytes from page-locked memory (the link's own rate in this run, CUDA events)
+    and the host-path upload (vlb_upload_matrix, re-layout on the host) of the same matrices."""
+    import torch
+
+    import vastloom_b200 as vb
+    from vastloom_b200 import synth
+
+    spec = synth.config(1)
+    H, I = spec.hidden, spec.intermediate
+    rng = np.random.default_rng(5)
+    n_rec = 32
+    t = vb.TYPE_IQ2_XXS
+    shapes = ((I, H), (I, H), (H, I))
+    recs = []
+    for e in range(n_rec):
+        parts = [np.asarray(synth.matrix(rng, t, r, c, synth.D_SCALE[t]), np.uint8).reshape(-1) for r, c in shapes]
+        recs.append(np.concatenate(parts))
+    nbytes = recs[0].nbytes
+    tensors = []
+    off = 0
+    for r, c in shapes:
+        nb = vb.matrix_bytes(t, r, c)
+        tensors.append((r, c, off, nb))
+        off += nb
+    pins = [dev.host_buffer(nbytes) for _ in range(n_rec)]
+    for p, rec in zip(pins, recs):
+        p.array[:] = rec
+
+    def ident(e, j):
+        return ((e + 1) * 8 + j) * 2 + 1
+
+    def record_pass():
+        ups = [dev.upload_record(p.array, [(ident(e, j), t, r, c, o, nb) for j, (r, c, o, nb) in enumerate(tensors)])
+               for e, p in enumerate(pins)]
+        return [m for u in ups for m in u.finish()]
+
+    for m in record_pass():  # warm: staging grown, stream created
+        dev.release_matrix(m)
+    times = []
+    for _ in range(3):
+        dev.synchronize()
+        t0 = time.perf_counter()
+        mats = record_pass()
+        times.append(time.perf_counter() - t0)
+        for m in mats:
+            dev.release_matrix(m)
+    rec_s = min(times)
+    # the link: one copy of every record from page-locked memory into one device buffer
+    src = [torch.from_numpy(p.array) for p in pins]
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    for s_ in src[:4]:
+        dst.copy_(s_, non_blocking=True)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for s_ in src:
+        dst.copy_(s_, non_blocking=True)
+    ev1.record()
+    ev1.synchronize()
+    link_s = ev0.elapsed_time(ev1) / 1e3
+    # the host path on the same records
+    t0 = time.perf_counter()
+    host_mats = []
+    for e, rec in enumerate(recs[:8]):
+        for j, (r, c, o, nb) in enumerate(tensors):
+            host_mats.append(dev.upload_matrix(t, r, c, rec[o:o + nb], identity=ident(e, j)))
+    host_s = (time.perf_counter() - t0) * n_rec / 8
+    for m in host_mats:
+        dev.release_matrix(m)
+    for p in pins:
+        p.free()
+    del src, dst
+    total = n_rec * nbytes
+    return {
+        "workload": f"{n_rec} config-1 expert records (IQ2_XXS, {nbytes} B each) from page-locked memory",
+        "record_path": {"ms": round(rec_s * 1e3, 3), "gbs": round(total / rec_s / 1e9, 2),
+                        "timing": "host wall clock, first start to last finish, best of 3"},
+        "h2d_copy": {"ms": round(link_s * 1e3, 3), "gbs": round(total / link_s / 1e9, 2),
+                     "timing": "CUDA events around plain copies of the same bytes"},
+        "host_path": {"ms": round(host_s * 1e3, 3), "gbs": round(total / host_s / 1e9, 2),
+                      "timing": "host wall clock of vlb_upload_matrix on 8 records, scaled to all"},
+        "frac_of_link": round(link_s / rec_s, 4),
+    }
 
 
 def run_reference(args, rank, world):

@@ -156,6 +156,44 @@ int vlb_release_matrix(vlb_handle* h, vlb_matrix* m);
 /* Resident bytes of a matrix (scales + bodies). */
 uint64_t vlb_matrix_bytes(const vlb_matrix* m);
 
+/* ---- expert records to device (DeepseekV4ExpertPackRecord, include/vastloom/inference/
+ * deepseek_v4_expert_pack.hpp:24-41; the VRAM half of ResidencyObject, include/vastloom/model/
+ * residency.hpp:114-145, src/model/residency.cpp:183-212) ----------------------------------
+ * One expert's record is one contiguous span of ggml bytes holding its tensors back to back
+ * (`offset` = the tensor's packed_offset inside the record). vlb_upload_record_async copies the
+ * whole span to the device in ONE host-to-device copy on the handle's upload stream (a stream of
+ * its own, so the copy overlaps the handle's compute) and re-lays every block out on the device;
+ * the matrices come out identical to vlb_upload_matrix's. It returns once the work is enqueued:
+ * the record's host bytes must stay unchanged until vlb_upload_finish returns, and the copy is
+ * asynchronous only from page-locked memory (vlb_host_alloc). reserved_bytes: VRAM the caller
+ * already holds in its governor for these matrices (ResidencyObject::begin_vram_copy reserves
+ * the record's bytes); the governor hooks are charged only for the device bytes above it, in
+ * tensor order, and for the device copy of the record ("vlb-upload-staging", kept and grown
+ * for later records). At most 64 tensors per record and 256 records in flight per handle. */
+typedef struct vlb_upload vlb_upload;
+typedef struct vlb_record_tensor {
+    uint64_t cache_identity; /* deepseek_v4_expert_provider.cpp:75-90 for routed experts */
+    uint32_t ggml_type;
+    uint32_t reserved0;
+    uint64_t rows;           /* shape[1] */
+    uint64_t storage_cols;   /* shape[0] */
+    uint64_t offset;         /* packed_offset within the record */
+    uint64_t bytes;          /* rows x blocks per row x block bytes */
+} vlb_record_tensor;
+int vlb_upload_record_async(vlb_handle* h, const void* record_host, size_t record_bytes,
+                            const vlb_record_tensor* tensors, uint32_t n_tensors,
+                            uint64_t reserved_bytes, vlb_upload** out);
+/* *done = 1 once the copy and the re-layout have finished (never blocks). */
+int vlb_upload_query(vlb_handle* h, vlb_upload* u, int* done);
+/* Waits for the upload, checks every block as the reference's decoders do, and hands out one
+ * matrix per tensor (out[n_tensors], record order). On any failure (a block scale that is not
+ * finite: VLB_ERR_INVALID_FORMAT naming the tensor) every matrix of the record is released.
+ * Either way the upload object is consumed. */
+int vlb_upload_finish(vlb_handle* h, vlb_upload* u, vlb_matrix** out, uint32_t n_tensors);
+/* Page-locked host memory for records (cudaHostAlloc); freed with vlb_host_free. */
+int vlb_host_alloc(vlb_handle* h, size_t bytes, void** out);
+int vlb_host_free(vlb_handle* h, void* p);
+
 /* The per-row operator seam: DeepseekV4MatvecAccelerator::matvec (deepseek_v4_reference.hpp:
  * 440-451) for a resident matrix, host input (storage_cols floats, zero-padded by the caller)
  * and host output (rows floats). Synchronous, like matvec_*_with_transfer

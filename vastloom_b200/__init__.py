@@ -112,6 +112,12 @@ class _Governor(C.Structure):
     _fields_ = [("ctx", C.c_void_p), ("reserve", RESERVE_FN), ("release", RELEASE_FN)]
 
 
+class _RecordTensor(C.Structure):
+    _fields_ = [("cache_identity", C.c_uint64), ("ggml_type", C.c_uint32), ("reserved0", C.c_uint32),
+                ("rows", C.c_uint64), ("storage_cols", C.c_uint64), ("offset", C.c_uint64),
+                ("bytes", C.c_uint64)]
+
+
 class _LayerDesc(C.Structure):
     _fields_ = [
         ("hidden", C.c_uint32),
@@ -151,7 +157,8 @@ EXPORTS = (
     "vlb_layer_prefill_tokens vlb_layer_set_input_norm vlb_layer_forward_routes_device vlb_layer_status vlb_ep_workspace_bytes "
     "vlb_ep_plan_device vlb_ep_plan_half_device vlb_ep_pack_half_device vlb_ep_combine_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device "
     "vlb_ep_nccl_version vlb_ep_unique_id vlb_ep_comm_init vlb_ep_comm_destroy vlb_ep_comm_abort "
-    "vlb_ep_all_to_all_device vlb_ep_layer_create vlb_ep_layer_destroy vlb_ep_forward_device vlb_ep_last_phases"
+    "vlb_ep_all_to_all_device vlb_ep_layer_create vlb_ep_layer_destroy vlb_ep_forward_device vlb_ep_last_phases "
+    "vlb_upload_record_async vlb_upload_query vlb_upload_finish vlb_host_alloc vlb_host_free"
 ).split()
 
 
@@ -222,6 +229,11 @@ def load_library() -> C.CDLL:
         "vlb_ep_layer_destroy": (I, [P, P]),
         "vlb_ep_forward_device": (I, [P, P, P, P, U32, P, P]),
         "vlb_ep_last_phases": (I, [P, C.POINTER(C.c_float), C.POINTER(U64)]),
+        "vlb_upload_record_async": (I, [P, P, SZ, C.POINTER(_RecordTensor), U32, U64, C.POINTER(P)]),
+        "vlb_upload_query": (I, [P, P, C.POINTER(C.c_int)]),
+        "vlb_upload_finish": (I, [P, P, C.POINTER(P), U32]),
+        "vlb_host_alloc": (I, [P, SZ, C.POINTER(P)]),
+        "vlb_host_free": (I, [P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -298,6 +310,44 @@ class DeviceBuffer:
         if self.ptr:
             self.dev._check(self.dev.lib.vlb_free(self.dev.h, self.ptr))
             self.ptr = C.c_void_p()
+
+
+class RecordUpload:
+    """An expert record on its way to the device (vlb_upload_record_async)."""
+
+    def __init__(self, dev: "Device", ptr: C.c_void_p, record: np.ndarray, tensors: list):
+        self.dev, self.ptr, self.record, self.tensors = dev, ptr, record, tensors
+
+    def done(self) -> bool:
+        d = C.c_int(0)
+        self.dev._check(self.dev.lib.vlb_upload_query(self.dev.h, self.ptr, C.byref(d)))
+        return bool(d.value)
+
+    def finish(self) -> list:
+        n = len(self.tensors)
+        out = (C.c_void_p * n)()
+        ptr, self.ptr = self.ptr, None
+        self.dev._check(self.dev.lib.vlb_upload_finish(self.dev.h, ptr, out, n))
+        self.record = None
+        return [Matrix(C.c_void_p(out[i]), t, rows, cols, ident, nb)
+                for i, (ident, t, rows, cols, _off, nb) in enumerate(self.tensors)]
+
+
+class PinnedBuffer:
+    """Page-locked host memory from the library (vlb_host_alloc), viewed as a uint8 array."""
+
+    def __init__(self, dev: "Device", nbytes: int):
+        self.dev = dev
+        p = C.c_void_p()
+        dev._check(dev.lib.vlb_host_alloc(dev.h, nbytes, C.byref(p)))
+        self.ptr = p
+        self.array = np.ctypeslib.as_array((C.c_uint8 * nbytes).from_address(p.value))
+
+    def free(self) -> None:
+        if self.ptr:
+            self.array = None
+            self.dev._check(self.dev.lib.vlb_host_free(self.dev.h, self.ptr))
+            self.ptr = None
 
 
 class Device:
@@ -378,6 +428,22 @@ class Device:
         self._check(self.lib.vlb_upload_matrix(self.h, identity, ggml_type, rows, cols, _ptr(payload),
                                                payload.nbytes, C.byref(m)))
         return Matrix(m, ggml_type, rows, cols, identity, int(payload.nbytes))
+
+    def upload_record(self, record, tensors, reserved_bytes: int = 0) -> "RecordUpload":
+        """Starts the device upload of one expert record (vlb_upload_record_async). `record`: the
+        record's bytes (kept alive by the returned object until finish); `tensors`: one
+        (identity, ggml_type, rows, storage_cols, offset, nbytes) tuple per tensor."""
+        record = np.ascontiguousarray(np.frombuffer(record, dtype=np.uint8) if isinstance(record, (bytes, bytearray)) else record)
+        arr = (_RecordTensor * len(tensors))()
+        for i, (ident, t, rows, cols, off, nb) in enumerate(tensors):
+            arr[i] = _RecordTensor(ident, t, 0, rows, cols, off, nb)
+        u = C.c_void_p()
+        self._check(self.lib.vlb_upload_record_async(self.h, _ptr(record), record.nbytes, arr, len(tensors),
+                                                     reserved_bytes, C.byref(u)))
+        return RecordUpload(self, u, record, list(tensors))
+
+    def host_buffer(self, nbytes: int) -> "PinnedBuffer":
+        return PinnedBuffer(self, nbytes)
 
     def release_matrix(self, m: Matrix) -> None:
         if m.ptr:

@@ -13,9 +13,10 @@
 #include <new>
 #include <string>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
-#include "vlb_formats.cuh"
+#include "vlb_encode.cuh"
 #include "vlb_launch.h"
 
 using namespace vlb;
@@ -62,6 +63,14 @@ namespace vlb {
 void set_thread_error(const std::string& msg) { t_error = msg; }
 }  // namespace vlb
 
+// Record uploads: tensors per record, and records in flight per handle.
+constexpr uint32_t kUploadMaxTensors = 64;
+constexpr uint32_t kUploadSlots = 256;
+
+// Frees the host records of an upload the handle is closing under (its memory goes with the
+// handle's allocations).
+static void delete_unfinished_upload(vlb_upload* u);
+
 struct vlb_handle {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -76,10 +85,19 @@ struct vlb_handle {
     uint64_t* grid_iq2s = nullptr;
     struct Alloc {
         size_t bytes;
+        size_t hooked;  // the part reserved through the governor hooks (the rest the caller holds)
         std::string tag;
     };
     std::unordered_map<void*, Alloc> allocs;
     uint64_t allocated = 0;
+    // record uploads (vlb_upload_record_async): their own stream, the device copy of the record
+    // (grown only), a pinned arena of per-upload result words and the uploads in flight
+    cudaStream_t upload_stream = nullptr;
+    uint8_t* upload_stage = nullptr;
+    size_t upload_stage_cap = 0;
+    uint32_t* upload_results = nullptr;
+    std::vector<uint32_t> upload_slots;
+    std::unordered_set<vlb_upload*> uploads;
     float* seam_x = nullptr;
     float* seam_y = nullptr;
     size_t seam_x_cap = 0, seam_y_cap = 0;
@@ -115,31 +133,35 @@ struct vlb_handle {
 
     // Governor-first allocation (CudaDriver::allocate, cuda_driver.cpp:2929-3005): reserve the
     // exact bytes, check live free memory against the configured floor, then allocate; every
-    // failure after a successful reserve releases it again.
-    int galloc(size_t bytes, const char* tag, void** out) {
+    // failure after a successful reserve releases it again. `covered`: bytes of this allocation
+    // the caller already holds a reservation for (a residency object's VRAM destination), which
+    // the hooks are not charged for.
+    int galloc(size_t bytes, const char* tag, void** out, size_t covered = 0) {
         *out = nullptr;
         if (bytes == 0) return fail(VLB_ERR_INVALID_ARGUMENT, "zero-byte device allocation");
-        if (has_gov && gov.reserve && gov.reserve(gov.ctx, bytes, tag) != 0)
+        const size_t hooked = bytes - std::min(bytes, covered);
+        const bool charge = has_gov && hooked != 0;
+        if (charge && gov.reserve && gov.reserve(gov.ctx, hooked, tag) != 0)
             return fail(VLB_ERR_RESOURCE_EXHAUSTED,
                         std::string("governor refused the device reservation: ") + tag);
         size_t free_b = 0, total_b = 0;
         cudaError_t e = cudaMemGetInfo(&free_b, &total_b);
         if (e != cudaSuccess) {
-            if (has_gov && gov.release) gov.release(gov.ctx, bytes, tag);
+            if (charge && gov.release) gov.release(gov.ctx, hooked, tag);
             return cuda_fail("cudaMemGetInfo", e);
         }
         if ((uint64_t)free_b < (uint64_t)bytes + min_free_after) {
-            if (has_gov && gov.release) gov.release(gov.ctx, bytes, tag);
+            if (charge && gov.release) gov.release(gov.ctx, hooked, tag);
             return fail(VLB_ERR_RESOURCE_EXHAUSTED,
                         std::string("device allocation would cross the free-memory floor: ") + tag);
         }
         e = cudaMalloc(out, bytes);
         if (e != cudaSuccess) {
             *out = nullptr;
-            if (has_gov && gov.release) gov.release(gov.ctx, bytes, tag);
+            if (charge && gov.release) gov.release(gov.ctx, hooked, tag);
             return cuda_fail("cudaMalloc", e);
         }
-        allocs[*out] = Alloc{bytes, tag};
+        allocs[*out] = Alloc{bytes, hooked, tag};
         allocated += bytes;
         return VLB_OK;
     }
@@ -153,7 +175,8 @@ struct vlb_handle {
             // (cuda_driver.cpp:2881-2894).
             return cuda_fail("cudaFree", e);
         }
-        if (has_gov && gov.release) gov.release(gov.ctx, it->second.bytes, it->second.tag.c_str());
+        if (has_gov && gov.release && it->second.hooked)
+            gov.release(gov.ctx, it->second.hooked, it->second.tag.c_str());
         allocated -= it->second.bytes;
         allocs.erase(it);
         return VLB_OK;
@@ -313,12 +336,17 @@ void vlb_close(vlb_handle* h) {
         std::lock_guard<std::mutex> lock(h->mu);
         cudaSetDevice(h->device);
         cudaStreamSynchronize(h->stream);
+        if (h->upload_stream) cudaStreamSynchronize(h->upload_stream);
+        for (vlb_upload* u : h->uploads) delete_unfinished_upload(u);
+        h->uploads.clear();
         for (auto& kv : h->allocs) {
             cudaFree(kv.first);
-            if (h->has_gov && h->gov.release)
-                h->gov.release(h->gov.ctx, kv.second.bytes, kv.second.tag.c_str());
+            if (h->has_gov && h->gov.release && kv.second.hooked)
+                h->gov.release(h->gov.ctx, kv.second.hooked, kv.second.tag.c_str());
         }
         h->allocs.clear();
+        if (h->upload_stream) cudaStreamDestroy(h->upload_stream);
+        if (h->upload_results) cudaFreeHost(h->upload_results);
         cudaStreamDestroy(h->stream);
     }
     delete h;
@@ -390,8 +418,6 @@ uint64_t vlb_allocated_bytes(const vlb_handle* h) { return h ? h->allocated : 0;
 
 // ---- matrices -------------------------------------------------------------------------------
 
-static bool half_is_finite(uint16_t bits) { return ((bits >> 10) & 0x1fu) != 0x1fu; }
-
 static float half_bits_to_float(uint16_t bits) {
     const uint32_t e = (bits >> 10) & 0x1fu, m = bits & 0x3ffu;
     const float mag = e == 0 ? std::ldexp((float)m, -24) : std::ldexp((float)(m | 0x400u), (int)e - 25);
@@ -443,88 +469,43 @@ static float prefill_scale(uint32_t type, float dmax) {
     return std::ldexp(1.f, 14 - e);
 }
 
-// The whole-block formats (vlb_formats.cuh): validated as the reference's decoders validate
-// them, then stored one block per slot (the IQ2_S body two bytes further on, the MXFP4 scale byte
-// after its nibbles), tiled by 128 rows.
-static bool mxfp4_block_finite(const uint8_t* b) {
-    // decode_mxfp4_block (ggml_quantization.cpp:381-398) rejects a block with a non-finite value:
-    // the largest magnitude times the scale decides it
-    static const int kMag[8] = {0, 1, 2, 3, 4, 6, 8, 12};
-    int mx = 0;
-    for (int i = 0; i < 16; ++i) {
-        mx = std::max(mx, kMag[b[1 + i] & 7u]);
-        mx = std::max(mx, kMag[(b[1 + i] >> 4) & 7u]);
-    }
-    const uint32_t e = b[0];
-    const uint32_t bits = e < 2u ? 0x00200000u << e : (e - 1u) << 23;
-    float scale;
-    std::memcpy(&scale, &bits, 4);
-    return std::isfinite((float)mx * scale);
+// Checks one matrix's type, shape and payload size (both upload paths).
+static int check_matrix(vlb_handle* h, uint32_t type, size_t rows, size_t cols, size_t payload_bytes,
+                        TypeLayout* L) {
+    if (!type_layout(type, L)) return h->fail(VLB_ERR_UNSUPPORTED, "storage type has no device kernel");
+    if ((type == VLB_TYPE_IQ1_S && !h->grid_iq1s) || (type == VLB_TYPE_IQ2_XXS && !h->grid_iq2xxs) ||
+        (type == VLB_TYPE_IQ3_XXS && !h->grid_iq3xxs) || (type == VLB_TYPE_IQ2_S && !h->grid_iq2s))
+        return h->fail(VLB_ERR_NOT_FOUND, "the codebook for this storage type is not installed");
+    if (rows == 0 || cols == 0 || cols % L->block_elems != 0 || rows > 0xffffffffu ||
+        cols > 0xffffffffu || cols % 32 != 0)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "matrix dimensions are invalid");
+    if (payload_bytes != rows * (cols / L->block_elems) * L->block_bytes)
+        return h->fail(VLB_ERR_INVALID_FORMAT, "matrix payload size does not match its shape");
+    return VLB_OK;
 }
 
-static int upload_raw(vlb_handle* h, uint64_t identity, uint32_t type, size_t rows, size_t cols,
-                      const uint8_t* src, size_t payload_bytes, const TypeLayout& L, vlb_matrix** out) {
-    const size_t bpr = cols / L.block_elems, nblocks = rows * bpr;
-    for (size_t b = 0; b < nblocks; ++b) {
-        const uint8_t* blk = src + b * L.block_bytes;
-        bool ok = true;
-        if (type == VLB_TYPE_Q4_K || type == VLB_TYPE_Q5_K)  // decode_q4_k_block / q5_k: d and dmin
-            ok = half_is_finite((uint16_t)(blk[0] | (blk[1] << 8))) && half_is_finite((uint16_t)(blk[2] | (blk[3] << 8)));
-        else if (type == VLB_TYPE_Q6_K)  // decode_q6_k_block: d after the quants
-            ok = half_is_finite((uint16_t)(blk[208] | (blk[209] << 8)));
-        else if (type == VLB_TYPE_IQ2_S)
-            ok = half_is_finite((uint16_t)(blk[0] | (blk[1] << 8)));
-        else
-            ok = mxfp4_block_finite(blk);
-        if (!ok) return h->fail(VLB_ERR_INVALID_FORMAT, "quantized block scale is not finite");
-    }
-    const size_t rows_padded = (rows + kTileRows - 1) / kTileRows * kTileRows;
-    const size_t nslots = rows_padded * bpr, slot = L.body_bytes;
-    std::vector<uint8_t> staged;
-    try {
-        staged.assign(nslots * slot, 0);
-    } catch (const std::bad_alloc&) {
-        return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the matrix on the host");
-    }
-    for (size_t r = 0; r < rows; ++r)
-        for (size_t c = 0; c < bpr; ++c) {
-            const uint8_t* blk = src + (r * bpr + c) * L.block_bytes;
-            uint8_t* dst = staged.data() + blk_index((uint32_t)bpr, (uint32_t)r, (uint32_t)c) * slot;
-            if (type == VLB_TYPE_IQ2_S) {
-                std::memcpy(dst, blk, 2);
-                std::memcpy(dst + 4, blk + 2, L.block_bytes - 2);
-            } else if (type == VLB_TYPE_MXFP4) {
-                std::memcpy(dst, blk + 1, 16);
-                dst[16] = blk[0];
-            } else {
-                std::memcpy(dst, blk, L.block_bytes);
-            }
-        }
-    vlb_matrix* m = new (std::nothrow) vlb_matrix();
-    if (!m) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
-    int st = h->galloc(staged.size(), "vlb-resident-matrix", &m->mem);
-    if (st != VLB_OK) {
-        delete m;
-        return st;
-    }
-    cudaError_t e = cudaMemcpy(m->mem, staged.data(), staged.size(), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-        h->gfree(m->mem);
-        delete m;
-        return h->cuda_fail("cudaMemcpy(matrix)", e);
-    }
+// The record of a matrix whose image (matrix_image) sits at m->mem. dmag: the largest |d| of a
+// split-format matrix as fp16 bits (fp16 magnitudes order as integers).
+static void describe_matrix(vlb_matrix* m, vlb_handle* h, uint64_t identity, uint32_t type, const TypeLayout& L,
+                            const MatrixImage& img, size_t rows, size_t cols, size_t payload_bytes, uint16_t dmag) {
+    const uint32_t bpr = (uint32_t)(cols / L.block_elems);
+    const uint8_t* mem = reinterpret_cast<const uint8_t*>(m->mem);
     m->owner = h;
     m->identity = identity;
     m->type = type;
     m->rows = rows;
     m->cols = cols;
-    m->bpr = (uint32_t)bpr;
-    m->bytes = staged.size();
+    m->bpr = bpr;
+    m->bytes = img.resident;
     m->payload_bytes = payload_bytes;
-    m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr, nullptr,
-                   reinterpret_cast<const uint8_t*>(m->mem), nullptr, 1.f};
-    *out = m;
-    return VLB_OK;
+    if (raw_type(type)) {
+        m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, bpr, nullptr, mem, nullptr, 1.f};
+    } else {
+        m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, bpr, reinterpret_cast<const uint16_t*>(mem),
+                       mem + img.d_bytes + img.sc_bytes,
+                       img.sc_bytes ? reinterpret_cast<const uint32_t*>(mem + img.d_bytes) : nullptr,
+                       prefill_scale(type, half_bits_to_float(dmag))};
+    }
 }
 
 int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t rows,
@@ -533,71 +514,30 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
     if (!out || !payload) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null matrix argument");
     *out = nullptr;
     TypeLayout L{};
-    if (!type_layout(type, &L))
-        return h->fail(VLB_ERR_UNSUPPORTED, "storage type has no device kernel");
-    if ((type == VLB_TYPE_IQ1_S && !h->grid_iq1s) || (type == VLB_TYPE_IQ2_XXS && !h->grid_iq2xxs) ||
-        (type == VLB_TYPE_IQ3_XXS && !h->grid_iq3xxs) || (type == VLB_TYPE_IQ2_S && !h->grid_iq2s))
-        return h->fail(VLB_ERR_NOT_FOUND, "the codebook for this storage type is not installed");
-    if (rows == 0 || cols == 0 || cols % L.block_elems != 0 || rows > 0xffffffffu ||
-        cols > 0xffffffffu || cols % 32 != 0)
-        return h->fail(VLB_ERR_INVALID_ARGUMENT, "matrix dimensions are invalid");
-    const size_t bpr = cols / L.block_elems;
-    const size_t nblocks = rows * bpr;
-    if (payload_bytes != nblocks * L.block_bytes)
-        return h->fail(VLB_ERR_INVALID_FORMAT, "matrix payload size does not match its shape");
+    int st = check_matrix(h, type, rows, cols, payload_bytes, &L);
+    if (st != VLB_OK) return st;
     const uint8_t* src = static_cast<const uint8_t*>(payload);
-    if (raw_type(type)) return upload_raw(h, identity, type, rows, cols, src, payload_bytes, L, out);
-    // validate_block_scales (ggml_quantization.cpp:205-215): every block scale finite
-    uint16_t dmax_bits = 0;  // largest |d| (fp16 magnitudes order as integers)
+    const size_t bpr = cols / L.block_elems, nblocks = rows * bpr;
+    uint16_t dmag = 0;
     for (size_t b = 0; b < nblocks; ++b) {
-        const uint16_t d = (uint16_t)(src[b * L.block_bytes] | (src[b * L.block_bytes + 1] << 8));
-        if (!half_is_finite(d))
-            return h->fail(VLB_ERR_INVALID_FORMAT, "quantized block scale is not finite");
-        if ((d & 0x7fffu) > dmax_bits) dmax_bits = (uint16_t)(d & 0x7fffu);
+        const uint8_t* blk = src + b * L.block_bytes;
+        if (!block_finite(type, blk)) return h->fail(VLB_ERR_INVALID_FORMAT, "quantized block scale is not finite");
+        if (!raw_type(type)) dmag = std::max<uint16_t>(dmag, ld_u16(blk) & 0x7fffu);
     }
-    // tiled device layout (blk_index): rows padded to whole 128-row tiles with zero blocks
-    const size_t rows_padded = (rows + kTileRows - 1) / kTileRows * kTileRows;
-    const size_t nslots = rows_padded * bpr;
-    const bool iq2 = type == VLB_TYPE_IQ2_XXS, iq3 = type == VLB_TYPE_IQ3_XXS;
-    const bool scaled = iq2 || iq3;  // sign words re-encoded, group scales gathered per block
-    const size_t d_bytes = (nslots * 2 + 255) / 256 * 256;
-    const size_t sc_bytes = scaled ? (nslots * 4 + 255) / 256 * 256 : 0;
-    const size_t body_bytes = nslots * L.body_bytes;
+    const MatrixImage img = matrix_image(type, L, rows, cols);
     std::vector<uint8_t> staged;
     try {
-        staged.assign(d_bytes + sc_bytes + body_bytes, 0);
+        staged.assign(img.total, 0);
     } catch (const std::bad_alloc&) {
         return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the matrix on the host");
     }
-    uint16_t* dst_d = reinterpret_cast<uint16_t*>(staged.data());
-    uint32_t* dst_sc = reinterpret_cast<uint32_t*>(staged.data() + d_bytes);
-    uint8_t* dst_b = staged.data() + d_bytes + sc_bytes;
-    const size_t copy = L.block_bytes - 2;
     for (size_t r = 0; r < rows; ++r)
-        for (size_t c = 0; c < bpr; ++c) {
-            const uint8_t* blk = src + (r * bpr + c) * L.block_bytes;
-            const size_t at = blk_index((uint32_t)bpr, (uint32_t)r, (uint32_t)c);
-            dst_d[at] = (uint16_t)(blk[0] | (blk[1] << 8));
-            uint8_t* body = dst_b + at * L.body_bytes;
-            std::memcpy(body, blk + 2, copy);
-            if (scaled) {
-                // group words (IQ2_XXS: after each group's 4 index bytes; IQ3_XXS: after the 64
-                // index bytes) -> pair-layout sign words, scales gathered per block
-                uint32_t scales = 0;
-                for (uint32_t g = 0; g < 8; ++g) {
-                    uint8_t* word = iq2 ? body + g * 8 + 4 : body + 64 + g * 4;
-                    uint32_t aux;
-                    std::memcpy(&aux, word, 4);
-                    scales |= (aux >> 28) << (4 * g);
-                    const uint32_t sw = iq2_pair_signs(aux);
-                    std::memcpy(word, &sw, 4);
-                }
-                dst_sc[at] = scales;
-            }
-        }
+        for (size_t c = 0; c < bpr; ++c)
+            encode_block(type, L, img, src + (r * bpr + c) * L.block_bytes,
+                         blk_index((uint32_t)bpr, (uint32_t)r, (uint32_t)c), staged.data());
     vlb_matrix* m = new (std::nothrow) vlb_matrix();
     if (!m) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
-    int st = h->galloc(staged.size(), "vlb-resident-matrix", &m->mem);
+    st = h->galloc(staged.size(), "vlb-resident-matrix", &m->mem);
     if (st != VLB_OK) {
         delete m;
         return st;
@@ -608,23 +548,254 @@ int vlb_upload_matrix(vlb_handle* h, uint64_t identity, uint32_t type, size_t ro
         delete m;
         return h->cuda_fail("cudaMemcpy(matrix)", e);
     }
-    m->owner = h;
-    m->identity = identity;
-    m->type = type;
-    m->rows = rows;
-    m->cols = cols;
-    m->bpr = (uint32_t)bpr;
-    m->bytes = nslots * 2 + (scaled ? nslots * 4 : 0) + body_bytes;
-    m->payload_bytes = payload_bytes;
-    m->dm = DevMat{type, (uint32_t)rows, (uint32_t)cols, (uint32_t)bpr,
-                   reinterpret_cast<const uint16_t*>(m->mem),
-                   reinterpret_cast<const uint8_t*>(m->mem) + d_bytes + sc_bytes,
-                   scaled ? reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(m->mem) + d_bytes)
-                          : nullptr,
-                   prefill_scale(type, half_bits_to_float(dmax_bits))};
+    describe_matrix(m, h, identity, type, L, img, rows, cols, payload_bytes, dmag);
     *out = m;
     return VLB_OK;
 }
+
+// ---- expert records: one host-to-device copy, the re-layout on the device ------------------
+
+}  // extern "C"
+
+namespace {
+
+// One tensor of a record for encode_record_kernel.
+struct RecordJob {
+    const uint8_t* src;  // its ggml bytes in the device copy of the record
+    uint8_t* img;        // its matrix image
+    uint32_t* result;    // [0] nonzero = a block the reference rejects, [1] largest |d| (fp16 bits)
+    MatrixImage m;
+    TypeLayout L;
+    uint32_t type, bpr;
+    size_t nblocks;
+};
+
+__global__ void __launch_bounds__(256) encode_record_kernel(RecordJob j) {
+    uint32_t bad = 0, dmag = 0;
+    const bool split = !raw_type(j.type);
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < j.nblocks; b += (size_t)gridDim.x * blockDim.x) {
+        const uint8_t* blk = j.src + b * j.L.block_bytes;
+        if (!block_finite(j.type, blk)) bad = 1u;
+        if (split) dmag = max(dmag, (uint32_t)(ld_u16(blk) & 0x7fffu));
+        const uint32_t r = (uint32_t)(b / j.bpr), c = (uint32_t)(b % j.bpr);
+        encode_block(j.type, j.L, j.m, blk, blk_index(j.bpr, r, c), j.img);
+    }
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    dmag = __reduce_max_sync(0xffffffffu, dmag);
+    if ((threadIdx.x & 31u) == 0u) {
+        if (bad) atomicOr(j.result, 1u);
+        if (dmag) atomicMax(j.result + 1, dmag);
+    }
+}
+
+}  // namespace
+
+struct vlb_upload {
+    vlb_handle* owner = nullptr;
+    std::vector<vlb_record_tensor> tensors;
+    std::vector<vlb_matrix*> mats;
+    uint32_t slot = 0;  // its results in the handle's pinned arena
+    cudaEvent_t done = nullptr;
+};
+
+static void delete_unfinished_upload(vlb_upload* u) {
+    for (vlb_matrix* m : u->mats) delete m;
+    if (u->done) cudaEventDestroy(u->done);
+    delete u;
+}
+
+// Releases an upload's matrices and its results slot (stream work on them has finished or was
+// never enqueued).
+static void drop_upload(vlb_handle* h, vlb_upload* u) {
+    for (vlb_matrix* m : u->mats) {
+        if (!m) continue;
+        h->gfree(m->mem);
+        delete m;
+    }
+    u->mats.clear();
+    if (u->done) cudaEventDestroy(u->done);
+    h->upload_slots.push_back(u->slot);
+    h->uploads.erase(u);
+    delete u;
+}
+
+extern "C" {
+
+int vlb_upload_record_async(vlb_handle* h, const void* record, size_t record_bytes,
+                            const vlb_record_tensor* tensors, uint32_t n, uint64_t reserved_bytes,
+                            vlb_upload** out) {
+    VLB_LOCK(h);
+    if (!out || !record || !tensors || record_bytes == 0)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "null record argument");
+    *out = nullptr;
+    if (n == 0 || n > kUploadMaxTensors)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "a record holds 1 to 64 tensors");
+    std::vector<TypeLayout> layouts(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        const vlb_record_tensor& t = tensors[i];
+        const int st = check_matrix(h, t.ggml_type, t.rows, t.storage_cols, t.bytes, &layouts[i]);
+        if (st != VLB_OK) return h->fail(st, "record tensor " + std::to_string(i) + ": " + h->err);
+        if (t.offset > record_bytes || t.bytes > record_bytes - t.offset)
+            return h->fail(VLB_ERR_INVALID_FORMAT, "record tensor " + std::to_string(i) + " lies outside the record");
+    }
+    if (!h->upload_stream) {
+        VLB_CUDA(h, cudaStreamCreateWithFlags(&h->upload_stream, cudaStreamNonBlocking));
+        void* arena = nullptr;
+        VLB_CUDA(h, cudaHostAlloc(&arena, (size_t)kUploadSlots * kUploadMaxTensors * 8, cudaHostAllocPortable));
+        h->upload_results = static_cast<uint32_t*>(arena);
+        for (uint32_t s = kUploadSlots; s-- > 0;) h->upload_slots.push_back(s);
+    }
+    if (h->upload_slots.empty())
+        return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "too many record uploads in flight");
+    // the device copy of the record, then the results words; grown only, reused in stream order
+    const size_t res_off = (record_bytes + 255) / 256 * 256;
+    const size_t stage_need = res_off + (size_t)kUploadMaxTensors * 8;
+    if (h->upload_stage_cap < stage_need) {
+        if (h->upload_stage) {
+            VLB_CUDA(h, cudaStreamSynchronize(h->upload_stream));
+            h->gfree(h->upload_stage);
+        }
+        h->upload_stage = nullptr;
+        h->upload_stage_cap = 0;
+        const int st = h->galloc(stage_need, "vlb-upload-staging", reinterpret_cast<void**>(&h->upload_stage));
+        if (st != VLB_OK) return st;
+        h->upload_stage_cap = stage_need;
+    }
+    vlb_upload* u = new (std::nothrow) vlb_upload();
+    if (!u) return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the upload record");
+    u->owner = h;
+    u->slot = h->upload_slots.back();
+    h->upload_slots.pop_back();
+    h->uploads.insert(u);
+    u->tensors.assign(tensors, tensors + n);
+    u->mats.assign(n, nullptr);
+    // device images; the caller's VRAM reservation covers the first reserved_bytes of them
+    uint64_t prepaid = reserved_bytes;
+    for (uint32_t i = 0; i < n; ++i) {
+        const vlb_record_tensor& t = tensors[i];
+        const MatrixImage img = matrix_image(t.ggml_type, layouts[i], t.rows, t.storage_cols);
+        vlb_matrix* m = new (std::nothrow) vlb_matrix();
+        if (!m) {
+            drop_upload(h, u);
+            return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to allocate the matrix record");
+        }
+        const uint64_t covered = std::min<uint64_t>(prepaid, img.total);
+        const int st = h->galloc(img.total, "vlb-resident-matrix", &m->mem, covered);
+        if (st != VLB_OK) {
+            delete m;
+            const std::string msg = h->err;
+            drop_upload(h, u);
+            return h->fail(st, msg);
+        }
+        prepaid -= covered;
+        u->mats[i] = m;
+    }
+    cudaStream_t s = h->upload_stream;
+    uint32_t* res_dev = reinterpret_cast<uint32_t*>(h->upload_stage + res_off);
+    uint32_t* res_host = h->upload_results + (size_t)u->slot * kUploadMaxTensors * 2;
+    cudaError_t e = cudaEventCreateWithFlags(&u->done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMemsetAsync(res_dev, 0, (size_t)n * 8, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h->upload_stage, record, record_bytes, cudaMemcpyHostToDevice, s);
+    for (uint32_t i = 0; i < n && e == cudaSuccess; ++i) {
+        const vlb_record_tensor& t = tensors[i];
+        RecordJob j{};
+        j.src = h->upload_stage + t.offset;
+        j.img = static_cast<uint8_t*>(u->mats[i]->mem);
+        j.result = res_dev + 2 * i;
+        j.L = layouts[i];
+        j.m = matrix_image(t.ggml_type, j.L, t.rows, t.storage_cols);
+        j.type = t.ggml_type;
+        j.bpr = (uint32_t)(t.storage_cols / j.L.block_elems);
+        j.nblocks = (size_t)t.rows * j.bpr;
+        e = cudaMemsetAsync(j.img, 0, j.m.total, s);
+        if (e != cudaSuccess) break;
+        const size_t want = (j.nblocks + 255) / 256;
+        const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>(want, 148u * 8u));
+        encode_record_kernel<<<grid, 256, 0, s>>>(j);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(res_host, res_dev, (size_t)n * 8, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaEventRecord(u->done, s);
+    if (e != cudaSuccess) {
+        cudaStreamSynchronize(s);
+        drop_upload(h, u);
+        return h->cuda_fail("record upload", e);
+    }
+    *out = u;
+    return VLB_OK;
+}
+
+int vlb_upload_query(vlb_handle* h, vlb_upload* u, int* done) {
+    VLB_LOCK(h);
+    if (!u || !done || u->owner != h || !h->uploads.count(u))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "upload does not belong to this handle");
+    const cudaError_t e = cudaEventQuery(u->done);
+    if (e == cudaErrorNotReady) {
+        *done = 0;
+        return VLB_OK;
+    }
+    if (e != cudaSuccess) return h->cuda_fail("cudaEventQuery(upload)", e);
+    *done = 1;
+    return VLB_OK;
+}
+
+int vlb_upload_finish(vlb_handle* h, vlb_upload* u, vlb_matrix** out, uint32_t n) {
+    VLB_LOCK(h);
+    if (!u || u->owner != h || !h->uploads.count(u))
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "upload does not belong to this handle");
+    // the copy and the re-layout kernels wait on nothing, so this wait ends
+    const cudaError_t e = cudaEventSynchronize(u->done);
+    if (e != cudaSuccess) {
+        cudaStreamSynchronize(h->upload_stream);
+        drop_upload(h, u);
+        return h->cuda_fail("record upload", e);
+    }
+    const uint32_t* res = h->upload_results + (size_t)u->slot * kUploadMaxTensors * 2;
+    const uint32_t count = (uint32_t)u->tensors.size();
+    for (uint32_t i = 0; i < count; ++i)
+        if (res[2 * i]) {
+            drop_upload(h, u);
+            return h->fail(VLB_ERR_INVALID_FORMAT,
+                           "record tensor " + std::to_string(i) + ": quantized block scale is not finite");
+        }
+    if (!out || n != count) {
+        drop_upload(h, u);
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "the output array must hold one matrix per record tensor");
+    }
+    for (uint32_t i = 0; i < count; ++i) {
+        const vlb_record_tensor& t = u->tensors[i];
+        TypeLayout L{};
+        type_layout(t.ggml_type, &L);
+        describe_matrix(u->mats[i], h, t.cache_identity, t.ggml_type, L,
+                        matrix_image(t.ggml_type, L, t.rows, t.storage_cols), t.rows, t.storage_cols, t.bytes,
+                        (uint16_t)res[2 * i + 1]);
+        out[i] = u->mats[i];
+    }
+    u->mats.clear();
+    drop_upload(h, u);
+    return VLB_OK;
+}
+
+int vlb_host_alloc(vlb_handle* h, size_t bytes, void** out) {
+    VLB_LOCK(h);
+    if (!out || bytes == 0) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid pinned allocation");
+    *out = nullptr;
+    const cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+        *out = nullptr;
+        (void)cudaGetLastError();
+        return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, cuda_msg("cudaHostAlloc", e));
+    }
+    return VLB_OK;
+}
+
+int vlb_host_free(vlb_handle* h, void* p) {
+    VLB_LOCK(h);
+    if (!p) return VLB_OK;
+    VLB_CUDA(h, cudaFreeHost(p));
+    return VLB_OK;
+}
+
 
 int vlb_release_matrix(vlb_handle* h, vlb_matrix* m) {
     VLB_LOCK(h);

@@ -186,9 +186,23 @@ def activations(spec: LayerSpec, T: int, seed: int):
     return x, tok, logits
 
 
-def upload_layer(dev, W: LayerWeights, max_tokens: int, layer_index: int = 0):
+def expert_record(W: LayerWeights, e: int, identities) -> tuple:
+    """Expert e's record as an expert pack holds it (its W1, W3, W2 ggml bytes back to back) and
+    its (identity, type, rows, storage_cols, offset, bytes) tensor list."""
+    H, I = W.spec.hidden, W.spec.intermediate
+    parts, tensors, off = [], [], 0
+    for ident, (name, rows, cols) in zip(identities, (("w1", I, H), ("w3", I, H), ("w2", H, I))):
+        t, b = getattr(W, name)[e]
+        parts.append(np.asarray(b, np.uint8).reshape(-1))
+        tensors.append((ident, t, rows, cols, off, parts[-1].nbytes))
+        off += parts[-1].nbytes
+    return np.concatenate(parts), tensors
+
+
+def upload_layer(dev, W: LayerWeights, max_tokens: int, layer_index: int = 0, records: bool = False):
     """Uploads every matrix (identities in the reference's expert style: nonzero, stable per
-    (layer, expert, role)) and creates the device layer."""
+    (layer, expert, role)) and creates the device layer. records=True moves each routed expert
+    as one record (vlb_upload_record_async), up to 64 in flight."""
     from . import MoeLayer
 
     spec = W.spec
@@ -198,7 +212,20 @@ def upload_layer(dev, W: LayerWeights, max_tokens: int, layer_index: int = 0):
         return ((layer_index * 1_000_003 + e) * 4 + role) * 2 + 1
 
     mats = {"w1": [], "w3": [], "w2": []}
-    for e in range(spec.experts):
+    if records:
+        pending = []
+
+        def drain(keep):
+            while len(pending) > keep:
+                for name, m in zip(("w1", "w3", "w2"), pending.pop(0).finish()):
+                    mats[name].append(m)
+
+        for e in range(spec.experts):
+            rec, tensors = expert_record(W, e, [ident(e, role) for role in range(3)])
+            pending.append(dev.upload_record(rec, tensors))
+            drain(63)
+        drain(0)
+    for e in range(0 if records else spec.experts):
         for role, (name, rows, cols) in enumerate((("w1", I, H), ("w3", I, H), ("w2", H, I))):
             t, b = getattr(W, name)[e]
             mats[name].append(dev.upload_matrix(t, rows, cols, b, identity=ident(e, role)))
