@@ -112,6 +112,50 @@ class _LayerBuilder:
         self.layer = L
 
 
+def _hc_argtypes(L, pre):
+    P, SZ, F = C.c_void_p, C.c_size_t, C.c_float
+    getattr(L, pre + "_hc_split_sinkhorn").argtypes = [P, P, P, SZ, SZ, SZ, F, P, P, P]
+    getattr(L, pre + "_hc_pre").argtypes = [P, P, P, P, SZ, SZ, SZ, SZ, F, F, P, P, P, P]
+    getattr(L, pre + "_hc_post").argtypes = [P, P, P, P, SZ, SZ, SZ, P]
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def _hc_split(lib, pre, mixes, scale, base, m, iters, eps):
+    """deepseek_v4_hc_split_sinkhorn: mixes [T, (2+m)m] -> pre [T, m], post [T, m], comb [T, m, m]."""
+    mixes = _f32(mixes)
+    T = mixes.shape[0]
+    p, q, c = np.empty((T, m), np.float32), np.empty((T, m), np.float32), np.empty((T, m, m), np.float32)
+    if getattr(lib, pre + "_hc_split_sinkhorn")(_p(mixes), _p(_f32(scale)), _p(_f32(base)), T, m, iters, eps,
+                                                _p(p), _p(q), _p(c)):
+        raise ValueError("hc_split_sinkhorn failed")
+    return p, q, c
+
+
+def _hc_pre(lib, pre, x, fn, scale, base, iters, norm_eps, hc_eps):
+    """deepseek_v4_hc_pre: x [T, m, W] -> reduced [T, W] and the split."""
+    x = _f32(x)
+    T, m, W = x.shape
+    red = np.empty((T, W), np.float32)
+    p, q, c = np.empty((T, m), np.float32), np.empty((T, m), np.float32), np.empty((T, m, m), np.float32)
+    if getattr(lib, pre + "_hc_pre")(_p(x), _p(_f32(fn)), _p(_f32(scale)), _p(_f32(base)), T, m, W, iters,
+                                     norm_eps, hc_eps, _p(red), _p(p), _p(q), _p(c)):
+        raise ValueError("hc_pre failed")
+    return red, p, q, c
+
+
+def _hc_post(lib, pre, sub, residual, post, comb):
+    """deepseek_v4_hc_post: sub [T, W], residual [T, m, W] -> [T, m, W]."""
+    residual = _f32(residual)
+    T, m, W = residual.shape
+    out = np.empty_like(residual)
+    if getattr(lib, pre + "_hc_post")(_p(_f32(sub)), _p(residual), _p(_f32(post)), _p(_f32(comb)), T, m, W, _p(out)):
+        raise ValueError("hc_post failed")
+    return out
+
+
 class Oracle:
     """The plain-C restatement (parity checker)."""
 
@@ -147,6 +191,7 @@ class Oracle:
         L.vlo_dispatch.argtypes = [P, SZ, SZ, SZ, P, P, P]
         L.vlo_dispatch.restype = None
         L.vlo_rms_norm.argtypes = [P, P, SZ, SZ, F, P]
+        _hc_argtypes(L, "vlo")
         L.vlo_moe_forward.argtypes = [C.POINTER(_OracleLayer), P, P, SZ, P, P, P, P]
 
     def grid(self, t):
@@ -246,6 +291,15 @@ class Oracle:
         self.lib.vlo_dispatch(_p(idx), T, k, E, _p(off), _p(pt), _p(ps))
         return off, pt, ps
 
+    def hc_split_sinkhorn(self, mixes, scale, base, m, iters, eps):
+        return _hc_split(self.lib, "vlo", mixes, scale, base, m, iters, eps)
+
+    def hc_pre(self, x, fn, scale, base, iters, norm_eps, hc_eps):
+        return _hc_pre(self.lib, "vlo", x, fn, scale, base, iters, norm_eps, hc_eps)
+
+    def hc_post(self, sub, residual, post, comb):
+        return _hc_post(self.lib, "vlo", sub, residual, post, comb)
+
     def rms_norm(self, x, w, eps):
         x = np.ascontiguousarray(x, np.float32)
         rows, width = x.shape
@@ -314,6 +368,7 @@ class Reference:
         L.vlr_route_learned.argtypes = [P, P, SZ, SZ, SZ, F, P, P]
         L.vlr_route_hash.argtypes = [P, P, P, SZ, SZ, SZ, SZ, F, P, P]
         L.vlr_rms_norm.argtypes = [P, P, SZ, SZ, F, P]
+        _hc_argtypes(L, "vlr")
         L.vlr_moe_forward.argtypes = [C.POINTER(_RefLayer), P, P, SZ, P, P, P, P, C.c_uint]
         L.vlr_qwen_route.argtypes = [P, P, SZ, SZ, SZ, SZ, I, P, P, P]
         L.vlr_expert_swiglu.argtypes = [P, P, P, P, P, SZ, SZ, SZ, F, P]
@@ -389,6 +444,15 @@ class Reference:
                                       _p(np.ascontiguousarray(up_w, np.float32)), _p(rw), T, H, I, limit, _p(out)):
             raise ValueError("reference expert_swiglu failed")
         return out
+
+    def hc_split_sinkhorn(self, mixes, scale, base, m, iters, eps):
+        return _hc_split(self.lib, "vlr", mixes, scale, base, m, iters, eps)
+
+    def hc_pre(self, x, fn, scale, base, iters, norm_eps, hc_eps):
+        return _hc_pre(self.lib, "vlr", x, fn, scale, base, iters, norm_eps, hc_eps)
+
+    def hc_post(self, sub, residual, post, comb):
+        return _hc_post(self.lib, "vlr", sub, residual, post, comb)
 
     def rms_norm(self, x, w, eps):
         x = np.ascontiguousarray(x, np.float32)

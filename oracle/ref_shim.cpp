@@ -139,6 +139,47 @@ int vlr_rms_norm(const float* x, const float* w, size_t rows, size_t width, floa
     return 0;
 }
 
+static void copy_split(const vi::DeepseekV4HyperConnectionSplit& s, float* pre, float* post, float* comb) {
+    std::memcpy(pre, s.pre.data(), s.pre.size() * sizeof(float));
+    std::memcpy(post, s.post.data(), s.post.size() * sizeof(float));
+    std::memcpy(comb, s.combination.data(), s.combination.size() * sizeof(float));
+}
+
+int vlr_hc_split_sinkhorn(const float* mixes, const float* scale, const float* base, size_t T, size_t m,
+                          size_t iters, float eps, float* pre, float* post, float* comb) {
+    auto r = vi::deepseek_v4_hc_split_sinkhorn({mixes, T * (2 + m) * m}, {scale, 3}, {base, (2 + m) * m}, T, m,
+                                               iters, eps);
+    if (!r) return -1;
+    copy_split(r.value(), pre, post, comb);
+    return 0;
+}
+
+int vlr_hc_pre(const float* x, const float* fn, const float* scale, const float* base, size_t T, size_t m,
+               size_t W, size_t iters, float norm_eps, float hc_eps, float* reduced, float* pre, float* post,
+               float* comb) {
+    const size_t mw = (2 + m) * m;
+    auto r = vi::deepseek_v4_hc_pre({x, T * m * W}, {fn, mw * m * W}, {scale, 3}, {base, mw}, T, m, W, iters,
+                                    norm_eps, hc_eps);
+    if (!r) return -1;
+    std::memcpy(reduced, r.value().reduced.data(), T * W * sizeof(float));
+    copy_split(r.value().split, pre, post, comb);
+    return 0;
+}
+
+int vlr_hc_post(const float* sub, const float* residual, const float* post, const float* comb, size_t T,
+                size_t m, size_t W, float* out) {
+    vi::DeepseekV4HyperConnectionSplit split;
+    split.token_count = T;
+    split.multiplier = m;
+    split.pre.assign(T * m, 1.0f);
+    split.post.assign(post, post + T * m);
+    split.combination.assign(comb, comb + T * m * m);
+    auto r = vi::deepseek_v4_hc_post({sub, T * W}, {residual, T * m * W}, split, W);
+    if (!r) return -1;
+    std::memcpy(out, r.value().data(), T * m * W * sizeof(float));
+    return 0;
+}
+
 // qwen38_moe_route (qwen3_8_flash_next_reference.cpp:1186-1239) for T tokens: hidden [T x H],
 // router [E x H]; logits [T x E] (may be null), idx / w [T x k].
 int vlr_qwen_route(const float* hidden, const float* router, size_t T, size_t H, size_t E, size_t k,

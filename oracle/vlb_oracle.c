@@ -576,6 +576,100 @@ int vlo_rms_norm(const float* x, const float* w, size_t rows, size_t width, floa
     return 0;
 }
 
+/* deepseek_v4_hc_split_sinkhorn, deepseek_v4_reference.cpp:387-477. mixes [T x (2+m)m]: per token
+ * the m pre logits, the m post logits, then the m x m combination logits (row-major,
+ * [source][destination]). */
+int vlo_hc_split_sinkhorn(const float* mixes, const float* scale, const float* base, size_t T, size_t m,
+                          size_t iters, float eps, float* pre, float* post, float* comb) {
+    if (T == 0 || m == 0 || m > 16 || iters == 0) return -1;
+    const size_t mw = (2 + m) * m;
+    for (size_t t = 0; t < T; ++t) {
+        const float* mx = mixes + t * mw;
+        for (size_t i = 0; i < m; ++i) {
+            pre[t * m + i] = vlo_sigmoid(mx[i] * scale[0] + base[i]) + eps;
+            post[t * m + i] = 2.0f * vlo_sigmoid(mx[m + i] * scale[1] + base[m + i]);
+        }
+        float* c = comb + t * m * m;
+        for (size_t r = 0; r < m; ++r) {  /* softmax over each row, plus eps */
+            float mxv = -INFINITY;
+            for (size_t j = 0; j < m; ++j) {
+                const size_t at = 2 * m + r * m + j;
+                c[r * m + j] = mx[at] * scale[2] + base[at];
+                if (c[r * m + j] > mxv) mxv = c[r * m + j];
+            }
+            double sum = 0.0;
+            for (size_t j = 0; j < m; ++j) {
+                c[r * m + j] = (float)exp((double)(c[r * m + j] - mxv));
+                sum += (double)c[r * m + j];
+            }
+            for (size_t j = 0; j < m; ++j) c[r * m + j] = (float)((double)c[r * m + j] / sum) + eps;
+        }
+        for (size_t it = 0; it < iters; ++it) {
+            if (it > 0)
+                for (size_t r = 0; r < m; ++r) {  /* rows */
+                    double sum = 0.0;
+                    for (size_t j = 0; j < m; ++j) sum += (double)c[r * m + j];
+                    for (size_t j = 0; j < m; ++j) c[r * m + j] = (float)((double)c[r * m + j] / (sum + (double)eps));
+                }
+            for (size_t j = 0; j < m; ++j) {  /* columns */
+                double sum = 0.0;
+                for (size_t r = 0; r < m; ++r) sum += (double)c[r * m + j];
+                for (size_t r = 0; r < m; ++r) c[r * m + j] = (float)((double)c[r * m + j] / (sum + (double)eps));
+            }
+        }
+    }
+    return 0;
+}
+
+/* deepseek_v4_hc_pre, deepseek_v4_reference.cpp:479-547 (the f32 mixing-weight form; the graph's
+ * hc_pre, deepseek_v4_graph.cpp:2276-2295). x [T x m x W], fn [(2+m)m x mW]; reduced [T x W]. */
+int vlo_hc_pre(const float* x, const float* fn, const float* scale, const float* base, size_t T, size_t m,
+               size_t W, size_t iters, float norm_eps, float hc_eps, float* reduced, float* pre, float* post,
+               float* comb) {
+    if (T == 0 || m == 0 || m > 16 || W == 0) return -1;
+    const size_t fw = m * W, mw = (2 + m) * m;
+    float* mixes = (float*)malloc(T * mw * sizeof(float));
+    if (!mixes) return -1;
+    for (size_t t = 0; t < T; ++t) {
+        const float* row = x + t * fw;
+        double sq = 0.0;
+        for (size_t c = 0; c < fw; ++c) { const double v = (double)row[c]; sq += v * v; }
+        const double inv = 1.0 / sqrt(sq / (double)fw + (double)norm_eps);
+        for (size_t r = 0; r < mw; ++r) {
+            double sum = 0.0;
+            for (size_t c = 0; c < fw; ++c) sum += (double)row[c] * (double)fn[r * fw + c];
+            mixes[t * mw + r] = (float)(sum * inv);
+        }
+    }
+    const int st = vlo_hc_split_sinkhorn(mixes, scale, base, T, m, iters, hc_eps, pre, post, comb);
+    free(mixes);
+    if (st) return st;
+    for (size_t t = 0; t < T; ++t)
+        for (size_t c = 0; c < W; ++c) {
+            double sum = 0.0;
+            for (size_t j = 0; j < m; ++j) sum += (double)pre[t * m + j] * (double)x[(t * m + j) * W + c];
+            reduced[t * W + c] = (float)sum;
+            if (!isfinite(reduced[t * W + c])) return -1;
+        }
+    return 0;
+}
+
+/* deepseek_v4_hc_post, deepseek_v4_reference.cpp:549-610: out[t, d] = post[d] * sub[t] +
+ * sum over sources s of comb[s][d] * residual[t, s], in f64. */
+int vlo_hc_post(const float* sub, const float* residual, const float* post, const float* comb, size_t T,
+                size_t m, size_t W, float* out) {
+    for (size_t t = 0; t < T; ++t)
+        for (size_t d = 0; d < m; ++d)
+            for (size_t c = 0; c < W; ++c) {
+                double v = (double)post[t * m + d] * (double)sub[t * W + c];
+                for (size_t s2 = 0; s2 < m; ++s2)
+                    v += (double)comb[(t * m + s2) * m + d] * (double)residual[(t * m + s2) * W + c];
+                out[(t * m + d) * W + c] = (float)v;
+                if (!isfinite(out[(t * m + d) * W + c])) return -1;
+            }
+    return 0;
+}
+
 static const void* grid_for(const vlo_moe_layer* L, uint32_t type) {
     switch (type) {
         case VLO_TYPE_IQ1_S: return L->grid_iq1_s;

@@ -79,6 +79,13 @@ int vlo_expert_swiglu(const float* x, const float* gate_w, const float* down_w, 
  * ordered by expert ascending, then token, then slot. */
 void vlo_dispatch(const uint32_t* idx, size_t T, size_t k, size_t E, uint32_t* offsets,
                   uint32_t* pair_token, uint32_t* pair_slot);
+int vlo_hc_split_sinkhorn(const float* mixes, const float* scale, const float* base, size_t T, size_t m,
+                          size_t iters, float eps, float* pre, float* post, float* comb);
+int vlo_hc_pre(const float* x, const float* fn, const float* scale, const float* base, size_t T, size_t m,
+               size_t W, size_t iters, float norm_eps, float hc_eps, float* reduced, float* pre, float* post,
+               float* comb);
+int vlo_hc_post(const float* sub, const float* residual, const float* post, const float* comb, size_t T,
+                size_t m, size_t W, float* out);
 int vlo_rms_norm(const float* x, const float* w, size_t rows, size_t width, float eps,
                  float* out);
 
