@@ -269,6 +269,36 @@ int vlb_layer_set_prefill_tokens(vlb_handle* h, vlb_layer* layer, uint32_t min_t
  * removes it. Rows must be 16-byte aligned; given-routes and half-row forwards are refused while
  * it is set. */
 int vlb_layer_set_input_norm(vlb_handle* h, vlb_layer* layer, const float* weight, float eps);
+
+/* Hyper-Connection entry and exit (the ffn half of a DeepSeek V4 block, deepseek_v4_graph.cpp:
+ * 2391-2408 and 2452-2469):
+ *     split, reduced = hc_pre(x)           deepseek_v4_hc_pre, deepseek_v4_reference.cpp:479-547
+ *     moe            = MoE(RMSNorm(reduced, norm_weight))
+ *     out            = hc_post(moe, x)     deepseek_v4_hc_post, :549-610
+ * With it set, x and out of vlb_layer_forward / vlb_layer_forward_device hold `multiplier` copies
+ * of each token's hidden state, [T x multiplier x hidden] f32. The entry is one kernel (the mixing
+ * projection as sequential f64 chains, the Sinkhorn split, the reduced row, the norm: mixes,
+ * reduced row and norm bit-identical with the reference, the split too except where CUDA's and the
+ * host's double exp differ in the last bit); the exit is fused into the combine (f64 sums in the
+ * reference's order). The mixing weight is the f32 `hc_ffn_fn` form (deepseek_v4_graph.cpp:
+ * 2289-2295). It replaces an input norm; NULL removes both. Given-routes and half-row forwards
+ * are refused while it is set. A reduced row that is not finite fails the forward with
+ * VLB_ERR_INVALID_FORMAT. */
+typedef struct vlb_hc_desc {
+    uint32_t multiplier;          /* m, 1..16 (config.hyper_multiplier); m x hidden <= 24576 */
+    uint32_t sinkhorn_iterations; /* >= 1 (config.sinkhorn_iterations) */
+    float norm_epsilon;           /* config.norm_epsilon: the mixing RMS and the ffn norm */
+    float hc_epsilon;             /* config.hyper_epsilon */
+    const float* mixing_weight;   /* hc_ffn_fn [(2+m)m x m*hidden] */
+    const float* scale;           /* hc_ffn_scale [3] */
+    const float* base;            /* hc_ffn_base [(2+m)m] */
+    const float* norm_weight;     /* ffn_norm.weight [hidden] */
+} vlb_hc_desc;
+int vlb_layer_set_hyper_connection(vlb_handle* h, vlb_layer* layer, const vlb_hc_desc* desc);
+/* The split of the last forward's first T tokens (host arrays; any may be NULL): pre and post
+ * [T x m], combination [T x m x m] ([source][destination]). */
+int vlb_layer_last_hyper_split(vlb_handle* h, vlb_layer* layer, uint32_t T, float* pre, float* post,
+                               float* combination);
 uint32_t vlb_layer_prefill_tokens(vlb_handle* h, vlb_layer* layer);
 
 /* Given-routes forward (an expert-parallel group): idx_dev u32 [T x k] expert ids of this layer

@@ -118,6 +118,12 @@ class _RecordTensor(C.Structure):
                 ("bytes", C.c_uint64)]
 
 
+class _HcDesc(C.Structure):
+    _fields_ = [("multiplier", C.c_uint32), ("sinkhorn_iterations", C.c_uint32), ("norm_epsilon", C.c_float),
+                ("hc_epsilon", C.c_float), ("mixing_weight", C.c_void_p), ("scale", C.c_void_p),
+                ("base", C.c_void_p), ("norm_weight", C.c_void_p)]
+
+
 class _LayerDesc(C.Structure):
     _fields_ = [
         ("hidden", C.c_uint32),
@@ -158,7 +164,8 @@ EXPORTS = (
     "vlb_ep_plan_device vlb_ep_plan_half_device vlb_ep_pack_half_device vlb_ep_combine_half_device vlb_layer_forward_rows_half_device vlb_ep_combine_device vlb_route_device vlb_route_device_noalloc vlb_router_logits_device vlb_rms_norm_device "
     "vlb_ep_nccl_version vlb_ep_unique_id vlb_ep_comm_init vlb_ep_comm_destroy vlb_ep_comm_abort "
     "vlb_ep_all_to_all_device vlb_ep_layer_create vlb_ep_layer_destroy vlb_ep_forward_device vlb_ep_last_phases "
-    "vlb_upload_record_async vlb_upload_query vlb_upload_finish vlb_host_alloc vlb_host_free"
+    "vlb_upload_record_async vlb_upload_query vlb_upload_finish vlb_host_alloc vlb_host_free "
+    "vlb_layer_set_hyper_connection vlb_layer_last_hyper_split"
 ).split()
 
 
@@ -234,6 +241,8 @@ def load_library() -> C.CDLL:
         "vlb_upload_finish": (I, [P, P, C.POINTER(P), U32]),
         "vlb_host_alloc": (I, [P, SZ, C.POINTER(P)]),
         "vlb_host_free": (I, [P, P]),
+        "vlb_layer_set_hyper_connection": (I, [P, P, C.POINTER(_HcDesc)]),
+        "vlb_layer_last_hyper_split": (I, [P, P, U32, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -589,10 +598,13 @@ class MoeLayer:
         (f32 [T, H], C-contiguous) may be supplied, e.g. page-locked, to receive the output."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         T = x.shape[0]
+        shape = (T, self.hc_m, self.H) if self.hc_m else (T, self.H)
+        if x.shape != shape:
+            raise ValueError(f"x must have shape {shape}")
         if out is None:
-            out = np.empty((T, self.H), dtype=np.float32)
-        elif out.dtype != np.float32 or out.shape != (T, self.H) or not out.flags["C_CONTIGUOUS"]:
-            raise ValueError("out must be a C-contiguous float32 array of shape (T, hidden)")
+            out = np.empty(shape, dtype=np.float32)
+        elif out.dtype != np.float32 or out.shape != shape or not out.flags["C_CONTIGUOUS"]:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
         tok = None if token_ids is None else np.ascontiguousarray(token_ids, dtype=np.uint32)
         lg = None if logits is None else np.ascontiguousarray(logits, dtype=np.float32)
         self.dev._check(self.dev.lib.vlb_layer_forward(
@@ -660,6 +672,34 @@ class MoeLayer:
             raise ValueError("the norm weight must have `hidden` elements")
         self.dev._check(self.dev.lib.vlb_layer_set_input_norm(self.dev.h, self.ptr, _ptr(w), eps))
         self._norm_w = w
+
+    hc_m = 0
+
+    def set_hyper_connection(self, multiplier: int, mixing_weight, scale, base, norm_weight,
+                             sinkhorn_iterations: int = 20, norm_eps: float = 1e-6, hc_eps: float = 1e-6) -> None:
+        """Hyper-Connection entry and exit around the MoE (vlb_layer_set_hyper_connection): x and
+        out become [T, multiplier, hidden]. multiplier 0 removes it (and the norm)."""
+        if multiplier == 0:
+            self.dev._check(self.dev.lib.vlb_layer_set_hyper_connection(self.dev.h, self.ptr, None))
+            self.hc_m = 0
+            return
+        m, H = multiplier, self.H
+        fn = np.ascontiguousarray(mixing_weight, np.float32)
+        sc, ba = np.ascontiguousarray(scale, np.float32), np.ascontiguousarray(base, np.float32)
+        nw = np.ascontiguousarray(norm_weight, np.float32)
+        if fn.size != (2 + m) * m * m * H or sc.size != 3 or ba.size != (2 + m) * m or nw.size != H:
+            raise ValueError("Hyper-Connection tensors have the wrong sizes")
+        d = _HcDesc(m, sinkhorn_iterations, norm_eps, hc_eps, _ptr(fn), _ptr(sc), _ptr(ba), _ptr(nw))
+        self.dev._check(self.dev.lib.vlb_layer_set_hyper_connection(self.dev.h, self.ptr, C.byref(d)))
+        self.hc_m = m
+
+    def last_hyper_split(self, T: int):
+        """(pre [T, m], post [T, m], combination [T, m, m]) of the last forward."""
+        m = self.hc_m
+        pre, post, comb = np.empty((T, m), np.float32), np.empty((T, m), np.float32), np.empty((T, m, m), np.float32)
+        self.dev._check(self.dev.lib.vlb_layer_last_hyper_split(self.dev.h, self.ptr, T, _ptr(pre), _ptr(post),
+                                                                _ptr(comb)))
+        return pre, post, comb
 
     PREFILL_NEVER = 0xFFFFFFFF
 

@@ -206,6 +206,10 @@ struct vlb_layer {
     // residual block entry (vlb_layer_set_input_norm): RMSNorm weight [H] and epsilon
     float* norm_w = nullptr;
     float norm_eps = 0.f;
+    // Hyper-Connection block (vlb_layer_set_hyper_connection): its parameters and split buffers in
+    // one allocation; x_dev / out_dev then hold m copies per token
+    void* hc_mem = nullptr;
+    uint32_t hc_m = 0;
     // workspace
     void* ws = nullptr;
     MoeParams p{};
@@ -865,7 +869,7 @@ static void free_layer(vlb_handle* h, vlb_layer* L) {
     for (auto& e : L->ev)
         if (e) cudaEventDestroy(e);
     void* ptrs[] = {L->router, L->bias, L->tid2eid, L->mats, L->ws,
-                    L->x_dev, L->tok_dev, L->logits_dev, L->out_dev, L->norm_w};
+                    L->x_dev, L->tok_dev, L->logits_dev, L->out_dev, L->norm_w, L->hc_mem};
     for (void* p : ptrs)
         if (p) h->gfree(p);
     delete L;
@@ -1059,6 +1063,8 @@ static int check_layer_flags(vlb_handle* h, uint32_t flags) {
     if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
     if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "an expert-kernel pipeline wait ran out of time");
     if (flags & 16u) return h->fail(VLB_ERR_INTERNAL_ERROR, "prefill shared memory is not 1 KB aligned");
+    if (flags & kLayerErrHcNonFinite)
+        return h->fail(VLB_ERR_INVALID_FORMAT, "Hyper-Connection reduced output is not finite");
     return VLB_OK;
 }
 
@@ -1098,6 +1104,7 @@ static int forward_locked(vlb_handle* h, vlb_layer* L, const float* x, const uin
         return h->fail(VLB_ERR_UNSUPPORTED, "a layer with an input norm takes plain token rows only");
     p.norm_w = L->norm_w;
     p.norm_eps = L->norm_eps;
+    p.hc_m = L->hc_m;
     if (L->norm_w && ((reinterpret_cast<uintptr_t>(x) % 16u) || L->desc.hidden > kRmsMaxWidth))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "input rows of a normed layer must be 16-byte aligned");
     // half rows carry fp16 operands already: only the tensor-core prefill path consumes them
@@ -1188,7 +1195,7 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_
     if (!L || !x || !out) return h->fail(VLB_ERR_INVALID_ARGUMENT, "invalid forward argument");
     if (T == 0 || T > L->desc.max_tokens)
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "token count is zero or above the layer's max_tokens");
-    const uint32_t H = L->desc.hidden, E = L->desc.experts;
+    const uint32_t H = L->desc.hidden * (L->hc_m ? L->hc_m : 1u), E = L->desc.experts;  // row width in and out
     cudaStream_t s = h->stream;
     VLB_CUDA(h, cudaMemcpyAsync(L->x_dev, x, (size_t)T * H * 4, cudaMemcpyHostToDevice, s));
     if (tok) VLB_CUDA(h, cudaMemcpyAsync(L->tok_dev, tok, (size_t)T * 4, cudaMemcpyHostToDevice, s));
@@ -1206,6 +1213,8 @@ int vlb_layer_forward(vlb_handle* h, vlb_layer* L, const float* x, const uint32_
 int vlb_layer_set_input_norm(vlb_handle* h, vlb_layer* L, const float* weight, float eps) {
     VLB_LOCK(h);
     if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
+    if (L->hc_m)
+        return h->fail(VLB_ERR_INVALID_ARGUMENT, "a Hyper-Connection layer takes its norm with its descriptor");
     const uint32_t H = L->desc.hidden;
     if (weight && !(eps > 0.f && std::isfinite(eps)))
         return h->fail(VLB_ERR_INVALID_ARGUMENT, "RMSNorm epsilon must be finite and positive");
@@ -1229,6 +1238,102 @@ int vlb_layer_set_input_norm(vlb_handle* h, vlb_layer* L, const float* weight, f
     }
     VLB_CUDA(h, cudaMemcpy(L->norm_w, weight, (size_t)H * 4, cudaMemcpyHostToDevice));
     L->norm_eps = eps;
+    return VLB_OK;
+}
+
+int vlb_layer_set_hyper_connection(vlb_handle* h, vlb_layer* L, const vlb_hc_desc* d) {
+    VLB_LOCK(h);
+    if (!L) return h->fail(VLB_ERR_INVALID_ARGUMENT, "null layer");
+    const uint32_t H = L->desc.hidden, T = L->desc.max_tokens;
+    if (d) {
+        const uint32_t m = d->multiplier;
+        if (m == 0 || m > 16 || d->sinkhorn_iterations == 0 || !d->mixing_weight || !d->scale || !d->base ||
+            !d->norm_weight)
+            return h->fail(VLB_ERR_INVALID_ARGUMENT, "Hyper-Connection dimensions are invalid");
+        if (!(d->norm_epsilon > 0.f && std::isfinite(d->norm_epsilon)) ||
+            !(d->hc_epsilon > 0.f && std::isfinite(d->hc_epsilon)))
+            return h->fail(VLB_ERR_INVALID_ARGUMENT, "Hyper-Connection epsilons must be finite and positive");
+        if ((size_t)m * H > kRmsMaxWidth)
+            return h->fail(VLB_ERR_UNSUPPORTED, "multiplier x hidden is too large for the Hyper-Connection entry");
+        const size_t mw = (size_t)(2 + m) * m, fw = (size_t)m * H;
+        for (size_t i = 0; i < mw * fw; ++i)
+            if (!std::isfinite(d->mixing_weight[i]))
+                return h->fail(VLB_ERR_INVALID_ARGUMENT, "Hyper-Connection mixing weight is not finite");
+        for (size_t i = 0; i < mw; ++i)
+            if (!std::isfinite(d->base[i])) return h->fail(VLB_ERR_INVALID_ARGUMENT, "Hyper-Connection base is not finite");
+        for (size_t i = 0; i < 3; ++i)
+            if (!std::isfinite(d->scale[i])) return h->fail(VLB_ERR_INVALID_ARGUMENT, "Hyper-Connection scale is not finite");
+        for (uint32_t c = 0; c < H; ++c)
+            if (!std::isfinite(d->norm_weight[c])) return h->fail(VLB_ERR_INVALID_ARGUMENT, "RMSNorm weight is not finite");
+    }
+    VLB_CUDA(h, cudaStreamSynchronize(h->stream));
+    if (L->gexec) {  // the captured forward does not have the new entry and exit
+        cudaGraphExecDestroy(L->gexec);
+        L->gexec = nullptr;
+    }
+    // the host-memory forward's staging: m copies per token with the Hyper-Connection, one without
+    const uint32_t m_new = d ? d->multiplier : 0u, rows_new = m_new ? m_new : 1u, rows_old = L->hc_m ? L->hc_m : 1u;
+    if (rows_new != rows_old) {
+        h->gfree(L->x_dev);
+        h->gfree(L->out_dev);
+        L->x_dev = L->out_dev = nullptr;
+        int st = h->galloc((size_t)T * rows_new * H * 4, "vlb-layer-x", (void**)&L->x_dev);
+        if (st == VLB_OK) st = h->galloc((size_t)T * rows_new * H * 4, "vlb-layer-out", (void**)&L->out_dev);
+        if (st != VLB_OK) {
+            L->hc_m = 0;  // the layer stays usable only after a successful set
+            return st;
+        }
+    }
+    if (L->hc_mem) h->gfree(L->hc_mem);
+    L->hc_mem = nullptr;
+    L->hc_m = 0;
+    if (!d) {
+        if (L->norm_w) h->gfree(L->norm_w);
+        L->norm_w = nullptr;
+        L->p.hc_m = 0;
+        return VLB_OK;
+    }
+    const uint32_t m = d->multiplier;
+    const size_t mw = (size_t)(2 + m) * m, fw = (size_t)m * H;
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t o_fn = 0, o_scale = up(mw * fw * 4), o_base = o_scale + 256, o_pre = o_base + up(mw * 4);
+    const size_t o_post = o_pre + up((size_t)T * m * 4), o_comb = o_post + up((size_t)T * m * 4);
+    const size_t total = o_comb + up((size_t)T * m * m * 4);
+    int st = h->galloc(total, "vlb-hyper-connection", &L->hc_mem);
+    if (st != VLB_OK) return st;
+    char* b = static_cast<char*>(L->hc_mem);
+    VLB_CUDA(h, cudaMemcpy(b + o_fn, d->mixing_weight, mw * fw * 4, cudaMemcpyHostToDevice));
+    VLB_CUDA(h, cudaMemcpy(b + o_scale, d->scale, 12, cudaMemcpyHostToDevice));
+    VLB_CUDA(h, cudaMemcpy(b + o_base, d->base, mw * 4, cudaMemcpyHostToDevice));
+    if (!L->norm_w) {
+        st = h->galloc((size_t)H * 4, "vlb-input-norm", (void**)&L->norm_w);
+        if (st != VLB_OK) return st;
+    }
+    VLB_CUDA(h, cudaMemcpy(L->norm_w, d->norm_weight, (size_t)H * 4, cudaMemcpyHostToDevice));
+    L->norm_eps = d->norm_epsilon;
+    MoeParams& p = L->p;
+    p.hc_iters = d->sinkhorn_iterations;
+    p.hc_eps = d->hc_epsilon;
+    p.hc_fn = reinterpret_cast<const float*>(b + o_fn);
+    p.hc_scale = reinterpret_cast<const float*>(b + o_scale);
+    p.hc_base = reinterpret_cast<const float*>(b + o_base);
+    p.hc_pre = reinterpret_cast<float*>(b + o_pre);
+    p.hc_post = reinterpret_cast<float*>(b + o_post);
+    p.hc_comb = reinterpret_cast<float*>(b + o_comb);
+    L->hc_m = m;
+    return VLB_OK;
+}
+
+int vlb_layer_last_hyper_split(vlb_handle* h, vlb_layer* L, uint32_t T, float* pre, float* post, float* comb) {
+    VLB_LOCK(h);
+    if (!L || !L->hc_m) return h->fail(VLB_ERR_INVALID_ARGUMENT, "the layer has no Hyper-Connection");
+    if (T == 0 || T > L->last_T) return h->fail(VLB_ERR_INVALID_ARGUMENT, "more tokens than the last forward had");
+    const size_t m = L->hc_m;
+    cudaStream_t s = h->stream;
+    if (pre) VLB_CUDA(h, cudaMemcpyAsync(pre, L->p.hc_pre, T * m * 4, cudaMemcpyDeviceToHost, s));
+    if (post) VLB_CUDA(h, cudaMemcpyAsync(post, L->p.hc_post, T * m * 4, cudaMemcpyDeviceToHost, s));
+    if (comb) VLB_CUDA(h, cudaMemcpyAsync(comb, L->p.hc_comb, T * m * m * 4, cudaMemcpyDeviceToHost, s));
+    VLB_CUDA(h, cudaStreamSynchronize(s));
     return VLB_OK;
 }
 

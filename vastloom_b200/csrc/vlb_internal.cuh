@@ -69,6 +69,10 @@ __host__ __device__ inline bool type_layout(uint32_t type, TypeLayout* l) {
 
 constexpr uint32_t kTileRows = 128;
 
+// Layer error flag (MoeParams::counters[3]) of a Hyper-Connection reduced row that is not finite
+// (deepseek_v4_hc_pre rejects it, deepseek_v4_reference.cpp:544-545).
+constexpr uint32_t kLayerErrHcNonFinite = 32u;
+
 // Index of block `blk` of row `row` in the tiled d / body arrays of a matrix with `bpr` blocks per
 // row; consecutive blocks of one row are kTileRows entries apart.
 __host__ __device__ __forceinline__ size_t blk_index(uint32_t bpr, uint32_t row, uint32_t blk) {
@@ -281,6 +285,20 @@ struct MoeParams {
     float norm_eps;
     float* x_norm;           // [T x H] workspace
     const float* x_residual; // set by launch_moe for a residual block: the original rows
+    // Hyper-Connection block (hc_m > 0; the input norm is set too): x and out hold m copies of
+    // each token's hidden state, [T x m x H]. The entry computes the token's split (pre, post,
+    // combination) and its reduced row, then the input norm; the combine writes
+    // out[t, d] = post[d] * MoE[t] + sum_s comb[s][d] * x[t, s]
+    uint32_t hc_m;           // 0: no Hyper-Connection
+    uint32_t hc_iters;       // Sinkhorn iterations
+    float hc_eps;            // the split's epsilon (the mixing RMS uses norm_eps)
+    const float* hc_fn;      // [(2+m)m x mH] mixing weight
+    const float* hc_scale;   // [3]
+    const float* hc_base;    // [(2+m)m]
+    float* hc_pre;           // [T x m] workspace: the split of the last forward
+    float* hc_post;          // [T x m]
+    float* hc_comb;          // [T x m x m], [source][destination]
+    const float* hc_state;   // set by launch_moe: the original [T x m x H] rows
     uint32_t max_units;
     uint32_t* disp_counts;   // [ceil(T*k / 1024) x E]: per-chunk expert counts of the multi-CTA dispatch
     // K-split scratch of the decode kernels (small batches): 16 warps x 32 lanes x 8 floats of

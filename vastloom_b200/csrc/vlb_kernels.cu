@@ -878,6 +878,192 @@ __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __rest
 }
 
 // ---------------------------------------------------------------------------------------------
+// Hyper-Connection around the MoE (the ffn half of block_prefill / block_incremental,
+// deepseek_v4_graph.cpp:2391-2408: hc_pre, ffn_norm, moe_forward, hc_post).
+//
+// Entry, one CTA per token (deepseek_v4_hc_pre, deepseek_v4_reference.cpp:479-547, and the
+// split, :387-477): the token's m x H state is staged in shared memory as f64; every mixing row
+// r < (2+m)m and the sum of squares is one thread's sequential f64 chain in column order (each
+// product of two f32 values is exact in f64, so fma(a, b, s) rounds like the reference's
+// s + a * b), which makes the mixes bit-identical; the split runs on lanes of warp 0 (lane r owns
+// row r of the combination, then lane c column c; the reference's order within each row and
+// column); the reduced row overwrites copy 0 of the staged state (each column is read by its own
+// thread before it writes it), then the ffn norm runs as rms_norm_kernel does. Only CUDA's double
+// exp can differ from the host's (at most 1 ulp of an f64, rarely visible after the f32 rounding).
+__device__ __forceinline__ float hc_affine(float mix, float scale, float base) {
+    return __fadd_rn(__fmul_rn(mix, scale), base);  // mixes * scale + base, no contraction
+}
+
+__global__ void __launch_bounds__(256) hc_entry_kernel(MoeParams p) {
+    extern __shared__ __align__(16) double hrow[];  // [m x H] as f64
+    __shared__ float mix[16 * 18];
+    __shared__ float cmb[16 * 16];
+    __shared__ float pre_s[16];
+    __shared__ double inv_s, ninv_s;
+    __shared__ float wmax[8];
+    const uint32_t t = blockIdx.x, m = p.hc_m, H = p.H, fw = m * H, mw = (2u + m) * m;
+    const float* xr = p.x + (size_t)t * fw;
+    for (uint32_t c = threadIdx.x * 4u; c < fw; c += blockDim.x * 4u) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + c);
+        *reinterpret_cast<double2*>(hrow + c) = make_double2(v.x, v.y);
+        *reinterpret_cast<double2*>(hrow + c + 2) = make_double2(v.z, v.w);
+    }
+    __syncthreads();
+    // the mixing projection and the RMS of the flattened state (thread mw)
+    double chain[2] = {0.0, 0.0};
+    uint32_t rows[2] = {0xffffffffu, 0xffffffffu};
+    for (uint32_t i = 0, r = threadIdx.x; r <= mw && i < 2u; r += blockDim.x, ++i) {
+        rows[i] = r;
+        double s = 0.0;
+        if (r == mw) {
+            for (uint32_t c = 0; c < fw; c += 4u) {
+                const double2 a = *reinterpret_cast<const double2*>(hrow + c);
+                const double2 b = *reinterpret_cast<const double2*>(hrow + c + 2);
+                s = __fma_rn(a.x, a.x, s);
+                s = __fma_rn(a.y, a.y, s);
+                s = __fma_rn(b.x, b.x, s);
+                s = __fma_rn(b.y, b.y, s);
+            }
+        } else {
+            const float4* wr = reinterpret_cast<const float4*>(p.hc_fn + (size_t)r * fw);
+            uint32_t c = 0;
+            for (; c + 16u <= fw; c += 16u) {
+                float4 w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) w[j] = __ldg(wr + c / 4u + j);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    s = __fma_rn(hrow[c + 4 * j + 0], (double)w[j].x, s);
+                    s = __fma_rn(hrow[c + 4 * j + 1], (double)w[j].y, s);
+                    s = __fma_rn(hrow[c + 4 * j + 2], (double)w[j].z, s);
+                    s = __fma_rn(hrow[c + 4 * j + 3], (double)w[j].w, s);
+                }
+            }
+            for (; c < fw; c += 4u) {
+                const float4 w = __ldg(wr + c / 4u);
+                s = __fma_rn(hrow[c + 0], (double)w.x, s);
+                s = __fma_rn(hrow[c + 1], (double)w.y, s);
+                s = __fma_rn(hrow[c + 2], (double)w.z, s);
+                s = __fma_rn(hrow[c + 3], (double)w.w, s);
+            }
+        }
+        chain[i] = s;
+        if (r == mw) inv_s = 1.0 / sqrt(s / (double)fw + (double)p.norm_eps);
+    }
+    __syncthreads();
+    for (uint32_t i = 0; i < 2u; ++i)
+        if (rows[i] < mw) mix[rows[i]] = (float)(chain[i] * inv_s);
+    __syncthreads();
+    if (threadIdx.x < 32u) {
+        const uint32_t lane = threadIdx.x;
+        const float eps = p.hc_eps;
+        const double deps = (double)eps;
+        if (lane < m) {
+            const float pr = __fadd_rn(sigmoid_dev(hc_affine(mix[lane], p.hc_scale[0], p.hc_base[lane])), eps);
+            const float po = __fmul_rn(2.0f, sigmoid_dev(hc_affine(mix[m + lane], p.hc_scale[1], p.hc_base[m + lane])));
+            pre_s[lane] = pr;
+            p.hc_pre[(size_t)t * m + lane] = pr;
+            p.hc_post[(size_t)t * m + lane] = po;
+            // row `lane`: softmax over its m entries, plus eps
+            float* row = cmb + lane * m;
+            float mx = -INFINITY;
+            for (uint32_t j = 0; j < m; ++j) {
+                const uint32_t at = 2u * m + lane * m + j;
+                row[j] = hc_affine(mix[at], p.hc_scale[2], p.hc_base[at]);
+                mx = fmaxf(mx, row[j]);
+            }
+            double sum = 0.0;
+            for (uint32_t j = 0; j < m; ++j) {
+                row[j] = (float)exp((double)__fsub_rn(row[j], mx));
+                sum = __dadd_rn(sum, (double)row[j]);
+            }
+            for (uint32_t j = 0; j < m; ++j) row[j] = __fadd_rn((float)__ddiv_rn((double)row[j], sum), eps);
+        }
+        __syncwarp();
+        for (uint32_t it = 0; it < p.hc_iters; ++it) {
+            if (it > 0u) {
+                if (lane < m) {  // rows
+                    float* row = cmb + lane * m;
+                    double sum = 0.0;
+                    for (uint32_t j = 0; j < m; ++j) sum = __dadd_rn(sum, (double)row[j]);
+                    const double d = __dadd_rn(sum, deps);
+                    for (uint32_t j = 0; j < m; ++j) row[j] = (float)__ddiv_rn((double)row[j], d);
+                }
+                __syncwarp();
+            }
+            if (lane < m) {  // columns
+                double sum = 0.0;
+                for (uint32_t r = 0; r < m; ++r) sum = __dadd_rn(sum, (double)cmb[r * m + lane]);
+                const double d = __dadd_rn(sum, deps);
+                for (uint32_t r = 0; r < m; ++r) cmb[r * m + lane] = (float)__ddiv_rn((double)cmb[r * m + lane], d);
+            }
+            __syncwarp();
+        }
+        for (uint32_t i = lane; i < m * m; i += 32u) p.hc_comb[(size_t)t * m * m + i] = cmb[i];
+    }
+    __syncthreads();
+    // reduced[c] = sum over copies j of pre[j] * x[j][c] (f64, copy order), kept in copy 0's slot
+    bool bad = false;
+    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+        double s = 0.0;
+        for (uint32_t j = 0; j < m; ++j) s = __fma_rn((double)pre_s[j], hrow[(size_t)j * H + c], s);
+        const float rf = (float)s;
+        bad |= !isfinite(rf);
+        hrow[c] = (double)rf;
+    }
+    if (bad) atomicOr(p.counters + 3, kLayerErrHcNonFinite);
+    __syncthreads();
+    // the ffn norm of the reduced row (rms_norm_kernel's arithmetic)
+    if (threadIdx.x == 0) {
+        double sq = 0.0;
+        for (uint32_t c = 0; c < H; ++c) sq = __fma_rn(hrow[c], hrow[c], sq);
+        ninv_s = 1.0 / sqrt(sq / (double)H + (double)p.norm_eps);
+    }
+    __syncthreads();
+    const double inv = ninv_s;
+    float mxv = 0.f;
+    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+        const float o = (float)(__dmul_rn(__dmul_rn(hrow[c], inv), (double)p.norm_w[c]));
+        p.x_norm[(size_t)t * H + c] = o;
+        if (p.xd) p.xd[(size_t)t * H + c] = (double)o;
+        mxv = fmaxf(mxv, fabsf(o));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mxv = fmaxf(mxv, __shfl_xor_sync(0xffffffffu, mxv, o));
+    if ((threadIdx.x & 31u) == 0) wmax[threadIdx.x >> 5] = mxv;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = 0.f;
+        for (uint32_t i = 0; i < blockDim.x / 32u; ++i) mm = fmaxf(mm, wmax[i]);
+        p.xmax[t] = __float_as_uint(mm);
+    }
+}
+
+// Exit: out[t, d] = f32(post[d] * moe + sum over sources s of comb[s][d] * x[t, s]) in f64 (the
+// reference's order; each product of two f32 values is exact in f64).
+__device__ __forceinline__ void hc_post_store(const MoeParams& p, uint32_t t, uint32_t c4, float4 moe) {
+    const uint32_t m = p.hc_m, H = p.H;
+    const float* post = p.hc_post + (size_t)t * m;
+    const float* comb = p.hc_comb + (size_t)t * m * m;
+    const float* st = p.hc_state + (size_t)t * m * H + c4;
+    for (uint32_t d = 0; d < m; ++d) {
+        const double pd = (double)post[d];
+        double v0 = __dmul_rn(pd, (double)moe.x), v1 = __dmul_rn(pd, (double)moe.y);
+        double v2 = __dmul_rn(pd, (double)moe.z), v3 = __dmul_rn(pd, (double)moe.w);
+        for (uint32_t s = 0; s < m; ++s) {
+            const double cs = (double)comb[s * m + d];
+            const float4 r = *reinterpret_cast<const float4*>(st + (size_t)s * H);
+            v0 = __fma_rn(cs, (double)r.x, v0);
+            v1 = __fma_rn(cs, (double)r.y, v1);
+            v2 = __fma_rn(cs, (double)r.z, v2);
+            v3 = __fma_rn(cs, (double)r.w, v3);
+        }
+        *reinterpret_cast<float4*>(p.out + ((size_t)t * m + d) * H + c4) =
+            make_float4((float)v0, (float)v1, (float)v2, (float)v3);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Combine (deepseek_v4_graph.cpp:2214-2227, :2263-2266; olmoe_runtime.cpp:1282-1285).
 __global__ void __launch_bounds__(256) combine_kernel(MoeParams p) {
     const uint32_t c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4u;
@@ -907,6 +1093,10 @@ __global__ void __launch_bounds__(256) combine_kernel(MoeParams p) {
             acc.y = __fadd_rn(acc.y, v.y);
             acc.z = __fadd_rn(acc.z, v.z);
             acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (p.hc_m) {  // Hyper-Connection exit (deepseek_v4_hc_post, deepseek_v4_reference.cpp:549-610)
+            hc_post_store(p, t, c4, acc);
+            continue;
         }
         if (p.x_residual) {  // residual block: x + MoE(RMSNorm(x)), one f32 addition
             const float4 v = *reinterpret_cast<const float4*>(p.x_residual + (size_t)t * p.H + c4);
@@ -1111,7 +1301,18 @@ cudaError_t launch_moe(const MoeParams& p_in, cudaStream_t s, cudaEvent_t* ev) {
                                                              p.counters + 3);
         e = cudaGetLastError();
     } else {
-        if (p.norm_w) {
+        if (p.hc_m) {
+            // Hyper-Connection entry: split + reduced row + ffn norm, one CTA per token; the
+            // combine writes the m copies back
+            const size_t smem = (size_t)p.hc_m * p.H * 8u;
+            if ((e = set_smem_once(hc_entry_kernel, smem)) != cudaSuccess) return e;
+            MoeParams q = p;
+            q.xd = (p.logits_in || given) ? nullptr : p.xd;
+            hc_entry_kernel<<<p.T, 256, smem, s>>>(q);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            p.hc_state = p.x;
+            p.x = p.x_norm;
+        } else if (p.norm_w) {
             // residual block entry: xn = RMSNorm(x) with each row's max|xn| (the prescale); the
             // layer then runs on xn and the combine adds x back
             if ((e = launch_rms_norm(p.x, p.norm_w, p.T, p.H, p.norm_eps, p.x_norm, p.xmax,
