@@ -301,6 +301,7 @@ def run_ours(args, rank, world, local_rank):
         result["configs"] = run_config_objects(args, dev, stream, flush_l2, rank, world, cfg1=(W, layer))
         result["formats"] = run_format_objects(args, dev, stream)
         result["records"] = run_record_objects(args, dev)
+        result["hyper_connection"] = run_hc_object(args, dev, stream, flush_l2, W, layer)
     layer.destroy()
     for lst in layer.matrices.values():
         for m in lst:
@@ -881,6 +882,62 @@ def run_format_objects(args, dev, stream):
                 dev.release_matrix(m)
     return {"workload": "vlb_matvec_device, 4096 x 4096 matrix, 16 matrices in turn (> L2), 64 calls",
             "timing": "CUDA events on the library stream", "by_type": out}
+
+
+def run_hc_object(args, dev, stream, flush_l2, W, layer):
+    """The config-1 layer with and without the Hyper-Connection entry and exit (m = 4 copies of
+    the hidden state, 20 Sinkhorn iterations, f32 mixing weight [24 x 16384]) at T = 1 and 64:
+    device time per forward (CUDA events, cold L2) and the profiled phases. The entry's mixing
+    projection is 24 sequential f64 chains of m x H = 16,384 steps per token (the reference's
+    summation order, needed for bit-identical mixes): a latency floor that does not shrink with T."""
+    import torch
+
+    H, m = W.spec.hidden, 4
+    rng = np.random.default_rng(12)
+    mw = (2 + m) * m
+    fn = (rng.standard_normal((mw, m * H)) * 0.02).astype(np.float32)
+    scale = (rng.random(3) + 0.5).astype(np.float32)
+    base = (rng.standard_normal(mw) * 0.1).astype(np.float32)
+    norm_w = np.ones(H, np.float32)
+    out = {"workload": "cfg1 layer (IQ2_XXS experts + Q8_0 shared), Hyper-Connection m=4, 20 iterations"}
+
+    def timed(T, rows):
+        x = torch.from_numpy(rng.standard_normal((T, rows, H)).astype(np.float32)).cuda()
+        y = torch.empty_like(x)
+        for _ in range(3):
+            flush_l2()
+            layer.forward_device(x.data_ptr(), T, y.data_ptr(), stream=dev.stream)
+        torch.cuda.synchronize()
+        n = max(5, min(args.steps, 20))
+        tot = 0.0
+        for _ in range(n):
+            flush_l2()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            layer.forward_device(x.data_ptr(), T, y.data_ptr(), stream=dev.stream)
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        layer.status()
+        layer.set_profiling(True)
+        layer.forward_device(x.data_ptr(), T, y.data_ptr(), stream=dev.stream)
+        torch.cuda.synchronize()
+        phases = {k: round(v, 4) for k, v in layer.phase_times().items()}
+        layer.set_profiling(False)
+        return tot / n, phases
+
+    try:
+        for T in (1, 64):
+            plain_ms, plain_ph = timed(T, 1)
+            layer.set_hyper_connection(m, fn, scale, base, norm_w, sinkhorn_iterations=20)
+            hc_ms, hc_ph = timed(T, m)
+            layer.set_hyper_connection(0, None, None, None, None)
+            out[f"T{T}"] = {"ms_plain": round(plain_ms, 4), "ms_hc": round(hc_ms, 4),
+                            "added_ms": round(hc_ms - plain_ms, 4), "phases_plain": plain_ph, "phases_hc": hc_ph}
+    finally:
+        if layer.hc_m:
+            layer.set_hyper_connection(0, None, None, None, None)
+    return out
 
 
 def run_record_objects(args, dev):

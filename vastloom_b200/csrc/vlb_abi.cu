@@ -1063,6 +1063,8 @@ static int check_layer_flags(vlb_handle* h, uint32_t flags) {
     if (flags & 4u) return h->fail(VLB_ERR_INVALID_ARGUMENT, "selected route weights cannot be normalized");
     if (flags & 8u) return h->fail(VLB_ERR_INTERNAL_ERROR, "an expert-kernel pipeline wait ran out of time");
     if (flags & 16u) return h->fail(VLB_ERR_INTERNAL_ERROR, "prefill shared memory is not 1 KB aligned");
+    if (flags & kLayerErrHcTimeout)
+        return h->fail(VLB_ERR_INTERNAL_ERROR, "a Hyper-Connection entry wait ran out of time");
     if (flags & kLayerErrHcNonFinite)
         return h->fail(VLB_ERR_INVALID_FORMAT, "Hyper-Connection reduced output is not finite");
     return VLB_OK;
@@ -1253,7 +1255,7 @@ int vlb_layer_set_hyper_connection(vlb_handle* h, vlb_layer* L, const vlb_hc_des
         if (!(d->norm_epsilon > 0.f && std::isfinite(d->norm_epsilon)) ||
             !(d->hc_epsilon > 0.f && std::isfinite(d->hc_epsilon)))
             return h->fail(VLB_ERR_INVALID_ARGUMENT, "Hyper-Connection epsilons must be finite and positive");
-        if ((size_t)m * H > kRmsMaxWidth)
+        if (!hc_entry_fits(m, H))
             return h->fail(VLB_ERR_UNSUPPORTED, "multiplier x hidden is too large for the Hyper-Connection entry");
         const size_t mw = (size_t)(2 + m) * m, fw = (size_t)m * H;
         for (size_t i = 0; i < mw * fw; ++i)
@@ -1296,13 +1298,22 @@ int vlb_layer_set_hyper_connection(vlb_handle* h, vlb_layer* L, const vlb_hc_des
     const uint32_t m = d->multiplier;
     const size_t mw = (size_t)(2 + m) * m, fw = (size_t)m * H;
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-    const size_t o_fn = 0, o_scale = up(mw * fw * 4), o_base = o_scale + 256, o_pre = o_base + up(mw * 4);
+    const size_t o_fn = 0, o_scale = up(mw * fw * 8), o_base = o_scale + 256, o_pre = o_base + up(mw * 4);
     const size_t o_post = o_pre + up((size_t)T * m * 4), o_comb = o_post + up((size_t)T * m * 4);
     const size_t total = o_comb + up((size_t)T * m * m * 4);
     int st = h->galloc(total, "vlb-hyper-connection", &L->hc_mem);
     if (st != VLB_OK) return st;
     char* b = static_cast<char*>(L->hc_mem);
-    VLB_CUDA(h, cudaMemcpy(b + o_fn, d->mixing_weight, mw * fw * 4, cudaMemcpyHostToDevice));
+    {
+        // the entry's chains read f64 operands (a widening per step would cost more than the step)
+        std::vector<double> fnd;
+        try {
+            fnd.assign(d->mixing_weight, d->mixing_weight + mw * fw);
+        } catch (const std::bad_alloc&) {
+            return h->fail(VLB_ERR_RESOURCE_EXHAUSTED, "unable to stage the mixing weight");
+        }
+        VLB_CUDA(h, cudaMemcpy(b + o_fn, fnd.data(), mw * fw * 8, cudaMemcpyHostToDevice));
+    }
     VLB_CUDA(h, cudaMemcpy(b + o_scale, d->scale, 12, cudaMemcpyHostToDevice));
     VLB_CUDA(h, cudaMemcpy(b + o_base, d->base, mw * 4, cudaMemcpyHostToDevice));
     if (!L->norm_w) {
@@ -1314,7 +1325,7 @@ int vlb_layer_set_hyper_connection(vlb_handle* h, vlb_layer* L, const vlb_hc_des
     MoeParams& p = L->p;
     p.hc_iters = d->sinkhorn_iterations;
     p.hc_eps = d->hc_epsilon;
-    p.hc_fn = reinterpret_cast<const float*>(b + o_fn);
+    p.hc_fn = reinterpret_cast<const double*>(b + o_fn);
     p.hc_scale = reinterpret_cast<const float*>(b + o_scale);
     p.hc_base = reinterpret_cast<const float*>(b + o_base);
     p.hc_pre = reinterpret_cast<float*>(b + o_pre);

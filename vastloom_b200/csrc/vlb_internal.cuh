@@ -72,6 +72,8 @@ constexpr uint32_t kTileRows = 128;
 // Layer error flag (MoeParams::counters[3]) of a Hyper-Connection reduced row that is not finite
 // (deepseek_v4_hc_pre rejects it, deepseek_v4_reference.cpp:544-545).
 constexpr uint32_t kLayerErrHcNonFinite = 32u;
+// ... and of a Hyper-Connection entry whose weight-streaming wait ran out of time.
+constexpr uint32_t kLayerErrHcTimeout = 64u;
 
 // Index of block `blk` of row `row` in the tiled d / body arrays of a matrix with `bpr` blocks per
 // row; consecutive blocks of one row are kTileRows entries apart.
@@ -292,7 +294,7 @@ struct MoeParams {
     uint32_t hc_m;           // 0: no Hyper-Connection
     uint32_t hc_iters;       // Sinkhorn iterations
     float hc_eps;            // the split's epsilon (the mixing RMS uses norm_eps)
-    const float* hc_fn;      // [(2+m)m x mH] mixing weight
+    const double* hc_fn;     // [(2+m)m x mH] mixing weight, widened to f64 at set time
     const float* hc_scale;   // [3]
     const float* hc_base;    // [(2+m)m]
     float* hc_pre;           // [T x m] workspace: the split of the last forward

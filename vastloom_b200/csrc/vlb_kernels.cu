@@ -880,28 +880,154 @@ __global__ void __launch_bounds__(256) token_prescale_kernel(const float* __rest
 // ---------------------------------------------------------------------------------------------
 // Hyper-Connection around the MoE (the ffn half of block_prefill / block_incremental,
 // deepseek_v4_graph.cpp:2391-2408: hc_pre, ffn_norm, moe_forward, hc_post).
-//
+constexpr size_t kHcSmemLimit = 224u * 1024u;  // dynamic shared memory of the entry kernel
+constexpr uint32_t kHcMaxStages = 3;
+constexpr uint32_t kHcSlots = 224;          // chain threads (warps 0-6); warp 7 streams the weight
+constexpr uint32_t kHcProducerWarp = 7;
+constexpr uint64_t kHcWaitNs = 2000000000ull;  // a stage wait that outlasts 2 s is a failure
+
 // Entry, one CTA per token (deepseek_v4_hc_pre, deepseek_v4_reference.cpp:479-547, and the
 // split, :387-477): the token's m x H state is staged in shared memory as f64; every mixing row
 // r < (2+m)m and the sum of squares is one thread's sequential f64 chain in column order (each
 // product of two f32 values is exact in f64, so fma(a, b, s) rounds like the reference's
-// s + a * b), which makes the mixes bit-identical; the split runs on lanes of warp 0 (lane r owns
-// row r of the combination, then lane c column c; the reference's order within each row and
-// column); the reduced row overwrites copy 0 of the staged state (each column is read by its own
-// thread before it writes it), then the ffn norm runs as rms_norm_kernel does. Only CUDA's double
-// exp can differ from the host's (at most 1 ulp of an f64, rarely visible after the f32 rounding).
+// s + a * b), which makes the mixes bit-identical; the mixing weight (kept in f64) streams through
+// a 3-stage shared-memory ring in column chunks (bulk copies by a producer warp, mbarrier
+// hand-offs), so a chain never waits on memory: its floor is the dependent FMA (8.2 cycles on B200,
+// measured); in this kernel a step costs about 19 cycles (a standalone loop of the same shape
+// runs at 10.5-13). The split gives each combination element its own thread, which
+// re-walks its row or column sum in the reference's order; the reduced row overwrites copy 0 of
+// the staged state (each column is read by its own thread before it writes it), then the ffn norm
+// runs as rms_norm_kernel does. Only CUDA's double exp can differ from the host's (at most 1 ulp of
+// an f64, rarely visible after the f32 rounding).
 __device__ __forceinline__ float hc_affine(float mix, float scale, float base) {
     return __fadd_rn(__fmul_rn(mix, scale), base);  // mixes * scale + base, no contraction
 }
 
+// Shared-memory plan of the entry: the token's state widened to f64 [m x H], then a ring of 3
+// (else 2) stages of the f64 mixing weight, each `chunk` columns of all (2+m)m rows (row stride
+// chunk + 2 doubles: 16-byte reads of different rows fall in different bank groups). chunk divides
+// m x H (a multiple of 256). Operands are f64 in shared memory because a float-to-double conversion per
+// chain step costs more issue slots than the chain's FMA latency (about 31 cycles a step against
+// 8 on B200).
+struct HcPlan {
+    uint32_t chunk;   // columns per staged chunk (divides m x H)
+    uint32_t stages;  // ring depth (3, else 2)
+};
+__host__ __device__ inline size_t hc_plan_bytes(uint32_t m, uint32_t H, HcPlan pl) {
+    return (size_t)m * H * 8u + (size_t)pl.stages * (2u + m) * m * (pl.chunk + 2u) * 8u;
+}
+__host__ __device__ inline HcPlan hc_plan(uint32_t m, uint32_t H) {
+    for (uint32_t st = 3; st >= 2u; --st)
+        for (uint32_t c = 128; c >= 16u; c >>= 1)
+            if (hc_plan_bytes(m, H, HcPlan{c, st}) <= kHcSmemLimit) return HcPlan{c, st};
+    return HcPlan{16, 2};
+}
+__host__ __device__ inline size_t hc_entry_smem(uint32_t m, uint32_t H) { return hc_plan_bytes(m, H, hc_plan(m, H)); }
+
+// Bounded wait on an mbarrier phase for the entry (false after the time limit or once another
+// thread of the CTA gave up).
+__device__ __forceinline__ bool hc_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
+    if (tc::mbar_try(bar, parity)) return true;
+    const uint64_t t0 = tc::global_ns();
+    for (uint32_t i = 1; i < (1u << 30); ++i) {
+        if (tc::mbar_try_sleep(bar, parity, 20000u)) return true;
+        if (*abort) return false;
+        if (tc::global_ns() - t0 > kHcWaitNs) return false;
+    }
+    return false;
+}
+
+// The chain warps' walk over the staged chunks (CH: the plan's chunk, a compile-time loop length
+// so that the loads of the next columns are hoisted above the current FMAs).
+template <uint32_t CH>
+__device__ __forceinline__ void hc_consume(const double* stage, const double* hrow, uint64_t* full, uint64_t* empty,
+                                           volatile uint32_t* abort, uint32_t* flags, uint32_t ns, uint32_t nk,
+                                           uint32_t mw, uint32_t r0, uint32_t r1, bool a0, bool a1, uint32_t lane,
+                                           double& s0, double& s1) {
+    constexpr uint32_t cs = CH + 2u;
+    for (uint32_t k = 0; k < nk; ++k) {
+        bool ok = true;
+        if (lane == 0) ok = hc_wait(full + k % ns, (k / ns) & 1u, abort);
+        ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0u;
+        if (!ok) {
+            if (lane == 0) {
+                *abort = 1u;
+                atomicOr(flags, kLayerErrHcTimeout);
+            }
+            return;
+        }
+        const double* buf = stage + (size_t)(k % ns) * mw * cs;
+        const double* xk = hrow + (size_t)k * CH;
+        const double* w0 = r0 < mw ? buf + (size_t)r0 * cs : xk;
+        if (a1) {
+            const double* w1 = r1 < mw ? buf + (size_t)r1 * cs : xk;
+#pragma unroll 16
+            for (uint32_t c = 0; c < CH; c += 2u) {
+                const double2 xv = *reinterpret_cast<const double2*>(xk + c);
+                const double2 u = *reinterpret_cast<const double2*>(w0 + c);
+                const double2 v = *reinterpret_cast<const double2*>(w1 + c);
+                s0 = __fma_rn(xv.x, u.x, s0);
+                s1 = __fma_rn(xv.x, v.x, s1);
+                s0 = __fma_rn(xv.y, u.y, s0);
+                s1 = __fma_rn(xv.y, v.y, s1);
+            }
+        } else if (a0) {
+#pragma unroll 16
+            for (uint32_t c = 0; c < CH; c += 2u) {
+                const double2 xv = *reinterpret_cast<const double2*>(xk + c);
+                const double2 u = *reinterpret_cast<const double2*>(w0 + c);
+                s0 = __fma_rn(xv.x, u.x, s0);
+                s0 = __fma_rn(xv.y, u.y, s0);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(empty + k % ns);
+    }
+}
+
 __global__ void __launch_bounds__(256) hc_entry_kernel(MoeParams p) {
-    extern __shared__ __align__(16) double hrow[];  // [m x H] as f64
+    extern __shared__ __align__(16) double hsm[];
     __shared__ float mix[16 * 18];
     __shared__ float cmb[16 * 16];
     __shared__ float pre_s[16];
     __shared__ double inv_s, ninv_s;
     __shared__ float wmax[8];
+    __shared__ __align__(8) uint64_t full[kHcMaxStages], empty[kHcMaxStages];
+    __shared__ uint32_t abort_s;
     const uint32_t t = blockIdx.x, m = p.hc_m, H = p.H, fw = m * H, mw = (2u + m) * m;
+    const HcPlan pl = hc_plan(m, H);
+    const uint32_t chunk = pl.chunk, ns = pl.stages, cs = chunk + 2u, nk = fw / chunk;
+    double* hrow = hsm;             // [m x H]
+    double* stage = hsm + fw;       // [stages][mw][cs]
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    // chain slots: consumer thread i < 224 walks mixing rows i and i + 224; slot mw walks the sum
+    // of squares, whose "weights" are the state itself (the same instructions, so no divergence).
+    // Warp 7 streams the mixing weight: chunk k of every row into stage k % stages with bulk
+    // copies completing on full[k % stages]; the chain warps release a stage on empty[].
+    const uint32_t r0 = threadIdx.x, r1 = threadIdx.x + kHcSlots;
+    const uint32_t chain_warps = min(kHcSlots / 32u, (mw + 32u) / 32u);
+    const bool consumer = warp < chain_warps, producer = warp == kHcProducerWarp;
+    const bool a0 = consumer && r0 <= mw, a1 = consumer && r1 <= mw;
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < ns; ++i) {
+            tc::mbar_init(full + i, 1);
+            tc::mbar_init(empty + i, chain_warps);
+        }
+        abort_s = 0;
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+    const uint32_t stage_bytes = mw * chunk * 8u;
+    auto issue = [&](uint32_t k) {  // the whole producer warp
+        double* dst = stage + (size_t)(k % ns) * mw * cs;
+        if (lane == 0) tc::mbar_arrive_expect_tx(full + k % ns, stage_bytes);
+        __syncwarp();
+        for (uint32_t r = lane; r < mw; r += 32u)
+            tc::bulk_load(tc::smem_u32(dst + (size_t)r * cs), p.hc_fn + (size_t)r * fw + (size_t)k * chunk,
+                          chunk * 8u, full + k % ns);
+    };
+    if (producer)
+        for (uint32_t k = 0; k < ns && k < nk; ++k) issue(k);
     const float* xr = p.x + (size_t)t * fw;
     for (uint32_t c = threadIdx.x * 4u; c < fw; c += blockDim.x * 4u) {
         const float4 v = *reinterpret_cast<const float4*>(xr + c);
@@ -909,97 +1035,112 @@ __global__ void __launch_bounds__(256) hc_entry_kernel(MoeParams p) {
         *reinterpret_cast<double2*>(hrow + c + 2) = make_double2(v.z, v.w);
     }
     __syncthreads();
-    // the mixing projection and the RMS of the flattened state (thread mw)
-    double chain[2] = {0.0, 0.0};
-    uint32_t rows[2] = {0xffffffffu, 0xffffffffu};
-    for (uint32_t i = 0, r = threadIdx.x; r <= mw && i < 2u; r += blockDim.x, ++i) {
-        rows[i] = r;
-        double s = 0.0;
-        if (r == mw) {
-            for (uint32_t c = 0; c < fw; c += 4u) {
-                const double2 a = *reinterpret_cast<const double2*>(hrow + c);
-                const double2 b = *reinterpret_cast<const double2*>(hrow + c + 2);
-                s = __fma_rn(a.x, a.x, s);
-                s = __fma_rn(a.y, a.y, s);
-                s = __fma_rn(b.x, b.x, s);
-                s = __fma_rn(b.y, b.y, s);
-            }
-        } else {
-            const float4* wr = reinterpret_cast<const float4*>(p.hc_fn + (size_t)r * fw);
-            uint32_t c = 0;
-            for (; c + 16u <= fw; c += 16u) {
-                float4 w[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) w[j] = __ldg(wr + c / 4u + j);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    s = __fma_rn(hrow[c + 4 * j + 0], (double)w[j].x, s);
-                    s = __fma_rn(hrow[c + 4 * j + 1], (double)w[j].y, s);
-                    s = __fma_rn(hrow[c + 4 * j + 2], (double)w[j].z, s);
-                    s = __fma_rn(hrow[c + 4 * j + 3], (double)w[j].w, s);
+    double s0 = 0.0, s1 = 0.0;
+    if (producer) {
+        uint32_t issued = min(ns, nk);
+        for (uint32_t k = ns; k < nk; ++k) {
+            bool ok = true;
+            if (lane == 0) ok = hc_wait(empty + k % ns, ((k / ns) - 1u) & 1u, &abort_s);
+            ok = __shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) != 0u;
+            if (!ok) {
+                if (lane == 0) {
+                    abort_s = 1u;
+                    atomicOr(p.counters + 3, kLayerErrHcTimeout);
                 }
+                break;
             }
-            for (; c < fw; c += 4u) {
-                const float4 w = __ldg(wr + c / 4u);
-                s = __fma_rn(hrow[c + 0], (double)w.x, s);
-                s = __fma_rn(hrow[c + 1], (double)w.y, s);
-                s = __fma_rn(hrow[c + 2], (double)w.z, s);
-                s = __fma_rn(hrow[c + 3], (double)w.w, s);
-            }
+            issue(k);
+            issued = k + 1u;
         }
-        chain[i] = s;
-        if (r == mw) inv_s = 1.0 / sqrt(s / (double)fw + (double)p.norm_eps);
+        // no copy may still be landing when the CTA leaves: wait (bounded) for every issued chunk
+        if (lane == 0)
+            for (uint32_t k = issued > ns ? issued - ns : 0u; k < issued; ++k)
+                if (!hc_wait(full + k % ns, (k / ns) & 1u, &abort_s)) {
+                    atomicOr(p.counters + 3, kLayerErrHcTimeout);
+                    break;
+                }
+    } else if (consumer) {
+        switch (chunk) {
+            case 128: hc_consume<128>(stage, hrow, full, empty, &abort_s, p.counters + 3, ns, nk, mw, r0, r1, a0, a1, lane, s0, s1); break;
+            case 64: hc_consume<64>(stage, hrow, full, empty, &abort_s, p.counters + 3, ns, nk, mw, r0, r1, a0, a1, lane, s0, s1); break;
+            case 32: hc_consume<32>(stage, hrow, full, empty, &abort_s, p.counters + 3, ns, nk, mw, r0, r1, a0, a1, lane, s0, s1); break;
+            default: hc_consume<16>(stage, hrow, full, empty, &abort_s, p.counters + 3, ns, nk, mw, r0, r1, a0, a1, lane, s0, s1); break;
+        }
     }
+    __syncthreads();
+    if (a0 && r0 == mw) inv_s = 1.0 / sqrt(s0 / (double)fw + (double)p.norm_eps);
+    if (a1 && r1 == mw) inv_s = 1.0 / sqrt(s1 / (double)fw + (double)p.norm_eps);
+    double chain[2] = {s0, s1};
+    uint32_t rows[2] = {a0 ? r0 : 0xffffffffu, a1 ? r1 : 0xffffffffu};
     __syncthreads();
     for (uint32_t i = 0; i < 2u; ++i)
         if (rows[i] < mw) mix[rows[i]] = (float)(chain[i] * inv_s);
     __syncthreads();
-    if (threadIdx.x < 32u) {
-        const uint32_t lane = threadIdx.x;
-        const float eps = p.hc_eps;
-        const double deps = (double)eps;
-        if (lane < m) {
-            const float pr = __fadd_rn(sigmoid_dev(hc_affine(mix[lane], p.hc_scale[0], p.hc_base[lane])), eps);
-            const float po = __fmul_rn(2.0f, sigmoid_dev(hc_affine(mix[m + lane], p.hc_scale[1], p.hc_base[m + lane])));
-            pre_s[lane] = pr;
-            p.hc_pre[(size_t)t * m + lane] = pr;
-            p.hc_post[(size_t)t * m + lane] = po;
-            // row `lane`: softmax over its m entries, plus eps
-            float* row = cmb + lane * m;
-            float mx = -INFINITY;
-            for (uint32_t j = 0; j < m; ++j) {
-                const uint32_t at = 2u * m + lane * m + j;
-                row[j] = hc_affine(mix[at], p.hc_scale[2], p.hc_base[at]);
-                mx = fmaxf(mx, row[j]);
+    // the split: thread i < m * m owns combination element (i / m, i % m); every row or column
+    // sum is re-walked by each of its threads in the reference's order, so all of them see the
+    // same value and the m * m divisions of a pass run at once. m * m <= 32 stays in warp 0.
+    {
+        const bool in_warp = m * m <= 32u;
+        if (!in_warp || threadIdx.x < 32u) {
+            const uint32_t i = threadIdx.x, r = i / m, j = i % m;
+            const bool own = i < m * m;
+            const float eps = p.hc_eps;
+            const double deps = (double)eps;
+            auto sync = [&] {
+                if (in_warp) __syncwarp();
+                else __syncthreads();
+            };
+            if (i < m) {
+                const float pr = __fadd_rn(sigmoid_dev(hc_affine(mix[i], p.hc_scale[0], p.hc_base[i])), eps);
+                const float po = __fmul_rn(2.0f, sigmoid_dev(hc_affine(mix[m + i], p.hc_scale[1], p.hc_base[m + i])));
+                pre_s[i] = pr;
+                p.hc_pre[(size_t)t * m + i] = pr;
+                p.hc_post[(size_t)t * m + i] = po;
             }
-            double sum = 0.0;
-            for (uint32_t j = 0; j < m; ++j) {
-                row[j] = (float)exp((double)__fsub_rn(row[j], mx));
-                sum = __dadd_rn(sum, (double)row[j]);
-            }
-            for (uint32_t j = 0; j < m; ++j) row[j] = __fadd_rn((float)__ddiv_rn((double)row[j], sum), eps);
-        }
-        __syncwarp();
-        for (uint32_t it = 0; it < p.hc_iters; ++it) {
-            if (it > 0u) {
-                if (lane < m) {  // rows
-                    float* row = cmb + lane * m;
-                    double sum = 0.0;
-                    for (uint32_t j = 0; j < m; ++j) sum = __dadd_rn(sum, (double)row[j]);
-                    const double d = __dadd_rn(sum, deps);
-                    for (uint32_t j = 0; j < m; ++j) row[j] = (float)__ddiv_rn((double)row[j], d);
+            // row softmax plus eps (the row's maximum in column order, as std::max keeps it)
+            float v = 0.f;
+            if (own) {
+                float mx = -INFINITY;
+                for (uint32_t q = 0; q < m; ++q) {
+                    const uint32_t at = 2u * m + r * m + q;
+                    const float a = hc_affine(mix[at], p.hc_scale[2], p.hc_base[at]);
+                    mx = mx < a ? a : mx;
                 }
-                __syncwarp();
+                const uint32_t at = 2u * m + r * m + j;
+                v = (float)exp((double)__fsub_rn(hc_affine(mix[at], p.hc_scale[2], p.hc_base[at]), mx));
+                cmb[i] = v;
             }
-            if (lane < m) {  // columns
+            sync();
+            if (own) {
                 double sum = 0.0;
-                for (uint32_t r = 0; r < m; ++r) sum = __dadd_rn(sum, (double)cmb[r * m + lane]);
-                const double d = __dadd_rn(sum, deps);
-                for (uint32_t r = 0; r < m; ++r) cmb[r * m + lane] = (float)__ddiv_rn((double)cmb[r * m + lane], d);
+                for (uint32_t q = 0; q < m; ++q) sum = __dadd_rn(sum, (double)cmb[r * m + q]);
+                v = __fadd_rn((float)__ddiv_rn((double)v, sum), eps);
             }
-            __syncwarp();
+            sync();
+            if (own) cmb[i] = v;
+            sync();
+            for (uint32_t it = 0; it < p.hc_iters; ++it) {
+                if (it > 0u) {  // rows
+                    if (own) {
+                        double sum = 0.0;
+                        for (uint32_t q = 0; q < m; ++q) sum = __dadd_rn(sum, (double)cmb[r * m + q]);
+                        v = (float)__ddiv_rn((double)v, __dadd_rn(sum, deps));
+                    }
+                    sync();
+                    if (own) cmb[i] = v;
+                    sync();
+                }
+                if (own) {  // columns
+                    double sum = 0.0;
+                    for (uint32_t q = 0; q < m; ++q) sum = __dadd_rn(sum, (double)cmb[q * m + j]);
+                    v = (float)__ddiv_rn((double)v, __dadd_rn(sum, deps));
+                }
+                sync();
+                if (own) cmb[i] = v;
+                sync();
+            }
+            if (own) p.hc_comb[(size_t)t * m * m + i] = v;
         }
-        for (uint32_t i = lane; i < m * m; i += 32u) p.hc_comb[(size_t)t * m * m + i] = cmb[i];
     }
     __syncthreads();
     // reduced[c] = sum over copies j of pre[j] * x[j][c] (f64, copy order), kept in copy 0's slot
@@ -1016,7 +1157,12 @@ __global__ void __launch_bounds__(256) hc_entry_kernel(MoeParams p) {
     // the ffn norm of the reduced row (rms_norm_kernel's arithmetic)
     if (threadIdx.x == 0) {
         double sq = 0.0;
-        for (uint32_t c = 0; c < H; ++c) sq = __fma_rn(hrow[c], hrow[c], sq);
+#pragma unroll 8
+        for (uint32_t c = 0; c < H; c += 2u) {
+            const double2 v = *reinterpret_cast<const double2*>(hrow + c);
+            sq = __fma_rn(v.x, v.x, sq);
+            sq = __fma_rn(v.y, v.y, sq);
+        }
         ninv_s = 1.0 / sqrt(sq / (double)H + (double)p.norm_eps);
     }
     __syncthreads();
@@ -1304,7 +1450,7 @@ cudaError_t launch_moe(const MoeParams& p_in, cudaStream_t s, cudaEvent_t* ev) {
         if (p.hc_m) {
             // Hyper-Connection entry: split + reduced row + ffn norm, one CTA per token; the
             // combine writes the m copies back
-            const size_t smem = (size_t)p.hc_m * p.H * 8u;
+            const size_t smem = hc_entry_smem(p.hc_m, p.H);
             if ((e = set_smem_once(hc_entry_kernel, smem)) != cudaSuccess) return e;
             MoeParams q = p;
             q.xd = (p.logits_in || given) ? nullptr : p.xd;
@@ -1412,6 +1558,11 @@ cudaError_t launch_stable_sort(const MoeParams& p, cudaStream_t s) {
     if ((e = set_smem_once(dispatch_scatter_kernel, ssmem)) != cudaSuccess) return e;
     dispatch_scatter_kernel<<<chunks, kDispatchThreads, ssmem, s>>>(p, p.disp_counts);
     return cudaGetLastError();
+}
+
+bool hc_entry_fits(uint32_t m, uint32_t H) {
+    if (m == 0 || m > 16 || H == 0 || ((size_t)m * H) % 256u) return false;
+    return hc_entry_smem(m, H) <= kHcSmemLimit;
 }
 
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,

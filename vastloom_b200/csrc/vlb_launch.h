@@ -68,6 +68,8 @@ cudaError_t launch_ep_combine(const float* y, const uint32_t* elem_row, uint32_t
 // width % 4 == 0 and
 // width <= kRmsMaxWidth (the row is staged in shared memory).
 constexpr uint32_t kRmsMaxWidth = 24576;  // the row staged as f64 in shared memory
+// Whether the Hyper-Connection entry kernel's shared-memory plan fits m copies of a hidden row.
+bool hc_entry_fits(uint32_t m, uint32_t H);
 cudaError_t launch_rms_norm(const float* x, const float* w, uint32_t rows, uint32_t width,
                             float eps, float* out, uint32_t* xmax, double* out_d, cudaStream_t s);
 
