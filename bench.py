@@ -419,6 +419,8 @@ def run_ep(args, dev, rank, world, local_rank):
                   "against": "the same tokens through one GPU holding all experts, exact decode path"},
     }
     assert check_max <= 4e-3, f"expert-parallel output differs from the single-GPU layer: {check_max}"
+    if native and world > 1:
+        res["nvlink_all_to_all"] = all_to_all_reference(ncomm, lib_stream, comm, xd, world, T, spec, res)
     if native:
         layer.close()
         ncomm.close()
@@ -427,6 +429,45 @@ def run_ep(args, dev, rank, world, local_rank):
     if created_group:
         torch.distributed.destroy_process_group()
     return res
+
+
+def all_to_all_reference(ncomm, stream, comm, like, world, T, spec, res):
+    """The exchange's own roofline: a plain NCCL all-to-all on the same communicator and stream,
+    equal splits, at the step's two sizes (dispatch: T*k fp16 rows of H; return: the same rows'
+    fp16 results), CUDA events around 5 calls after 2, max over ranks. algbw = bytes a rank sends
+    / time; busbw = algbw * (N-1)/N (the bytes that cross NVLink), against the pool's measured
+    770 GB/s per direction peer copy. The step's dispatch and return phases are then expressed
+    as a fraction of this reference time."""
+    import torch
+
+    out = {"timing": "CUDA events on the library stream, 5 calls after 2, max over ranks",
+           "peer_copy_gbs_reference": 770.0}
+    sizes = {"dispatch": T * spec.top_k * spec.hidden * 2, "return": T * spec.top_k * spec.hidden * 2}
+    for name, total in sizes.items():
+        per = (total // world) // 256 * 256
+        send = torch.empty(per * world, dtype=torch.uint8, device="cuda")
+        recv = torch.empty(per * world, dtype=torch.uint8, device="cuda")
+        for _ in range(2):
+            ncomm.all_to_all(send.data_ptr(), [per] * world, recv.data_ptr(), [per] * world, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            ncomm.all_to_all(send.data_ptr(), [per] * world, recv.data_ptr(), [per] * world, stream=stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = comm.max_over_ranks(e0.elapsed_time(e1) / 5, like)
+        alg = per * world / (ms / 1000.0) / 1e9
+        bus = alg * (world - 1) / world
+        entry = {"bytes_per_rank": per * world, "ms": round(ms, 4), "algbw_gbs": round(alg, 1),
+                 "busbw_gbs": round(bus, 1), "busbw_frac_of_peer_copy": round(bus / 770.0, 4)}
+        phase = res["phases_ms_rank0"].get(f"{name}_s")
+        if phase:
+            entry["step_phase_ms"] = phase
+            entry["step_phase_over_reference"] = round(phase / ms, 3)
+        out[name] = entry
+        del send, recv
+    return out
 
 
 def ep_parity_check(dev, W, x_host, logits_host, out_ep):

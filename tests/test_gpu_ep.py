@@ -140,8 +140,12 @@ def test_gpu_ep_two_ranks_match_single_gpu_layer(balanced):
 def _leave_main(rank, world, port, q):
     """Rank 1 runs one step with rank 0 and then leaves (between steps, nothing of it in flight);
     rank 0's next step must end with the library's bounded wait (EpExchangeError "counts") and
-    every later step must be refused. NVLS is off, so no NVLink multicast object is involved."""
+    every later step must be refused. NVLS is off, so no NVLink multicast object is involved, and
+    the rows travel over NCCL (VLB_EP_EXCHANGE=nccl): no rank holds a mapping of the departing
+    rank's memory. (With peer stores the step's first collective, the counts exchange, fails the
+    same way before any store.)"""
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["VLB_EP_EXCHANGE"] = "nccl"
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)

@@ -10,7 +10,15 @@
 //   -> pack fp16 results -> results all-to-all -> combine in slot order.
 //
 // The exchanges are grouped ncclSend / ncclRecv on the caller's stream, ordered with the kernels
-// without host synchronisation except where sizes are needed. NCCL is loaded at run time (dlopen
+// without host synchronisation except where sizes are needed. With two or more ranks whose GPUs
+// reach each other (CUDA IPC over NVLink), the two large payloads - the dispatched fp16 rows and
+// the fp16 results coming back - move instead by peer stores: every rank maps its peers' receive
+// buffers at layer creation and one copy kernel writes each peer's rows straight into place (the
+// full count matrix, exchanged first, gives every rank its offsets in every peer's buffer). The
+// small meta / scale exchange that follows on the same stream is the fence: a receiver's NCCL
+// receive completes only after the sender's NCCL call ran, which is after its copy kernel (whose
+// stores end with a system-scope fence). The next step's counts exchange orders the reuse of the
+// buffers the same way. VLB_EP_EXCHANGE=nccl keeps everything on NCCL. NCCL is loaded at run time (dlopen
 // of $VLB_NCCL_LIBRARY, else libnccl.so.2, reusing the copy the process already has), so the
 // library itself loads and runs its other entry points without NCCL.
 //
@@ -212,9 +220,18 @@ struct vlb_ep_layer {
     uint16_t* group_yh = nullptr;
     float* group_ys = nullptr;
     std::vector<void*> group_owned;
+    // peer mode: this rank's receive buffer for dispatched rows (fixed, the worst case of every
+    // rank sending it all its pairs) and every rank's receive buffers mapped here (IPC)
+    bool peer = false;
+    uint16_t* peer_rows = nullptr;
+    uint64_t peer_rows_cap = 0;          // rows of peer_rows
+    std::vector<uint16_t*> rows_at;      // [W] each rank's dispatch receive buffer
+    std::vector<uint16_t*> back_at;      // [W] each rank's results receive buffer (back_yh)
+    std::vector<uint64_t> rows_cap_at, back_cap_at;
+    std::vector<void*> ipc_opened;
     // pinned host words
     uint32_t* offsets_host = nullptr;
-    uint64_t* counts_host = nullptr;
+    uint64_t* counts_host = nullptr;     // [W]: send counts, [W]: received counts, [W x W]: matrix
     cudaEvent_t sync_ev = nullptr;
     cudaEvent_t phase[6] = {};
     bool have_phases = false;
@@ -246,7 +263,8 @@ struct vlb_ep_layer {
         int st = vlb_layer_create(h, &d, &group);
         if (st != VLB_OK) return handle_fail(h, st);
         const size_t hr = (size_t)cap * H;
-        if ((st = alloc(hr * 2, "vlb-ep-group-rows", (void**)&group_rows, group_owned)) ||
+        if (peer) group_rows = peer_rows;  // fixed: its peers write into it
+        if ((!peer && (st = alloc(hr * 2, "vlb-ep-group-rows", (void**)&group_rows, group_owned))) ||
             (st = alloc((size_t)cap * 12, "vlb-ep-group-meta", (void**)&group_meta, group_owned)) ||
             (st = alloc(hr * 4, "vlb-ep-group-y", (void**)&group_y, group_owned)) ||
             (st = alloc(hr * 2, "vlb-ep-group-yh", (void**)&group_yh, group_owned)) ||
@@ -256,6 +274,8 @@ struct vlb_ep_layer {
         return VLB_OK;
     }
     void release() {
+        for (void* q : ipc_opened) cudaIpcCloseMemHandle(q);
+        ipc_opened.clear();
         if (group) vlb_layer_destroy(h, group);
         group = nullptr;
         free_list(group_owned);
@@ -292,6 +312,157 @@ int exchange_rows(vlb_ep_comm* c, const void* send, const uint64_t* send_count, 
     if (r != ncclSuccess && r != ncclInProgress) return c->abort_with(VLB_ERR_IO_ERROR, std::string(what) + ": " + nccl_msg("ncclSend/ncclRecv", r));
     if (e != ncclSuccess && e != ncclInProgress) return c->abort_with(VLB_ERR_IO_ERROR, std::string(what) + ": " + nccl_msg("ncclGroupEnd", e));
     return c->settle(what);
+}
+
+// ---- peer-store exchange --------------------------------------------------------------------
+constexpr uint32_t kPeerMaxRanks = 16;
+struct PeerSegs {
+    const uint4* src[kPeerMaxRanks];
+    uint4* dst[kPeerMaxRanks];
+    uint64_t n16[kPeerMaxRanks];
+    uint32_t count;
+};
+
+// Copies every segment (local source, a peer's mapped memory or this GPU's as destination), all
+// CTAs striding over one segment after another, four 16-byte loads in flight per thread; the
+// stores are made visible system-wide before the kernel ends.
+__global__ void __launch_bounds__(256) peer_copy_kernel(PeerSegs g) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint32_t sgi = 0; sgi < g.count; ++sgi) {
+        const uint4* __restrict__ src = g.src[sgi];
+        uint4* dst = g.dst[sgi];
+        const uint64_t n = g.n16[sgi];
+        uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        for (; i + 3u * stride < n; i += 4u * stride) {
+            const uint4 a = src[i], b = src[i + stride], c = src[i + 2u * stride], d = src[i + 3u * stride];
+            dst[i] = a;
+            dst[i + stride] = b;
+            dst[i + 2u * stride] = c;
+            dst[i + 3u * stride] = d;
+        }
+        for (; i < n; i += stride) dst[i] = src[i];
+    }
+    __threadfence_system();
+}
+
+int launch_peer_copy(const PeerSegs& g, cudaStream_t s) {
+    bool any = false;
+    for (uint32_t i = 0; i < g.count; ++i) any = any || g.n16[i] != 0;
+    if (!any) return VLB_OK;
+    int sms = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    peer_copy_kernel<<<(unsigned)sms * 4u, 256, 0, s>>>(g);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VLB_OK : fail(VLB_ERR_IO_ERROR, cuda_msg("peer_copy_kernel", e));
+}
+
+// Maps every peer's receive buffers (CUDA IPC handles exchanged over the communicator) and agrees
+// with every peer on using them: peer mode only if every rank mapped every peer. Collective: every
+// rank of the communicator calls it at layer creation.
+int enable_peer_exchange(vlb_ep_layer* l) {
+    vlb_ep_comm* c = l->c;
+    const uint32_t W = (uint32_t)c->world, me = (uint32_t)c->rank;
+    const char* env = std::getenv("VLB_EP_EXCHANGE");
+    bool want = W > 1 && W <= kPeerMaxRanks && !(env && std::string(env) == "nccl");
+    // this rank's record: two IPC handles, the two capacities, and whether it wants peer mode
+    struct Rec {
+        cudaIpcMemHandle_t rows, back;
+        uint64_t rows_cap, back_cap;
+        uint64_t ok;
+    };
+    static_assert(sizeof(Rec) % 8 == 0, "record size");
+    Rec mine{};
+    const uint64_t n = (uint64_t)l->max_tokens * l->k;
+    if (want) {
+        l->peer_rows_cap = (uint64_t)W * n + l->max_tokens;
+        void* p = nullptr;
+        if (l->alloc(l->peer_rows_cap * l->H * 2, "vlb-ep-peer-rows", &p, l->owned) != VLB_OK) {
+            want = false;
+            l->peer_rows_cap = 0;
+        } else {
+            l->peer_rows = static_cast<uint16_t*>(p);
+        }
+    }
+    if (want && (cudaIpcGetMemHandle(&mine.rows, l->peer_rows) != cudaSuccess ||
+                 cudaIpcGetMemHandle(&mine.back, l->back_yh) != cudaSuccess)) {
+        (void)cudaGetLastError();
+        want = false;
+    }
+    mine.rows_cap = l->peer_rows_cap;
+    mine.back_cap = n;
+    mine.ok = want ? 1u : 0u;
+    // everyone's record to everyone (the same record to every peer)
+    std::vector<Rec> all(W), out(W, mine);
+    void* dev_buf = nullptr;
+    int st = l->alloc(sizeof(Rec) * W * 2, "vlb-ep-ipc", &dev_buf, l->owned);
+    if (st != VLB_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(vlb_stream(l->h));
+    char* d = static_cast<char*>(dev_buf);
+    cudaError_t ce = cudaMemcpyAsync(d, out.data(), sizeof(Rec) * W, cudaMemcpyHostToDevice, s);
+    if (ce != cudaSuccess) return fail(VLB_ERR_IO_ERROR, cuda_msg("cudaMemcpyAsync(ipc records)", ce));
+    std::vector<uint64_t> ones(W, sizeof(Rec));
+    if ((st = exchange_rows(c, d, ones.data(), d + sizeof(Rec) * W, ones.data(), 1, s, "setup")) != VLB_OK) return st;
+    ce = cudaMemcpyAsync(all.data(), d + sizeof(Rec) * W, sizeof(Rec) * W, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaEventRecord(l->sync_ev, s);
+    if (ce != cudaSuccess) return fail(VLB_ERR_IO_ERROR, cuda_msg("ipc records", ce));
+    if ((st = c->wait(l->sync_ev, "setup")) != VLB_OK) return st;
+    bool every = true;
+    for (uint32_t q = 0; q < W; ++q) every = every && all[q].ok;
+    l->rows_at.assign(W, nullptr);
+    l->back_at.assign(W, nullptr);
+    l->rows_cap_at.assign(W, 0);
+    l->back_cap_at.assign(W, 0);
+    uint64_t mapped = 1;
+    for (uint32_t q = 0; q < W && every; ++q) {
+        l->rows_cap_at[q] = all[q].rows_cap;
+        l->back_cap_at[q] = all[q].back_cap;
+        if (q == me) {
+            l->rows_at[q] = l->peer_rows;
+            l->back_at[q] = l->back_yh;
+            continue;
+        }
+        void* pr = nullptr;
+        void* pb = nullptr;
+        if (cudaIpcOpenMemHandle(&pr, all[q].rows, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            (void)cudaGetLastError();
+            mapped = 0;
+            break;
+        }
+        l->ipc_opened.push_back(pr);
+        if (cudaIpcOpenMemHandle(&pb, all[q].back, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            (void)cudaGetLastError();
+            mapped = 0;
+            break;
+        }
+        l->ipc_opened.push_back(pb);
+        l->rows_at[q] = static_cast<uint16_t*>(pr);
+        l->back_at[q] = static_cast<uint16_t*>(pb);
+    }
+    if (!every) mapped = 0;
+    // agree: peer mode only if every rank mapped every peer
+    std::vector<uint64_t> flags(W, mapped), got(W, 0);
+    uint64_t* fd = reinterpret_cast<uint64_t*>(d);
+    ce = cudaMemcpyAsync(fd, flags.data(), 8 * W, cudaMemcpyHostToDevice, s);
+    if (ce != cudaSuccess) return fail(VLB_ERR_IO_ERROR, cuda_msg("cudaMemcpyAsync(peer flags)", ce));
+    std::vector<uint64_t> eights(W, 8);
+    if ((st = exchange_rows(c, fd, eights.data(), fd + W, eights.data(), 1, s, "setup")) != VLB_OK) return st;
+    ce = cudaMemcpyAsync(got.data(), fd + W, 8 * W, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaEventRecord(l->sync_ev, s);
+    if (ce != cudaSuccess) return fail(VLB_ERR_IO_ERROR, cuda_msg("peer flags", ce));
+    if ((st = c->wait(l->sync_ev, "setup")) != VLB_OK) return st;
+    bool all_mapped = true;
+    for (uint32_t q = 0; q < W; ++q) all_mapped = all_mapped && got[q] == 1;
+    if (!all_mapped) {
+        for (void* q : l->ipc_opened) cudaIpcCloseMemHandle(q);
+        l->ipc_opened.clear();
+        l->rows_at.clear();
+        l->back_at.clear();
+        return VLB_OK;  // NCCL carries the rows
+    }
+    l->peer = true;
+    return VLB_OK;
 }
 
 int layer_refuse(vlb_ep_layer* l) {
@@ -465,7 +636,7 @@ int vlb_ep_layer_create(vlb_handle* h, vlb_ep_comm* c, const vlb_ep_layer_desc* 
         (st = l->alloc(n * 4, "vlb-ep-elem-row", (void**)&l->elem_row, o)) ||
         (st = l->alloc(T * Hs * 2, "vlb-ep-own-rows", (void**)&l->own_rows, o)) ||
         (st = l->alloc(T * 12, "vlb-ep-own-meta", (void**)&l->own_meta, o)) ||
-        (st = l->alloc((size_t)W * 16, "vlb-ep-counts", (void**)&l->counts_dev, o)) ||
+        (st = l->alloc((size_t)W * W * 16 + (size_t)W * 16, "vlb-ep-counts", (void**)&l->counts_dev, o)) ||
         (st = l->alloc(n * Hs * 2, "vlb-ep-back-rows", (void**)&l->back_yh, o)) ||
         (st = l->alloc(n * 4, "vlb-ep-back-scales", (void**)&l->back_ys, o))) {
         l->release();
@@ -500,13 +671,18 @@ int vlb_ep_layer_create(vlb_handle* h, vlb_ep_comm* c, const vlb_ep_layer_desc* 
         }
     }
     cudaError_t ce = cudaHostAlloc((void**)&l->offsets_host, ((size_t)l->E + 1) * 4, cudaHostAllocDefault);
-    if (ce == cudaSuccess) ce = cudaHostAlloc((void**)&l->counts_host, (size_t)W * 16, cudaHostAllocDefault);
+    if (ce == cudaSuccess) ce = cudaHostAlloc((void**)&l->counts_host, (size_t)W * 16 + (size_t)W * W * 8, cudaHostAllocDefault);
     if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&l->sync_ev, cudaEventDisableTiming);
     for (int i = 0; i < 6 && ce == cudaSuccess; ++i) ce = cudaEventCreate(&l->phase[i]);
     if (ce != cudaSuccess) {
         l->release();
         delete l;
         return fail(VLB_ERR_IO_ERROR, cuda_msg("expert-parallel host buffers", ce));
+    }
+    if ((st = enable_peer_exchange(l)) != VLB_OK) {
+        l->release();
+        delete l;
+        return st;
     }
     // receive side sized for the balanced load with headroom; a heavier step regrows it
     st = l->reserve((uint32_t)((n + W - 1) / W + T));
@@ -564,30 +740,73 @@ int vlb_ep_forward_device(vlb_handle* h, vlb_ep_layer* l, const float* x, const 
     uint64_t* recv_count = l->counts_host + W;
     for (uint32_t p = 0; p < W; ++p)
         send_count[p] = (uint64_t)l->offsets_host[(p + 1) * epr] - l->offsets_host[p * epr];
-    // counts: one u64 to and from every rank
-    cudaError_t ce = cudaMemcpyAsync(l->counts_dev, send_count, (size_t)W * 8, cudaMemcpyHostToDevice, s);
+    // counts: one u64 to and from every rank; in peer mode every rank's whole send-count vector
+    // to every rank (matrix[q][p] = rows rank q sends rank p), which gives each rank its offsets
+    // in every peer's receive buffers
+    uint64_t* matrix = l->counts_host + 2 * W;
+    cudaError_t ce = cudaSuccess;
+    if (l->peer) {
+        for (uint32_t p = 0; p < W; ++p) std::memcpy(matrix + (size_t)p * W, send_count, (size_t)W * 8);
+        ce = cudaMemcpyAsync(l->counts_dev, matrix, (size_t)W * W * 8, cudaMemcpyHostToDevice, s);
+    } else {
+        ce = cudaMemcpyAsync(l->counts_dev, send_count, (size_t)W * 8, cudaMemcpyHostToDevice, s);
+    }
     if (ce != cudaSuccess) return fail(VLB_ERR_IO_ERROR, cuda_msg("cudaMemcpyAsync(counts)", ce));
     {
-        std::vector<uint64_t> ones(W, 8);
-        st = exchange_rows(c, l->counts_dev, ones.data(), l->counts_dev + W, ones.data(), 1, s, "counts");
-    }
-    if (st == VLB_OK) {
-        ce = cudaMemcpyAsync(recv_count, l->counts_dev + W, (size_t)W * 8, cudaMemcpyDeviceToHost, s);
-        if (ce == cudaSuccess) ce = cudaEventRecord(l->sync_ev, s);
-        st = ce != cudaSuccess ? fail(VLB_ERR_IO_ERROR, cuda_msg("cudaMemcpyAsync(counts)", ce))
-                               : c->wait(l->sync_ev, "counts");
+        const uint64_t per = l->peer ? (uint64_t)W * 8 : 8;
+        std::vector<uint64_t> sizes(W, per);
+        st = exchange_rows(c, l->counts_dev, sizes.data(), l->counts_dev + (size_t)W * (per / 8), sizes.data(), 1, s,
+                           "counts");
+        if (st == VLB_OK) {
+            ce = cudaMemcpyAsync(l->peer ? matrix : recv_count, l->counts_dev + (size_t)W * (per / 8),
+                                 (size_t)W * per, cudaMemcpyDeviceToHost, s);
+            if (ce == cudaSuccess) ce = cudaEventRecord(l->sync_ev, s);
+            st = ce != cudaSuccess ? fail(VLB_ERR_IO_ERROR, cuda_msg("cudaMemcpyAsync(counts)", ce))
+                                   : c->wait(l->sync_ev, "counts");
+        }
     }
     if (st != VLB_OK) {
         l->failed = "counts";
         return st;
     }
+    if (l->peer) {
+        for (uint32_t q = 0; q < W; ++q) recv_count[q] = matrix[(size_t)q * W + (uint32_t)c->rank];
+        if (matrix[(size_t)c->rank * W + 0] != send_count[0]) {
+            l->failed = "counts";
+            return fail(VLB_ERR_INTERNAL_ERROR, "counts: the exchanged count matrix does not hold this rank's own row");
+        }
+    }
     uint64_t R = 0;
     for (uint32_t p = 0; p < W; ++p) R += recv_count[p];
-    if (R + T > 0xffffffffull) return fail(VLB_ERR_RESOURCE_EXHAUSTED, "too many received rows");
+    if (R + T > 0xffffffffull || (l->peer && R + T > l->peer_rows_cap)) {
+        l->failed = "counts";
+        return fail(VLB_ERR_RESOURCE_EXHAUSTED, "too many received rows");
+    }
     if ((st = l->reserve((uint32_t)(R + T))) != VLB_OK) return st;
     cudaEventRecord(l->phase[1], s);
-    // dispatch: fp16 rows, then their meta words
-    st = exchange_rows(c, l->send_rows, send_count, l->group_rows, recv_count, (size_t)H * 2, s, "dispatch");
+    // dispatch: fp16 rows (peer stores, or NCCL), then their meta words (NCCL; in peer mode also
+    // the fence that makes the stored rows safe to read on every receiver)
+    const uint32_t me = (uint32_t)c->rank;
+    if (l->peer) {
+        PeerSegs g{};
+        g.count = W;
+        uint64_t so = 0;
+        for (uint32_t p = 0; p < W; ++p) {
+            uint64_t off = 0;  // rows of ranks before this one in p's receive buffer
+            for (uint32_t q = 0; q < me; ++q) off += matrix[(size_t)q * W + p];
+            if (off + send_count[p] > l->rows_cap_at[p]) {
+                l->failed = "dispatch";
+                return fail(VLB_ERR_RESOURCE_EXHAUSTED, "dispatch: a peer's receive buffer is too small for this step");
+            }
+            g.src[p] = reinterpret_cast<const uint4*>(l->send_rows + so * H);
+            g.dst[p] = reinterpret_cast<uint4*>(l->rows_at[p] + off * H);
+            g.n16[p] = send_count[p] * H * 2 / 16;
+            so += send_count[p];
+        }
+        st = launch_peer_copy(g, s);
+    } else {
+        st = exchange_rows(c, l->send_rows, send_count, l->group_rows, recv_count, (size_t)H * 2, s, "dispatch");
+    }
     if (st == VLB_OK)
         st = exchange_rows(c, l->send_meta, send_count, l->group_meta, recv_count, 12, s, "dispatch");
     if (st != VLB_OK) {
@@ -607,7 +826,28 @@ int vlb_ep_forward_device(vlb_handle* h, vlb_ep_layer* l, const float* x, const 
     // results back as fp16 rows with a power-of-two scale each
     if ((st = vlb_ep_pack_half_device(h, l->group_y, (uint32_t)R, H, l->group_yh, l->group_ys, s)) != VLB_OK)
         return handle_fail(h, st);
-    st = exchange_rows(c, l->group_yh, recv_count, l->back_yh, send_count, (size_t)H * 2, s, "return");
+    if (l->peer) {
+        // the results of rank q's rows go back into q's results buffer after the rows q sent to
+        // ranks before this one (q's send order)
+        PeerSegs g{};
+        g.count = W;
+        uint64_t ro = 0;
+        for (uint32_t q = 0; q < W; ++q) {
+            uint64_t off = 0;
+            for (uint32_t p = 0; p < me; ++p) off += matrix[(size_t)q * W + p];
+            if (off + recv_count[q] > l->back_cap_at[q]) {
+                l->failed = "return";
+                return fail(VLB_ERR_RESOURCE_EXHAUSTED, "return: a peer's results buffer is too small for this step");
+            }
+            g.src[q] = reinterpret_cast<const uint4*>(l->group_yh + ro * H);
+            g.dst[q] = reinterpret_cast<uint4*>(l->back_at[q] + off * H);
+            g.n16[q] = recv_count[q] * H * 2 / 16;
+            ro += recv_count[q];
+        }
+        st = launch_peer_copy(g, s);
+    } else {
+        st = exchange_rows(c, l->group_yh, recv_count, l->back_yh, send_count, (size_t)H * 2, s, "return");
+    }
     if (st == VLB_OK) st = exchange_rows(c, l->group_ys, recv_count, l->back_ys, send_count, 4, s, "return");
     if (st != VLB_OK) {
         l->failed = "return";
