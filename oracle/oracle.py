@@ -193,6 +193,7 @@ class Oracle:
         L.vlo_rms_norm.argtypes = [P, P, SZ, SZ, F, P]
         _hc_argtypes(L, "vlo")
         L.vlo_moe_forward.argtypes = [C.POINTER(_OracleLayer), P, P, SZ, P, P, P, P]
+        L.vlo_v4_expert_activation.argtypes = [U32, P, P, SZ, SZ, P, P, F, P, P]
 
     def grid(self, t):
         g = self.grids.get(t)
@@ -291,6 +292,15 @@ class Oracle:
         self.lib.vlo_dispatch(_p(idx), T, k, E, _p(off), _p(pt), _p(ps))
         return off, pt, ps
 
+    def v4_expert_activation(self, t, w1, w3, I, H, x, route_w, limit):
+        """Down-projection input of one DeepSeek V4 expert for one token (f32 [I])."""
+        x = np.ascontiguousarray(x, np.float32)
+        act = np.empty(I, np.float32)
+        rw = None if route_w is None else np.array([route_w], np.float32)
+        if self.lib.vlo_v4_expert_activation(t, _p(w1), _p(w3), I, H, _p(x), _p(rw), limit, self.grid(t), _p(act)):
+            raise ValueError("oracle expert activation failed")
+        return act
+
     def hc_split_sinkhorn(self, mixes, scale, base, m, iters, eps):
         return _hc_split(self.lib, "vlo", mixes, scale, base, m, iters, eps)
 
@@ -372,6 +382,8 @@ class Reference:
         L.vlr_moe_forward.argtypes = [C.POINTER(_RefLayer), P, P, SZ, P, P, P, P, C.c_uint]
         L.vlr_qwen_route.argtypes = [P, P, SZ, SZ, SZ, SZ, I, P, P, P]
         L.vlr_expert_swiglu.argtypes = [P, P, P, P, P, SZ, SZ, SZ, F, P]
+        L.vlr_graph_prefill.argtypes = [P, SZ, P, SZ, P, SZ, P, SZ, P, P, SZ, P, P, SZ, SZ,
+                                        C.POINTER(SZ), C.c_char_p, SZ]
 
     def grid(self, t: int) -> bytes:
         n = self.lib.vlr_grid(t, None, 0)
@@ -475,3 +487,62 @@ class Reference:
         if st:
             raise ValueError(f"reference moe_forward failed ({st})")
         return out, idx, w
+
+    def graph_prefill(self, config: dict, tensors: dict, packed: dict, token_ids, rec_cols: int = 64,
+                      rec_cap: int = 4096):
+        """deepseek_v4_reference_prefill over a reduced graph (deepseek_v4_graph.cpp:4651).
+
+        config: the fixture's configuration (list-valued fields as lists); tensors: name ->
+        (numpy f32 or u32 array); packed: name -> (ggml type, rows, logical columns, storage
+        columns, encoded uint8 bytes, cache identity). Returns (logits, [(indices, weights)] per
+        routed layer, main layers first, then the offered rows as (identities, inputs [n x rec_cols]))."""
+        entries, keep = [], []
+        for key, v in config.items():
+            for item in (v if isinstance(v, list) else [v]):
+                kb = key.encode()
+                keep.append(kb)
+                entries.append((kb, float(item)))
+        cfg = (_GraphConfigEntry * len(entries))(*[_GraphConfigEntry(k, v) for k, v in entries])
+        items = []
+        for name, arr in tensors.items():
+            a = np.ascontiguousarray(arr)
+            kind = 0 if a.dtype == np.float32 else 1
+            if kind == 1:
+                a = np.ascontiguousarray(a, np.uint32)
+            keep.append(a)
+            items.append(_GraphTensor(name.encode(), kind, a.ctypes.data, a.size, 0, 0, 0, 0, 0))
+        for name, (t, rows, lc, sc, enc, ident) in packed.items():
+            e = np.ascontiguousarray(enc, np.uint8)
+            keep.append(e)
+            items.append(_GraphTensor(name.encode(), 2, e.ctypes.data, e.size, t, rows, lc, sc, ident))
+        arr = (_GraphTensor * len(items))(*items)
+        tok = np.ascontiguousarray(token_ids, np.uint32)
+        T = tok.size
+        V = int(config["vocabulary_size"])
+        k = int(config["experts_per_token"])
+        n_layers = int(config["layers"]) + int(config.get("mtp_layers", 0))
+        logits = np.empty(V, np.float32)
+        ridx = np.empty((n_layers, T, k), np.uint32)
+        rw = np.empty((n_layers, T, k), np.float32)
+        ids = np.zeros(rec_cap, np.uint64)
+        rows = np.zeros((rec_cap, rec_cols), np.float32)
+        n = C.c_size_t(0)
+        err = C.create_string_buffer(512)
+        st = self.lib.vlr_graph_prefill(cfg, len(entries), arr, len(items), _p(tok), T, _p(logits), V,
+                                        _p(ridx), _p(rw), n_layers, _p(ids), _p(rows), rec_cols, rec_cap,
+                                        C.byref(n), err, len(err))
+        if st:
+            raise ValueError(f"reference prefill failed: {err.value.decode()}")
+        if n.value > rec_cap:
+            raise ValueError(f"{n.value} offered rows exceed the recording capacity {rec_cap}")
+        return logits, [(ridx[i], rw[i]) for i in range(n_layers)], (ids[: n.value], rows[: n.value])
+
+
+class _GraphConfigEntry(C.Structure):
+    _fields_ = [("key", C.c_char_p), ("value", C.c_double)]
+
+
+class _GraphTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("kind", C.c_int), ("data", C.c_void_p), ("n", C.c_size_t),
+                ("ggml_type", C.c_uint32), ("rows", C.c_size_t), ("logical_columns", C.c_size_t),
+                ("storage_columns", C.c_size_t), ("identity", C.c_uint64)]

@@ -12,6 +12,7 @@
 #include <cstdint>
 #include <cstring>
 #include <span>
+#include <string>
 #include <vector>
 
 #include "vastloom/inference/deepseek_v4_reference.hpp"
@@ -335,6 +336,160 @@ int vlr_moe_forward(const vlr_moe_layer* Lp, const float* x, const uint32_t* tok
     if (!shared.empty())
         for (size_t i = 0; i < T * H; ++i) out[i] += shared[i];
     return 0;
+}
+
+// One tensor of a reduced DeepSeek V4 graph handed over from a fixture: kind 0 is f32 (n values),
+// kind 1 is u32 (n values), kind 2 a packed ggml matrix (n bytes; type, rows, logical and storage
+// columns, cache identity).
+struct vlr_graph_tensor {
+    const char* name;
+    int kind;
+    const void* data;
+    size_t n;
+    uint32_t ggml_type;
+    size_t rows, logical_columns, storage_columns;
+    uint64_t identity;
+};
+
+// The graph's numeric configuration by field name (deepseek_v4_reference.hpp:61-102).
+struct vlr_graph_config_entry {
+    const char* key;
+    double value;
+};
+
+namespace {
+
+// A matvec accelerator that declines every row (so the graph computes it on its own CPU path) and
+// records what it was offered: the matrix's cache identity and the row's padded input, in call
+// order. Through it a test sees the graph's file-static moe_forward from outside: the MoE input
+// (the shared expert's gate rows) and every expert's down-projection input.
+class OfferRecorder final : public vi::DeepseekV4MatvecAccelerator {
+public:
+    OfferRecorder(uint64_t* ids, float* rows, size_t cols, size_t cap)
+        : ids_(ids), rows_(rows), cols_(cols), cap_(cap) {}
+    vastloom::Result<bool> matvec(const vi::DeepseekV4PackedMatrix& matrix, std::span<const float> input,
+                                  std::span<float>) override {
+        if (count_ < cap_) {
+            ids_[count_] = matrix.cache_identity;
+            float* row = rows_ + count_ * cols_;
+            std::fill(row, row + cols_, 0.0F);
+            std::copy_n(input.begin(), std::min(cols_, input.size()), row);
+        }
+        ++count_;
+        return false;
+    }
+    size_t count() const { return count_; }
+
+private:
+    uint64_t* ids_;
+    float* rows_;
+    size_t cols_, cap_, count_ = 0;
+};
+
+bool set_config(vi::DeepseekV4ReferenceConfig& c, const std::string& key, double v) {
+    const auto z = static_cast<size_t>(v);
+    const auto f = static_cast<float>(v);
+    if (key == "vocabulary_size") c.vocabulary_size = z;
+    else if (key == "width") c.width = z;
+    else if (key == "intermediate_width") c.intermediate_width = z;
+    else if (key == "layers") c.layer_count = z;
+    else if (key == "hash_layers") c.hash_layer_count = z;
+    else if (key == "mtp_layers") c.mtp_layer_count = z;
+    else if (key == "heads") c.head_count = z;
+    else if (key == "experts") c.expert_count = z;
+    else if (key == "experts_per_token") c.experts_per_token = z;
+    else if (key == "query_lora_rank") c.query_lora_rank = z;
+    else if (key == "head_width") c.head_width = z;
+    else if (key == "rope_width") c.rope_width = z;
+    else if (key == "output_groups") c.output_groups = z;
+    else if (key == "output_lora_rank") c.output_lora_rank = z;
+    else if (key == "window_size") c.window_size = z;
+    else if (key == "compression_ratios") c.compression_ratios.push_back(z);
+    else if (key == "mtp_compression_ratios") c.mtp_compression_ratios.push_back(z);
+    else if (key == "compression_rope_theta") c.compression_rope_theta = f;
+    else if (key == "original_context") c.original_context = z;
+    else if (key == "rope_theta") c.rope_theta = f;
+    else if (key == "rope_factor") c.rope_factor = f;
+    else if (key == "beta_fast") c.beta_fast = f;
+    else if (key == "beta_slow") c.beta_slow = f;
+    else if (key == "index_heads") c.index_head_count = z;
+    else if (key == "index_head_width") c.index_head_width = z;
+    else if (key == "index_top_k") c.index_top_k = z;
+    else if (key == "hyper_multiplier") c.hyper_multiplier = z;
+    else if (key == "sinkhorn_iterations") c.sinkhorn_iterations = z;
+    else if (key == "norm_epsilon") c.norm_epsilon = f;
+    else if (key == "hyper_epsilon") c.hyper_epsilon = f;
+    else if (key == "route_scale") c.route_scale = f;
+    else if (key == "swiglu_limit") c.swiglu_limit = f;
+    else return false;
+    return true;
+}
+
+}  // namespace
+
+// deepseek_v4_reference_prefill (deepseek_v4_graph.cpp:4651) over a reduced graph built from the
+// given configuration entries (list-valued fields repeat their key, in order) and tensors.
+// Outputs: logits [V]; route indices / weights [(layers + mtp_layers) x T x k], main layers first;
+// every matvec row offered to the accelerator (only packed matrices are offered) as
+// (identity, first rec_cols inputs), up to rec_cap rows, with the total count in *rec_n.
+// Returns 0, or -1 with the reference's error message in err.
+int vlr_graph_prefill(const vlr_graph_config_entry* cfg, size_t n_cfg, const vlr_graph_tensor* tensors,
+                      size_t n_tensors, const uint32_t* token_ids, size_t T, float* logits, size_t V,
+                      uint32_t* route_idx, float* route_w, size_t n_route_layers, uint64_t* rec_ids,
+                      float* rec_rows, size_t rec_cols, size_t rec_cap, size_t* rec_n, char* err,
+                      size_t err_cap) {
+    const auto fail = [&](const std::string& m) {
+        if (err && err_cap) {
+            std::strncpy(err, m.c_str(), err_cap - 1);
+            err[err_cap - 1] = '\0';
+        }
+        return -1;
+    };
+    try {
+        vi::DeepseekV4ReferenceGraph graph;
+        for (size_t i = 0; i < n_cfg; ++i)
+            if (!set_config(graph.config, cfg[i].key, cfg[i].value))
+                return fail(std::string("unknown configuration key ") + cfg[i].key);
+        for (size_t i = 0; i < n_tensors; ++i) {
+            const auto& t = tensors[i];
+            if (t.kind == 0) {
+                const auto* p = static_cast<const float*>(t.data);
+                graph.float_tensors.emplace(t.name, std::vector<float>(p, p + t.n));
+            } else if (t.kind == 1) {
+                const auto* p = static_cast<const uint32_t*>(t.data);
+                graph.integer_tensors.emplace(t.name, std::vector<uint32_t>(p, p + t.n));
+            } else {
+                const auto* p = static_cast<const std::byte*>(t.data);
+                vi::DeepseekV4PackedMatrix m(t.ggml_type, t.rows, t.logical_columns, t.storage_columns,
+                                             std::vector<std::byte>(p, p + t.n));
+                m.cache_identity = t.identity;
+                graph.packed_matrices.emplace(t.name, std::move(m));
+            }
+        }
+        OfferRecorder recorder(rec_ids, rec_rows, rec_cols, rec_cap);
+        graph.accelerator = &recorder;
+        auto r = vi::deepseek_v4_reference_prefill(graph, {token_ids, T});
+        if (!r) return fail(r.error().message + ": " + r.error().context);
+        const auto& res = r.value();
+        if (res.logits.size() != V) return fail("logit count differs from the vocabulary");
+        std::memcpy(logits, res.logits.data(), V * sizeof(float));
+        const size_t k = graph.config.experts_per_token;
+        size_t layer = 0;
+        for (const auto* traces : {&res.layers, &res.mtp_layers})
+            for (const auto& tr : *traces) {
+                if (layer >= n_route_layers) return fail("more routed layers than route buffers");
+                if (tr.route.indices.size() != T * k || tr.route.weights.size() != T * k)
+                    return fail("route shape differs from tokens x top_k");
+                std::memcpy(route_idx + layer * T * k, tr.route.indices.data(), T * k * sizeof(uint32_t));
+                std::memcpy(route_w + layer * T * k, tr.route.weights.data(), T * k * sizeof(float));
+                ++layer;
+            }
+        if (layer != n_route_layers) return fail("fewer routed layers than route buffers");
+        *rec_n = recorder.count();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e.what());
+    }
 }
 
 }  // extern "C"

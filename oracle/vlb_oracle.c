@@ -742,6 +742,24 @@ static int v4_expert(const vlo_moe_layer* L, const vlo_matrix* w1, const vlo_mat
     return mv(L, w2, act, out);
 }
 
+/* The activation row execute_expert hands to the down product (deepseek_v4_graph.cpp:1855-1890:
+ * gate and up products, the optional clamp, SwiGLU in double, route weight when given), act f32[I]
+ * for one token. Exposed so that tests can compare it with the down-projection input the
+ * reference graph offers to its matvec accelerator. */
+int vlo_v4_expert_activation(uint32_t type, const uint8_t* w1, const uint8_t* w3, size_t I, size_t H,
+                             const float* x, const float* route_w, float limit, const void* grid,
+                             float* act) {
+    float* gate = (float*)malloc(I * sizeof(float));
+    float* up = (float*)malloc(I * sizeof(float));
+    int st = vlo_matvec(type, w1, I, H, x, gate, grid);
+    if (!st) st = vlo_matvec(type, w3, I, H, x, up, grid);
+    for (size_t c = 0; c < I && !st; ++c)
+        act[c] = (float)v4_swiglu((double)gate[c], (double)up[c], limit, route_w);
+    free(gate);
+    free(up);
+    return st;
+}
+
 /* OLMoE expert, olmoe_runtime.cpp:1276-1281: SwiGLU in float with expf. */
 static int olmoe_expert(const vlo_moe_layer* L, const vlo_matrix* w1, const vlo_matrix* w3,
                         const vlo_matrix* w2, const float* x, float* gate, float* up,

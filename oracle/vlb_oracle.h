@@ -123,6 +123,12 @@ typedef struct vlo_moe_layer {
     const void* grid_iq2_s;
 } vlo_moe_layer;
 
+/* The down-projection input of one DeepSeek V4 expert for one token (gate/up matvecs of type
+ * `type`, I x H each; clamp at `limit` when positive; route weight when route_w is not NULL). */
+int vlo_v4_expert_activation(uint32_t type, const uint8_t* w1, const uint8_t* w3, size_t I, size_t H,
+                             const float* x, const float* route_w, float limit, const void* grid,
+                             float* act);
+
 /* One MoE layer over T tokens: out f32[T x H]; idx/weights [T x k] receive the route. Optional
  * logits_in (f32 [T x E]) replaces the router projection (config 3 feeds logits directly). */
 int vlo_moe_forward(const vlo_moe_layer* layer, const float* x, const uint32_t* token_ids,
