@@ -188,6 +188,13 @@ def run_ours(args, rank, world, local_rank):
         with torch.cuda.stream(stream):
             flush.zero_()
 
+    if args.only_hc:
+        # the Hyper-Connection layer alone at T = --tokens (profiling runs of hc_entry_kernel)
+        res = {"metric": METRIC, "n_gpus": world,
+               "hyper_connection": run_hc_object(args, dev, stream, flush_l2, W, layer, tokens=(T,), plain=False)}
+        layer.destroy()
+        dev.close()
+        return res
     for _ in range(args.warmup):
         flush_l2()
         step()
@@ -925,7 +932,7 @@ def run_format_objects(args, dev, stream):
             "timing": "CUDA events on the library stream", "by_type": out}
 
 
-def run_hc_object(args, dev, stream, flush_l2, W, layer):
+def run_hc_object(args, dev, stream, flush_l2, W, layer, tokens=(1, 64), plain=True):
     """The config-1 layer with and without the Hyper-Connection entry and exit (m = 4 copies of
     the hidden state, 20 Sinkhorn iterations, f32 mixing weight [24 x 16384]) at T = 1 and 64:
     device time per forward (CUDA events, cold L2) and the profiled phases. The entry's mixing
@@ -968,13 +975,14 @@ def run_hc_object(args, dev, stream, flush_l2, W, layer):
         return tot / n, phases
 
     try:
-        for T in (1, 64):
-            plain_ms, plain_ph = timed(T, 1)
+        for T in tokens:
+            plain_ms, plain_ph = timed(T, 1) if plain else (None, None)
             layer.set_hyper_connection(m, fn, scale, base, norm_w, sinkhorn_iterations=20)
             hc_ms, hc_ph = timed(T, m)
             layer.set_hyper_connection(0, None, None, None, None)
-            out[f"T{T}"] = {"ms_plain": round(plain_ms, 4), "ms_hc": round(hc_ms, 4),
-                            "added_ms": round(hc_ms - plain_ms, 4), "phases_plain": plain_ph, "phases_hc": hc_ph}
+            out[f"T{T}"] = {"ms_plain": plain_ms and round(plain_ms, 4), "ms_hc": round(hc_ms, 4),
+                            "added_ms": plain_ms and round(hc_ms - plain_ms, 4), "phases_plain": plain_ph,
+                            "phases_hc": hc_ph}
     finally:
         if layer.hc_m:
             layer.set_hyper_connection(0, None, None, None, None)
@@ -1128,6 +1136,8 @@ def main():
     ap.add_argument("--prefill-experts", type=int, default=256,
                     help="routed experts of the prefill case (smaller = a profiling-sized case)")
     ap.add_argument("--only-prefill", action="store_true", help="run the prefill object alone")
+    ap.add_argument("--only-hc", action="store_true",
+                    help="run the Hyper-Connection layer alone at T = --tokens (no plain-layer comparison)")
     ap.add_argument("--no-ep", action="store_true", help="skip the configuration-4 expert-parallel object")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the decode objects of configurations 0, 1 (T = 1, 8) and 2 (chain)")
