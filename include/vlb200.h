@@ -19,6 +19,8 @@
  *     VLB_ERR_IO_ERROR.
  * Threading: calls on one handle are serialised by the handle's mutex; each handle owns one CUDA
  * stream on one device (the reference serialises its backend the same way, cuda_driver.cpp:2093).
+ * A call on a handle makes the handle's device current on the calling thread and leaves it
+ * current.
  * Memory: every device allocation the library makes is first reserved through the caller's
  * governor callbacks (CudaDriver::allocate reserves before cuMemAlloc, cuda_driver.cpp:2929-3005).
  */

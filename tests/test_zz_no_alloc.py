@@ -20,18 +20,26 @@ import vastloom_b200 as vb
 pytestmark = pytest.mark.gpu
 
 
+def _call_noalloc(dev, logits_b, bias_b, tok_b, tab_b, vocab, T, E, k, score, scale, idx_b, w_b):
+    """One vlb_route_device_noalloc call on dev's ordinal and stream; returns (status, message)."""
+    st = dev.lib.vlb_route_device_noalloc(
+        dev.ordinal, score, 1 if tab_b else 0, logits_b.ptr, bias_b.ptr if bias_b else None,
+        tok_b.ptr if tok_b else None, tab_b.ptr if tab_b else None, vocab, T, E, k, scale,
+        idx_b.ptr, w_b.ptr, C.c_void_p(dev.stream))
+    if st == 0:
+        return st, ""
+    buf = C.create_string_buffer(512)
+    dev.lib.vlb_thread_error(buf, 512)
+    return st, buf.value.decode()
+
+
 def _noalloc_route(dev, logits_b, bias_b, tok_b, tab_b, vocab, T, E, k, score, scale):
     idx_b = dev.buffer(T * k * 4, "test-idx")
     w_b = dev.buffer(T * k * 4, "test-w")
     try:
-        st = dev.lib.vlb_route_device_noalloc(
-            dev.ordinal, score, 1 if tab_b else 0, logits_b.ptr, bias_b.ptr if bias_b else None,
-            tok_b.ptr if tok_b else None, tab_b.ptr if tab_b else None, vocab, T, E, k, scale,
-            idx_b.ptr, w_b.ptr, C.c_void_p(dev.stream))
+        st, msg = _call_noalloc(dev, logits_b, bias_b, tok_b, tab_b, vocab, T, E, k, score, scale, idx_b, w_b)
         if st != 0:
-            buf = C.create_string_buffer(512)
-            dev.lib.vlb_thread_error(buf, 512)
-            raise vb.VlbError(st, buf.value.decode())
+            raise vb.VlbError(st, msg)
         return (idx_b.download(np.uint32, T * k).reshape(T, k),
                 w_b.download(np.float32, T * k).reshape(T, k))
     finally:
@@ -75,26 +83,33 @@ def test_noalloc_route_matches_allocating_route_twice(device, oracle, score):
 
 def test_noalloc_route_on_another_device_restores_the_current_one():
     """With two GPUs: device 0 current, a call for ordinal 1 runs there (its own copy of the fixed
-    array, looked up on its first call) and leaves device 0 current."""
+    array, looked up on its first call) and leaves device 0 current. The handle's own calls
+    (allocations, copies) make the handle's device current, so every buffer is allocated first
+    and device 0 is made current right before the no-allocation call."""
     if vb.device_count() < 2:
         pytest.skip("needs two GPUs")
     import ctypes
 
     rt = ctypes.CDLL("libcudart.so.12")  # the runtime instance libvlb200.so is linked against
     cur = ctypes.c_int(-1)
+    T, E, k = 9, 64, 4
     with vb.Device(1) as dev1:
         rng = np.random.default_rng(5)
-        logits = rng.standard_normal((9, 64)).astype(np.float32)
-        bias = (rng.standard_normal(64) * 0.01).astype(np.float32)
-        want_idx, want_w = dev1.route(logits, 4, 1.0, bias=bias)
+        logits = rng.standard_normal((T, E)).astype(np.float32)
+        bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
+        want_idx, want_w = dev1.route(logits, k, 1.0, bias=bias)
         lb, bb = dev1.to_device(logits), dev1.to_device(bias)
+        idx_b, w_b = dev1.buffer(T * k * 4, "test-idx"), dev1.buffer(T * k * 4, "test-w")
         try:
             assert rt.cudaSetDevice(0) == 0
-            idx, w = _noalloc_route(dev1, lb, bb, None, None, 0, 9, 64, 4, vb.SCORE_SQRT_SOFTPLUS, 1.0)
+            st, msg = _call_noalloc(dev1, lb, bb, None, None, 0, T, E, k, vb.SCORE_SQRT_SOFTPLUS, 1.0, idx_b, w_b)
             assert rt.cudaGetDevice(ctypes.byref(cur)) == 0 and cur.value == 0
+            assert st == 0, msg
+            idx = idx_b.download(np.uint32, T * k).reshape(T, k)
+            w = w_b.download(np.float32, T * k).reshape(T, k)
         finally:
-            lb.free()
-            bb.free()
+            for b in (lb, bb, idx_b, w_b):
+                b.free()
         assert np.array_equal(idx, want_idx) and w.tobytes() == want_w.tobytes()
 
 
