@@ -409,8 +409,7 @@ def run_ep(args, dev, rank, world, local_rank):
         "config": {"workload": f"cfg4-ep-zipf-T{T}x{world}", "hidden": spec.hidden,
                    "intermediate": spec.intermediate, "experts": spec.experts, "experts_per_gpu": spec.experts // world,
                    "top_k": spec.top_k, "tokens_per_gpu": T, "zipf_s": spec.zipf_s,
-                   "exchange": "NCCL all-to-all: fp16 rows + (expert, weight, max|x|) words out, fp16 results "
-                               "with a per-row power-of-two scale back",
+                   "exchange": ep_exchange_label(world, native),
                    "driver": ("C++ (vlb_ep_forward_device, the library's own NCCL communicator)" if native
                               else "Python orchestration over torch.distributed"),
                    "placement": "balanced by the measured expert load (longest-processing-time greedy, E/N per GPU)",
@@ -436,6 +435,18 @@ def run_ep(args, dev, rank, world, local_rank):
     if created_group:
         torch.distributed.destroy_process_group()
     return res
+
+
+def ep_exchange_label(world, native):
+    """How the expert-parallel step moves its rows (the library's policy; phases_ms shows the cost)."""
+    payload = ("fp16 rows + (expert, weight, max|x|) words out, fp16 results with a per-row power-of-two "
+               "scale back")
+    if world == 1:
+        return "one rank: NCCL send/receive to itself; " + payload
+    if native and world <= 16 and os.environ.get("VLB_EP_EXCHANGE", "") != "nccl":
+        return ("rows and results by peer stores into CUDA-IPC-mapped receive buffers over NVLink when every "
+                "rank maps every peer (else NCCL all-to-all); counts and meta words over NCCL; " + payload)
+    return "NCCL all-to-all: " + payload
 
 
 def all_to_all_reference(ncomm, stream, comm, like, world, T, spec, res):
