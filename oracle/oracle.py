@@ -509,12 +509,14 @@ class Reference:
             kind = 0 if a.dtype == np.float32 else 1
             if kind == 1:
                 a = np.ascontiguousarray(a, np.uint32)
-            keep.append(a)
-            items.append(_GraphTensor(name.encode(), kind, a.ctypes.data, a.size, 0, 0, 0, 0, 0))
+            nb = name.encode()
+            keep += [a, nb]
+            items.append(_GraphTensor(nb, kind, a.ctypes.data, a.size, 0, 0, 0, 0, 0))
         for name, (t, rows, lc, sc, enc, ident) in packed.items():
             e = np.ascontiguousarray(enc, np.uint8)
-            keep.append(e)
-            items.append(_GraphTensor(name.encode(), 2, e.ctypes.data, e.size, t, rows, lc, sc, ident))
+            nb = name.encode()
+            keep += [e, nb]
+            items.append(_GraphTensor(nb, 2, e.ctypes.data, e.size, t, rows, lc, sc, ident))
         arr = (_GraphTensor * len(items))(*items)
         tok = np.ascontiguousarray(token_ids, np.uint32)
         T = tok.size
