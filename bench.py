@@ -324,10 +324,12 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_ep(args, dev, rank, world, local_rank):
-    """Configuration 4: 256 experts sharded over the N ranks (N = 1: all local), args.ep_tokens
-    tokens per rank with Zipf(1.1)-skewed routing logits, all-to-all dispatch and return over
-    NCCL. Device-timed per step (CUDA events on the library stream around the whole step), max
-    over ranks; also the per-rank expert-phase time, whose spread is the load imbalance."""
+    """Configuration 4: 256 experts placed over the N ranks by measured load (N = 1: all local),
+    args.ep_tokens tokens per rank with Zipf(1.1)-skewed routing logits; dispatch and return by
+    peer stores or NCCL (ep_exchange_label). Device-timed per step (CUDA events on the library
+    stream around the whole step), max over ranks; also the per-rank expert-phase time, whose
+    spread is the load imbalance, and a check of every token against one GPU holding all
+    experts."""
     import torch
 
     from vastloom_b200 import synth
