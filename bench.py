@@ -273,14 +273,7 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded; configuration distributions, no checkpoint)",
-        "config": {
-            "workload": f"cfg1-v4flash-decode-T{T}",
-            "hidden": spec.hidden, "intermediate": spec.intermediate, "experts": spec.experts,
-            "top_k": spec.top_k, "shared_experts": 1, "tokens_per_gpu": T,
-            "routed_type": "IQ2_XXS", "shared_type": "Q8_0", "routing": "sqrt_softplus+bias, renorm",
-            "parallelism": "replicas" if world > 1 else "single",
-            "l2": "flushed (256 MiB write) before every timed step",
-        },
+        "config": headline_config(spec, T, world),
         "roofline": {
             "bound": "hbm", "kernel": kernel_name, "achieved": round(achieved, 1),
             "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
@@ -1092,6 +1085,18 @@ def run_record_objects(args, dev):
     }
 
 
+def headline_config(spec, T, world):
+    """The headline workload (configuration-1 decode), the same dict on both arms of the bench."""
+    return {
+        "workload": f"cfg1-v4flash-decode-T{T}",
+        "hidden": spec.hidden, "intermediate": spec.intermediate, "experts": spec.experts,
+        "top_k": spec.top_k, "shared_experts": 1, "tokens_per_gpu": T,
+        "routed_type": "IQ2_XXS", "shared_type": "Q8_0", "routing": "sqrt_softplus+bias, renorm",
+        "parallelism": "replicas" if world > 1 else "single",
+        "l2": "flushed (256 MiB write) before every timed step",
+    }
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU implementation of the same layer and batch."""
     from vastloom_b200 import synth
@@ -1125,9 +1130,10 @@ def run_reference(args, rank, world):
         "ms_per_step": round(1000 * total / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (f64 accumulation)",
         "data": "synthetic (seeded; configuration distributions, no checkpoint)",
-        "config": {"workload": f"cfg1-v4flash-decode-T{T}", "tokens_per_step": per_step},
+        "config": headline_config(spec, T, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{per_step} token(s) of the {T}-token batch per step"},
+                         "sample": (f"{per_step} token(s) of the {T}-token batch per step through the "
+                                    f"reference's layer loop on {threads} host threads (CPU: no L2 flush)")},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
